@@ -1,0 +1,145 @@
+"""XTIER_* settings: one declarative registry, read from the environment.
+
+Every switch is declared once below (name, kind, default, one line of help). `get(name)` parses it, `names()` lists
+them (the committed `env_names.txt` is generated from this table and checked by a test), and `check_environment()`
+warns about XTIER_* variables nobody reads (a typo would otherwise silently do nothing). The public surface follows
+the reference's switches (xtier/config.py:1-46, xtier/env_names.txt) where they mean the same thing here; settings
+that only exist for SGLang or for the reference's SM120 packs are not carried over.
+"""
+from __future__ import annotations
+
+import dataclasses
+import logging
+import os
+
+logger = logging.getLogger('xtier_b200')
+
+
+@dataclasses.dataclass(frozen=True)
+class Setting:
+    name: str
+    kind: str          # 'flag' | 'int' | 'float' | 'str' | 'list' (cpu/layer list '0-3,8')
+    default: object
+    help: str
+
+
+_S = Setting
+SETTINGS: tuple[Setting, ...] = (
+    _S('XTIER', 'flag', True, 'master switch of the tiered MoE layers (0: every expert on the GPU, no CPU tier)'),
+    _S('XTIER_LAYERS', 'str', 'all', 'model layers whose routed experts are tiered: all or a list 0-11,20'),
+    _S('XTIER_THREADS', 'int', 0, 'CPU expert engine workers (0: every CPU but one for the mailbox dispatcher)'),
+    _S('XTIER_ISA', 'str', 'auto', 'CPU engine kernels: auto, avx512 (AVX-512 BF16), avx2, scalar'),
+    _S('XTIER_SPIN_US', 'int', 200, 'engine workers spin this long before sleeping on a futex'),
+    _S('XTIER_MAIN_CPUS', 'str', '', 'CPUs of the other threads of the process (auto: all but the workers)'),
+    _S('XTIER_DISPATCH_CPU', 'int', -1, 'CPU the mailbox dispatcher thread is pinned to (-1: last CPU)'),
+    _S('XTIER_DECODE_MAX', 'int', 64, 'calls of up to this many tokens use the mailbox decode path (graph capturable)'),
+    _S('XTIER_SLOT_TOKENS', 'int', 16, 'tokens of one mailbox decode slot at the most'),
+    _S('XTIER_CPU_TIMEOUT_S', 'float', 60.0, 'a mailbox request unanswered for this long fails the step (bounded wait)'),
+    _S('XTIER_CACHE_SLOTS', 'int', -1, 'GPU hot-expert slots per layer (-1: every expert, 0: none)'),
+    _S('XTIER_CACHE_FRACTION', 'float', 0.0, 'hot slots as a fraction of the experts (overrides CACHE_SLOTS when >0)'),
+    _S('XTIER_CACHE_FULL', 'list', '', 'layers that keep every expert on the GPU'),
+    _S('XTIER_CACHE_PLAN', 'str', '', 'planner output {"slots": {layer: n}} or "auto"'),
+    _S('XTIER_CACHE_PROFILE', 'str', '', 'route-count profile that fills the hot slots at start'),
+    _S('XTIER_CACHE_ADAPT', 'flag', True, 'adaptive hot-expert swaps from decayed route counts'),
+    _S('XTIER_CACHE_EVERY', 'int', 4, 'decode windows between policy rounds'),
+    _S('XTIER_CACHE_SWAPS', 'int', 16, 'swaps per policy round at most'),
+    _S('XTIER_CACHE_DECAY', 'float', 0.7, 'decay of the route counts per round'),
+    _S('XTIER_CACHE_MIN_GAIN', 'float', 1.5, 'minimum count advantage of an incoming expert over its victim'),
+    _S('XTIER_CACHE_LOG', 'int', 0, 'log the cache statistics every N policy rounds (0: off)'),
+    _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in memory only a prefill needs (VMM granules)'),
+    _S('XTIER_CACHE_ELASTIC_RESERVE_GIB', 'float', 2.0, 'memory the elastic slots always leave free'),
+    _S('XTIER_GPU2_SLOTS', 'str', '', 'hot slots on peer GPUs read over NVLink: N per layer, or auto'),
+    _S('XTIER_EP', 'int', 0, 'expert-parallel ranks of the hot-slot pool (0: the world size)'),
+    _S('XTIER_COLD', 'flag', False, 'cold experts in NVMe relayout files, read on demand with O_DIRECT'),
+    _S('XTIER_COLD_DIR', 'str', '', 'directories (one per drive, comma separated) of the cold-expert store'),
+    _S('XTIER_COLD_FRACTION', 'float', 0.0, 'share of each layer\'s experts kept cold (not in RAM)'),
+    _S('XTIER_COLD_THREADS', 'int', 4, 'reader threads per cold-store file'),
+    _S('XTIER_FAST_LOAD', 'flag', False, 'read expert tensors straight from safetensors into engine shards (O_DIRECT)'),
+    _S('XTIER_LOAD_DIGEST', 'flag', False, 'log a digest of every loaded layer'),
+    _S('XTIER_TAIL_SKIP', 'str', '', 'K/N: decode calls of top-N skip experts outside every token\'s K largest routes'),
+    _S('XTIER_TAIL_SKIP_TOKENS', 'int', 8, 'tail skip applies to calls of at most this many tokens'),
+    _S('XTIER_GPU_PREFILL_MIN', 'int', 1024, 'prefill calls of at least this many tokens run every expert on the GPU'),
+    _S('XTIER_HYBRID_PREFILL_MAX', 'int', 2560, 'partly cached prefill below this: GPU hot routes || CPU the rest'),
+    _S('XTIER_PREFILL_CHUNK', 'int', 8, 'experts uploaded per chunk of the host-resident GPU prefill'),
+    _S('XTIER_PREFILL_SLOTS', 'int', 4, 'staging slots of the prefill upload ring'),
+    _S('XTIER_ROUTE_TRACE', 'str', '', 'binary route trace of the CPU decode calls (planner input)'),
+    _S('XTIER_TIMING', 'flag', False, 'log synchronized MoE time per forward'),
+    _S('XTIER_PREFILL_PROFILE', 'flag', False, 'CUDA events per prefill phase'),
+    _S('XTIER_DEBUG_BOUNDS', 'flag', False, 'bounds-checked kernels: a bad index sets the device error word'),
+    _S('XTIER_DEBUG_STALL_US', 'int', 0, 'test only: the mailbox dispatcher stalls this long per request'),
+    _S('XTIER_DEBUG_SEQ_START', 'int', 0, 'test only: first sequence number of the swap ring (wrap tests)'),
+    _S('XTIER_ROWS_MODE', 'str', 'direct', 'row tables: direct (O_DIRECT reads) or ram (mapped and locked)'),
+    _S('XTIER_ROWS_IO_THREADS', 'int', 32, 'row-table IO threads'),
+    _S('XTIER_ROWS_CACHE_MB', 'int', 1024, 'row-table cache size'),
+    _S('XTIER_PLAN_LAMBDA', 'float', 0.0, 'planner weight of the upload cost (0: sweep)'),
+    _S('XTIER_PLANNER_PROBE', 'str', '', 'planner probe file (plan_probe output) for XTIER_CACHE_PLAN=auto'),
+    _S('XTIER_PLANNER_TRACE', 'str', '', 'route profile for XTIER_CACHE_PLAN=auto'),
+    _S('XTIER_CACHE_BUDGET_GIB', 'float', 0.0, 'GPU memory for hot slots over all layers (planner budget)'),
+    _S('XTIER_ENGINE_LIB', 'str', '', 'path of the CPU engine library (default: the in-tree build)'),
+    _S('XTIER_CONSOLE_PORT', 'int', 8765, 'console HTTP port'),
+    _S('XTIER_PACKS', 'str', 'all', 'model packs: all, none or a list'),
+)
+
+_BY_NAME = {s.name: s for s in SETTINGS}
+
+
+def cpulist(text: str) -> list[int]:
+    """'0-3,8' -> [0, 1, 2, 3, 8]"""
+    out: list[int] = []
+    for part in str(text).replace(' ', '').replace('\n', '').split(','):
+        if part:
+            lo, _, hi = part.partition('-')
+            out.extend(range(int(lo), int(hi or lo) + 1))
+    return out
+
+
+def _parse(s: Setting, raw: str):
+    if s.kind == 'flag':
+        return raw.strip().lower() in ('1', 'true', 'yes', 'on')
+    if s.kind == 'int':
+        return int(raw)
+    if s.kind == 'float':
+        return float(raw)
+    if s.kind == 'list':
+        return cpulist(raw)
+    return raw
+
+
+def get(name: str):
+    s = _BY_NAME[name]
+    raw = os.environ.get(name)
+    if raw is None or raw.strip() == '':
+        return cpulist(s.default) if s.kind == 'list' else s.default
+    try:
+        return _parse(s, raw)
+    except ValueError as e:
+        raise ValueError(f'xtier_b200: {name}={raw!r} is not a valid {s.kind}') from e
+
+
+def names() -> list[str]:
+    return sorted(_BY_NAME)
+
+
+def unknown_names(environ=None) -> list[str]:
+    env = os.environ if environ is None else environ
+    return sorted(k for k in env if k.startswith('XTIER') and k not in _BY_NAME)
+
+
+def check_environment(environ=None) -> list[str]:
+    bad = unknown_names(environ)
+    for k in bad:
+        logger.warning('xtier_b200: %s is set but no setting of that name exists (typo?)', k)
+    return bad
+
+
+def layer_selected(layer: int) -> bool:
+    spec = str(get('XTIER_LAYERS')).strip()
+    return spec in ('', 'all') or layer in cpulist(spec)
+
+
+def env_names_text() -> str:
+    return '\n'.join(names()) + '\n'
+
+
+def help_text() -> str:
+    return '\n'.join(f'{s.name}={s.default!s:8} {s.help}' for s in sorted(SETTINGS, key=lambda s: s.name))
