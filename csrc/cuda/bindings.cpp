@@ -1,0 +1,223 @@
+// torch op registrations of the sm_100a kernels (namespace `xtier`). Every op writes into tensors the caller owns and
+// allocates nothing, so the ops can be captured into CUDA graphs. Checks are done once per call on the host.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include "params.h"
+
+extern "C" int xt_mailbox_view(void *h, void *out);
+
+namespace {
+
+using at::Tensor;
+using xt::AttnDecodeParams;
+using xt::DownParams;
+using xt::GateUpParams;
+using xt::RopeParams;
+using xt::RouteParams;
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(bool ok, const char *what) { TORCH_CHECK(ok, "xtier: ", what); }
+
+void check_rc(int rc, const char *op) { TORCH_CHECK(rc == 0, "xtier: ", op, " launch failed (code ", rc, ")"); }
+
+template <typename T>
+T *ptr(const Tensor &t) {
+    return reinterpret_cast<T *>(t.data_ptr());
+}
+
+template <typename T>
+T *optr(const std::optional<Tensor> &t) {
+    return t.has_value() && t->defined() ? reinterpret_cast<T *>(t->data_ptr()) : nullptr;
+}
+
+void cuda_contig(const Tensor &t, const char *name) {
+    TORCH_CHECK(t.is_cuda() && t.is_contiguous(), "xtier: ", name, " must be a contiguous CUDA tensor");
+}
+
+XtMailbox mailbox_view(int64_t handle) {
+    XtMailbox v{};
+    if (handle) TORCH_CHECK(xt_mailbox_view(reinterpret_cast<void *>(handle), &v) > 0, "xtier: bad mailbox handle");
+    return v;
+}
+
+void add_rmsnorm(const Tensor &x, const std::optional<Tensor> &residual, const Tensor &w, const Tensor &out,
+                 double eps) {
+    cuda_contig(x, "x");
+    cuda_contig(out, "out");
+    check(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "add_rmsnorm wants bf16");
+    const int H = int(x.size(-1));
+    const int T = int(x.numel() / H);
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_add_rmsnorm(x.data_ptr(), optr<void>(residual), w.data_ptr(), out.data_ptr(), T, H, float(eps),
+                            stream()),
+             "add_rmsnorm");
+}
+
+void qk_norm_rope_kv(const Tensor &qkv, const std::optional<Tensor> &qn, const std::optional<Tensor> &kn,
+                     const Tensor &pos, const Tensor &batch, const Tensor &q, const Tensor &kc, const Tensor &vc,
+                     int64_t hq, int64_t hkv, double theta, double eps) {
+    cuda_contig(qkv, "qkv");
+    cuda_contig(kc, "k_cache");
+    cuda_contig(vc, "v_cache");
+    check(pos.scalar_type() == at::kInt && batch.scalar_type() == at::kInt, "positions and batch must be int32");
+    RopeParams p{};
+    p.qkv = ptr<const __nv_bfloat16>(qkv);
+    p.qn = optr<const __nv_bfloat16>(qn);
+    p.kn = optr<const __nv_bfloat16>(kn);
+    p.pos = ptr<const int32_t>(pos);
+    p.batch = ptr<const int32_t>(batch);
+    p.q = ptr<__nv_bfloat16>(q);
+    p.kc = ptr<__nv_bfloat16>(kc);
+    p.vc = ptr<__nv_bfloat16>(vc);
+    p.Hq = int(hq);
+    p.Hkv = int(hkv);
+    p.D = int(kc.size(-1));
+    p.L = int(kc.size(-2));
+    p.T = int(pos.numel());
+    p.theta = float(theta);
+    p.eps = float(eps);
+    check(qkv.size(-1) == (hq + 2 * hkv) * p.D, "qkv width");
+    c10::cuda::CUDAGuard g(qkv.device());
+    check_rc(xt_qk_norm_rope_kv(&p, stream()), "qk_norm_rope_kv");
+}
+
+void attn_decode(const Tensor &q, const Tensor &kc, const Tensor &vc, const Tensor &seqlens, const Tensor &out,
+                 const Tensor &ws_o, const Tensor &ws_ml, const Tensor &counters, int64_t splits, double scale) {
+    cuda_contig(q, "q");
+    cuda_contig(kc, "k_cache");
+    AttnDecodeParams p{};
+    p.q = ptr<const __nv_bfloat16>(q);
+    p.kc = ptr<const __nv_bfloat16>(kc);
+    p.vc = ptr<const __nv_bfloat16>(vc);
+    p.seqlens = ptr<const int32_t>(seqlens);
+    p.out = ptr<__nv_bfloat16>(out);
+    p.ws_o = ptr<float>(ws_o);
+    p.ws_ml = ptr<float>(ws_ml);
+    p.counters = ptr<uint32_t>(counters);
+    const int B = int(q.size(0));
+    p.Hq = int(q.size(1));
+    p.Hkv = int(kc.size(1));
+    p.L = int(kc.size(2));
+    p.splits = int(splits);
+    p.scale_log2 = float(scale * 1.4426950408889634);
+    const int G = p.Hq / p.Hkv;
+    check(ws_o.numel() >= int64_t(B) * p.Hkv * splits * G * 128, "ws_o too small");
+    check(ws_ml.numel() >= int64_t(B) * p.Hkv * splits * G * 2, "ws_ml too small");
+    check(counters.numel() >= int64_t(B) * p.Hkv, "counters too small");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_attn_decode(&p, B, stream()), "attn_decode");
+}
+
+void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &bias, const std::optional<Tensor> &corr,
+               const std::optional<Tensor> &table, const std::optional<Tensor> &shared_slots, const Tensor &ids,
+               const Tensor &w, const Tensor &slots, int64_t k, int64_t mode, int64_t n_group, int64_t topk_group,
+               bool renorm, double scale, int64_t layer, int64_t mailbox) {
+    cuda_contig(x, "x");
+    cuda_contig(wr, "router weight");
+    RouteParams p{};
+    p.x = ptr<const __nv_bfloat16>(x);
+    p.wr = ptr<const __nv_bfloat16>(wr);
+    p.bias = optr<const float>(bias);
+    p.corr = optr<const float>(corr);
+    p.table = optr<const int32_t>(table);
+    p.shared_slots = optr<const int32_t>(shared_slots);
+    p.ids = ptr<int32_t>(ids);
+    p.w = ptr<float>(w);
+    p.slots = ptr<int32_t>(slots);
+    p.m = int(x.size(0));
+    p.H = int(x.size(1));
+    p.E = int(wr.size(0));
+    p.k = int(k);
+    p.n_shared = shared_slots.has_value() ? int(shared_slots->numel()) : 0;
+    p.mode = int(mode);
+    p.n_group = int(n_group);
+    p.topk_group = int(topk_group);
+    p.renorm = renorm;
+    p.scale = float(scale);
+    p.layer = int(layer);
+    check(ids.numel() >= int64_t(p.m) * (p.k + p.n_shared), "ids too small");
+    check(p.k <= p.E, "k > experts");
+    XtMailbox mb = mailbox_view(mailbox);
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_moe_route(&p, &mb, mailbox != 0, stream()), "moe_route");
+}
+
+void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const Tensor &s13, const Tensor &g13,
+                 const Tensor &mid, int64_t fmt, double limit, double alpha, double beta) {
+    cuda_contig(w13, "w13");
+    cuda_contig(s13, "s13");
+    GateUpParams p{};
+    p.x = ptr<const __nv_bfloat16>(x);
+    p.slots = ptr<const int32_t>(slots);
+    p.w13 = ptr<const uint8_t>(w13);
+    p.s13 = ptr<const uint8_t>(s13);
+    p.g13 = ptr<const float>(g13);
+    p.mid = ptr<float>(mid);
+    p.routes = int(slots.numel());
+    p.kk = int(slots.size(-1));
+    p.H = int(x.size(-1));
+    p.I = int(w13.size(1) / 2);
+    p.fmt = int(fmt);
+    p.limit = float(limit);
+    p.alpha = float(alpha);
+    p.beta = float(beta);
+    check(mid.numel() >= int64_t(p.routes) * p.I, "mid too small");
+    check(w13.size(2) * 2 == p.H, "w13 / x hidden mismatch");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_moe_gate_up(&p, stream()), "moe_gate_up");
+}
+
+void moe_down(const Tensor &mid, const Tensor &slots, const Tensor &w, const Tensor &w2, const Tensor &s2,
+              const Tensor &g2, const std::optional<Tensor> &add, const Tensor &out,
+              const std::optional<Tensor> &out_f32, int64_t fmt, int64_t mailbox) {
+    cuda_contig(w2, "w2");
+    DownParams p{};
+    p.mid = ptr<const float>(mid);
+    p.slots = ptr<const int32_t>(slots);
+    p.w = ptr<const float>(w);
+    p.w2 = ptr<const uint8_t>(w2);
+    p.s2 = ptr<const uint8_t>(s2);
+    p.g2 = ptr<const float>(g2);
+    p.add = optr<const __nv_bfloat16>(add);
+    p.out = ptr<__nv_bfloat16>(out);
+    p.out_f32 = optr<float>(out_f32);
+    p.kk = int(slots.size(-1));
+    p.H = int(w2.size(1));
+    p.I = int(w2.size(2) * 2);
+    p.fmt = int(fmt);
+    const int m = int(slots.size(0));
+    check(p.H % 4 == 0, "hidden % 4");
+    XtMailbox mb = mailbox_view(mailbox);
+    c10::cuda::CUDAGuard g(out.device());
+    check_rc(xt_moe_down(&p, &mb, mailbox != 0, m, stream()), "moe_down");
+}
+
+}  // namespace
+
+TORCH_LIBRARY(xtier, m) {
+    m.def("add_rmsnorm(Tensor x, Tensor(a!)? residual, Tensor w, Tensor(b!) out, float eps) -> ()");
+    m.def("qk_norm_rope_kv(Tensor qkv, Tensor? q_norm, Tensor? k_norm, Tensor pos, Tensor batch, Tensor(a!) q, "
+          "Tensor(b!) k_cache, Tensor(c!) v_cache, int hq, int hkv, float theta, float eps) -> ()");
+    m.def("attn_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seqlens, Tensor(a!) out, Tensor(b!) ws_o, "
+          "Tensor(c!) ws_ml, Tensor(d!) counters, int splits, float scale) -> ()");
+    m.def("moe_route(Tensor x, Tensor wr, Tensor? bias, Tensor? corr, Tensor? table, Tensor? shared_slots, "
+          "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, int k, int mode, int n_group, int topk_group, bool renorm, "
+          "float scale, int layer, int mailbox) -> ()");
+    m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
+          "float limit, float alpha, float beta) -> ()");
+    m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
+          "Tensor(b!)? out_f32, int fmt, int mailbox) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
+    m.impl("add_rmsnorm", &add_rmsnorm);
+    m.impl("qk_norm_rope_kv", &qk_norm_rope_kv);
+    m.impl("attn_decode", &attn_decode);
+    m.impl("moe_route", &moe_route);
+    m.impl("moe_gate_up", &moe_gate_up);
+    m.impl("moe_down", &moe_down);
+}

@@ -1,0 +1,85 @@
+// Shared device helpers of the sm_100a kernels (B200 only: compiled with -gencode arch=compute_100a,code=sm_100a).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define XT_DEV __device__ __forceinline__
+
+namespace xt {
+
+XT_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+XT_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sum over groups of L consecutive lanes (L a power of two <= 32); every lane of a group gets the group's sum.
+template <int L>
+XT_DEV float group_sum(float v) {
+#pragma unroll
+    for (int o = L / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Four E2M1 pairs (one 32-bit word, byte i = elements 2i and 2i+1, low nibble first) -> four f16x2, using the
+// hardware conversion of sm_100 (cvt.rn.f16x2.e2m1x2 puts the low nibble in the low half).
+XT_DEV void e2m1x8_to_h2(uint32_t w, __half2 (&out)[4]) {
+    uint32_t r0, r1, r2, r3;
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}\n"
+        : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+        : "r"(w));
+    out[0] = *reinterpret_cast<__half2 *>(&r0);
+    out[1] = *reinterpret_cast<__half2 *>(&r1);
+    out[2] = *reinterpret_cast<__half2 *>(&r2);
+    out[3] = *reinterpret_cast<__half2 *>(&r3);
+}
+
+// Two E4M3 bytes (low byte first) -> two floats (hardware conversion through f16x2)
+XT_DEV float2 e4m3x2_to_f2(uint16_t v) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;\n" : "=r"(r) : "h"(v));
+    return __half22float2(*reinterpret_cast<__half2 *>(&r));
+}
+
+XT_DEV float e4m3_to_f(uint8_t b) { return e4m3x2_to_f2(uint16_t(b)).x; }
+
+XT_DEV float ue8m0_to_f(uint8_t b) { return b ? __uint_as_float(uint32_t(b) << 23) : 5.877471754e-39f; }
+
+XT_DEV uint4 ldg_nc_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// System-scope acquire load / release store (mapped host memory shared with the CPU).
+XT_DEV uint32_t ld_acquire_sys(const volatile uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+XT_DEV void st_release_sys(volatile uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+XT_DEV uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+    return t;
+}
+
+XT_DEV float bf16_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+}  // namespace xt

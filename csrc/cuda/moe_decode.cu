@@ -1,0 +1,483 @@
+// Decode-time MoE on the GPU hot-slot pool (W4A16: FP4 weights x BF16 activations, FP32 sums), with the CPU tier
+// reached through the mailbox. Three kernels per MoE call, all CUDA-graph capturable:
+//
+//   moe_route   one CTA per token: router logits (BF16 GEMV), softmax or grouped-sigmoid top-k, renormalization and
+//               routed scale; each route is split by the residency table (GPU slot, or the CPU); tokens with CPU
+//               routes are written into the mailbox slot and the last CTA publishes the request.
+//   moe_gate_up one CTA per (route, block of I rows): SwiGLU(g13[0] * x.Wg, g13[1] * x.Wu) of the route's slot, FP32.
+//   moe_down    one CTA per (token, block of H rows): sum over the token's GPU routes, in route order, of
+//               w * g2 * mid.Wd; then (bounded) wait for the CPU part, add it, write BF16. No atomics: every output
+//               element has one writer and a fixed summation order, so the result is deterministic.
+//
+// The GEMVs are weight-bandwidth bound at decode sizes (1-16 tokens per expert), so they run on CUDA cores with the
+// hardware E2M1 and E4M3 conversions of sm_100: each lane streams 16-byte weight chunks (ld.global.nc, no L1
+// allocation), converts 8 codes per cvt pair to f16x2, and accumulates one 16- (NVFP4) or 32-element (MXFP4) block in
+// f16x2 before scaling into FP32. `LPR` lanes share a row (LPR * CH * 16 bytes = row bytes), so the activation slice
+// of a lane stays in registers for all its rows.
+// Reference parity: xtier/cache/pool.py:80-110 (_pack: residency split), :170-250 (_gate_up, _down, _combine),
+// :251-258 (_unpack: CPU part + GPU part); xtier/backend/kernels.py:25-57 (mailbox pack/unpack).
+#include "../include/xt_mailbox.h"
+#include "common.cuh"
+#include "params.h"
+
+#include <stdio.h>
+
+namespace xt {
+
+
+constexpr int ROUTE_THREADS = 256;
+constexpr int MAX_E = 512;
+
+__global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p, XtMailbox mb, int use_mb) {
+    __shared__ float logits[MAX_E];
+    __shared__ float sel[MAX_E];
+    __shared__ int chosen[XT_MB_MAX_ROUTES];
+    __shared__ float chosen_w[XT_MB_MAX_ROUTES];
+    __shared__ int any_cpu;
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int kk = p.k + p.n_shared;
+    const __nv_bfloat16 *xt = p.x + size_t(t) * p.H;
+    if (tid == 0) any_cpu = 0;
+
+    // logits: one warp per expert row, 16-byte loads (H % 256 == 0 checked on the host)
+    for (int e = warp; e < p.E; e += ROUTE_THREADS / 32) {
+        const __nv_bfloat16 *we = p.wr + size_t(e) * p.H;
+        float acc = 0.f;
+        for (int c = lane * 8; c < p.H; c += 256) {
+            uint4 a = *reinterpret_cast<const uint4 *>(xt + c);
+            uint4 b = *reinterpret_cast<const uint4 *>(we + c);
+            const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
+            const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&b);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float2 fa = __bfloat1622float2(a2[i]), fb = __bfloat1622float2(b2[i]);
+                acc = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, acc));
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) logits[e] = acc + (p.bias ? p.bias[e] : 0.f);
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // scores -> selection values
+        if (p.mode == 0) {   // softmax over all experts
+            float mx = -INFINITY;
+            for (int e = lane; e < p.E; e += 32) mx = fmaxf(mx, logits[e]);
+            mx = warp_max(mx);
+            float s = 0.f;
+            for (int e = lane; e < p.E; e += 32) s += __expf(logits[e] - mx);
+            s = warp_sum(s);
+            for (int e = lane; e < p.E; e += 32) {
+                float v = __expf(logits[e] - mx) / s;
+                logits[e] = v;
+                sel[e] = v;
+            }
+        } else {   // sigmoid scores; selection adds the correction bias; groups by the sum of their top two
+            for (int e = lane; e < p.E; e += 32) {
+                float v = 1.f / (1.f + __expf(-logits[e]));
+                logits[e] = v;
+                sel[e] = v + (p.corr ? p.corr[e] : 0.f);
+            }
+            __syncwarp();
+            if (p.n_group > 1) {
+                const int gs = p.E / p.n_group;
+                float gscore = -INFINITY;
+                if (lane < p.n_group) {
+                    float a = -INFINITY, b = -INFINITY;
+                    for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
+                        float v = sel[e];
+                        if (v > a) {
+                            b = a;
+                            a = v;
+                        } else if (v > b) {
+                            b = v;
+                        }
+                    }
+                    gscore = a + b;
+                }
+                unsigned keep = 0;
+                for (int r = 0; r < p.topk_group; ++r) {
+                    float v = (lane < p.n_group && !((keep >> lane) & 1)) ? gscore : -INFINITY;
+                    float bv = v;
+                    int bi = lane;
+                    for (int o = 16; o > 0; o >>= 1) {
+                        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                        if (ov > bv || (ov == bv && oi < bi)) {
+                            bv = ov;
+                            bi = oi;
+                        }
+                    }
+                    keep |= 1u << bi;
+                }
+                __syncwarp();
+                for (int e = lane; e < p.E; e += 32)
+                    if (!((keep >> (e / gs)) & 1)) sel[e] = -INFINITY;
+            }
+        }
+        __syncwarp();
+        // top-k by selection value (ties: lower expert id)
+        for (int r = 0; r < p.k; ++r) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int e = lane; e < p.E; e += 32)
+                if (sel[e] > bv) {
+                    bv = sel[e];
+                    bi = e;
+                }
+            for (int o = 16; o > 0; o >>= 1) {
+                float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (lane == 0) {
+                const bool ok = bi < p.E && bv > -INFINITY;   // fewer eligible experts than k: a zero-weight route
+                chosen[r] = ok ? bi : 0;
+                chosen_w[r] = ok ? logits[bi] : 0.f;
+                if (ok) sel[bi] = -INFINITY;
+            }
+            __syncwarp();
+        }
+        if (lane == 0) {
+            float s = 0.f;
+            for (int r = 0; r < p.k; ++r) s += chosen_w[r];
+            float f = (p.renorm && s > 0.f ? 1.f / s : 1.f) * p.scale;
+            for (int r = 0; r < p.k; ++r) chosen_w[r] *= f;
+        }
+        __syncwarp();
+        if (lane < kk) {
+            int e, slot;
+            float wv;
+            if (lane < p.k) {
+                e = chosen[lane];
+                wv = chosen_w[lane];
+                slot = p.table ? p.table[e] : e;
+            } else {
+                e = -1;
+                wv = 1.f;
+                slot = p.shared_slots[lane - p.k];
+            }
+            const size_t o = size_t(t) * kk + lane;
+            p.ids[o] = e;
+            p.w[o] = wv;
+            p.slots[o] = slot;
+            if (use_mb) {
+                const size_t mo = size_t(t) * kk + lane;   // [m, kk] as the engine takes it
+                mb.ids[mo] = (slot < 0) ? e : -1;
+                mb.w[mo] = wv;
+                mb.orig[mo] = e;
+                if (slot < 0) atomicOr(&any_cpu, 1);
+            }
+        }
+    }
+    if (!use_mb) return;
+    __syncthreads();
+    // this token's activations to the slot (host memory over PCIe), then count the CTA as done
+    if (any_cpu) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(xt);
+        uint4 *dst = reinterpret_cast<uint4 *>(mb.x + size_t(t) * p.H);
+        for (int i = tid; i < p.H / 8; i += ROUTE_THREADS) dst[i] = src[i];
+        if (tid == 0) atomicOr(&mb.dev->any, 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        unsigned prev = atomicAdd(&mb.dev->done, 1u);
+        if (prev == unsigned(p.m) - 1) {   // last CTA of the call publishes it
+            __threadfence_system();
+            unsigned any = atomicExch(&mb.dev->any, 0u);
+            mb.dev->done = 0;
+            mb.dev->pending = any;
+            if (any) {
+                unsigned seq = mb.dev->seq + 1;
+                mb.dev->seq = seq;
+                mb.hdr->layer = p.layer;
+                mb.hdr->m = p.m;
+                mb.hdr->k = kk;
+                mb.hdr->hidden = p.H;
+                __threadfence_system();
+                st_release_sys(&mb.hdr->req, seq);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ FP4 GEMV core
+struct ExpertPtrs {
+    const uint8_t *w;    // packed rows, row stride in bytes = K / 2
+    const uint8_t *s;    // block scales, row stride K / bs
+    size_t slot_w, slot_s;   // bytes between slots
+};
+
+// dot of one 16-byte chunk (32 elements) with 16 f16x2 activations; fmt 0 NVFP4 (two E4M3 scales), 1 MXFP4 (one)
+XT_DEV float chunk_dot(uint4 wv, const __half2 (&x)[16], const uint8_t *sp, int fmt) {
+    __half2 h[4];
+    __half2 a0 = __float2half2_rn(0.f), a1 = __float2half2_rn(0.f);
+    e2m1x8_to_h2(wv.x, h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a0 = __hfma2(h[i], x[i], a0);
+    e2m1x8_to_h2(wv.y, h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a0 = __hfma2(h[i], x[4 + i], a0);
+    e2m1x8_to_h2(wv.z, h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a1 = __hfma2(h[i], x[8 + i], a1);
+    e2m1x8_to_h2(wv.w, h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a1 = __hfma2(h[i], x[12 + i], a1);
+    float2 f0 = __half22float2(a0), f1 = __half22float2(a1);
+    if (fmt == 0) {
+        float2 s = e4m3x2_to_f2(*reinterpret_cast<const uint16_t *>(sp));
+        return (f0.x + f0.y) * s.x + (f1.x + f1.y) * s.y;
+    }
+    return (f0.x + f0.y + f1.x + f1.y) * ue8m0_to_f(*sp);
+}
+
+template <int LPR, int CH>
+XT_DEV void load_x_bf16(const __nv_bfloat16 *x, int q, __half2 (&xr)[CH][16]) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + size_t(c * LPR + q) * 32);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            uint4 u = src[v];
+            const __nv_bfloat162 *b = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xr[c][v * 4 + i] = __float22half2_rn(__bfloat1622float2(b[i]));
+        }
+    }
+}
+
+template <int LPR, int CH>
+XT_DEV void load_x_f32(const float *x, int q, __half2 (&xr)[CH][16]) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + size_t(c * LPR + q) * 32);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            float4 f = src[v];
+            xr[c][v * 2] = __floats2half2_rn(f.x, f.y);
+            xr[c][v * 2 + 1] = __floats2half2_rn(f.z, f.w);
+        }
+    }
+}
+
+// One row: K = LPR * CH * 32 elements, lane q of its group covers chunks c*LPR+q. Returns the group-reduced sum.
+template <int LPR, int CH>
+XT_DEV float row_dot(const uint8_t *wrow, const uint8_t *srow, int fmt, int q, const __half2 (&xr)[CH][16]) {
+    uint4 wv[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) wv[c] = ldg_nc_v4(wrow + size_t(c * LPR + q) * 16);
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int chunk = c * LPR + q;
+        const uint8_t *sp = fmt == 0 ? srow + chunk * 2 : srow + chunk;
+        acc += chunk_dot(wv[c], xr[c], sp, fmt);
+    }
+    return group_sum<LPR>(acc);
+}
+
+
+constexpr int GU_WARPS = 8;
+
+template <int LPR, int CH>
+__global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams p) {
+    const int r = blockIdx.x;
+    const int slot = p.slots[r];
+    if (slot < 0) return;
+    const int t = r / p.kk;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int RPW = 32 / LPR;   // rows per warp step
+    const int q = lane % LPR, sub = lane / LPR;
+    __half2 xr[CH][16];
+    load_x_bf16<LPR, CH>(p.x + size_t(t) * p.H, q, xr);
+    const int bs = p.fmt == 0 ? 16 : 32;
+    const size_t wrow = p.H / 2, srow = p.H / bs;
+    const uint8_t *W = p.w13 + size_t(slot) * 2 * p.I * wrow;
+    const uint8_t *S = p.s13 + size_t(slot) * 2 * p.I * srow;
+    const float gg = p.g13[2 * slot], gu = p.g13[2 * slot + 1];
+    const int rows_per_cta = GU_WARPS * RPW;
+    const int j_raw = blockIdx.y * rows_per_cta + warp * RPW + sub;
+    const int j = min(j_raw, p.I - 1);   // every lane takes part in the group shuffles; out-of-range rows store nothing
+    float g = row_dot<LPR, CH>(W + j * wrow, S + j * srow, p.fmt, q, xr) * gg;
+    float u = row_dot<LPR, CH>(W + (p.I + j) * wrow, S + (p.I + j) * srow, p.fmt, q, xr) * gu;
+    if (q == 0 && j_raw < p.I) {
+        if (p.limit > 0.f) {
+            g = fminf(g, p.limit);
+            u = fmaxf(-p.limit, fminf(u, p.limit));
+        }
+        float h = (p.alpha == 1.f && p.beta == 0.f) ? g / (1.f + __expf(-g)) * u
+                                                     : g / (1.f + __expf(-p.alpha * g)) * (u + p.beta);
+        p.mid[size_t(r) * p.I + j] = h;
+    }
+}
+
+
+constexpr int DN_WARPS = 4;
+
+template <int LPR, int CH, int U>
+__global__ void __launch_bounds__(DN_WARPS * 32) moe_down_kernel(DownParams p, XtMailbox mb, int use_mb) {
+    const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int RPW = 32 / LPR;
+    const int q = lane % LPR, sub = lane / LPR;
+    const int bs = p.fmt == 0 ? 16 : 32;
+    const size_t wrow = p.I / 2, srow = p.I / bs;
+    const int rows_per_cta = DN_WARPS * RPW * U;
+    const int h0 = blockIdx.y * rows_per_cta + warp * RPW * U + sub;
+    float acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = 0.f;
+    for (int j = 0; j < p.kk; ++j) {
+        const int r = t * p.kk + j;
+        const int slot = p.slots[r];
+        if (slot < 0) continue;
+        __half2 xr[CH][16];
+        load_x_f32<LPR, CH>(p.mid + size_t(r) * p.I, q, xr);
+        const float wt = p.w[r] * p.g2[slot];
+        const uint8_t *W = p.w2 + size_t(slot) * p.H * wrow;
+        const uint8_t *S = p.s2 + size_t(slot) * p.H * srow;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int h = min(h0 + u * RPW, p.H - 1);   // all lanes shuffle; rows past H are dropped below
+            acc[u] += wt * row_dot<LPR, CH>(W + h * wrow, S + h * srow, p.fmt, q, xr);
+        }
+    }
+    // stage the GPU part of this CTA's rows in shared memory
+    __shared__ float part[DN_WARPS * RPW * U];
+    const int hb = blockIdx.y * rows_per_cta;
+    if (q == 0) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) part[warp * RPW * U + sub + u * RPW] = acc[u];
+    }
+    // CPU part: wait for the dispatcher's answer (bounded), then add it
+    __shared__ int cpu_ok;
+    if (threadIdx.x == 0) {
+        int ok = 0;
+        if (use_mb && mb.dev->pending) {
+            const unsigned seq = mb.dev->seq;
+            const uint64_t t0 = globaltimer_ns();
+            for (;;) {
+                if (ld_acquire_sys(&mb.hdr->resp) == seq) {
+                    ok = 1;
+                    break;
+                }
+                if (globaltimer_ns() - t0 > mb.timeout_ns) {
+                    atomicExch(&mb.dev->error, 1u);
+                    mb.hdr->gpu_error = 1;
+                    break;
+                }
+                __nanosleep(256);
+            }
+        }
+        cpu_ok = ok;
+    }
+    __syncthreads();
+    // four rows per thread: one 16-byte read of the CPU result (mapped host memory) per four outputs
+    for (int i = threadIdx.x; i * 4 < rows_per_cta; i += blockDim.x) {
+        const int h = hb + i * 4;
+        if (h >= p.H) break;
+        float v[4] = {part[i * 4], part[i * 4 + 1], part[i * 4 + 2], part[i * 4 + 3]};
+        const size_t o = size_t(t) * p.H + h;
+        if (p.out_f32) *reinterpret_cast<float4 *>(p.out_f32 + o) = make_float4(v[0], v[1], v[2], v[3]);
+        if (cpu_ok) {
+            float4 c;
+            asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+                         : "=f"(c.x), "=f"(c.y), "=f"(c.z), "=f"(c.w)
+                         : "l"(mb.y + o));
+            v[0] += c.x;
+            v[1] += c.y;
+            v[2] += c.z;
+            v[3] += c.w;
+        }
+        if (p.add) {
+            uint2 a = *reinterpret_cast<const uint2 *>(p.add + o);
+            const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
+            float2 f0 = __bfloat1622float2(a2[0]), f1 = __bfloat1622float2(a2[1]);
+            v[0] += f0.x;
+            v[1] += f0.y;
+            v[2] += f1.x;
+            v[3] += f1.y;
+        }
+        __nv_bfloat162 r0 = __floats2bfloat162_rn(v[0], v[1]), r1 = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 outv;
+        outv.x = *reinterpret_cast<uint32_t *>(&r0);
+        outv.y = *reinterpret_cast<uint32_t *>(&r1);
+        *reinterpret_cast<uint2 *>(p.out + o) = outv;
+    }
+}
+
+}  // namespace xt
+
+// ------------------------------------------------------------------------------------------------ host launchers
+using namespace xt;
+
+static int pick_lpr(int row_bytes, int *ch) {
+    const int chunks = row_bytes / 16;
+    if (row_bytes % 16) return 0;
+    for (int lpr : {32, 16, 8, 4}) {
+        if (chunks % lpr == 0 && chunks / lpr <= 8) {
+            *ch = chunks / lpr;
+            return lpr;
+        }
+    }
+    return 0;
+}
+
+#define XT_GU_CASE(L, C)                                                                        \
+    if (lpr == L && ch == C) {                                                                  \
+        constexpr int rows = GU_WARPS * (32 / L);                                               \
+        dim3 grid(p.routes, (p.I + rows - 1) / rows);                                           \
+        moe_gate_up_kernel<L, C><<<grid, GU_WARPS * 32, 0, stream>>>(p);                        \
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;                                      \
+    }
+
+#define XT_DN_CASE(L, C, U)                                                                     \
+    if (lpr == L && ch == C) {                                                                  \
+        constexpr int rows = DN_WARPS * (32 / L) * U;                                           \
+        dim3 grid(m, (p.H + rows - 1) / rows);                                                  \
+        moe_down_kernel<L, C, U><<<grid, DN_WARPS * 32, 0, stream>>>(p, mb, use_mb);            \
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;                                      \
+    }
+
+extern "C" {
+
+int xt_moe_route(const RouteParams *p, const XtMailbox *mb, int use_mb, cudaStream_t stream) {
+    if (p->E > MAX_E || p->H % 256 || p->k + p->n_shared > XT_MB_MAX_ROUTES || p->k > 32) return -2;
+    if (use_mb && p->m > XT_MB_MAX_TOKENS) return -3;
+    XtMailbox empty{};
+    moe_route_kernel<<<p->m, ROUTE_THREADS, 0, stream>>>(*p, use_mb ? *mb : empty, use_mb);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int xt_moe_gate_up(const GateUpParams *pp, cudaStream_t stream) {
+    GateUpParams p = *pp;
+    int ch = 0;
+    int lpr = pick_lpr(p.H / 2, &ch);
+    if ((p.fmt == 0 && p.H % 16) || (p.fmt == 1 && p.H % 32)) return -2;
+    XT_GU_CASE(32, 1) XT_GU_CASE(32, 2) XT_GU_CASE(32, 3) XT_GU_CASE(32, 4) XT_GU_CASE(32, 5) XT_GU_CASE(32, 6)
+    XT_GU_CASE(32, 7) XT_GU_CASE(32, 8) XT_GU_CASE(16, 1) XT_GU_CASE(16, 3) XT_GU_CASE(16, 5) XT_GU_CASE(16, 7)
+    XT_GU_CASE(8, 1) XT_GU_CASE(8, 3) XT_GU_CASE(8, 5) XT_GU_CASE(8, 7) XT_GU_CASE(4, 1) XT_GU_CASE(4, 3)
+    XT_GU_CASE(4, 5) XT_GU_CASE(4, 7)
+    return -4;
+}
+
+int xt_moe_down(const DownParams *pp, const XtMailbox *mbp, int use_mb, int m, cudaStream_t stream) {
+    DownParams p = *pp;
+    XtMailbox mb = use_mb ? *mbp : XtMailbox{};
+    int ch = 0;
+    int lpr = pick_lpr(p.I / 2, &ch);
+    if (p.kk > XT_MB_MAX_ROUTES) return -2;
+    XT_DN_CASE(32, 1, 4) XT_DN_CASE(32, 2, 4) XT_DN_CASE(32, 3, 2) XT_DN_CASE(32, 4, 2) XT_DN_CASE(32, 5, 2)
+    XT_DN_CASE(32, 6, 1) XT_DN_CASE(32, 7, 1) XT_DN_CASE(32, 8, 1) XT_DN_CASE(16, 1, 2) XT_DN_CASE(16, 3, 1)
+    XT_DN_CASE(16, 5, 1) XT_DN_CASE(16, 7, 1) XT_DN_CASE(8, 1, 1) XT_DN_CASE(8, 3, 1) XT_DN_CASE(8, 5, 1)
+    XT_DN_CASE(8, 7, 1) XT_DN_CASE(4, 1, 1) XT_DN_CASE(4, 3, 1) XT_DN_CASE(4, 5, 1) XT_DN_CASE(4, 7, 1)
+    return -4;
+}
+
+}  // extern "C"

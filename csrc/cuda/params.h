@@ -1,0 +1,85 @@
+// Launch parameters of the sm_100a kernels and their C launchers: shared by the .cu files and the torch bindings.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../include/xt_mailbox.h"
+
+namespace xt {
+
+struct RouteParams {
+    const __nv_bfloat16 *x;   // [m, H]
+    const __nv_bfloat16 *wr;  // [E, H] router weight
+    const float *bias;        // [E] added to the logits before selection (may be null)
+    const float *corr;        // [E] grouped mode: selection bias (e_score_correction_bias), may be null
+    const int32_t *table;     // [E] residency: slot or -1 (null: expert id == slot, everything on the GPU)
+    const int32_t *shared_slots;   // [n_shared]
+    int32_t *ids;             // [m, kk] original expert ids (-1 for shared)
+    float *w;                 // [m, kk]
+    int32_t *slots;           // [m, kk] GPU slot or -1
+    int m, H, E, k, n_shared, mode, n_group, topk_group, renorm, layer;
+    float scale;
+};
+
+struct GateUpParams {
+    const __nv_bfloat16 *x;   // [m, H]
+    const int32_t *slots;     // [m, kk]
+    const uint8_t *w13;       // [S, 2I, H/2]
+    const uint8_t *s13;       // [S, 2I, H/bs]
+    const float *g13;         // [S, 2]
+    float *mid;               // [m*kk, I] fp32
+    int routes, kk, H, I, fmt;
+    float limit, alpha, beta;
+};
+
+struct DownParams {
+    const float *mid;         // [m*kk, I]
+    const int32_t *slots;     // [m, kk]
+    const float *w;           // [m, kk]
+    const uint8_t *w2;        // [S, H, I/2]
+    const uint8_t *s2;        // [S, H, I/bs]
+    const float *g2;          // [S]
+    const __nv_bfloat16 *add; // [m, H] optional extra term (e.g. a shared expert computed elsewhere), may be null
+    __nv_bfloat16 *out;       // [m, H]
+    float *out_f32;           // [m, H] optional FP32 copy of the GPU part (tests), may be null
+    int kk, H, I, fmt;
+};
+
+struct RopeParams {
+    const __nv_bfloat16 *qkv;   // [T, (Hq + 2 Hkv) * D]
+    const __nv_bfloat16 *qn;    // [D] or null
+    const __nv_bfloat16 *kn;    // [D] or null
+    const int32_t *pos;         // [T]
+    const int32_t *batch;       // [T] cache row of each token
+    __nv_bfloat16 *q;           // [T, Hq, D]
+    __nv_bfloat16 *kc, *vc;     // [B, Hkv, L, D]
+    int T, Hq, Hkv, D, L;
+    float theta, eps;
+};
+
+struct AttnDecodeParams {
+    const __nv_bfloat16 *q;     // [B, Hq, D]
+    const __nv_bfloat16 *kc;    // [B, Hkv, L, D]
+    const __nv_bfloat16 *vc;
+    const int32_t *seqlens;     // [B] keys to attend (including the current token)
+    __nv_bfloat16 *out;         // [B, Hq, D]
+    float *ws_o;                // [B, Hkv, S, G, D]
+    float *ws_ml;               // [B, Hkv, S, G, 2]
+    uint32_t *counters;         // [B, Hkv], zero before the first launch; the merging CTA resets its entry
+    int Hq, Hkv, L, splits;
+    float scale_log2;           // softmax scale * log2(e)
+};
+
+}  // namespace xt
+
+extern "C" {
+int xt_add_rmsnorm(const void *x, void *residual, const void *w, void *out, int T, int H, float eps,
+                   cudaStream_t stream);
+int xt_qk_norm_rope_kv(const xt::RopeParams *p, cudaStream_t stream);
+int xt_attn_decode(const xt::AttnDecodeParams *p, int B, cudaStream_t stream);
+int xt_moe_route(const xt::RouteParams *p, const XtMailbox *mb, int use_mb, cudaStream_t stream);
+int xt_moe_gate_up(const xt::GateUpParams *p, cudaStream_t stream);
+int xt_moe_down(const xt::DownParams *p, const XtMailbox *mb, int use_mb, int m, cudaStream_t stream);
+}

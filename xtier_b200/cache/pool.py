@@ -1,0 +1,186 @@
+"""Tiered MoE layer: GPU hot-expert slots + CPU engine for the rest, in the same call.
+
+`TieredMoE` owns one layer's router, a GPU slot pool holding `len(hot)` routed experts (plus the shared experts, which
+always live on the GPU) in the checkpoint's FP4 layout, the residency table expert -> slot (-1: CPU), and a CPU engine
+holding every routed expert. A decode call (<= 16 tokens) runs three kernels (csrc/cuda/moe_decode.cu): route+split
+(publishing the CPU part to the mailbox), gate/up on the hot slots, down + route-ordered combine with the CPU result.
+Prefill calls (more tokens) run the GPU part while a host thread runs the CPU engine on the other routes
+(hybrid prefill), then add the two.
+
+The residency table is device memory read at replay time, so swapping a slot's expert needs no graph recapture:
+`swap()` unpublishes the victim, copies the new expert's bytes into the slot and publishes it, all on the compute
+stream, so a replay never reads a slot in flight.
+
+Reference parity: xtier/cache/pool.py:1-43 (decode split, residency tables, adaptive swaps), :418-589 (LayerPool),
+xtier/cache/prefill.py:154 (hybrid prefill), xtier/backend/method.py:320-421 (per-call dispatch).
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from .. import ops
+from ..formats import MXFP4, NVFP4, ExpertWeights
+
+MAX_DECODE_TOKENS = 16
+
+
+class TieredMoE:
+    def __init__(self, layer: int, router_w: torch.Tensor, experts: ExpertWeights, top_k: int,
+                 hot: list[int] | None = None, shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1,
+                 topk_group: int = 1, renorm: bool = True, scale: float = 1.0, router_bias: torch.Tensor | None = None,
+                 corr_bias: torch.Tensor | None = None, limit: float = 0.0, mailbox=None, engine=None,
+                 device='cuda', max_tokens: int = MAX_DECODE_TOKENS, host_experts: ExpertWeights | None = None):
+        self.layer = layer
+        self.device = torch.device(device)
+        self.E, self.H, self.I = experts.experts, experts.hidden, experts.inter
+        self.fmt = experts.fmt
+        self.fmt_code = 0 if self.fmt == NVFP4 else 1
+        self.k = top_k
+        self.mode, self.n_group, self.topk_group, self.renorm, self.scale = mode, n_group, topk_group, renorm, scale
+        self.limit = limit
+        self.router_w = router_w.to(self.device, torch.bfloat16).contiguous()
+        self.router_bias = None if router_bias is None else router_bias.to(self.device, torch.float32).contiguous()
+        self.corr_bias = None if corr_bias is None else corr_bias.to(self.device, torch.float32).contiguous()
+        self.hot = list(range(self.E)) if hot is None else list(hot)
+        self.n_shared = 0 if shared is None else shared.experts
+        S = len(self.hot)
+        # host copy of every routed expert: the source of swaps (None: the residency is fixed)
+        self.host = host_experts
+        src = experts
+        parts = []
+        if S:
+            parts.append(src.select(torch.tensor(self.hot, device=src.w13.device)).to(self.device))
+        if shared is not None:
+            parts.append(shared.to(self.device))
+        if parts:
+            self.pool = ExpertWeights(self.fmt, *[torch.cat([getattr(p, f) for p in parts]).contiguous()
+                                                  for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
+            self.pool.g13 = self.pool.g13.float().contiguous()
+            self.pool.g2 = self.pool.g2.float().contiguous()
+        else:
+            self.pool = None
+        table = torch.full((self.E,), -1, dtype=torch.int32)
+        for s, e in enumerate(self.hot):
+            table[e] = s
+        self.table = table.to(self.device)
+        self.table_host = table.clone()
+        self.shared_slots = (torch.arange(S, S + self.n_shared, dtype=torch.int32, device=self.device)
+                             if self.n_shared else None)
+        self.engine = engine
+        self.mailbox = mailbox if (engine is not None and S < self.E) else None
+        if self.mailbox is not None:
+            self.mailbox.register(layer, engine)
+        self.kk = self.k + self.n_shared
+        self._alloc(max_tokens)
+
+    def _alloc(self, m: int):
+        self.max_m = m
+        dev = self.device
+        self.ids = torch.empty(m, self.kk, dtype=torch.int32, device=dev)
+        self.w = torch.empty(m, self.kk, dtype=torch.float32, device=dev)
+        self.slots = torch.empty(m, self.kk, dtype=torch.int32, device=dev)
+        self.mid = torch.empty(m * self.kk, self.I, dtype=torch.float32, device=dev)
+
+    @property
+    def all_hot(self) -> bool:
+        return len(self.hot) == self.E
+
+    # ------------------------------------------------------------------ decode (graph capturable)
+    def route(self, x: torch.Tensor, use_mailbox: bool):
+        m = x.shape[0]
+        ops.moe_route(x, self.router_w, self.router_bias, self.corr_bias,
+                      None if self.all_hot else self.table, self.shared_slots,
+                      self.ids[:m], self.w[:m], self.slots[:m], self.k, self.mode, self.n_group, self.topk_group,
+                      self.renorm, self.scale, self.layer,
+                      self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0)
+
+    def experts_gpu(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None, use_mailbox: bool,
+                    out_f32: torch.Tensor | None = None):
+        m = x.shape[0]
+        if self.pool is not None:
+            ops.moe_gate_up(x, self.slots[:m], self.pool.w13, self.pool.s13, self.pool.g13, self.mid[:m * self.kk],
+                            self.fmt_code, self.limit)
+            ops.moe_down(self.mid[:m * self.kk], self.slots[:m], self.w[:m], self.pool.w2, self.pool.s2, self.pool.g2,
+                         add, out, out_f32, self.fmt_code,
+                         self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0)
+        else:   # no GPU slots at all: every route on the CPU
+            raise NotImplementedError('a layer without GPU slots needs at least the shared/hot pool')
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None):
+        """x bf16 [m, H] -> out bf16 [m, H] (= MoE(x) + add)."""
+        m = x.shape[0]
+        out = torch.empty_like(x) if out is None else out
+        if m <= MAX_DECODE_TOKENS and m <= self.max_m:
+            use_mb = self.mailbox is not None
+            self.route(x, use_mb)
+            self.experts_gpu(x, out, add, use_mb)
+            return out
+        return self.prefill(x, out, add)
+
+    # ------------------------------------------------------------------ prefill (hybrid: GPU hot || CPU rest)
+    def prefill(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None = None, chunk: int = 1024):
+        for s in range(0, x.shape[0], chunk):
+            e = min(x.shape[0], s + chunk)
+            self._prefill_chunk(x[s:e], out[s:e], None if add is None else add[s:e])
+        return out
+
+    def _prefill_chunk(self, x, out, add):
+        m = x.shape[0]
+        if m > self.max_m:
+            self._alloc(max(m, self.max_m))
+        self.route(x, False)
+        cpu_thread = None
+        cpu_out = None
+        if not self.all_hot and self.engine is not None:
+            ids = self.ids[:m, :self.k]
+            slots = self.slots[:m, :self.k]
+            cpu_ids = torch.where(slots < 0, ids, torch.full_like(ids, -1)).cpu()
+            w = self.w[:m, :self.k].float().cpu()
+            xc = x.cpu()
+            cpu_out = torch.empty(m, self.H, dtype=torch.float32).pin_memory()
+            box = {}
+
+            def run():
+                try:
+                    self.engine.forward(xc, cpu_ids, w, out=cpu_out)
+                except Exception as ex:   # re-raised on the caller's thread
+                    box['err'] = ex
+
+            cpu_thread = threading.Thread(target=run, daemon=True)
+            cpu_thread.start()
+        gpu = torch.empty(m, self.H, dtype=torch.float32, device=self.device)
+        self.experts_gpu(x, out, add, False, out_f32=gpu)
+        if cpu_thread is not None:
+            cpu_thread.join()
+            if 'err' in box:
+                raise box['err']
+            total = gpu + cpu_out.to(self.device, non_blocking=True)
+            if add is not None:
+                total += add.float()
+            out.copy_(total.to(out.dtype))
+        return out
+
+    # ------------------------------------------------------------------ residency changes
+    def swap(self, incoming: int, victim: int):
+        """Replaces hot expert `victim` by `incoming` (stream-ordered with every kernel launched so far/after)."""
+        slot = int(self.table_host[victim])
+        if slot < 0 or int(self.table_host[incoming]) >= 0:
+            raise ValueError(f'swap {incoming} <- {victim}: bad residency')
+        self.table[victim] = -1
+        self.table_host[victim] = -1
+        for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+            getattr(self.pool, f)[slot].copy_(getattr(self.host, f)[incoming], non_blocking=True)
+        self.table[incoming] = slot
+        self.table_host[incoming] = slot
+        self.hot[slot] = incoming
+
+    def resident(self) -> list[int]:
+        return list(self.hot)
+
+    def gpu_bytes(self) -> int:
+        if self.pool is None:
+            return 0
+        return sum(getattr(self.pool, f).numel() * getattr(self.pool, f).element_size()
+                   for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'))

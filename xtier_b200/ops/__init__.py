@@ -1,0 +1,84 @@
+"""Python entry to the sm_100a kernels (libxt_cuda.so, registered as torch.ops.xtier.*).
+
+The library is built in-tree (xtier_b200/_build.py) and loaded once. On a machine with a CUDA device a missing or
+unloadable library is an error, never a silent fallback: every op here runs the native kernel or raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import torch
+
+_LIB = Path(__file__).resolve().parent.parent / '_lib' / 'libxt_cuda.so'
+_loaded = False
+_cdll = None
+
+
+def lib_path() -> Path:
+    return _LIB
+
+
+def load():
+    """Loads the op library (building it first if it is missing)."""
+    global _loaded, _cdll
+    if _loaded:
+        return
+    if not _LIB.exists():
+        from .. import _build
+        _build.build(verbose=False)
+    if not _LIB.exists():
+        raise RuntimeError(f'xtier_b200: {_LIB} is missing; run python -m xtier_b200._build')
+    torch.ops.load_library(str(_LIB))
+    _cdll = C.CDLL(str(_LIB))
+    _loaded = True
+
+
+def cdll():
+    load()
+    return _cdll
+
+
+def _ops():
+    load()
+    return torch.ops.xtier
+
+
+def add_rmsnorm(x, residual, w, out, eps: float):
+    _ops().add_rmsnorm(x, residual, w, out, eps)
+    return out
+
+
+def rmsnorm(x, w, eps: float, out=None):
+    out = torch.empty_like(x) if out is None else out
+    _ops().add_rmsnorm(x, None, w, out, eps)
+    return out
+
+
+def qk_norm_rope_kv(qkv, q_norm, k_norm, pos, batch, q_out, k_cache, v_cache, hq: int, hkv: int, theta: float,
+                    eps: float):
+    _ops().qk_norm_rope_kv(qkv, q_norm, k_norm, pos, batch, q_out, k_cache, v_cache, hq, hkv, theta, eps)
+
+
+def attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits: int, scale: float):
+    _ops().attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits, scale)
+
+
+def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, k: int, mode: int = 0, n_group: int = 1,
+              topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0, mailbox: int = 0):
+    _ops().moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, k, mode, n_group, topk_group, renorm,
+                     scale, layer, mailbox)
+
+
+def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0):
+    _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta)
+
+
+def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0):
+    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, fmt, mailbox)
+
+
+def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
+    """Key splits of the decode attention: enough CTAs to cover the SMs twice, at least 64 keys per split."""
+    want = max(1, (2 * sms + batch * kv_heads - 1) // (batch * kv_heads))
+    return max(1, min(64, want, (max_len + 63) // 64))

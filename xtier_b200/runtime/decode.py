@@ -1,0 +1,106 @@
+"""Decode runtime: KV state, CUDA-graph capture of one decode step, and the public `generate` API.
+
+A decode step (all layers, the mailbox round trips to the CPU engine included) is captured once into a CUDA graph and
+replayed per token. Inside the graph the step also advances itself (next token -> input, position + 1), so a
+device-timed loop is pure replays. `generate()` is the end-to-end path a user calls: per step it copies the input
+token from pinned host memory, replays the graph and reads the next token back to the host.
+
+Reference parity: the reference relies on SGLang's CUDA-graph runner and scheduler; this is the
+framework's own minimal runner for the named configs.
+"""
+from __future__ import annotations
+
+import torch
+
+
+class Generator:
+    def __init__(self, model, batch: int = 1, max_len: int = 4096, use_graph: bool = True):
+        self.model = model
+        self.batch = batch
+        self.max_len = max_len
+        self.state = model.alloc_state(batch, max_len)
+        self.buf = model.decode_buffers(batch)
+        self.use_graph = use_graph
+        self.graph = None
+        self.host_tokens = torch.zeros(batch, dtype=torch.int64).pin_memory()
+        self.host_next = torch.zeros(batch, dtype=torch.int64).pin_memory()
+
+    # ------------------------------------------------------------------ steps
+    def _step_body(self):
+        self.model.decode_step(self.state, self.buf)
+        self.buf['tokens'].copy_(self.buf['next'])
+        self.buf['pos'].add_(1)
+
+    def capture(self, warmup: int = 2):
+        """Captures one self-advancing decode step. Warm-up runs rewrite the current position only."""
+        pos0 = self.buf['pos'].clone()
+        tok0 = self.buf['tokens'].clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.model.decode_step(self.state, self.buf)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step_body()
+        torch.cuda.synchronize()
+        self.buf['pos'].copy_(pos0)
+        self.buf['tokens'].copy_(tok0)
+        self.check()
+
+    def step(self):
+        """One decode step on the device (no host synchronization)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step_body()
+
+    def check(self):
+        mb = getattr(self.model, 'mailbox', None)
+        if mb is not None:
+            mb.check()
+
+    # ------------------------------------------------------------------ public API
+    def prefill(self, prompts: torch.Tensor):
+        """prompts [batch, T] token ids (host or device): fills the KV cache, sets the first decode input."""
+        prompts = torch.as_tensor(prompts)
+        first = []
+        for b in range(self.batch):
+            first.append(self.model.prefill(self.state, prompts[b].to(self.model.device), row=b))
+        T = prompts.shape[1]
+        self.buf['tokens'].copy_(torch.cat(first).view(-1))
+        self.buf['pos'].fill_(T)
+        torch.cuda.synchronize()
+        self.check()
+
+    def generate(self, prompts: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+        """Greedy generation: [batch, T] prompt ids -> [batch, max_new_tokens] new ids (host tensor)."""
+        self.prefill(prompts)
+        if self.use_graph and self.graph is None:
+            self.capture()
+        out = torch.empty(self.batch, max_new_tokens, dtype=torch.int64)
+        self.host_tokens.copy_(self.buf['tokens'].cpu())
+        for i in range(max_new_tokens):
+            self.decode_one()
+            out[:, i] = self.host_next
+        self.check()
+        return out
+
+    def decode_one(self):
+        """End-to-end step: H2D copy of the input token from pinned memory, replay, D2H read of the next token."""
+        self.buf['tokens'].copy_(self.host_tokens, non_blocking=True)
+        self.step()
+        self.host_next.copy_(self.buf['next'], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        self.host_tokens.copy_(self.host_next)
+        return self.host_next
+
+    @property
+    def h2d_bytes_per_step(self) -> int:
+        return self.host_tokens.numel() * self.host_tokens.element_size()
+
+    @property
+    def d2h_bytes_per_step(self) -> int:
+        return self.host_next.numel() * self.host_next.element_size()
