@@ -126,7 +126,8 @@ def main():
     mine = cpus[local * per:(local + 1) * per] if world > 1 else cpus
     os.sched_setaffinity(0, mine)
     threads = args.threads or max(1, len(mine) - 2)
-    os.environ['XTIER_DISPATCH_CPU'] = str(mine[-1])
+    os.environ["XTIER_DISPATCH_CPU"] = str(mine[-1])
+    os.environ.setdefault("XTIER_SPIN_US", "5000")   # decode calls come every few hundred microseconds: keep workers hot
     torch.set_num_threads(1)
 
     from xtier_b200.engine.mailbox import Mailbox

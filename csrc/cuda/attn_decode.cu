@@ -2,9 +2,9 @@
 //
 // Grid (splits, Hkv, B), 4 warps. A CTA takes the G = Hq/Hkv query heads of one KV head and a contiguous key range,
 // walked in tiles of 128 keys with an online softmax:
-//   scores  each warp takes 32 keys; per key every lane loads 4 dims of K (8 bytes, the warp reads the 256-byte row
-//           once), forms G partial dots, and a butterfly reduce-scatter over the lanes (log2(32) + log2(G) shuffles
-//           instead of 5 G) leaves each head's full dot on a group of lanes, which writes it to shared memory.
+//   scores  each warp takes 32 keys, one per lane: the lane loads its key's 256-byte row (16 independent 16-byte
+//           loads in flight) and forms the G head dots against the pre-scaled queries in shared memory (broadcast
+//           reads), so no cross-lane reduction is needed.
 //   softmax one warp per head: tile max, running max and sum, exp2 in place.
 //   values  lane l accumulates dims 4l..4l+3 of all G heads; the probabilities are read from shared memory as
 //           [key][head] so G heads of one key are one or two vector loads.
@@ -23,39 +23,6 @@ constexpr int AD_TILE = 32 * AD_WARPS;
 constexpr int AD_D = 128;
 
 
-// reduce-scatter of G per-lane values: afterwards every lane holds the full (32-lane) sum of value index
-// head_of(lane), where head_of(lane) takes log2(G) lane bits from the top (bit 4 first)
-template <int G>
-XT_DEV float butterfly(float (&v)[G], int lane) {
-    int cnt = G;
-    int o = 16;
-#pragma unroll
-    for (int step = 0; (1 << step) < G; ++step) {
-        const int half = cnt / 2;
-        const bool upper = lane & o;
-#pragma unroll
-        for (int i = 0; i < G / 2; ++i) {
-            if (i < half) {
-                float send = upper ? v[i] : v[i + half];
-                float keep = upper ? v[i + half] : v[i];
-                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        }
-        cnt = half;
-        o >>= 1;
-    }
-    float r = v[0];
-    for (; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-    return r;
-}
-
-template <int G>
-XT_DEV int head_of(int lane) {
-    int h = 0, o = 16;
-    for (int g = G; g > 1; g >>= 1, o >>= 1) h = h * 2 + ((lane & o) ? 1 : 0);
-    return h;
-}
-
 template <int G>
 __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodeParams p) {
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -65,27 +32,20 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     chunk = (chunk + 31) & ~31;
     const int k_begin = split * chunk, k_end = min(N, k_begin + chunk);
 
-    __shared__ float S[AD_TILE][G];
+    // the score tile and the final cross-warp reduction never live at the same time: one buffer holds either
+    __shared__ __align__(16) float buf[AD_WARPS * G * AD_D];
+    float(&S)[AD_TILE][G] = *reinterpret_cast<float(*)[AD_TILE][G]>(buf);
+    float(&red)[AD_WARPS][G][AD_D] = *reinterpret_cast<float(*)[AD_WARPS][G][AD_D]>(buf);
+    __shared__ __align__(16) float qs[G][AD_D];
     __shared__ float m_run[G], l_run[G], alpha[G];
-    __shared__ float red[AD_WARPS][G][AD_D];
 
-    // this lane's 4 dims of every head's query, pre-scaled
-    float qr[G][4];
     const __nv_bfloat16 *qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * G) * AD_D;
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-        uint2 u = *reinterpret_cast<const uint2 *>(qb + h * AD_D + lane * 4);
-        const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&u);
-        float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
-        qr[h][0] = f0.x * p.scale_log2;
-        qr[h][1] = f0.y * p.scale_log2;
-        qr[h][2] = f1.x * p.scale_log2;
-        qr[h][3] = f1.y * p.scale_log2;
-    }
+    for (int i = threadIdx.x; i < G * AD_D; i += blockDim.x) qs[i / AD_D][i % AD_D] = __bfloat162float(qb[i]) * p.scale_log2;
     if (threadIdx.x < G) {
         m_run[threadIdx.x] = -INFINITY;
         l_run[threadIdx.x] = 0.f;
     }
+    __syncthreads();
     float acc[G][4];
 #pragma unroll
     for (int h = 0; h < G; ++h)
@@ -95,27 +55,39 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     const size_t head_off = (size_t(b) * p.Hkv + kvh) * p.L;
     const __nv_bfloat16 *K = p.kc + head_off * AD_D;
     const __nv_bfloat16 *V = p.vc + head_off * AD_D;
-    const int my_head = head_of<G>(lane);
-    constexpr int LANES_PER_HEAD = 32 / G;
 
     for (int t0 = k_begin; t0 < k_end; t0 += AD_TILE) {
-        // ---- scores of this warp's 32 keys
-#pragma unroll 4
-        for (int i = 0; i < 32; ++i) {
-            const int key = t0 + warp * 32 + i;
-            float v[G];
-            if (key < k_end) {
-                uint2 u = *reinterpret_cast<const uint2 *>(K + size_t(key) * AD_D + lane * 4);
-                const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&u);
-                float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
+        // ---- scores: lane = key
+        {
+            const int key = t0 + warp * 32 + lane;
+            const bool valid = key < k_end;
+            const uint4 *kr = reinterpret_cast<const uint4 *>(K + size_t(valid ? key : k_begin) * AD_D);
+            uint4 kv[AD_D / 8];
 #pragma unroll
-                for (int h = 0; h < G; ++h) v[h] = qr[h][0] * f0.x + qr[h][1] * f0.y + qr[h][2] * f1.x + qr[h][3] * f1.y;
-            } else {
+            for (int c = 0; c < AD_D / 8; ++c) kv[c] = kr[c];
+            float s[G];
 #pragma unroll
-                for (int h = 0; h < G; ++h) v[h] = 0.f;
+            for (int h = 0; h < G; ++h) s[h] = 0.f;
+#pragma unroll
+            for (int c = 0; c < AD_D / 8; ++c) {
+                const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&kv[c]);
+                float kf[8];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float2 f = __bfloat1622float2(k2[i]);
+                    kf[2 * i] = f.x;
+                    kf[2 * i + 1] = f.y;
+                }
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float4 q0 = *reinterpret_cast<const float4 *>(&qs[h][c * 8]);
+                    const float4 q1 = *reinterpret_cast<const float4 *>(&qs[h][c * 8 + 4]);
+                    s[h] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
+                            q1.z * kf[6] + q1.w * kf[7];
+                }
             }
-            float s = butterfly<G>(v, lane);
-            if ((lane % LANES_PER_HEAD) == 0) S[warp * 32 + i][my_head] = key < k_end ? s : -INFINITY;
+#pragma unroll
+            for (int h = 0; h < G; ++h) S[warp * 32 + lane][h] = valid ? s[h] : -INFINITY;
         }
         __syncthreads();
         // ---- online softmax per head
@@ -140,27 +112,34 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
             }
         }
         __syncthreads();
-        // ---- values
+        // ---- values: lane owns dims 4l..4l+3, the warp walks its 32 keys eight at a time
 #pragma unroll
         for (int h = 0; h < G; ++h) {
             const float a = alpha[h];
 #pragma unroll
             for (int d = 0; d < 4; ++d) acc[h][d] *= a;
         }
-#pragma unroll 4
-        for (int i = 0; i < 32; ++i) {
-            const int key = t0 + warp * 32 + i;
-            if (key >= k_end) break;
-            uint2 u = *reinterpret_cast<const uint2 *>(V + size_t(key) * AD_D + lane * 4);
-            const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&u);
-            float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
+        const int nk = min(32, k_end - (t0 + warp * 32));
+        for (int i0 = 0; i0 < nk; i0 += 8) {
+            uint2 vv[8];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float pr = S[warp * 32 + i][h];
-                acc[h][0] += pr * f0.x;
-                acc[h][1] += pr * f0.y;
-                acc[h][2] += pr * f1.x;
-                acc[h][3] += pr * f1.y;
+            for (int i = 0; i < 8; ++i) {
+                const int key = t0 + warp * 32 + min(i0 + i, nk - 1);
+                vv[i] = *reinterpret_cast<const uint2 *>(V + size_t(key) * AD_D + lane * 4);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (i0 + i >= nk) break;
+                const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&vv[i]);
+                float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float pr = S[warp * 32 + i0 + i][h];
+                    acc[h][0] += pr * f0.x;
+                    acc[h][1] += pr * f0.y;
+                    acc[h][2] += pr * f1.x;
+                    acc[h][3] += pr * f1.y;
+                }
             }
         }
         __syncthreads();

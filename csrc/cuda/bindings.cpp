@@ -114,8 +114,9 @@ void attn_decode(const Tensor &q, const Tensor &kc, const Tensor &vc, const Tens
 
 void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &bias, const std::optional<Tensor> &corr,
                const std::optional<Tensor> &table, const std::optional<Tensor> &shared_slots, const Tensor &ids,
-               const Tensor &w, const Tensor &slots, int64_t k, int64_t mode, int64_t n_group, int64_t topk_group,
-               bool renorm, double scale, int64_t layer, int64_t mailbox) {
+               const Tensor &w, const Tensor &slots, const Tensor &ws_logits, const Tensor &ws_count, int64_t k,
+               int64_t mode, int64_t n_group, int64_t topk_group, bool renorm, double scale, int64_t layer,
+               int64_t mailbox) {
     cuda_contig(x, "x");
     cuda_contig(wr, "router weight");
     RouteParams p{};
@@ -128,6 +129,8 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
     p.ids = ptr<int32_t>(ids);
     p.w = ptr<float>(w);
     p.slots = ptr<int32_t>(slots);
+    p.ws_logits = ptr<float>(ws_logits);
+    p.ws_count = ptr<uint32_t>(ws_count);
     p.m = int(x.size(0));
     p.H = int(x.size(1));
     p.E = int(wr.size(0));
@@ -141,6 +144,7 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
     p.layer = int(layer);
     check(ids.numel() >= int64_t(p.m) * (p.k + p.n_shared), "ids too small");
     check(p.k <= p.E, "k > experts");
+    check(ws_logits.numel() >= int64_t(p.m) * p.E && ws_count.numel() >= p.m, "router scratch too small");
     XtMailbox mb = mailbox_view(mailbox);
     c10::cuda::CUDAGuard g(x.device());
     check_rc(xt_moe_route(&p, &mb, mailbox != 0, stream()), "moe_route");
@@ -196,6 +200,17 @@ void moe_down(const Tensor &mid, const Tensor &slots, const Tensor &w, const Ten
     check_rc(xt_moe_down(&p, &mb, mailbox != 0, m, stream()), "moe_down");
 }
 
+void gemv(const Tensor &x, const Tensor &w, const std::optional<Tensor> &add, const Tensor &out) {
+    cuda_contig(x, "x");
+    cuda_contig(w, "w");
+    cuda_contig(out, "out");
+    check(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemv wants bf16");
+    const int K = int(x.size(-1)), m = int(x.numel() / K), N = int(w.size(0));
+    check(w.size(1) == K && out.numel() == int64_t(m) * N, "gemv shapes");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_gemv_bf16(x.data_ptr(), w.data_ptr(), optr<void>(add), out.data_ptr(), m, N, K, stream()), "gemv");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(xtier, m) {
@@ -205,8 +220,9 @@ TORCH_LIBRARY(xtier, m) {
     m.def("attn_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seqlens, Tensor(a!) out, Tensor(b!) ws_o, "
           "Tensor(c!) ws_ml, Tensor(d!) counters, int splits, float scale) -> ()");
     m.def("moe_route(Tensor x, Tensor wr, Tensor? bias, Tensor? corr, Tensor? table, Tensor? shared_slots, "
-          "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, int k, int mode, int n_group, int topk_group, bool renorm, "
-          "float scale, int layer, int mailbox) -> ()");
+          "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, Tensor(d!) ws_logits, Tensor(e!) ws_count, int k, int mode, "
+          "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox) -> ()");
+    m.def("gemv(Tensor x, Tensor w, Tensor? add, Tensor(a!) out) -> ()");
     m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
           "float limit, float alpha, float beta) -> ()");
     m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
@@ -220,4 +236,5 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("moe_route", &moe_route);
     m.impl("moe_gate_up", &moe_gate_up);
     m.impl("moe_down", &moe_down);
+    m.impl("gemv", &gemv);
 }

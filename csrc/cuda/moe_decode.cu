@@ -26,37 +26,60 @@ namespace xt {
 
 
 constexpr int ROUTE_THREADS = 256;
+constexpr int ROUTE_WARPS = ROUTE_THREADS / 32;   // one expert row per warp in phase A
 constexpr int MAX_E = 512;
 
+// Phase A (every CTA): logits of ROUTE_WARPS experts of token blockIdx.y, one warp per expert, all of a row's 16-byte
+// loads in flight at once (H <= 8192). Phase B (the last CTA of the token to finish): selection, split and mailbox.
 __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p, XtMailbox mb, int use_mb) {
     __shared__ float logits[MAX_E];
     __shared__ float sel[MAX_E];
     __shared__ int chosen[XT_MB_MAX_ROUTES];
     __shared__ float chosen_w[XT_MB_MAX_ROUTES];
     __shared__ int any_cpu;
-    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ bool last_cta;
+    const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kk = p.k + p.n_shared;
     const __nv_bfloat16 *xt = p.x + size_t(t) * p.H;
-    if (tid == 0) any_cpu = 0;
-
-    // logits: one warp per expert row, 16-byte loads (H % 256 == 0 checked on the host)
-    for (int e = warp; e < p.E; e += ROUTE_THREADS / 32) {
-        const __nv_bfloat16 *we = p.wr + size_t(e) * p.H;
-        float acc = 0.f;
-        for (int c = lane * 8; c < p.H; c += 256) {
-            uint4 a = *reinterpret_cast<const uint4 *>(xt + c);
-            uint4 b = *reinterpret_cast<const uint4 *>(we + c);
-            const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
-            const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&b);
+    {
+        const int e = blockIdx.x * ROUTE_WARPS + warp;
+        if (e < p.E) {
+            const uint4 *we = reinterpret_cast<const uint4 *>(p.wr + size_t(e) * p.H);
+            const uint4 *xv = reinterpret_cast<const uint4 *>(xt);
+            const int chunks = p.H / 8;   // 16-byte chunks, multiple of 32 (H % 256 == 0)
+            uint4 wb[32];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float2 fa = __bfloat1622float2(a2[i]), fb = __bfloat1622float2(b2[i]);
-                acc = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, acc));
+            for (int i = 0; i < 32; ++i)
+                if (i * 32 < chunks) wb[i] = ldg_nc_v4(we + i * 32 + lane);
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if (i * 32 >= chunks) break;
+                const uint4 a = xv[i * 32 + lane];
+                const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
+                const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&wb[i]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float2 fa = __bfloat1622float2(a2[j]), fb = __bfloat1622float2(b2[j]);
+                    acc = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, acc));
+                }
             }
+            acc = warp_sum(acc);
+            if (lane == 0) p.ws_logits[size_t(t) * p.E + e] = acc + (p.bias ? p.bias[e] : 0.f);
         }
-        acc = warp_sum(acc);
-        if (lane == 0) logits[e] = acc + (p.bias ? p.bias[e] : 0.f);
     }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(&p.ws_count[t], 1u);
+        last_cta = prev == gridDim.x - 1;
+        if (last_cta) p.ws_count[t] = 0;   // ready for the next call
+        any_cpu = 0;
+    }
+    __syncthreads();
+    if (!last_cta) return;
+    __threadfence();
+    for (int e = tid; e < p.E; e += ROUTE_THREADS) logits[e] = __ldcg(p.ws_logits + size_t(t) * p.E + e);
     __syncthreads();
 
     if (warp == 0) {
@@ -318,45 +341,55 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams
 }
 
 
-constexpr int DN_WARPS = 4;
-
+// One warp per route of the token (kk <= 16 warps); a CTA owns RPW*U output rows. Each warp loads its route's FP32
+// intermediate slice and all U*CH weight chunks of its rows before any arithmetic; the per-route partial sums meet in
+// shared memory and are added in route order (deterministic), then the CPU part and the optional extra term.
 template <int LPR, int CH, int U>
-__global__ void __launch_bounds__(DN_WARPS * 32) moe_down_kernel(DownParams p, XtMailbox mb, int use_mb) {
-    const int t = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownParams p, XtMailbox mb, int use_mb) {
     constexpr int RPW = 32 / LPR;
+    constexpr int ROWS = RPW * U;
+    static_assert(ROWS % 4 == 0, "the epilogue writes four rows per thread");
+    __shared__ float part[XT_MB_MAX_ROUTES][ROWS];
+    __shared__ int cpu_ok;
+    const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31, j = threadIdx.x >> 5;   // warp j = route j
     const int q = lane % LPR, sub = lane / LPR;
     const int bs = p.fmt == 0 ? 16 : 32;
     const size_t wrow = p.I / 2, srow = p.I / bs;
-    const int rows_per_cta = DN_WARPS * RPW * U;
-    const int h0 = blockIdx.y * rows_per_cta + warp * RPW * U + sub;
-    float acc[U];
+    const int hb = blockIdx.y * ROWS;
+    const int r = t * p.kk + j;
+    const int slot = p.slots[r];
+    if (slot >= 0) {   // warp-uniform
+        const uint8_t *W = p.w2 + size_t(slot) * p.H * wrow;
+        const uint8_t *S = p.s2 + size_t(slot) * p.H * srow;
+        uint4 wv[U][CH];
 #pragma unroll
-    for (int u = 0; u < U; ++u) acc[u] = 0.f;
-    for (int j = 0; j < p.kk; ++j) {
-        const int r = t * p.kk + j;
-        const int slot = p.slots[r];
-        if (slot < 0) continue;
+        for (int u = 0; u < U; ++u) {
+            const int h = min(hb + u * RPW + sub, p.H - 1);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) wv[u][c] = ldg_nc_v4(W + h * wrow + size_t(c * LPR + q) * 16);
+        }
         __half2 xr[CH][16];
         load_x_f32<LPR, CH>(p.mid + size_t(r) * p.I, q, xr);
         const float wt = p.w[r] * p.g2[slot];
-        const uint8_t *W = p.w2 + size_t(slot) * p.H * wrow;
-        const uint8_t *S = p.s2 + size_t(slot) * p.H * srow;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int h = min(h0 + u * RPW, p.H - 1);   // all lanes shuffle; rows past H are dropped below
-            acc[u] += wt * row_dot<LPR, CH>(W + h * wrow, S + h * srow, p.fmt, q, xr);
-        }
-    }
-    // stage the GPU part of this CTA's rows in shared memory
-    __shared__ float part[DN_WARPS * RPW * U];
-    const int hb = blockIdx.y * rows_per_cta;
-    if (q == 0) {
+            const int h = min(hb + u * RPW + sub, p.H - 1);
+            float acc = 0.f;
 #pragma unroll
-        for (int u = 0; u < U; ++u) part[warp * RPW * U + sub + u * RPW] = acc[u];
+            for (int c = 0; c < CH; ++c) {
+                const int chunk = c * LPR + q;
+                const uint8_t *sp = p.fmt == 0 ? S + h * srow + chunk * 2 : S + h * srow + chunk;
+                acc += chunk_dot(wv[u][c], xr[c], sp, p.fmt);
+            }
+            acc = group_sum<LPR>(acc);
+            if (q == 0) part[j][u * RPW + sub] = wt * acc;
+        }
+    } else if (lane < RPW) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) part[j][u * RPW + lane] = 0.f;
     }
     // CPU part: wait for the dispatcher's answer (bounded), then add it
-    __shared__ int cpu_ok;
     if (threadIdx.x == 0) {
         int ok = 0;
         if (use_mb && mb.dev->pending) {
@@ -372,17 +405,20 @@ __global__ void __launch_bounds__(DN_WARPS * 32) moe_down_kernel(DownParams p, X
                     mb.hdr->gpu_error = 1;
                     break;
                 }
-                __nanosleep(256);
+                __nanosleep(128);
             }
         }
         cpu_ok = ok;
     }
     __syncthreads();
     // four rows per thread: one 16-byte read of the CPU result (mapped host memory) per four outputs
-    for (int i = threadIdx.x; i * 4 < rows_per_cta; i += blockDim.x) {
+    for (int i = threadIdx.x; i * 4 < ROWS; i += blockDim.x) {
         const int h = hb + i * 4;
         if (h >= p.H) break;
-        float v[4] = {part[i * 4], part[i * 4 + 1], part[i * 4 + 2], part[i * 4 + 3]};
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int jj = 0; jj < p.kk; ++jj)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] += part[jj][i * 4 + e];
         const size_t o = size_t(t) * p.H + h;
         if (p.out_f32) *reinterpret_cast<float4 *>(p.out_f32 + o) = make_float4(v[0], v[1], v[2], v[3]);
         if (cpu_ok) {
@@ -439,19 +475,21 @@ static int pick_lpr(int row_bytes, int *ch) {
 
 #define XT_DN_CASE(L, C, U)                                                                     \
     if (lpr == L && ch == C) {                                                                  \
-        constexpr int rows = DN_WARPS * (32 / L) * U;                                           \
+        constexpr int rows = (32 / L) * U;                                                      \
         dim3 grid(m, (p.H + rows - 1) / rows);                                                  \
-        moe_down_kernel<L, C, U><<<grid, DN_WARPS * 32, 0, stream>>>(p, mb, use_mb);            \
+        moe_down_kernel<L, C, U><<<grid, 32 * p.kk, 0, stream>>>(p, mb, use_mb);                \
         return cudaGetLastError() == cudaSuccess ? 0 : -1;                                      \
     }
 
 extern "C" {
 
 int xt_moe_route(const RouteParams *p, const XtMailbox *mb, int use_mb, cudaStream_t stream) {
-    if (p->E > MAX_E || p->H % 256 || p->k + p->n_shared > XT_MB_MAX_ROUTES || p->k > 32) return -2;
+    if (p->E > MAX_E || p->H % 256 || p->H > 8192 || p->k + p->n_shared > XT_MB_MAX_ROUTES || p->k > 32) return -2;
     if (use_mb && p->m > XT_MB_MAX_TOKENS) return -3;
+    if (!p->ws_logits || !p->ws_count) return -5;
     XtMailbox empty{};
-    moe_route_kernel<<<p->m, ROUTE_THREADS, 0, stream>>>(*p, use_mb ? *mb : empty, use_mb);
+    dim3 grid((p->E + ROUTE_WARPS - 1) / ROUTE_WARPS, p->m);
+    moe_route_kernel<<<grid, ROUTE_THREADS, 0, stream>>>(*p, use_mb ? *mb : empty, use_mb);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -473,10 +511,10 @@ int xt_moe_down(const DownParams *pp, const XtMailbox *mbp, int use_mb, int m, c
     int ch = 0;
     int lpr = pick_lpr(p.I / 2, &ch);
     if (p.kk > XT_MB_MAX_ROUTES) return -2;
-    XT_DN_CASE(32, 1, 4) XT_DN_CASE(32, 2, 4) XT_DN_CASE(32, 3, 2) XT_DN_CASE(32, 4, 2) XT_DN_CASE(32, 5, 2)
-    XT_DN_CASE(32, 6, 1) XT_DN_CASE(32, 7, 1) XT_DN_CASE(32, 8, 1) XT_DN_CASE(16, 1, 2) XT_DN_CASE(16, 3, 1)
-    XT_DN_CASE(16, 5, 1) XT_DN_CASE(16, 7, 1) XT_DN_CASE(8, 1, 1) XT_DN_CASE(8, 3, 1) XT_DN_CASE(8, 5, 1)
-    XT_DN_CASE(8, 7, 1) XT_DN_CASE(4, 1, 1) XT_DN_CASE(4, 3, 1) XT_DN_CASE(4, 5, 1) XT_DN_CASE(4, 7, 1)
+    XT_DN_CASE(32, 1, 8) XT_DN_CASE(32, 2, 8) XT_DN_CASE(32, 3, 4) XT_DN_CASE(32, 4, 4) XT_DN_CASE(32, 5, 4)
+    XT_DN_CASE(32, 6, 4) XT_DN_CASE(32, 7, 4) XT_DN_CASE(32, 8, 4) XT_DN_CASE(16, 1, 8) XT_DN_CASE(16, 3, 4)
+    XT_DN_CASE(16, 5, 2) XT_DN_CASE(16, 7, 2) XT_DN_CASE(8, 1, 8) XT_DN_CASE(8, 3, 4) XT_DN_CASE(8, 5, 2)
+    XT_DN_CASE(8, 7, 2) XT_DN_CASE(4, 1, 4) XT_DN_CASE(4, 3, 2) XT_DN_CASE(4, 5, 2) XT_DN_CASE(4, 7, 1)
     return -4;
 }
 

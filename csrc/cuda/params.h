@@ -19,6 +19,8 @@ struct RouteParams {
     int32_t *ids;             // [m, kk] original expert ids (-1 for shared)
     float *w;                 // [m, kk]
     int32_t *slots;           // [m, kk] GPU slot or -1
+    float *ws_logits;         // [m, E] scratch: router logits of the call
+    uint32_t *ws_count;       // [m] scratch: CTAs done per token (zero before the first call; reset by the kernel)
     int m, H, E, k, n_shared, mode, n_group, topk_group, renorm, layer;
     float scale;
 };
@@ -82,4 +84,5 @@ int xt_attn_decode(const xt::AttnDecodeParams *p, int B, cudaStream_t stream);
 int xt_moe_route(const xt::RouteParams *p, const XtMailbox *mb, int use_mb, cudaStream_t stream);
 int xt_moe_gate_up(const xt::GateUpParams *p, cudaStream_t stream);
 int xt_moe_down(const xt::DownParams *p, const XtMailbox *mb, int use_mb, int m, cudaStream_t stream);
+int xt_gemv_bf16(const void *x, const void *W, const void *add, void *y, int m, int N, int K, cudaStream_t stream);
 }

@@ -82,6 +82,8 @@ class TieredMoE:
         self.w = torch.empty(m, self.kk, dtype=torch.float32, device=dev)
         self.slots = torch.empty(m, self.kk, dtype=torch.int32, device=dev)
         self.mid = torch.empty(m * self.kk, self.I, dtype=torch.float32, device=dev)
+        self.ws_logits = torch.empty(m, self.E, dtype=torch.float32, device=dev)
+        self.ws_count = torch.zeros(m, dtype=torch.int32, device=dev)
 
     @property
     def all_hot(self) -> bool:
@@ -92,9 +94,9 @@ class TieredMoE:
         m = x.shape[0]
         ops.moe_route(x, self.router_w, self.router_bias, self.corr_bias,
                       None if self.all_hot else self.table, self.shared_slots,
-                      self.ids[:m], self.w[:m], self.slots[:m], self.k, self.mode, self.n_group, self.topk_group,
-                      self.renorm, self.scale, self.layer,
-                      self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0)
+                      self.ids[:m], self.w[:m], self.slots[:m], self.ws_logits, self.ws_count, self.k, self.mode,
+                      self.n_group, self.topk_group,
+                      self.renorm, self.scale, self.layer, self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0)
 
     def experts_gpu(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None, use_mailbox: bool,
                     out_f32: torch.Tensor | None = None):

@@ -43,13 +43,33 @@ class Qwen3MoeConfig:
         return Qwen3MoeConfig(**base)
 
 
-def zipf_bias(E: int, s: float, gen: torch.Generator) -> torch.Tensor:
-    """log of a Zipf(s) popularity over a random permutation of the experts: added to the router logits, it makes the
-    softmax route probabilities proportional to the popularity (times the data-dependent part)."""
+def zipf_temperature(E: int, k: int, s: float, logit_std: float, hot_fraction: float = 0.4, seed: int = 0) -> float:
+    """Strength tau of the router bias tau * log(p_zipf) for which the experts' measured route shares follow the
+    Zipf(s) popularity: the hot_fraction most popular experts receive the Zipf head mass of the routes after top-k
+    selection on logits ~ N(0, logit_std^2) + bias. (tau = 1 would concentrate far more than Zipf: the top-k of a
+    peaked softmax takes almost only the head.) Found by bisection on a fixed Monte-Carlo sample."""
+    g = torch.Generator().manual_seed(seed)
+    r = torch.arange(1, E + 1, dtype=torch.float64)
+    p = r.pow(-s)
+    p = p / p.sum()
+    n_hot = max(1, int(round(hot_fraction * E)))
+    target = float(p[:n_hot].sum())
+    noise = torch.randn(4096, E, generator=g, dtype=torch.float64) * logit_std
+    lo, hi = 0.0, 4.0
+    for _ in range(30):
+        tau = (lo + hi) / 2
+        ids = (noise + tau * p.log()).topk(k, -1).indices
+        share = float((ids < n_hot).double().mean())
+        lo, hi = (tau, hi) if share < target else (lo, tau)
+    return (lo + hi) / 2
+
+
+def zipf_bias(E: int, s: float, gen: torch.Generator, tau: float = 1.0) -> torch.Tensor:
+    """tau * log of a Zipf(s) popularity over a random permutation of the experts, added to the router logits."""
     ranks = torch.randperm(E, generator=gen).float() + 1.0
     p = ranks.pow(-s)
     p = p / p.sum()
-    return p.log()
+    return tau * p.log()
 
 
 class Qwen3MoeModel:
@@ -74,6 +94,8 @@ class Qwen3MoeModel:
         n_hot = cfg.experts if hot_fraction >= 1.0 else max(1, int(round(hot_fraction * cfg.experts)))
         self.mailbox = mailbox
         self.engines = []
+        # router logits are N(0, (std * sqrt(H))^2) for RMS-normalized hidden states
+        self.zipf_tau = zipf_temperature(cfg.experts, cfg.top_k, cfg.zipf_s, cfg.std * H ** 0.5)
         for li in range(cfg.layers):
             L = dict(
                 in_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
@@ -84,7 +106,7 @@ class Qwen3MoeModel:
                 o=randn(H, cfg.heads * D),
             )
             router = randn(cfg.experts, H)
-            bias = zipf_bias(cfg.experts, cfg.zipf_s, g)
+            bias = zipf_bias(cfg.experts, cfg.zipf_s, g, self.zipf_tau)
             seed_l = seed * 1000 + li
             if synthetic_experts:   # random codes generated on the GPU (fast), copied to the host for the CPU tier
                 ew = formats.synthetic_experts(cfg.experts, H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
@@ -142,6 +164,9 @@ class Qwen3MoeModel:
             q=torch.empty(batch, cfg.heads, cfg.head_dim, dtype=torch.bfloat16, device=dev),
             attn=torch.empty(batch, cfg.heads, cfg.head_dim, dtype=torch.bfloat16, device=dev),
             moe_out=torch.empty(batch, H, dtype=torch.bfloat16, device=dev),
+            qkv=torch.empty(batch, (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim, dtype=torch.bfloat16, device=dev),
+            o=torch.empty(batch, H, dtype=torch.bfloat16, device=dev),
+            logits=torch.empty(batch, cfg.vocab, dtype=torch.bfloat16, device=dev),
             next=torch.zeros(batch, dtype=torch.int64, device=dev),
         )
 
@@ -157,22 +182,23 @@ class Qwen3MoeModel:
                 ops.add_rmsnorm(buf['residual'], None, L['in_norm'], buf['h'], cfg.eps)
             else:
                 ops.add_rmsnorm(buf['moe_out'], buf['residual'], L['in_norm'], buf['h'], cfg.eps)
-            qkv = torch.matmul(buf['h'], L['qkv'].t())
-            ops.qk_norm_rope_kv(qkv, L['q_norm'], L['k_norm'], buf['pos'], buf['rows'], buf['q'], st['k'][li],
+            ops.linear(buf['h'], L['qkv'], out=buf['qkv'])
+            ops.qk_norm_rope_kv(buf['qkv'], L['q_norm'], L['k_norm'], buf['pos'], buf['rows'], buf['q'], st['k'][li],
                                 st['v'][li], cfg.heads, cfg.kv_heads, cfg.rope_theta, cfg.eps)
             ops.attn_decode(buf['q'], st['k'][li], st['v'][li], buf['seqlens'], buf['attn'], st['ws_o'], st['ws_ml'],
                             st['counters'], st['splits'], scale)
-            o = torch.matmul(buf['attn'].view(B, -1), L['o'].t())
-            ops.add_rmsnorm(o, buf['residual'], L['post_norm'], buf['h'], cfg.eps)
+            ops.linear(buf['attn'].view(B, -1), L['o'], out=buf['o'])
+            ops.add_rmsnorm(buf['o'], buf['residual'], L['post_norm'], buf['h'], cfg.eps)
             L['moe'].forward(buf['h'], out=buf['moe_out'])
         ops.add_rmsnorm(buf['moe_out'], buf['residual'], self.final_norm, buf['h'], cfg.eps)
-        logits = torch.matmul(buf['h'], self.lm_head.t())
-        torch.argmax(logits, dim=-1, out=buf['next'])
+        torch.matmul(buf['h'], self.lm_head.t(), out=buf['logits'])
+        torch.argmax(buf['logits'], dim=-1, out=buf['next'])
         return buf['next']
 
     # ------------------------------------------------------------------ prefill (one sequence)
-    def prefill(self, st: dict, tokens: torch.Tensor, row: int = 0, start: int = 0) -> torch.Tensor:
-        """Runs `tokens` [T] of sequence `row` from position `start`; fills the KV cache; returns the next token."""
+    def prefill(self, st: dict, tokens: torch.Tensor, row: int = 0, start: int = 0, return_logits: bool = False):
+        """Runs `tokens` [T] of sequence `row` from position `start`; fills the KV cache; returns the next token
+        (and the last position's logits with return_logits)."""
         cfg = self.cfg
         dev = self.device
         T = tokens.shape[0]
@@ -202,4 +228,66 @@ class Qwen3MoeModel:
         ops.add_rmsnorm(moe_out, residual, self.final_norm, h, cfg.eps)
         logits = torch.matmul(h[-1:], self.lm_head.t())
         st['lengths'][row] = start + T
-        return torch.argmax(logits, dim=-1)
+        nxt = torch.argmax(logits, dim=-1)
+        return (nxt, logits[0]) if return_logits else nxt
+
+    # ------------------------------------------------------------------ fp32 reference (tests)
+    def reference_logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Plain fp32 PyTorch forward of the whole sequence (dequantized experts, causal attention): logits of the
+        last position. The oracle of the model tests."""
+        cfg = self.cfg
+        dev = self.device
+        f = torch.float32
+        D, Hq, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+        T = tokens.shape[0]
+
+        def rms(x, w):
+            return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.eps) * w.float()
+
+        pos = torch.arange(T, device=dev, dtype=torch.float64)
+        inv = cfg.rope_theta ** (-torch.arange(0, D // 2, device=dev, dtype=torch.float64) * 2 / D)
+        ang = pos[:, None] * inv[None]
+        cos, sin = ang.cos().to(f)[:, None], ang.sin().to(f)[:, None]
+
+        def rope(t):
+            a, b = t[..., :D // 2], t[..., D // 2:]
+            return torch.cat([a * cos - b * sin, b * cos + a * sin], -1)
+
+        x = self.embed.index_select(0, tokens.to(dev)).to(f)
+        mask = torch.ones(T, T, device=dev, dtype=torch.bool).tril()
+        for L in self.layers:
+            h = rms(x, L['in_norm'])
+            qkv = (h @ L['qkv'].to(f).t()).view(T, Hq + 2 * Hkv, D)
+            q = rope(rms(qkv[:, :Hq], L['q_norm']))
+            k = rope(rms(qkv[:, Hq:Hq + Hkv], L['k_norm']))
+            v = qkv[:, Hq + Hkv:]
+            G = Hq // Hkv
+            k = k.repeat_interleave(G, 1)
+            v = v.repeat_interleave(G, 1)
+            s = torch.einsum('thd,shd->hts', q, k) / D ** 0.5
+            s = s.masked_fill(~mask, float('-inf')).softmax(-1)
+            a = torch.einsum('hts,shd->thd', s, v).reshape(T, Hq * D)
+            x = x + a @ L['o'].to(f).t()
+            h = rms(x, L['post_norm'])
+            moe = L['moe']
+            logits = h @ moe.router_w.to(f).t() + (moe.router_bias if moe.router_bias is not None else 0)
+            p = logits.softmax(-1)
+            w, ids = p.topk(cfg.top_k, -1)
+            w = w / w.sum(-1, keepdim=True)
+            out = torch.zeros_like(x)
+            ew = moe.host if moe.host is not None else moe.pool
+            slot_of = {e: e for e in range(moe.E)} if moe.host is not None else {e: s for s, e in enumerate(moe.hot)}
+            cache = {}
+            for t in range(T):
+                for j in range(cfg.top_k):
+                    e = int(ids[t, j])
+                    if e not in cache:
+                        w1, w3, w2 = ew.dequant(slot_of[e])
+                        cache[e] = (w1.to(dev), w3.to(dev), w2.to(dev))
+                    w1, w3, w2 = cache[e]
+                    g = h[t] @ w1.t()
+                    u = h[t] @ w3.t()
+                    out[t] += w[t, j] * ((torch.nn.functional.silu(g) * u) @ w2.t())
+            x = x + out
+        x = rms(x, self.final_norm)
+        return x[-1] @ self.lm_head.to(f).t()

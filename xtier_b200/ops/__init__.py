@@ -64,10 +64,27 @@ def attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits
     _ops().attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits, scale)
 
 
-def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, k: int, mode: int = 0, n_group: int = 1,
-              topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0, mailbox: int = 0):
-    _ops().moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, k, mode, n_group, topk_group, renorm,
-                     scale, layer, mailbox)
+def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k: int, mode: int = 0,
+              n_group: int = 1, topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0,
+              mailbox: int = 0):
+    _ops().moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k, mode, n_group,
+                     topk_group, renorm, scale, layer, mailbox)
+
+
+def gemv(x, w, out, add=None):
+    """out[m, N] = x[m, K] . w[N, K]^T (+ add), m <= 16, BF16 (the decode projections)."""
+    _ops().gemv(x, w, add, out)
+    return out
+
+
+def linear(x, w, out=None):
+    """x @ w^T: the weight-streaming GEMV for decode-sized inputs, cuBLAS otherwise."""
+    m = x.numel() // x.shape[-1]
+    if m <= 16 and x.shape[-1] * m * 2 <= 200 * 1024 and x.is_contiguous():
+        out = torch.empty(*x.shape[:-1], w.shape[0], dtype=x.dtype, device=x.device) if out is None else out
+        _ops().gemv(x, w, None, out)
+        return out
+    return torch.matmul(x, w.t(), out=out) if out is not None else torch.matmul(x, w.t())
 
 
 def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0):
@@ -79,6 +96,6 @@ def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, ma
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
-    """Key splits of the decode attention: enough CTAs to cover the SMs twice, at least 64 keys per split."""
+    """Key splits of the decode attention: up to one 128-key tile per split, at most enough CTAs for two per SM."""
     want = max(1, (2 * sms + batch * kv_heads - 1) // (batch * kv_heads))
-    return max(1, min(64, want, (max_len + 63) // 64))
+    return max(1, min(64, want, (max_len + 127) // 128))
