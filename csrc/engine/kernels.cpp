@@ -152,48 +152,87 @@ static void store_mid_avx512(void *dst, int K, int j, float v) {
     d[K + pos] = f32_to_bf16_rne(v - bf16_to_f32(hi));
 }
 
-XT_AVX512 static inline __m512 scales16(const uint8_t *sr, int c, int fmt) {
-    if (fmt == NVFP4) {   // 4 blocks of 16 in this 64-chunk: lanes 4b..4b+3 hold block b
-        uint32_t v;
-        memcpy(&v, sr + c / 16, 4);
-        const __m512i sh = _mm512_setr_epi32(0, 0, 0, 0, 8, 8, 8, 8, 16, 16, 16, 16, 24, 24, 24, 24);
-        __m512i b = _mm512_and_si512(_mm512_srlv_epi32(_mm512_set1_epi32(int(v)), sh), _mm512_set1_epi32(0x7F));
-        // E4M3 magnitude bits placed at FP32 exponent/mantissa position are 2^-120 times the value (subnormals too)
-        return _mm512_mul_ps(_mm512_castsi512_ps(_mm512_slli_epi32(b, 20)), _mm512_set1_ps(0x1p120f));
+// All block scales of one row -> FP32 (16 at a time; the tail of the buffer is padded, never read as a scale).
+XT_AVX512 static void row_scales(const uint8_t *sr, int nblocks, int fmt, float *sf) {
+    for (int i = 0; i < nblocks; i += 16) {
+        const __mmask16 m = nblocks - i >= 16 ? __mmask16(0xFFFF) : __mmask16((1u << (nblocks - i)) - 1);
+        const __m512i b = _mm512_cvtepu8_epi32(_mm_maskz_loadu_epi8(m, sr + i));
+        __m512 f;
+        if (fmt == NVFP4) {
+            const __m512i mag = _mm512_and_si512(b, _mm512_set1_epi32(0x7F));
+            const __m512 normal =
+                _mm512_castsi512_ps(_mm512_add_epi32(_mm512_slli_epi32(mag, 20), _mm512_set1_epi32(120 << 23)));
+            const __m512 sub = _mm512_mul_ps(_mm512_cvtepi32_ps(mag), _mm512_set1_ps(0x1p-9f));
+            f = _mm512_mask_blend_ps(_mm512_cmplt_epi32_mask(mag, _mm512_set1_epi32(8)), normal, sub);
+        } else {
+            f = _mm512_castsi512_ps(_mm512_slli_epi32(b, 23));   // exponent byte 0 reads as 0 instead of 2^-127
+        }
+        _mm512_storeu_ps(sf + i, f);
     }
-    uint16_t v;   // 2 blocks of 32: lanes 0..7 block 0, 8..15 block 1
-    memcpy(&v, sr + c / 32, 2);
-    const __m512i sh = _mm512_setr_epi32(0, 0, 0, 0, 0, 0, 0, 0, 8, 8, 8, 8, 8, 8, 8, 8);
-    __m512i b = _mm512_and_si512(_mm512_srlv_epi32(_mm512_set1_epi32(int(v)), sh), _mm512_set1_epi32(0xFF));
-    return _mm512_castsi512_ps(_mm512_slli_epi32(b, 23));   // exponent byte 0 reads as 0 instead of 2^-127
+}
+
+// N tokens (compile time, so the accumulators stay in registers) and HILO (the down projection's hi+lo intermediate)
+// are template parameters; two accumulators per token alternate between chunks to halve the FMA dependency chain.
+template <int N, bool HILO>
+XT_AVX512 static void dot_avx512_n(const uint8_t *w, size_t ws, const uint8_t *s, size_t ss, int rows, int K, int fmt,
+                                   const void *const *xs, float *out) {
+    const __m512i lut = _mm512_loadu_si512(kE2M1Bf16);
+    const __m512i m15 = _mm512_set1_epi16(15);
+    // lane l of a 64-element chunk covers elements 4l..4l+3: NVFP4 block l/4, MXFP4 block l/8
+    const __m512i rep = fmt == NVFP4 ? _mm512_setr_epi32(0, 0, 0, 0, 1, 1, 1, 1, 2, 2, 2, 2, 3, 3, 3, 3)
+                                     : _mm512_setr_epi32(0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1, 1, 1, 1, 1);
+    const int bs = fmt == NVFP4 ? 16 : 32;
+    const int bshift = fmt == NVFP4 ? 4 : 5;   // c / bs without a division in the loop
+    alignas(64) float sf[16384 / 16 + 16];
+    const uint16_t *x[N];
+    for (int t = 0; t < N; ++t) x[t] = static_cast<const uint16_t *>(xs[t]);
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t *wr = w + r * ws, *sr = s + r * ss;
+        row_scales(sr, K / bs, fmt, sf);
+        __m512 acc0[N], acc1[N];
+#pragma GCC unroll 8
+        for (int t = 0; t < N; ++t) acc0[t] = acc1[t] = _mm512_setzero_ps();
+#define XT_CHUNK(CC, ACC)                                                                                      \
+    {                                                                                                          \
+        const int c_ = (CC);                                                                                   \
+        __m512i b = _mm512_cvtepu8_epi16(_mm256_loadu_si256(reinterpret_cast<const __m256i *>(wr + c_ / 2)));  \
+        __m512bh we = (__m512bh)_mm512_permutexvar_epi16(_mm512_and_si512(b, m15), lut);                       \
+        __m512bh wo = (__m512bh)_mm512_permutexvar_epi16(_mm512_srli_epi16(b, 4), lut);                        \
+        __m512 sc = _mm512_permutexvar_ps(rep, _mm512_castps128_ps512(_mm_loadu_ps(sf + (c_ >> bshift))));     \
+        _Pragma("GCC unroll 8") for (int t = 0; t < N; ++t) {                                                  \
+            const uint16_t *xt = x[t] + c_;                                                                    \
+            __m512 d = _mm512_dpbf16_ps(_mm512_setzero_ps(), we, (__m512bh)_mm512_loadu_si512(xt));            \
+            d = _mm512_dpbf16_ps(d, wo, (__m512bh)_mm512_loadu_si512(xt + 32));                                \
+            if (HILO) {                                                                                        \
+                d = _mm512_dpbf16_ps(d, we, (__m512bh)_mm512_loadu_si512(xt + K));                             \
+                d = _mm512_dpbf16_ps(d, wo, (__m512bh)_mm512_loadu_si512(xt + K + 32));                        \
+            }                                                                                                  \
+            ACC[t] = _mm512_fmadd_ps(d, sc, ACC[t]);                                                           \
+        }                                                                                                      \
+    }
+        int c = 0;
+        for (; c + 128 <= K; c += 128) {
+            XT_CHUNK(c, acc0)
+            XT_CHUNK(c + 64, acc1)
+        }
+        if (c < K) XT_CHUNK(c, acc0)
+#undef XT_CHUNK
+#pragma GCC unroll 8
+        for (int t = 0; t < N; ++t) out[r * N + t] = _mm512_reduce_add_ps(_mm512_add_ps(acc0[t], acc1[t]));
+    }
 }
 
 XT_AVX512 static void dot_avx512(const uint8_t *w, size_t ws, const uint8_t *s, size_t ss, int rows, int K, int fmt,
                                  const void *const *xs, int n, int hilo, float *out) {
-    const __m512i lut = _mm512_loadu_si512(kE2M1Bf16);
-    const __m512i m15 = _mm512_set1_epi16(15);
-    for (int r = 0; r < rows; ++r) {
-        const uint8_t *wr = w + r * ws, *sr = s + r * ss;
-        __m512 acc[MAX_TOK];
-        for (int t = 0; t < n; ++t) acc[t] = _mm512_setzero_ps();
-        for (int c = 0; c < K; c += 64) {
-            __m512i b = _mm512_cvtepu8_epi16(_mm256_loadu_si256(reinterpret_cast<const __m256i *>(wr + c / 2)));
-            __m512bh we = (__m512bh)_mm512_permutexvar_epi16(_mm512_and_si512(b, m15), lut);
-            __m512bh wo = (__m512bh)_mm512_permutexvar_epi16(_mm512_srli_epi16(b, 4), lut);
-            __m512 sc = scales16(sr, c, fmt);
-            for (int t = 0; t < n; ++t) {
-                const uint16_t *x = static_cast<const uint16_t *>(xs[t]) + c;
-                __m512 d = _mm512_dpbf16_ps(_mm512_setzero_ps(), we, (__m512bh)_mm512_loadu_si512(x));
-                d = _mm512_dpbf16_ps(d, wo, (__m512bh)_mm512_loadu_si512(x + 32));
-                if (hilo) {
-                    d = _mm512_dpbf16_ps(d, we, (__m512bh)_mm512_loadu_si512(x + K));
-                    d = _mm512_dpbf16_ps(d, wo, (__m512bh)_mm512_loadu_si512(x + K + 32));
-                }
-                acc[t] = _mm512_fmadd_ps(d, sc, acc[t]);
-            }
-        }
-        for (int t = 0; t < n; ++t) out[r * n + t] = _mm512_reduce_add_ps(acc[t]);
+#define XT_DOT_N(NN)                                                                                  \
+    case NN:                                                                                          \
+        return hilo ? dot_avx512_n<NN, true>(w, ws, s, ss, rows, K, fmt, xs, out)                    \
+                    : dot_avx512_n<NN, false>(w, ws, s, ss, rows, K, fmt, xs, out);
+    switch (n) {
+        XT_DOT_N(1) XT_DOT_N(2) XT_DOT_N(3) XT_DOT_N(4) XT_DOT_N(5) XT_DOT_N(6) XT_DOT_N(7) XT_DOT_N(8)
+        default: break;
     }
+#undef XT_DOT_N
 }
 
 static const Kernels kAvx512 = {"avx512", 64, 2, 4, prep_x_avx512, store_mid_avx512, dot_avx512};
