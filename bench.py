@@ -101,6 +101,7 @@ def main():
     ap.add_argument('--layers', type=int, default=48)
     ap.add_argument('--threads', type=int, default=0, help='CPU engine workers per rank (0: auto)')
     ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--profile', type=int, default=0, help='print per-kernel device time of N graph replays and exit')
     args = ap.parse_args()
     if args.impl == 'reference':
         return reference_arm(args)
@@ -154,6 +155,19 @@ def main():
         gen.step()
     torch.cuda.synchronize()
     gen.check()
+
+    if args.profile:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(args.profile):
+                gen.step()
+            torch.cuda.synchronize()
+        if rank == 0:
+            print(prof.key_averages().table(sort_by='cuda_time_total', row_limit=25, max_name_column_width=70))
+        gen.graph = None
+        if mailbox is not None:
+            mailbox.stop()
+        return
 
     def barrier():
         if world > 1:

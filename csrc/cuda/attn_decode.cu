@@ -173,20 +173,35 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // merge: every split's (max, sum) into shared memory at once, one weight per (split, head), then each output
+    // element is a weighted sum over the splits whose loads are all independent (no serial L2 round trips)
+    constexpr int MAX_SPLITS = 64;
+    __shared__ float wsplit[MAX_SPLITS][G];
     const size_t base = (size_t(b) * p.Hkv + kvh) * p.splits * G;
-    for (int i = threadIdx.x; i < G * AD_D; i += blockDim.x) {
-        const int h = i / AD_D, d = i % AD_D;
+    float *mls = buf;   // the score / reduction buffer is free again
+    for (int i = threadIdx.x; i < p.splits * G * 2; i += blockDim.x) mls[i] = __ldcg(p.ws_ml + base * 2 + i);
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int h = threadIdx.x;
         float M = -INFINITY;
-        for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.ws_ml[(base + size_t(s) * G + h) * 2]);
-        float L = 0.f, O = 0.f;
+        for (int s = 0; s < p.splits; ++s) M = fmaxf(M, mls[(s * G + h) * 2]);
+        float L = 0.f;
         for (int s = 0; s < p.splits; ++s) {
-            const float ms = p.ws_ml[(base + size_t(s) * G + h) * 2];
-            if (ms == -INFINITY) continue;
-            const float f = exp2f(ms - M);
-            L += p.ws_ml[(base + size_t(s) * G + h) * 2 + 1] * f;
-            O += p.ws_o[(base + size_t(s) * G + h) * AD_D + d] * f;
+            const float ms = mls[(s * G + h) * 2];
+            const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
+            wsplit[s][h] = f;
+            L += mls[(s * G + h) * 2 + 1] * f;
         }
-        p.out[(size_t(b) * p.Hq + size_t(kvh) * G + h) * AD_D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        for (int s = 0; s < p.splits; ++s) wsplit[s][h] *= inv;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * AD_D; i += blockDim.x) {
+        const int h = i / AD_D;
+        float O = 0.f;
+#pragma unroll 8
+        for (int s = 0; s < p.splits; ++s) O += __ldcg(p.ws_o + (base + size_t(s) * G) * AD_D + i) * wsplit[s][h];
+        p.out[(size_t(b) * p.Hq + size_t(kvh) * G + h) * AD_D + i % AD_D] = __float2bfloat16(O);
     }
     if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0;
 }
@@ -198,7 +213,7 @@ using namespace xt;
 extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t stream) {
     AttnDecodeParams p = *pp;
     const int G = p.Hq / p.Hkv;
-    if (p.Hq % p.Hkv) return -2;
+    if (p.Hq % p.Hkv || p.splits < 1 || p.splits > 64) return -2;
     dim3 grid(p.splits, p.Hkv, B);
     switch (G) {
         case 1: attn_decode_kernel<1><<<grid, AD_WARPS * 32, 0, stream>>>(p); break;

@@ -211,6 +211,21 @@ void gemv(const Tensor &x, const Tensor &w, const std::optional<Tensor> &add, co
     check_rc(xt_gemv_bf16(x.data_ptr(), w.data_ptr(), optr<void>(add), out.data_ptr(), m, N, K, stream()), "gemv");
 }
 
+void gemm_tc(const Tensor &a, const Tensor &b, const std::optional<Tensor> &residual, const Tensor &out,
+             const Tensor &err) {
+    cuda_contig(a, "a");
+    cuda_contig(b, "b");
+    cuda_contig(out, "out");
+    check(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_tc wants bf16");
+    const int K = int(a.size(-1)), M = int(a.numel() / K), N = int(b.size(0));
+    check(b.size(1) == K && out.numel() == int64_t(M) * N, "gemm_tc shapes");
+    check(err.scalar_type() == at::kInt && err.is_cuda(), "gemm_tc error word: int32 CUDA tensor");
+    c10::cuda::CUDAGuard g(a.device());
+    check_rc(xt_gemm_tc(a.data_ptr(), b.data_ptr(), out.data_ptr(), optr<void>(residual), M, N, K, ptr<int>(err),
+                        stream()),
+             "gemm_tc");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(xtier, m) {
@@ -223,6 +238,7 @@ TORCH_LIBRARY(xtier, m) {
           "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, Tensor(d!) ws_logits, Tensor(e!) ws_count, int k, int mode, "
           "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox) -> ()");
     m.def("gemv(Tensor x, Tensor w, Tensor? add, Tensor(a!) out) -> ()");
+    m.def("gemm_tc(Tensor a, Tensor b, Tensor? residual, Tensor(a!) out, Tensor(b!) err) -> ()");
     m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
           "float limit, float alpha, float beta) -> ()");
     m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
@@ -237,4 +253,5 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("moe_gate_up", &moe_gate_up);
     m.impl("moe_down", &moe_down);
     m.impl("gemv", &gemv);
+    m.impl("gemm_tc", &gemm_tc);
 }

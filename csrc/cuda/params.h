@@ -84,5 +84,7 @@ int xt_attn_decode(const xt::AttnDecodeParams *p, int B, cudaStream_t stream);
 int xt_moe_route(const xt::RouteParams *p, const XtMailbox *mb, int use_mb, cudaStream_t stream);
 int xt_moe_gate_up(const xt::GateUpParams *p, cudaStream_t stream);
 int xt_moe_down(const xt::DownParams *p, const XtMailbox *mb, int use_mb, int m, cudaStream_t stream);
+int xt_gemm_tc(const void *A, const void *B, void *D, const void *R, int M, int N, int K, int *error,
+               cudaStream_t stream);
 int xt_gemv_bf16(const void *x, const void *W, const void *add, void *y, int m, int N, int K, cudaStream_t stream);
 }
