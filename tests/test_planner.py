@@ -1,0 +1,86 @@
+"""Planner on the CPU: Clark's expected max vs Monte Carlo, the DP stays within budget and beats or matches the
+uniform layout, route traces round-trip into profiles, and the CLI tools chain (trace -> profile -> plan)."""
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+
+from xtier_b200.planner import auto, cost, trace
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_expected_max_vs_monte_carlo():
+    rng = np.random.default_rng(0)
+    for m1, s1, m2, s2 in [(10, 1, 10, 1), (10, 2, 12, 1), (5, 0.5, 20, 3)]:
+        mc = np.maximum(rng.normal(m1, s1, 400000), rng.normal(m2, s2, 400000)).mean()
+        assert abs(cost.expected_max(m1, s1, m2, s2) - mc) < 0.02 * mc
+
+
+def _profile(L=6, E=32, seed=0):
+    rng = np.random.default_rng(seed)
+    layers = {}
+    for l in range(L):
+        z = (np.arange(1, E + 1) ** -(0.6 + 0.15 * l))
+        z = rng.permutation(z / z.sum() * 8)   # 8 routes per token
+        layers[str(l)] = np.minimum(z, 1.0).tolist()
+    return {'layers': layers, 'tokens': {str(l): 1000 for l in range(L)}}
+
+
+def test_dp_within_budget_and_not_worse_than_uniform():
+    prof = _profile()
+    curves = auto.curves_from_profile(prof, cost.Coeffs())
+    for budget in (0, 10, 40, 96, 300):
+        for g in (1, 4):
+            plan = auto.solve(curves, budget, g)
+            assert sum(plan) <= budget
+            assert all(0 <= n <= 32 for n in plan)
+            assert auto.plan_time(curves, plan) <= auto.plan_time(curves, auto.uniform(curves, budget)) + 1e-9
+    # exhaustive check on a tiny case
+    small = [c[:5] for c in curves[:3]]
+    import itertools
+    best = min((sum(c[n] for c, n in zip(small, ns)), ns) for ns in itertools.product(range(5), repeat=3)
+               if sum(ns) <= 6)
+    plan = auto.solve(small, 6)
+    assert abs(auto.plan_time(small, plan) - best[0]) < 1e-9
+
+
+def test_curve_monotone_in_slots():
+    c = cost.layer_time_curve(np.array(_profile()['layers']['0']), cost.Coeffs(g1=0.0))
+    assert np.all(np.diff(c) <= 1e-9)   # more hot slots never costs more when GPU experts are free
+
+
+def test_trace_roundtrip_and_tools(tmp_path):
+    rng = np.random.default_rng(1)
+    recs = [(float(i), 10.0, i % 3, 0, rng.integers(0, 16, size=(2, 4))) for i in range(60)]
+    p = tmp_path / 'trace.bin'
+    trace.write_trace(p, recs)
+    got = list(trace.read_trace(p))
+    assert len(got) == 60 and np.array_equal(got[5][6], recs[5][4])
+    prof = trace.profile_from_trace(p, 16)
+    assert abs(sum(prof['layers']['0']) - 4.0) < 1e-9   # 4 routes per token
+    env = dict(PYTHONPATH=str(ROOT))
+    subprocess.run([sys.executable, '-m', 'xtier_b200.tools.plan_trace', str(p), '--experts', '16', '--out',
+                    str(tmp_path / 'prof.json')], check=True, env=env, capture_output=True)
+    subprocess.run([sys.executable, '-m', 'xtier_b200.tools.plan_auto', '--profile', str(tmp_path / 'prof.json'),
+                    '--budget-slots', '20', '--write', str(tmp_path / 'plan.json')], check=True, env=env,
+                   capture_output=True)
+    plan = json.loads((tmp_path / 'plan.json').read_text())
+    assert sum(plan['slots'].values()) <= 20 and set(plan['slots']) == {'0', '1', '2'}
+
+
+def test_layer_slots_from_env(monkeypatch, tmp_path):
+    from xtier_b200 import planner
+    planner._plan_cache.clear()
+    monkeypatch.setenv('XTIER_CACHE_SLOTS', '10')
+    assert planner.layer_slots(3, 64) == 10
+    monkeypatch.setenv('XTIER_CACHE_FRACTION', '0.25')
+    assert planner.layer_slots(3, 64) == 16
+    (tmp_path / 'p.json').write_text(json.dumps({'slots': {'3': 7}}))
+    monkeypatch.setenv('XTIER_CACHE_PLAN', str(tmp_path / 'p.json'))
+    assert planner.layer_slots(3, 64) == 7 and planner.layer_slots(4, 64) == 16
+    monkeypatch.setenv('XTIER_CACHE_FULL', '4')
+    assert planner.layer_slots(4, 64) == 64
+    planner._plan_cache.clear()
