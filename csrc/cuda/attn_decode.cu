@@ -196,12 +196,37 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
         for (int s = 0; s < p.splits; ++s) wsplit[s][h] *= inv;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * AD_D; i += blockDim.x) {
+    // four consecutive dims per thread (16-byte loads), all splits' loads of a group issued back to back
+    for (int i = threadIdx.x * 4; i < G * AD_D; i += blockDim.x * 4) {
         const int h = i / AD_D;
-        float O = 0.f;
-#pragma unroll 8
-        for (int s = 0; s < p.splits; ++s) O += __ldcg(p.ws_o + (base + size_t(s) * G) * AD_D + i) * wsplit[s][h];
-        p.out[(size_t(b) * p.Hq + size_t(kvh) * G + h) * AD_D + i % AD_D] = __float2bfloat16(O);
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 *src = reinterpret_cast<const float4 *>(p.ws_o + base * AD_D + i);
+        const size_t stride4 = size_t(G) * AD_D / 4;   // float4s between consecutive splits
+        int s = 0;
+        for (; s + 8 <= p.splits; s += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + (s + j) * stride4);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float wgt = wsplit[s + j][h];
+                O.x += v[j].x * wgt;
+                O.y += v[j].y * wgt;
+                O.z += v[j].z * wgt;
+                O.w += v[j].w * wgt;
+            }
+        }
+        for (; s < p.splits; ++s) {
+            const float4 v = __ldcg(src + s * stride4);
+            const float wgt = wsplit[s][h];
+            O.x += v.x * wgt;
+            O.y += v.y * wgt;
+            O.z += v.z * wgt;
+            O.w += v.w * wgt;
+        }
+        __nv_bfloat16 *dst = p.out + (size_t(b) * p.Hq + size_t(kvh) * G + h) * AD_D + i % AD_D;
+        reinterpret_cast<__nv_bfloat162 *>(dst)[0] = __floats2bfloat162_rn(O.x, O.y);
+        reinterpret_cast<__nv_bfloat162 *>(dst)[1] = __floats2bfloat162_rn(O.z, O.w);
     }
     if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0;
 }

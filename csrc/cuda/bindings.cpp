@@ -177,7 +177,8 @@ void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const 
 
 void moe_down(const Tensor &mid, const Tensor &slots, const Tensor &w, const Tensor &w2, const Tensor &s2,
               const Tensor &g2, const std::optional<Tensor> &add, const Tensor &out,
-              const std::optional<Tensor> &out_f32, int64_t fmt, int64_t mailbox) {
+              const std::optional<Tensor> &out_f32, const std::optional<Tensor> &gpu_part, int64_t fmt,
+              int64_t mailbox) {
     cuda_contig(w2, "w2");
     DownParams p{};
     p.mid = ptr<const float>(mid);
@@ -189,6 +190,7 @@ void moe_down(const Tensor &mid, const Tensor &slots, const Tensor &w, const Ten
     p.add = optr<const __nv_bfloat16>(add);
     p.out = ptr<__nv_bfloat16>(out);
     p.out_f32 = optr<float>(out_f32);
+    p.gpu_part = optr<float>(gpu_part);
     p.kk = int(slots.size(-1));
     p.H = int(w2.size(1));
     p.I = int(w2.size(2) * 2);
@@ -242,7 +244,7 @@ TORCH_LIBRARY(xtier, m) {
     m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
           "float limit, float alpha, float beta) -> ()");
     m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
-          "Tensor(b!)? out_f32, int fmt, int mailbox) -> ()");
+          "Tensor(b!)? out_f32, Tensor(c!)? gpu_part, int fmt, int mailbox) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(xtier, CUDA, m) {

@@ -350,7 +350,6 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
     constexpr int ROWS = RPW * U;
     static_assert(ROWS % 4 == 0, "the epilogue writes four rows per thread");
     __shared__ float part[XT_MB_MAX_ROUTES][ROWS];
-    __shared__ int cpu_ok;
     const int t = blockIdx.x;
     const int lane = threadIdx.x & 31, j = threadIdx.x >> 5;   // warp j = route j
     const int q = lane % LPR, sub = lane / LPR;
@@ -389,29 +388,10 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
 #pragma unroll
         for (int u = 0; u < U; ++u) part[j][u * RPW + lane] = 0.f;
     }
-    // CPU part: wait for the dispatcher's answer (bounded), then add it
-    if (threadIdx.x == 0) {
-        int ok = 0;
-        if (use_mb && mb.dev->pending) {
-            const unsigned seq = mb.dev->seq;
-            const uint64_t t0 = globaltimer_ns();
-            for (;;) {
-                if (ld_acquire_sys(&mb.hdr->resp) == seq) {
-                    ok = 1;
-                    break;
-                }
-                if (globaltimer_ns() - t0 > mb.timeout_ns) {
-                    atomicExch(&mb.dev->error, 1u);
-                    mb.hdr->gpu_error = 1;
-                    break;
-                }
-                __nanosleep(128);
-            }
-        }
-        cpu_ok = ok;
-    }
     __syncthreads();
-    // four rows per thread: one 16-byte read of the CPU result (mapped host memory) per four outputs
+    // with a CPU part pending, this kernel leaves the sum to moe_combine (one poller per token instead of every CTA
+    // polling host memory); otherwise it writes the final rows itself
+    const bool defer = use_mb && mb.dev->pending;
     for (int i = threadIdx.x; i * 4 < ROWS; i += blockDim.x) {
         const int h = hb + i * 4;
         if (h >= p.H) break;
@@ -421,15 +401,9 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
             for (int e = 0; e < 4; ++e) v[e] += part[jj][i * 4 + e];
         const size_t o = size_t(t) * p.H + h;
         if (p.out_f32) *reinterpret_cast<float4 *>(p.out_f32 + o) = make_float4(v[0], v[1], v[2], v[3]);
-        if (cpu_ok) {
-            float4 c;
-            asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];\n"
-                         : "=f"(c.x), "=f"(c.y), "=f"(c.z), "=f"(c.w)
-                         : "l"(mb.y + o));
-            v[0] += c.x;
-            v[1] += c.y;
-            v[2] += c.z;
-            v[3] += c.w;
+        if (defer) {
+            *reinterpret_cast<float4 *>(p.gpu_part + o) = make_float4(v[0], v[1], v[2], v[3]);
+            continue;
         }
         if (p.add) {
             uint2 a = *reinterpret_cast<const uint2 *>(p.add + o);
@@ -445,6 +419,62 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
         outv.x = *reinterpret_cast<uint32_t *>(&r0);
         outv.y = *reinterpret_cast<uint32_t *>(&r1);
         *reinterpret_cast<uint2 *>(p.out + o) = outv;
+    }
+}
+
+// out[t] = GPU part + CPU part (+ add), one CTA per token. Only when the call has a CPU part: thread 0 waits for the
+// dispatcher's answer with a deadline (a timeout sets the error words and the CPU part is left out), then the CTA reads
+// the token's FP32 CPU row from mapped host memory in 16-byte pieces.
+__global__ void __launch_bounds__(256) moe_combine_kernel(const float *gpu_part, const __nv_bfloat16 *add,
+                                                          __nv_bfloat16 *out, int H, XtMailbox mb) {
+    if (!mb.dev->pending) return;
+    __shared__ int ok;
+    const int t = blockIdx.x;
+    if (threadIdx.x == 0) {
+        int got = 0;
+        const unsigned seq = mb.dev->seq;
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+            if (ld_acquire_sys(&mb.hdr->resp) == seq) {
+                got = 1;
+                break;
+            }
+            if (globaltimer_ns() - t0 > mb.timeout_ns) {
+                atomicExch(&mb.dev->error, 1u);
+                mb.hdr->gpu_error = 1;
+                break;
+            }
+        }
+        ok = got;
+    }
+    __syncthreads();
+    for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
+        const size_t o = size_t(t) * H + h;
+        float4 v = *reinterpret_cast<const float4 *>(gpu_part + o);
+        if (ok) {
+            float4 c;
+            asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+                         : "=f"(c.x), "=f"(c.y), "=f"(c.z), "=f"(c.w)
+                         : "l"(mb.y + o));
+            v.x += c.x;
+            v.y += c.y;
+            v.z += c.z;
+            v.w += c.w;
+        }
+        if (add) {
+            uint2 a = *reinterpret_cast<const uint2 *>(add + o);
+            const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
+            float2 f0 = __bfloat1622float2(a2[0]), f1 = __bfloat1622float2(a2[1]);
+            v.x += f0.x;
+            v.y += f0.y;
+            v.z += f1.x;
+            v.w += f1.y;
+        }
+        __nv_bfloat162 r0 = __floats2bfloat162_rn(v.x, v.y), r1 = __floats2bfloat162_rn(v.z, v.w);
+        uint2 outv;
+        outv.x = *reinterpret_cast<uint32_t *>(&r0);
+        outv.y = *reinterpret_cast<uint32_t *>(&r1);
+        *reinterpret_cast<uint2 *>(out + o) = outv;
     }
 }
 
@@ -478,6 +508,7 @@ static int pick_lpr(int row_bytes, int *ch) {
         constexpr int rows = (32 / L) * U;                                                      \
         dim3 grid(m, (p.H + rows - 1) / rows);                                                  \
         moe_down_kernel<L, C, U><<<grid, 32 * p.kk, 0, stream>>>(p, mb, use_mb);                \
+        if (use_mb) moe_combine_kernel<<<m, 256, 0, stream>>>(p.gpu_part, p.add, p.out, p.H, mb); \
         return cudaGetLastError() == cudaSuccess ? 0 : -1;                                      \
     }
 
@@ -511,6 +542,7 @@ int xt_moe_down(const DownParams *pp, const XtMailbox *mbp, int use_mb, int m, c
     int ch = 0;
     int lpr = pick_lpr(p.I / 2, &ch);
     if (p.kk > XT_MB_MAX_ROUTES) return -2;
+    if (use_mb && !p.gpu_part) return -5;
     XT_DN_CASE(32, 1, 8) XT_DN_CASE(32, 2, 8) XT_DN_CASE(32, 3, 4) XT_DN_CASE(32, 4, 4) XT_DN_CASE(32, 5, 4)
     XT_DN_CASE(32, 6, 4) XT_DN_CASE(32, 7, 4) XT_DN_CASE(32, 8, 4) XT_DN_CASE(16, 1, 8) XT_DN_CASE(16, 3, 4)
     XT_DN_CASE(16, 5, 2) XT_DN_CASE(16, 7, 2) XT_DN_CASE(8, 1, 8) XT_DN_CASE(8, 3, 4) XT_DN_CASE(8, 5, 2)

@@ -46,6 +46,7 @@ struct DownParams {
     const __nv_bfloat16 *add; // [m, H] optional extra term (e.g. a shared expert computed elsewhere), may be null
     __nv_bfloat16 *out;       // [m, H]
     float *out_f32;           // [m, H] optional FP32 copy of the GPU part (tests), may be null
+    float *gpu_part;          // [m, H] scratch: the GPU part while a CPU part is pending (mailbox calls)
     int kk, H, I, fmt;
 };
 

@@ -84,6 +84,7 @@ class TieredMoE:
         self.mid = torch.empty(m * self.kk, self.I, dtype=torch.float32, device=dev)
         self.ws_logits = torch.empty(m, self.E, dtype=torch.float32, device=dev)
         self.ws_count = torch.zeros(m, dtype=torch.int32, device=dev)
+        self.gpu_part = torch.empty(m, self.H, dtype=torch.float32, device=dev)
 
     @property
     def all_hot(self) -> bool:
@@ -106,7 +107,8 @@ class TieredMoE:
                             self.fmt_code, self.limit)
             ops.moe_down(self.mid[:m * self.kk], self.slots[:m], self.w[:m], self.pool.w2, self.pool.s2, self.pool.g2,
                          add, out, out_f32, self.fmt_code,
-                         self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0)
+                         self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0,
+                         gpu_part=self.gpu_part[:m])
         else:   # no GPU slots at all: every route on the CPU
             raise NotImplementedError('a layer without GPU slots needs at least the shared/hot pool')
 

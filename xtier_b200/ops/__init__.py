@@ -91,8 +91,8 @@ def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alph
     _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta)
 
 
-def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0):
-    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, fmt, mailbox)
+def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0, gpu_part=None):
+    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, gpu_part, fmt, mailbox)
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
