@@ -1,0 +1,52 @@
+// Peer memory plumbing for the in-kernel NVLink paths: export / import CUDA IPC handles of device buffers, so that every
+// rank maps every peer's buffer and kernels can load from and store to it directly (plain ld/st over NVLink; no TMA
+// multicast is ever issued on peer memory). The handle bytes travel between processes through torch.distributed.
+#include <cuda_runtime.h>
+#include <string.h>
+
+extern "C" {
+
+// Writes the 64-byte IPC handle of the allocation containing `ptr` into out. 0 or a CUDA error code.
+int xt_ipc_export(void *ptr, void *out) {
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+    if (e != cudaSuccess) return int(e);
+    memcpy(out, &h, sizeof h);
+    return 0;
+}
+
+// Maps a peer's allocation; *ptr receives its address in this process. 0 or a CUDA error code.
+int xt_ipc_open(const void *handle, void **ptr) {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return int(e);
+}
+
+int xt_ipc_close(void *ptr) { return int(cudaIpcCloseMemHandle(ptr)); }
+
+int xt_ipc_handle_bytes(void) { return int(sizeof(cudaIpcMemHandle_t)); }
+
+// 1 when this device can access `peer` directly (NVLink / PCIe P2P).
+int xt_can_access_peer(int dev, int peer) {
+    int ok = 0;
+    cudaDeviceCanAccessPeer(&ok, dev, peer);
+    return ok;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+// A dedicated zeroed device allocation for a symmetric buffer (its IPC handle then names exactly this buffer).
+int xt_ipc_alloc(size_t bytes, void **ptr) {
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e != cudaSuccess) return int(e);
+    e = cudaMemset(*ptr, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return int(e);
+}
+
+int xt_ipc_free(void *ptr) { return int(cudaFree(ptr)); }
+
+}  // extern "C"

@@ -551,3 +551,251 @@ int xt_moe_down(const DownParams *pp, const XtMailbox *mbp, int use_mb, int m, c
 }
 
 }  // extern "C"
+
+// ================================================================================================ expert parallelism
+// Four launches per MoE call on every rank (phase 0..3), all capturable in a CUDA graph:
+//   0 ep_dispatch   routes of this rank's tokens -> stores of the token rows and route metadata straight into the
+//                   owner ranks' receive slots (peer memory over NVLink), then a release flag per destination
+//   1 ep_gate_up    persistent: waits (bounded) for every source's flag, then SwiGLU(gate, up) of every received route
+//   2 ep_down_send  persistent: down projection of every received route; the epilogue stores the weighted FP32 row into
+//                   the source rank's return buffer and, once all of a source's routes are done, releases its flag
+//   3 ep_combine    waits (bounded) for every owner's return flag, sums each token's routes in route order (+ add)
+// The epoch in state[0] (advanced by the dispatch of every call, identically on every rank) tags the flags, so graph
+// replays need no host involvement. Waits poll this rank's own memory (peers write into it), never a peer's.
+namespace xt {
+
+constexpr int EP_MAX_ROUTES = 1024;   // T * k per rank
+constexpr int EP_MAX_W = 8;
+
+XT_DEV uint8_t *ep_buf(const EpParams &p, int r) { return reinterpret_cast<uint8_t *>(p.peer[r]); }
+
+XT_DEV bool ep_wait_flag(const volatile uint32_t *f, uint32_t epoch, unsigned long long timeout_ns) {
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(f) != epoch) {
+        if (globaltimer_ns() - t0 > timeout_ns) return false;
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
+    __shared__ int dest[EP_MAX_ROUTES], pos[EP_MAX_ROUTES];
+    __shared__ bool last;
+    const int n = p.T * p.k;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dest[i] = p.ids[i] / p.El;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        int c = 0;
+        for (int j = 0; j < i; ++j) c += dest[j] == dest[i];
+        pos[i] = c;   // slot of route i in its destination's region for this source (route order)
+    }
+    __syncthreads();
+    for (int i = blockIdx.x * nw + warp; i < n; i += gridDim.x * nw) {
+        const int d = dest[i], t = i / p.k;
+        uint8_t *base = ep_buf(p, d);
+        const size_t slot = size_t(p.rank) * p.R + pos[i];
+        uint4 *dst = reinterpret_cast<uint4 *>(base + p.off_rx + slot * p.H * 2);
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.x + size_t(t) * p.H);
+        for (int c = lane; c < p.H / 8; c += 32) dst[c] = src[c];
+        if (lane == 0) {
+            int4 m = make_int4(p.ids[i] % p.El, t, i % p.k, __float_as_int(p.w[i]));
+            *reinterpret_cast<int4 *>(base + p.off_meta + slot * 16) = m;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const unsigned prev = atomicAdd(&p.state[1], 1u);
+        last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x < p.W) {
+        const int d = threadIdx.x;
+        int c = 0;
+        for (int i = 0; i < n; ++i) c += dest[i] == d;
+        const uint32_t epoch = p.state[0] + 1;
+        uint8_t *base = ep_buf(p, d);
+        *reinterpret_cast<volatile int *>(base + p.off_cnt + size_t(p.rank) * 128) = c;
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<volatile uint32_t *>(base + p.off_flag + size_t(p.rank) * 128), epoch);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        p.state[0] = p.state[0] + 1;
+        p.state[1] = 0;
+    }
+}
+
+// every CTA: wait for all sources of this epoch, then read their counts into shared memory (prefix offsets)
+XT_DEV bool ep_gather_counts(const EpParams &p, uint32_t epoch, int *off /*[W+1]*/) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        int good = 1;
+        uint8_t *me = ep_buf(p, p.rank);
+        for (int s = 0; s < p.W && good; ++s)
+            good = ep_wait_flag(reinterpret_cast<const volatile uint32_t *>(me + p.off_flag + size_t(s) * 128), epoch,
+                                p.timeout_ns);
+        if (!good) atomicExch(p.error, 1);
+        off[0] = 0;
+        for (int s = 0; s < p.W; ++s)
+            off[s + 1] = off[s] + (good ? *reinterpret_cast<const volatile int *>(me + p.off_cnt + size_t(s) * 128) : 0);
+        ok = good;
+    }
+    __syncthreads();
+    return ok;
+}
+
+XT_DEV void ep_locate(const EpParams &p, const int *off, int r, int &s, int &slot) {
+    s = 0;
+    while (s + 1 < p.W && r >= off[s + 1]) ++s;
+    slot = s * p.R + (r - off[s]);
+}
+
+template <int LPR, int CH>
+__global__ void __launch_bounds__(GU_WARPS * 32) ep_gate_up_kernel(EpParams p) {
+    __shared__ int off[EP_MAX_W + 1];
+    const uint32_t epoch = p.state[0];
+    if (!ep_gather_counts(p, epoch, off)) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int RPW = 32 / LPR;
+    constexpr int ROWS = GU_WARPS * RPW;
+    const int q = lane % LPR, sub = lane / LPR;
+    const int yb_count = (p.I + ROWS - 1) / ROWS;
+    const int items = off[p.W] * yb_count;
+    const int bs = p.fmt == 0 ? 16 : 32;
+    const size_t wrow = p.H / 2, srow = p.H / bs;
+    const uint8_t *me = ep_buf(p, p.rank);
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const int r = it / yb_count, yb = it % yb_count;
+        int s, slot;
+        ep_locate(p, off, r, s, slot);
+        const int4 m = *reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16);
+        const int e = m.x;
+        __half2 xr[CH][16];
+        load_x_bf16<LPR, CH>(reinterpret_cast<const __nv_bfloat16 *>(me + p.off_rx + size_t(slot) * p.H * 2), q, xr);
+        const uint8_t *W = p.w13 + size_t(e) * 2 * p.I * wrow;
+        const uint8_t *S = p.s13 + size_t(e) * 2 * p.I * srow;
+        const int j_raw = yb * ROWS + warp * RPW + sub;
+        const int j = min(j_raw, p.I - 1);
+        float g = row_dot<LPR, CH>(W + j * wrow, S + j * srow, p.fmt, q, xr) * p.g13[2 * e];
+        float u = row_dot<LPR, CH>(W + (p.I + j) * wrow, S + (p.I + j) * srow, p.fmt, q, xr) * p.g13[2 * e + 1];
+        if (q == 0 && j_raw < p.I) p.mid[size_t(slot) * p.I + j] = g / (1.f + __expf(-g)) * u;
+    }
+}
+
+template <int LPR, int CH>
+__global__ void __launch_bounds__(GU_WARPS * 32) ep_down_send_kernel(EpParams p) {
+    __shared__ int off[EP_MAX_W + 1];
+    const uint32_t epoch = p.state[0];
+    if (!ep_gather_counts(p, epoch, off)) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int RPW = 32 / LPR;
+    constexpr int ROWS = GU_WARPS * RPW;
+    const int q = lane % LPR, sub = lane / LPR;
+    const int hb_count = (p.H + ROWS - 1) / ROWS;
+    const int items = off[p.W] * hb_count;
+    const int bs = p.fmt == 0 ? 16 : 32;
+    const size_t wrow = p.I / 2, srow = p.I / bs;
+    const uint8_t *me = ep_buf(p, p.rank);
+    // sources that sent nothing are answered at once
+    if (blockIdx.x == 0 && threadIdx.x < p.W && off[threadIdx.x + 1] == off[threadIdx.x]) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<volatile uint32_t *>(ep_buf(p, threadIdx.x) + p.off_rflag +
+                                                             size_t(p.rank) * 128),
+                       epoch);
+    }
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const int r = it / hb_count, hb = it % hb_count;
+        int s, slot;
+        ep_locate(p, off, r, s, slot);
+        const int4 m = *reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16);
+        const int e = m.x, t = m.y, j = m.z;
+        const float wt = __int_as_float(m.w) * p.g2[e];
+        __half2 xr[CH][16];
+        load_x_f32<LPR, CH>(p.mid + size_t(slot) * p.I, q, xr);
+        const uint8_t *W = p.w2 + size_t(e) * p.H * wrow;
+        const uint8_t *S = p.s2 + size_t(e) * p.H * srow;
+        const int h_raw = hb * ROWS + warp * RPW + sub;
+        const int h = min(h_raw, p.H - 1);
+        const float v = wt * row_dot<LPR, CH>(W + h * wrow, S + h * srow, p.fmt, q, xr);
+        if (q == 0 && h_raw < p.H) {
+            float *dst = reinterpret_cast<float *>(ep_buf(p, s) + p.off_ret) + (size_t(t) * p.k + j) * p.H + h;
+            *dst = v;   // straight into the source rank's return buffer
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            const unsigned need = unsigned(off[s + 1] - off[s]) * unsigned(hb_count);
+            const unsigned prev = atomicAdd(&p.state[8 + s], 1u);
+            if (prev == need - 1) {
+                p.state[8 + s] = 0;
+                st_release_sys(reinterpret_cast<volatile uint32_t *>(ep_buf(p, s) + p.off_rflag + size_t(p.rank) * 128),
+                               epoch);
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
+    __shared__ int ok;
+    const int t = blockIdx.x;
+    const uint32_t epoch = p.state[0];
+    if (threadIdx.x == 0) {
+        int good = 1;
+        const uint8_t *me = ep_buf(p, p.rank);
+        for (int d = 0; d < p.W && good; ++d)
+            good = ep_wait_flag(reinterpret_cast<const volatile uint32_t *>(me + p.off_rflag + size_t(d) * 128), epoch,
+                                p.timeout_ns);
+        if (!good) atomicExch(p.error, 1);
+        ok = good;
+    }
+    __syncthreads();
+    const float *ret = reinterpret_cast<const float *>(ep_buf(p, p.rank) + p.off_ret);
+    for (int h = threadIdx.x; h < p.H; h += blockDim.x) {
+        float v = 0.f;
+        if (ok)
+            for (int j = 0; j < p.k; ++j) v += __ldcv(ret + (size_t(t) * p.k + j) * p.H + h);
+        if (p.add) v += __bfloat162float(p.add[size_t(t) * p.H + h]);
+        p.out[size_t(t) * p.H + h] = __float2bfloat16(v);
+    }
+}
+
+}  // namespace xt
+
+#define XT_EP_CASE(KERNEL, L, C, ROWS_K)                                              \
+    if (lpr == L && ch == C) {                                                        \
+        KERNEL<L, C><<<grid, GU_WARPS * 32, 0, stream>>>(p);                          \
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;                            \
+    }
+
+extern "C" int xt_ep_moe(const EpParams *pp, int phase, cudaStream_t stream) {
+    EpParams p = *pp;
+    if (p.W > EP_MAX_W || p.T * p.k > EP_MAX_ROUTES || p.H % 256) return -2;
+    int sms = 148;
+    if (phase == 0) {
+        const int n = p.T * p.k;
+        const int grid = n < 8 ? 1 : (n + 63) / 64 > 64 ? 64 : (n + 63) / 64;
+        ep_dispatch_kernel<<<grid, 256, 0, stream>>>(p);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
+    if (phase == 3) {
+        ep_combine_kernel<<<p.T, 256, 0, stream>>>(p);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
+    const int grid = sms * 4;
+    int ch = 0;
+    const int lpr = pick_lpr(phase == 1 ? p.H / 2 : p.I / 2, &ch);
+    if (phase == 1) {
+        XT_EP_CASE(ep_gate_up_kernel, 32, 1, 0) XT_EP_CASE(ep_gate_up_kernel, 32, 2, 0)
+        XT_EP_CASE(ep_gate_up_kernel, 32, 4, 0) XT_EP_CASE(ep_gate_up_kernel, 32, 7, 0)
+        XT_EP_CASE(ep_gate_up_kernel, 16, 1, 0) XT_EP_CASE(ep_gate_up_kernel, 8, 1, 0)
+        XT_EP_CASE(ep_gate_up_kernel, 32, 5, 0) XT_EP_CASE(ep_gate_up_kernel, 16, 5, 0)
+    } else if (phase == 2) {
+        XT_EP_CASE(ep_down_send_kernel, 32, 1, 0) XT_EP_CASE(ep_down_send_kernel, 32, 2, 0)
+        XT_EP_CASE(ep_down_send_kernel, 8, 3, 0) XT_EP_CASE(ep_down_send_kernel, 8, 1, 0)
+        XT_EP_CASE(ep_down_send_kernel, 4, 1, 0) XT_EP_CASE(ep_down_send_kernel, 4, 5, 0)
+        XT_EP_CASE(ep_down_send_kernel, 16, 1, 0) XT_EP_CASE(ep_down_send_kernel, 32, 4, 0)
+    }
+    return -4;
+}

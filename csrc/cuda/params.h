@@ -89,3 +89,32 @@ int xt_gemm_tc(const void *A, const void *B, void *D, const void *R, int M, int 
                cudaStream_t stream);
 int xt_gemv_bf16(const void *x, const void *W, const void *add, void *y, int m, int N, int K, cudaStream_t stream);
 }
+
+namespace xt {
+// Expert-parallel MoE over symmetric peer memory (csrc/cuda/moe_decode.cu, ep_* kernels). Every rank holds the same
+// buffer layout; peer[r] is rank r's buffer as mapped in this process.
+//   rx    [W src][R][H] bf16     tokens received from each source rank
+//   meta  [W src][R] int4        {local expert, source token, source route, weight bits}
+//   cnt   [W src] int32 (128 B apart)   routes received from each source
+//   flag  [W src] uint32 (128 B apart)  epoch of the source's last dispatch into this buffer
+//   ret   [T*k][H] fp32          weighted expert outputs of this rank's own routes, written by the owner ranks
+//   rflag [W dst] uint32 (128 B apart)  epoch of the owner rank's last return into this buffer
+struct EpParams {
+    int W, rank, E, El, H, I, k, T, R, fmt;
+    const uint64_t *peer;        // [W] device array
+    size_t off_rx, off_meta, off_cnt, off_flag, off_ret, off_rflag;
+    const __nv_bfloat16 *x;      // [T, H]
+    const int32_t *ids;          // [T, k] global expert ids
+    const float *w;              // [T, k]
+    uint32_t *state;             // local: [0] epoch, [1] dispatch arrivals, [8 + s] down-send progress per source
+    float *mid;                  // local scratch [W*R, I]
+    const uint8_t *w13, *s13, *w2, *s2;   // this rank's El experts
+    const float *g13, *g2;
+    const __nv_bfloat16 *add;    // [T, H] extra term of the combine (shared experts), may be null
+    __nv_bfloat16 *out;          // [T, H]
+    unsigned long long timeout_ns;
+    int *error;
+};
+}  // namespace xt
+
+extern "C" int xt_ep_moe(const xt::EpParams *p, int phase, cudaStream_t stream);
