@@ -1,13 +1,13 @@
 // GQA decode attention over a contiguous BF16 KV cache [B, Hkv, L, D=128], split over the keys (flash-decoding).
 //
-// Grid (splits, Hkv, B), 4 warps. A CTA takes the G = Hq/Hkv query heads of one KV head and a contiguous key range,
-// walked in tiles of 128 keys with an online softmax:
+// Grid (splits, Hkv, B), 8 warps. A CTA takes the G = Hq/Hkv query heads of one KV head and a fixed slice of the cache
+// (L / splits keys, cut at the sequence length), walked in tiles of 256 keys with an online softmax:
 //   scores  each warp takes 32 keys, one per lane: the lane loads its key's 256-byte row (16 independent 16-byte
 //           loads in flight) and forms the G head dots against the pre-scaled queries in shared memory (broadcast
 //           reads), so no cross-lane reduction is needed.
 //   softmax one warp per head: tile max, running max and sum, exp2 in place.
-//   values  lane l accumulates dims 4l..4l+3 of all G heads; the probabilities are read from shared memory as
-//           [key][head] so G heads of one key are one or two vector loads.
+//   values  lane l accumulates dims 4l..4l+3 of all G heads; the warp's 32 value rows are loaded (8 bytes per lane)
+//           before the softmax, so the whole tile costs two memory round trips.
 // Each split writes its unnormalized output, max and sum to a workspace; the last CTA of a (batch, KV head) to finish
 // merges the splits (an arrival counter that it resets), so one launch does the whole step and the grid shape does not
 // depend on the sequence length (graph capture). Sequence lengths are read from device memory.
@@ -18,26 +18,40 @@
 
 namespace xt {
 
-constexpr int AD_WARPS = 4;
-constexpr int AD_TILE = 32 * AD_WARPS;
+constexpr int AD_WARPS = 8;
+constexpr int AD_TILE = 32 * AD_WARPS;   // keys per tile: one per lane
 constexpr int AD_D = 128;
+constexpr int AD_MAX_SPLITS = 64;
 
+template <int G>
+struct AdSmem {   // dynamic shared memory layout
+    static constexpr size_t S = size_t(AD_TILE) * G * 4;          // scores of a tile [key][head]
+    static constexpr size_t RED = size_t(AD_WARPS) * G * AD_D * 4;  // cross-warp reduction [warp][head][dim]
+    static constexpr size_t BUF = S > RED ? S : RED;
+    static constexpr size_t Q = size_t(G) * AD_D * 4;
+    static constexpr size_t BYTES = BUF + Q + 3 * G * 4 + AD_MAX_SPLITS * G * 4 + 64;
+};
 
 template <int G>
 __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodeParams p) {
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int N = p.seqlens[b];
-    int chunk = (N + p.splits - 1) / p.splits;
-    chunk = (chunk + 31) & ~31;
-    const int k_begin = split * chunk, k_end = min(N, k_begin + chunk);
-
-    // the score tile and the final cross-warp reduction never live at the same time: one buffer holds either
-    __shared__ __align__(16) float buf[AD_WARPS * G * AD_D];
+    extern __shared__ __align__(16) uint8_t dsm[];
+    float *buf = reinterpret_cast<float *>(dsm);
     float(&S)[AD_TILE][G] = *reinterpret_cast<float(*)[AD_TILE][G]>(buf);
     float(&red)[AD_WARPS][G][AD_D] = *reinterpret_cast<float(*)[AD_WARPS][G][AD_D]>(buf);
-    __shared__ __align__(16) float qs[G][AD_D];
-    __shared__ float m_run[G], l_run[G], alpha[G];
+    float(&qs)[G][AD_D] = *reinterpret_cast<float(*)[G][AD_D]>(dsm + AdSmem<G>::BUF);
+    float *m_run = reinterpret_cast<float *>(dsm + AdSmem<G>::BUF + AdSmem<G>::Q);
+    float *l_run = m_run + G, *alpha = l_run + G;
+    float(&wsplit)[AD_MAX_SPLITS][G] = *reinterpret_cast<float(*)[AD_MAX_SPLITS][G]>(alpha + G);
+    __shared__ bool last;
+
+    // the split's key range is a fixed slice of the cache, so the first tile's K loads need no sequence length
+    const int chunk = (p.L + p.splits - 1) / p.splits;
+    const int k_begin = split * chunk;
+    const size_t head_off = (size_t(b) * p.Hkv + kvh) * p.L;
+    const __nv_bfloat16 *K = p.kc + head_off * AD_D;
+    const __nv_bfloat16 *V = p.vc + head_off * AD_D;
 
     const __nv_bfloat16 *qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * G) * AD_D;
     for (int i = threadIdx.x; i < G * AD_D; i += blockDim.x) qs[i / AD_D][i % AD_D] = __bfloat162float(qb[i]) * p.scale_log2;
@@ -45,6 +59,8 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
         m_run[threadIdx.x] = -INFINITY;
         l_run[threadIdx.x] = 0.f;
     }
+    const int N = p.seqlens[b];
+    const int k_end = min(N, k_begin + chunk);
     __syncthreads();
     float acc[G][4];
 #pragma unroll
@@ -52,16 +68,12 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
 #pragma unroll
         for (int d = 0; d < 4; ++d) acc[h][d] = 0.f;
 
-    const size_t head_off = (size_t(b) * p.Hkv + kvh) * p.L;
-    const __nv_bfloat16 *K = p.kc + head_off * AD_D;
-    const __nv_bfloat16 *V = p.vc + head_off * AD_D;
-
     for (int t0 = k_begin; t0 < k_end; t0 += AD_TILE) {
-        // ---- scores: lane = key
+        // ---- scores: one key per lane, its whole 256-byte row in flight at once
         {
             const int key = t0 + warp * 32 + lane;
             const bool valid = key < k_end;
-            const uint4 *kr = reinterpret_cast<const uint4 *>(K + size_t(valid ? key : k_begin) * AD_D);
+            const uint4 *kr = reinterpret_cast<const uint4 *>(K + size_t(valid ? key : t0) * AD_D);
             uint4 kv[AD_D / 8];
 #pragma unroll
             for (int c = 0; c < AD_D / 8; ++c) kv[c] = kr[c];
@@ -89,6 +101,14 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
 #pragma unroll
             for (int h = 0; h < G; ++h) S[warp * 32 + lane][h] = valid ? s[h] : -INFINITY;
         }
+        // ---- this warp's 32 value rows (8 bytes per lane each) in flight while the softmax runs
+        const int nk = max(0, min(32, k_end - (t0 + warp * 32)));
+        uint2 vv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int key = t0 + warp * 32 + min(i, max(nk - 1, 0));
+            vv[i] = *reinterpret_cast<const uint2 *>(V + size_t(key) * AD_D + lane * 4);
+        }
         __syncthreads();
         // ---- online softmax per head
         for (int h = warp; h < G; h += AD_WARPS) {
@@ -112,34 +132,25 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
             }
         }
         __syncthreads();
-        // ---- values: lane owns dims 4l..4l+3, the warp walks its 32 keys eight at a time
+        // ---- values: lane owns dims 4l..4l+3 of every head
 #pragma unroll
         for (int h = 0; h < G; ++h) {
             const float a = alpha[h];
 #pragma unroll
             for (int d = 0; d < 4; ++d) acc[h][d] *= a;
         }
-        const int nk = min(32, k_end - (t0 + warp * 32));
-        for (int i0 = 0; i0 < nk; i0 += 8) {
-            uint2 vv[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int key = t0 + warp * 32 + min(i0 + i, nk - 1);
-                vv[i] = *reinterpret_cast<const uint2 *>(V + size_t(key) * AD_D + lane * 4);
-            }
+        for (int i = 0; i < 32; ++i) {
+            if (i >= nk) break;
+            const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&vv[i]);
+            float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (i0 + i >= nk) break;
-                const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&vv[i]);
-                float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
-#pragma unroll
-                for (int h = 0; h < G; ++h) {
-                    const float pr = S[warp * 32 + i0 + i][h];
-                    acc[h][0] += pr * f0.x;
-                    acc[h][1] += pr * f0.y;
-                    acc[h][2] += pr * f1.x;
-                    acc[h][3] += pr * f1.y;
-                }
+            for (int h = 0; h < G; ++h) {
+                const float pr = S[warp * 32 + i][h];
+                acc[h][0] += pr * f0.x;
+                acc[h][1] += pr * f0.y;
+                acc[h][2] += pr * f1.x;
+                acc[h][3] += pr * f1.y;
             }
         }
         __syncthreads();
@@ -162,8 +173,7 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
         p.ws_ml[(part + threadIdx.x) * 2] = m_run[threadIdx.x];
         p.ws_ml[(part + threadIdx.x) * 2 + 1] = l_run[threadIdx.x];
     }
-    // ---- the last split to arrive merges
-    __shared__ bool last;
+    // ---- the last split to arrive merges (arrival counter, reset by the merging CTA)
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -173,12 +183,8 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // merge: every split's (max, sum) into shared memory at once, one weight per (split, head), then each output
-    // element is a weighted sum over the splits whose loads are all independent (no serial L2 round trips)
-    constexpr int MAX_SPLITS = 64;
-    __shared__ float wsplit[MAX_SPLITS][G];
     const size_t base = (size_t(b) * p.Hkv + kvh) * p.splits * G;
-    float *mls = buf;   // the score / reduction buffer is free again
+    float *mls = buf;
     for (int i = threadIdx.x; i < p.splits * G * 2; i += blockDim.x) mls[i] = __ldcg(p.ws_ml + base * 2 + i);
     __syncthreads();
     if (threadIdx.x < G) {
@@ -196,33 +202,24 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
         for (int s = 0; s < p.splits; ++s) wsplit[s][h] *= inv;
     }
     __syncthreads();
-    // four consecutive dims per thread (16-byte loads), all splits' loads of a group issued back to back
+    // four consecutive dims per thread; every split's 16-byte load issued before any is used (up to 16 splits)
+    const size_t stride4 = size_t(G) * AD_D / 4;
     for (int i = threadIdx.x * 4; i < G * AD_D; i += blockDim.x * 4) {
         const int h = i / AD_D;
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 *src = reinterpret_cast<const float4 *>(p.ws_o + base * AD_D + i);
-        const size_t stride4 = size_t(G) * AD_D / 4;   // float4s between consecutive splits
-        int s = 0;
-        for (; s + 8 <= p.splits; s += 8) {
-            float4 v[8];
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < p.splits; s0 += 16) {
+            float4 v[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + (s + j) * stride4);
+            for (int j = 0; j < 16; ++j) v[j] = s0 + j < p.splits ? __ldcg(src + (s0 + j) * stride4) : make_float4(0, 0, 0, 0);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float wgt = wsplit[s + j][h];
+            for (int j = 0; j < 16; ++j) {
+                const float wgt = s0 + j < p.splits ? wsplit[s0 + j][h] : 0.f;
                 O.x += v[j].x * wgt;
                 O.y += v[j].y * wgt;
                 O.z += v[j].z * wgt;
                 O.w += v[j].w * wgt;
             }
-        }
-        for (; s < p.splits; ++s) {
-            const float4 v = __ldcg(src + s * stride4);
-            const float wgt = wsplit[s][h];
-            O.x += v.x * wgt;
-            O.y += v.y * wgt;
-            O.z += v.z * wgt;
-            O.w += v.w * wgt;
         }
         __nv_bfloat16 *dst = p.out + (size_t(b) * p.Hq + size_t(kvh) * G + h) * AD_D + i % AD_D;
         reinterpret_cast<__nv_bfloat162 *>(dst)[0] = __floats2bfloat162_rn(O.x, O.y);
@@ -238,15 +235,23 @@ using namespace xt;
 extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t stream) {
     AttnDecodeParams p = *pp;
     const int G = p.Hq / p.Hkv;
-    if (p.Hq % p.Hkv || p.splits < 1 || p.splits > 64) return -2;
+    if (p.Hq % p.Hkv || p.splits < 1 || p.splits > AD_MAX_SPLITS) return -2;
     dim3 grid(p.splits, p.Hkv, B);
+#define XT_AD(GG)                                                                                                  \
+    case GG: {                                                                                                     \
+        static bool attr = false;                                                                                  \
+        const int smem = int(AdSmem<GG>::BYTES);                                                                   \
+        if (!attr) {                                                                                               \
+            cudaFuncSetAttribute(attn_decode_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);       \
+            attr = true;                                                                                           \
+        }                                                                                                          \
+        attn_decode_kernel<GG><<<grid, AD_WARPS * 32, smem, stream>>>(p);                                          \
+        break;                                                                                                     \
+    }
     switch (G) {
-        case 1: attn_decode_kernel<1><<<grid, AD_WARPS * 32, 0, stream>>>(p); break;
-        case 2: attn_decode_kernel<2><<<grid, AD_WARPS * 32, 0, stream>>>(p); break;
-        case 4: attn_decode_kernel<4><<<grid, AD_WARPS * 32, 0, stream>>>(p); break;
-        case 8: attn_decode_kernel<8><<<grid, AD_WARPS * 32, 0, stream>>>(p); break;
-        case 16: attn_decode_kernel<16><<<grid, AD_WARPS * 32, 0, stream>>>(p); break;
+        XT_AD(1) XT_AD(2) XT_AD(4) XT_AD(8) XT_AD(16)
         default: return -3;
     }
+#undef XT_AD
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

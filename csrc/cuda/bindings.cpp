@@ -228,6 +228,53 @@ void gemm_tc(const Tensor &a, const Tensor &b, const std::optional<Tensor> &resi
              "gemm_tc");
 }
 
+void ep_moe(const Tensor &x, const Tensor &ids, const Tensor &w, const Tensor &peer, const Tensor &state,
+            const Tensor &mid, const Tensor &w13, const Tensor &s13, const Tensor &g13, const Tensor &w2,
+            const Tensor &s2, const Tensor &g2, const std::optional<Tensor> &add, const Tensor &out, const Tensor &err,
+            int64_t W, int64_t rank, int64_t E, int64_t fmt, int64_t R, std::vector<int64_t> offsets, double timeout_s,
+            int64_t phases) {
+    cuda_contig(x, "x");
+    xt::EpParams p{};
+    p.W = int(W);
+    p.rank = int(rank);
+    p.E = int(E);
+    p.El = int(E / W);
+    p.H = int(x.size(1));
+    p.I = int(w13.size(1) / 2);
+    p.k = int(ids.size(1));
+    p.T = int(x.size(0));
+    p.R = int(R);
+    p.fmt = int(fmt);
+    p.peer = ptr<const uint64_t>(peer);
+    check(offsets.size() == 6, "ep offsets");
+    p.off_rx = size_t(offsets[0]);
+    p.off_meta = size_t(offsets[1]);
+    p.off_cnt = size_t(offsets[2]);
+    p.off_flag = size_t(offsets[3]);
+    p.off_ret = size_t(offsets[4]);
+    p.off_rflag = size_t(offsets[5]);
+    p.x = ptr<const __nv_bfloat16>(x);
+    p.ids = ptr<const int32_t>(ids);
+    p.w = ptr<const float>(w);
+    p.state = ptr<uint32_t>(state);
+    p.mid = ptr<float>(mid);
+    p.w13 = ptr<const uint8_t>(w13);
+    p.s13 = ptr<const uint8_t>(s13);
+    p.g13 = ptr<const float>(g13);
+    p.w2 = ptr<const uint8_t>(w2);
+    p.s2 = ptr<const uint8_t>(s2);
+    p.g2 = ptr<const float>(g2);
+    p.add = optr<const __nv_bfloat16>(add);
+    p.out = ptr<__nv_bfloat16>(out);
+    p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+    p.error = ptr<int>(err);
+    check(p.T * p.k <= p.R, "ep: more routes than a receive region holds");
+    check(mid.numel() >= int64_t(W) * R * p.I, "ep mid scratch too small");
+    c10::cuda::CUDAGuard g(x.device());
+    for (int ph = 0; ph < 4; ++ph)
+        if ((phases >> ph) & 1) check_rc(xt_ep_moe(&p, ph, stream()), "ep_moe");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(xtier, m) {
@@ -241,6 +288,9 @@ TORCH_LIBRARY(xtier, m) {
           "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox) -> ()");
     m.def("gemv(Tensor x, Tensor w, Tensor? add, Tensor(a!) out) -> ()");
     m.def("gemm_tc(Tensor a, Tensor b, Tensor? residual, Tensor(a!) out, Tensor(b!) err) -> ()");
+    m.def("ep_moe(Tensor x, Tensor ids, Tensor w, Tensor peer, Tensor(a!) state, Tensor(b!) mid, Tensor w13, "
+          "Tensor s13, Tensor g13, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(c!) out, Tensor(d!) err, "
+          "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases) -> ()");
     m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
           "float limit, float alpha, float beta) -> ()");
     m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
@@ -256,4 +306,5 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("moe_down", &moe_down);
     m.impl("gemv", &gemv);
     m.impl("gemm_tc", &gemm_tc);
+    m.impl("ep_moe", &ep_moe);
 }

@@ -96,6 +96,7 @@ def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, ma
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
-    """Key splits of the decode attention: up to one 128-key tile per split, at most enough CTAs for two per SM."""
+    """Key splits of the decode attention: about one 256-key tile per split, at most enough CTAs for two per SM and
+    at most 64 splits (the merge reads every split's partial)."""
     want = max(1, (2 * sms + batch * kv_heads - 1) // (batch * kv_heads))
-    return max(1, min(64, want, (max_len + 127) // 128))
+    return max(1, min(64, want, (max_len + 255) // 256))

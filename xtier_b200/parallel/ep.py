@@ -1,0 +1,176 @@
+"""Expert-parallel MoE over NVLink peer memory, and its NCCL baseline.
+
+Expert e lives on rank e // (E / W). Each rank routes its own tokens, then one op (`torch.ops.xtier.ep_moe`, four
+kernels, csrc/cuda/moe_decode.cu) moves every route's token row into the owner's receive slot with in-kernel peer
+stores, computes the received routes on the owner's FP4 experts (W4A16, like the hot-slot decode kernels), stores each
+weighted result straight back into the source rank's return buffer from the down projection's epilogue, and sums
+each token's routes in route order. Flags carry a per-call epoch, so a CUDA graph replays the exchange with no host
+work, and every wait is bounded (a timeout sets the error word and the call's output lacks the missing parts).
+
+`EPComm` is shared by all MoE layers of a model (the layers run one after another): one symmetric buffer, the epoch
+state and the scratch. `nccl_ep_moe()` is the baseline the fused path is measured against: all_to_all_single of the
+routed rows and metadata, the same expert kernels locally, all_to_all_single back.
+
+(The reference refuses EP, xtier/backend/method.py:105; its second-GPU pool relays through host memory.)
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..formats import NVFP4, ExpertWeights
+from . import dist as xdist
+from .symm import SymmetricBuffer
+
+
+class EPComm:
+    def __init__(self, hidden: int, inter: int, experts: int, top_k: int, max_tokens: int, device=None,
+                 timeout_s: float = 10.0):
+        env = xdist.get()
+        self.W, self.rank = env.world, env.rank
+        self.H, self.I, self.E, self.k, self.T = hidden, inter, experts, top_k, max_tokens
+        if experts % self.W:
+            raise ValueError(f'{experts} experts do not split over {self.W} ranks')
+        self.El = experts // self.W
+        self.R = max_tokens * top_k   # worst case: every route of a source goes to one rank
+        self.device = device or env.device
+        W, R, H = self.W, self.R, hidden
+        off = 0
+        offs = []
+
+        def region(nbytes):
+            nonlocal off
+            offs.append(off)
+            off += (nbytes + 255) // 256 * 256
+
+        region(W * R * H * 2)          # rx
+        region(W * R * 16)             # meta
+        region(W * 128)                # cnt
+        region(W * 128)                # flag
+        region(max_tokens * top_k * H * 4)   # ret
+        region(W * 128)                # rflag
+        self.offsets = offs
+        self.buf = SymmetricBuffer(off, self.device)
+        self.state = torch.zeros(64, dtype=torch.int32, device=self.device)
+        self.mid = torch.empty(W * R * inter, dtype=torch.float32, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.timeout_s = timeout_s
+
+    def check(self):
+        if int(self.err.item()):
+            self.err.zero_()
+            raise RuntimeError('xtier_b200 EP: a wait for a peer rank timed out')
+
+    def close(self):
+        self.buf.close()
+
+
+class EPMoE:
+    """One MoE layer's routed experts split over the ranks (+ shared experts computed locally)."""
+
+    def __init__(self, layer: int, comm: EPComm, router_w: torch.Tensor, local: ExpertWeights, top_k: int,
+                 shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1, topk_group: int = 1,
+                 renorm: bool = True, scale: float = 1.0, router_bias=None, corr_bias=None):
+        self.comm = comm
+        self.layer = layer
+        self.k = top_k
+        self.local = local.to(comm.device).contiguous()
+        self.local.g13 = self.local.g13.float().contiguous()
+        self.local.g2 = self.local.g2.float().contiguous()
+        self.fmt_code = 0 if local.fmt == NVFP4 else 1
+        self.router = _Router(router_w, comm.E, top_k, mode, n_group, topk_group, renorm, scale, router_bias,
+                              corr_bias, comm.device, comm.T)
+        self.shared = _SharedExperts(shared, comm.device, comm.T) if shared is not None else None
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None):
+        c = self.comm
+        T = x.shape[0]
+        out = torch.empty_like(x) if out is None else out
+        ids, w = self.router(x)
+        extra = add
+        if self.shared is not None:
+            extra = self.shared(x, add)
+        torch.ops.xtier.ep_moe(x, ids, w, c.buf.peer_table, c.state, c.mid, self.local.w13, self.local.s13,
+                               self.local.g13, self.local.w2, self.local.s2, self.local.g2, extra, out, c.err, c.W,
+                               c.rank, c.E, self.fmt_code, c.R, c.offsets, c.timeout_s, 0xF)
+        return out
+
+
+class _Router:
+    def __init__(self, router_w, E, k, mode, n_group, topk_group, renorm, scale, bias, corr, device, max_tokens):
+        self.w = router_w.to(device, torch.bfloat16).contiguous()
+        self.E, self.k = E, k
+        self.mode, self.n_group, self.topk_group, self.renorm, self.scale = mode, n_group, topk_group, renorm, scale
+        self.bias = None if bias is None else bias.to(device, torch.float32).contiguous()
+        self.corr = None if corr is None else corr.to(device, torch.float32).contiguous()
+        self.ids = torch.empty(max_tokens, k, dtype=torch.int32, device=device)
+        self.wt = torch.empty(max_tokens, k, dtype=torch.float32, device=device)
+        self.slots = torch.empty(max_tokens, k, dtype=torch.int32, device=device)
+        self.ws_logits = torch.empty(max_tokens, E, dtype=torch.float32, device=device)
+        self.ws_count = torch.zeros(max_tokens, dtype=torch.int32, device=device)
+
+    def __call__(self, x):
+        T = x.shape[0]
+        ops.moe_route(x, self.w, self.bias, self.corr, None, None, self.ids[:T], self.wt[:T], self.slots[:T],
+                      self.ws_logits, self.ws_count, self.k, self.mode, self.n_group, self.topk_group, self.renorm,
+                      self.scale)
+        return self.ids[:T], self.wt[:T]
+
+
+class _SharedExperts:
+    """Shared experts of a layer on every rank: the decode expert kernels with one route per token per shared
+    expert, weight 1."""
+
+    def __init__(self, shared: ExpertWeights, device, max_tokens: int):
+        self.p = shared.to(device).contiguous()
+        self.p.g13 = self.p.g13.float().contiguous()
+        self.p.g2 = self.p.g2.float().contiguous()
+        n = shared.experts
+        self.fmt_code = 0 if shared.fmt == NVFP4 else 1
+        self.slots = torch.arange(n, dtype=torch.int32, device=device).repeat(max_tokens, 1).contiguous()
+        self.w = torch.ones(max_tokens, n, dtype=torch.float32, device=device)
+        self.mid = torch.empty(max_tokens * n, shared.inter, dtype=torch.float32, device=device)
+        self.out = torch.empty(max_tokens, shared.hidden, dtype=torch.bfloat16, device=device)
+
+    def __call__(self, x, add=None):
+        T = x.shape[0]
+        ops.moe_gate_up(x, self.slots[:T], self.p.w13, self.p.s13, self.p.g13, self.mid[:T * self.slots.shape[1]],
+                        self.fmt_code)
+        ops.moe_down(self.mid[:T * self.slots.shape[1]], self.slots[:T], self.w[:T], self.p.w2, self.p.s2, self.p.g2,
+                     add, self.out[:T], fmt=self.fmt_code)
+        return self.out[:T]
+
+
+def nccl_ep_moe(x, ids, w, local: ExpertWeights, E: int, group=None):
+    """Baseline: NCCL all-to-all of the routed rows, local expert compute, all-to-all back, route-ordered sum.
+    Returns bf16 [T, H]. Not graph-captured (data-dependent split sizes)."""
+    env = xdist.get()
+    W, T, k = env.world, x.shape[0], ids.shape[1]
+    El = E // W
+    dest = (ids // El).flatten()
+    order = torch.argsort(dest * (T * k) + torch.arange(T * k, device=x.device))   # by destination, route order
+    send_counts = torch.bincount(dest, minlength=W)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    sc, rc = send_counts.tolist(), recv_counts.tolist()
+    rows = x.repeat_interleave(k, 0)[order]
+    meta = torch.stack([(ids.flatten() % El)[order], w.flatten()[order].view(torch.int32)], 1).contiguous()
+    r_rows = torch.empty(sum(rc), x.shape[1], dtype=x.dtype, device=x.device)
+    r_meta = torch.empty(sum(rc), 2, dtype=torch.int32, device=x.device)
+    dist.all_to_all_single(r_rows, rows, rc, sc, group=group)
+    dist.all_to_all_single(r_meta, meta, rc, sc, group=group)
+    n = r_rows.shape[0]
+    y = torch.empty(n, x.shape[1], dtype=torch.bfloat16, device=x.device)
+    if n:
+        slots = r_meta[:, 0:1].contiguous()
+        wt = r_meta[:, 1:2].contiguous().view(torch.float32)
+        mid = torch.empty(n, local.inter, dtype=torch.float32, device=x.device)
+        fmt = 0 if local.fmt == NVFP4 else 1
+        ops.moe_gate_up(r_rows, slots, local.w13, local.s13, local.g13, mid, fmt)
+        ops.moe_down(mid, slots, wt, local.w2, local.s2, local.g2, None, y, fmt=fmt)
+    back = torch.empty(T * k, x.shape[1], dtype=torch.bfloat16, device=x.device)
+    dist.all_to_all_single(back, y, sc, rc, group=group)
+    res = torch.empty_like(back)
+    res[order] = back
+    return res.view(T, k, -1).float().sum(1).to(torch.bfloat16)
