@@ -255,3 +255,153 @@ extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t st
 #undef XT_AD
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
+
+// ================================================================================================================
+// xt_attn_decode_noalloc: the decode attention above for callers that cannot allocate device memory.
+//
+// This entry point has no counterpart in the reference. Some callers cannot call cudaMalloc: code that runs inside
+// another framework's memory pool with no allocator handed to it, plugins whose host process forbids allocation after
+// start-up, and real-time serving loops that must never hit the driver allocator. xt_attn_decode needs a workspace for
+// the split partials (output, max and sum per split and head) and arrival counters; here that workspace is a
+// file-scope device array of fixed size, so the caller passes only the inputs and the output.
+//
+//  * Limit: B * Hkv * splits * G * (128 + 2) floats must fit in XT_AD_NOALLOC_FLOATS (512 Ki floats, 2 MiB), and
+//    B * Hkv must not exceed XT_AD_NOALLOC_COUNTERS (4096); larger calls return XT_AD_NOALLOC_TOO_BIG and the text of
+//    xt_attn_decode_noalloc_error() says which limit was exceeded. Every GPU that loads this library holds the 2 MiB
+//    (plus 16 KiB of counters) until the process exits.
+//  * Set-up: the first call on a device looks up the array's device address with cudaGetSymbolAddress (and sets the
+//    kernels' shared-memory attribute) with that device current. Make that first call before any stream capture.
+//  * The array is shared by every call and keeps the last call's contents. Each call clears the arrival counters it
+//    uses (cudaMemsetAsync on its stream) before the kernel; calls that overlap on the GPU (different streams, or
+//    different host threads) race on the array and give wrong results: serialize them.
+//  * The call allocates nothing: no cudaMalloc, no cudaFree, no library routine that allocates.
+// ================================================================================================================
+#include <mutex>
+#include <string>
+
+#define XT_AD_NOALLOC_FLOATS (512 * 1024)
+#define XT_AD_NOALLOC_COUNTERS 4096
+#define XT_AD_NOALLOC_TOO_BIG (-6)
+
+static __device__ __align__(256) float xt_ad_noalloc_scratch[XT_AD_NOALLOC_FLOATS];
+static __device__ __align__(256) uint32_t xt_ad_noalloc_counters[XT_AD_NOALLOC_COUNTERS];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float *g_noalloc_scratch[kMaxDevices];
+uint32_t *g_noalloc_counters[kMaxDevices];
+thread_local std::string g_noalloc_err;
+
+// Device addresses of the arrays on the current device (looked up once per device). 0, or a CUDA error code.
+int noalloc_setup(int dev) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_scratch[dev]) return 0;
+    void *s = nullptr, *c = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&s, xt_ad_noalloc_scratch);
+    if (e != cudaSuccess) return int(e);
+    e = cudaGetSymbolAddress(&c, xt_ad_noalloc_counters);
+    if (e != cudaSuccess) return int(e);
+    e = cudaFuncSetAttribute(attn_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(AdSmem<1>::BYTES));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(AdSmem<2>::BYTES));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(AdSmem<4>::BYTES));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(AdSmem<8>::BYTES));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(AdSmem<16>::BYTES));
+    if (e != cudaSuccess) return int(e);
+    g_noalloc_counters[dev] = static_cast<uint32_t *>(c);
+    g_noalloc_scratch[dev] = static_cast<float *>(s);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+// q [B, Hq, 128] bf16, k_cache / v_cache [B, Hkv, L, 128] bf16, seqlens [B] int32 (device), out [B, Hq, 128] bf16;
+// all device pointers on the current device. Same result as xt_attn_decode with the same splits. Returns 0; -2 bad
+// arguments; XT_AD_NOALLOC_TOO_BIG when the workspace would exceed the fixed array; a positive CUDA error code from
+// the set-up; -1 when the launch failed.
+int xt_attn_decode_noalloc(const void *q, const void *k_cache, const void *v_cache, const int32_t *seqlens, void *out,
+                           int B, int Hq, int Hkv, int L, int splits, float scale, cudaStream_t stream) {
+    if (!q || !k_cache || !v_cache || !seqlens || !out || B < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv || L < 1 ||
+        splits < 1 || splits > AD_MAX_SPLITS) {
+        g_noalloc_err = "attn_decode_noalloc: bad arguments";
+        return -2;
+    }
+    const int G = Hq / Hkv;
+    const size_t units = size_t(B) * Hkv * splits * G;
+    if (units * (AD_D + 2) > size_t(XT_AD_NOALLOC_FLOATS)) {
+        g_noalloc_err = "attn_decode_noalloc: B * Hkv * splits * (Hq / Hkv) * 130 = " +
+                        std::to_string(units * (AD_D + 2)) + " floats exceeds the fixed workspace of " +
+                        std::to_string(XT_AD_NOALLOC_FLOATS) + " floats; use fewer splits or xt_attn_decode";
+        return XT_AD_NOALLOC_TOO_BIG;
+    }
+    if (size_t(B) * Hkv > size_t(XT_AD_NOALLOC_COUNTERS)) {
+        g_noalloc_err = "attn_decode_noalloc: B * Hkv exceeds the " + std::to_string(XT_AD_NOALLOC_COUNTERS) +
+                        " arrival counters of the fixed workspace";
+        return XT_AD_NOALLOC_TOO_BIG;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        g_noalloc_err = "attn_decode_noalloc: no current device";
+        return -2;
+    }
+    const int rc = noalloc_setup(dev);
+    if (rc != 0) {
+        g_noalloc_err = "attn_decode_noalloc: cudaGetSymbolAddress / attribute set-up failed";
+        return rc;
+    }
+    // the counters must start at zero; everything else is written before it is read
+    if (cudaMemsetAsync(g_noalloc_counters[dev], 0, sizeof(uint32_t) * size_t(B) * Hkv, stream) != cudaSuccess) {
+        g_noalloc_err = "attn_decode_noalloc: clearing the counters failed";
+        return -1;
+    }
+    AttnDecodeParams p{};
+    p.q = static_cast<const __nv_bfloat16 *>(q);
+    p.kc = static_cast<const __nv_bfloat16 *>(k_cache);
+    p.vc = static_cast<const __nv_bfloat16 *>(v_cache);
+    p.seqlens = seqlens;
+    p.out = static_cast<__nv_bfloat16 *>(out);
+    p.ws_o = g_noalloc_scratch[dev];
+    p.ws_ml = g_noalloc_scratch[dev] + units * AD_D;
+    p.counters = g_noalloc_counters[dev];
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.L = L;
+    p.splits = splits;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    dim3 grid(splits, Hkv, B);
+    switch (G) {
+        case 1: attn_decode_kernel<1><<<grid, AD_WARPS * 32, AdSmem<1>::BYTES, stream>>>(p); break;
+        case 2: attn_decode_kernel<2><<<grid, AD_WARPS * 32, AdSmem<2>::BYTES, stream>>>(p); break;
+        case 4: attn_decode_kernel<4><<<grid, AD_WARPS * 32, AdSmem<4>::BYTES, stream>>>(p); break;
+        case 8: attn_decode_kernel<8><<<grid, AD_WARPS * 32, AdSmem<8>::BYTES, stream>>>(p); break;
+        case 16: attn_decode_kernel<16><<<grid, AD_WARPS * 32, AdSmem<16>::BYTES, stream>>>(p); break;
+        default: g_noalloc_err = "attn_decode_noalloc: Hq / Hkv must be 1, 2, 4, 8 or 16"; return -2;
+    }
+    if (cudaGetLastError() != cudaSuccess) {
+        g_noalloc_err = "attn_decode_noalloc: launch failed";
+        return -1;
+    }
+    return 0;
+}
+
+// Text of the last error of xt_attn_decode_noalloc on this host thread.
+const char *xt_attn_decode_noalloc_error(void) { return g_noalloc_err.c_str(); }
+
+// The fixed workspace limits: out[0] = floats of the split workspace, out[1] = arrival counters.
+void xt_attn_decode_noalloc_limits(long long *out) {
+    out[0] = XT_AD_NOALLOC_FLOATS;
+    out[1] = XT_AD_NOALLOC_COUNTERS;
+}
+
+}  // extern "C"
