@@ -77,22 +77,38 @@ def gemv(x, w, out, add=None):
     return out
 
 
+_gemm_err: dict = {}
+
+
+def gemm_error_word(device) -> torch.Tensor:
+    """The tcgen05 GEMM's error word of `device` (non-zero after a bounded wait in the kernel ran out)."""
+    key = torch.device(device)
+    if key not in _gemm_err:
+        _gemm_err[key] = torch.zeros(1, dtype=torch.int32, device=key)
+    return _gemm_err[key]
+
+
+def gemm(a, b, out=None, residual=None):
+    """out[M, N] = a[M, K] . b[N, K]^T (+ residual) on the tcgen05 tensor cores (TMA, TMEM, persistent)."""
+    M, N = a.numel() // a.shape[-1], b.shape[0]
+    out = torch.empty(*a.shape[:-1], N, dtype=a.dtype, device=a.device) if out is None else out
+    _ops().gemm_tc(a, b, residual, out, gemm_error_word(a.device))
+    return out
+
+
 def linear(x, w, out=None):
-    """x @ w^T: the weight-streaming GEMV for decode-sized inputs, cuBLAS otherwise."""
+    """x @ w^T in BF16: the weight-streaming GEMV for decode-sized inputs (<= 16 rows), the tcgen05 GEMM for larger
+    ones (cuBLAS only for shapes TMA cannot describe: K not a multiple of 8 or unaligned rows)."""
     m = x.numel() // x.shape[-1]
-    if m <= 16 and x.shape[-1] * m * 2 <= 200 * 1024 and x.is_contiguous():
+    K = x.shape[-1]
+    if m <= 16 and K * m * 2 <= 200 * 1024 and x.is_contiguous():
         out = torch.empty(*x.shape[:-1], w.shape[0], dtype=x.dtype, device=x.device) if out is None else out
         _ops().gemv(x, w, None, out)
         return out
+    if (x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.is_contiguous() and w.is_contiguous()
+            and K % 8 == 0 and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0 and x.is_cuda):
+        return gemm(x, w, out)
     return torch.matmul(x, w.t(), out=out) if out is not None else torch.matmul(x, w.t())
-
-
-def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0):
-    _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta)
-
-
-def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0, gpu_part=None):
-    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, gpu_part, fmt, mailbox)
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
