@@ -1,0 +1,73 @@
+"""Console on the CPU: every option value of every card builds a command, the page renders, the API answers, POSTs
+without the console header are refused, and a launch starts and stops a (stand-in) server process group."""
+import itertools
+import json
+import threading
+import urllib.error
+import urllib.request
+from http.server import ThreadingHTTPServer
+
+import pytest
+
+from xtier_b200.console import __main__ as cmain
+from xtier_b200.console import core
+
+
+def test_every_option_builds_a_command():
+    cards = core.load_cards()
+    assert {'qwen3-moe', 'deepseek-v3'} <= set(cards)
+    for card in cards.values():
+        opts = card['options']
+        for o in opts:
+            for value, _ in o['choices']:
+                argv, env, resolved = core.Console.command.__get__(type('C', (), {'cards': cards})())(
+                    card['id'], {o['key']: value})
+                assert argv and all(isinstance(a, str) for a in argv)
+                assert resolved[o['key']] == value
+                assert all(isinstance(v, str) for v in env.values())
+        with pytest.raises(ValueError):
+            core.validate(card, {'no_such_option': '1'})
+        with pytest.raises(ValueError):
+            core.validate(card, {opts[0]['key']: 'not-a-choice'})
+
+
+def _serve(console):
+    srv = ThreadingHTTPServer(('127.0.0.1', 0), cmain.make_handler(console, cmain.Jobs(console)))
+    threading.Thread(target=srv.serve_forever, daemon=True).start()
+    return srv, f'http://127.0.0.1:{srv.server_address[1]}'
+
+
+def test_page_api_and_post_guard(tmp_path):
+    console = core.Console(tmp_path)
+    srv, url = _serve(console)
+    try:
+        page = urllib.request.urlopen(url + '/').read().decode()
+        assert 'xtier_b200 console' in page and 'qwen3-moe' in page
+        st = json.loads(urllib.request.urlopen(url + '/api/status').read())
+        assert st['running'] is False and 'qwen3-moe' in st['models']
+        req = urllib.request.Request(url + '/api/stop', data=b'{}', method='POST',
+                                     headers={'Content-Type': 'application/json'})
+        with pytest.raises(urllib.error.HTTPError) as e:
+            urllib.request.urlopen(req)
+        assert e.value.code == 403
+        req = urllib.request.Request(url + '/api/start', data=json.dumps({'model': 'nope'}).encode(), method='POST',
+                                     headers={'Content-Type': 'application/json', 'X-Xtier-Console': '1'})
+        with pytest.raises(urllib.error.HTTPError) as e:
+            urllib.request.urlopen(req)
+        assert e.value.code == 400
+    finally:
+        srv.shutdown()
+
+
+def test_start_and_stop_a_server_process(tmp_path):
+    cfg = tmp_path / 'cfg' / 'dummy'
+    cfg.mkdir(parents=True)
+    (cfg / 'console.py').write_text(
+        "MODEL = {'id': 'dummy', 'name': 'dummy', 'port': 1, 'options': []}\n"
+        "def build(options, port):\n"
+        "    return ['python', '-c', 'import time; print(\"up\", flush=True); time.sleep(60)'], {}\n")
+    console = core.Console(tmp_path / 'state', config_dir=tmp_path / 'cfg')
+    cur = console.start('dummy', {})
+    assert cur['pid'] > 0 and console.status()['running']
+    assert console.stop() is True
+    assert not console.status()['running']

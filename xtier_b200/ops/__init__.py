@@ -111,6 +111,14 @@ def linear(x, w, out=None):
     return torch.matmul(x, w.t(), out=out) if out is not None else torch.matmul(x, w.t())
 
 
+def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0):
+    _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta)
+
+
+def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0, gpu_part=None):
+    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, gpu_part, fmt, mailbox)
+
+
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
     """Key splits of the decode attention: about one 256-key tile per split, at most enough CTAs for two per SM and
     at most 64 splits (the merge reads every split's partial)."""
