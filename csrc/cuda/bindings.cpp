@@ -275,6 +275,56 @@ void ep_moe(const Tensor &x, const Tensor &ids, const Tensor &w, const Tensor &p
         if ((phases >> ph) & 1) check_rc(xt_ep_moe(&p, ph, stream()), "ep_moe");
 }
 
+xt::TpParams tp_params(const Tensor &peer, const Tensor &state, const Tensor &out, const Tensor &err, int64_t M,
+                       int64_t N, int64_t K, int64_t W, int64_t rank, const std::vector<int64_t> &offs,
+                       double timeout_s) {
+    check(offs.size() == 4, "tp offsets: data0, data1, flags0, flags1");
+    xt::TpParams p{};
+    p.M = int(M);
+    p.N = int(N);
+    p.K = int(K);
+    p.W = int(W);
+    p.rank = int(rank);
+    p.peer = ptr<const uint64_t>(peer);
+    p.off_data[0] = size_t(offs[0]);
+    p.off_data[1] = size_t(offs[1]);
+    p.off_flags[0] = size_t(offs[2]);
+    p.off_flags[1] = size_t(offs[3]);
+    p.state = ptr<uint32_t>(state);
+    p.out = ptr<__nv_bfloat16>(out);
+    p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+    p.error = ptr<int>(err);
+    return p;
+}
+
+void gemm_rs(const Tensor &a, const Tensor &b, const Tensor &peer, const Tensor &state,
+             const std::optional<Tensor> &residual, const Tensor &out, const Tensor &err, int64_t W, int64_t rank,
+             std::vector<int64_t> offs, double timeout_s) {
+    cuda_contig(a, "a");
+    cuda_contig(b, "b");
+    cuda_contig(out, "out");
+    const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+    check(b.size(1) == K && out.numel() == M / W * N, "gemm_rs shapes");
+    xt::TpParams p = tp_params(peer, state, out, err, M, N, K, W, rank, offs, timeout_s);
+    p.residual = optr<const __nv_bfloat16>(residual);
+    c10::cuda::CUDAGuard g(a.device());
+    check_rc(xt_gemm_rs(a.data_ptr(), b.data_ptr(), &p, stream()), "gemm_rs");
+}
+
+void ag_gemm(const Tensor &a_shard, const Tensor &b, const Tensor &peer, int64_t local_base, const Tensor &state,
+             const Tensor &out, const Tensor &err, int64_t W, int64_t rank, std::vector<int64_t> offs,
+             double timeout_s) {
+    cuda_contig(a_shard, "a_shard");
+    cuda_contig(b, "b");
+    cuda_contig(out, "out");
+    const int64_t M = a_shard.size(0) * W, K = a_shard.size(1), N = b.size(0);
+    check(b.size(1) == K && out.numel() == M * N, "ag_gemm shapes");
+    xt::TpParams p = tp_params(peer, state, out, err, M, N, K, W, rank, offs, timeout_s);
+    p.a_shard = ptr<const __nv_bfloat16>(a_shard);
+    c10::cuda::CUDAGuard g(a_shard.device());
+    check_rc(xt_ag_gemm(b.data_ptr(), reinterpret_cast<const void *>(local_base), &p, stream()), "ag_gemm");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(xtier, m) {
@@ -291,6 +341,10 @@ TORCH_LIBRARY(xtier, m) {
     m.def("ep_moe(Tensor x, Tensor ids, Tensor w, Tensor peer, Tensor(a!) state, Tensor(b!) mid, Tensor w13, "
           "Tensor s13, Tensor g13, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(c!) out, Tensor(d!) err, "
           "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases) -> ()");
+    m.def("gemm_rs(Tensor a, Tensor b, Tensor peer, Tensor(a!) state, Tensor? residual, Tensor(b!) out, "
+          "Tensor(c!) err, int W, int rank, int[] offsets, float timeout_s) -> ()");
+    m.def("ag_gemm(Tensor a_shard, Tensor b, Tensor peer, int local_base, Tensor(a!) state, Tensor(b!) out, "
+          "Tensor(c!) err, int W, int rank, int[] offsets, float timeout_s) -> ()");
     m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
           "float limit, float alpha, float beta) -> ()");
     m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
@@ -307,4 +361,6 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("gemv", &gemv);
     m.impl("gemm_tc", &gemm_tc);
     m.impl("ep_moe", &ep_moe);
+    m.impl("gemm_rs", &gemm_rs);
+    m.impl("ag_gemm", &ag_gemm);
 }

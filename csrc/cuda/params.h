@@ -118,3 +118,25 @@ struct EpParams {
 }  // namespace xt
 
 extern "C" int xt_ep_moe(const xt::EpParams *p, int phase, cudaStream_t stream);
+
+namespace xt {
+// Tensor-parallel GEMMs fused with their collective (csrc/cuda/gemm_tp.cu).
+struct TpParams {
+    int M, N, K, W, rank;
+    const uint64_t *peer;       // [W] symmetric buffer bases (this process's mappings)
+    size_t off_data[2];         // RS: receive region [W][M/W][N] bf16; AG: gather region [M][K] bf16 (per parity)
+    size_t off_flags[2];        // RS: [W][tiles per owner] u32; AG: [M/128] u32 (per parity)
+    uint32_t *state;            // local: [0] epoch, [1] arrivals of the reduce
+    __nv_bfloat16 *out;         // RS: [M/W, N] reduced rows of this rank; AG: [M, N]
+    const __nv_bfloat16 *residual;   // RS: [M/W, N] added to the reduced rows, may be null
+    const __nv_bfloat16 *a_shard;    // AG push: [M/W, K]
+    unsigned long long timeout_ns;
+    int *error;
+};
+}  // namespace xt
+
+extern "C" {
+int xt_gemm_rs(const void *a, const void *b, const xt::TpParams *p, cudaStream_t stream);
+int xt_ag_gemm(const void *b, const void *local_base, const xt::TpParams *p, cudaStream_t stream);
+}
+

@@ -152,14 +152,15 @@ def nccl_ep_moe(x, ids, w, local: ExpertWeights, E: int, group=None):
     order = torch.argsort(dest * (T * k) + torch.arange(T * k, device=x.device))   # by destination, route order
     send_counts = torch.bincount(dest, minlength=W)
     recv_counts = torch.empty_like(send_counts)
-    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    a2a = dist.all_to_all_single if W > 1 else (lambda o, i, *a, **k: o.copy_(i))
+    a2a(recv_counts, send_counts, group=group)
     sc, rc = send_counts.tolist(), recv_counts.tolist()
     rows = x.repeat_interleave(k, 0)[order]
     meta = torch.stack([(ids.flatten() % El)[order], w.flatten()[order].view(torch.int32)], 1).contiguous()
     r_rows = torch.empty(sum(rc), x.shape[1], dtype=x.dtype, device=x.device)
     r_meta = torch.empty(sum(rc), 2, dtype=torch.int32, device=x.device)
-    dist.all_to_all_single(r_rows, rows, rc, sc, group=group)
-    dist.all_to_all_single(r_meta, meta, rc, sc, group=group)
+    a2a(r_rows, rows, rc, sc, group=group)
+    a2a(r_meta, meta, rc, sc, group=group)
     n = r_rows.shape[0]
     y = torch.empty(n, x.shape[1], dtype=torch.bfloat16, device=x.device)
     if n:
@@ -170,7 +171,7 @@ def nccl_ep_moe(x, ids, w, local: ExpertWeights, E: int, group=None):
         ops.moe_gate_up(r_rows, slots, local.w13, local.s13, local.g13, mid, fmt)
         ops.moe_down(mid, slots, wt, local.w2, local.s2, local.g2, None, y, fmt=fmt)
     back = torch.empty(T * k, x.shape[1], dtype=torch.bfloat16, device=x.device)
-    dist.all_to_all_single(back, y, sc, rc, group=group)
+    a2a(back, y, sc, rc, group=group)
     res = torch.empty_like(back)
     res[order] = back
     return res.view(T, k, -1).float().sum(1).to(torch.bfloat16)
