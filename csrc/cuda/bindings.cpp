@@ -257,7 +257,8 @@ void ep_moe(const Tensor &x, const Tensor &ids, const Tensor &w, const Tensor &p
     p.ids = ptr<const int32_t>(ids);
     p.w = ptr<const float>(w);
     p.state = ptr<uint32_t>(state);
-    p.mid = ptr<float>(mid);
+    check(mid.scalar_type() == at::kHalf, "ep mid scratch must be float16");
+    p.mid = ptr<__half>(mid);
     p.w13 = ptr<const uint8_t>(w13);
     p.s13 = ptr<const uint8_t>(s13);
     p.g13 = ptr<const float>(g13);

@@ -19,6 +19,7 @@
 #include "../include/xt_mailbox.h"
 #include "common.cuh"
 #include "params.h"
+#include "fp4_stream.cuh"
 
 #include <stdio.h>
 
@@ -556,9 +557,10 @@ int xt_moe_down(const DownParams *pp, const XtMailbox *mbp, int use_mb, int m, c
 // Four launches per MoE call on every rank (phase 0..3), all capturable in a CUDA graph:
 //   0 ep_dispatch   routes of this rank's tokens -> stores of the token rows and route metadata straight into the
 //                   owner ranks' receive slots (peer memory over NVLink), then a release flag per destination
-//   1 ep_gate_up    persistent: waits (bounded) for every source's flag, then SwiGLU(gate, up) of every received route
-//   2 ep_down_send  persistent: down projection of every received route; the epilogue stores the weighted FP32 row into
-//                   the source rank's return buffer and, once all of a source's routes are done, releases its flag
+//   1 ep_gate_up    persistent: waits (bounded) for every source's flag, then SwiGLU(gate, up) of every received route,
+//                   weights streamed through a shared-memory ring by bulk copies (fp4_stream.cuh)
+//   2 ep_down       persistent, same streaming: down projection of every received route; the epilogue stores the
+//                   weighted FP32 rows into the source rank's return buffer, and the last CTA releases the flags
 //   3 ep_combine    waits (bounded) for every owner's return flag, sums each token's routes in route order (+ add)
 // The epoch in state[0] (advanced by the dispatch of every call, identically on every rank) tags the flags, so graph
 // replays need no host involvement. Waits poll this rank's own memory (peers write into it), never a peer's.
@@ -596,7 +598,15 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
         const size_t slot = size_t(p.rank) * p.R + pos[i];
         uint4 *dst = reinterpret_cast<uint4 *>(base + p.off_rx + slot * p.H * 2);
         const uint4 *src = reinterpret_cast<const uint4 *>(p.x + size_t(t) * p.H);
-        for (int c = lane; c < p.H / 8; c += 32) dst[c] = src[c];
+        for (int c = lane; c < p.H / 8; c += 32) {   // BF16 in, f16 on the wire (the expert kernels compute in f16x2)
+            uint4 v = src[c];
+            const __nv_bfloat162 *b = reinterpret_cast<const __nv_bfloat162 *>(&v);
+            uint4 o;
+            __half2 *h = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) h[q] = __float22half2_rn(__bfloat1622float2(b[q]));
+            dst[c] = o;
+        }
         if (lane == 0) {
             int4 m = make_int4(p.ids[i] % p.El, t, i % p.k, __float_as_int(p.w[i]));
             *reinterpret_cast<int4 *>(base + p.off_meta + slot * 16) = m;
@@ -652,88 +662,153 @@ XT_DEV void ep_locate(const EpParams &p, const int *off, int r, int &s, int &slo
     slot = s * p.R + (r - off[s]);
 }
 
-template <int LPR, int CH>
-__global__ void __launch_bounds__(GU_WARPS * 32) ep_gate_up_kernel(EpParams p) {
+// Phase 1, persistent: items = (received route, R/2 rows of gate and the same R/2 rows of up) streamed through the
+// shared-memory ring of fp4_stream.cuh; row group rs owns gate rows [rs*RPW/2, (rs+1)*RPW/2) and the matching up rows,
+// so SwiGLU is applied where the sums meet. Each CTA takes a contiguous range of items (few route changes, so the
+// activation slice and the metadata load rarely). mid is f16 [W*R, I].
+template <int RPW>
+__global__ void __launch_bounds__(fs::THREADS, 1) ep_gate_up_stream(EpParams p, fs::Geo geo) {
+    extern __shared__ uint8_t smem_raw[];
     __shared__ int off[EP_MAX_W + 1];
+    __shared__ volatile int abort_flag;
     const uint32_t epoch = p.state[0];
     if (!ep_gather_counts(p, epoch, off)) return;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int RPW = 32 / LPR;
-    constexpr int ROWS = GU_WARPS * RPW;
-    const int q = lane % LPR, sub = lane / LPR;
-    const int yb_count = (p.I + ROWS - 1) / ROWS;
-    const int items = off[p.W] * yb_count;
-    const int bs = p.fmt == 0 ? 16 : 32;
-    const size_t wrow = p.H / 2, srow = p.H / bs;
+    const fs::Ring ring = fs::ring_init(smem_raw, geo, &abort_flag, p.error);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int half = geo.R / 2;
+    const int nrb = p.I / half;
+    const int items = off[p.W] * nrb;
+    const int it0 = int((long long)items * blockIdx.x / gridDim.x);
+    const int it1 = int((long long)items * (blockIdx.x + 1) / gridDim.x);
     const uint8_t *me = ep_buf(p, p.rank);
-    for (int it = blockIdx.x; it < items; it += gridDim.x) {
-        const int r = it / yb_count, yb = it % yb_count;
-        int s, slot;
-        ep_locate(p, off, r, s, slot);
-        const int4 m = *reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16);
-        const int e = m.x;
-        __half2 xr[CH][16];
-        load_x_bf16<LPR, CH>(reinterpret_cast<const __nv_bfloat16 *>(me + p.off_rx + size_t(slot) * p.H * 2), q, xr);
-        const uint8_t *W = p.w13 + size_t(e) * 2 * p.I * wrow;
-        const uint8_t *S = p.s13 + size_t(e) * 2 * p.I * srow;
-        const int j_raw = yb * ROWS + warp * RPW + sub;
-        const int j = min(j_raw, p.I - 1);
-        float g = row_dot<LPR, CH>(W + j * wrow, S + j * srow, p.fmt, q, xr) * p.g13[2 * e];
-        float u = row_dot<LPR, CH>(W + (p.I + j) * wrow, S + (p.I + j) * srow, p.fmt, q, xr) * p.g13[2 * e + 1];
-        if (q == 0 && j_raw < p.I) p.mid[size_t(slot) * p.I + j] = g / (1.f + __expf(-g)) * u;
+    fs::Cursor cur_ring;
+    if (warp == fs::CW) {
+        uint32_t filled = 0;
+        int cur = -1, e = 0;
+        for (int it = it0; it < it1; ++it) {
+            const int r = it / nrb, rb = it % nrb;
+            if (r != cur) {
+                int s, slot;
+                ep_locate(p, off, r, s, slot);
+                e = reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x;
+                cur = r;
+            }
+            const size_t g0 = size_t(e) * 2 * p.I + size_t(rb) * half, u0 = g0 + p.I;
+            const fs::Run runs[2] = {{p.w13 + g0 * geo.wrow, p.s13 + g0 * geo.srow, half, 0},
+                                     {p.w13 + u0 * geo.wrow, p.s13 + u0 * geo.srow, half, half}};
+            if (!fs::produce(ring, geo, runs, 2, cur_ring, filled)) break;
+        }
+        fs::produce_drain(ring, geo, filled);
+        return;
+    }
+    fs::Lane L = fs::lane_setup(geo);
+    constexpr int H2 = RPW / 2, STRIDE = 32 / RPW;
+    int rows[RPW];
+#pragma unroll
+    for (int i = 0; i < H2; ++i) {
+        rows[i] = L.rs * H2 + i;
+        rows[H2 + i] = half + L.rs * H2 + i;
+    }
+    int cur = -1, slot = 0;
+    float gg = 0.f, gu = 0.f;
+    for (int it = it0; it < it1; ++it) {
+        const int r = it / nrb, rb = it % nrb;
+        if (r != cur) {
+            int s;
+            ep_locate(p, off, r, s, slot);
+            fs::lane_load_x(L, reinterpret_cast<const __half *>(me + p.off_rx + size_t(slot) * p.H * 2));
+            const int e = reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x;
+            gg = p.g13[2 * e];
+            gu = p.g13[2 * e + 1];
+            cur = r;
+        }
+        float v;
+        const int st = fs::consume<RPW>(ring, geo, L, rows, v, cur_ring);
+        if (!st) break;
+        const float u = __shfl_xor_sync(0xffffffffu, v, 16);
+        if (st == 1 && lane < 16 && lane % STRIDE == 0) {
+            const float g = v * gg, uu = u * gu;
+            p.mid[size_t(slot) * p.I + rb * half + L.rs * H2 + lane / STRIDE] =
+                __float2half_rn(g / (1.f + __expf(-g)) * uu);
+        }
     }
 }
 
-template <int LPR, int CH>
-__global__ void __launch_bounds__(GU_WARPS * 32) ep_down_send_kernel(EpParams p) {
+// Phase 2, persistent: items = (received route, R rows of the down projection); row group rs owns rows
+// [rs*RPW, (rs+1)*RPW) and stores them with one coalesced store straight into the source rank's return buffer (peer
+// memory over NVLink). Every thread fences its stores at system scope before the CTA counts itself done; the last CTA
+// releases every source's return flag.
+template <int RPW>
+__global__ void __launch_bounds__(fs::THREADS, 1) ep_down_stream(EpParams p, fs::Geo geo) {
+    extern __shared__ uint8_t smem_raw[];
     __shared__ int off[EP_MAX_W + 1];
+    __shared__ volatile int abort_flag;
+    __shared__ bool last;
     const uint32_t epoch = p.state[0];
     if (!ep_gather_counts(p, epoch, off)) return;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int RPW = 32 / LPR;
-    constexpr int ROWS = GU_WARPS * RPW;
-    const int q = lane % LPR, sub = lane / LPR;
-    const int hb_count = (p.H + ROWS - 1) / ROWS;
-    const int items = off[p.W] * hb_count;
-    const int bs = p.fmt == 0 ? 16 : 32;
-    const size_t wrow = p.I / 2, srow = p.I / bs;
+    const fs::Ring ring = fs::ring_init(smem_raw, geo, &abort_flag, p.error);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nrb = p.H / geo.R;
+    const int items = off[p.W] * nrb;
+    const int it0 = int((long long)items * blockIdx.x / gridDim.x);
+    const int it1 = int((long long)items * (blockIdx.x + 1) / gridDim.x);
     const uint8_t *me = ep_buf(p, p.rank);
-    // sources that sent nothing are answered at once
-    if (blockIdx.x == 0 && threadIdx.x < p.W && off[threadIdx.x + 1] == off[threadIdx.x]) {
+    fs::Cursor cur_ring;
+    if (warp == fs::CW) {
+        uint32_t filled = 0;
+        int cur = -1, e = 0;
+        for (int it = it0; it < it1; ++it) {
+            const int r = it / nrb, hb = it % nrb;
+            if (r != cur) {
+                int s, slot;
+                ep_locate(p, off, r, s, slot);
+                e = reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x;
+                cur = r;
+            }
+            const size_t row0 = size_t(e) * p.H + size_t(hb) * geo.R;
+            const fs::Run run = {p.w2 + row0 * geo.wrow, p.s2 + row0 * geo.srow, geo.R, 0};
+            if (!fs::produce(ring, geo, &run, 1, cur_ring, filled)) break;
+        }
+        fs::produce_drain(ring, geo, filled);
+    } else {
+        constexpr int STRIDE = 32 / RPW;
+        fs::Lane L = fs::lane_setup(geo);
+        int rows[RPW];
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) rows[i] = L.rs * RPW + i;
+        int cur = -1;
+        float wt = 0.f;
+        float *dst_row = nullptr;
+        for (int it = it0; it < it1; ++it) {
+            const int r = it / nrb, hb = it % nrb;
+            if (r != cur) {
+                int s, slot;
+                ep_locate(p, off, r, s, slot);
+                fs::lane_load_x(L, p.mid + size_t(slot) * p.I);
+                const int4 m = *reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16);
+                wt = __int_as_float(m.w) * p.g2[m.x];
+                dst_row = reinterpret_cast<float *>(ep_buf(p, s) + p.off_ret) + (size_t(m.y) * p.k + m.z) * p.H;
+                cur = r;
+            }
+            float v;
+            const int st = fs::consume<RPW>(ring, geo, L, rows, v, cur_ring);
+            if (!st) break;
+            if (st == 1 && lane % STRIDE == 0) dst_row[hb * geo.R + L.rs * RPW + lane / STRIDE] = v * wt;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(&p.state[8], 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x < p.W) {
+        if (threadIdx.x == 0) p.state[8] = 0;
         __threadfence_system();
         st_release_sys(reinterpret_cast<volatile uint32_t *>(ep_buf(p, threadIdx.x) + p.off_rflag +
                                                              size_t(p.rank) * 128),
                        epoch);
-    }
-    for (int it = blockIdx.x; it < items; it += gridDim.x) {
-        const int r = it / hb_count, hb = it % hb_count;
-        int s, slot;
-        ep_locate(p, off, r, s, slot);
-        const int4 m = *reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16);
-        const int e = m.x, t = m.y, j = m.z;
-        const float wt = __int_as_float(m.w) * p.g2[e];
-        __half2 xr[CH][16];
-        load_x_f32<LPR, CH>(p.mid + size_t(slot) * p.I, q, xr);
-        const uint8_t *W = p.w2 + size_t(e) * p.H * wrow;
-        const uint8_t *S = p.s2 + size_t(e) * p.H * srow;
-        const int h_raw = hb * ROWS + warp * RPW + sub;
-        const int h = min(h_raw, p.H - 1);
-        const float v = wt * row_dot<LPR, CH>(W + h * wrow, S + h * srow, p.fmt, q, xr);
-        if (q == 0 && h_raw < p.H) {
-            float *dst = reinterpret_cast<float *>(ep_buf(p, s) + p.off_ret) + (size_t(t) * p.k + j) * p.H + h;
-            *dst = v;   // straight into the source rank's return buffer
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            const unsigned need = unsigned(off[s + 1] - off[s]) * unsigned(hb_count);
-            const unsigned prev = atomicAdd(&p.state[8 + s], 1u);
-            if (prev == need - 1) {
-                p.state[8 + s] = 0;
-                st_release_sys(reinterpret_cast<volatile uint32_t *>(ep_buf(p, s) + p.off_rflag + size_t(p.rank) * 128),
-                               epoch);
-            }
-        }
     }
 }
 
@@ -763,16 +838,9 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
 
 }  // namespace xt
 
-#define XT_EP_CASE(KERNEL, L, C, ROWS_K)                                              \
-    if (lpr == L && ch == C) {                                                        \
-        KERNEL<L, C><<<grid, GU_WARPS * 32, 0, stream>>>(p);                          \
-        return cudaGetLastError() == cudaSuccess ? 0 : -1;                            \
-    }
-
 extern "C" int xt_ep_moe(const EpParams *pp, int phase, cudaStream_t stream) {
     EpParams p = *pp;
-    if (p.W > EP_MAX_W || p.T * p.k > EP_MAX_ROUTES || p.H % 256) return -2;
-    int sms = 148;
+    if (p.W > EP_MAX_W || p.T * p.k > EP_MAX_ROUTES || p.H % 256 || p.I % 16) return -2;
     if (phase == 0) {
         const int n = p.T * p.k;
         const int grid = n < 8 ? 1 : (n + 63) / 64 > 64 ? 64 : (n + 63) / 64;
@@ -783,19 +851,33 @@ extern "C" int xt_ep_moe(const EpParams *pp, int phase, cudaStream_t stream) {
         ep_combine_kernel<<<p.T, 256, 0, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
-    const int grid = sms * 4;
-    int ch = 0;
-    const int lpr = pick_lpr(phase == 1 ? p.H / 2 : p.I / 2, &ch);
-    if (phase == 1) {
-        XT_EP_CASE(ep_gate_up_kernel, 32, 1, 0) XT_EP_CASE(ep_gate_up_kernel, 32, 2, 0)
-        XT_EP_CASE(ep_gate_up_kernel, 32, 4, 0) XT_EP_CASE(ep_gate_up_kernel, 32, 7, 0)
-        XT_EP_CASE(ep_gate_up_kernel, 16, 1, 0) XT_EP_CASE(ep_gate_up_kernel, 8, 1, 0)
-        XT_EP_CASE(ep_gate_up_kernel, 32, 5, 0) XT_EP_CASE(ep_gate_up_kernel, 16, 5, 0)
-    } else if (phase == 2) {
-        XT_EP_CASE(ep_down_send_kernel, 32, 1, 0) XT_EP_CASE(ep_down_send_kernel, 32, 2, 0)
-        XT_EP_CASE(ep_down_send_kernel, 8, 3, 0) XT_EP_CASE(ep_down_send_kernel, 8, 1, 0)
-        XT_EP_CASE(ep_down_send_kernel, 4, 1, 0) XT_EP_CASE(ep_down_send_kernel, 4, 5, 0)
-        XT_EP_CASE(ep_down_send_kernel, 16, 1, 0) XT_EP_CASE(ep_down_send_kernel, 32, 4, 0)
+    static bool attr = false;
+    if (!attr) {
+        const void *fns[4] = {reinterpret_cast<const void *>(ep_gate_up_stream<4>),
+                              reinterpret_cast<const void *>(ep_gate_up_stream<8>),
+                              reinterpret_cast<const void *>(ep_down_stream<4>),
+                              reinterpret_cast<const void *>(ep_down_stream<8>)};
+        for (const void *f : fns)
+            if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, fs::SMEM_BYTES) != cudaSuccess)
+                return -5;
+        attr = true;
     }
-    return -4;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    fs::Geo geo;
+    if (phase == 1) {
+        if (!fs::make_geo(p.H, p.fmt, 2, geo) || p.I % (geo.R / 2)) return -3;
+        if (geo.rpw == 8)
+            ep_gate_up_stream<8><<<sms, fs::THREADS, fs::SMEM_BYTES, stream>>>(p, geo);
+        else
+            ep_gate_up_stream<4><<<sms, fs::THREADS, fs::SMEM_BYTES, stream>>>(p, geo);
+    } else {
+        if (!fs::make_geo(p.I, p.fmt, 1, geo) || p.H % geo.R) return -3;
+        if (geo.rpw == 8)
+            ep_down_stream<8><<<sms, fs::THREADS, fs::SMEM_BYTES, stream>>>(p, geo);
+        else
+            ep_down_stream<4><<<sms, fs::THREADS, fs::SMEM_BYTES, stream>>>(p, geo);
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

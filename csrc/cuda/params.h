@@ -1,6 +1,7 @@
 // Launch parameters of the sm_100a kernels and their C launchers: shared by the .cu files and the torch bindings.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -107,7 +108,7 @@ struct EpParams {
     const int32_t *ids;          // [T, k] global expert ids
     const float *w;              // [T, k]
     uint32_t *state;             // local: [0] epoch, [1] dispatch arrivals, [8 + s] down-send progress per source
-    float *mid;                  // local scratch [W*R, I]
+    __half *mid;                 // local scratch [W*R, I] f16 (SwiGLU output)
     const uint8_t *w13, *s13, *w2, *s2;   // this rank's El experts
     const float *g13, *g2;
     const __nv_bfloat16 *add;    // [T, H] extra term of the combine (shared experts), may be null

@@ -93,3 +93,29 @@ def test_ep_moe_two_gpus(fmt_name, H, I, E, k, T):
         assert rel < 1e-2, (rank, rel)
         assert rel_nccl < 1e-2, (rank, rel_nccl)
         assert same, rank
+
+
+@pytest.mark.parametrize('fmt_name,H,I,E,k,T', [('mxfp4', 7168, 2048, 16, 8, 4), ('nvfp4', 2048, 768, 32, 8, 3),
+                                                ('nvfp4', 4096, 1536, 8, 4, 2)])
+def test_ep_moe_one_gpu_shapes(fmt_name, H, I, E, k, T):
+    """The fused EP op at world size 1 (no process group; the peer table holds this GPU's own buffer) on
+    DeepSeek-V3 / Qwen3 expert shapes: exercises every K split of the streaming expert kernels."""
+    from xtier_b200 import formats, ops
+    from xtier_b200.parallel import dist as xdist
+    from xtier_b200.parallel.ep import EPComm, EPMoE
+    for v in ('RANK', 'WORLD_SIZE', 'LOCAL_RANK'):
+        os.environ.pop(v, None)
+    env = xdist.init(timeout_s=60)
+    ops.load()
+    ex = formats.random_experts(E, H, I, fmt_name, seed=3, std=0.05)
+    router = (torch.randn(E, H, generator=torch.Generator().manual_seed(4)) * 0.02).bfloat16()
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(5)).bfloat16()
+    comm = EPComm(H, I, E, k, T, env.device, timeout_s=5.0)
+    layer = EPMoE(0, comm, router, ex, k)
+    out = layer.forward(x.to(env.device))
+    torch.cuda.synchronize()
+    comm.check()
+    ref = formats.reference_moe(x, layer.router.ids[:T].cpu(), layer.router.wt[:T].cpu(), ex)
+    rel = float((out.cpu().float() - ref).norm() / ref.norm())
+    comm.close()
+    assert rel < 1e-2, rel

@@ -53,7 +53,7 @@ class EPComm:
         self.offsets = offs
         self.buf = SymmetricBuffer(off, self.device)
         self.state = torch.zeros(64, dtype=torch.int32, device=self.device)
-        self.mid = torch.empty(W * R * inter, dtype=torch.float32, device=self.device)
+        self.mid = torch.empty(W * R * inter, dtype=torch.float16, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.timeout_s = timeout_s
 
