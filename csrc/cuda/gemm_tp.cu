@@ -23,6 +23,7 @@ namespace xt {
 
 
 constexpr int TP_BM = 128, TP_BK = 64, TP_STAGES = 4, TP_THREADS = 192;
+constexpr int TP_GROUP_M = 16;   // raster groups of 128-row tiles (L2 reuse of A and B)
 
 template <int BN>
 struct TpSmem {
@@ -65,8 +66,9 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
     auto tile_at = [&](int i, int &owner, int &tm, int &tn, int &j) {
         owner = (p.rank + (MODE == 0 ? 1 : 0) + i / tpo) % p.W;
         j = i % tpo;
-        tm = owner * mb_per_owner + j % mb_per_owner;
-        tn = j / mb_per_owner;
+        int tml;
+        tc::tile_coords(j, mb_per_owner, tiles_n, TP_GROUP_M, tml, tn);
+        tm = owner * mb_per_owner + tml;
     };
 
     if (threadIdx.x == 0) {
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
                 tile_at(i, owner, tm, tn, j);
                 if (MODE == 1) {   // the A block must have landed in this rank's gather buffer
                     const volatile uint32_t *f =
-                        reinterpret_cast<const volatile uint32_t *>(me + p.off_flags[par]) + tm;
+                        reinterpret_cast<const volatile uint32_t *>(me + (par ? p.off_flags[1] : p.off_flags[0])) + tm;
                     if (!tp_wait_flag(f, epoch, p.timeout_ns)) {
                         fail();
                         break;
@@ -202,7 +204,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
             __nv_bfloat16 *dst_row;
             if (MODE == 0)
                 dst_row = reinterpret_cast<__nv_bfloat16 *>(reinterpret_cast<uint8_t *>(p.peer[owner]) +
-                                                           p.off_data[par]) +
+                                                           (par ? p.off_data[1] : p.off_data[0])) +
                           (size_t(p.rank) * Mo + (row - owner * Mo)) * p.N;
             else
                 dst_row = p.out + size_t(row) * p.N;
@@ -225,7 +227,9 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
                         *reinterpret_cast<uint4 *>(dst_row + col + v * 8) = o;
                     }
                 } else {
-                    for (int q = 0; q < 32 && col + q < p.N; ++q) dst_row[col + q] = __float2bfloat16(__uint_as_float(r[q]));
+#pragma unroll
+                    for (int q = 0; q < 32; ++q)   // static indices keep r in registers
+                        if (col + q < p.N) dst_row[col + q] = __float2bfloat16(__uint_as_float(r[q]));
                 }
             }
             tc::tc_fence_before();
@@ -236,7 +240,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
                 if (warp == 2 && lane == 0) {
                     __threadfence_system();
                     st_release_sys(reinterpret_cast<volatile uint32_t *>(reinterpret_cast<uint8_t *>(p.peer[owner]) +
-                                                                         p.off_flags[par]) +
+                                                                         (par ? p.off_flags[1] : p.off_flags[0])) +
                                        size_t(p.rank) * tpo + j,
                                    epoch);
                 }
@@ -258,7 +262,8 @@ __global__ void __launch_bounds__(256) rs_reduce_kernel(TpParams p) {
     __shared__ bool last;
     const int Mo = p.M / p.W, mb_per_owner = Mo / TP_BM;
     const int j = blockIdx.x;
-    const int tml = j % mb_per_owner, tn = j / mb_per_owner;
+    int tml, tn;
+    tc::tile_coords(j, mb_per_owner, (p.N + BN - 1) / BN, TP_GROUP_M, tml, tn);
     const int tiles_n = (p.N + BN - 1) / BN;
     const int tpo = mb_per_owner * tiles_n;
     const uint32_t epoch = p.state[0] + 1;
@@ -267,13 +272,13 @@ __global__ void __launch_bounds__(256) rs_reduce_kernel(TpParams p) {
     if (threadIdx.x == 0) {
         int good = 1;
         for (int s = 0; s < p.W && good; ++s)
-            good = tp_wait_flag(reinterpret_cast<const volatile uint32_t *>(me + p.off_flags[par]) + size_t(s) * tpo + j,
+            good = tp_wait_flag(reinterpret_cast<const volatile uint32_t *>(me + (par ? p.off_flags[1] : p.off_flags[0])) + size_t(s) * tpo + j,
                                 epoch, p.timeout_ns);
         if (!good) atomicExch(p.error, 1);
         ok = good;
     }
     __syncthreads();
-    const __nv_bfloat16 *recv = reinterpret_cast<const __nv_bfloat16 *>(me + p.off_data[par]);
+    const __nv_bfloat16 *recv = reinterpret_cast<const __nv_bfloat16 *>(me + (par ? p.off_data[1] : p.off_data[0]));
     const int cols = min(BN, p.N - tn * BN);
     for (int e = threadIdx.x * 8; e < TP_BM * BN; e += blockDim.x * 8) {
         const int r = e / BN, c = e % BN;
@@ -330,13 +335,13 @@ __global__ void __launch_bounds__(256) ag_push_kernel(TpParams p) {
     uint8_t *dst_base = reinterpret_cast<uint8_t *>(p.peer[d]);
     const size_t row0 = size_t(p.rank) * Mo + size_t(blk) * TP_BM;
     const uint4 *src = reinterpret_cast<const uint4 *>(p.a_shard + size_t(blk) * TP_BM * p.K);
-    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(dst_base + p.off_data[par]) + row0 * p.K);
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(dst_base + (par ? p.off_data[1] : p.off_data[0])) + row0 * p.K);
     const size_t n = size_t(TP_BM) * p.K / 8;
     for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence_system();
-        st_release_sys(reinterpret_cast<volatile uint32_t *>(dst_base + p.off_flags[par]) + row0 / TP_BM, epoch);
+        st_release_sys(reinterpret_cast<volatile uint32_t *>(dst_base + (par ? p.off_flags[1] : p.off_flags[0])) + row0 / TP_BM, epoch);
     }
 }
 

@@ -101,6 +101,80 @@ XT_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 XT_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
+// Grouped rasterization of a tiles_m x tiles_n grid: runs of `gm` tile rows are walked across all tile columns before
+// the next run starts, so the A rows and B columns that the CTAs in flight touch stay resident in L2 (walking whole
+// column panels would stream all of A from DRAM once per panel).
+__host__ __device__ inline void tile_coords(int t, int tiles_m, int tiles_n, int gm, int &tm, int &tn) {
+    const int span = gm * tiles_n;
+    const int first = (t / span) * gm;
+    const int rows = tiles_m - first < gm ? tiles_m - first : gm;
+    const int r = t % span;
+    tm = first + r % rows;
+    tn = r / rows;
+}
+
+// ---- CTA pairs (cluster of 2, tcgen05 cta_group::2): the even CTA of the pair is the leader that issues the MMAs of a
+// 256-row tile; each CTA holds half of A (128 rows) and half of B (N/2 rows) of every k-block in its own shared memory,
+// and its own 128 accumulator rows in its TMEM.
+XT_DEV uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+
+XT_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// shared::cluster address of the variable at `p` (shared::cta) in CTA `rank` of the cluster
+XT_DEV uint32_t mapa(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+XT_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D TMA tile load into this CTA's shared memory whose completion (bytes) is counted on the LEADER's barrier at the
+// same offset (the peer bit of the barrier address cleared).
+XT_DEV void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];\n" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar) & 0xFEFFFFFFu), "r"(x), "r"(y)
+        : "memory");
+}
+
+XT_DEV void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+XT_DEV void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::); }
+
+XT_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[smem halves] . B[smem halves]^T, issued by the leader
+XT_DEV void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives once on the barrier at shared::cluster address `cluster_bar` (either CTA of the pair) when every
+// cta_group::2 tcgen05 operation issued so far by this thread has completed.
+XT_DEV void mma_commit_pair(uint32_t cluster_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(cluster_bar)
+                 : "memory");
+}
+
 // Shared-memory matrix descriptor of a K-major operand tile written by TMA with 128-byte swizzle: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (stride byte offset), layout type SWIZZLE_128B (2), descriptor version 1 (sm_100).
 // The tile base must be 1024-byte aligned (base offset 0). Advancing K inside the 128-byte swizzle atom is done by
