@@ -1,16 +1,18 @@
 // GQA decode attention over a contiguous BF16 KV cache [B, Hkv, L, D=128], split over the keys (flash-decoding).
 //
-// Grid (splits, Hkv, B), 8 warps. A CTA takes the G = Hq/Hkv query heads of one KV head and a fixed slice of the cache
-// (L / splits keys, cut at the sequence length), walked in tiles of 256 keys with an online softmax:
-//   scores  each warp takes 32 keys, one per lane: the lane loads its key's 256-byte row (16 independent 16-byte
-//           loads in flight) and forms the G head dots against the pre-scaled queries in shared memory (broadcast
-//           reads), so no cross-lane reduction is needed.
+// Grid (splits, Hkv, B), 8 warps. A CTA takes the G = Hq/Hkv query heads of one KV head and 1/splits of the sequence's
+// keys (the split is cut from the sequence length read on the device, so every split has work and the grid does not
+// depend on the length: graph capture), walked in tiles of 64 keys with an online softmax:
+//   scores  a warp takes 8 keys, 4 lanes per key: each lane loads 64 bytes of its key's row (4 independent 16-byte
+//           loads) and forms the partial dots of its 32 dims with the G pre-scaled queries (shared-memory broadcast
+//           reads); two shuffles finish each dot.
 //   softmax one warp per head: tile max, running max and sum, exp2 in place.
-//   values  lane l accumulates dims 4l..4l+3 of all G heads; the warp's 32 value rows are loaded (8 bytes per lane)
-//           before the softmax, so the whole tile costs two memory round trips.
-// Each split writes its unnormalized output, max and sum to a workspace; the last CTA of a (batch, KV head) to finish
-// merges the splits (an arrival counter that it resets), so one launch does the whole step and the grid shape does not
-// depend on the sequence length (graph capture). Sequence lengths are read from device memory.
+//   values  the warp's 8 value rows are loaded before the softmax (8 bytes per lane each); lane l accumulates dims
+//           4l..4l+3 of every head over its warp's keys.
+// With 64-key tiles a 2K-token sequence spreads over ~36 splits x Hkv CTAs, so the step costs about one memory round
+// trip plus a short dependent chain per CTA. Each split writes its unnormalized output, max and sum to a workspace;
+// the last CTA of a (batch, KV head) to finish merges the splits (an arrival counter that it resets), so one launch
+// does the whole step.
 // Reference parity: the reference leaves dense decode attention to SGLang's backends; this kernel is the dense
 // attention of the Qwen3-style config (GQA 32/4, head dim 128).
 #include "common.cuh"
@@ -19,15 +21,18 @@
 namespace xt {
 
 constexpr int AD_WARPS = 8;
-constexpr int AD_TILE = 32 * AD_WARPS;   // keys per tile: one per lane
+constexpr int AD_KPW = 8;                    // keys per warp and tile
+constexpr int AD_TILE = AD_KPW * AD_WARPS;   // keys per tile
 constexpr int AD_D = 128;
 constexpr int AD_MAX_SPLITS = 64;
 
 template <int G>
 struct AdSmem {   // dynamic shared memory layout
-    static constexpr size_t S = size_t(AD_TILE) * G * 4;          // scores of a tile [key][head]
+    static constexpr size_t S = size_t(AD_TILE) * G * 4;            // scores of a tile [key][head]
     static constexpr size_t RED = size_t(AD_WARPS) * G * AD_D * 4;  // cross-warp reduction [warp][head][dim]
-    static constexpr size_t BUF = S > RED ? S : RED;
+    static constexpr size_t MERGE = size_t(AD_MAX_SPLITS) * G * 2 * 4;
+    static constexpr size_t BUF0 = S > RED ? S : RED;
+    static constexpr size_t BUF = BUF0 > MERGE ? BUF0 : MERGE;
     static constexpr size_t Q = size_t(G) * AD_D * 4;
     static constexpr size_t BYTES = BUF + Q + 3 * G * 4 + AD_MAX_SPLITS * G * 4 + 64;
 };
@@ -46,20 +51,18 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     float(&wsplit)[AD_MAX_SPLITS][G] = *reinterpret_cast<float(*)[AD_MAX_SPLITS][G]>(alpha + G);
     __shared__ bool last;
 
-    // the split's key range is a fixed slice of the cache, so the first tile's K loads need no sequence length
-    const int chunk = (p.L + p.splits - 1) / p.splits;
-    const int k_begin = split * chunk;
     const size_t head_off = (size_t(b) * p.Hkv + kvh) * p.L;
     const __nv_bfloat16 *K = p.kc + head_off * AD_D;
     const __nv_bfloat16 *V = p.vc + head_off * AD_D;
-
     const __nv_bfloat16 *qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * G) * AD_D;
     for (int i = threadIdx.x; i < G * AD_D; i += blockDim.x) qs[i / AD_D][i % AD_D] = __bfloat162float(qb[i]) * p.scale_log2;
     if (threadIdx.x < G) {
         m_run[threadIdx.x] = -INFINITY;
         l_run[threadIdx.x] = 0.f;
     }
-    const int N = p.seqlens[b];
+    const int N = min(p.seqlens[b], p.L);
+    const int chunk = (((N + p.splits - 1) / p.splits) + 7) & ~7;
+    const int k_begin = split * chunk;
     const int k_end = min(N, k_begin + chunk);
     __syncthreads();
     float acc[G][4];
@@ -67,47 +70,55 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     for (int h = 0; h < G; ++h)
 #pragma unroll
         for (int d = 0; d < 4; ++d) acc[h][d] = 0.f;
+    const int kq = lane >> 2, qd = lane & 3;   // key of the warp's 8, quarter of the 128 dims
 
     for (int t0 = k_begin; t0 < k_end; t0 += AD_TILE) {
-        // ---- scores: one key per lane, its whole 256-byte row in flight at once
-        {
-            const int key = t0 + warp * 32 + lane;
-            const bool valid = key < k_end;
-            const uint4 *kr = reinterpret_cast<const uint4 *>(K + size_t(valid ? key : t0) * AD_D);
-            uint4 kv[AD_D / 8];
+        const int kw = t0 + warp * AD_KPW;   // first key of this warp
+        // ---- loads: 64 bytes of one key row per lane, and the warp's 8 value rows (8 bytes per lane each)
+        const int key = kw + kq;
+        const bool valid = key < k_end;
+        const uint4 *kr = reinterpret_cast<const uint4 *>(K + size_t(valid ? key : k_begin) * AD_D + qd * 32);
+        uint4 kv[4];
 #pragma unroll
-            for (int c = 0; c < AD_D / 8; ++c) kv[c] = kr[c];
+        for (int c = 0; c < 4; ++c) kv[c] = kr[c];
+        uint2 vv[AD_KPW];
+#pragma unroll
+        for (int i = 0; i < AD_KPW; ++i) {
+            const int kvk = min(kw + i, k_end - 1);
+            vv[i] = *reinterpret_cast<const uint2 *>(V + size_t(max(kvk, k_begin)) * AD_D + lane * 4);
+        }
+        // ---- scores
+        {
             float s[G];
 #pragma unroll
             for (int h = 0; h < G; ++h) s[h] = 0.f;
 #pragma unroll
-            for (int c = 0; c < AD_D / 8; ++c) {
+            for (int c = 0; c < 4; ++c) {
                 const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&kv[c]);
                 float kf[8];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    float2 f = __bfloat1622float2(k2[i]);
+                    const float2 f = __bfloat1622float2(k2[i]);
                     kf[2 * i] = f.x;
                     kf[2 * i + 1] = f.y;
                 }
 #pragma unroll
                 for (int h = 0; h < G; ++h) {
-                    const float4 q0 = *reinterpret_cast<const float4 *>(&qs[h][c * 8]);
-                    const float4 q1 = *reinterpret_cast<const float4 *>(&qs[h][c * 8 + 4]);
+                    const float4 q0 = *reinterpret_cast<const float4 *>(&qs[h][qd * 32 + c * 8]);
+                    const float4 q1 = *reinterpret_cast<const float4 *>(&qs[h][qd * 32 + c * 8 + 4]);
                     s[h] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
                             q1.z * kf[6] + q1.w * kf[7];
                 }
             }
 #pragma unroll
-            for (int h = 0; h < G; ++h) S[warp * 32 + lane][h] = valid ? s[h] : -INFINITY;
-        }
-        // ---- this warp's 32 value rows (8 bytes per lane each) in flight while the softmax runs
-        const int nk = max(0, min(32, k_end - (t0 + warp * 32)));
-        uint2 vv[32];
+            for (int h = 0; h < G; ++h) {
+                s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
+                s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
+            }
+            if (qd == 0) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int key = t0 + warp * 32 + min(i, max(nk - 1, 0));
-            vv[i] = *reinterpret_cast<const uint2 *>(V + size_t(key) * AD_D + lane * 4);
+                for (int h = 0; h < G; ++h) S[warp * AD_KPW + kq][h] = valid ? s[h] : -INFINITY;
+            }
         }
         __syncthreads();
         // ---- online softmax per head
@@ -119,7 +130,7 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
             const float m_new = fmaxf(m_old, mx);
             float sum = 0.f;
             for (int i = lane; i < AD_TILE; i += 32) {
-                float e = (m_new == -INFINITY) ? 0.f : exp2f(S[i][h] - m_new);
+                const float e = (m_new == -INFINITY) ? 0.f : exp2f(S[i][h] - m_new);
                 S[i][h] = e;
                 sum += e;
             }
@@ -132,7 +143,7 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
             }
         }
         __syncthreads();
-        // ---- values: lane owns dims 4l..4l+3 of every head
+        // ---- values: lane owns dims 4l..4l+3 of every head, over its warp's 8 keys
 #pragma unroll
         for (int h = 0; h < G; ++h) {
             const float a = alpha[h];
@@ -140,13 +151,12 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
             for (int d = 0; d < 4; ++d) acc[h][d] *= a;
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            if (i >= nk) break;
+        for (int i = 0; i < AD_KPW; ++i) {
             const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&vv[i]);
-            float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
+            const float2 f0 = __bfloat1622float2(u2[0]), f1 = __bfloat1622float2(u2[1]);
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-                const float pr = S[warp * 32 + i][h];
+                const float pr = S[warp * AD_KPW + i][h];   // 0 for keys past the end (score -inf)
                 acc[h][0] += pr * f0.x;
                 acc[h][1] += pr * f0.y;
                 acc[h][2] += pr * f1.x;

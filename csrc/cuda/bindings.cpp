@@ -326,6 +326,15 @@ void ag_gemm(const Tensor &a_shard, const Tensor &b, const Tensor &peer, int64_t
     check_rc(xt_ag_gemm(b.data_ptr(), reinterpret_cast<const void *>(local_base), &p, stream()), "ag_gemm");
 }
 
+void l2_prefetch(const Tensor &ptrs, const Tensor &bytes, int64_t ctas) {
+    check(ptrs.scalar_type() == at::kLong && bytes.scalar_type() == at::kLong && ptrs.numel() == bytes.numel(),
+          "l2_prefetch: int64 pointer and size tensors of one length");
+    c10::cuda::CUDAGuard g(ptrs.device());
+    check_rc(xt_l2_prefetch(ptr<const uint64_t>(ptrs), ptr<const uint64_t>(bytes), int(ptrs.numel()), int(ctas),
+                            stream()),
+             "l2_prefetch");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(xtier, m) {
@@ -342,6 +351,7 @@ TORCH_LIBRARY(xtier, m) {
     m.def("ep_moe(Tensor x, Tensor ids, Tensor w, Tensor peer, Tensor(a!) state, Tensor(b!) mid, Tensor w13, "
           "Tensor s13, Tensor g13, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(c!) out, Tensor(d!) err, "
           "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases) -> ()");
+    m.def("l2_prefetch(Tensor ptrs, Tensor bytes, int ctas) -> ()");
     m.def("gemm_rs(Tensor a, Tensor b, Tensor peer, Tensor(a!) state, Tensor? residual, Tensor(b!) out, "
           "Tensor(c!) err, int W, int rank, int[] offsets, float timeout_s) -> ()");
     m.def("ag_gemm(Tensor a_shard, Tensor b, Tensor peer, int local_base, Tensor(a!) state, Tensor(b!) out, "
@@ -364,4 +374,5 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("ep_moe", &ep_moe);
     m.impl("gemm_rs", &gemm_rs);
     m.impl("ag_gemm", &ag_gemm);
+    m.impl("l2_prefetch", &l2_prefetch);
 }

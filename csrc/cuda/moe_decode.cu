@@ -42,6 +42,12 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
     const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kk = p.k + p.n_shared;
     const __nv_bfloat16 *xt = p.x + size_t(t) * p.H;
+    if (use_mb) {   // this CTA's slice of the token's activations to the mailbox slot first: the PCIe writes overlap
+        const uint4 *src = reinterpret_cast<const uint4 *>(xt);   // the logits and are long done at publication
+        uint4 *dst = reinterpret_cast<uint4 *>(mb.x + size_t(t) * p.H);
+        const int n = p.H / 8, per = (n + gridDim.x - 1) / gridDim.x;
+        for (int i = blockIdx.x * per + tid; i < min(n, (blockIdx.x + 1) * per); i += ROUTE_THREADS) dst[i] = src[i];
+    }
     {
         const int e = blockIdx.x * ROUTE_WARPS + warp;
         if (e < p.E) {
@@ -72,6 +78,7 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
     __threadfence();
     __syncthreads();
     if (tid == 0) {
+        if (use_mb) __threadfence_system();   // the slice of x above, before the count
         const unsigned prev = atomicAdd(&p.ws_count[t], 1u);
         last_cta = prev == gridDim.x - 1;
         if (last_cta) p.ws_count[t] = 0;   // ready for the next call
@@ -200,24 +207,19 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
     }
     if (!use_mb) return;
     __syncthreads();
-    // this token's activations to the slot (host memory over PCIe), then count the CTA as done
-    if (any_cpu) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(xt);
-        uint4 *dst = reinterpret_cast<uint4 *>(mb.x + size_t(t) * p.H);
-        for (int i = tid; i < p.H / 8; i += ROUTE_THREADS) dst[i] = src[i];
-        if (tid == 0) atomicOr(&mb.dev->any, 1u);
-    }
-    __syncthreads();
+    // count the token as done; the last token of the call publishes it with a single system fence (x went to the
+    // slot in phase A; the route arrays were written above by this CTA)
     if (tid == 0) {
-        __threadfence_system();
-        unsigned prev = atomicAdd(&mb.dev->done, 1u);
-        if (prev == unsigned(p.m) - 1) {   // last CTA of the call publishes it
-            __threadfence_system();
-            unsigned any = atomicExch(&mb.dev->any, 0u);
+        if (any_cpu) atomicOr(&mb.dev->any, 1u);
+        if (p.m > 1) __threadfence_system();   // other tokens' CTAs: their route arrays before the count
+        const unsigned prev = atomicAdd(&mb.dev->done, 1u);
+        if (prev == unsigned(p.m) - 1) {
+            __threadfence();
+            const unsigned any = atomicExch(&mb.dev->any, 0u);
             mb.dev->done = 0;
             mb.dev->pending = any;
             if (any) {
-                unsigned seq = mb.dev->seq + 1;
+                const unsigned seq = mb.dev->seq + 1;
                 mb.dev->seq = seq;
                 mb.hdr->layer = p.layer;
                 mb.hdr->m = p.m;

@@ -139,5 +139,6 @@ struct TpParams {
 extern "C" {
 int xt_gemm_rs(const void *a, const void *b, const xt::TpParams *p, cudaStream_t stream);
 int xt_ag_gemm(const void *b, const void *local_base, const xt::TpParams *p, cudaStream_t stream);
+int xt_l2_prefetch(const uint64_t *ptrs, const uint64_t *bytes, int n, int ctas, cudaStream_t stream);
 }
 

@@ -29,6 +29,7 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_LAYERS', 'str', 'all', 'model layers whose routed experts are tiered: all or a list 0-11,20'),
     _S('XTIER_THREADS', 'int', 0, 'CPU expert engine workers (0: every CPU but one for the mailbox dispatcher)'),
     _S('XTIER_ISA', 'str', 'auto', 'CPU engine kernels: auto, avx512 (AVX-512 BF16), avx2, scalar'),
+    _S('XTIER_L2_PREFETCH', 'int', 1, 'decode graphs prefetch the next layer\'s dense weights and KV cache into L2'),
     _S('XTIER_GEMM_PAIR', 'int', 0, '1: BF16 GEMMs with M >= 1024 run the CTA-pair (tcgen05 cta_group::2) kernel'),
     _S('XTIER_SPIN_US', 'int', 200, 'engine workers spin this long before sleeping on a futex'),
     _S('XTIER_MAIN_CPUS', 'str', '', 'CPUs of the other threads of the process (auto: all but the workers)'),

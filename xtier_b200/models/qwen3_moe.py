@@ -14,7 +14,7 @@ import math
 
 import torch
 
-from .. import formats, ops
+from .. import config, formats, ops
 from ..cache.pool import TieredMoE
 
 
@@ -146,7 +146,20 @@ class Qwen3MoeModel:
             counters=torch.zeros(batch * Hkv, dtype=torch.int32, device=dev),
             lengths=torch.zeros(batch, dtype=torch.int32, device=dev),
         )
+        if config.get('XTIER_L2_PREFETCH'):
+            st['prefetch'] = [self._prefetch_list(li, st) for li in range(len(self.layers))]
+            st['side'] = torch.cuda.Stream(device=dev) if dev.type == 'cuda' else None
         return st
+
+    def _prefetch_list(self, li: int, st: dict):
+        """Device arrays (addresses, bytes) of what layer li's dense part streams: QKV and output projections,
+        router, KV cache. A side branch of the decode graph pulls them into L2 while layer li-1 waits on its CPU
+        experts."""
+        L = self.layers[li]
+        ts = [L['qkv'], L['o'], L['moe'].router_w, st['k'][li], st['v'][li]]
+        ptrs = torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=self.device)
+        sizes = torch.tensor([t.numel() * t.element_size() for t in ts], dtype=torch.int64, device=self.device)
+        return ptrs, sizes
 
     # ------------------------------------------------------------------ decode step (graph capturable)
     def decode_buffers(self, batch: int) -> dict:
@@ -174,6 +187,8 @@ class Qwen3MoeModel:
         """One token per sequence: reads buf['tokens'], buf['pos'] (device), writes buf['next'] (greedy)."""
         cfg = self.cfg
         B = buf['tokens'].shape[0]
+        side = st.get('side') if B <= 16 else None
+        main = torch.cuda.current_stream(self.device) if side is not None else None
         torch.add(buf['pos'], 1, out=buf['seqlens'])
         torch.index_select(self.embed, 0, buf['tokens'], out=buf['residual'])
         scale = 1.0 / math.sqrt(cfg.head_dim)
@@ -189,10 +204,16 @@ class Qwen3MoeModel:
                             st['counters'], st['splits'], scale)
             ops.linear(buf['attn'].view(B, -1), L['o'], out=buf['o'])
             ops.add_rmsnorm(buf['o'], buf['residual'], L['post_norm'], buf['h'], cfg.eps)
+            if side is not None and li + 1 < len(self.layers):   # next layer's weights into L2 meanwhile
+                side.wait_stream(main)
+                with torch.cuda.stream(side):
+                    ops.l2_prefetch(*st['prefetch'][li + 1])
             L['moe'].forward(buf['h'], out=buf['moe_out'])
         ops.add_rmsnorm(buf['moe_out'], buf['residual'], self.final_norm, buf['h'], cfg.eps)
-        torch.matmul(buf['h'], self.lm_head.t(), out=buf['logits'])
+        ops.gemv(buf['h'], self.lm_head, buf['logits'])
         torch.argmax(buf['logits'], dim=-1, out=buf['next'])
+        if side is not None:
+            main.wait_stream(side)
         return buf['next']
 
     # ------------------------------------------------------------------ prefill (one sequence)

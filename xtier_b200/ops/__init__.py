@@ -111,6 +111,11 @@ def linear(x, w, out=None):
     return torch.matmul(x, w.t(), out=out) if out is not None else torch.matmul(x, w.t())
 
 
+def l2_prefetch(ptrs, sizes, ctas: int = 16):
+    """Bulk-prefetch the device ranges (int64 address and byte tensors on the device) into L2."""
+    _ops().l2_prefetch(ptrs, sizes, ctas)
+
+
 def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0):
     _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta)
 
@@ -120,7 +125,8 @@ def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, ma
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
-    """Key splits of the decode attention: about one 256-key tile per split, at most enough CTAs for two per SM and
-    at most 64 splits (the merge reads every split's partial)."""
-    want = max(1, (2 * sms + batch * kv_heads - 1) // (batch * kv_heads))
-    return max(1, min(64, want, (max_len + 255) // 256))
+    """Key splits of the decode attention: enough CTAs (splits x batch x kv_heads) to cover every SM about once, at
+    most one per 64 keys of the cache and at most 64 (the merge reads every split's partial). The kernel cuts the
+    splits from the actual sequence length, so all of them have work."""
+    want = max(1, (sms + batch * kv_heads - 1) // (batch * kv_heads))
+    return max(1, min(64, want, (max_len + 63) // 64))
