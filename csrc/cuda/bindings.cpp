@@ -335,6 +335,69 @@ void l2_prefetch(const Tensor &ptrs, const Tensor &bytes, int64_t ctas) {
              "l2_prefetch");
 }
 
+void mla_kv_write(const Tensor &lat, const Tensor &slot, const Tensor &codes, const Tensor &scales, const Tensor &rope) {
+    cuda_contig(lat, "lat");
+    check(lat.size(-1) == 576 && slot.scalar_type() == at::kLong && slot.numel() == lat.size(0), "mla_kv_write shapes");
+    check(codes.size(-1) == 256 && scales.size(-1) == 32 && rope.size(-1) == 64, "mla cache layout");
+    c10::cuda::CUDAGuard g(lat.device());
+    check_rc(xt_mla_kv_write(lat.data_ptr(), ptr<const int64_t>(slot), codes.data_ptr(), scales.data_ptr(),
+                             rope.data_ptr(), int(lat.size(0)), stream()),
+             "mla_kv_write");
+}
+
+void mla_decode(const Tensor &q, const Tensor &idx, const Tensor &codes, const Tensor &scales, const Tensor &rope,
+                const Tensor &kg, const Tensor &vt, const Tensor &part_o, const Tensor &part_ml, const Tensor &out,
+                double scale, const Tensor &err) {
+    cuda_contig(q, "q");
+    cuda_contig(idx, "idx");
+    const int64_t Q = q.size(0), nsel = idx.size(1);
+    check(q.size(1) == 128 && q.size(2) == 576 && idx.size(0) == Q && idx.scalar_type() == at::kInt, "mla_decode q/idx");
+    check(kg.numel() >= Q * nsel * 576 && vt.numel() >= Q * 512 * nsel, "mla_decode gather scratch too small");
+    check(part_o.numel() >= Q * (nsel / 128) * 128 * 512 && part_ml.numel() >= Q * (nsel / 128) * 128 * 2,
+          "mla_decode partial scratch too small");
+    check(out.numel() == Q * 128 * 512, "mla_decode out [Q, 128, 512]");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_mla_decode(q.data_ptr(), ptr<const int32_t>(idx), int(Q), int(nsel), codes.data_ptr(),
+                           scales.data_ptr(), rope.data_ptr(), kg.data_ptr(), vt.data_ptr(), ptr<float>(part_o),
+                           ptr<float>(part_ml), out.data_ptr(), float(scale), ptr<int>(err), stream()),
+             "mla_decode");
+}
+
+void dsa_key_write(const Tensor &k, const Tensor &slot, const Tensor &codes, const Tensor &kscale) {
+    cuda_contig(k, "k");
+    check(k.size(-1) == 128 && slot.scalar_type() == at::kLong && slot.numel() == k.size(0) &&
+              codes.size(-1) == 128 && kscale.scalar_type() == at::kFloat,
+          "dsa_key_write shapes");
+    c10::cuda::CUDAGuard g(k.device());
+    check_rc(xt_dsa_key_write(k.data_ptr(), ptr<const int64_t>(slot), codes.data_ptr(), ptr<float>(kscale),
+                              int(k.size(0)), stream()),
+             "dsa_key_write");
+}
+
+void dsa_index_decode(const Tensor &q, const Tensor &w, const Tensor &codes, const Tensor &kscale, const Tensor &base,
+                      const Tensor &len, const Tensor &scores) {
+    cuda_contig(q, "q");
+    check(q.size(1) == 64 && q.size(2) == 128 && w.size(1) == 64 && base.scalar_type() == at::kLong &&
+              len.scalar_type() == at::kInt && scores.scalar_type() == at::kFloat,
+          "dsa_index_decode shapes");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_dsa_index_decode(q.data_ptr(), ptr<const float>(w), codes.data_ptr(), ptr<const float>(kscale),
+                                 ptr<const int64_t>(base), ptr<const int32_t>(len), ptr<float>(scores),
+                                 int(q.size(0)), int(scores.size(1)), stream()),
+             "dsa_index_decode");
+}
+
+void topk_rows(const Tensor &scores, int64_t K, const Tensor &out) {
+    cuda_contig(scores, "scores");
+    check(scores.scalar_type() == at::kFloat && out.scalar_type() == at::kInt && out.size(0) == scores.size(0) &&
+              out.size(1) == K,
+          "topk_rows shapes");
+    c10::cuda::CUDAGuard g(scores.device());
+    check_rc(xt_topk_rows(ptr<const float>(scores), int(scores.size(0)), int(scores.size(1)), int(K),
+                          ptr<int32_t>(out), stream()),
+             "topk_rows");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(xtier, m) {
@@ -352,6 +415,13 @@ TORCH_LIBRARY(xtier, m) {
           "Tensor s13, Tensor g13, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(c!) out, Tensor(d!) err, "
           "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases) -> ()");
     m.def("l2_prefetch(Tensor ptrs, Tensor bytes, int ctas) -> ()");
+    m.def("dsa_key_write(Tensor k, Tensor slot, Tensor(a!) codes, Tensor(b!) kscale) -> ()");
+    m.def("dsa_index_decode(Tensor q, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, "
+          "Tensor(a!) scores) -> ()");
+    m.def("topk_rows(Tensor scores, int K, Tensor(a!) out) -> ()");
+    m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");
+    m.def("mla_decode(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!) kg, Tensor(b!) vt, "
+          "Tensor(c!) part_o, Tensor(d!) part_ml, Tensor(e!) out, float scale, Tensor(f!) err) -> ()");
     m.def("gemm_rs(Tensor a, Tensor b, Tensor peer, Tensor(a!) state, Tensor? residual, Tensor(b!) out, "
           "Tensor(c!) err, int W, int rank, int[] offsets, float timeout_s) -> ()");
     m.def("ag_gemm(Tensor a_shard, Tensor b, Tensor peer, int local_base, Tensor(a!) state, Tensor(b!) out, "
@@ -375,4 +445,9 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("gemm_rs", &gemm_rs);
     m.impl("ag_gemm", &ag_gemm);
     m.impl("l2_prefetch", &l2_prefetch);
+    m.impl("mla_kv_write", &mla_kv_write);
+    m.impl("mla_decode", &mla_decode);
+    m.impl("dsa_key_write", &dsa_key_write);
+    m.impl("dsa_index_decode", &dsa_index_decode);
+    m.impl("topk_rows", &topk_rows);
 }

@@ -1,0 +1,479 @@
+// DeepSeek-style MLA attention over an NVFP4 latent KV cache, decode path (sm_100a):
+//
+//   mla_kv_write    one warp per new token: the 512 latent values -> NVFP4 (E2M1 codes + one E4M3 scale per 16,
+//                   global scale 1), the 64 rotary values stay BF16. 416 bytes per token instead of 1152.
+//   mla_gather      the selected keys of each query (an index list per query: the DSA indexer's top-k, or 0..n-1 for
+//                   dense attention) dequantized into a K tile [keys, 576] and a transposed V tile [512, keys], BF16,
+//                   the operand layouts of the tensor-core kernel below (both K-major).
+//   mla_attend      one CTA per (query, block of 128 selected keys), tcgen05 + TMEM + TMA:
+//                     S[128 heads, 128 keys] = Q[128, 576] . K^T            (9 k-blocks of 64, TMEM columns 256..383)
+//                     P = exp2(S * scale - rowmax) in BF16, written to shared memory in the 128-byte-swizzled
+//                         K-major layout the MMA reads (4 softmax warps, one head row per thread)
+//                     O[128, 512] = P . V                                    (two N = 256 halves: TMEM columns 0..255
+//                                                                             and 256..511 -- the second reuses S's)
+//                   and writes the unnormalized O with the row max and sum; a block is one softmax pass, so no
+//                   accumulator rescaling is needed inside the CTA.
+//   mla_merge       per (query, head): the blocks' partials -> softmax-weighted sum -> BF16 latent output [128, 512]
+//                   (the per-head value projection W_uv follows as a batched GEMM).
+// Every mbarrier wait is bounded; a wait that runs out sets the error word and the CTA winds down.
+// Reference parity: xtier/packs/deepseek_v4/sparse_mla.py:1-20 (sparse MLA over a quantized KV cache: BF16 tensor-core
+// Q.K with FP32 scores, P in BF16 for the PV product, FP32 accumulation, split keys merged in FP32; invalid indices
+// (-1) never enter the sums).
+#include <cudaTypedefs.h>
+
+#include "params.h"
+#include "tc_common.cuh"
+
+namespace xt {
+
+constexpr int MLA_H = 128;       // heads (the UMMA M)
+constexpr int MLA_L = 512;       // latent dims
+constexpr int MLA_R = 64;        // rotary dims
+constexpr int MLA_D = MLA_L + MLA_R;
+constexpr int MLA_BK = 64;       // k-block (one 128-byte swizzle row of BF16)
+constexpr int MLA_NB = 128;      // selected keys per CTA
+constexpr int MLA_STAGES = 4;
+constexpr int MLA_THREADS = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 softmax / epilogue
+
+// ------------------------------------------------------------------------------------------------ cache write
+__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;\n" : "=h"(r) : "f"(0.f), "f"(v));
+    return uint8_t(r & 0xFF);
+}
+
+// two floats -> one byte of two E2M1 codes (a in the low nibble), round to nearest even, saturating at 6
+__device__ __forceinline__ uint8_t f32x2_to_e2m1(float a, float b) {
+    uint16_t r;
+    asm("{\n .reg .b8 t;\n cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n cvt.u16.u8 %0, t;\n}\n" : "=h"(r) : "f"(a), "f"(b));
+    return uint8_t(r);
+}
+
+__global__ void __launch_bounds__(256) mla_kv_write_kernel(const __nv_bfloat16 *__restrict__ lat, const int64_t *slot,
+                                                           uint8_t *codes, uint8_t *scales, __nv_bfloat16 *rope,
+                                                           int T) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const __nv_bfloat16 *x = lat + size_t(warp) * MLA_D;
+    const size_t s = size_t(slot[warp]);
+    // lane = one block of 16 latent values
+    float v[16];
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + lane * 16);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const uint4 u = src[c];
+        const __nv_bfloat162 *b = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(b[i]);
+            v[c * 8 + 2 * i] = f.x;
+            v[c * 8 + 2 * i + 1] = f.y;
+        }
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const uint8_t sc = f32_to_e4m3(amax / 6.f);
+    const float sf = e4m3_to_f(sc);
+    const float inv = sf > 0.f ? 1.f / sf : 0.f;
+    uint32_t w[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            acc |= uint32_t(f32x2_to_e2m1(v[h * 8 + 2 * i] * inv, v[h * 8 + 2 * i + 1] * inv)) << (8 * i);
+        w[h] = acc;
+    }
+    *reinterpret_cast<uint2 *>(codes + s * (MLA_L / 2) + lane * 8) = make_uint2(w[0], w[1]);
+    scales[s * (MLA_L / 16) + lane] = sc;
+    reinterpret_cast<__nv_bfloat162 *>(rope + s * MLA_R)[lane] =
+        reinterpret_cast<const __nv_bfloat162 *>(x + MLA_L)[lane];
+}
+
+// ------------------------------------------------------------------------------------------------ gather
+// grid (blocks of 32 selected keys, queries); idx [Q, nsel] int32 slots (-1: none). Kg [Q, nsel, 576], Vt [Q, 512,
+// nsel]. The block's latent rows are staged in shared memory so the transposed V rows are written 64 bytes at a time.
+__global__ void __launch_bounds__(256) mla_gather_kernel(const int32_t *__restrict__ idx, int nsel,
+                                                         const uint8_t *__restrict__ codes,
+                                                         const uint8_t *__restrict__ scales,
+                                                         const __nv_bfloat16 *__restrict__ rope,
+                                                         __nv_bfloat16 *__restrict__ Kg, __nv_bfloat16 *__restrict__ Vt) {
+    __shared__ __align__(16) __nv_bfloat16 tile[32][MLA_L + 8];
+    const int q = blockIdx.y, j0 = blockIdx.x * 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int jj = warp; jj < 32; jj += 8) {
+        const int j = j0 + jj;
+        const int s = j < nsel ? idx[size_t(q) * nsel + j] : -1;
+        __nv_bfloat16 *krow = Kg + (size_t(q) * nsel + min(j, nsel - 1)) * MLA_D;
+        // lane: 16 latent values (8 code bytes, one scale)
+        __nv_bfloat162 out[8];
+        if (s >= 0) {
+            const uint2 cw = *reinterpret_cast<const uint2 *>(codes + size_t(s) * (MLA_L / 2) + lane * 8);
+            const float sf = e4m3_to_f(scales[size_t(s) * (MLA_L / 16) + lane]);
+            __half2 h[4];
+            e2m1x8_to_h2(cw.x, h);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(h[i]);
+                out[i] = __floats2bfloat162_rn(f.x * sf, f.y * sf);
+            }
+            e2m1x8_to_h2(cw.y, h);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(h[i]);
+                out[4 + i] = __floats2bfloat162_rn(f.x * sf, f.y * sf);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) out[i] = __floats2bfloat162_rn(0.f, 0.f);
+        }
+        if (j < nsel) {
+            uint4 *dst = reinterpret_cast<uint4 *>(krow + lane * 16);
+            dst[0] = *reinterpret_cast<uint4 *>(&out[0]);
+            dst[1] = *reinterpret_cast<uint4 *>(&out[4]);
+            const __nv_bfloat162 r = s >= 0 ? reinterpret_cast<const __nv_bfloat162 *>(rope + size_t(s) * MLA_R)[lane]
+                                            : __floats2bfloat162_rn(0.f, 0.f);
+            reinterpret_cast<__nv_bfloat162 *>(krow + MLA_L)[lane] = r;
+        }
+        *reinterpret_cast<uint4 *>(&tile[jj][lane * 16]) = *reinterpret_cast<uint4 *>(&out[0]);
+        *reinterpret_cast<uint4 *>(&tile[jj][lane * 16 + 8]) = *reinterpret_cast<uint4 *>(&out[4]);
+    }
+    __syncthreads();
+    // Vt rows: dim d, keys j0..j0+31 (64 bytes): 4 threads per row, 16 bytes each
+    const int nk = min(32, nsel - j0);
+    for (int i = threadIdx.x; i < MLA_L * 4; i += blockDim.x) {
+        const int d = i >> 2, part = i & 3;
+        __nv_bfloat162 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = __halves2bfloat162(tile[part * 8 + 2 * k][d], tile[part * 8 + 2 * k + 1][d]);
+        if (part * 8 < nk)
+            *reinterpret_cast<uint4 *>(Vt + (size_t(q) * MLA_L + d) * nsel + j0 + part * 8) =
+                *reinterpret_cast<uint4 *>(v);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ attend
+struct MlaSmem {
+    static constexpr int STAGE = 32 * 1024;   // S: Q k-block 16 KB + K k-block 16 KB; O: one Vt tile [256, 64] 32 KB
+    static constexpr int P_BYTES = MLA_H * MLA_NB * 2;   // 32 KB: two swizzle atoms of [128 rows x 64 keys]
+    static constexpr int BYTES = MLA_STAGES * STAGE + P_BYTES + 1024 + 1024;
+};
+
+__global__ void __launch_bounds__(MLA_THREADS, 1)
+    mla_attend_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
+                      const __grid_constant__ CUtensorMap tma_v, const int32_t *__restrict__ idx, int nsel,
+                      float scale_log2, float *__restrict__ part_o, float *__restrict__ part_ml, int *error) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ps = smem + MLA_STAGES * MlaSmem::STAGE;   // P, 1024-aligned
+    uint64_t *full = reinterpret_cast<uint64_t *>(ps + MlaSmem::P_BYTES);
+    uint64_t *empty = full + MLA_STAGES;
+    uint64_t *sfull = empty + MLA_STAGES;
+    uint64_t *pfull = sfull + 1;
+    uint64_t *ofull = pfull + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ofull + 1);
+    __shared__ int valid[MLA_NB];
+    __shared__ volatile int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int blk = blockIdx.x, q = blockIdx.y;
+    const int nblk = gridDim.x;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < MLA_STAGES; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(sfull, 1);
+        tc::mbar_init(pfull, 4);
+        tc::mbar_init(ofull, 1);
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tma_q);
+        tc::prefetch_tmap(&tma_k);
+        tc::prefetch_tmap(&tma_v);
+    }
+    for (int j = threadIdx.x; j < MLA_NB; j += blockDim.x) {
+        const int jj = blk * MLA_NB + j;
+        valid[j] = jj < nsel && idx[size_t(q) * nsel + jj] >= 0;
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto fail = [&]() {
+        abort_flag = 1;
+        atomicExch(error, 1);
+    };
+    constexpr int KB_S = MLA_D / MLA_BK;   // 9 k-blocks of Q.K^T
+    constexpr int KB_O = MLA_NB / MLA_BK;  // 2 k-blocks of P.V per half
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            auto next = [&]() {
+                if (++stage == MLA_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            };
+            for (int kb = 0; kb < KB_S && !abort_flag; ++kb, next()) {
+                if (!tc::mbar_wait(&empty[stage], phase ^ 1)) {
+                    fail();
+                    break;
+                }
+                uint8_t *sa = smem + stage * MlaSmem::STAGE;
+                tc::mbar_arrive_expect_tx(&full[stage], 32 * 1024);
+                tc::tma_load_2d(sa, &tma_q, &full[stage], kb * MLA_BK, q * MLA_H);
+                tc::tma_load_2d(sa + 16 * 1024, &tma_k, &full[stage], kb * MLA_BK, q * nsel + blk * MLA_NB);
+            }
+            for (int half = 0; half < 2 && !abort_flag; ++half)
+                for (int kb = 0; kb < KB_O && !abort_flag; ++kb, next()) {
+                    if (!tc::mbar_wait(&empty[stage], phase ^ 1)) {
+                        fail();
+                        break;
+                    }
+                    uint8_t *sa = smem + stage * MlaSmem::STAGE;
+                    tc::mbar_arrive_expect_tx(&full[stage], 32 * 1024);
+                    tc::tma_load_2d(sa, &tma_v, &full[stage], blk * MLA_NB + kb * MLA_BK, q * MLA_L + half * 256);
+                }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            auto next = [&]() {
+                if (++stage == MLA_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            };
+            const uint32_t idesc_s = tc::idesc_bf16_f32(MLA_H, MLA_NB);
+            const uint32_t idesc_o = tc::idesc_bf16_f32(MLA_H, 256);
+            bool ok = true;
+            for (int kb = 0; kb < KB_S && ok; ++kb, next()) {
+                if (!(ok = tc::mbar_wait(&full[stage], phase))) break;
+                tc::tc_fence_after();
+                const uint32_t sa = tc::smem_u32(smem + stage * MlaSmem::STAGE);
+                const uint64_t ad = tc::sw128_kmajor_desc(sa), bd = tc::sw128_kmajor_desc(sa + 16 * 1024);
+#pragma unroll
+                for (int k = 0; k < MLA_BK / 16; ++k)
+                    tc::mma_f16(tmem + 256, ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc_s,
+                                (kb > 0 || k > 0) ? 1u : 0u);
+                tc::mma_commit(&empty[stage]);
+            }
+            if (ok) tc::mma_commit(sfull);
+            if (ok && !(ok = tc::mbar_wait(pfull, 0))) fail();
+            tc::tc_fence_after();
+            for (int half = 0; half < 2 && ok; ++half)
+                for (int kb = 0; kb < KB_O && ok; ++kb, next()) {
+                    if (!(ok = tc::mbar_wait(&full[stage], phase))) break;
+                    tc::tc_fence_after();
+                    const uint32_t sv = tc::smem_u32(smem + stage * MlaSmem::STAGE);
+                    const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_u32(ps) + kb * 16 * 1024);
+                    const uint64_t bd = tc::sw128_kmajor_desc(sv);
+#pragma unroll
+                    for (int k = 0; k < MLA_BK / 16; ++k)
+                        tc::mma_f16(tmem + uint32_t(half * 256), ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc_o,
+                                    (kb > 0 || k > 0) ? 1u : 0u);
+                    tc::mma_commit(&empty[stage]);
+                }
+            if (ok) tc::mma_commit(ofull);
+            else fail();
+        }
+    } else {
+        // softmax / epilogue: warp w reads TMEM lanes 32*(w%4)..+31 = heads
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;   // head
+        const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        bool ok = true;
+        if (lane == 0) ok = tc::mbar_wait(sfull, 0);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        float m = -INFINITY, l = 0.f;
+        if (ok && !abort_flag) {
+            tc::tc_fence_after();
+            float sv[MLA_NB];
+#pragma unroll
+            for (int c = 0; c < MLA_NB / 32; ++c) {
+                uint32_t r[32];
+                tc::tmem_ld32(lane_base + 256 + uint32_t(c * 32), r);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    sv[c * 32 + i] = valid[c * 32 + i] ? __uint_as_float(r[i]) * scale_log2 : -INFINITY;
+            }
+#pragma unroll
+            for (int i = 0; i < MLA_NB; ++i) m = fmaxf(m, sv[i]);
+            // P in BF16, 128-byte swizzled K-major: atom a = keys 64a..64a+63, row `row`, 16-byte chunk c at c ^ (row&7)
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+                uint8_t *rowp = ps + a * 16 * 1024 + row * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    __nv_bfloat162 pv[4];
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const int k0 = a * 64 + c * 8 + 2 * t;
+                        const float p0 = m == -INFINITY ? 0.f : exp2f(sv[k0] - m);
+                        const float p1 = m == -INFINITY ? 0.f : exp2f(sv[k0 + 1] - m);
+                        pv[t] = __floats2bfloat162_rn(p0, p1);
+                        const float2 back = __bfloat1622float2(pv[t]);
+                        l += back.x + back.y;
+                    }
+                    *reinterpret_cast<uint4 *>(rowp + ((c ^ (row & 7)) << 4)) = *reinterpret_cast<uint4 *>(pv);
+                }
+            }
+        }
+        // P visible to the tensor core (async proxy), TMEM reads of S done before O overwrites it
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(pfull);
+        if (lane == 0 && ok) ok = tc::mbar_wait(ofull, 0);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        const size_t unit = size_t(q) * nblk + blk;
+        float *po = part_o + (unit * MLA_H + row) * MLA_L;
+        if (ok && !abort_flag) {
+            tc::tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < MLA_L / 32; ++c) {
+                uint32_t r[32];
+                tc::tmem_ld32(lane_base + uint32_t(c * 32), r);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int v = 0; v < 8; ++v)
+                    reinterpret_cast<float4 *>(po + c * 32)[v] =
+                        make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                    __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            }
+        } else {
+            if (lane == 0 && !ok) fail();
+            for (int c = 0; c < MLA_L; ++c) po[c] = 0.f;
+            m = -INFINITY;
+            l = 0.f;
+        }
+        part_ml[(unit * MLA_H + row) * 2] = m;
+        part_ml[(unit * MLA_H + row) * 2 + 1] = l;
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ merge
+// grid (heads, queries), 128 threads: thread t -> dims 4t..4t+3
+__global__ void __launch_bounds__(128) mla_merge_kernel(const float *__restrict__ part_o,
+                                                        const float *__restrict__ part_ml, int nblk,
+                                                        __nv_bfloat16 *__restrict__ out) {
+    const int h = blockIdx.x, q = blockIdx.y;
+    float M = -INFINITY;
+    for (int b = 0; b < nblk; ++b) M = fmaxf(M, part_ml[((size_t(q) * nblk + b) * MLA_H + h) * 2]);
+    float L = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int b = 0; b < nblk; ++b) {
+        const size_t unit = (size_t(q) * nblk + b) * MLA_H + h;
+        const float mb = part_ml[unit * 2];
+        const float f = mb == -INFINITY ? 0.f : exp2f(mb - M);
+        L += part_ml[unit * 2 + 1] * f;
+        const float4 v = reinterpret_cast<const float4 *>(part_o + unit * MLA_L)[threadIdx.x];
+        o.x += v.x * f;
+        o.y += v.y * f;
+        o.z += v.z * f;
+        o.w += v.w * f;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    __nv_bfloat162 *dst = reinterpret_cast<__nv_bfloat162 *>(out + (size_t(q) * MLA_H + h) * MLA_L) + threadIdx.x * 2;
+    dst[0] = __floats2bfloat162_rn(o.x * inv, o.y * inv);
+    dst[1] = __floats2bfloat162_rn(o.z * inv, o.w * inv);
+}
+
+}  // namespace xt
+
+using namespace xt;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 mla_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult qr;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+bool mla_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = mla_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+    cuuint32_t box[2] = {cuuint32_t(MLA_BK), box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+// lat [T, 576] bf16 -> cache slot[t] (codes [slots, 256] u8, scales [slots, 32] u8, rope [slots, 64] bf16)
+int xt_mla_kv_write(const void *lat, const int64_t *slot, void *codes, void *scales, void *rope, int T,
+                    cudaStream_t stream) {
+    if (T <= 0) return 0;
+    const int warps = 8;
+    mla_kv_write_kernel<<<(T + warps - 1) / warps, warps * 32, 0, stream>>>(
+        static_cast<const __nv_bfloat16 *>(lat), slot, static_cast<uint8_t *>(codes), static_cast<uint8_t *>(scales),
+        static_cast<__nv_bfloat16 *>(rope), T);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Attention of Q queries (128 heads each) over their selected cache slots. q [Q, 128, 576] bf16 (absorbed: latent
+// part q_nope . W_uk, then the rotary part), idx [Q, nsel] int32 (nsel % 128 == 0; -1 = no key), scratch: Kg [Q, nsel,
+// 576] bf16, Vt [Q, 512, nsel] bf16, part_o [Q, nsel/128, 128, 512] f32, part_ml [Q, nsel/128, 128, 2] f32.
+// out [Q, 128, 512] bf16 = softmax(scale * q.k) . v over the selected keys (latent values).
+int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
+                  const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,
+                  int *error, cudaStream_t stream) {
+    if (Q <= 0 || nsel <= 0 || nsel % MLA_NB) return -2;
+    dim3 gg(nsel / 32, Q);
+    mla_gather_kernel<<<gg, 256, 0, stream>>>(idx, nsel, static_cast<const uint8_t *>(codes),
+                                              static_cast<const uint8_t *>(scales),
+                                              static_cast<const __nv_bfloat16 *>(rope),
+                                              static_cast<__nv_bfloat16 *>(Kg), static_cast<__nv_bfloat16 *>(Vt));
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    CUtensorMap mq, mk, mv;
+    if (!mla_map(&mq, q, uint64_t(Q) * MLA_H, MLA_D, MLA_H) ||
+        !mla_map(&mk, Kg, uint64_t(Q) * nsel, MLA_D, MLA_NB) ||
+        !mla_map(&mv, Vt, uint64_t(Q) * MLA_L, uint64_t(nsel), 256))
+        return -3;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(mla_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MlaSmem::BYTES) !=
+            cudaSuccess)
+            return -4;
+        attr = true;
+    }
+    const int nblk = nsel / MLA_NB;
+    dim3 ga(nblk, Q);
+    mla_attend_kernel<<<ga, MLA_THREADS, MlaSmem::BYTES, stream>>>(mq, mk, mv, idx, nsel,
+                                                                  scale * 1.4426950408889634f, part_o, part_ml, error);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    dim3 gm(MLA_H, Q);
+    mla_merge_kernel<<<gm, 128, 0, stream>>>(part_o, part_ml, nblk, static_cast<__nv_bfloat16 *>(out));
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // extern "C"

@@ -1,0 +1,60 @@
+"""DSA selection on the GPU against fp32 PyTorch: FP8 index-key cache round trip, indexer scores (ReLU head sum over
+64 heads, per-query lengths), top-k sets and their ascending order (with -1 padding on short rows), and the whole
+sparse decode chain (indexer -> top-k -> MLA over the selected latent rows)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_index_scores_and_topk(cuda_ops):
+    from xtier_b200.attention import dsa
+    g = torch.Generator(device='cuda').manual_seed(3)
+    rows, max_len = 3, 3000
+    cache = dsa.IndexCache(rows, max_len)
+    k = torch.randn(rows * max_len, 128, device='cuda', generator=g).bfloat16()
+    cache.write(k, torch.arange(rows * max_len, device='cuda'))
+    back = cache.dequant(torch.arange(rows * max_len, device='cuda'))
+    assert float((back - k.float()).norm() / k.float().norm()) < 0.05   # E4M3: 3 mantissa bits
+    Q = 4
+    q = torch.randn(Q, 64, 128, device='cuda', generator=g).bfloat16()
+    w = torch.rand(Q, 64, device='cuda', generator=g)
+    qrows = torch.tensor([0, 1, 2, 1], device='cuda')
+    lens = torch.tensor([3000, 1500, 700, 2999], device='cuda', dtype=torch.int32)
+    sc = dsa.index_scores(q, w, cache, qrows, lens)
+    ref = dsa.reference_scores(q, w, cache, qrows, lens)
+    fin = torch.isfinite(ref)
+    assert torch.equal(fin, torch.isfinite(sc))
+    assert float((sc[fin] - ref[fin]).abs().max() / ref[fin].abs().max()) < 1e-3
+    K = 1024
+    idx = dsa.topk(sc, K)
+    want = dsa.reference_topk(sc, K)
+    for r in range(Q):
+        row = idx[r].tolist()
+        got = [i for i in row if i >= 0]
+        assert got == sorted(got)                       # ascending
+        assert set(got) == want[r], r
+        assert all(i == -1 for i in row[len(got):])     # padding at the end only
+    assert (idx[2] >= 0).sum() == 700                  # short row: every finite score, then -1
+
+
+def test_sparse_decode_chain(cuda_ops):
+    from xtier_b200.attention import dsa
+    from xtier_b200.attention.mla import LatentCache, MlaWorkspace, default_scale, mla_decode, reference_decode
+    g = torch.Generator(device='cuda').manual_seed(5)
+    rows, max_len, K = 2, 4096, 2048
+    icache, lcache = dsa.IndexCache(rows, max_len), LatentCache(rows, max_len)
+    n = rows * max_len
+    icache.write(torch.randn(n, 128, device='cuda', generator=g).bfloat16(), torch.arange(n, device='cuda'))
+    lcache.write(torch.randn(n, 576, device='cuda', generator=g).bfloat16(), torch.arange(n, device='cuda'))
+    qrows = torch.tensor([0, 1], device='cuda')
+    lens = torch.tensor([4000, 1800], device='cuda', dtype=torch.int32)
+    sc = dsa.index_scores(torch.randn(2, 64, 128, device='cuda', generator=g).bfloat16(),
+                          torch.rand(2, 64, device='cuda', generator=g), icache, qrows, lens)
+    slots = dsa.select_slots(sc, qrows, K, max_len)
+    assert int((slots[1] >= 0).sum()) == 1800
+    q = (torch.randn(2, 128, 576, device='cuda', generator=g) * 0.5).bfloat16()
+    ws = MlaWorkspace(2, K)
+    out = mla_decode(q, slots, lcache, ws, default_scale())
+    ref = reference_decode(q, slots, lcache, default_scale())
+    assert float((out.float() - ref).norm() / ref.norm()) < 2e-2
