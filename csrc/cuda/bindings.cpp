@@ -387,6 +387,20 @@ void dsa_index_decode(const Tensor &q, const Tensor &w, const Tensor &codes, con
              "dsa_index_decode");
 }
 
+void dsa_index_tc(const Tensor &q8, const Tensor &w, const Tensor &codes, const Tensor &kscale, const Tensor &base,
+                  const Tensor &len, const Tensor &scores, int64_t nq, const Tensor &err) {
+    cuda_contig(q8, "q8");
+    check(q8.scalar_type() == at::kByte && q8.size(1) == 64 && q8.size(2) == 128 && codes.size(-1) == 128 &&
+              w.scalar_type() == at::kFloat && scores.scalar_type() == at::kFloat,
+          "dsa_index_tc shapes");
+    c10::cuda::CUDAGuard g(q8.device());
+    check_rc(xt_dsa_index_tc(q8.data_ptr(), ptr<const float>(w), codes.data_ptr(), codes.size(0),
+                             ptr<const float>(kscale), ptr<const int64_t>(base), ptr<const int32_t>(len),
+                             ptr<float>(scores), int(q8.size(0)), int(scores.size(1)), int(nq), ptr<int>(err),
+                             stream()),
+             "dsa_index_tc");
+}
+
 void topk_rows(const Tensor &scores, int64_t K, const Tensor &out) {
     cuda_contig(scores, "scores");
     check(scores.scalar_type() == at::kFloat && out.scalar_type() == at::kInt && out.size(0) == scores.size(0) &&
@@ -419,6 +433,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("dsa_index_decode(Tensor q, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, "
           "Tensor(a!) scores) -> ()");
     m.def("topk_rows(Tensor scores, int K, Tensor(a!) out) -> ()");
+    m.def("dsa_index_tc(Tensor q8, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, Tensor(a!) scores, "
+          "int nq, Tensor(b!) err) -> ()");
     m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");
     m.def("mla_decode(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!) kg, Tensor(b!) vt, "
           "Tensor(c!) part_o, Tensor(d!) part_ml, Tensor(e!) out, float scale, Tensor(f!) err) -> ()");
@@ -450,4 +466,5 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("dsa_key_write", &dsa_key_write);
     m.impl("dsa_index_decode", &dsa_index_decode);
     m.impl("topk_rows", &topk_rows);
+    m.impl("dsa_index_tc", &dsa_index_tc);
 }

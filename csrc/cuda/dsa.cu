@@ -14,8 +14,10 @@
 // Reference parity: the reference drives DeepSeek V4's indexer through SGLang and its packs (xtier/packs/
 // deepseek_v4/paged_indexer.py:1-13 scores a decode step's compressed index keys and selects with a top-k kernel;
 // xtier/packs/qwen4_exp/qsa_prefill.py:1-12 the ReLU head-sum MQA logits).
-#include "common.cuh"
+#include <cudaTypedefs.h>
+
 #include "params.h"
+#include "tc_common.cuh"
 
 namespace xt {
 
@@ -103,6 +105,102 @@ __global__ void __launch_bounds__(256) dsa_index_decode_kernel(const __nv_bfloat
     if (hq == 0 && key < max_len) scores[size_t(t) * max_len + key] = valid ? part : -INFINITY;
 }
 
+// ------------------------------------------------------------------------------------------------ tensor-core indexer
+// One CTA per (128 keys, NQ queries that share the keys' cache row): D[128 keys, 64 NQ] = K8[128, 128] . Q8^T on
+// tcgen05 (kind::f8f6f4, E4M3 x E4M3, FP32 accumulation in TMEM; K = 128 = one 128-byte swizzle row), then each
+// epilogue thread owns one key (one TMEM lane) and reduces its row: score[q, key] = kscale[key] *
+// sum_h w[q, h] * relu(D[key, q*64 + h]) (w already carries the query's FP8 scale). Causal rows (prefill) mask keys
+// past the query's position.
+template <int NQ>
+__global__ void __launch_bounds__(192, 1)
+    dsa_index_tc_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constant__ CUtensorMap tma_q,
+                        const float *__restrict__ w, const float *__restrict__ kscale, const int64_t *__restrict__ base,
+                        const int32_t *__restrict__ len, float *__restrict__ scores, int max_len, int *error) {
+    constexpr int N = IDX_HEADS * NQ;
+    __shared__ __align__(1024) uint8_t sk[128 * 128];
+    __shared__ __align__(1024) uint8_t sq[N * 128];
+    __shared__ uint64_t full, done;
+    __shared__ uint32_t tmem_slot;
+    __shared__ float ws[NQ][IDX_HEADS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x, qg = blockIdx.y;
+    const int q0 = qg * NQ;
+    const int64_t row_base = base[q0];   // the NQ queries share the cache row
+    int nmax = 0;
+    for (int i = 0; i < NQ; ++i) nmax = max(nmax, len[q0 + i]);
+    const bool any = tile * 128 < nmax;
+    for (int i = threadIdx.x; i < NQ * IDX_HEADS; i += blockDim.x) ws[i / IDX_HEADS][i % IDX_HEADS] = w[size_t(q0) * IDX_HEADS + i];
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&full, 1);
+        tc::mbar_init(&done, 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&tmem_slot, N < 32 ? 32 : N);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+    if (any) {
+        if (warp == 0 && lane == 0) {
+            tc::mbar_arrive_expect_tx(&full, 128 * 128 + N * 128);
+            tc::tma_load_2d(sk, &tma_k, &full, 0, int(row_base) + tile * 128);
+            tc::tma_load_2d(sq, &tma_q, &full, 0, q0 * IDX_HEADS);
+        } else if (warp == 1 && lane == 0) {
+            if (tc::mbar_wait(&full, 0)) {
+                tc::tc_fence_after();
+                // kind::f8f6f4: D F32 (bit 4), A and B E4M3 (format 0), N / 8, M / 16
+                const uint32_t idesc = (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+                const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_u32(sk)), bd = tc::sw128_kmajor_desc(tc::smem_u32(sq));
+#pragma unroll
+                for (int k = 0; k < 4; ++k)   // K = 32 bytes per MMA
+                    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                 " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+                                 "l"(ad + uint64_t(2 * k)), "l"(bd + uint64_t(2 * k)), "r"(idesc), "r"(k > 0 ? 1u : 0u)
+                                 : "memory");
+                tc::mma_commit(&done);
+            } else {
+                atomicExch(error, 1);
+                tc::mbar_arrive(&done);   // let the epilogue go (it writes -inf)
+            }
+        } else if (warp >= 2) {
+            const int quarter = warp & 3;
+            const int key = tile * 128 + quarter * 32 + lane;
+            if (lane == 0) ok = tc::mbar_wait(&done, 0);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            tc::tc_fence_after();
+            const float ks = key < max_len ? kscale[row_base + key] : 0.f;
+#pragma unroll
+            for (int qq = 0; qq < NQ; ++qq) {
+                float acc = 0.f;
+#pragma unroll
+                for (int c = 0; c < IDX_HEADS / 32; ++c) {
+                    uint32_t r[32];
+                    tc::tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(qq * IDX_HEADS + c * 32), r);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc += ws[qq][c * 32 + i] * fmaxf(__uint_as_float(r[i]), 0.f);
+                }
+                if (key < max_len)
+                    scores[size_t(q0 + qq) * max_len + key] = (ok && key < len[q0 + qq]) ? acc * ks : -INFINITY;
+            }
+        }
+    } else if (threadIdx.x >= 64) {   // nothing to score in this tile: -inf for every query
+        const int key = tile * 128 + threadIdx.x - 64;
+        if (key < max_len)
+            for (int qq = 0; qq < NQ; ++qq) scores[size_t(q0 + qq) * max_len + key] = -INFINITY;
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, N < 32 ? 32 : N);
+    }
+}
+
 // order-preserving image of a float: larger float -> larger unsigned (NaN never occurs here)
 __device__ __forceinline__ uint32_t fkey(float f) {
     const uint32_t u = __float_as_uint(f);
@@ -143,68 +241,125 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(const float *__re
     __shared__ int hist[256];
     __shared__ int warp_sums[32];
     __shared__ uint32_t prefix_s;
-    __shared__ int need_s;
+    __shared__ int need_s, finite_s;
     const int row = blockIdx.x;
     const float *x = scores + size_t(row) * n;
     int32_t *o = out + size_t(row) * K;
-    // radix select of the K-th largest key among finite scores
+    const bool vec = (n % 4) == 0;   // rows 16-byte aligned
+    // radix select of the K-th largest key among finite scores (pass 0 also counts them)
     uint32_t prefix = 0;
     int need = K;
-    int finite = 0;
-    for (int i = threadIdx.x; i < n; i += TK_THREADS) finite += x[i] > -INFINITY;
-    int tot;
-    block_scan(finite, warp_sums, &tot);
-    const bool all = tot <= K;
-    if (!all) {
-        for (int pass = 0; pass < 4; ++pass) {
-            const int shift = 24 - 8 * pass;
-            const uint32_t mask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
-            for (int i = threadIdx.x; i < 256; i += TK_THREADS) hist[i] = 0;
-            __syncthreads();
-            for (int i = threadIdx.x; i < n; i += TK_THREADS) {
-                const float v = x[i];
-                if (v == -INFINITY) continue;
-                const uint32_t k = fkey(v);
+    bool all = false;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        const uint32_t mask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
+        for (int i = threadIdx.x; i < 256; i += TK_THREADS) hist[i] = 0;
+        if (threadIdx.x == 0) finite_s = 0;
+        __syncthreads();
+        int fin = 0;
+        // 4 consecutive elements per thread and step, 4 steps unrolled: 16 loads in flight per thread
+#pragma unroll 4
+        for (int i0 = threadIdx.x * 4; i0 < n; i0 += TK_THREADS * 4) {
+            float v[4];
+            if (vec && i0 + 3 < n) {
+                const float4 f = *reinterpret_cast<const float4 *>(x + i0);
+                v[0] = f.x;
+                v[1] = f.y;
+                v[2] = f.z;
+                v[3] = f.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[e] = i0 + e < n ? x[i0 + e] : -INFINITY;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (v[e] == -INFINITY) continue;
+                ++fin;
+                const uint32_t k = fkey(v[e]);
                 if ((k & mask) == (prefix & mask)) atomicAdd(&hist[(k >> shift) & 0xFF], 1);
             }
-            __syncthreads();
-            if (threadIdx.x == 0) {   // walk the buckets from the largest
-                int acc = 0, b = 255;
-                for (; b > 0; --b) {
+        }
+        if (pass == 0) {
+            fin += __shfl_xor_sync(0xffffffffu, fin, 16);
+            fin += __shfl_xor_sync(0xffffffffu, fin, 8);
+            fin += __shfl_xor_sync(0xffffffffu, fin, 4);
+            fin += __shfl_xor_sync(0xffffffffu, fin, 2);
+            fin += __shfl_xor_sync(0xffffffffu, fin, 1);
+            if ((threadIdx.x & 31) == 0) atomicAdd(&finite_s, fin);
+        }
+        __syncthreads();
+        if (pass == 0 && finite_s <= K) {
+            all = true;
+            break;
+        }
+        if (threadIdx.x < 32) {   // bucket of the need-th largest: lane l sums buckets 255-8l .. 248-8l, warp scan
+            const int l = threadIdx.x;
+            int c8 = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) c8 += hist[255 - 8 * l - j];
+            int inc = c8;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (l >= o) inc += y;
+            }
+            const unsigned hit = __ballot_sync(0xffffffffu, inc >= need);
+            const int L = hit ? __ffs(hit) - 1 : 31;
+            if (l == L) {
+                int acc = inc - c8, b = 255 - 8 * l;
+                for (int j = 0; j < 7; ++j, --b) {
                     if (acc + hist[b] >= need) break;
                     acc += hist[b];
                 }
                 prefix_s = prefix | (uint32_t(b) << shift);
                 need_s = need - acc;
             }
-            __syncthreads();
-            prefix = prefix_s;
-            need = need_s;
-            __syncthreads();
         }
+        __syncthreads();
+        prefix = prefix_s;
+        need = need_s;
+        __syncthreads();
     }
-    // ordered compaction: keys above the threshold, then `need` of the keys equal to it, in index order
+    // ordered compaction, 4 consecutive elements per thread and one block scan per chunk: keys above the threshold,
+    // then `need` of the keys equal to it, in index order
     const uint32_t thr = prefix;
     int gt_before = 0, eq_before = 0;
-    for (int c0 = 0; c0 < n; c0 += TK_THREADS) {
-        const int i = c0 + threadIdx.x;
-        const float v = i < n ? x[i] : -INFINITY;
-        const bool fin = v > -INFINITY;
-        const uint32_t k = fin ? fkey(v) : 0u;
-        const int gt = all ? int(fin) : int(fin && k > thr);
-        const int eq = all ? 0 : int(fin && k == thr);
-        int t_gt, t_eq;
-        const int p_gt = block_scan(gt, warp_sums, &t_gt);
-        const int p_eq = block_scan(eq, warp_sums, &t_eq);
-        const int eq_rank = eq_before + p_eq;
-        const bool take_eq = eq && eq_rank < need;
-        // output position: elements taken before i in index order
-        const int taken_before_gt = gt_before + p_gt;
-        const int taken_before_eq = min(eq_before + p_eq, need);
-        const int pos = taken_before_gt + taken_before_eq;
-        if ((gt || take_eq) && pos < K) o[pos] = i;
-        gt_before += t_gt;
-        eq_before += t_eq;
+    for (int c0 = 0; c0 < n; c0 += TK_THREADS * 4) {
+        const int i0 = c0 + threadIdx.x * 4;
+        int gt[4], eq[4], cg = 0, ce = 0;
+        float vv[4];
+        if (vec && i0 + 3 < n) {
+            const float4 f = *reinterpret_cast<const float4 *>(x + i0);
+            vv[0] = f.x;
+            vv[1] = f.y;
+            vv[2] = f.z;
+            vv[3] = f.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) vv[e] = i0 + e < n ? x[i0 + e] : -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float v = vv[e];
+            const bool fin = v > -INFINITY;
+            const uint32_t k = fin ? fkey(v) : 0u;
+            gt[e] = all ? int(fin) : int(fin && k > thr);
+            eq[e] = all ? 0 : int(fin && k == thr);
+            cg += gt[e];
+            ce += eq[e];
+        }
+        int tot;
+        const int pre = block_scan((cg << 16) | ce, warp_sums, &tot);
+        int pg = gt_before + (pre >> 16), pe = eq_before + (pre & 0xFFFF);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int pos = pg + min(pe, need);
+            if ((gt[e] || (eq[e] && pe < need)) && pos < K) o[pos] = i0 + e;
+            pg += gt[e];
+            pe += eq[e];
+        }
+        gt_before += tot >> 16;
+        eq_before += tot & 0xFFFF;
     }
     const int taken = gt_before + (all ? 0 : min(eq_before, need));
     for (int i = taken + threadIdx.x; i < K; i += TK_THREADS) o[i] = -1;
@@ -230,6 +385,44 @@ int xt_dsa_index_decode(const void *q, const float *w, const void *codes, const 
     dsa_index_decode_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(q), w,
                                                       static_cast<const uint8_t *>(codes), kscale, base, len, scores,
                                                       max_len);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+namespace {
+bool dsa_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult qr;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) != cudaSuccess ||
+            qr != cudaDriverEntryPointSuccess)
+            return false;
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    cuuint64_t dims[2] = {cuuint64_t(IDX_DIM), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(IDX_DIM)};
+    cuuint32_t box[2] = {cuuint32_t(IDX_DIM), box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+// Tensor-core indexer: q8 [Q, 64, 128] E4M3 (queries pre-quantized, w carries their scales), codes [slots, 128] E4M3,
+// nq queries per CTA share a cache row (1 for decode rows, 2 for a prefill chunk of one sequence).
+int xt_dsa_index_tc(const void *q8, const float *w, const void *codes, int64_t slots, const float *kscale,
+                    const int64_t *base, const int32_t *len, float *scores, int Q, int max_len, int nq, int *error,
+                    cudaStream_t stream) {
+    if (Q <= 0 || max_len <= 0 || (nq != 1 && nq != 2) || Q % nq) return -2;
+    CUtensorMap mk, mq;
+    if (!dsa_map(&mk, codes, uint64_t(slots), 128) || !dsa_map(&mq, q8, uint64_t(Q) * IDX_HEADS, IDX_HEADS * nq))
+        return -3;
+    dim3 grid((max_len + 127) / 128, Q / nq);
+    if (nq == 1)
+        dsa_index_tc_kernel<1><<<grid, 192, 0, stream>>>(mk, mq, w, kscale, base, len, scores, max_len, error);
+    else
+        dsa_index_tc_kernel<2><<<grid, 192, 0, stream>>>(mk, mq, w, kscale, base, len, scores, max_len, error);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -145,6 +145,9 @@ int xt_mla_kv_write(const void *lat, const int64_t *slot, void *codes, void *sca
 int xt_dsa_key_write(const void *k, const int64_t *slot, void *codes, float *kscale, int T, cudaStream_t stream);
 int xt_dsa_index_decode(const void *q, const float *w, const void *codes, const float *kscale, const int64_t *base,
                         const int32_t *len, float *scores, int Q, int max_len, cudaStream_t stream);
+int xt_dsa_index_tc(const void *q8, const float *w, const void *codes, int64_t slots, const float *kscale,
+                    const int64_t *base, const int32_t *len, float *scores, int Q, int max_len, int nq, int *error,
+                    cudaStream_t stream);
 int xt_topk_rows(const float *scores, int rows, int n, int K, int32_t *out, cudaStream_t stream);
 int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
                   const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,

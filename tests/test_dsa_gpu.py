@@ -21,11 +21,24 @@ def test_index_scores_and_topk(cuda_ops):
     w = torch.rand(Q, 64, device='cuda', generator=g)
     qrows = torch.tensor([0, 1, 2, 1], device='cuda')
     lens = torch.tensor([3000, 1500, 700, 2999], device='cuda', dtype=torch.int32)
-    sc = dsa.index_scores(q, w, cache, qrows, lens)
     ref = dsa.reference_scores(q, w, cache, qrows, lens)
     fin = torch.isfinite(ref)
-    assert torch.equal(fin, torch.isfinite(sc))
-    assert float((sc[fin] - ref[fin]).abs().max() / ref[fin].abs().max()) < 1e-3
+    sc_cc = dsa.index_scores(q, w, cache, qrows, lens, tensor_cores=False)       # CUDA cores, BF16 queries
+    assert torch.equal(fin, torch.isfinite(sc_cc))
+    assert float((sc_cc[fin] - ref[fin]).abs().max() / ref[fin].abs().max()) < 1e-3
+    err = torch.zeros(1, dtype=torch.int32, device='cuda')
+    sc = dsa.index_scores(q, w, cache, qrows, lens, err=err)                      # tcgen05, FP8 queries
+    ref8 = dsa.reference_scores(q, w, cache, qrows, lens, fp8_queries=True)
+    assert int(err) == 0 and torch.equal(fin, torch.isfinite(sc))
+    assert float((sc[fin] - ref8[fin]).abs().max() / ref8[fin].abs().max()) < 1e-3
+    # two queries of one cache row per CTA (prefill layout)
+    q2rows = torch.tensor([1, 1, 2, 2], device='cuda')
+    lens2 = torch.tensor([1500, 900, 700, 3000], device='cuda', dtype=torch.int32)
+    sc2 = dsa.index_scores(q, w, cache, q2rows, lens2, err=err, per_cta=2)
+    ref2 = dsa.reference_scores(q, w, cache, q2rows, lens2, fp8_queries=True)
+    fin2 = torch.isfinite(ref2)
+    assert int(err) == 0 and torch.equal(fin2, torch.isfinite(sc2))
+    assert float((sc2[fin2] - ref2[fin2]).abs().max() / ref2[fin2].abs().max()) < 1e-3
     K = 1024
     idx = dsa.topk(sc, K)
     want = dsa.reference_topk(sc, K)

@@ -33,16 +33,33 @@ class IndexCache:
         return self.codes[s].view(torch.float8_e4m3fn).float() * self.scale[s, None]
 
 
+def quantize_queries(q: torch.Tensor, w: torch.Tensor):
+    """q [Q, 64, 128] -> FP8 E4M3 bytes with one scale per (query, head), folded into the head weights (relu commutes
+    with a positive scale): returns (q8 uint8 [Q, 64, 128], w' fp32 [Q, 64])."""
+    qf = q.float()
+    s = (qf.abs().amax(-1) / 448.0).clamp_min(1e-12)
+    q8 = (qf / s[..., None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    return q8.contiguous(), (w.float() * s).contiguous()
+
+
 def index_scores(q: torch.Tensor, w: torch.Tensor, cache: IndexCache, rows: torch.Tensor, lengths: torch.Tensor,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, tensor_cores: bool = True, err: torch.Tensor | None = None,
+                 per_cta: int = 1) -> torch.Tensor:
     """q [Q, 64, 128] BF16, w [Q, 64] fp32, rows / lengths [Q] (each query's cache row and key count) -> scores
-    [Q, max_len] fp32 (-inf past the length)."""
+    [Q, max_len] fp32 (-inf past the length). The tensor-core path quantizes the queries to FP8 (E4M3 x E4M3 MMA);
+    per_cta = 2 lets two consecutive queries of one cache row share each key tile (prefill)."""
     Q = q.shape[0]
     out = torch.empty(Q, cache.max_len, dtype=torch.float32, device=q.device) if out is None else out
     base = rows.long() * cache.max_len
     ops.load()
-    torch.ops.xtier.dsa_index_decode(q.contiguous(), w.float().contiguous(), cache.codes, cache.scale, base,
-                                     lengths.int().contiguous(), out)
+    if tensor_cores:
+        q8, w8 = quantize_queries(q, w)
+        err = torch.zeros(1, dtype=torch.int32, device=q.device) if err is None else err
+        torch.ops.xtier.dsa_index_tc(q8, w8, cache.codes, cache.scale, base, lengths.int().contiguous(), out,
+                                     per_cta, err)
+    else:
+        torch.ops.xtier.dsa_index_decode(q.contiguous(), w.float().contiguous(), cache.codes, cache.scale, base,
+                                         lengths.int().contiguous(), out)
     return out
 
 
@@ -60,8 +77,12 @@ def select_slots(scores: torch.Tensor, rows: torch.Tensor, k: int, max_len: int)
     return torch.where(pos >= 0, pos + (rows.long() * max_len)[:, None].int(), pos)
 
 
-def reference_scores(q, w, cache: IndexCache, rows, lengths) -> torch.Tensor:
+def reference_scores(q, w, cache: IndexCache, rows, lengths, fp8_queries: bool = False) -> torch.Tensor:
+    """fp32 oracle; fp8_queries=True scores the FP8-rounded queries the tensor-core path uses."""
     Q = q.shape[0]
+    if fp8_queries:
+        q8, w = quantize_queries(q, w)
+        q = q8.view(torch.float8_e4m3fn).float()
     out = torch.full((Q, cache.max_len), float('-inf'), device=q.device)
     for i in range(Q):
         n = int(lengths[i])
