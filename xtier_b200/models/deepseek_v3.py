@@ -48,6 +48,11 @@ class DeepSeekV3Config:
     eps: float = 1e-6
     fmt: str = formats.MXFP4
     std: float = 0.02
+    attn: str = 'auto'        # decode attention: 'torch' (BF16 latent cache), 'mla' (NVFP4 latent cache, tcgen05),
+                              # 'dsa' (indexer top-k + 'mla'); 'auto' = 'mla' when the MLA kernels' shape fits
+    index_heads: int = 64     # DSA lightning indexer
+    index_dim: int = 128
+    index_topk: int = 2048
 
     @staticmethod
     def tiny(**kw):
@@ -95,6 +100,12 @@ class DeepSeekV3Model:
                      kv_a=randn(cfg.kv_lora + cfg.qk_rope, H), kv_a_norm=ones(cfg.kv_lora),
                      kv_b=randn(cfg.heads * (cfg.qk_nope + cfg.v_head), cfg.kv_lora),
                      o=randn(H, cfg.heads * cfg.v_head))
+            if cfg.attn == 'dsa':   # own seeds: the other weights are the same with and without the indexer
+                gi = torch.Generator(device=dev).manual_seed(seed * 7919 + li)
+                L['idx_q'] = (torch.randn(cfg.index_heads * cfg.index_dim, cfg.q_lora, device=dev, generator=gi)
+                              * cfg.std).bfloat16()
+                L['idx_k'] = (torch.randn(cfg.index_dim, H, device=dev, generator=gi) * cfg.std).bfloat16()
+                L['idx_w'] = (torch.randn(cfg.index_heads, H, device=dev, generator=gi) * cfg.std).bfloat16()
             kvb = L['kv_b'].view(cfg.heads, cfg.qk_nope + cfg.v_head, cfg.kv_lora)
             L['w_uk'] = kvb[:, :cfg.qk_nope].contiguous()          # [h, nope, lora]
             L['w_uv'] = kvb[:, cfg.qk_nope:].contiguous()          # [h, v, lora]
@@ -122,12 +133,29 @@ class DeepSeekV3Model:
             self.layers.append(L)
 
     # ------------------------------------------------------------------ state
+    def kernel_attention(self) -> bool:
+        """True when decode attention runs on the MLA kernels (NVFP4 latent cache, tcgen05)."""
+        cfg = self.cfg
+        fits = cfg.heads == 128 and cfg.kv_lora == 512 and cfg.qk_rope == 64 and self.device.type == 'cuda'
+        if cfg.attn in ('mla', 'dsa') and not fits:
+            raise ValueError('the MLA kernels need 128 heads, kv_lora 512 and qk_rope 64')
+        return cfg.attn in ('mla', 'dsa') or (cfg.attn == 'auto' and fits)
+
     def alloc_state(self, batch: int, max_len: int) -> dict:
         cfg = self.cfg
-        return dict(batch=batch, max_len=max_len,
-                    cache=[torch.zeros(batch, max_len, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16,
-                                       device=self.device) for _ in self.layers],
-                    lengths=torch.zeros(batch, dtype=torch.int32, device=self.device))
+        st = dict(batch=batch, max_len=max_len,
+                  cache=[torch.zeros(batch, max_len, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16,
+                                     device=self.device) for _ in self.layers],
+                  lengths=torch.zeros(batch, dtype=torch.int32, device=self.device))
+        if self.kernel_attention():
+            from ..attention.mla import BLOCK, LatentCache, MlaWorkspace
+            st['latent'] = [LatentCache(batch, max_len, self.device) for _ in self.layers]
+            nsel = cfg.index_topk if cfg.attn == 'dsa' else (max_len + BLOCK - 1) // BLOCK * BLOCK
+            st['mla_ws'] = MlaWorkspace(batch, nsel, self.device)
+            if cfg.attn == 'dsa':
+                from ..attention.dsa import IndexCache
+                st['index'] = [IndexCache(batch, max_len, self.device) for _ in self.layers]
+        return st
 
     # ------------------------------------------------------------------ blocks
     def _mla_project(self, L, h, pos):
@@ -136,6 +164,7 @@ class DeepSeekV3Model:
         T = h.shape[0]
         q_a = ops.linear(h, L['q_a'])
         q_a = ops.rmsnorm(q_a.contiguous(), L['q_a_norm'], cfg.eps)
+        self._q_a = q_a
         q = ops.linear(q_a, L['q_b']).view(T, cfg.heads, cfg.qk_nope + cfg.qk_rope)
         q_pe = _rope(q[..., cfg.qk_nope:].transpose(0, 1), pos, cfg.rope_theta).transpose(0, 1)
         q = torch.cat([q[..., :cfg.qk_nope], q_pe], -1)
@@ -160,6 +189,29 @@ class DeepSeekV3Model:
             o_lat = p @ kv[:, :cfg.kv_lora]                 # [h, lora]
             out[b] = torch.einsum('hl,hvl->hv', o_lat, L['w_uv'].float())
         return out.to(torch.bfloat16).view(B, -1)
+
+    def _mla_decode_kernel(self, li, L, st, q, h, q_a, rows, lens):
+        """Absorbed MLA decode on the tensor cores over the NVFP4 latent cache: every cached position (dense) or the
+        DSA indexer's top-k (sparse). q [B, heads, nope+rope] -> [B, heads * v]."""
+        from ..attention import dsa
+        from ..attention.mla import mla_decode
+        cfg = self.cfg
+        B = q.shape[0]
+        q_lat = torch.einsum('bhn,hnl->bhl', q[..., :cfg.qk_nope].float(), L['w_uk'].float())
+        qf = torch.cat([q_lat, q[..., cfg.qk_nope:].float()], -1).to(torch.bfloat16).contiguous()
+        lc = st['latent'][li]
+        if cfg.attn == 'dsa':
+            qi = ops.linear(q_a, L['idx_q']).view(B, cfg.index_heads, cfg.index_dim)
+            w = ops.linear(h, L['idx_w']).float() * cfg.index_heads ** -0.5
+            scores = dsa.index_scores(qi, w, st['index'][li], rows, lens)
+            idx = dsa.select_slots(scores, rows, cfg.index_topk, st['max_len'])
+        else:
+            nsel = st['mla_ws'].nsel
+            pos = torch.arange(nsel, device=q.device, dtype=torch.int32)[None]
+            idx = torch.where(pos < lens[:, None], pos + rows[:, None] * st['max_len'], -1).int()
+        o_lat = mla_decode(qf, idx, lc, st['mla_ws'], 1.0 / math.sqrt(cfg.qk_nope + cfg.qk_rope))
+        out = torch.einsum('bhl,hvl->bhv', o_lat.float(), L['w_uv'].float())
+        return out.to(torch.bfloat16).reshape(B, -1)
 
     def _mla_prefill(self, L, q, lat, start):
         """Expanded MLA (causal) for one sequence: q [T, h, nope+rope], lat [start+T, lora+rope] -> [T, h*v]."""
@@ -201,9 +253,17 @@ class DeepSeekV3Model:
             q, lat = self._mla_project(L, h, pos)
             cache = st['cache'][li]
             cache[rows.long(), pos.long()] = lat
+            if 'latent' in st:
+                slots = rows.long() * st['max_len'] + pos.long()
+                st['latent'][li].write(lat, slots)
+                if 'index' in st:
+                    st['index'][li].write(ops.linear(h, L['idx_k']), slots)
             if decode:
                 lens = pos + 1
-                a = self._mla_decode(L, q, cache[rows.long()], lens)
+                if 'latent' in st:
+                    a = self._mla_decode_kernel(li, L, st, q, h, self._q_a, rows, lens)
+                else:
+                    a = self._mla_decode(L, q, cache[rows.long()], lens)
             else:
                 start = int(pos[0])
                 a = self._mla_prefill(L, q, cache[int(rows[0]), :start + T], start)
