@@ -401,6 +401,32 @@ void dsa_index_tc(const Tensor &q8, const Tensor &w, const Tensor &codes, const 
              "dsa_index_tc");
 }
 
+void moe_grouped(const Tensor &x, const Tensor &codes, const Tensor &scales, const Tensor &gscale,
+                 const Tensor &tiles, bool gate_up, int64_t I, int64_t fmt, const std::optional<Tensor> &route_w,
+                 const Tensor &out, const Tensor &err) {
+    cuda_contig(x, "x");
+    cuda_contig(codes, "codes");
+    cuda_contig(scales, "scales");
+    cuda_contig(tiles, "tiles");
+    check(x.scalar_type() == at::kBFloat16 && tiles.scalar_type() == at::kInt && tiles.size(1) == 4,
+          "moe_grouped: bf16 x, int32 tiles [T, 4]");
+    const int64_t R = x.size(0), K = x.size(1), slots = codes.size(0), N_rows = codes.size(1);
+    check(codes.size(2) * 2 == K, "moe_grouped: codes [slots, N_rows, K/2]");
+    if (gate_up)
+        check(out.scalar_type() == at::kBFloat16 && out.size(0) == R && out.size(1) == I && N_rows == 2 * I,
+              "moe_grouped gate_up: mid [R, I] bf16");
+    else
+        check(out.scalar_type() == at::kFloat && out.size(0) == R && out.size(1) == N_rows && route_w.has_value(),
+              "moe_grouped down: y [R, H] f32 and route weights");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_moe_grouped(x.data_ptr(), int(R), codes.data_ptr(), int(slots), ptr<const int32_t>(tiles),
+                            int(tiles.size(0)), gate_up ? 1 : 0, int(K), int(N_rows), int(I), int(fmt),
+                            scales.data_ptr(), ptr<const float>(gscale), optr<const float>(route_w),
+                            gate_up ? out.data_ptr() : nullptr, gate_up ? nullptr : ptr<float>(out),
+                            int(out.size(1)), ptr<int>(err), stream()),
+             "moe_grouped");
+}
+
 void topk_rows(const Tensor &scores, int64_t K, const Tensor &out) {
     cuda_contig(scores, "scores");
     check(scores.scalar_type() == at::kFloat && out.scalar_type() == at::kInt && out.size(0) == scores.size(0) &&
@@ -433,6 +459,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("dsa_index_decode(Tensor q, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, "
           "Tensor(a!) scores) -> ()");
     m.def("topk_rows(Tensor scores, int K, Tensor(a!) out) -> ()");
+    m.def("moe_grouped(Tensor x, Tensor codes, Tensor scales, Tensor gscale, Tensor tiles, bool gate_up, int I, "
+          "int fmt, Tensor? route_w, Tensor(a!) out, Tensor(b!) err) -> ()");
     m.def("dsa_index_tc(Tensor q8, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, Tensor(a!) scores, "
           "int nq, Tensor(b!) err) -> ()");
     m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");
@@ -466,5 +494,6 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("dsa_key_write", &dsa_key_write);
     m.impl("dsa_index_decode", &dsa_index_decode);
     m.impl("topk_rows", &topk_rows);
+    m.impl("moe_grouped", &moe_grouped);
     m.impl("dsa_index_tc", &dsa_index_tc);
 }

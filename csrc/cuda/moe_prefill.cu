@@ -1,0 +1,380 @@
+// Grouped FP4 expert GEMM for prefill on the 5th-generation tensor cores (sm_100a: tcgen05 + TMEM + TMA).
+//
+// Routes are sorted by expert slot (host side), so each slot's tokens form a contiguous run of rows of the gathered
+// activations X [R, K] (BF16; each run padded to a multiple of 128 rows). A tile is (run, 128 rows, BN = 128 output
+// rows of the expert); the tile list comes from the host. Persistent CTAs, one per SM, 10 warps:
+//   warp 0    TMA producer: per k-block of 64, the X tile [128 x 64] BF16 (128-byte swizzle) and the expert's raw
+//             FP4 codes [128 rows x 32 bytes] (two boxes of 64 rows: gate and up rows for GATE_UP, consecutive rows
+//             for DOWN)
+//   warps 6-9 dequantization: E2M1 codes x block scale (E4M3 per 16 or UE8M0 per 32) -> BF16, written in the
+//             128-byte-swizzled K-major layout the MMA reads. E2M1 x E4M3 has at most 4 significant bits, so the
+//             BF16 weights are exact: the GEMM is W4A16 with FP32 accumulation, the numerics of the decode kernels.
+//   warp 1    MMA issuer (kind::f16, M 128, N 128, K 16 per instruction), double-buffered TMEM accumulators
+//   warps 2-5 epilogue: GATE_UP -> SwiGLU(g13[0] * gate, g13[1] * up) of the tile's 64 columns -> mid BF16;
+//             DOWN -> route weight * g2 * D -> Y FP32 rows (summed per token afterwards in route order)
+// Every mbarrier wait is bounded; a wait that runs out sets the error word and the CTA winds down.
+// Reference parity: xtier/backend/prefill.py:64-140 (grouped gate/up and down over sorted route tiles with SwiGLU)
+// and :1511 (FlashInfer CUTLASS fused MoE on SM100), replaced here by one kernel of this project's own.
+#include <cudaTypedefs.h>
+
+#include "params.h"
+#include "tc_common.cuh"
+
+namespace xt {
+
+constexpr int GP_BM = 128, GP_BN = 128, GP_BK = 64, GP_STAGES = 4, GP_THREADS = 320;
+
+struct GpSmem {
+    static constexpr int A = GP_BM * GP_BK * 2;          // 16 KB
+    static constexpr int RAW = GP_BN * GP_BK / 2;         // 4 KB of codes
+    static constexpr int B = GP_BN * GP_BK * 2;           // 16 KB of BF16 weights
+    static constexpr int STAGE = A + B + RAW;             // A and B 1024-aligned, RAW after them
+    static constexpr int BYTES = GP_STAGES * STAGE + 1024 + 1024;
+};
+
+struct GpParams {
+    const int32_t *tiles;     // [T, 4]: slot, first row in X, n-tile, valid rows
+    int T;
+    int K, N_rows;            // K of this GEMM; rows of one expert's weight matrix (2I or H)
+    int I;                    // GATE_UP: the expert's intermediate size (up rows start at I)
+    int fmt;                  // 0 NVFP4, 1 MXFP4
+    const uint8_t *scales;    // [slots, N_rows, K / bs]
+    const float *gscale;      // GATE_UP: g13 [slots, 2]; DOWN: g2 [slots]
+    const float *route_w;     // DOWN: [R] route weight of each row of X
+    __nv_bfloat16 *mid;       // GATE_UP out: [R, I]
+    float *y;                 // DOWN out: [R, H]
+    int out_cols;             // I (gate/up) or H (down)
+    int *error;
+};
+
+template <bool GATE_UP>
+__global__ void __launch_bounds__(GP_THREADS, 1)
+    moe_grouped_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_w,
+                       GpParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + GP_STAGES * GpSmem::STAGE);
+    uint64_t *ready = full + GP_STAGES;
+    uint64_t *empty = ready + GP_STAGES;
+    uint64_t *tfull = empty + GP_STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    __shared__ volatile int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblocks = p.K / GP_BK;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < GP_STAGES; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&ready[s], 4);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tempty[b], 4);
+        }
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tma_x);
+        tc::prefetch_tmap(&tma_w);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 2 * GP_BN);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto fail = [&]() {
+        abort_flag = 1;
+        atomicExch(p.error, 1);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            for (int t = blockIdx.x; t < p.T && !abort_flag; t += gridDim.x) {
+                const int4 tl = reinterpret_cast<const int4 *>(p.tiles)[t];
+                const int slot = tl.x, row0 = tl.y, nt = tl.z;
+                const int wrow0 = GATE_UP ? slot * p.N_rows + nt * (GP_BN / 2) : slot * p.N_rows + nt * GP_BN;
+                const int wrow1 = GATE_UP ? slot * p.N_rows + p.I + nt * (GP_BN / 2) : wrow0 + GP_BN / 2;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!tc::mbar_wait(&empty[stage], phase ^ 1)) {
+                        fail();
+                        break;
+                    }
+                    uint8_t *st = smem + stage * GpSmem::STAGE;
+                    uint8_t *raw = st + GpSmem::A + GpSmem::B;
+                    tc::mbar_arrive_expect_tx(&full[stage], GpSmem::A + GpSmem::RAW);
+                    tc::tma_load_2d(st, &tma_x, &full[stage], kb * GP_BK, row0);
+                    tc::tma_load_2d(raw, &tma_w, &full[stage], kb * (GP_BK / 2), wrow0);
+                    tc::tma_load_2d(raw + GpSmem::RAW / 2, &tma_w, &full[stage], kb * (GP_BK / 2), wrow1);
+                    issued = min(issued + 1, GP_STAGES);
+                    if (++stage == GP_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (abort_flag)
+                for (int q = 0; q < issued; ++q) {
+                    if (--stage < 0) {
+                        stage = GP_STAGES - 1;
+                        phase ^= 1;
+                    }
+                    tc::mbar_wait(&full[stage], phase, 1u << 20);
+                }
+        }
+    } else if (warp >= 6) {
+        // dequantization warps: 128 threads, 8 chunks of 8 codes each per k-block (BN rows x 8 chunks)
+        const int dt = threadIdx.x - 6 * 32;
+        const int bs = p.fmt == 0 ? 16 : 32;
+        const int srow = p.K / bs;
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int t = blockIdx.x; t < p.T && !abort_flag; t += gridDim.x) {
+            const int4 tl = reinterpret_cast<const int4 *>(p.tiles)[t];
+            const int slot = tl.x, nt = tl.z;
+            for (int kb = 0; kb < kblocks; ++kb) {
+                bool ok = true;
+                if (lane == 0) ok = tc::mbar_wait(&full[stage], phase);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok || abort_flag) {
+                    if (lane == 0 && !ok) fail();
+                    break;
+                }
+                uint8_t *st = smem + stage * GpSmem::STAGE;
+                uint8_t *bt = st + GpSmem::A;
+                const uint8_t *raw = bt + GpSmem::B;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int c = dt + i * 128;   // chunk index: row r, 8-element chunk q
+                    const int r = c >> 3, q = c & 7;
+                    const int wr = GATE_UP ? (r < 64 ? nt * 64 + r : p.I + nt * 64 + (r - 64)) : nt * GP_BN + r;
+                    const uint8_t *sp = p.scales + (size_t(slot) * p.N_rows + wr) * srow;
+                    const int kel = kb * GP_BK + q * 8;   // first element of the chunk
+                    const float sf = p.fmt == 0 ? e4m3_to_f(sp[kel / 16]) : ue8m0_to_f(sp[kel / 32]);
+                    const uint32_t codes = *reinterpret_cast<const uint32_t *>(raw + r * 32 + q * 4);
+                    __half2 h[4];
+                    e2m1x8_to_h2(codes, h);
+                    uint4 o;
+                    __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(h[j]);
+                        o2[j] = __floats2bfloat162_rn(f.x * sf, f.y * sf);
+                    }
+                    *reinterpret_cast<uint4 *>(bt + r * 128 + ((q ^ (r & 7)) << 4)) = o;
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&ready[stage]);
+                if (++stage == GP_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_bf16_f32(GP_BM, GP_BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            for (int t = blockIdx.x; t < p.T && !abort_flag; t += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t use = uint32_t(local >> 1);
+                if (!tc::mbar_wait(&tempty[acc], (use & 1) ^ 1)) {
+                    fail();
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc * GP_BN);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!tc::mbar_wait(&full[stage], phase) || !tc::mbar_wait(&ready[stage], phase)) {
+                        fail();
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t sa = tc::smem_u32(smem + stage * GpSmem::STAGE);
+                    const uint64_t ad = tc::sw128_kmajor_desc(sa), bd = tc::sw128_kmajor_desc(sa + GpSmem::A);
+#pragma unroll
+                    for (int k = 0; k < GP_BK / 16; ++k)
+                        tc::mma_f16(d, ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    tc::mma_commit(&empty[stage]);
+                    if (++stage == GP_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                tc::mma_commit(&tfull[acc]);
+            }
+        }
+    } else {
+        // epilogue warps 2-5: TMEM lanes 32*(w%4).. = tile rows
+        const int quarter = warp & 3;
+        const int rit = quarter * 32 + lane;
+        int local = 0;
+        for (int t = blockIdx.x; t < p.T; t += gridDim.x, ++local) {
+            const int4 tl = reinterpret_cast<const int4 *>(p.tiles)[t];
+            const int slot = tl.x, row0 = tl.y, nt = tl.z, valid = tl.w;
+            const int acc = local & 1;
+            const uint32_t use = uint32_t(local >> 1);
+            bool ok = true;
+            if (lane == 0) ok = tc::mbar_wait(&tfull[acc], use & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok || abort_flag) {
+                if (lane == 0) fail();
+                break;
+            }
+            __syncwarp();
+            tc::tc_fence_after();
+            const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * GP_BN);
+            const int row = row0 + rit;
+            if (GATE_UP) {
+                const float gg = p.gscale[2 * slot], gu = p.gscale[2 * slot + 1];
+#pragma unroll 1
+                for (int c0 = 0; c0 < 64; c0 += 32) {
+                    uint32_t g[32], u[32];
+                    tc::tmem_ld32(base + uint32_t(c0), g);
+                    tc::tmem_ld32(base + uint32_t(64 + c0), u);
+                    tc::tmem_ld_wait();
+                    if (rit < valid) {
+                        __nv_bfloat16 *dst = p.mid + size_t(row) * p.out_cols + nt * 64 + c0;
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            uint4 o;
+                            __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                float h[2];
+#pragma unroll
+                                for (int e = 0; e < 2; ++e) {
+                                    const float a = __uint_as_float(g[v * 8 + 2 * i + e]) * gg;
+                                    const float b = __uint_as_float(u[v * 8 + 2 * i + e]) * gu;
+                                    h[e] = a / (1.f + __expf(-a)) * b;
+                                }
+                                o2[i] = __floats2bfloat162_rn(h[0], h[1]);
+                            }
+                            reinterpret_cast<uint4 *>(dst)[v] = o;
+                        }
+                    }
+                }
+            } else {
+                const float scale = rit < valid ? p.route_w[row] * p.gscale[slot] : 0.f;
+#pragma unroll 1
+                for (int c0 = 0; c0 < GP_BN; c0 += 32) {
+                    uint32_t r[32];
+                    tc::tmem_ld32(base + uint32_t(c0), r);
+                    tc::tmem_ld_wait();
+                    if (rit < valid) {
+                        float *dst = p.y + size_t(row) * p.out_cols + nt * GP_BN + c0;
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            reinterpret_cast<float4 *>(dst)[v] =
+                                make_float4(__uint_as_float(r[4 * v]) * scale, __uint_as_float(r[4 * v + 1]) * scale,
+                                            __uint_as_float(r[4 * v + 2]) * scale, __uint_as_float(r[4 * v + 3]) * scale);
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 2 * GP_BN);
+    }
+}
+
+}  // namespace xt
+
+using namespace xt;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 gp_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult qr;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+}  // namespace
+
+extern "C" {
+
+// One grouped GEMM over the tile list. x [R, K] BF16 (sorted, runs padded to 128 rows), codes [slots * N_rows, K/2],
+// scales [slots * N_rows, K/bs]. gate_up: mid [R, I] = SwiGLU(...); else y [R, H] = w * g2 * (x . W2^T).
+int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int32_t *tiles, int T, int gate_up,
+                   int K, int N_rows, int I, int fmt, const void *scales, const float *gscale, const float *route_w,
+                   void *mid, float *y, int out_cols, int *error, cudaStream_t stream) {
+    if (T <= 0) return 0;
+    if (K % GP_BK || R % GP_BM || N_rows % (gate_up ? 2 : GP_BN) || (gate_up && I % 64)) return -2;
+    auto fn = gp_encode_fn();
+    if (!fn) return -3;
+    CUtensorMap mx, mw;
+    {
+        cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(R)};
+        cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+        cuuint32_t box[2] = {GP_BK, GP_BM};
+        cuuint32_t estr[2] = {1, 1};
+        if (fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return -3;
+    }
+    {
+        cuuint64_t dims[2] = {cuuint64_t(K / 2), cuuint64_t(slots) * cuuint64_t(N_rows)};
+        cuuint64_t strides[1] = {cuuint64_t(K / 2)};
+        cuuint32_t box[2] = {GP_BK / 2, GP_BN / 2};
+        cuuint32_t estr[2] = {1, 1};
+        if (fn(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(codes), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return -3;
+    }
+    GpParams p{};
+    p.tiles = tiles;
+    p.T = T;
+    p.K = K;
+    p.N_rows = N_rows;
+    p.I = I;
+    p.fmt = fmt;
+    p.scales = static_cast<const uint8_t *>(scales);
+    p.gscale = gscale;
+    p.route_w = route_w;
+    p.mid = static_cast<__nv_bfloat16 *>(mid);
+    p.y = y;
+    p.out_cols = out_cols;
+    p.error = error;
+    static bool attr[2] = {false, false};
+    if (!attr[gate_up ? 1 : 0]) {
+        const void *f = gate_up ? reinterpret_cast<const void *>(moe_grouped_kernel<true>)
+                                : reinterpret_cast<const void *>(moe_grouped_kernel<false>);
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, GpSmem::BYTES) != cudaSuccess)
+            return -4;
+        attr[gate_up ? 1 : 0] = true;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = T < sms ? T : sms;
+    if (gate_up)
+        moe_grouped_kernel<true><<<grid, GP_THREADS, GpSmem::BYTES, stream>>>(mx, mw, p);
+    else
+        moe_grouped_kernel<false><<<grid, GP_THREADS, GpSmem::BYTES, stream>>>(mx, mw, p);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // extern "C"

@@ -149,6 +149,9 @@ int xt_dsa_index_tc(const void *q8, const float *w, const void *codes, int64_t s
                     const int64_t *base, const int32_t *len, float *scores, int Q, int max_len, int nq, int *error,
                     cudaStream_t stream);
 int xt_topk_rows(const float *scores, int rows, int n, int K, int32_t *out, cudaStream_t stream);
+int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int32_t *tiles, int T, int gate_up,
+                   int K, int N_rows, int I, int fmt, const void *scales, const float *gscale, const float *route_w,
+                   void *mid, float *y, int out_cols, int *error, cudaStream_t stream);
 int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
                   const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,
                   int *error, cudaStream_t stream);

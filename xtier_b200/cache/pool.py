@@ -20,10 +20,11 @@ import threading
 
 import torch
 
-from .. import ops
+from .. import config, ops
 from ..formats import MXFP4, NVFP4, ExpertWeights
 
 MAX_DECODE_TOKENS = 16
+_STAGING: dict = {}   # (cold experts, H, I, fmt, device) -> staging ExpertWeights shared by the layers
 
 
 class TieredMoE:
@@ -125,9 +126,17 @@ class TieredMoE:
 
     # ------------------------------------------------------------------ prefill (hybrid: GPU hot || CPU rest)
     def prefill(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None = None, chunk: int = 1024):
+        grouped = (x.shape[0] >= config.get('XTIER_GPU_PREFILL_MIN') and self.pool is not None
+                   and (self.all_hot or self.host is not None))
+        if grouped:   # every expert on the GPU: cold ones uploaded once for the whole call, larger chunks
+            stage = None if self.all_hot else self._staged()
+            chunk = 8192
         for s in range(0, x.shape[0], chunk):
             e = min(x.shape[0], s + chunk)
-            self._prefill_chunk(x[s:e], out[s:e], None if add is None else add[s:e])
+            if grouped:
+                self._prefill_grouped(x[s:e], out[s:e], None if add is None else add[s:e], stage)
+            else:
+                self._prefill_chunk(x[s:e], out[s:e], None if add is None else add[s:e])
         return out
 
     def _prefill_chunk(self, x, out, add):
@@ -165,6 +174,80 @@ class TieredMoE:
                 total += add.float()
             out.copy_(total.to(out.dtype))
         return out
+
+    def _prefill_grouped(self, x, out, add, stage=None):
+        """Prefill on the tensor cores: the hot (and shared) routes on the slot pool, the other routes on a staging
+        copy of the layer's cold experts uploaded from pinned host memory (the PCIe copy is the cost; every cold expert
+        is read once per call instead of once per 8 tokens by the CPU engine)."""
+        from .prefill import grouped_experts
+        m = x.shape[0]
+        if m > self.max_m:
+            self._alloc(max(m, self.max_m))
+        self.route(x, False)
+        slots, w = self.slots[:m], self.w[:m]
+        total = grouped_experts(x, slots, w, self.pool)
+        if not self.all_hot:
+            ids = self.ids[:m, :self.k]
+            cold = torch.where(slots[:, :self.k] < 0, self._cold_index[ids.long().clamp_min(0)],
+                               torch.full_like(ids, -1))
+            total += grouped_experts(x, cold, w[:, :self.k], stage)
+        if add is not None:
+            total += add.float()
+        out.copy_(total.to(out.dtype))
+        return out
+
+    def upload_async(self, stream: torch.cuda.Stream, after: torch.cuda.Event | None = None):
+        """Starts this layer's cold-expert upload on `stream` (after `after`, e.g. the previous user of the staging
+        buffer being done); the next prefill call of the layer waits for it instead of copying itself."""
+        if self.all_hot or self.host is None:
+            return
+        with torch.cuda.stream(stream):
+            if after is not None:
+                stream.wait_event(after)
+            stage = self._upload_cold()
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        self._pending = (stage, ev)
+
+    def _staged(self) -> ExpertWeights:
+        pending = getattr(self, '_pending', None)
+        if pending is not None:
+            self._pending = None
+            torch.cuda.current_stream(self.device).wait_event(pending[1])
+            return pending[0]
+        return self._upload_cold()
+
+    def prepare_prefill(self):
+        """Pinned host copy of the layer's cold experts (the source of the prefill uploads); done at model build so
+        the first prefill does not pay for page-locking."""
+        if self.all_hot or self.host is None or getattr(self, '_host_cold', None) is not None:
+            return
+        self._upload_cold(copy=False)
+
+    def _upload_cold(self, copy: bool = True) -> ExpertWeights:
+        """The layer's cold experts in a staging pool on the GPU (shared by the layers of one shape), copied from a
+        pinned host copy made on first use."""
+        if getattr(self, '_host_cold', None) is None:
+            cold = [e for e in range(self.E) if self.table_host[e] < 0]
+            idx = torch.full((self.E,), -1, dtype=torch.int32)
+            idx[cold] = torch.arange(len(cold), dtype=torch.int32)
+            self._cold_index = idx.to(self.device)
+            hc = self.host.select(torch.tensor(cold))
+            self._host_cold = ExpertWeights(self.fmt, *[getattr(hc, f).contiguous().pin_memory()
+                                                        for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
+            self._host_cold.g13 = self._host_cold.g13.float().pin_memory()
+            self._host_cold.g2 = self._host_cold.g2.float().pin_memory()
+        hc = self._host_cold
+        key = (hc.experts, self.H, self.I, self.fmt, self.device, self.layer % 2)   # two buffers: layer parity
+        stage = _STAGING.get(key)
+        if stage is None:
+            stage = ExpertWeights(self.fmt, *[torch.empty_like(getattr(hc, f), device=self.device)
+                                              for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
+            _STAGING[key] = stage
+        if copy:
+            for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+                getattr(stage, f).copy_(getattr(hc, f), non_blocking=True)
+        return stage
 
     # ------------------------------------------------------------------ residency changes
     def swap(self, incoming: int, victim: int):

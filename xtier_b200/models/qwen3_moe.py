@@ -127,6 +127,7 @@ class Qwen3MoeModel:
                 self.engines.append(engine)
             L['moe'] = TieredMoE(li, router, ew, cfg.top_k, hot=hot, router_bias=bias, mailbox=mailbox,
                                  engine=engine, device=dev, host_experts=host)
+            L['moe'].prepare_prefill()
             del ew
             self.layers.append(L)
 
@@ -230,12 +231,16 @@ class Qwen3MoeModel:
         h = torch.empty_like(residual)
         moe_out = torch.empty_like(residual)
         q = torch.empty(T, cfg.heads, D, dtype=torch.bfloat16, device=dev)
+        copy_stream = None
+        if T >= config.get('XTIER_GPU_PREFILL_MIN') and dev.type == 'cuda':
+            copy_stream = getattr(self, '_copy_stream', None) or torch.cuda.Stream(device=dev)
+            self._copy_stream = copy_stream
         for li, L in enumerate(self.layers):
             if li == 0:
                 ops.add_rmsnorm(residual, None, L['in_norm'], h, cfg.eps)
             else:
                 ops.add_rmsnorm(moe_out, residual, L['in_norm'], h, cfg.eps)
-            qkv = torch.matmul(h, L['qkv'].t())
+            qkv = ops.linear(h, L['qkv'])
             ops.qk_norm_rope_kv(qkv, L['q_norm'], L['k_norm'], pos, rows, q, st['k'][li], st['v'][li], cfg.heads,
                                 cfg.kv_heads, cfg.rope_theta, cfg.eps)
             kk = st['k'][li][row:row + 1, :, :start + T]
@@ -243,11 +248,17 @@ class Qwen3MoeModel:
             qq = q.transpose(0, 1).unsqueeze(0)
             attn = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=(start == 0),
                                                                     enable_gqa=True)
-            o = torch.matmul(attn[0].transpose(0, 1).reshape(T, -1), L['o'].t())
+            o = ops.linear(attn[0].transpose(0, 1).reshape(T, -1).contiguous(), L['o'])
             ops.add_rmsnorm(o, residual, L['post_norm'], h, cfg.eps)
+            if copy_stream is not None and li + 1 < len(self.layers):
+                # the next layer's cold experts cross PCIe while this layer computes; its staging buffer (layer
+                # parity) was last read by layer li - 1, whose MoE is done when this layer's starts
+                done = torch.cuda.Event()
+                done.record()
+                self.layers[li + 1]['moe'].upload_async(copy_stream, after=done)
             L['moe'].forward(h, out=moe_out)
         ops.add_rmsnorm(moe_out, residual, self.final_norm, h, cfg.eps)
-        logits = torch.matmul(h[-1:], self.lm_head.t())
+        logits = ops.linear(h[-1:].contiguous(), self.lm_head)
         st['lengths'][row] = start + T
         nxt = torch.argmax(logits, dim=-1)
         return (nxt, logits[0]) if return_logits else nxt
