@@ -2,11 +2,11 @@
 //
 // Routes are sorted by expert slot (host side), so each slot's tokens form a contiguous run of rows of the gathered
 // activations X [R, K] (BF16; each run padded to a multiple of 128 rows). A tile is (run, 128 rows, BN = 128 output
-// rows of the expert); the tile list comes from the host. Persistent CTAs, one per SM, 10 warps:
+// rows of the expert); the tile list comes from the host. Persistent CTAs, one per SM, 14 warps:
 //   warp 0    TMA producer: per k-block of 64, the X tile [128 x 64] BF16 (128-byte swizzle) and the expert's raw
 //             FP4 codes [128 rows x 32 bytes] (two boxes of 64 rows: gate and up rows for GATE_UP, consecutive rows
 //             for DOWN)
-//   warps 6-9 dequantization: E2M1 codes x block scale (E4M3 per 16 or UE8M0 per 32) -> BF16, written in the
+//   warps 6-13 dequantization: E2M1 codes x block scale (E4M3 per 16 or UE8M0 per 32) -> BF16, written in the
 //             128-byte-swizzled K-major layout the MMA reads. E2M1 x E4M3 has at most 4 significant bits, so the
 //             BF16 weights are exact: the GEMM is W4A16 with FP32 accumulation, the numerics of the decode kernels.
 //   warp 1    MMA issuer (kind::f16, M 128, N 128, K 16 per instruction), double-buffered TMEM accumulators
@@ -22,7 +22,8 @@
 
 namespace xt {
 
-constexpr int GP_BM = 128, GP_BN = 128, GP_BK = 64, GP_STAGES = 4, GP_THREADS = 320;
+constexpr int GP_BM = 128, GP_BN = 128, GP_BK = 64, GP_STAGES = 4, GP_THREADS = 448;
+constexpr int GP_DQ_WARPS = 8;   // dequantization warps (6..13)
 
 struct GpSmem {
     static constexpr int A = GP_BM * GP_BK * 2;          // 16 KB
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
         abort_flag = 0;
         for (int s = 0; s < GP_STAGES; ++s) {
             tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&ready[s], 4);
+            tc::mbar_init(&ready[s], GP_DQ_WARPS);
             tc::mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -128,7 +129,8 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                 }
         }
     } else if (warp >= 6) {
-        // dequantization warps: 128 threads, 8 chunks of 8 codes each per k-block (BN rows x 8 chunks)
+        // dequantization warps: 256 threads, 4 chunks of 8 codes each per k-block (BN rows x 8 chunks); the block
+        // scales of a k-block are loaded before waiting for its codes, so their latency hides behind the wait
         const int dt = threadIdx.x - 6 * 32;
         const int bs = p.fmt == 0 ? 16 : 32;
         const int srow = p.K / bs;
@@ -137,7 +139,20 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
         for (int t = blockIdx.x; t < p.T && !abort_flag; t += gridDim.x) {
             const int4 tl = reinterpret_cast<const int4 *>(p.tiles)[t];
             const int slot = tl.x, nt = tl.z;
+            const uint8_t *sp[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = dt + i * 256, r = c >> 3;
+                const int wr = GATE_UP ? (r < 64 ? nt * 64 + r : p.I + nt * 64 + (r - 64)) : nt * GP_BN + r;
+                sp[i] = p.scales + (size_t(slot) * p.N_rows + wr) * srow;
+            }
             for (int kb = 0; kb < kblocks; ++kb) {
+                float sf[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int kel = kb * GP_BK + ((dt + i * 256) & 7) * 8;
+                    sf[i] = p.fmt == 0 ? e4m3_to_f(sp[i][kel / 16]) : ue8m0_to_f(sp[i][kel / 32]);
+                }
                 bool ok = true;
                 if (lane == 0) ok = tc::mbar_wait(&full[stage], phase);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -149,13 +164,9 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                 uint8_t *bt = st + GpSmem::A;
                 const uint8_t *raw = bt + GpSmem::B;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int c = dt + i * 128;   // chunk index: row r, 8-element chunk q
+                for (int i = 0; i < 4; ++i) {
+                    const int c = dt + i * 256;   // chunk index: row r, 8-element chunk q
                     const int r = c >> 3, q = c & 7;
-                    const int wr = GATE_UP ? (r < 64 ? nt * 64 + r : p.I + nt * 64 + (r - 64)) : nt * GP_BN + r;
-                    const uint8_t *sp = p.scales + (size_t(slot) * p.N_rows + wr) * srow;
-                    const int kel = kb * GP_BK + q * 8;   // first element of the chunk
-                    const float sf = p.fmt == 0 ? e4m3_to_f(sp[kel / 16]) : ue8m0_to_f(sp[kel / 32]);
                     const uint32_t codes = *reinterpret_cast<const uint32_t *>(raw + r * 32 + q * 4);
                     __half2 h[4];
                     e2m1x8_to_h2(codes, h);
@@ -164,7 +175,7 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const float2 f = __half22float2(h[j]);
-                        o2[j] = __floats2bfloat162_rn(f.x * sf, f.y * sf);
+                        o2[j] = __floats2bfloat162_rn(f.x * sf[i], f.y * sf[i]);
                     }
                     *reinterpret_cast<uint4 *>(bt + r * 128 + ((q ^ (r & 7)) << 4)) = o;
                 }

@@ -21,32 +21,39 @@ TILE = 128
 
 def plan(slots: torch.Tensor):
     """slots [m, k] int32 (-1: not on the GPU) -> (order: route ids sorted by slot, rows: destination row of each
-    sorted route in X, R: padded row count, runs: list of (slot, first row, count))."""
+    sorted route in X, R: padded row count, runs: CPU int64 [n, 3] of (slot, first row, count)). One device->host
+    copy (the per-slot counts)."""
     flat = slots.flatten().long()
     gpu = torch.nonzero(flat >= 0).flatten()
     if gpu.numel() == 0:
-        return gpu, gpu, 0, []
+        return gpu, gpu, 0, torch.zeros(0, 3, dtype=torch.long)
     key = flat[gpu]
     perm = torch.sort(key, stable=True).indices
     order = gpu[perm]
-    sorted_slots = key[perm]
-    uniq, counts = torch.unique_consecutive(sorted_slots, return_counts=True)
-    uniq, counts = uniq.tolist(), counts.tolist()
-    runs, rows, r0 = [], [], 0
-    for s, c in zip(uniq, counts):
-        runs.append((s, r0, c))
-        rows.append(torch.arange(r0, r0 + c))
-        r0 += (c + TILE - 1) // TILE * TILE
-    return order, torch.cat(rows).to(slots.device), r0, runs
+    uniq, counts = torch.unique_consecutive(key[perm], return_counts=True)
+    padded = (counts + TILE - 1) // TILE * TILE
+    starts = torch.cumsum(padded, 0) - padded                      # first row of each run in X
+    run_of = torch.repeat_interleave(torch.arange(counts.numel(), device=slots.device), counts)
+    first = torch.cumsum(counts, 0) - counts                         # first sorted route of each run
+    rows = starts[run_of] + (torch.arange(order.numel(), device=slots.device) - first[run_of])
+    runs = torch.stack([uniq, starts, counts], 1).cpu()
+    R = int(runs[-1, 1] + (runs[-1, 2] + TILE - 1) // TILE * TILE)
+    return order, rows, R, runs
 
 
-def _tiles(runs, n_tiles: int, device) -> torch.Tensor:
-    t = []
-    for s, r0, c in runs:
-        for mt in range(0, c, TILE):
-            for nt in range(n_tiles):
-                t.append((s, r0 + mt, nt, min(TILE, c - mt)))
-    return torch.tensor(t, dtype=torch.int32, device=device).reshape(-1, 4)
+def _tiles(runs: torch.Tensor, n_tiles: int, device) -> torch.Tensor:
+    """[T, 4] int32 (slot, first row, n-tile, valid rows) for every 128-row block of every run x every n-tile."""
+    mt = (runs[:, 2] + TILE - 1) // TILE
+    run = torch.repeat_interleave(torch.arange(runs.shape[0]), mt)
+    first_block = torch.cumsum(mt, 0) - mt
+    blk = torch.arange(run.numel()) - first_block[run]
+    row0 = runs[run, 1] + blk * TILE
+    valid = torch.clamp(runs[run, 2] - blk * TILE, max=TILE)
+    slot = runs[run, 0]
+    T = run.numel()
+    t = torch.stack([slot.repeat_interleave(n_tiles), row0.repeat_interleave(n_tiles),
+                     torch.arange(n_tiles).repeat(T), valid.repeat_interleave(n_tiles)], 1)
+    return t.to(torch.int32).to(device, non_blocking=True)
 
 
 def grouped_experts(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: ExpertWeights,
@@ -58,7 +65,7 @@ def grouped_experts(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool:
     dev = x.device
     out = torch.zeros(m, H, dtype=torch.float32, device=dev)
     order, rows, R, runs = plan(slots)
-    if not runs:
+    if runs.shape[0] == 0:
         return out
     if H % 128 or I % 64:
         raise ValueError('grouped prefill needs H % 128 == 0 and I % 64 == 0')
