@@ -4,12 +4,14 @@
 //            ranks); the full result D = sum_r A_r B_r^T is reduce-scattered by rows (rank j owns rows
 //            [j*M/W, (j+1)*M/W)). The epilogue stores every output tile as a BF16 partial straight into its owner's
 //            receive slot [src][rows][N] over NVLink and then releases a per-(src, tile) flag; the tile walk starts
-//            with the next rank's rows, so the transfers of finished tiles overlap the MMAs of the next ones. The
-//            owner then sums the W partials of each of its tiles in rank order (rs_reduce_kernel, FP32 sums).
+//            with the next rank's rows, so the transfers of finished tiles overlap the MMAs of the next ones; the
+//            rank's own tiles come last, and their epilogue waits for the peers' partials of the same tile and sums
+//            the W partials in rank order (FP32, + residual) into the output rows: no separate reduction pass.
 //   MODE_AG  all-gather -> GEMM:      rank r holds the row shard A_r [M/W, K] (a column-parallel layer: B_r [N_r, K]);
-//            ag_push_kernel stores A_r into every rank's gather buffer [M, K] (its own included) in 128-row blocks,
-//            each released with a flag; the GEMM's TMA producer waits (bounded) for a block's flag and then loads the
-//            block from this rank's own gather buffer. The walk starts with the local rows.
+//            two push warps of every CTA store A_r into every peer's gather buffer [M, K] in 128-row blocks, each
+//            released with a flag, while the same kernel's MMAs run: the walk starts with the local rows, which the
+//            TMA producer reads straight from A_r; a peer's block is loaded (from this rank's own gather buffer)
+//            once its flag has arrived (bounded wait).
 // TMA only ever reads this rank's own memory; peer memory is touched only with plain stores and flag loads.
 // The receive and gather regions are double buffered by call parity (a rank can run at most one call ahead of its
 // peers), and a per-call epoch in device memory tags the flags, so the calls replay from CUDA graphs with no host
@@ -22,7 +24,7 @@
 namespace xt {
 
 
-constexpr int TP_BM = 128, TP_BK = 64, TP_STAGES = 4, TP_THREADS = 192;
+constexpr int TP_BM = 128, TP_BK = 64, TP_STAGES = 4, TP_THREADS = 192, TP_THREADS_AG = 256;
 constexpr int TP_GROUP_M = 16;   // raster groups of 128-row tiles (L2 reuse of A and B)
 
 template <int BN>
@@ -41,9 +43,9 @@ XT_DEV bool tp_wait_flag(const volatile uint32_t *f, uint32_t epoch, unsigned lo
 }
 
 template <int BN, int MODE>
-__global__ void __launch_bounds__(TP_THREADS, 1)
+__global__ void __launch_bounds__(TP_THREADS_AG, 1)
     gemm_tp_kernel(const __grid_constant__ CUtensorMap tma_a0, const __grid_constant__ CUtensorMap tma_a1,
-                   const __grid_constant__ CUtensorMap tma_b, TpParams p) {
+                   const __grid_constant__ CUtensorMap tma_b, const __grid_constant__ CUtensorMap tma_l, TpParams p) {
     using L = TpSmem<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -108,7 +110,8 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
             for (int i = blockIdx.x; i < tiles && !abort_flag; i += gridDim.x) {
                 int owner, tm, tn, j;
                 tile_at(i, owner, tm, tn, j);
-                if (MODE == 1) {   // the A block must have landed in this rank's gather buffer
+                const bool local_rows = MODE == 1 && owner == p.rank;   // AG: this rank's rows come from a_shard
+                if (MODE == 1 && !local_rows) {   // a peer's A block must have landed in this rank's gather buffer
                     const volatile uint32_t *f =
                         reinterpret_cast<const volatile uint32_t *>(me + (par ? p.off_flags[1] : p.off_flags[0])) + tm;
                     if (!tp_wait_flag(f, epoch, p.timeout_ns)) {
@@ -125,7 +128,10 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
                     uint8_t *sa = smem + stage * L::STAGE;
                     uint8_t *sb = sa + L::A_BYTES;
                     tc::mbar_arrive_expect_tx(&full[stage], L::STAGE);
-                    tc::tma_load_2d(sa, tma_a, &full[stage], kb * TP_BK, tm * TP_BM);
+                    if (local_rows)
+                        tc::tma_load_2d(sa, &tma_l, &full[stage], kb * TP_BK, (tm - owner * mb_per_owner) * TP_BM);
+                    else
+                        tc::tma_load_2d(sa, tma_a, &full[stage], kb * TP_BK, tm * TP_BM);
                     tc::tma_load_2d(sb, &tma_b, &full[stage], kb * TP_BK, tn * BN);
                     issued = min(issued + 1, TP_STAGES);
                     if (++stage == TP_STAGES) {
@@ -181,6 +187,38 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
                 tc::mma_commit(&tfull[acc]);
             }
         }
+    } else if (warp >= 6) {
+        // AG push warps (MODE 1 only): this rank's 128-row blocks into every peer's gather buffer over NVLink, each
+        // released with a flag; the blocks are spread over the CTAs, and the GEMM's local tiles run meanwhile
+        if (MODE == 1) {
+            const int pt = threadIdx.x - 192;   // 64 threads
+            const int items = (p.W - 1) * mb_per_owner;
+            const size_t n = size_t(TP_BM) * p.K / 8;   // 16-byte pieces per block
+            for (int it = blockIdx.x; it < items; it += gridDim.x) {
+                const int d = (p.rank + 1 + it / mb_per_owner) % p.W, blk = it % mb_per_owner;
+                uint8_t *dst_base = reinterpret_cast<uint8_t *>(p.peer[d]);
+                const size_t row0 = size_t(p.rank) * Mo + size_t(blk) * TP_BM;
+                const uint4 *src = reinterpret_cast<const uint4 *>(p.a_shard + size_t(blk) * TP_BM * p.K);
+                uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(
+                                                            dst_base + (par ? p.off_data[1] : p.off_data[0])) +
+                                                        row0 * p.K);
+                size_t i = pt;
+                for (; i + 3 * 64 < n; i += 4 * 64) {
+                    const uint4 v0 = src[i], v1 = src[i + 64], v2 = src[i + 128], v3 = src[i + 192];
+                    dst[i] = v0;
+                    dst[i + 64] = v1;
+                    dst[i + 128] = v2;
+                    dst[i + 192] = v3;
+                }
+                for (; i < n; i += 64) dst[i] = src[i];
+                __threadfence_system();
+                asm volatile("bar.sync 2, 64;\n" ::: "memory");
+                if (pt == 0)
+                    st_release_sys(reinterpret_cast<volatile uint32_t *>(dst_base + (par ? p.off_flags[1] : p.off_flags[0])) +
+                                       row0 / TP_BM,
+                                   epoch);
+            }
+        }
     } else {
         const int quarter = warp & 3;
         const int row_in_tile = quarter * 32 + lane;
@@ -201,11 +239,33 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
             tc::tc_fence_after();
             const int row = tm * TP_BM + row_in_tile;
             const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+            // RS: a peer's tile goes to its owner's receive slot; an own tile (walked last) meets the peers'
+            // partials here: wait for their flags, then sum all W partials in rank order (+ residual) and write the
+            // final rows -- no separate reduction pass
+            const bool own = MODE == 0 && owner == p.rank;
+            const __nv_bfloat16 *recv = reinterpret_cast<const __nv_bfloat16 *>(
+                reinterpret_cast<const uint8_t *>(p.peer[p.rank]) + (par ? p.off_data[1] : p.off_data[0]));
+            if (own) {
+                bool good = true;
+                if (lane == 0) {
+                    const volatile uint32_t *fl = reinterpret_cast<const volatile uint32_t *>(
+                        reinterpret_cast<const uint8_t *>(p.peer[p.rank]) + (par ? p.off_flags[1] : p.off_flags[0]));
+                    for (int s = 0; s < p.W && good; ++s)
+                        if (s != p.rank) good = tp_wait_flag(fl + size_t(s) * tpo + j, epoch, p.timeout_ns);
+                }
+                good = __shfl_sync(0xffffffffu, good, 0);
+                if (!good) {
+                    if (lane == 0) fail();
+                    break;
+                }
+            }
             __nv_bfloat16 *dst_row;
-            if (MODE == 0)
+            if (MODE == 0 && !own)
                 dst_row = reinterpret_cast<__nv_bfloat16 *>(reinterpret_cast<uint8_t *>(p.peer[owner]) +
                                                            (par ? p.off_data[1] : p.off_data[0])) +
                           (size_t(p.rank) * Mo + (row - owner * Mo)) * p.N;
+            else if (own)
+                dst_row = p.out + size_t(row - owner * Mo) * p.N;
             else
                 dst_row = p.out + size_t(row) * p.N;
 #pragma unroll 1
@@ -215,7 +275,48 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
                 tc::tmem_ld_wait();
                 const int col = tn * BN + c0;
                 if (col >= p.N) continue;
-                if (col + 32 <= p.N) {
+                if (own) {   // sum in rank order, this rank's partial from TMEM in its place
+                    const int lrow = row - owner * Mo;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        float f[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) f[q] = 0.f;
+                        for (int sr = 0; sr < p.W; ++sr) {
+                            if (sr == p.rank) {
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) f[q] += __bfloat162float(__float2bfloat16(__uint_as_float(r[v * 8 + q])));
+                            } else if (col + v * 8 + 8 <= p.N) {
+                                const uint4 pv = __ldcv(reinterpret_cast<const uint4 *>(
+                                    recv + (size_t(sr) * Mo + lrow) * p.N + col + v * 8));
+                                const __nv_bfloat162 *p2 = reinterpret_cast<const __nv_bfloat162 *>(&pv);
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    const float2 g = __bfloat1622float2(p2[q]);
+                                    f[2 * q] += g.x;
+                                    f[2 * q + 1] += g.y;
+                                }
+                            }
+                        }
+                        if (p.residual && col + v * 8 + 8 <= p.N) {
+                            const uint4 rv = *reinterpret_cast<const uint4 *>(p.residual + size_t(lrow) * p.N + col + v * 8);
+                            const __nv_bfloat162 *r2 = reinterpret_cast<const __nv_bfloat162 *>(&rv);
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const float2 g = __bfloat1622float2(r2[q]);
+                                f[2 * q] += g.x;
+                                f[2 * q + 1] += g.y;
+                            }
+                        }
+                        if (col + v * 8 + 8 <= p.N) {
+                            uint4 o;
+                            __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) o2[q] = __floats2bfloat162_rn(f[2 * q], f[2 * q + 1]);
+                            *reinterpret_cast<uint4 *>(dst_row + col + v * 8) = o;
+                        }
+                    }
+                } else if (col + 32 <= p.N) {
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         uint4 o;
@@ -235,7 +336,8 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&tempty[acc]);
-            if (MODE == 0) {   // all four epilogue warps stored the tile: release it to its owner
+            if (MODE == 0 && !own) {   // all four epilogue warps stored the tile: release it to its owner (the
+                // barrier orders the warps' peer stores before the flag thread's system fence, which is cumulative)
                 asm volatile("bar.sync 1, 128;\n" ::: "memory");
                 if (warp == 2 && lane == 0) {
                     __threadfence_system();
@@ -252,96 +354,6 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
     if (warp == 1) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, 2 * BN);
-    }
-}
-
-// Owner side of MODE_RS: one CTA per owned tile waits for the W partials, sums them in rank order (+ residual).
-template <int BN>
-__global__ void __launch_bounds__(256) rs_reduce_kernel(TpParams p) {
-    __shared__ int ok;
-    __shared__ bool last;
-    const int Mo = p.M / p.W, mb_per_owner = Mo / TP_BM;
-    const int j = blockIdx.x;
-    int tml, tn;
-    tc::tile_coords(j, mb_per_owner, (p.N + BN - 1) / BN, TP_GROUP_M, tml, tn);
-    const int tiles_n = (p.N + BN - 1) / BN;
-    const int tpo = mb_per_owner * tiles_n;
-    const uint32_t epoch = p.state[0] + 1;
-    const int par = epoch & 1;
-    const uint8_t *me = reinterpret_cast<const uint8_t *>(p.peer[p.rank]);
-    if (threadIdx.x == 0) {
-        int good = 1;
-        for (int s = 0; s < p.W && good; ++s)
-            good = tp_wait_flag(reinterpret_cast<const volatile uint32_t *>(me + (par ? p.off_flags[1] : p.off_flags[0])) + size_t(s) * tpo + j,
-                                epoch, p.timeout_ns);
-        if (!good) atomicExch(p.error, 1);
-        ok = good;
-    }
-    __syncthreads();
-    const __nv_bfloat16 *recv = reinterpret_cast<const __nv_bfloat16 *>(me + (par ? p.off_data[1] : p.off_data[0]));
-    const int cols = min(BN, p.N - tn * BN);
-    for (int e = threadIdx.x * 8; e < TP_BM * BN; e += blockDim.x * 8) {
-        const int r = e / BN, c = e % BN;
-        if (c >= cols) continue;
-        const int row = tml * TP_BM + r, col = tn * BN + c;
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (ok) {
-            for (int s = 0; s < p.W; ++s) {
-                const uint4 v = __ldcv(reinterpret_cast<const uint4 *>(recv + (size_t(s) * Mo + row) * p.N + col));
-                const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&v);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float2 f = __bfloat1622float2(v2[q]);
-                    acc[2 * q] += f.x;
-                    acc[2 * q + 1] += f.y;
-                }
-            }
-        }
-        if (p.residual) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(p.residual + size_t(row) * p.N + col);
-            const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&v);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float2 f = __bfloat1622float2(v2[q]);
-                acc[2 * q] += f.x;
-                acc[2 * q + 1] += f.y;
-            }
-        }
-        uint4 o;
-        __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) o2[q] = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
-        *reinterpret_cast<uint4 *>(p.out + size_t(row) * p.N + col) = o;
-    }
-    // the last tile of this call advances the epoch
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        last = atomicAdd(&p.state[1], 1u) == gridDim.x - 1;
-        if (last) {
-            p.state[1] = 0;
-            p.state[0] = epoch;
-        }
-    }
-}
-
-// MODE_AG producer: this rank's shard into every rank's gather buffer, one flag per 128-row block.
-__global__ void __launch_bounds__(256) ag_push_kernel(TpParams p) {
-    const int Mo = p.M / p.W, blocks = Mo / TP_BM;
-    const uint32_t epoch = p.state[0] + 1;
-    const int par = epoch & 1;
-    // grid: (blocks, W destinations)
-    const int blk = blockIdx.x, d = (p.rank + blockIdx.y) % p.W;
-    uint8_t *dst_base = reinterpret_cast<uint8_t *>(p.peer[d]);
-    const size_t row0 = size_t(p.rank) * Mo + size_t(blk) * TP_BM;
-    const uint4 *src = reinterpret_cast<const uint4 *>(p.a_shard + size_t(blk) * TP_BM * p.K);
-    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(dst_base + (par ? p.off_data[1] : p.off_data[0])) + row0 * p.K);
-    const size_t n = size_t(TP_BM) * p.K / 8;
-    for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<volatile uint32_t *>(dst_base + (par ? p.off_flags[1] : p.off_flags[0])) + row0 / TP_BM, epoch);
     }
 }
 
@@ -378,8 +390,8 @@ bool tp_map(CUtensorMap *map, const void *ptr, int rows, int cols, int box_rows)
 }
 
 template <int BN, int MODE>
-int tp_launch(const CUtensorMap &ma0, const CUtensorMap &ma1, const CUtensorMap &mb, const TpParams &p,
-              cudaStream_t stream) {
+int tp_launch(const CUtensorMap &ma0, const CUtensorMap &ma1, const CUtensorMap &mb, const CUtensorMap &ml,
+              const TpParams &p, cudaStream_t stream) {
     const int smem = TpSmem<BN>::BYTES;
     static bool attr = false;
     if (!attr) {
@@ -392,7 +404,8 @@ int tp_launch(const CUtensorMap &ma0, const CUtensorMap &ma1, const CUtensorMap 
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = (p.M / TP_BM) * ((p.N + BN - 1) / BN);
-    gemm_tp_kernel<BN, MODE><<<tiles < sms ? tiles : sms, TP_THREADS, smem, stream>>>(ma0, ma1, mb, p);
+    gemm_tp_kernel<BN, MODE><<<tiles < sms ? tiles : sms, MODE == 1 ? TP_THREADS_AG : TP_THREADS, smem, stream>>>(
+        ma0, ma1, mb, ml, p);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -408,13 +421,9 @@ int xt_gemm_rs(const void *a, const void *b, const TpParams *pp, cudaStream_t st
     CUtensorMap ma, mb;
     const int bn = p.N >= 2048 ? 256 : 128;
     if (!tp_map(&ma, a, p.M, p.K, TP_BM) || !tp_map(&mb, b, p.N, p.K, bn)) return -3;
-    int rc = bn == 256 ? tp_launch<256, 0>(ma, ma, mb, p, stream) : tp_launch<128, 0>(ma, ma, mb, p, stream);
+    int rc = bn == 256 ? tp_launch<256, 0>(ma, ma, mb, ma, p, stream) : tp_launch<128, 0>(ma, ma, mb, ma, p, stream);
     if (rc) return rc;
-    const int tpo = (p.M / p.W / TP_BM) * ((p.N + bn - 1) / bn);
-    if (bn == 256)
-        rs_reduce_kernel<256><<<tpo, 256, 0, stream>>>(p);
-    else
-        rs_reduce_kernel<128><<<tpo, 256, 0, stream>>>(p);
+    tp_bump_epoch<<<1, 1, 0, stream>>>(p.state);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -425,16 +434,13 @@ int xt_ag_gemm(const void *b, const void *local_base, const TpParams *pp, cudaSt
     TpParams p = *pp;
     if (p.W < 1 || p.M % (TP_BM * p.W) || p.K % 8 || p.N % 8 || !local_base) return -2;
     const int Mo = p.M / p.W;
-    dim3 pg(Mo / TP_BM, p.W);
-    ag_push_kernel<<<pg, 256, 0, stream>>>(p);
-    if (cudaGetLastError() != cudaSuccess) return -1;
-    CUtensorMap ma0, ma1, mb;
+    CUtensorMap ma0, ma1, mb, ml;
     const int bn = p.N >= 2048 ? 256 : 128;
     const uint8_t *base = static_cast<const uint8_t *>(local_base);
     if (!tp_map(&ma0, base + p.off_data[0], p.M, p.K, TP_BM) || !tp_map(&ma1, base + p.off_data[1], p.M, p.K, TP_BM) ||
-        !tp_map(&mb, b, p.N, p.K, bn))
+        !tp_map(&mb, b, p.N, p.K, bn) || !tp_map(&ml, p.a_shard, Mo, p.K, TP_BM))
         return -3;
-    int rc = bn == 256 ? tp_launch<256, 1>(ma0, ma1, mb, p, stream) : tp_launch<128, 1>(ma0, ma1, mb, p, stream);
+    int rc = bn == 256 ? tp_launch<256, 1>(ma0, ma1, mb, ml, p, stream) : tp_launch<128, 1>(ma0, ma1, mb, ml, p, stream);
     if (rc) return rc;
     tp_bump_epoch<<<1, 1, 0, stream>>>(p.state);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;

@@ -74,6 +74,10 @@ def main(argv=None):
         res[name] = dict(fused_us=round(tf, 1), nccl_us=round(tb, 1), speedup=round(tb / tf, 3),
                          roofline_us=round(target, 1), of_roofline=round(target / tf, 3),
                          tflops=round(fl / tf / 1e6, 1))
+    # the same GEMMs alone (this rank's shard, no collective), for the overhead of the fused exchange
+    res['gemm_rs']['gemm_only_us'] = round(timed(lambda: ops.gemm(act, w2)), 1)
+    xfull = torch.cat([x] * W)
+    res['ag_gemm']['gemm_only_us'] = round(timed(lambda: ops.gemm(xfull, w13)), 1)
     comm.check()
     if r == 0:
         print(json.dumps(res), flush=True)
