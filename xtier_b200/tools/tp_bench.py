@@ -26,6 +26,7 @@ def main(argv=None):
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--peak-tflops', type=float, default=1590.0)
     ap.add_argument('--link-gbs', type=float, default=770.0)
+    ap.add_argument('--iters-only', action='store_true', help='fused ops only (no NCCL baseline): a single GPU')
     a = ap.parse_args(argv)
     from .. import ops
     from ..parallel import dist as xdist
@@ -69,9 +70,10 @@ def main(argv=None):
     for name, fused, base, fl, link in (
             ('gemm_rs', lambda: comm.gemm_rs(act, w2, out=o_rs), lambda: nccl_gemm_rs(act, w2), fl_rs, link_rs),
             ('ag_gemm', lambda: comm.ag_gemm(x, w13, out=o_ag), lambda: nccl_ag_gemm(x, w13), fl_ag, link_ag)):
-        tf, tb = timed(fused), timed(base)
+        tf = timed(fused)
+        tb = timed(base) if (W > 1 and not a.iters_only) else float('nan')
         target = max(fl / (a.peak_tflops * 1e12), link / (a.link_gbs * 1e9)) * 1e6
-        res[name] = dict(fused_us=round(tf, 1), nccl_us=round(tb, 1), speedup=round(tb / tf, 3),
+        res[name] = dict(fused_us=round(tf, 1), nccl_us=round(tb, 1) if tb == tb else None, speedup=round(tb / tf, 3) if tb == tb else None,
                          roofline_us=round(target, 1), of_roofline=round(target / tf, 3),
                          tflops=round(fl / tf / 1e6, 1))
     # the same GEMMs alone (this rank's shard, no collective), for the overhead of the fused exchange
