@@ -440,6 +440,11 @@ void topk_rows(const Tensor &scores, int64_t K, const Tensor &out) {
 
 }  // namespace
 
+// cudaLaunchHostFunc on a raw stream handle (graph capture records a host node); used by the row tables' lookup
+extern "C" int xt_launch_host_fn(void *stream, void (*fn)(void *), void *arg) {
+    return cudaLaunchHostFunc(static_cast<cudaStream_t>(stream), fn, arg) == cudaSuccess ? 0 : -1;
+}
+
 TORCH_LIBRARY(xtier, m) {
     m.def("add_rmsnorm(Tensor x, Tensor(a!)? residual, Tensor w, Tensor(b!) out, float eps) -> ()");
     m.def("qk_norm_rope_kv(Tensor qkv, Tensor? q_norm, Tensor? k_norm, Tensor pos, Tensor batch, Tensor(a!) q, "

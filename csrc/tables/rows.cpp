@@ -372,4 +372,22 @@ void xt_rows_close(void *h) {
 
 const char *xt_rows_error(void) { return g_err.c_str(); }
 
+// Graph-capturable lookup: a CUDA host-function node calls this with a context the caller keeps alive. The ids were
+// copied into pinned host memory by the node before it; the rows land in pinned host memory for the copy node after
+// it. A failed lookup leaves zero rows and sets ctx->error (the caller checks it between replays); nothing here calls
+// CUDA, as a host node must not.
+struct XtRowsGraphCtx {
+    void *store;
+    const long long *ids;
+    int n;
+    void *rows;
+    void *scales;
+    volatile int error;
+};
+
+void xt_rows_host_fn(void *arg) {
+    auto *c = static_cast<XtRowsGraphCtx *>(arg);
+    if (xt_rows_lookup(c->store, c->ids, c->n, c->rows, c->scales) != 0) c->error = 1;
+}
+
 }  // extern "C"

@@ -42,3 +42,23 @@ def test_tp_range_and_bad_id(table):
     with pytest.raises(IndexError, match='outside'):
         st.lookup(np.array([1000]))
     st.close()
+
+
+def test_host_function_callback(table):
+    """The graph lookup's host node, called directly: rows for the context's ids, error word on a bad id."""
+    import ctypes as C
+    from xtier_b200.tables import lib
+    from xtier_b200.tables.lookup import _Ctx
+    data, scales, segs = table
+    st = RowStore(segs, 96, 3, io_threads=2, cache_rows=16)
+    ids = np.array([3, 999, 400, 3], dtype=np.int64)
+    rows = np.zeros((4, 96), dtype=np.uint8)
+    sc = np.zeros((4, 3), dtype=np.uint8)
+    ctx = _Ctx(st.handle, ids.ctypes.data, 4, rows.ctypes.data, sc.ctypes.data, 0)
+    fn = C.CFUNCTYPE(None, C.c_void_p)(C.cast(lib().xt_rows_host_fn, C.c_void_p).value)
+    fn(C.addressof(ctx))
+    assert ctx.error == 0 and np.array_equal(rows, data[ids]) and np.array_equal(sc, scales[ids])
+    ids[1] = 5000
+    fn(C.addressof(ctx))
+    assert ctx.error == 1
+    st.close()
