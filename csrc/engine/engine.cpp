@@ -288,6 +288,7 @@ struct Plan {
     Pool *pool;
     std::vector<Shard> shards;
     std::vector<float> g13, g2;           // per slot (+shared): gate, up / down multipliers
+    std::vector<float> eg13, eg2;         // per routed expert (optional): copied into a slot when the expert lands
     std::vector<int> slot_of, expert_of;  // expert -> slot, slot -> expert
     std::vector<int> pins;
     std::atomic<int> busy{0};
@@ -494,7 +495,7 @@ struct PrepJob : Job {   // prepares the token vectors, spread over the workers
 
 static int cold_ensure(Plan *p, const std::vector<int> &need_experts, bool decode);
 
-static int build_groups(Plan *p, int m, int k, const int32_t *ids, const float *w, bool decode) {
+static int build_groups(Plan *p, int m, int k, const int32_t *ids, const float *w, bool decode, bool shared_too) {
     struct Route {
         int e, t;
         float w;
@@ -563,7 +564,7 @@ static int build_groups(Plan *p, int m, int k, const int32_t *ids, const float *
         }
         p->groups.push_back(g);
     }
-    for (int s = 0; s < p->shared; ++s)
+    for (int s = 0; s < (shared_too ? p->shared : 0); ++s)
         for (int t0 = 0; t0 < m; t0 += MAX_TOK) {
             Group g;
             g.slot = p->slots + s;
@@ -580,18 +581,14 @@ static int build_groups(Plan *p, int m, int k, const int32_t *ids, const float *
     return int(p->groups.size());
 }
 
-static int forward_impl(Plan *p, int m, int k, const uint16_t *x, const int32_t *ids, const float *w, float *y,
-                        bool decode, bool probe) {
-    if (!p || m < 1 || k < 0 || (k > 0 && (!ids || !w)) || !x || (!y && !probe)) {
-        set_error("engine: bad forward arguments");
-        return -1;
-    }
+static int forward_once(Plan *p, int m, int k, const uint16_t *x, const int32_t *ids, const float *w, float *y,
+                        bool decode, bool probe, bool shared_too) {
     if (p->busy.exchange(1)) {
         set_error("engine: concurrent forward on one plan");
         return -1;
     }
     std::lock_guard<std::mutex> lk(p->pool->use);
-    int ng = build_groups(p, m, k, ids, w, decode);
+    int ng = build_groups(p, m, k, ids, w, decode, shared_too);
     if (ng < 0) {
         p->busy.store(0);
         return -1;
@@ -626,6 +623,48 @@ static int forward_impl(Plan *p, int m, int k, const uint16_t *x, const int32_t 
     return ng;
 }
 
+// A call that needs more distinct experts than a cold-backed plan has unpinned RAM slots runs in batches of experts
+// (ascending ids; the shared experts with the first batch), the batches' outputs summed in batch order.
+static int forward_impl(Plan *p, int m, int k, const uint16_t *x, const int32_t *ids, const float *w, float *y,
+                        bool decode, bool probe) {
+    if (!p || m < 1 || k < 0 || (k > 0 && (!ids || !w)) || !x || (!y && !probe)) {
+        set_error("engine: bad forward arguments");
+        return -1;
+    }
+    if (p->slots >= p->E || k == 0) return forward_once(p, m, k, x, ids, w, y, decode, probe, true);
+    std::vector<char> seen(p->E, 0);
+    std::vector<int> need;
+    for (size_t i = 0; i < size_t(m) * k; ++i) {
+        const int e = ids[i];
+        if (e >= 0 && e < p->E && !seen[e]) {
+            seen[e] = 1;
+            need.push_back(e);
+        }
+    }
+    int cap = 0;
+    for (int s = 0; s < p->slots; ++s) cap += __atomic_load_n(&p->pins[s], __ATOMIC_ACQUIRE) <= 0;
+    if (int(need.size()) <= cap) return forward_once(p, m, k, x, ids, w, y, decode, probe, true);
+    if (cap < 1) {
+        set_error("engine: every RAM slot is pinned; no room for the call's experts");
+        return -1;
+    }
+    std::sort(need.begin(), need.end());
+    std::vector<int32_t> bids(size_t(m) * k);
+    std::vector<float> part(probe ? 0 : size_t(m) * p->H);
+    int total = 0;
+    for (size_t b0 = 0; b0 < need.size(); b0 += size_t(cap)) {
+        const int lo = need[b0], hi = need[std::min(need.size(), b0 + size_t(cap)) - 1];
+        for (size_t i = 0; i < bids.size(); ++i) bids[i] = (ids[i] >= lo && ids[i] <= hi) ? ids[i] : -1;
+        float *dst = (b0 == 0 || probe) ? y : part.data();
+        const int ng = forward_once(p, m, k, x, bids.data(), w, dst, decode, probe, b0 == 0);
+        if (ng < 0) return -1;
+        total += ng;
+        if (b0 > 0 && !probe)
+            for (size_t i = 0; i < part.size(); ++i) y[i] += part[i];
+    }
+    return total;
+}
+
 // ------------------------------------------------------------------------------------------------ cold experts
 }  // namespace xt
 
@@ -633,6 +672,14 @@ extern "C" int xt_cold_read(void *store, int jobs, const int *files, const long 
                             const size_t *sizes, int n);
 
 namespace xt {
+
+// The slot's global scales follow the expert that now occupies it (when per-expert scales were given).
+static void slot_scales(Plan *p, int slot, int e) {
+    if (p->eg13.empty()) return;
+    p->g13[2 * size_t(slot)] = p->eg13[2 * size_t(e)];
+    p->g13[2 * size_t(slot) + 1] = p->eg13[2 * size_t(e) + 1];
+    p->g2[slot] = p->eg2[e];
+}
 
 static int cold_ensure(Plan *p, const std::vector<int> &need, bool decode) {
     for (auto &s : p->score) s *= p->decay;
@@ -690,6 +737,7 @@ static int cold_ensure(Plan *p, const std::vector<int> &need, bool decode) {
         if (old >= 0) p->slot_of[old] = -1;
         p->expert_of[victim] = e;
         p->slot_of[e] = victim;
+        slot_scales(p, victim, e);
         p->cold_stats[1] += 1;
     }
     p->cold_stats[2] += (now_us() - t0) * 1e-6;
@@ -856,7 +904,19 @@ int xt_engine_place(void *plan, int expert, int slot) {
     if (prev >= 0) p->expert_of[prev] = -1;
     p->expert_of[slot] = expert;
     p->slot_of[expert] = slot;
+    slot_scales(p, slot, expert);
     return old;
+}
+
+int xt_engine_expert_scales(void *plan, const float *g13, const float *g2) {
+    Plan *p = static_cast<Plan *>(plan);
+    if (!p || !g13 || !g2) return -1;
+    if (p->busy.load()) return -3;
+    p->eg13.assign(g13, g13 + size_t(p->E) * 2);
+    p->eg2.assign(g2, g2 + p->E);
+    for (int s = 0; s < p->slots; ++s)
+        if (p->expert_of[s] >= 0) slot_scales(p, s, p->expert_of[s]);
+    return 0;
 }
 
 int xt_engine_slot_pin(void *plan, int expert) {

@@ -50,6 +50,9 @@ int xt_engine_slot_table(void *plan, int32_t *table);
 // Mark `expert` as held by `slot` after its weights were written there. Returns the previous expert of the slot or -1;
 // -2 bad arguments, -3 a forward in progress.
 int xt_engine_place(void *plan, int expert, int slot);
+// Global scales of every routed expert (g13 [E, 2], g2 [E]); from then on a slot takes the scales of the expert placed
+// or read into it (cold reads, place). Returns 0, -1 on bad arguments, -3 while a forward runs.
+int xt_engine_expert_scales(void *plan, const float *g13, const float *g2);
 // Pin the slot holding `expert` against eviction while another thread reads it (-1: not in RAM).
 int xt_engine_slot_pin(void *plan, int expert);
 void xt_engine_slot_unpin(void *plan, int slot);

@@ -1,0 +1,171 @@
+"""Cold experts on drives: record layout against the engine's slots, manifest reuse and CRC checks, an engine whose
+misses come from the store (per-expert global scales follow the expert into its slot), start-up fill from the store,
+relayout to other drives / weights / node counts, and punching the checkpoint's copy (compare, marker, restore)."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from xtier_b200 import checkpoint, formats
+from xtier_b200.cache import cold
+from xtier_b200.engine import CpuEngine
+
+H, I, E = 256, 128, 8
+
+
+def _experts(fmt=formats.NVFP4, seed=0):
+    ew = formats.random_experts(E, H, I, fmt, seed=seed)
+    # distinct global scales per expert, so a slot holding the wrong expert's scales shows up
+    ew.g13 = (torch.rand(E, 2, generator=torch.Generator().manual_seed(seed)) + 0.5) * ew.g13.float()
+    ew.g2 = (torch.rand(E, generator=torch.Generator().manual_seed(seed + 1)) + 0.5) * ew.g2.float()
+    return ew
+
+
+def _routes(m, k, seed):
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(m)]).int()
+    w = torch.rand(m, k, generator=g)
+    x = torch.randn(m, H, generator=g).bfloat16()
+    return x, ids, w
+
+
+@pytest.mark.parametrize('fmt', [formats.NVFP4, formats.MXFP4])
+def test_record_layout_matches_engine_slots(fmt):
+    ew = _experts(fmt)
+    eng = CpuEngine(ew, threads=2)
+    N = eng.nodes()
+    sizes = [eng.slot_pieces(0, n)[1] for n in range(N)]
+    for n in range(N):
+        assert sizes[n] == cold.piece_bytes(H, I, fmt, N)
+        ptrs, sz = eng.slot_pieces(3, n)
+        pieces = cold.shard_pieces(ew, 3, n, N)
+        for p, q, b in zip(ptrs, pieces, sz):   # the engine slot holds exactly these bytes
+            got = np.ctypeslib.as_array((np.ctypeslib.ctypes.c_uint8 * b).from_address(p))
+            assert np.array_equal(got, q)
+    eng.close()
+
+
+def test_manifest_reuse_crc_and_source(tmp_path):
+    ew = _experts()
+    d = tmp_path / 'd0'
+    pool = cold.ColdPool([d])
+    src = [['layer0.safetensors', 123, 456]]
+    assert pool.ensure_layer(0, ew, 1, src) is False        # written
+    assert pool.ensure_layer(0, ew, 1, src) is True         # reused
+    pool.close()
+    pool = cold.ColdPool([d])                                # restart: the manifest is read back
+    assert pool.layer_ok(0, H, I, ew.fmt, 1, E, src)
+    assert not pool.layer_ok(0, H, I, ew.fmt, 1, E, [['layer0.safetensors', 123, 999]])   # source changed
+    # corrupt the last 4 KiB of record 5
+    ent = pool.entry(0)
+    dr, off = ent['loc'][5]
+    with open(pool.files[dr], 'r+b') as f:
+        f.seek(off + ent['record'] - 10)
+        f.write(b'\xff' * 4)
+    assert pool.check_layer(0) == [5]
+    assert pool.ensure_layer(0, ew, 1, src) is False        # rewritten
+    assert pool.check_layer(0) == []
+    back = pool.load_layer(0)
+    for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+        assert torch.equal(getattr(back, f), getattr(ew, f).float() if f in ('g13', 'g2') else getattr(ew, f)), f
+    pool.close()
+
+
+@pytest.mark.parametrize('fmt', [formats.NVFP4, formats.MXFP4])
+def test_engine_reads_misses_from_the_store(tmp_path, fmt):
+    ew = _experts(fmt, seed=4)
+    full = CpuEngine(ew, threads=2)
+    pool = cold.ColdPool([tmp_path / 'a', tmp_path / 'b'], parts='3:1')
+    eng = cold.cold_engine(0, ew, pool, 0.5, popularity=torch.arange(E, 0, -1).float(), gpu_hot=[0], threads=2)
+    assert eng.shape()['slots'] == E // 2
+    drives = [dd for dd, _ in pool.entry(0)['loc']]
+    assert drives.count(0) == 3 * drives.count(1)            # dealt 3:1
+    for i in range(6):                                        # different expert sets: misses and evictions
+        x, ids, w = _routes(1, 4, seed=10 + i)
+        assert torch.equal(eng.forward(x, ids, w), full.forward(x, ids, w)), i
+    for i in range(3):     # more distinct experts than RAM slots: batches of experts, summed in batch order
+        x, ids, w = _routes(4, 4, seed=20 + i)
+        want = full.forward(x, ids, w)
+        got = eng.forward(x, ids, w)
+        assert torch.allclose(got, want, rtol=1e-5, atol=1e-6), i
+        ref = formats.reference_moe(x, ids, w, ew)
+        assert torch.allclose(got, ref, rtol=2e-2, atol=2e-3)
+    st = eng.cold_stats()
+    assert st['reads'] > 0 and pool.stats()['bytes_read'] > 0
+    eng.close()
+    full.close()
+    pool.close()
+
+
+def test_fill_engine_from_store(tmp_path):
+    ew = _experts(seed=7)
+    pool = cold.ColdPool([tmp_path / 'a'])
+    eng0 = CpuEngine(ew, threads=2)
+    N = eng0.nodes()
+    pool.write_layer(3, ew, N)
+    resident = [6, 2, 5, -1]
+    eng = CpuEngine(ew, threads=2, slots=4, fill=False)      # no expert bytes from the checkpoint
+    pool.fill_engine(eng, 3, resident)
+    pool.attach(eng, 3)
+    assert list(eng.slot_table()[[6, 2, 5]]) == [0, 1, 2]
+    x, ids, w = _routes(2, 3, seed=1)
+    assert torch.equal(eng.forward(x, ids, w), eng0.forward(x, ids, w))
+    eng.close()
+    eng0.close()
+    pool.close()
+
+
+def test_relayout_to_other_drives_and_nodes(tmp_path):
+    from xtier_b200.tools.cold_relayout import relayout
+    ew = _experts(formats.MXFP4, seed=2)
+    src = cold.ColdPool([tmp_path / 's'])
+    src.write_layer(0, ew, 1, [['f', 1, 2]])
+    src.write_layer(1, _experts(formats.MXFP4, seed=3), 1)
+    src.close()
+    dst_dirs = f'{tmp_path / "x"},{tmp_path / "y"}'
+    rep = relayout(str(tmp_path / 's'), dst_dirs, parts='1:1', nodes=2, log=lambda s: None)
+    assert sorted(rep) == [0, 1]
+    dst = cold.ColdPool(dst_dirs)
+    assert dst.entry(0)['shape'][3] == 2 and dst.entry(0)['source'] == [['f', 1, 2]]
+    back = dst.load_layer(0)
+    assert torch.equal(back.w13, ew.w13) and torch.equal(back.s2, ew.s2) and torch.equal(back.g2, ew.g2.float())
+    dst.close()
+    with pytest.raises(SystemExit):        # a store onto itself is refused
+        relayout(str(tmp_path / 's'), str(tmp_path / 's'), log=lambda s: None)
+
+
+def test_punch_compare_marker_restore(tmp_path):
+    from xtier_b200.tools import cold_punch
+    ew = _experts(seed=9)
+    ck = tmp_path / 'model'
+    ck.mkdir()
+    path = ck / 'layer0.safetensors'
+    checkpoint.save_experts(path, ew)
+    original = path.read_bytes()
+    mtime = os.stat(path).st_mtime_ns
+    pool = cold.ColdPool([tmp_path / 'c'])
+    got = cold.open_layer(pool, 0, path, nodes=1)
+    assert torch.equal(got.w13, ew.w13)
+    assert cold_punch.compare(pool, pool.ranges()) == []
+    try:
+        cold_punch.punch(pool, pool.ranges(), log=lambda s: None)
+    except OSError as e:        # a filesystem without hole punching
+        pytest.skip(f'fallocate punch unsupported here: {e}')
+    assert (ck / checkpoint.MARKER).exists() and os.stat(path).st_mtime_ns == mtime
+    assert path.stat().st_size == len(original)
+    with pytest.raises(RuntimeError):
+        checkpoint.load_experts(path)
+    ranges = json.loads(pool.ranges_path.read_text())['0']['tensors']
+    data = path.read_bytes()
+    off, stride = ranges['w13']
+    lo = (off + 4095) // 4096 * 4096
+    assert data[lo:lo + 4096] == bytes(4096)                 # the tensor's inner blocks are gone
+    assert data[:off] == original[:off]                      # the header and what precedes are untouched
+    rebuilt = cold.open_layer(pool, 0, path, nodes=1)        # from the store alone
+    assert torch.equal(rebuilt.w2, ew.w2)
+    cold_punch.restore(pool, pool.ranges(), log=lambda s: None)
+    assert path.read_bytes() == original and not (ck / checkpoint.MARKER).exists()
+    assert os.stat(path).st_mtime_ns == mtime
+    pool.close()

@@ -58,6 +58,35 @@ def read_header(path) -> tuple[dict, int]:
         return json.loads(f.read(n)), 8 + n
 
 
+MARKER = 'XTIER-COLD-ONLY'
+
+
+def expert_ranges(path, prefix: str = 'experts.') -> dict:
+    """Where each expert tensor of a layer file sits: {name: [absolute byte offset, bytes per expert]} for the four
+    tensors a cold record holds (codes and block scales; the global scales stay in the file)."""
+    header, data0 = read_header(path)
+    out = {}
+    for n in ('w13', 's13', 'w2', 's2'):
+        h = header[prefix + n]
+        a, b = h['data_offsets']
+        out[n] = [data0 + a, (b - a) // h['shape'][0]]
+    return out
+
+
+def cold_only(path) -> bool:
+    """True when `path` is listed in the punch marker beside it: its expert tensors live only in the cold store."""
+    import os
+    from pathlib import Path
+    m = Path(path).parent / MARKER
+    if not m.exists():
+        return False
+    try:
+        files = json.loads(m.read_text()).get('files', {})
+    except ValueError:
+        return True     # an unreadable marker: refuse rather than read zeros
+    return Path(path).name in files or str(path) in files
+
+
 def _aligned(nbytes: int) -> np.ndarray:
     raw = np.empty(nbytes + 4096, dtype=np.uint8)
     o = (-raw.ctypes.data) % 4096
@@ -66,6 +95,10 @@ def _aligned(nbytes: int) -> np.ndarray:
 
 def load_experts(path, prefix: str = 'experts.', direct: bool | None = None, threads: int = 8) -> ExpertWeights:
     """direct=None follows XTIER_FAST_LOAD."""
+    if cold_only(path):
+        raise RuntimeError(f'{path}: its expert tensors were punched out (marker {MARKER}); load this layer from the '
+                           'cold store (ColdPool.load_layer / fill_engine) or restore it with tools/cold_punch.py '
+                           '--restore')
     if direct is None:
         from . import config
         direct = bool(config.get('XTIER_FAST_LOAD'))

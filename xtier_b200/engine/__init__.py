@@ -50,6 +50,7 @@ def lib():
         L.xt_engine_tail_stats.argtypes = [_P, _P]
         L.xt_engine_slot_table.argtypes = [_P, _P]
         L.xt_engine_place.argtypes = [_P, _I, _I]
+        L.xt_engine_expert_scales.argtypes = [_P, _P, _P]
         L.xt_engine_slot_pin.argtypes = [_P, _I]
         L.xt_engine_slot_unpin.argtypes = [_P, _I]
         L.xt_engine_slot_pieces.argtypes = [_P, _I, _I, _P, _P]
@@ -182,6 +183,16 @@ class CpuEngine:
 
     def place(self, expert: int, slot: int) -> int:
         return lib().xt_engine_place(self.plan, expert, slot)
+
+    def set_expert_scales(self, g13: torch.Tensor, g2: torch.Tensor):
+        """Global scales of every routed expert (g13 [E, 2], g2 [E]); a slot then takes the scales of whichever expert
+        is placed or read into it (needed with a cold store, whose records hold only codes and block scales)."""
+        a = g13.detach().float().cpu().contiguous()
+        b = g2.detach().float().cpu().contiguous()
+        if a.numel() != 2 * self.E or b.numel() != self.E:
+            raise ValueError('expert scales: g13 [E, 2] and g2 [E] expected')
+        if lib().xt_engine_expert_scales(self.plan, _ptr(a), _ptr(b)) != 0:
+            raise RuntimeError('xtier_b200 engine: expert scales refused (a forward is running?)')
 
     def nodes(self) -> int:
         return lib().xt_engine_nodes(self.plan)

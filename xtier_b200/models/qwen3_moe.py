@@ -94,6 +94,13 @@ class Qwen3MoeModel:
         n_hot = cfg.experts if hot_fraction >= 1.0 else max(1, int(round(hot_fraction * cfg.experts)))
         self.mailbox = mailbox
         self.engines = []
+        self.cold = None
+        if config.get('XTIER_COLD') and n_hot < cfg.experts:
+            from ..cache.cold import ColdPool
+            if not config.get('XTIER_COLD_DIR'):
+                raise ValueError('XTIER_COLD=1 needs XTIER_COLD_DIR (one directory per drive, comma separated)')
+            self.cold = ColdPool(config.get('XTIER_COLD_DIR'), parts=config.get('XTIER_COLD_PARTS') or None,
+                                 threads=config.get('XTIER_COLD_THREADS'))
         # router logits are N(0, (std * sqrt(H))^2) for RMS-normalized hidden states
         self.zipf_tau = zipf_temperature(cfg.experts, cfg.top_k, cfg.zipf_s, cfg.std * H ** 0.5)
         for li in range(cfg.layers):
@@ -123,7 +130,12 @@ class Qwen3MoeModel:
             if hot is not None and len(hot) < cfg.experts:
                 from ..engine import CpuEngine
                 host = ew.to('cpu')
-                engine = CpuEngine(host, threads=engine_threads)
+                if self.cold is not None:   # RAM slots for part of the experts, the rest read from the drives
+                    from ..cache.cold import cold_engine
+                    engine = cold_engine(li, host, self.cold, config.get('XTIER_COLD_FRACTION'), bias.cpu(), hot,
+                                         threads=engine_threads)
+                else:
+                    engine = CpuEngine(host, threads=engine_threads)
                 self.engines.append(engine)
             L['moe'] = TieredMoE(li, router, ew, cfg.top_k, hot=hot, router_bias=bias, mailbox=mailbox,
                                  engine=engine, device=dev, host_experts=host)
