@@ -43,3 +43,27 @@ def test_tiny_qwen3_grouped_prefill_matches_reference(cuda_ops, monkeypatch):
     ref = model.reference_logits(prompt)
     rel = float((lp.float() - ref.float()).norm() / ref.float().norm())
     assert rel < 3e-2, rel
+
+
+def test_grouped_prefill_after_swaps(cuda_ops, monkeypatch):
+    """After adaptive swaps move experts between the GPU slots and the CPU side, a grouped prefill still covers every
+    route: a swapped-out expert takes over the staging index of the one swapped in."""
+    from xtier_b200.models.qwen3_moe import Qwen3MoeConfig, Qwen3MoeModel
+    monkeypatch.setenv('XTIER_GPU_PREFILL_MIN', '16')
+    cfg = Qwen3MoeConfig.tiny(std=0.05, hidden=256, inter=128)
+    model = Qwen3MoeModel(cfg, device='cuda', seed=5, hot_fraction=0.5, synthetic_experts=False, engine_threads=2)
+    prompt = torch.randint(0, cfg.vocab, (40,), generator=torch.Generator().manual_seed(4)).cuda()
+    st = model.alloc_state(1, 64)
+    model.prefill(st, prompt)            # builds the staging copies
+    for L in model.layers:
+        moe = L['moe']
+        hot = moe.resident()
+        cold = [e for e in range(moe.E) if e not in hot]
+        moe.swap(cold[0], hot[0])
+        moe.swap(cold[1], hot[1])
+    torch.cuda.synchronize()
+    st = model.alloc_state(1, 64)
+    _, lp = model.prefill(st, prompt, return_logits=True)
+    ref = model.reference_logits(prompt)
+    rel = float((lp.float() - ref.float()).norm() / ref.float().norm())
+    assert rel < 3e-2, rel

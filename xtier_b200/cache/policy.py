@@ -36,13 +36,18 @@ class AdaptivePolicy:
         self.rounds = 0
         self.total_swaps = 0
 
-    def plan_layer(self, layer, counts: np.ndarray, budget: int) -> list[tuple[int, int]]:
-        """(incoming, victim) pairs for one layer, best gain first."""
+    def plan_layer(self, layer, counts: np.ndarray, budget: int) -> list[tuple[int, int | None]]:
+        """(incoming, victim) pairs for one layer, best gain first; victim None: an empty elastic slot takes it."""
         resident = list(layer.resident())
         res_set = set(resident)
         cold = [e for e in np.argsort(-counts) if e not in res_set and counts[e] > 0]
-        victims = sorted(resident, key=lambda e: counts[e])
         out = []
+        el = getattr(layer, 'elastic', None)
+        free = 0 if el is None else el.mapped - len(el.occupants())
+        while cold and free > 0 and len(out) < budget:
+            out.append((int(cold.pop(0)), None))
+            free -= 1
+        victims = sorted(resident, key=lambda e: counts[e])
         for inc, vic in zip(cold, victims):
             if len(out) >= budget:
                 break
@@ -66,7 +71,10 @@ class AdaptivePolicy:
                 break
             counts, _ = self.mailbox.layer_stats(layer.layer, layer.E)
             for inc, vic in self.plan_layer(layer, counts, budget):
-                layer.swap(inc, vic)
+                if vic is None:
+                    layer.fill(inc)
+                else:
+                    layer.swap(inc, vic)
                 done += 1
                 budget -= 1
         self.total_swaps += done

@@ -74,6 +74,7 @@ class TieredMoE:
         if self.mailbox is not None:
             self.mailbox.register(layer, engine)
         self.kk = self.k + self.n_shared
+        self.elastic = None       # ElasticSlots (cache/elastic.py) when the layer has extra slots
         self._alloc(max_tokens)
 
     def _alloc(self, m: int):
@@ -261,13 +262,40 @@ class TieredMoE:
             getattr(self.pool, f)[slot].copy_(getattr(self.host, f)[incoming], non_blocking=True)
         self.table[incoming] = slot
         self.table_host[incoming] = slot
+        if slot >= len(self.hot):   # an elastic slot: both experts keep their prefill staging index
+            self.elastic.occupant[slot - self.elastic.first] = incoming
+            return
         self.hot[slot] = incoming
+        if getattr(self, '_host_cold', None) is not None:
+            # the prefill staging covers exactly the non-resident experts: the victim takes the incoming expert's
+            # staging index (its pinned host bytes are replaced); an upload made before the swap is stale
+            idx = int(self._cold_index[incoming])
+            self._cold_index[victim] = idx
+            self._cold_index[incoming] = -1
+            for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+                getattr(self._host_cold, f)[idx].copy_(getattr(self.host, f)[victim])
+            self._pending = None
+
+    def fill(self, incoming: int):
+        """Puts a non-resident expert into an empty elastic slot (stream-ordered like `swap`). Experts in elastic
+        slots keep their prefill staging index, since their slot can be released again."""
+        slot = None if self.elastic is None else self.elastic.free_slot()
+        if slot is None or int(self.table_host[incoming]) >= 0:
+            raise ValueError(f'fill {incoming}: no free elastic slot or already resident')
+        for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+            getattr(self.pool, f)[slot].copy_(getattr(self.host, f)[incoming], non_blocking=True)
+        self.table[incoming] = slot
+        self.table_host[incoming] = slot
+        self.elastic.occupant[slot - self.elastic.first] = incoming
 
     def resident(self) -> list[int]:
-        return list(self.hot)
+        return list(self.hot) + (self.elastic.occupants() if self.elastic is not None else [])
 
     def gpu_bytes(self) -> int:
         if self.pool is None:
             return 0
-        return sum(getattr(self.pool, f).numel() * getattr(self.pool, f).element_size()
-                   for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'))
+        n = sum(getattr(self.pool, f).numel() * getattr(self.pool, f).element_size() for f in ('g13', 'g2'))
+        if self.elastic is not None:     # reserved address space is not memory: count what is mapped
+            return n + self.elastic.mapped_bytes()
+        return n + sum(getattr(self.pool, f).numel() * getattr(self.pool, f).element_size()
+                       for f in ('w13', 'w2', 's13', 's2'))

@@ -48,6 +48,15 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_CACHE_DECAY', 'float', 0.7, 'decay of the route counts per round'),
     _S('XTIER_CACHE_MIN_GAIN', 'float', 1.5, 'minimum count advantage of an incoming expert over its victim'),
     _S('XTIER_CACHE_LOG', 'int', 0, 'log the cache statistics every N policy rounds (0: off)'),
+    _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in VMM-backed memory that prefills take back'),
+    _S('XTIER_CACHE_ELASTIC_MAX', 'float', 2.0, 'address space per layer, as a multiple of its base hot slots'),
+    _S('XTIER_CACHE_ELASTIC_RESERVE_GIB', 'float', 2.0, 'free device memory never given to extra slots'),
+    _S('XTIER_CACHE_ELASTIC_CRITICAL_GIB', 'float', 1.0, 'free memory under this releases every extra slot'),
+    _S('XTIER_CACHE_ELASTIC_MARGIN', 'float', 1.25, 'factor on the predicted need of an allocating forward'),
+    _S('XTIER_CACHE_ELASTIC_IDLE', 'int', 32, 'decode steps after an allocating forward before slots grow again'),
+    _S('XTIER_CACHE_ELASTIC_CHECK', 'int', 16, 'decode steps between critical-memory checks'),
+    _S('XTIER_CACHE_ELASTIC_COOLDOWN_S', 'float', 600.0, 'no growth for this long after a critical release'),
+    _S('XTIER_CACHE_ELASTIC_EXTRAPOLATE', 'float', 2.0, 'how far a learnt need is scaled up to bound a larger one'),
     _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in memory only a prefill needs (VMM granules)'),
     _S('XTIER_CACHE_ELASTIC_RESERVE_GIB', 'float', 2.0, 'memory the elastic slots always leave free'),
     _S('XTIER_GPU2_SLOTS', 'str', '', 'hot slots on peer GPUs read over NVLink: N per layer, or auto'),

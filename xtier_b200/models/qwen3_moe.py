@@ -142,6 +142,16 @@ class Qwen3MoeModel:
             L['moe'].prepare_prefill()
             del ew
             self.layers.append(L)
+        # adaptive hot-slot swaps (AdaptivePolicy) and elastic extra slots (Governor), stepped between decode steps by
+        # the runtime (runtime/decode.py Generator)
+        self.policy = None
+        self.governor = None
+        if mailbox is not None and n_hot < cfg.experts:
+            from ..cache.policy import AdaptivePolicy
+            self.policy = AdaptivePolicy([L['moe'] for L in self.layers], mailbox)
+            if config.get('XTIER_CACHE_ELASTIC'):
+                from ..cache.elastic import Governor, install
+                self.governor = Governor(install(self))
 
     # ------------------------------------------------------------------ state
     def alloc_state(self, batch: int, max_len: int) -> dict:

@@ -14,8 +14,12 @@ import torch
 
 
 class Generator:
-    def __init__(self, model, batch: int = 1, max_len: int = 4096, use_graph: bool = True):
+    def __init__(self, model, batch: int = 1, max_len: int = 4096, use_graph: bool = True, policy=None,
+                 governor=None):
         self.model = model
+        # between decode steps: adaptive hot-slot swaps and the elastic cache's sizing (the model's, unless given)
+        self.policy = policy if policy is not None else getattr(model, 'policy', None)
+        self.governor = governor if governor is not None else getattr(model, 'governor', None)
         self.batch = batch
         self.max_len = max_len
         self.state = model.alloc_state(batch, max_len)
@@ -67,9 +71,19 @@ class Generator:
         """prompts [batch, T] token ids (host or device): fills the KV cache, sets the first decode input."""
         prompts = torch.as_tensor(prompts)
         first = []
-        for b in range(self.batch):
-            first.append(self.model.prefill(self.state, prompts[b].to(self.model.device), row=b))
         T = prompts.shape[1]
+        gov = self.governor
+        for b in range(self.batch):
+            ids = prompts[b].to(self.model.device)
+            if gov is None:
+                first.append(self.model.prefill(self.state, ids, row=b))
+                continue
+            gov.before_alloc(T, T)     # extra slots go back until the predicted need fits
+            torch.cuda.synchronize()
+            before = torch.cuda.memory_allocated()
+            torch.cuda.reset_peak_memory_stats()
+            first.append(gov.guarded(self.model.prefill, self.state, ids, row=b))
+            gov.after_forward(T, T, before, torch.cuda.max_memory_allocated())
         self.buf['tokens'].copy_(torch.cat(first).view(-1))
         self.buf['pos'].fill_(T)
         torch.cuda.synchronize()
@@ -85,8 +99,16 @@ class Generator:
         for i in range(max_new_tokens):
             self.decode_one()
             out[:, i] = self.host_next
+            self.between_steps()
         self.check()
         return out
+
+    def between_steps(self):
+        """Host work between two decode steps (no kernel of the step is in flight): swap rounds, elastic sizing."""
+        if self.policy is not None:
+            self.policy.step()
+        if self.governor is not None:
+            self.governor.after_decode()
 
     def decode_one(self):
         """End-to-end step: H2D copy of the input token from pinned memory, replay, D2H read of the next token."""
