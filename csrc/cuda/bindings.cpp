@@ -116,7 +116,7 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
                const std::optional<Tensor> &table, const std::optional<Tensor> &shared_slots, const Tensor &ids,
                const Tensor &w, const Tensor &slots, const Tensor &ws_logits, const Tensor &ws_count, int64_t k,
                int64_t mode, int64_t n_group, int64_t topk_group, bool renorm, double scale, int64_t layer,
-               int64_t mailbox) {
+               int64_t mailbox, const std::optional<Tensor> &active) {
     cuda_contig(x, "x");
     cuda_contig(wr, "router weight");
     RouteParams p{};
@@ -126,6 +126,8 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
     p.corr = optr<const float>(corr);
     p.table = optr<const int32_t>(table);
     p.shared_slots = optr<const int32_t>(shared_slots);
+    p.active = optr<const int32_t>(active);
+    if (active) check(active->numel() >= x.size(0) && active->scalar_type() == at::kInt, "active: int32 [m] flags");
     p.ids = ptr<int32_t>(ids);
     p.w = ptr<float>(w);
     p.slots = ptr<int32_t>(slots);
@@ -211,6 +213,66 @@ void gemv(const Tensor &x, const Tensor &w, const std::optional<Tensor> &add, co
     check(w.size(1) == K && out.numel() == int64_t(m) * N, "gemv shapes");
     c10::cuda::CUDAGuard g(x.device());
     check_rc(xt_gemv_bf16(x.data_ptr(), w.data_ptr(), optr<void>(add), out.data_ptr(), m, N, K, stream()), "gemv");
+}
+
+void fp8_rows(const Tensor &tab, const Tensor &scales, const std::optional<Tensor> &ids, int64_t lo, int64_t hi,
+              int64_t blk, const Tensor &out) {
+    cuda_contig(tab, "tab");
+    cuda_contig(scales, "scales");
+    cuda_contig(out, "out");
+    check(tab.scalar_type() == at::kByte && scales.scalar_type() == at::kByte && out.scalar_type() == at::kBFloat16,
+          "fp8_rows: uint8 payload and scales, bf16 out");
+    const int64_t dim = tab.size(-1);
+    const int64_t n = ids ? ids->numel() : tab.numel() / dim;
+    check(out.numel() == n * dim && scales.size(-1) == dim / blk, "fp8_rows shapes");
+    if (ids) check(ids->is_cuda() && ids->is_contiguous() && ids->scalar_type() == at::kLong, "fp8_rows: int64 ids");
+    c10::cuda::CUDAGuard g(tab.device());
+    check_rc(xt_fp8_rows(tab.data_ptr(), scales.data_ptr(), ids ? ids->data_ptr<int64_t>() : nullptr, lo, hi, int(n),
+                         int(dim), int(blk), out.data_ptr(), stream()),
+             "fp8_rows");
+}
+
+void gemv_fp8(const Tensor &x, const Tensor &w, const Tensor &s, const std::optional<Tensor> &add, const Tensor &out) {
+    cuda_contig(x, "x");
+    cuda_contig(w, "w");
+    cuda_contig(s, "s");
+    cuda_contig(out, "out");
+    check(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kByte && s.scalar_type() == at::kFloat,
+          "gemv_fp8: bf16 x, uint8 (E4M3) w, fp32 scales");
+    const int K = int(x.size(-1)), m = int(x.numel() / K), N = int(w.size(0));
+    check(w.size(1) == K && s.size(0) == N && s.size(1) == K / 128 && out.numel() == int64_t(m) * N, "gemv_fp8 shapes");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_gemv_fp8(x.data_ptr(), w.data_ptr(), s.data_ptr<float>(), optr<void>(add), out.data_ptr(), m, N, K,
+                         stream()),
+             "gemv_fp8");
+}
+
+void spec_truncate(const Tensor &q, const Tensor &tokens, const std::optional<Tensor> &topk, const Tensor &flags,
+                   double threshold) {
+    check(q.is_cuda() && q.dim() == 3 && q.scalar_type() == at::kFloat && q.stride(2) == 1, "spec_truncate: fp32 q [B, S, V]");
+    const int64_t B = q.size(0), S = q.size(1), V = q.size(2);
+    cuda_contig(tokens, "tokens");
+    cuda_contig(flags, "flags");
+    check(tokens.scalar_type() == at::kLong && tokens.numel() == B * (S + 1), "spec_truncate: int64 tokens [B, S + 1]");
+    check(flags.scalar_type() == at::kInt && flags.numel() >= B * (S + 1), "spec_truncate: int32 flags [B * (S + 1)]");
+    if (topk) check(topk->is_cuda() && topk->scalar_type() == at::kInt && topk->numel() >= B, "spec_truncate: int32 top_k");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_spec_truncate(q.data_ptr<float>(), tokens.data_ptr<int64_t>(), topk ? topk->data_ptr<int32_t>() : nullptr,
+                              flags.data_ptr<int32_t>(), float(threshold), q.stride(0), q.stride(1), int(B), int(S),
+                              int(V), stream()),
+             "spec_truncate");
+}
+
+void fp8_dequant(const Tensor &w, const Tensor &s, const Tensor &out) {
+    cuda_contig(w, "w");
+    cuda_contig(s, "s");
+    cuda_contig(out, "out");
+    const int N = int(w.size(0)), K = int(w.size(1));
+    check(w.scalar_type() == at::kByte && s.scalar_type() == at::kFloat && out.scalar_type() == at::kBFloat16 &&
+              s.size(0) == N && s.size(1) == K / 128 && out.numel() == int64_t(N) * K,
+          "fp8_dequant shapes");
+    c10::cuda::CUDAGuard g(w.device());
+    check_rc(xt_fp8_dequant(w.data_ptr(), s.data_ptr<float>(), out.data_ptr(), N, K, stream()), "fp8_dequant");
 }
 
 void gemm_tc(const Tensor &a, const Tensor &b, const std::optional<Tensor> &residual, const Tensor &out,
@@ -453,8 +515,12 @@ TORCH_LIBRARY(xtier, m) {
           "Tensor(c!) ws_ml, Tensor(d!) counters, int splits, float scale) -> ()");
     m.def("moe_route(Tensor x, Tensor wr, Tensor? bias, Tensor? corr, Tensor? table, Tensor? shared_slots, "
           "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, Tensor(d!) ws_logits, Tensor(e!) ws_count, int k, int mode, "
-          "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox) -> ()");
+          "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox, Tensor? active=None) -> ()");
     m.def("gemv(Tensor x, Tensor w, Tensor? add, Tensor(a!) out) -> ()");
+    m.def("fp8_rows(Tensor tab, Tensor scales, Tensor? ids, int lo, int hi, int blk, Tensor(a!) out) -> ()");
+    m.def("gemv_fp8(Tensor x, Tensor w, Tensor s, Tensor? add, Tensor(a!) out) -> ()");
+    m.def("fp8_dequant(Tensor w, Tensor s, Tensor(a!) out) -> ()");
+    m.def("spec_truncate(Tensor(a!) q, Tensor tokens, Tensor? topk, Tensor(b!) flags, float threshold) -> ()");
     m.def("gemm_tc(Tensor a, Tensor b, Tensor? residual, Tensor(a!) out, Tensor(b!) err) -> ()");
     m.def("ep_moe(Tensor x, Tensor ids, Tensor w, Tensor peer, Tensor(a!) state, Tensor(b!) mid, Tensor w13, "
           "Tensor s13, Tensor g13, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(c!) out, Tensor(d!) err, "
@@ -489,6 +555,10 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("moe_gate_up", &moe_gate_up);
     m.impl("moe_down", &moe_down);
     m.impl("gemv", &gemv);
+    m.impl("fp8_rows", &fp8_rows);
+    m.impl("gemv_fp8", &gemv_fp8);
+    m.impl("fp8_dequant", &fp8_dequant);
+    m.impl("spec_truncate", &spec_truncate);
     m.impl("gemm_tc", &gemm_tc);
     m.impl("ep_moe", &ep_moe);
     m.impl("gemm_rs", &gemm_rs);

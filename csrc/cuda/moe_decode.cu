@@ -183,7 +183,11 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
         if (lane < kk) {
             int e, slot;
             float wv;
-            if (lane < p.k) {
+            if (lane < p.k && p.active && !p.active[t]) {   // flagged off: no routed expert anywhere
+                e = -1;
+                wv = 0.f;
+                slot = -1;
+            } else if (lane < p.k) {
                 e = chosen[lane];
                 wv = chosen_w[lane];
                 slot = p.table ? p.table[e] : e;
@@ -201,7 +205,7 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
                 mb.ids[mo] = (slot < 0) ? e : -1;
                 mb.w[mo] = wv;
                 mb.orig[mo] = e;
-                if (slot < 0) atomicOr(&any_cpu, 1);
+                if (slot < 0 && e >= 0) atomicOr(&any_cpu, 1);
             }
         }
     }

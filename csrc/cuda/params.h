@@ -17,6 +17,7 @@ struct RouteParams {
     const float *corr;        // [E] grouped mode: selection bias (e_score_correction_bias), may be null
     const int32_t *table;     // [E] residency: slot or -1 (null: expert id == slot, everything on the GPU)
     const int32_t *shared_slots;   // [n_shared]
+    const int32_t *active;    // [m] token flags (may be null): a token with flag 0 skips its routed experts
     int32_t *ids;             // [m, kk] original expert ids (-1 for shared)
     float *w;                 // [m, kk]
     int32_t *slots;           // [m, kk] GPU slot or -1
@@ -89,6 +90,13 @@ int xt_moe_down(const xt::DownParams *p, const XtMailbox *mb, int use_mb, int m,
 int xt_gemm_tc(const void *A, const void *B, void *D, const void *R, int M, int N, int K, int *error,
                cudaStream_t stream);
 int xt_gemv_bf16(const void *x, const void *W, const void *add, void *y, int m, int N, int K, cudaStream_t stream);
+int xt_fp8_rows(const void *tab, const void *sc, const int64_t *ids, long long lo, long long hi, int n, int dim,
+                int blk, void *out, cudaStream_t stream);
+int xt_gemv_fp8(const void *x, const void *W, const float *S, const void *add, void *y, int m, int N, int K,
+                cudaStream_t stream);
+int xt_fp8_dequant(const void *W, const float *S, void *out, int N, int K, cudaStream_t stream);
+int xt_spec_truncate(float *q, const int64_t *tokens, const int32_t *topk, int32_t *flags, float th,
+                     long long stride_b, long long stride_s, int B, int S, int V, cudaStream_t stream);
 }
 
 namespace xt {

@@ -1,0 +1,80 @@
+"""Speculative decoding on the GPU: the truncation kernel against its PyTorch oracle, token flags in the MoE router
+(a flagged-off token skips its routed experts), a continuation prefill chunk (causal over the cached prefix), and
+chain speculative decoding whose greedy output equals the target model's own greedy decoding."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_truncate_kernel_matches_reference(cuda_ops):
+    from xtier_b200.runtime.speculative import truncate, truncate_reference
+    g = torch.Generator().manual_seed(0)
+    B, S, V = 5, 4, 1000
+    q = torch.softmax(torch.randn(B, S, V, generator=g) * 4, -1)
+    tokens = torch.randint(0, V, (B, S + 1), generator=g)
+    tokens[:, 1:] = torch.argmax(q, -1)                     # drafts = the draft's own argmax (mixed confidences)
+    for greedy in (False, True):
+        qd = q.cuda()
+        flags = truncate(qd, tokens.cuda(), 0.2, greedy=greedy)
+        torch.cuda.synchronize()
+        qr, fr = truncate_reference(q, tokens, 0.2, greedy=greedy)
+        assert torch.equal(flags.cpu(), fr)
+        assert torch.equal(qd.cpu(), qr)
+
+
+def test_token_flags_skip_routed_experts(cuda_ops):
+    from xtier_b200 import formats
+    from xtier_b200.cache.pool import TieredMoE
+    E, H, I, k = 8, 256, 128, 2
+    ex = formats.random_experts(E, H, I, formats.NVFP4, seed=3, std=0.05)
+    router = (torch.randn(E, H) * 0.02).bfloat16()
+    layer = TieredMoE(0, router, ex, k, device='cuda')
+    x = torch.randn(3, H).bfloat16().cuda()
+    add = torch.randn(3, H).bfloat16().cuda()
+    active = torch.tensor([1, 0, 1], dtype=torch.int32, device='cuda')
+    out = layer.forward(x, add=add, active=active)
+    torch.cuda.synchronize()
+    ids = layer.ids[:3, :k].cpu()
+    assert bool((ids[1] == -1).all()) and bool((ids[[0, 2]] >= 0).all())
+    assert torch.equal(out[1].cpu(), add[1].cpu())         # no routed expert: the residual only
+    ref = formats.reference_moe(x.cpu(), ids, layer.w[:3, :k].cpu(), ex) + add.cpu().float()
+    rel = float((out[[0, 2]].cpu().float() - ref[[0, 2]]).norm() / ref[[0, 2]].norm())
+    assert rel < 1e-2, rel
+
+
+def _tiny(seed, layers=2):
+    from xtier_b200.models.qwen3_moe import Qwen3MoeConfig, Qwen3MoeModel
+    cfg = Qwen3MoeConfig.tiny(std=0.05, hidden=256, inter=128)
+    cfg.layers = layers
+    return Qwen3MoeModel(cfg, device='cuda', seed=seed, hot_fraction=1.0, synthetic_experts=False)
+
+
+def test_continuation_prefill_is_causal(cuda_ops):
+    model = _tiny(11)
+    prompt = torch.randint(0, model.cfg.vocab, (40,), generator=torch.Generator().manual_seed(1)).cuda()
+    st = model.alloc_state(1, 64)
+    model.prefill(st, prompt[:24])
+    _, lp = model.prefill(st, prompt[24:], start=24, return_logits=True)
+    ref = model.reference_logits(prompt)
+    rel = float((lp.float() - ref.float()).norm() / ref.float().norm())
+    assert rel < 3e-2, rel
+
+
+def test_speculative_greedy_equals_target_greedy(cuda_ops):
+    from xtier_b200.runtime.speculative import SpeculativeDecoder
+    target = _tiny(21)
+    draft = _tiny(21, layers=1)          # the target's first layer and head: a cheap, often-right draft
+    prompt = torch.randint(0, target.cfg.vocab, (12,), generator=torch.Generator().manual_seed(2)).cuda()
+    st = target.alloc_state(1, 128)
+    want = []
+    nxt = target.prefill(st, prompt)
+    pos = prompt.shape[0]
+    for _ in range(20):
+        want.append(int(nxt))
+        nxt = target.prefill(st, nxt.view(1), start=pos)
+        pos += 1
+    sd = SpeculativeDecoder(target, draft, steps=4, threshold=0.2, max_len=128)
+    got = sd.generate(prompt, 20)
+    assert got == want, (got, want)
+    assert sd.stats['rounds'] < 20                      # some drafts were accepted

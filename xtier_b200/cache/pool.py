@@ -93,13 +93,14 @@ class TieredMoE:
         return len(self.hot) == self.E
 
     # ------------------------------------------------------------------ decode (graph capturable)
-    def route(self, x: torch.Tensor, use_mailbox: bool):
+    def route(self, x: torch.Tensor, use_mailbox: bool, active: torch.Tensor | None = None):
         m = x.shape[0]
         ops.moe_route(x, self.router_w, self.router_bias, self.corr_bias,
                       None if self.all_hot else self.table, self.shared_slots,
                       self.ids[:m], self.w[:m], self.slots[:m], self.ws_logits, self.ws_count, self.k, self.mode,
                       self.n_group, self.topk_group,
-                      self.renorm, self.scale, self.layer, self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0)
+                      self.renorm, self.scale, self.layer,
+                      self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0, active)
 
     def experts_gpu(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None, use_mailbox: bool,
                     out_f32: torch.Tensor | None = None):
@@ -114,13 +115,15 @@ class TieredMoE:
         else:   # no GPU slots at all: every route on the CPU
             raise NotImplementedError('a layer without GPU slots needs at least the shared/hot pool')
 
-    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None):
-        """x bf16 [m, H] -> out bf16 [m, H] (= MoE(x) + add)."""
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None,
+                active: torch.Tensor | None = None):
+        """x bf16 [m, H] -> out bf16 [m, H] (= MoE(x) + add). `active`: int32 [m] token flags of a decode-sized
+        call; flag-0 tokens skip their routed experts (their output is the shared experts' only)."""
         m = x.shape[0]
         out = torch.empty_like(x) if out is None else out
         if m <= MAX_DECODE_TOKENS and m <= self.max_m:
             use_mb = self.mailbox is not None
-            self.route(x, use_mb)
+            self.route(x, use_mb, active)
             self.experts_gpu(x, out, add, use_mb)
             return out
         return self.prefill(x, out, add)

@@ -240,9 +240,11 @@ class Qwen3MoeModel:
         return buf['next']
 
     # ------------------------------------------------------------------ prefill (one sequence)
-    def prefill(self, st: dict, tokens: torch.Tensor, row: int = 0, start: int = 0, return_logits: bool = False):
+    def prefill(self, st: dict, tokens: torch.Tensor, row: int = 0, start: int = 0, return_logits: bool = False,
+                all_logits: bool = False, active: torch.Tensor | None = None):
         """Runs `tokens` [T] of sequence `row` from position `start`; fills the KV cache; returns the next token
-        (and the last position's logits with return_logits)."""
+        (and the last position's logits with return_logits; every position's with all_logits, e.g. a speculative
+        verify). `active` (int32 [T] token flags, calls of <= 16 tokens): flag-0 tokens skip their routed experts."""
         cfg = self.cfg
         dev = self.device
         T = tokens.shape[0]
@@ -268,8 +270,13 @@ class Qwen3MoeModel:
             kk = st['k'][li][row:row + 1, :, :start + T]
             vv = st['v'][li][row:row + 1, :, :start + T]
             qq = q.transpose(0, 1).unsqueeze(0)
-            attn = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=(start == 0),
-                                                                    enable_gqa=True)
+            if start == 0 or T == 1:
+                attn = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=(start == 0),
+                                                                        enable_gqa=True)
+            else:   # a continuation chunk: query i sees keys up to position start + i
+                mask = (torch.arange(start + T, device=dev)[None, :] <=
+                        (start + torch.arange(T, device=dev))[:, None])
+                attn = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, enable_gqa=True)
             o = ops.linear(attn[0].transpose(0, 1).reshape(T, -1).contiguous(), L['o'])
             ops.add_rmsnorm(o, residual, L['post_norm'], h, cfg.eps)
             if copy_stream is not None and li + 1 < len(self.layers):
@@ -278,8 +285,12 @@ class Qwen3MoeModel:
                 done = torch.cuda.Event()
                 done.record()
                 self.layers[li + 1]['moe'].upload_async(copy_stream, after=done)
-            L['moe'].forward(h, out=moe_out)
+            L['moe'].forward(h, out=moe_out, active=active)
         ops.add_rmsnorm(moe_out, residual, self.final_norm, h, cfg.eps)
+        if all_logits:
+            logits = ops.linear(h, self.lm_head)
+            st['lengths'][row] = start + T
+            return torch.argmax(logits, dim=-1), logits
         logits = ops.linear(h[-1:].contiguous(), self.lm_head)
         st['lengths'][row] = start + T
         nxt = torch.argmax(logits, dim=-1)

@@ -66,15 +66,63 @@ def attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits
 
 def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k: int, mode: int = 0,
               n_group: int = 1, topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0,
-              mailbox: int = 0):
+              mailbox: int = 0, active=None):
+    """`active` (int32 [m], optional): token flags; a token with flag 0 skips its routed experts (GPU and CPU),
+    e.g. a verify token after a truncated draft."""
     _ops().moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k, mode, n_group,
-                     topk_group, renorm, scale, layer, mailbox)
+                     topk_group, renorm, scale, layer, mailbox, active)
 
 
 def gemv(x, w, out, add=None):
     """out[m, N] = x[m, K] . w[N, K]^T (+ add), m <= 16, BF16 (the decode projections)."""
     _ops().gemv(x, w, add, out)
     return out
+
+
+def fp8_rows(table, scales, out, ids=None, block: int = 128, lo: int = 0, hi: int = 2 ** 62):
+    """BF16 rows of an FP8 (E4M3) table with E8M0 block scales: out[r] = e4m3(row) * 2^(e - 127). With `ids`
+    (int64, device) rows ids - lo of `table` are gathered and ids outside [lo, hi) give zeros; without, `table` holds
+    the rows already gathered."""
+    _ops().fp8_rows(table, scales, ids, lo, hi, block, out)
+    return out
+
+
+def gemv_fp8(x, w, s, out, add=None):
+    """out[m, N] = x[m, K] . (w[N, K] E4M3 * s[N, K/128])^T (+ add), m <= 16 (W8A16 decode)."""
+    _ops().gemv_fp8(x, w, s, add, out)
+    return out
+
+
+def fp8_dequant(w, s, out=None):
+    """w[N, K] E4M3 * s[N, K/128] -> BF16 [N, K]."""
+    out = torch.empty(w.shape, dtype=torch.bfloat16, device=w.device) if out is None else out
+    _ops().fp8_dequant(w, s, out)
+    return out
+
+
+def spec_truncate(q, tokens, flags, threshold: float, topk=None):
+    """Chain-draft truncation in place: q [B, S, V] draft probabilities (fp32, zeroed at the first dropped draft),
+    tokens [B, S + 1] verify input, flags [B * (S + 1)] int32 out (1: the token is computed)."""
+    _ops().spec_truncate(q, tokens, topk, flags, threshold)
+
+
+_FP8_SCRATCH: dict = {}
+
+
+def linear_fp8(x, w, s, out=None):
+    """x @ (w * s)^T with FP8 weights (per row x 128-column scales): the W8A16 GEMV for decode-sized inputs, else a
+    dequant pass into a per-device scratch and the tcgen05 BF16 GEMM (prefill is compute-bound)."""
+    m = x.numel() // x.shape[-1]
+    K = x.shape[-1]
+    if m <= 16 and K * m * 2 <= 200 * 1024:
+        out = torch.empty(*x.shape[:-1], w.shape[0], dtype=torch.bfloat16, device=x.device) if out is None else out
+        return gemv_fp8(x, w, s, out)
+    key = (x.device, w.numel())
+    buf = _FP8_SCRATCH.get(key)
+    if buf is None:
+        buf = _FP8_SCRATCH[key] = torch.empty(w.numel(), dtype=torch.bfloat16, device=x.device)
+    wb = fp8_dequant(w, s, buf.view(w.shape))
+    return linear(x.reshape(m, K), wb, out)
 
 
 _gemm_err: dict = {}

@@ -1,0 +1,138 @@
+"""Speculative decoding with a chain draft: draft S tokens with a small model, truncate the chain at the draft's
+confidence, verify all of it in one target forward, accept losslessly.
+
+Per round, for one sequence at position `pos` whose last accepted token is `t0`:
+1. the draft model proposes d_1..d_S autoregressively, keeping its probabilities q_j (temperature-scaled softmax);
+2. `truncate` (csrc/cuda/spec.cu) keeps the leading drafts with q_j(d_j) >= threshold (at least one; all of them for
+   greedy decoding), zeroes the q row of the first dropped draft and sets the verify tokens' flags, so the target's
+   MoE layers skip the routed experts of tokens whose output nobody reads;
+3. the target runs [t0, d_1..d_S] from `pos` in one forward (causal over its KV cache), giving p_0..p_S;
+4. `verify_chain` accepts d_j with probability min(1, p_j(d_j) / q_j(d_j)) in order (a zero q row never accepts) and
+   on the first rejection samples from the residual (p_j - q_j)+; when every draft is accepted it samples a bonus token
+   from p_S. For greedy decoding it accepts while d_j == argmax p_j and then takes argmax p. Either way the output has
+   exactly the target's distribution (greedy: the target's own greedy tokens).
+Stale KV entries past the accepted prefix are overwritten by the next round (attention reads positions < pos only).
+(Reference parity: xtier/packs/speculative/truncate.py (truncation rule, token flags, zeroed q row), the verify rule of
+SGLang's chain sampler it relies on.)
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+
+
+def truncate(q: torch.Tensor, tokens: torch.Tensor, threshold: float, greedy: bool = False,
+             flags: torch.Tensor | None = None) -> torch.Tensor:
+    """q [B, S, V] fp32 (modified in place), tokens [B, S + 1] int64 -> flags int32 [B, S + 1]."""
+    B, S, _ = q.shape
+    flags = torch.empty(B * (S + 1), dtype=torch.int32, device=q.device) if flags is None else flags
+    topk = torch.ones(B, dtype=torch.int32, device=q.device) if greedy else None
+    ops.spec_truncate(q, tokens.contiguous(), flags, threshold, topk)
+    return flags.view(B, S + 1)
+
+
+def truncate_reference(q: torch.Tensor, tokens: torch.Tensor, threshold: float, greedy: bool = False):
+    """The same rule in plain PyTorch (the tests' oracle); returns (q', flags)."""
+    q = q.clone()
+    B, S, _ = q.shape
+    flags = torch.zeros(B, S + 1, dtype=torch.int32)
+    for b in range(B):
+        own = q[b, torch.arange(S), tokens[b, 1:]]
+        low = (own < threshold).nonzero()
+        keep = S if greedy else max(int(low[0]) if low.numel() else S, 1)
+        flags[b, :keep + 1] = 1
+        if keep < S:
+            q[b, keep] = 0
+    return q, flags
+
+
+def verify_chain(p: torch.Tensor, q: torch.Tensor, drafts: torch.Tensor, generator: torch.Generator | None = None,
+                 greedy: bool = False) -> list[int]:
+    """One sequence: p [S + 1, V] target probabilities, q [S, V] draft probabilities, drafts [S] -> the accepted
+    tokens followed by one corrected or bonus token (1 to S + 1 tokens)."""
+    S = drafts.shape[0]
+    out = []
+    if greedy:
+        best = torch.argmax(p, dim=-1).tolist()
+        for j in range(S):
+            if int(drafts[j]) != best[j]:
+                return out + [best[j]]
+            out.append(best[j])
+        return out + [best[S]]
+    u = torch.rand(S, generator=generator, device='cpu')
+    pc, qc = p.float().cpu(), q.float().cpu()
+    for j in range(S):
+        d = int(drafts[j])
+        pj, qj = float(pc[j, d]), float(qc[j, d])
+        if qj > 0 and float(u[j]) * qj <= pj:
+            out.append(d)
+            continue
+        resid = torch.clamp(pc[j] - qc[j], min=0)
+        resid = resid if float(resid.sum()) > 0 else pc[j]
+        return out + [int(torch.multinomial(resid / resid.sum(), 1, generator=generator))]
+    return out + [int(torch.multinomial(pc[S] / pc[S].sum(), 1, generator=generator))]
+
+
+class SpeculativeDecoder:
+    """Chain speculative decoding of one sequence (row 0) of `target` with `draft` (both models with the
+    `prefill(st, tokens, start=..., all_logits=...)` interface and their own KV state)."""
+
+    def __init__(self, target, draft, steps: int = 4, threshold: float = 0.2, temperature: float = 0.0,
+                 max_len: int = 4096, seed: int = 0):
+        self.target, self.draft = target, draft
+        self.S, self.th, self.temp = steps, threshold, temperature
+        self.st_t = target.alloc_state(1, max_len)
+        self.st_d = draft.alloc_state(1, max_len)
+        self.gen = torch.Generator().manual_seed(seed)
+        self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0)
+
+    def _probs(self, logits: torch.Tensor) -> torch.Tensor:
+        if self.temp <= 0:
+            return torch.nn.functional.one_hot(torch.argmax(logits, -1), logits.shape[-1]).float()
+        return torch.softmax(logits.float() / self.temp, dim=-1)
+
+    def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> list[int]:
+        """Up to `max_new_tokens` new tokens after `prompt` [T]."""
+        dev = self.target.device
+        prompt = prompt.to(dev)
+        T = prompt.shape[0]
+        greedy = self.temp <= 0
+        _, lt = self.target.prefill(self.st_t, prompt, return_logits=True)
+        first = (int(torch.argmax(lt)) if greedy else
+                 int(torch.multinomial(self._probs(lt).cpu(), 1, generator=self.gen)))
+        seq = prompt.tolist() + [first]
+        if T > 1:
+            self.draft.prefill(self.st_d, prompt[:-1])
+        pos = T            # position of the last accepted token; the target holds KV for positions < pos
+        dpos = T - 1       # the draft holds KV for positions < dpos
+        while len(seq) - T < max_new_tokens:
+            if dpos < pos:   # the draft catches up on accepted tokens it has not seen
+                self.draft.prefill(self.st_d, torch.tensor(seq[dpos:pos], device=dev), start=dpos)
+                dpos = pos
+            last = seq[pos]
+            drafts, qs, cur = [], [], last
+            for j in range(self.S):
+                _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
+                                           return_logits=True)
+                qj = self._probs(ld)
+                d = int(torch.argmax(qj)) if greedy else int(torch.multinomial(qj.cpu(), 1, generator=self.gen))
+                drafts.append(d)
+                qs.append(qj)
+                cur = d
+            q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
+            vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
+            flags = truncate(q, vt, self.th, greedy=greedy)
+            _, logits = self.target.prefill(self.st_t, vt[0], start=pos, all_logits=True, active=flags[0])
+            keep = int(flags[0].sum()) - 1
+            acc = verify_chain(self._probs(logits)[:keep + 1], q[0, :keep], torch.tensor(drafts[:keep]), self.gen,
+                               greedy)
+            self.stats['rounds'] += 1
+            self.stats['drafted'] += self.S
+            self.stats['kept'] += keep
+            self.stats['accepted'] += len(acc) - 1
+            seq.extend(acc)
+            # the draft fed last, d_1..d_{S-1} at pos..pos+S-1: valid up to the accepted ones
+            dpos = pos + min(len(acc), self.S)
+            pos = len(seq) - 1
+        return seq[T:T + max_new_tokens]
