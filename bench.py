@@ -101,6 +101,8 @@ def main():
     ap.add_argument('--layers', type=int, default=48)
     ap.add_argument('--threads', type=int, default=0, help='CPU engine workers per rank (0: auto)')
     ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--long-prefill', type=int, default=65536,
+                    help='also time a warm prefill of this many random tokens (0: skip)')
     ap.add_argument('--profile', type=int, default=0, help='print per-kernel device time of N graph replays and exit')
     args = ap.parse_args()
     if args.impl == 'reference':
@@ -213,6 +215,26 @@ def main():
         e2e = {'value': world * args.steps / e2e_s, 'unit': 'tok/s', 'h2d_bytes_per_step': gen.h2d_bytes_per_step,
                'd2h_bytes_per_step': gen.d2h_bytes_per_step, 'api': 'Generator.decode_one'}
 
+    long_prefill = None
+    if args.long_prefill:
+        # time to first token of a long prompt: a fresh KV state, one untimed run (allocations, upload buffers,
+        # kernel selection), then one timed by device events between barriers, max over ranks
+        st2 = model.alloc_state(1, args.long_prefill + 8)
+        ids = torch.randint(0, cfg.vocab, (args.long_prefill,), generator=torch.Generator().manual_seed(7 + rank))
+        ids = ids.cuda()
+        model.prefill(st2, ids)
+        barrier()
+        e0.record()
+        model.prefill(st2, ids)
+        e1.record()
+        barrier()
+        t_long = max_over_ranks(e0.elapsed_time(e1))
+        long_prefill = {'tokens': args.long_prefill, 'ttft_ms': round(t_long, 1),
+                        'tok_s': round(world * args.long_prefill / t_long * 1e3, 1),
+                        'timing': 'warm, device events, max over ranks', 'scaling': 'weak (one prompt per GPU)'}
+        del st2
+        torch.cuda.empty_cache()
+
     mb_stats = mailbox.stats() if mailbox is not None else {}
     launches_per_step = 7 * cfg.layers + 1   # norms x2, rope+kv, attention, route, gate/up, down per layer; final norm
     line = {
@@ -232,6 +254,7 @@ def main():
         'setup_s': {'build': round(build_s, 1), 'prefill': round(prefill_s, 2)},
         'prefill': {'tokens': args.prompt, 'ttft_ms': round(ttft_ms, 1),
                     'tok_s': round(args.prompt / ttft_ms * 1e3, 1), 'timing': 'warm, device events'},
+        'prefill_long': long_prefill,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -116,7 +116,7 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
                const std::optional<Tensor> &table, const std::optional<Tensor> &shared_slots, const Tensor &ids,
                const Tensor &w, const Tensor &slots, const Tensor &ws_logits, const Tensor &ws_count, int64_t k,
                int64_t mode, int64_t n_group, int64_t topk_group, bool renorm, double scale, int64_t layer,
-               int64_t mailbox, const std::optional<Tensor> &active) {
+               int64_t mailbox, const std::optional<Tensor> &active, const std::optional<Tensor> &logits_in) {
     cuda_contig(x, "x");
     cuda_contig(wr, "router weight");
     RouteParams p{};
@@ -127,6 +127,10 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
     p.table = optr<const int32_t>(table);
     p.shared_slots = optr<const int32_t>(shared_slots);
     p.active = optr<const int32_t>(active);
+    p.logits_in = optr<const float>(logits_in);
+    if (logits_in)
+        check(logits_in->scalar_type() == at::kFloat && logits_in->numel() >= x.size(0) * wr.size(0) && mailbox == 0,
+              "logits_in: fp32 [m, E], no mailbox");
     if (active) check(active->numel() >= x.size(0) && active->scalar_type() == at::kInt, "active: int32 [m] flags");
     p.ids = ptr<int32_t>(ids);
     p.w = ptr<float>(w);
@@ -261,6 +265,51 @@ void spec_truncate(const Tensor &q, const Tensor &tokens, const std::optional<Te
                               flags.data_ptr<int32_t>(), float(threshold), q.stride(0), q.stride(1), int(B), int(S),
                               int(V), stream()),
              "spec_truncate");
+}
+
+void gather_rows(const Tensor &x, const Tensor &src, const Tensor &X) {
+    cuda_contig(x, "x");
+    cuda_contig(src, "src");
+    cuda_contig(X, "X");
+    const int H = int(x.size(-1));
+    check(x.scalar_type() == at::kBFloat16 && X.scalar_type() == at::kBFloat16 && src.scalar_type() == at::kInt &&
+              X.numel() == src.numel() * H,
+          "gather_rows shapes");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_gather_rows(x.data_ptr(), src.data_ptr<int32_t>(), X.data_ptr(), int(src.numel()), H, stream()),
+             "gather_rows");
+}
+
+void route_combine(const Tensor &Ya, const Tensor &da, const std::optional<Tensor> &Yb,
+                   const std::optional<Tensor> &db, const std::optional<Tensor> &add, const Tensor &out) {
+    cuda_contig(Ya, "Ya");
+    cuda_contig(da, "da");
+    cuda_contig(out, "out");
+    const int H = int(out.size(-1)), m = int(out.numel() / H);
+    check(Ya.scalar_type() == at::kFloat && da.scalar_type() == at::kInt && da.numel() % m == 0, "route_combine a");
+    if (Yb) check(db && Yb->scalar_type() == at::kFloat && db->scalar_type() == at::kInt && db->numel() % m == 0,
+                  "route_combine b");
+    check(out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16, "route_combine out dtype");
+    if (add) check(add->scalar_type() == at::kBFloat16 && add->numel() == out.numel(), "route_combine add");
+    c10::cuda::CUDAGuard g(out.device());
+    check_rc(xt_route_combine(Ya.data_ptr<float>(), da.data_ptr<int32_t>(), int(da.numel() / m),
+                              Yb ? Yb->data_ptr<float>() : nullptr, db ? db->data_ptr<int32_t>() : nullptr,
+                              db ? int(db->numel() / m) : 0, add ? add->data_ptr() : nullptr, out.data_ptr(),
+                              out.scalar_type() == at::kFloat, m, H, stream()),
+             "route_combine");
+}
+
+void gemm_tc_f32(const Tensor &a, const Tensor &b, const Tensor &out, const Tensor &err) {
+    cuda_contig(a, "a");
+    cuda_contig(b, "b");
+    cuda_contig(out, "out");
+    check(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kFloat,
+          "gemm_tc_f32: bf16 operands, fp32 out");
+    const int K = int(a.size(-1)), M = int(a.numel() / K), N = int(b.size(0));
+    check(b.size(1) == K && out.numel() == int64_t(M) * N, "gemm_tc_f32 shapes");
+    c10::cuda::CUDAGuard g(a.device());
+    check_rc(xt_gemm_tc_f32(a.data_ptr(), b.data_ptr(), out.data_ptr<float>(), M, N, K, err.data_ptr<int>(), stream()),
+             "gemm_tc_f32");
 }
 
 void fp8_dequant(const Tensor &w, const Tensor &s, const Tensor &out) {
@@ -515,11 +564,15 @@ TORCH_LIBRARY(xtier, m) {
           "Tensor(c!) ws_ml, Tensor(d!) counters, int splits, float scale) -> ()");
     m.def("moe_route(Tensor x, Tensor wr, Tensor? bias, Tensor? corr, Tensor? table, Tensor? shared_slots, "
           "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, Tensor(d!) ws_logits, Tensor(e!) ws_count, int k, int mode, "
-          "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox, Tensor? active=None) -> ()");
+          "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox, Tensor? active=None, "
+          "Tensor? logits_in=None) -> ()");
     m.def("gemv(Tensor x, Tensor w, Tensor? add, Tensor(a!) out) -> ()");
     m.def("fp8_rows(Tensor tab, Tensor scales, Tensor? ids, int lo, int hi, int blk, Tensor(a!) out) -> ()");
     m.def("gemv_fp8(Tensor x, Tensor w, Tensor s, Tensor? add, Tensor(a!) out) -> ()");
     m.def("fp8_dequant(Tensor w, Tensor s, Tensor(a!) out) -> ()");
+    m.def("gemm_tc_f32(Tensor a, Tensor b, Tensor(a!) out, Tensor(b!) err) -> ()");
+    m.def("gather_rows(Tensor x, Tensor src, Tensor(a!) X) -> ()");
+    m.def("route_combine(Tensor Ya, Tensor da, Tensor? Yb, Tensor? db, Tensor? add, Tensor(a!) out) -> ()");
     m.def("spec_truncate(Tensor(a!) q, Tensor tokens, Tensor? topk, Tensor(b!) flags, float threshold) -> ()");
     m.def("gemm_tc(Tensor a, Tensor b, Tensor? residual, Tensor(a!) out, Tensor(b!) err) -> ()");
     m.def("ep_moe(Tensor x, Tensor ids, Tensor w, Tensor peer, Tensor(a!) state, Tensor(b!) mid, Tensor w13, "
@@ -558,6 +611,9 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("fp8_rows", &fp8_rows);
     m.impl("gemv_fp8", &gemv_fp8);
     m.impl("fp8_dequant", &fp8_dequant);
+    m.impl("gemm_tc_f32", &gemm_tc_f32);
+    m.impl("gather_rows", &gather_rows);
+    m.impl("route_combine", &route_combine);
     m.impl("spec_truncate", &spec_truncate);
     m.impl("gemm_tc", &gemm_tc);
     m.impl("ep_moe", &ep_moe);

@@ -68,7 +68,21 @@ struct TcSmem {
     static constexpr int BYTES = TC_STAGES * STAGE + 1024 /*barriers*/ + 1024 /*alignment*/;
 };
 
-template <int BN>
+// 32 FP32 accumulator columns of one output row stored as FP32 (the router logits of a prefill call)
+XT_DEV void store_row32_f32(float *D, const uint32_t (&r)[32], int row, int col, int N) {
+    float *dst = D + size_t(row) * N + col;
+    if (col + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+            reinterpret_cast<float4 *>(dst)[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                             __uint_as_float(r[4 * v + 2]),
+                                                             __uint_as_float(r[4 * v + 3]));
+    } else {
+        for (int i = 0; i < 32 && col + i < N; ++i) dst[i] = __uint_as_float(r[i]);
+    }
+}
+
+template <int BN, bool F32 = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    __nv_bfloat16 *__restrict__ D, const __nv_bfloat16 *__restrict__ R, int M, int N, int K,
@@ -214,7 +228,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc::tmem_ld32(base + uint32_t(c0), r);
                 tc::tmem_ld_wait();
                 const int col = tn * BN + c0;
-                if (row < M && col < N) store_row32(D, R, r, row, col, N);
+                if (row < M && col < N) {
+                    if constexpr (F32)
+                        store_row32_f32(reinterpret_cast<float *>(D), r, row, col, N);
+                    else
+                        store_row32(D, R, r, row, col, N);
+                }
             }
             tc::tc_fence_before();
             __syncwarp();
@@ -442,7 +461,7 @@ int num_sms() {
     return n;
 }
 
-template <int BN>
+template <int BN, bool F32 = false>
 int launch(const void *A, const void *B, void *Dp, const void *R, int M, int N, int K, int *error,
            cudaStream_t stream) {
     CUtensorMap ma, mb;
@@ -450,14 +469,15 @@ int launch(const void *A, const void *B, void *Dp, const void *R, int M, int N, 
     const int smem = TcSmem<BN>::BYTES;
     static bool attr = false;
     if (!attr) {
-        if (cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        if (cudaFuncSetAttribute(gemm_tc_kernel<BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
             return -4;
         attr = true;
     }
     const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    gemm_tc_kernel<BN><<<grid, TC_THREADS, smem, stream>>>(ma, mb, static_cast<__nv_bfloat16 *>(Dp),
-                                                           static_cast<const __nv_bfloat16 *>(R), M, N, K, error);
+    gemm_tc_kernel<BN, F32><<<grid, TC_THREADS, smem, stream>>>(ma, mb, static_cast<__nv_bfloat16 *>(Dp),
+                                                                static_cast<const __nv_bfloat16 *>(R), M, N, K, error);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -501,4 +521,12 @@ extern "C" int xt_gemm_tc(const void *A, const void *B, void *D, const void *R, 
     }
     if (N >= 2048) return launch<256>(A, B, D, R, M, N, K, error, stream);
     return launch<128>(A, B, D, R, M, N, K, error, stream);
+}
+
+// D[M, N] FP32 = A[M, K] . B[N, K]^T (BF16 operands): prefill router logits, kept in FP32 like the decode router's.
+extern "C" int xt_gemm_tc_f32(const void *A, const void *B, float *D, int M, int N, int K, int *error,
+                              cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || K % 8 || !error) return -2;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -2;
+    return launch<128, true>(A, B, D, nullptr, M, N, K, error, stream);
 }

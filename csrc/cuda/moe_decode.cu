@@ -42,6 +42,12 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
     const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kk = p.k + p.n_shared;
     const __nv_bfloat16 *xt = p.x + size_t(t) * p.H;
+    if (p.logits_in) {   // prefill: logits from the tensor-core GEMM, one CTA per token selects (no mailbox)
+        if (tid == 0) any_cpu = 0;
+        for (int e = tid; e < p.E; e += ROUTE_THREADS)
+            logits[e] = p.logits_in[size_t(t) * p.E + e] + (p.bias ? p.bias[e] : 0.f);
+        __syncthreads();
+    } else {
     if (use_mb) {   // this CTA's slice of the token's activations to the mailbox slot first: the PCIe writes overlap
         const uint4 *src = reinterpret_cast<const uint4 *>(xt);   // the logits and are long done at publication
         uint4 *dst = reinterpret_cast<uint4 *>(mb.x + size_t(t) * p.H);
@@ -89,6 +95,7 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
     __threadfence();
     for (int e = tid; e < p.E; e += ROUTE_THREADS) logits[e] = __ldcg(p.ws_logits + size_t(t) * p.E + e);
     __syncthreads();
+    }   // phase A
 
     if (warp == 0) {
         // scores -> selection values
@@ -526,7 +533,8 @@ int xt_moe_route(const RouteParams *p, const XtMailbox *mb, int use_mb, cudaStre
     if (use_mb && p->m > XT_MB_MAX_TOKENS) return -3;
     if (!p->ws_logits || !p->ws_count) return -5;
     XtMailbox empty{};
-    dim3 grid((p->E + ROUTE_WARPS - 1) / ROUTE_WARPS, p->m);
+    if (p->logits_in && use_mb) return -6;
+    dim3 grid(p->logits_in ? 1 : (p->E + ROUTE_WARPS - 1) / ROUTE_WARPS, p->m);
     moe_route_kernel<<<grid, ROUTE_THREADS, 0, stream>>>(*p, use_mb ? *mb : empty, use_mb);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

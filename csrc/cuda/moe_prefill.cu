@@ -389,3 +389,86 @@ int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------ gather / combine
+// Around the grouped GEMMs of a prefill call:
+// * gather_rows: X[r] = x[src[r]] (BF16 rows; src -1 -> a zero row, the padding of each expert's run), 16-byte copies.
+// * route_combine: out[t] = sum over the token's routes j in route order of the route's weighted down row (from the
+//   GPU-slot pass Ya or the uploaded-experts pass Yb, whichever computed that route; neither: nothing) + add[t], in
+//   FP32, written once as BF16 or FP32. One pass over the route rows instead of a gather, a select and k adds.
+namespace xt {
+
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint4 *__restrict__ x, const int32_t *__restrict__ src,
+                                                         uint4 *__restrict__ X, int R, int hv) {
+    const long long i = blockIdx.x * 256ll + threadIdx.x;
+    if (i >= (long long)R * hv) return;
+    const int r = int(i / hv), c = int(i % hv);
+    const int s = src[r];
+    X[i] = s >= 0 ? x[size_t(s) * hv + c] : make_uint4(0, 0, 0, 0);
+}
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(256) route_combine_kernel(const float *__restrict__ Ya, const int32_t *__restrict__ da,
+                                                           int ka, const float *__restrict__ Yb,
+                                                           const int32_t *__restrict__ db, int kb,
+                                                           const __nv_bfloat16 *__restrict__ add, void *out, int m,
+                                                           int H) {
+    const int hv = H / 4;
+    const long long i = blockIdx.x * 256ll + threadIdx.x;
+    if (i >= (long long)m * hv) return;
+    const int t = int(i / hv), c = int(i % hv);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int kk = ka > kb ? ka : kb;
+    for (int j = 0; j < kk; ++j) {
+        const int ra = j < ka ? da[size_t(t) * ka + j] : -1;
+        const int rb = (ra < 0 && Yb && j < kb) ? db[size_t(t) * kb + j] : -1;
+        const float *row = ra >= 0 ? Ya + size_t(ra) * H : (rb >= 0 ? Yb + size_t(rb) * H : nullptr);
+        if (row) {
+            const float4 v = reinterpret_cast<const float4 *>(row)[c];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+    }
+    if (add) {
+        const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(add + size_t(t) * H + 4 * c);
+        const float2 p = __bfloat1622float2(a2[0]), q = __bfloat1622float2(a2[1]);
+        acc.x += p.x;
+        acc.y += p.y;
+        acc.z += q.x;
+        acc.w += q.y;
+    }
+    if (OUT_F32) {
+        reinterpret_cast<float4 *>(out)[i] = acc;
+    } else {
+        __nv_bfloat162 o[2] = {__floats2bfloat162_rn(acc.x, acc.y), __floats2bfloat162_rn(acc.z, acc.w)};
+        reinterpret_cast<uint2 *>(out)[i] = *reinterpret_cast<uint2 *>(o);
+    }
+}
+
+}  // namespace xt
+
+extern "C" int xt_gather_rows(const void *x, const int32_t *src, void *X, int R, int H, cudaStream_t stream) {
+    if (H % 8 || R < 0) return -2;
+    if (R == 0) return 0;
+    const int hv = H / 8;
+    const long long th = (long long)R * hv;
+    xt::gather_rows_kernel<<<unsigned((th + 255) / 256), 256, 0, stream>>>(static_cast<const uint4 *>(x), src,
+                                                                           static_cast<uint4 *>(X), R, hv);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+extern "C" int xt_route_combine(const float *Ya, const int32_t *da, int ka, const float *Yb, const int32_t *db, int kb,
+                                const void *add, void *out, int out_f32, int m, int H, cudaStream_t stream) {
+    if (H % 4 || m < 0 || ka < 1 || (Yb && kb < 1)) return -2;
+    if (m == 0) return 0;
+    const long long th = (long long)m * (H / 4);
+    const unsigned grid = unsigned((th + 255) / 256);
+    auto A = static_cast<const __nv_bfloat16 *>(add);
+    if (out_f32)
+        xt::route_combine_kernel<true><<<grid, 256, 0, stream>>>(Ya, da, ka, Yb, db, kb, A, out, m, H);
+    else
+        xt::route_combine_kernel<false><<<grid, 256, 0, stream>>>(Ya, da, ka, Yb, db, kb, A, out, m, H);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}

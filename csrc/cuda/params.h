@@ -18,6 +18,7 @@ struct RouteParams {
     const int32_t *table;     // [E] residency: slot or -1 (null: expert id == slot, everything on the GPU)
     const int32_t *shared_slots;   // [n_shared]
     const int32_t *active;    // [m] token flags (may be null): a token with flag 0 skips its routed experts
+    const float *logits_in;   // [m, E] precomputed FP32 router logits (prefill; may be null): selection only
     int32_t *ids;             // [m, kk] original expert ids (-1 for shared)
     float *w;                 // [m, kk]
     int32_t *slots;           // [m, kk] GPU slot or -1
@@ -89,6 +90,7 @@ int xt_moe_gate_up(const xt::GateUpParams *p, cudaStream_t stream);
 int xt_moe_down(const xt::DownParams *p, const XtMailbox *mb, int use_mb, int m, cudaStream_t stream);
 int xt_gemm_tc(const void *A, const void *B, void *D, const void *R, int M, int N, int K, int *error,
                cudaStream_t stream);
+int xt_gemm_tc_f32(const void *A, const void *B, float *D, int M, int N, int K, int *error, cudaStream_t stream);
 int xt_gemv_bf16(const void *x, const void *W, const void *add, void *y, int m, int N, int K, cudaStream_t stream);
 int xt_fp8_rows(const void *tab, const void *sc, const int64_t *ids, long long lo, long long hi, int n, int dim,
                 int blk, void *out, cudaStream_t stream);
@@ -160,6 +162,9 @@ int xt_topk_rows(const float *scores, int rows, int n, int K, int32_t *out, cuda
 int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int32_t *tiles, int T, int gate_up,
                    int K, int N_rows, int I, int fmt, const void *scales, const float *gscale, const float *route_w,
                    void *mid, float *y, int out_cols, int *error, cudaStream_t stream);
+int xt_gather_rows(const void *x, const int32_t *src, void *X, int R, int H, cudaStream_t stream);
+int xt_route_combine(const float *Ya, const int32_t *da, int ka, const float *Yb, const int32_t *db, int kb,
+                     const void *add, void *out, int out_f32, int m, int H, cudaStream_t stream);
 int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
                   const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,
                   int *error, cudaStream_t stream);

@@ -67,3 +67,34 @@ def test_grouped_prefill_after_swaps(cuda_ops, monkeypatch):
     ref = model.reference_logits(prompt)
     rel = float((lp.float() - ref.float()).norm() / ref.float().norm())
     assert rel < 3e-2, rel
+
+
+@pytest.mark.parametrize('mode', [0, 1])
+def test_prefill_router_gemm_matches_decode_router(cuda_ops, mode):
+    """Prefill-sized calls take the router logits from the FP32-output tensor-core GEMM and only select in the route
+    kernel; the routes equal the decode router's (which computes the logits itself) up to near-ties."""
+    from xtier_b200 import formats
+    from xtier_b200.cache.pool import TieredMoE
+    E, H, I, k = 64, 1024, 256, 4
+    g = torch.Generator().manual_seed(mode)
+    ex = formats.random_experts(E, H, I, formats.NVFP4, seed=1, std=0.05)
+    router = (torch.randn(E, H, generator=g) * 0.05).bfloat16()
+    bias = torch.randn(E, generator=g) * 0.1
+    kw = dict(mode=1, n_group=8, topk_group=4, scale=2.5, corr_bias=torch.randn(E, generator=g) * 0.01) if mode else {}
+    layer = TieredMoE(0, router, ex, k, router_bias=bias, device='cuda', **kw)
+    x = torch.randn(300, H, generator=g).bfloat16().cuda()
+    layer._alloc(300)
+    layer.route(x, False)                      # m > 16: GEMM logits + selection
+    ids_p, w_p = layer.ids[:300, :k].clone(), layer.w[:300, :k].clone()
+    layer._alloc(16)
+    ids_d, w_d = [], []
+    for s in range(0, 300, 16):                # the decode router, 16 tokens at a time
+        xs = x[s:s + 16].contiguous()
+        layer.route(xs, False)
+        ids_d.append(layer.ids[:xs.shape[0], :k].clone())
+        w_d.append(layer.w[:xs.shape[0], :k].clone())
+    ids_d, w_d = torch.cat(ids_d), torch.cat(w_d)
+    same = (ids_p == ids_d).all(dim=1).float().mean().item()
+    assert same > 0.98, same
+    rows = (ids_p == ids_d).all(dim=1)
+    assert torch.allclose(w_p[rows], w_d[rows], rtol=1e-4, atol=1e-5)

@@ -25,6 +25,8 @@ from ..formats import MXFP4, NVFP4, ExpertWeights
 
 MAX_DECODE_TOKENS = 16
 _STAGING: dict = {}   # (cold experts, H, I, fmt, device) -> staging ExpertWeights shared by the layers
+_PREFILL_BUFS: dict = {}   # (kk, E, I, H, device) -> prefill route buffers shared by the layers
+_BUF_NAMES = ('ids', 'w', 'slots', 'mid', 'ws_logits', 'ws_count', 'gpu_part')
 
 
 class TieredMoE:
@@ -77,16 +79,31 @@ class TieredMoE:
         self.elastic = None       # ElasticSlots (cache/elastic.py) when the layer has extra slots
         self._alloc(max_tokens)
 
-    def _alloc(self, m: int):
-        self.max_m = m
+    def _make_bufs(self, m: int) -> dict:
         dev = self.device
-        self.ids = torch.empty(m, self.kk, dtype=torch.int32, device=dev)
-        self.w = torch.empty(m, self.kk, dtype=torch.float32, device=dev)
-        self.slots = torch.empty(m, self.kk, dtype=torch.int32, device=dev)
-        self.mid = torch.empty(m * self.kk, self.I, dtype=torch.float32, device=dev)
-        self.ws_logits = torch.empty(m, self.E, dtype=torch.float32, device=dev)
-        self.ws_count = torch.zeros(m, dtype=torch.int32, device=dev)
-        self.gpu_part = torch.empty(m, self.H, dtype=torch.float32, device=dev)
+        return dict(ids=torch.empty(m, self.kk, dtype=torch.int32, device=dev),
+                    w=torch.empty(m, self.kk, dtype=torch.float32, device=dev),
+                    slots=torch.empty(m, self.kk, dtype=torch.int32, device=dev),
+                    mid=torch.empty(m * self.kk, self.I, dtype=torch.float32, device=dev),
+                    ws_logits=torch.empty(m, self.E, dtype=torch.float32, device=dev),
+                    ws_count=torch.zeros(m, dtype=torch.int32, device=dev),
+                    gpu_part=torch.empty(m, self.H, dtype=torch.float32, device=dev))
+
+    def _alloc(self, m: int):
+        """The decode buffers: allocated once, so a captured decode graph keeps valid pointers whatever prefills run
+        between its replays (prefill calls use separate buffers, `_prefill_bufs`)."""
+        self.max_m = m
+        for k, v in self._make_bufs(m).items():
+            setattr(self, k, v)
+
+    def _prefill_bufs(self, m: int) -> dict:
+        """Route / scratch buffers of a prefill chunk of m tokens, shared by the layers of one shape (they run one
+        after another on the compute stream)."""
+        key = (self.kk, self.E, self.I, self.H, self.device)
+        cur = _PREFILL_BUFS.get(key)
+        if cur is None or cur['ids'].shape[0] < m:
+            cur = _PREFILL_BUFS[key] = self._make_bufs(m)
+        return cur
 
     @property
     def all_hot(self) -> bool:
@@ -95,12 +112,16 @@ class TieredMoE:
     # ------------------------------------------------------------------ decode (graph capturable)
     def route(self, x: torch.Tensor, use_mailbox: bool, active: torch.Tensor | None = None):
         m = x.shape[0]
+        logits = None
+        if m > MAX_DECODE_TOKENS and not use_mailbox:
+            # prefill-sized call: the router GEMM on the tensor cores (FP32 out), then per-token selection
+            logits = ops.gemm_f32(x, self.router_w, self.ws_logits[:m])
         ops.moe_route(x, self.router_w, self.router_bias, self.corr_bias,
                       None if self.all_hot else self.table, self.shared_slots,
                       self.ids[:m], self.w[:m], self.slots[:m], self.ws_logits, self.ws_count, self.k, self.mode,
                       self.n_group, self.topk_group,
                       self.renorm, self.scale, self.layer,
-                      self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0, active)
+                      self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0, active, logits)
 
     def experts_gpu(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None, use_mailbox: bool,
                     out_f32: torch.Tensor | None = None):
@@ -135,18 +156,26 @@ class TieredMoE:
         if grouped:   # every expert on the GPU: cold ones uploaded once for the whole call, larger chunks
             stage = None if self.all_hot else self._staged()
             chunk = 8192
-        for s in range(0, x.shape[0], chunk):
-            e = min(x.shape[0], s + chunk)
-            if grouped:
-                self._prefill_grouped(x[s:e], out[s:e], None if add is None else add[s:e], stage)
-            else:
-                self._prefill_chunk(x[s:e], out[s:e], None if add is None else add[s:e])
+        pf = self._prefill_bufs(min(chunk, x.shape[0]))
+        saved = {k: getattr(self, k) for k in _BUF_NAMES}, self.max_m
+        for k in _BUF_NAMES:
+            setattr(self, k, pf[k])
+        self.max_m = pf['ids'].shape[0]
+        try:
+            for s in range(0, x.shape[0], chunk):
+                e = min(x.shape[0], s + chunk)
+                if grouped:
+                    self._prefill_grouped(x[s:e], out[s:e], None if add is None else add[s:e], stage)
+                else:
+                    self._prefill_chunk(x[s:e], out[s:e], None if add is None else add[s:e])
+        finally:
+            for k, v in saved[0].items():
+                setattr(self, k, v)
+            self.max_m = saved[1]
         return out
 
     def _prefill_chunk(self, x, out, add):
         m = x.shape[0]
-        if m > self.max_m:
-            self._alloc(max(m, self.max_m))
         self.route(x, False)
         cpu_thread = None
         cpu_out = None
@@ -183,22 +212,17 @@ class TieredMoE:
         """Prefill on the tensor cores: the hot (and shared) routes on the slot pool, the other routes on a staging
         copy of the layer's cold experts uploaded from pinned host memory (the PCIe copy is the cost; every cold expert
         is read once per call instead of once per 8 tokens by the CPU engine)."""
-        from .prefill import grouped_experts
+        from .prefill import combine, grouped_routes
         m = x.shape[0]
-        if m > self.max_m:
-            self._alloc(max(m, self.max_m))
         self.route(x, False)
         slots, w = self.slots[:m], self.w[:m]
-        total = grouped_experts(x, slots, w, self.pool)
+        parts = [grouped_routes(x, slots, w, self.pool)]
         if not self.all_hot:
             ids = self.ids[:m, :self.k]
             cold = torch.where(slots[:, :self.k] < 0, self._cold_index[ids.long().clamp_min(0)],
                                torch.full_like(ids, -1))
-            total += grouped_experts(x, cold, w[:, :self.k], stage)
-        if add is not None:
-            total += add.float()
-        out.copy_(total.to(out.dtype))
-        return out
+            parts.append(grouped_routes(x, cold, w[:, :self.k], stage))
+        return combine(parts, out, None if add is None else add.contiguous())
 
     def upload_async(self, stream: torch.cuda.Stream, after: torch.cuda.Event | None = None):
         """Starts this layer's cold-expert upload on `stream` (after `after`, e.g. the previous user of the staging

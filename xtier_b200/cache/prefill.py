@@ -56,37 +56,58 @@ def _tiles(runs: torch.Tensor, n_tiles: int, device) -> torch.Tensor:
     return t.to(torch.int32).to(device, non_blocking=True)
 
 
-def grouped_experts(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: ExpertWeights,
-                    err: torch.Tensor | None = None) -> torch.Tensor:
-    """x [m, H] BF16, slots [m, k] GPU slot per route (-1 skips), w [m, k] route weights -> FP32 [m, H]: the sum over
-    each token's GPU routes of w * MoE_expert(x), in route order."""
+def grouped_routes(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: ExpertWeights,
+                   err: torch.Tensor | None = None):
+    """x [m, H] BF16, slots [m, k] GPU slot per route (-1 skips), w [m, k] route weights -> (Y [R, H] FP32: every
+    computed route's w * MoE_expert(x) row, dest [m * k] int32: the Y row of each route or -1); (None, None) when no
+    route has a slot. Token rows are gathered into the padded per-expert runs by a kernel (csrc/cuda/moe_prefill.cu
+    gather_rows); the down GEMM's epilogue applies the route weight."""
     m, k = slots.shape
     H, I = pool.hidden, pool.inter
     dev = x.device
-    out = torch.zeros(m, H, dtype=torch.float32, device=dev)
     order, rows, R, runs = plan(slots)
     if runs.shape[0] == 0:
-        return out
+        return None, None
     if H % 128 or I % 64:
         raise ValueError('grouped prefill needs H % 128 == 0 and I % 64 == 0')
-    tok = order // k
-    X = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
-    X[rows] = x[tok]
+    ops.load()
+    src = torch.full((R,), -1, dtype=torch.int32, device=dev)
+    src[rows] = (order // k).int()
+    X = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+    torch.ops.xtier.gather_rows(x.contiguous(), src, X)
     rw = torch.zeros(R, dtype=torch.float32, device=dev)
     rw[rows] = w.flatten().float()[order]
     err = torch.zeros(1, dtype=torch.int32, device=dev) if err is None else err
     fmt = 0 if pool.fmt == NVFP4 else 1
-    ops.load()
     mid = torch.empty(R, I, dtype=torch.bfloat16, device=dev)
     torch.ops.xtier.moe_grouped(X, pool.w13, pool.s13, pool.g13.float().contiguous(), _tiles(runs, I // 64, dev), True,
                                 I, fmt, None, mid, err)
     Y = torch.empty(R, H, dtype=torch.float32, device=dev)
     torch.ops.xtier.moe_grouped(mid, pool.w2, pool.s2, pool.g2.float().contiguous(), _tiles(runs, H // 128, dev),
                                 False, I, fmt, rw, Y, err)
-    # route-ordered sum per token: Y row of route (t, j) or zero
-    dest = torch.full((m * k,), -1, dtype=torch.long, device=dev)
-    dest[order] = rows.long()
-    per_route = torch.where(dest[:, None] >= 0, Y[dest.clamp_min(0)], torch.zeros((), device=dev)).view(m, k, H)
-    for j in range(k):
-        out += per_route[:, j]
+    dest = torch.full((m * k,), -1, dtype=torch.int32, device=dev)
+    dest[order] = rows.int()
+    return Y, dest
+
+
+def combine(parts, out: torch.Tensor, add: torch.Tensor | None = None) -> torch.Tensor:
+    """out [m, H] (BF16 or FP32) = per token, the sum of its routes' rows in route order over the (Y, dest) parts
+    (a route appears in at most one part) + add; one kernel pass."""
+    parts = [p for p in parts if p[0] is not None]
+    if not parts:
+        if add is None:
+            out.zero_()
+        else:
+            out.copy_(add)
+        return out
+    (Ya, da), (Yb, db) = parts[0], (parts[1] if len(parts) > 1 else (None, None))
+    torch.ops.xtier.route_combine(Ya, da, Yb, db, add, out)
     return out
+
+
+def grouped_experts(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: ExpertWeights,
+                    err: torch.Tensor | None = None) -> torch.Tensor:
+    """x [m, H] BF16, slots [m, k] GPU slot per route (-1 skips), w [m, k] route weights -> FP32 [m, H]: the sum over
+    each token's GPU routes of w * MoE_expert(x), in route order."""
+    out = torch.empty(slots.shape[0], pool.hidden, dtype=torch.float32, device=x.device)
+    return combine([grouped_routes(x, slots, w, pool, err)], out)

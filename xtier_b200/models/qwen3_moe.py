@@ -43,6 +43,25 @@ class Qwen3MoeConfig:
         return Qwen3MoeConfig(**base)
 
 
+def _sdpa(q, k, v, mask, causal: bool):
+    """Prefill attention (GQA). Long sequences are restricted to the fused kernels (flash / cuDNN / memory-efficient),
+    so a shape they cannot take fails instead of falling back to the math path, which materializes T x T scores; when
+    GQA itself is what they cannot take, the KV heads are expanded first."""
+    F = torch.nn.functional
+    if q.shape[2] * k.shape[2] < (1 << 26) or not q.is_cuda:
+        return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, is_causal=causal, enable_gqa=True)
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    fused = [SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
+    try:
+        with sdpa_kernel(fused):
+            return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, is_causal=causal, enable_gqa=True)
+    except RuntimeError:
+        rep = q.shape[1] // k.shape[1]
+        with sdpa_kernel(fused):
+            return F.scaled_dot_product_attention(q, k.repeat_interleave(rep, 1), v.repeat_interleave(rep, 1),
+                                                  attn_mask=mask, is_causal=causal)
+
+
 def zipf_temperature(E: int, k: int, s: float, logit_std: float, hot_fraction: float = 0.4, seed: int = 0) -> float:
     """Strength tau of the router bias tau * log(p_zipf) for which the experts' measured route shares follow the
     Zipf(s) popularity: the hot_fraction most popular experts receive the Zipf head mass of the routes after top-k
@@ -271,12 +290,11 @@ class Qwen3MoeModel:
             vv = st['v'][li][row:row + 1, :, :start + T]
             qq = q.transpose(0, 1).unsqueeze(0)
             if start == 0 or T == 1:
-                attn = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=(start == 0),
-                                                                        enable_gqa=True)
+                attn = _sdpa(qq, kk, vv, None, start == 0)
             else:   # a continuation chunk: query i sees keys up to position start + i
                 mask = (torch.arange(start + T, device=dev)[None, :] <=
                         (start + torch.arange(T, device=dev))[:, None])
-                attn = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, enable_gqa=True)
+                attn = _sdpa(qq, kk, vv, mask, False)
             o = ops.linear(attn[0].transpose(0, 1).reshape(T, -1).contiguous(), L['o'])
             ops.add_rmsnorm(o, residual, L['post_norm'], h, cfg.eps)
             if copy_stream is not None and li + 1 < len(self.layers):

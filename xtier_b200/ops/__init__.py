@@ -66,11 +66,20 @@ def attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits
 
 def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k: int, mode: int = 0,
               n_group: int = 1, topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0,
-              mailbox: int = 0, active=None):
+              mailbox: int = 0, active=None, logits_in=None):
     """`active` (int32 [m], optional): token flags; a token with flag 0 skips its routed experts (GPU and CPU),
-    e.g. a verify token after a truncated draft."""
+    e.g. a verify token after a truncated draft. `logits_in` (fp32 [m, E], prefill): precomputed router logits; the
+    kernel only selects (one CTA per token)."""
     _ops().moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k, mode, n_group,
-                     topk_group, renorm, scale, layer, mailbox, active)
+                     topk_group, renorm, scale, layer, mailbox, active, logits_in)
+
+
+def gemm_f32(a, b, out=None):
+    """a [M, K] . b [N, K]^T on the tensor cores with an FP32 result (BF16 operands)."""
+    M = a.numel() // a.shape[-1]
+    out = torch.empty(M, b.shape[0], dtype=torch.float32, device=a.device) if out is None else out
+    _ops().gemm_tc_f32(a, b, out, gemm_error_word(a.device))
+    return out
 
 
 def gemv(x, w, out, add=None):
