@@ -26,183 +26,227 @@
 namespace xt {
 
 
-constexpr int ROUTE_THREADS = 256;
-constexpr int ROUTE_WARPS = ROUTE_THREADS / 32;   // one expert row per warp in phase A
+constexpr int ROUTE_THREADS = 512;
+constexpr int ROUTE_WARPS = ROUTE_THREADS / 32;
+constexpr int ROUTE_CLUSTER = 8;   // CTAs per token (a portable cluster size)
 constexpr int MAX_E = 512;
 
-// Phase A (every CTA): logits of ROUTE_WARPS experts of token blockIdx.y, one warp per expert, all of a row's 16-byte
-// loads in flight at once (H <= 8192). Phase B (the last CTA of the token to finish): selection, split and mailbox.
-__global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p, XtMailbox mb, int use_mb) {
+// One warp selects token t's routes from its logits (shared `logits`, `sel` of E floats, `chosen`, `chosen_w` of k):
+// selection values (softmax, or sigmoid + correction bias with group pruning), top-k (ties: lower id), weights
+// (renormalized, scaled). Lane j < k + n_shared gets route j: (expert or -1 for a shared expert, weight, slot).
+XT_DEV void route_select(const RouteParams &p, int t, float *logits, float *sel, int *chosen, float *chosen_w, int lane,
+                         const int32_t *table, const float *corr, int &e_out, float &w_out, int &slot_out) {
+    const int kk = p.k + p.n_shared;
+    // scores -> selection values
+    if (p.mode == 0) {   // softmax over all experts
+        float mx = -INFINITY;
+        for (int e = lane; e < p.E; e += 32) mx = fmaxf(mx, logits[e]);
+        mx = warp_max(mx);
+        float s = 0.f;
+        for (int e = lane; e < p.E; e += 32) s += __expf(logits[e] - mx);
+        s = warp_sum(s);
+        for (int e = lane; e < p.E; e += 32) {
+            float v = __expf(logits[e] - mx) / s;
+            logits[e] = v;
+            sel[e] = v;
+        }
+    } else {   // sigmoid scores; selection adds the correction bias; groups by the sum of their top two
+        for (int e = lane; e < p.E; e += 32) {
+            float v = 1.f / (1.f + __expf(-logits[e]));
+            logits[e] = v;
+            sel[e] = v + (corr ? corr[e] : 0.f);
+        }
+        __syncwarp();
+        if (p.n_group > 1) {
+            const int gs = p.E / p.n_group;
+            float gscore = -INFINITY;
+            if (lane < p.n_group) {
+                float a = -INFINITY, b = -INFINITY;
+                for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
+                    float v = sel[e];
+                    if (v > a) {
+                        b = a;
+                        a = v;
+                    } else if (v > b) {
+                        b = v;
+                    }
+                }
+                gscore = a + b;
+            }
+            unsigned keep = 0;
+            for (int r = 0; r < p.topk_group; ++r) {
+                float v = (lane < p.n_group && !((keep >> lane) & 1)) ? gscore : -INFINITY;
+                float bv = v;
+                int bi = lane;
+                for (int o = 16; o > 0; o >>= 1) {
+                    float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > bv || (ov == bv && oi < bi)) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                keep |= 1u << bi;
+            }
+            __syncwarp();
+            for (int e = lane; e < p.E; e += 32)
+                if (!((keep >> (e / gs)) & 1)) sel[e] = -INFINITY;
+        }
+    }
+    __syncwarp();
+    // top-k by selection value (ties: lower expert id)
+    for (int r = 0; r < p.k; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < p.E; e += 32)
+            if (sel[e] > bv) {
+                bv = sel[e];
+                bi = e;
+            }
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            const bool ok = bi < p.E && bv > -INFINITY;   // fewer eligible experts than k: a zero-weight route
+            chosen[r] = ok ? bi : 0;
+            chosen_w[r] = ok ? logits[bi] : 0.f;
+            if (ok) sel[bi] = -INFINITY;
+        }
+        __syncwarp();
+    }
+    if (lane == 0) {
+        float s = 0.f;
+        for (int r = 0; r < p.k; ++r) s += chosen_w[r];
+        float f = (p.renorm && s > 0.f ? 1.f / s : 1.f) * p.scale;
+        for (int r = 0; r < p.k; ++r) chosen_w[r] *= f;
+    }
+    __syncwarp();
+    e_out = -1;
+    w_out = 0.f;
+    slot_out = -1;
+    if (lane < p.k && p.active && !p.active[t]) return;   // flagged off: no routed expert anywhere
+    if (lane < p.k) {
+        e_out = chosen[lane];
+        w_out = chosen_w[lane];
+        slot_out = table ? table[e_out] : e_out;
+    } else if (lane < kk) {
+        w_out = 1.f;
+        slot_out = p.shared_slots[lane - p.k];
+    }
+}
+
+// Prefill selection: logits precomputed (the FP32 router GEMM); one warp per token, eight tokens per CTA.
+constexpr int SEL_WARPS = 8;
+
+__global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteParams p) {
+    __shared__ float logits[SEL_WARPS][MAX_E];
+    __shared__ float sel[SEL_WARPS][MAX_E];
+    __shared__ int chosen[SEL_WARPS][XT_MB_MAX_ROUTES];
+    __shared__ float chosen_w[SEL_WARPS][XT_MB_MAX_ROUTES];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = blockIdx.x * SEL_WARPS + warp;
+    if (t >= p.m) return;
+    for (int e = lane; e < p.E; e += 32)
+        logits[warp][e] = p.logits_in[size_t(t) * p.E + e] + (p.bias ? p.bias[e] : 0.f);
+    __syncwarp();
+    int e, slot;
+    float wv;
+    route_select(p, t, logits[warp], sel[warp], chosen[warp], chosen_w[warp], lane, p.table, p.corr, e, wv, slot);
+    const int kk = p.k + p.n_shared;
+    if (lane < kk) {
+        const size_t o = size_t(t) * kk + lane;
+        p.ids[o] = e;
+        p.w[o] = wv;
+        p.slots[o] = slot;
+    }
+}
+
+// Decode router, one cluster of ROUTE_CLUSTER CTAs per token (blockIdx.y): every warp of the cluster computes whole
+// expert rows (16-byte loads, all of a row's loads in flight, FP32 sums) and stores the logit straight into the
+// leader CTA's shared memory (st.shared::cluster); one cluster barrier (release / acquire) hands them over, and the
+// leader's warp 0 selects (route_select) and writes the routes. The leader also prefetches the bias, correction bias
+// and residency table into its shared memory and, with the mailbox, copies the token's activations into the mapped
+// slot of the CPU tier while the rows stream; the last token's leader publishes the request with one system-scope
+// fence. No global scratch, counters or memory fences between CTAs.
+__global__ void __cluster_dims__(ROUTE_CLUSTER, 1, 1) __launch_bounds__(ROUTE_THREADS, 1)
+    moe_route_kernel(RouteParams p, XtMailbox mb, int use_mb) {
     __shared__ float logits[MAX_E];
     __shared__ float sel[MAX_E];
+    __shared__ float bias_s[MAX_E];
+    __shared__ float corr_s[MAX_E];
+    __shared__ int32_t table_s[MAX_E];
     __shared__ int chosen[XT_MB_MAX_ROUTES];
     __shared__ float chosen_w[XT_MB_MAX_ROUTES];
     __shared__ int any_cpu;
-    __shared__ bool last_cta;
     const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t rank = tc::cluster_rank();
     const int kk = p.k + p.n_shared;
-    const __nv_bfloat16 *xt = p.x + size_t(t) * p.H;
-    if (p.logits_in) {   // prefill: logits from the tensor-core GEMM, one CTA per token selects (no mailbox)
+    const int chunks = p.H / 8;
+    const uint4 *xg = reinterpret_cast<const uint4 *>(p.x + size_t(t) * p.H);
+    // every CTA of the cluster must have started before the leader's shared memory is written remotely: arrive now,
+    // wait just before the first remote store (the row loads overlap the barrier)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+    if (rank == 0) {
+        if (use_mb) {   // PCIe writes overlap the logits; published below by this CTA
+            uint4 *mbx = reinterpret_cast<uint4 *>(mb.x + size_t(t) * p.H);
+            for (int i = tid; i < chunks; i += ROUTE_THREADS) mbx[i] = xg[i];
+        }
+        for (int e = tid; e < p.E; e += ROUTE_THREADS) {
+            bias_s[e] = p.bias ? p.bias[e] : 0.f;
+            corr_s[e] = p.corr ? p.corr[e] : 0.f;
+            table_s[e] = p.table ? p.table[e] : e;
+        }
         if (tid == 0) any_cpu = 0;
-        for (int e = tid; e < p.E; e += ROUTE_THREADS)
-            logits[e] = p.logits_in[size_t(t) * p.E + e] + (p.bias ? p.bias[e] : 0.f);
-        __syncthreads();
-    } else {
-    if (use_mb) {   // this CTA's slice of the token's activations to the mailbox slot first: the PCIe writes overlap
-        const uint4 *src = reinterpret_cast<const uint4 *>(xt);   // the logits and are long done at publication
-        uint4 *dst = reinterpret_cast<uint4 *>(mb.x + size_t(t) * p.H);
-        const int n = p.H / 8, per = (n + gridDim.x - 1) / gridDim.x;
-        for (int i = blockIdx.x * per + tid; i < min(n, (blockIdx.x + 1) * per); i += ROUTE_THREADS) dst[i] = src[i];
     }
-    {
-        const int e = blockIdx.x * ROUTE_WARPS + warp;
-        if (e < p.E) {
-            const uint4 *we = reinterpret_cast<const uint4 *>(p.wr + size_t(e) * p.H);
-            const uint4 *xv = reinterpret_cast<const uint4 *>(xt);
-            const int chunks = p.H / 8;   // 16-byte chunks, multiple of 32 (H % 256 == 0)
-            uint4 wb[32];
+    const int gw = int(rank) * ROUTE_WARPS + warp;
+    bool waited = false;
+    for (int e = gw; e < p.E; e += ROUTE_CLUSTER * ROUTE_WARPS) {
+        const uint4 *we = reinterpret_cast<const uint4 *>(p.wr + size_t(e) * p.H);
+        float acc = 0.f;
+        for (int c0 = 0; c0 < chunks; c0 += 32 * 8) {
+            uint4 r[8], xv[8];
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (i * 32 < chunks) wb[i] = ldg_nc_v4(we + i * 32 + lane);
-            float acc = 0.f;
+            for (int i = 0; i < 8; ++i) {
+                const int c = c0 + i * 32 + lane;
+                r[i] = c < chunks ? ldg_nc_v4(we + c) : make_uint4(0, 0, 0, 0);
+                xv[i] = c < chunks ? xg[c] : make_uint4(0, 0, 0, 0);
+            }
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                if (i * 32 >= chunks) break;
-                const uint4 a = xv[i * 32 + lane];
-                const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
-                const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&wb[i]);
+            for (int i = 0; i < 8; ++i) {
+                const __nv_bfloat162 *x2 = reinterpret_cast<const __nv_bfloat162 *>(&xv[i]);
+                const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&r[i]);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    float2 fa = __bfloat1622float2(a2[j]), fb = __bfloat1622float2(b2[j]);
-                    acc = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, acc));
+                    const float2 fx = __bfloat1622float2(x2[j]), fw = __bfloat1622float2(w2[j]);
+                    acc = fmaf(fx.x, fw.x, fmaf(fx.y, fw.y, acc));
                 }
             }
-            acc = warp_sum(acc);
-            if (lane == 0) p.ws_logits[size_t(t) * p.E + e] = acc + (p.bias ? p.bias[e] : 0.f);
         }
+        acc = warp_sum(acc);
+        if (!waited) {
+            asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+            waited = true;
+        }
+        if (lane == 0)
+            asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(tc::mapa(&logits[e], 0)), "f"(acc) : "memory");
     }
-    __threadfence();
+    if (!waited) asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+    tc::cluster_sync();   // every logit is in the leader's shared memory
+    if (rank != 0) return;
+    for (int e = tid; e < p.E; e += ROUTE_THREADS) logits[e] += bias_s[e];
     __syncthreads();
-    if (tid == 0) {
-        if (use_mb) __threadfence_system();   // the slice of x above, before the count
-        const unsigned prev = atomicAdd(&p.ws_count[t], 1u);
-        last_cta = prev == gridDim.x - 1;
-        if (last_cta) p.ws_count[t] = 0;   // ready for the next call
-        any_cpu = 0;
-    }
-    __syncthreads();
-    if (!last_cta) return;
-    __threadfence();
-    for (int e = tid; e < p.E; e += ROUTE_THREADS) logits[e] = __ldcg(p.ws_logits + size_t(t) * p.E + e);
-    __syncthreads();
-    }   // phase A
 
     if (warp == 0) {
-        // scores -> selection values
-        if (p.mode == 0) {   // softmax over all experts
-            float mx = -INFINITY;
-            for (int e = lane; e < p.E; e += 32) mx = fmaxf(mx, logits[e]);
-            mx = warp_max(mx);
-            float s = 0.f;
-            for (int e = lane; e < p.E; e += 32) s += __expf(logits[e] - mx);
-            s = warp_sum(s);
-            for (int e = lane; e < p.E; e += 32) {
-                float v = __expf(logits[e] - mx) / s;
-                logits[e] = v;
-                sel[e] = v;
-            }
-        } else {   // sigmoid scores; selection adds the correction bias; groups by the sum of their top two
-            for (int e = lane; e < p.E; e += 32) {
-                float v = 1.f / (1.f + __expf(-logits[e]));
-                logits[e] = v;
-                sel[e] = v + (p.corr ? p.corr[e] : 0.f);
-            }
-            __syncwarp();
-            if (p.n_group > 1) {
-                const int gs = p.E / p.n_group;
-                float gscore = -INFINITY;
-                if (lane < p.n_group) {
-                    float a = -INFINITY, b = -INFINITY;
-                    for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
-                        float v = sel[e];
-                        if (v > a) {
-                            b = a;
-                            a = v;
-                        } else if (v > b) {
-                            b = v;
-                        }
-                    }
-                    gscore = a + b;
-                }
-                unsigned keep = 0;
-                for (int r = 0; r < p.topk_group; ++r) {
-                    float v = (lane < p.n_group && !((keep >> lane) & 1)) ? gscore : -INFINITY;
-                    float bv = v;
-                    int bi = lane;
-                    for (int o = 16; o > 0; o >>= 1) {
-                        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                        if (ov > bv || (ov == bv && oi < bi)) {
-                            bv = ov;
-                            bi = oi;
-                        }
-                    }
-                    keep |= 1u << bi;
-                }
-                __syncwarp();
-                for (int e = lane; e < p.E; e += 32)
-                    if (!((keep >> (e / gs)) & 1)) sel[e] = -INFINITY;
-            }
-        }
-        __syncwarp();
-        // top-k by selection value (ties: lower expert id)
-        for (int r = 0; r < p.k; ++r) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            for (int e = lane; e < p.E; e += 32)
-                if (sel[e] > bv) {
-                    bv = sel[e];
-                    bi = e;
-                }
-            for (int o = 16; o > 0; o >>= 1) {
-                float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if (lane == 0) {
-                const bool ok = bi < p.E && bv > -INFINITY;   // fewer eligible experts than k: a zero-weight route
-                chosen[r] = ok ? bi : 0;
-                chosen_w[r] = ok ? logits[bi] : 0.f;
-                if (ok) sel[bi] = -INFINITY;
-            }
-            __syncwarp();
-        }
-        if (lane == 0) {
-            float s = 0.f;
-            for (int r = 0; r < p.k; ++r) s += chosen_w[r];
-            float f = (p.renorm && s > 0.f ? 1.f / s : 1.f) * p.scale;
-            for (int r = 0; r < p.k; ++r) chosen_w[r] *= f;
-        }
-        __syncwarp();
+        int e, slot;
+        float wv;
+        route_select(p, t, logits, sel, chosen, chosen_w, lane, p.table ? table_s : nullptr, p.corr ? corr_s : nullptr,
+                     e, wv, slot);
         if (lane < kk) {
-            int e, slot;
-            float wv;
-            if (lane < p.k && p.active && !p.active[t]) {   // flagged off: no routed expert anywhere
-                e = -1;
-                wv = 0.f;
-                slot = -1;
-            } else if (lane < p.k) {
-                e = chosen[lane];
-                wv = chosen_w[lane];
-                slot = p.table ? p.table[e] : e;
-            } else {
-                e = -1;
-                wv = 1.f;
-                slot = p.shared_slots[lane - p.k];
-            }
             const size_t o = size_t(t) * kk + lane;
             p.ids[o] = e;
             p.w[o] = wv;
@@ -218,11 +262,11 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(RouteParams p,
     }
     if (!use_mb) return;
     __syncthreads();
-    // count the token as done; the last token of the call publishes it with a single system fence (x went to the
-    // slot in phase A; the route arrays were written above by this CTA)
+    // count the token as done; the last token of the call publishes it with a single system fence (x and the route
+    // arrays were written by this CTA before the barrier above)
     if (tid == 0) {
         if (any_cpu) atomicOr(&mb.dev->any, 1u);
-        if (p.m > 1) __threadfence_system();   // other tokens' CTAs: their route arrays before the count
+        if (p.m > 1) __threadfence_system();   // other tokens' leaders: their slot rows before the count
         const unsigned prev = atomicAdd(&mb.dev->done, 1u);
         if (prev == unsigned(p.m) - 1) {
             __threadfence();
@@ -533,9 +577,12 @@ int xt_moe_route(const RouteParams *p, const XtMailbox *mb, int use_mb, cudaStre
     if (use_mb && p->m > XT_MB_MAX_TOKENS) return -3;
     if (!p->ws_logits || !p->ws_count) return -5;
     XtMailbox empty{};
-    if (p->logits_in && use_mb) return -6;
-    dim3 grid(p->logits_in ? 1 : (p->E + ROUTE_WARPS - 1) / ROUTE_WARPS, p->m);
-    moe_route_kernel<<<grid, ROUTE_THREADS, 0, stream>>>(*p, use_mb ? *mb : empty, use_mb);
+    if (p->logits_in) {
+        if (use_mb) return -6;
+        route_select_kernel<<<(p->m + SEL_WARPS - 1) / SEL_WARPS, SEL_WARPS * 32, 0, stream>>>(*p);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
+    moe_route_kernel<<<dim3(ROUTE_CLUSTER, p->m), ROUTE_THREADS, 0, stream>>>(*p, use_mb ? *mb : empty, use_mb);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
