@@ -17,6 +17,8 @@
 // attention of the Qwen3-style config (GQA 32/4, head dim 128).
 #include "common.cuh"
 #include "params.h"
+#include "tc_common.cuh"
+#include <stdlib.h>
 
 namespace xt {
 
@@ -238,6 +240,310 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0;
 }
 
+
+// ---------------------------------------------------------------------------------------------------------------
+// Tensor-core variant for query groups of 8 or 16 heads (mma.sync m16n8k16, BF16 in, FP32 accumulate).
+//
+// The G heads of a KV head are the 16 rows of the MMA's A operand (rows past G are zero). A CTA of AM_WARPS warps
+// takes one split of the keys; every warp walks its own 16-key blocks (block i of the split goes to warp i % 4) with
+// its own online softmax, so no CTA-wide barrier sits in the key loop:
+//   S = Q K^T   the contraction over the 128 dims is permuted (the same permutation for Q and K, so the dot products
+//               are unchanged) such that thread (g, t) of the warp needs dims 32t..32t+31 of key g of each 8-key
+//               tile: four 16-byte global loads per key tile, the 16 fragments of Q held in registers all along;
+//   softmax     per head row: two shuffles for the max, the sum kept per thread and reduced once at the end;
+//   O += P V    P comes straight from the S accumulators (re-packed as the A operand); V goes through shared memory
+//               (cp.async, 16-byte chunks, XOR-swizzled by key) and ldmatrix.trans builds its fragments.
+// The next block's K fragments and V tile are in flight while the current block computes (double buffer). At the
+// end the CTA merges its warps in shared memory and writes the split's partial; the last split of a (batch, KV head)
+// merges the splits, as in the kernel above.
+constexpr int AM_WARPS = 4;
+constexpr int AM_KB = 16;   // keys per warp block
+
+template <int G>
+struct AmSmem {
+    static constexpr size_t V = size_t(AM_WARPS) * 2 * AM_KB * AD_D * 2;   // 32 KB: per warp, two V tiles
+    static constexpr size_t O = size_t(AM_WARPS) * G * AD_D * 4;          // warp partials
+    static constexpr size_t ML = size_t(AM_WARPS) * G * 2 * 4;
+    static constexpr size_t MERGE = size_t(AD_MAX_SPLITS) * G * 2 * 4 + size_t(AD_MAX_SPLITS) * G * 4;
+    static constexpr size_t BYTES = V + (O > MERGE ? O : MERGE) + ML + 64;
+};
+
+XT_DEV void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                           uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};\n"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+XT_DEV uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+XT_DEV uint4 ldg_v4(const void *p) { return *reinterpret_cast<const uint4 *>(p); }
+
+// one warp's block: K fragments of keys [kb, kb + 16) (clamped to `last`) into registers, V tile into shared memory
+XT_DEV void am_load(const __nv_bfloat16 *K, const __nv_bfloat16 *V, int kb, int last, int lane, uint4 (&kf)[2][4],
+                    uint8_t *vt) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int key = min(kb + j * 8 + g, last);
+        const uint8_t *row = reinterpret_cast<const uint8_t *>(K + size_t(key) * AD_D) + t * 64;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) kf[j][c] = ldg_v4(row + c * 16);
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const int i = lane + 32 * r;           // chunk of the 16 x 16 chunks of the tile
+        const int key = i >> 4, ch = i & 15;
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(V + size_t(min(kb + key, last)) * AD_D) + ch * 16;
+        const uint32_t dst = tc::smem_u32(vt + key * 256 + ((ch ^ (key & 7)) << 4));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+template <int G>
+XT_DEV void am_block(const uint32_t (&qa)[8][4], const uint4 (&kf)[2][4], const uint8_t *vt, int kb, int kend,
+                     float scale_log2, int lane, float (&o)[16][4], float (&m)[2], float (&l)[2]) {
+    const int t = lane & 3;
+    float sc[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+        const uint32_t *kw = reinterpret_cast<const uint32_t *>(&kf[j][0]);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) mma_bf16_16816(sc[j], qa[s][0], qa[s][1], qa[s][2], qa[s][3], kw[2 * s], kw[2 * s + 1]);
+    }
+    // scale, mask, online softmax per row (r = 0: head g, r = 1: head g + 8)
+    uint32_t pa[4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (r == 1 && G <= 8) {
+            pa[1] = pa[3] = 0u;
+            continue;
+        }
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int key = kb + j * 8 + t * 2 + e;
+                v[j * 2 + e] = key < kend ? sc[j][r * 2 + e] * scale_log2 : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m[r], mx);
+        const float alpha = mn == -INFINITY ? 1.f : exp2f(m[r] - mn);
+        float pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pr[i] = v[i] == -INFINITY ? 0.f : exp2f(v[i] - mn);
+        l[r] = l[r] * alpha + pr[0] + pr[1] + pr[2] + pr[3];
+        m[r] = mn;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+            o[nt][r * 2] *= alpha;
+            o[nt][r * 2 + 1] *= alpha;
+        }
+        pa[r] = pack_bf16(pr[0], pr[1]);       // keys t*2, t*2+1 of tile 0
+        pa[r + 2] = pack_bf16(pr[2], pr[3]);   // keys 8+t*2, 8+t*2+1 of tile 1
+    }
+    // O += P V: V^T fragments by ldmatrix.trans from the swizzled tile
+    const int key = (lane & 7) + ((lane >> 3) & 1) * 8, half = lane >> 4;
+#pragma unroll
+    for (int nt = 0; nt < 16; nt += 2) {
+        const int ch = nt + half;   // 16-byte chunk = 8 dims
+        const uint32_t addr = tc::smem_u32(vt + key * 256 + ((ch ^ (key & 7)) << 4));
+        uint32_t b0, b1, b2, b3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+                     : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
+                     : "r"(addr));
+        mma_bf16_16816(o[nt], pa[0], pa[1], pa[2], pa[3], b0, b1);
+        mma_bf16_16816(o[nt + 1], pa[0], pa[1], pa[2], pa[3], b2, b3);
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(AM_WARPS * 32) attn_decode_mma_kernel(AttnDecodeParams p) {
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+    extern __shared__ __align__(128) uint8_t dsm[];
+    uint8_t *vtiles = dsm + size_t(warp) * 2 * AM_KB * 256;
+    float(&os)[AM_WARPS][G][AD_D] = *reinterpret_cast<float(*)[AM_WARPS][G][AD_D]>(dsm + AmSmem<G>::V);
+    float(&mls)[AM_WARPS][G][2] =
+        *reinterpret_cast<float(*)[AM_WARPS][G][2]>(dsm + AmSmem<G>::V + (AmSmem<G>::O > AmSmem<G>::MERGE
+                                                                              ? AmSmem<G>::O
+                                                                              : AmSmem<G>::MERGE));
+    __shared__ bool last;
+
+    const size_t head_off = (size_t(b) * p.Hkv + kvh) * p.L;
+    const __nv_bfloat16 *K = p.kc + head_off * AD_D;
+    const __nv_bfloat16 *V = p.vc + head_off * AD_D;
+    const __nv_bfloat16 *qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * G) * AD_D;
+    // Q fragments (rows g and g + 8 of the permuted 16 x 128 operand): dims 32t..32t+31, words 2s / 2s+1 per step
+    uint32_t qa[8][4];
+    {
+        uint4 q0[4], q1[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            q0[c] = g < G ? ldg_v4(reinterpret_cast<const uint8_t *>(qb + size_t(g) * AD_D) + t * 64 + c * 16)
+                          : make_uint4(0, 0, 0, 0);
+            q1[c] = g + 8 < G ? ldg_v4(reinterpret_cast<const uint8_t *>(qb + size_t(g + 8) * AD_D) + t * 64 + c * 16)
+                              : make_uint4(0, 0, 0, 0);
+        }
+        const uint32_t *w0 = reinterpret_cast<const uint32_t *>(q0), *w1 = reinterpret_cast<const uint32_t *>(q1);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            qa[s][0] = w0[2 * s];
+            qa[s][1] = w1[2 * s];
+            qa[s][2] = w0[2 * s + 1];
+            qa[s][3] = w1[2 * s + 1];
+        }
+    }
+    const int N = min(p.seqlens[b], p.L);
+    const int chunk = (((N + p.splits - 1) / p.splits) + 7) & ~7;
+    const int k_begin = split * chunk;
+    const int k_end = min(N, k_begin + chunk);
+    float o[16][4];
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    const int last_key = max(k_end - 1, 0);
+    const int step = AM_WARPS * AM_KB;
+    int kb = k_begin + warp * AM_KB;
+    if (kb < k_end) {
+        uint4 ka[2][4], kn[2][4];
+        am_load(K, V, kb, last_key, lane, ka, vtiles);
+        for (;;) {
+            const int nb = kb + step;
+            if (nb < k_end) am_load(K, V, nb, last_key, lane, kn, vtiles + AM_KB * 256);
+            if (nb < k_end)
+                asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+            else
+                asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            __syncwarp();
+            am_block<G>(qa, ka, vtiles, kb, k_end, p.scale_log2, lane, o, m, l);
+            __syncwarp();
+            if (nb >= k_end) break;
+            kb = nb;
+            const int nb2 = kb + step;
+            if (nb2 < k_end) am_load(K, V, nb2, last_key, lane, ka, vtiles);
+            if (nb2 < k_end)
+                asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+            else
+                asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            __syncwarp();
+            am_block<G>(qa, kn, vtiles + AM_KB * 256, kb, k_end, p.scale_log2, lane, o, m, l);
+            __syncwarp();
+            if (nb2 >= k_end) break;
+            kb = nb2;
+        }
+    }
+    // ---- this warp's rows to shared memory (sums reduced over the row's four threads)
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
+        const int h = g + r * 8;
+        if (h < G) {
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt) {
+                os[warp][h][nt * 8 + t * 2] = o[nt][r * 2];
+                os[warp][h][nt * 8 + t * 2 + 1] = o[nt][r * 2 + 1];
+            }
+            if (t == 0) {
+                mls[warp][h][0] = m[r];
+                mls[warp][h][1] = l[r];
+            }
+        }
+    }
+    __syncthreads();
+    // ---- merge the warps: this split's unnormalized output, max and sum
+    const size_t part = ((size_t(b) * p.Hkv + kvh) * p.splits + split) * G;
+    for (int i = threadIdx.x; i < G * AD_D; i += blockDim.x) {
+        const int h = i / AD_D, d = i % AD_D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < AM_WARPS; ++w) M = fmaxf(M, mls[w][h][0]);
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < AM_WARPS; ++w) {
+            const float mw = mls[w][h][0];
+            acc += mw == -INFINITY ? 0.f : os[w][h][d] * exp2f(mw - M);
+        }
+        p.ws_o[part * AD_D + i] = acc;
+    }
+    if (threadIdx.x < G) {
+        const int h = threadIdx.x;
+        float M = -INFINITY;
+        for (int w = 0; w < AM_WARPS; ++w) M = fmaxf(M, mls[w][h][0]);
+        float L = 0.f;
+        for (int w = 0; w < AM_WARPS; ++w) {
+            const float mw = mls[w][h][0];
+            L += mw == -INFINITY ? 0.f : mls[w][h][1] * exp2f(mw - M);
+        }
+        p.ws_ml[(part + h) * 2] = M;
+        p.ws_ml[(part + h) * 2 + 1] = L;
+    }
+    // ---- the last split to arrive merges (arrival counter, reset by the merging CTA)
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&p.counters[b * p.Hkv + kvh], 1u);
+        last = prev == unsigned(p.splits) - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    float *msp = reinterpret_cast<float *>(dsm + AmSmem<G>::V);         // [splits][G][2]
+    float *wsp = msp + AD_MAX_SPLITS * G * 2;                            // [splits][G]
+    const size_t base = (size_t(b) * p.Hkv + kvh) * p.splits * G;
+    for (int i = threadIdx.x; i < p.splits * G * 2; i += blockDim.x) msp[i] = __ldcg(p.ws_ml + base * 2 + i);
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int h = threadIdx.x;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, msp[(s2 * G + h) * 2]);
+        float L = 0.f;
+        for (int s2 = 0; s2 < p.splits; ++s2) {
+            const float ms = msp[(s2 * G + h) * 2];
+            const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
+            wsp[s2 * G + h] = f;
+            L += msp[(s2 * G + h) * 2 + 1] * f;
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        for (int s2 = 0; s2 < p.splits; ++s2) wsp[s2 * G + h] *= inv;
+    }
+    __syncthreads();
+    const size_t stride4 = size_t(G) * AD_D / 4;
+    for (int i = threadIdx.x * 4; i < G * AD_D; i += blockDim.x * 4) {
+        const int h = i / AD_D;
+        const float4 *src = reinterpret_cast<const float4 *>(p.ws_o + base * AD_D + i);
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < p.splits; s0 += 16) {
+            float4 v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                v[j] = s0 + j < p.splits ? __ldcg(src + (s0 + j) * stride4) : make_float4(0, 0, 0, 0);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float wgt = s0 + j < p.splits ? wsp[(s0 + j) * G + h] : 0.f;
+                O.x += v[j].x * wgt;
+                O.y += v[j].y * wgt;
+                O.z += v[j].z * wgt;
+                O.w += v[j].w * wgt;
+            }
+        }
+        __nv_bfloat16 *dst = p.out + (size_t(b) * p.Hq + size_t(kvh) * G + h) * AD_D + i % AD_D;
+        reinterpret_cast<__nv_bfloat162 *>(dst)[0] = __floats2bfloat162_rn(O.x, O.y);
+        reinterpret_cast<__nv_bfloat162 *>(dst)[1] = __floats2bfloat162_rn(O.z, O.w);
+    }
+    if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0;
+}
+
 }  // namespace xt
 
 using namespace xt;
@@ -247,6 +553,26 @@ extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t st
     const int G = p.Hq / p.Hkv;
     if (p.Hq % p.Hkv || p.splits < 1 || p.splits > AD_MAX_SPLITS) return -2;
     dim3 grid(p.splits, p.Hkv, B);
+    static const bool legacy = [] {   // XTIER_ATTN_CUDA_CORES=1: the CUDA-core kernel for every group size
+        const char *v = getenv("XTIER_ATTN_CUDA_CORES");
+        return v && atoi(v) != 0;
+    }();
+    if (!legacy && (G == 8 || G == 16)) {
+#define XT_AM(GG)                                                                                                  \
+        {                                                                                                          \
+            static bool attr = false;                                                                              \
+            const int smem = int(AmSmem<GG>::BYTES);                                                               \
+            if (!attr) {                                                                                           \
+                cudaFuncSetAttribute(attn_decode_mma_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                     smem);                                                                        \
+                attr = true;                                                                                       \
+            }                                                                                                      \
+            attn_decode_mma_kernel<GG><<<grid, AM_WARPS * 32, smem, stream>>>(p);                                  \
+        }
+        if (G == 8) XT_AM(8) else XT_AM(16)
+#undef XT_AM
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
 #define XT_AD(GG)                                                                                                  \
     case GG: {                                                                                                     \
         static bool attr = false;                                                                                  \

@@ -251,3 +251,33 @@ def test_tiny_qwen3_prefill_and_decode_match_fp32_reference(cuda_ops):
     gen2.step()
     ref2 = model.reference_logits(seq.cuda())
     assert _rel(gen2.buf['logits'][0], ref2) < 3e-2, _rel(gen2.buf['logits'][0], ref2)
+
+
+@pytest.mark.parametrize('G,N,splits', [(8, 2084, 36), (8, 33, 37), (16, 1000, 8), (8, 32768, 37), (8, 5000, 3)])
+def test_attn_decode_tensor_core_path(cuda_ops, G, N, splits):
+    """The mma.sync path (query groups of 8 / 16 heads): uneven splits, blocks past the end of a split, more keys per
+    warp than one block (double-buffered loads), against the fp32 reference."""
+    torch.manual_seed(G + N)
+    B, Hkv, D = 2, 2, 128
+    L = N + 64
+    Hq = Hkv * G
+    q = torch.randn(B, Hq, D, device='cuda').bfloat16()
+    kc = torch.randn(B, Hkv, L, D, device='cuda').bfloat16()
+    vc = torch.randn(B, Hkv, L, D, device='cuda').bfloat16()
+    lens = torch.tensor([N, max(1, N // 3)], dtype=torch.int32, device='cuda')
+    ws_o = torch.empty(B * Hkv * splits * G * D, device='cuda')
+    ws_ml = torch.empty(B * Hkv * splits * G * 2, device='cuda')
+    cnt = torch.zeros(B * Hkv, dtype=torch.int32, device='cuda')
+    out = torch.empty_like(q)
+    scale = 1 / math.sqrt(D)
+    for _ in range(2):
+        cuda_ops.attn_decode(q, kc, vc, lens, out, ws_o, ws_ml, cnt, splits, scale)
+    torch.cuda.synchronize()
+    for b in range(B):
+        n = int(lens[b])
+        k = kc[b, :, :n].float().repeat_interleave(G, 0)
+        v = vc[b, :, :n].float().repeat_interleave(G, 0)
+        s = torch.einsum('hd,hnd->hn', q[b].float(), k) * scale
+        ref = torch.einsum('hn,hnd->hd', s.softmax(-1), v)
+        assert _rel(out[b], ref) < 1e-2, (b, _rel(out[b], ref))
+    assert int(cnt.sum()) == 0

@@ -182,8 +182,9 @@ def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, ma
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
-    """Key splits of the decode attention: enough CTAs (splits x batch x kv_heads) to cover every SM about once, at
-    most one per 64 keys of the cache and at most 64 (the merge reads every split's partial). The kernel cuts the
-    splits from the actual sequence length, so all of them have work."""
+    """Key splits of the decode attention: about 192 keys of the cache per split (measured on B200 with the tensor-core
+    kernel: fewer, longer splits lose to the load latency, more lose to the merge), at most enough CTAs (splits x batch
+    x kv_heads) to cover every SM once, at most 64 (the merge reads every split's partial). The kernel cuts the splits
+    from the actual sequence length, so all of them have work."""
     want = max(1, (sms + batch * kv_heads - 1) // (batch * kv_heads))
-    return max(1, min(64, want, (max_len + 63) // 64))
+    return max(1, min(64, want, (max_len + 191) // 192))
