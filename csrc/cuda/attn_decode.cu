@@ -663,8 +663,8 @@ int noalloc_setup(int dev) {
 extern "C" {
 
 // q [B, Hq, 128] bf16, k_cache / v_cache [B, Hkv, L, 128] bf16, seqlens [B] int32 (device), out [B, Hq, 128] bf16;
-// all device pointers on the current device. Same result as xt_attn_decode with the same splits. Returns 0; -2 bad
-// arguments; XT_AD_NOALLOC_TOO_BIG when the workspace would exceed the fixed array; a positive CUDA error code from
+// all device pointers on the current device. Runs the CUDA-core kernel for every group size (xt_attn_decode takes
+// the tensor-core kernel for groups of 8 and 16; the two agree to rounding). Returns 0; -2 bad arguments; XT_AD_NOALLOC_TOO_BIG when the workspace would exceed the fixed array; a positive CUDA error code from
 // the set-up; -1 when the launch failed.
 int xt_attn_decode_noalloc(const void *q, const void *k_cache, const void *v_cache, const int32_t *seqlens, void *out,
                            int B, int Hq, int Hkv, int L, int splits, float scale, cudaStream_t stream) {
