@@ -101,6 +101,9 @@ def main():
     ap.add_argument('--layers', type=int, default=48)
     ap.add_argument('--threads', type=int, default=0, help='CPU engine workers per rank (0: auto)')
     ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-peer', action='store_true',
+                    help='N > 1: keep every GPU\'s hot slots to itself (default: the hot slots of all GPUs form one pool '
+                         'read over NVLink)')
     ap.add_argument('--long-prefill', type=int, default=65536,
                     help='also time a warm prefill of this many random tokens (0: skip)')
     ap.add_argument('--profile', type=int, default=0, help='print per-kernel device time of N graph replays and exit')
@@ -140,8 +143,11 @@ def main():
     cfg = Qwen3MoeConfig(layers=args.layers)
     mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
     t0 = time.time()
-    model = Qwen3MoeModel(cfg, device='cuda', seed=1234 + rank, hot_fraction=args.hot, engine_threads=threads,
-                          mailbox=mailbox)
+    peer = world > 1 and not args.no_peer
+    # data parallel replicas of one model (same weights on every GPU); with peer slots each GPU keeps its 40 % budget
+    # of hot slots and reads the experts held by the other GPUs' slots over NVLink
+    model = Qwen3MoeModel(cfg, device='cuda', seed=1234, hot_fraction=args.hot, engine_threads=threads,
+                          mailbox=mailbox, peer=peer)
     if mailbox is not None:
         mailbox.start(cpu=mine[-1])
     os.sched_setaffinity(0, [mine[-2]] if len(mine) >= 2 else mine)   # main thread off the workers' CPUs
@@ -244,6 +250,8 @@ def main():
         'config': {'model': 'qwen3-style MoE 48L H2048 GQA32/4 128E top-8 I768 NVFP4 (BASELINE config 2)',
                    'global_batch': world, 'seq_len': args.prompt + args.warmup + args.steps,
                    'prompt': args.prompt, 'parallelism': f'dp{world}', 'hot_fraction': args.hot,
+                   'hot_slots': ('each GPU holds hot_fraction of the experts; the GPUs\' slots form one pool read '
+                                 'over NVLink peer memory' if peer else 'per GPU'),
                    'cpu_engine_threads': threads, 'layers': cfg.layers,
                    'l2': 'inputs larger than L2: each step streams > 1.8 GB of weights',
                    'weights': 'random-init, experts as random NVFP4 codes and block scales',

@@ -157,7 +157,8 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
 }
 
 void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const Tensor &s13, const Tensor &g13,
-                 const Tensor &mid, int64_t fmt, double limit, double alpha, double beta) {
+                 const Tensor &mid, int64_t fmt, double limit, double alpha, double beta,
+                 const std::optional<Tensor> &peer, int64_t spr) {
     cuda_contig(w13, "w13");
     cuda_contig(s13, "s13");
     GateUpParams p{};
@@ -175,6 +176,10 @@ void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const 
     p.limit = float(limit);
     p.alpha = float(alpha);
     p.beta = float(beta);
+    p.peer = peer ? reinterpret_cast<const unsigned long long *>(peer->data_ptr<int64_t>()) : nullptr;
+    p.spr = int(spr);
+    if (peer) check(peer->is_cuda() && peer->scalar_type() == at::kLong && peer->numel() % 6 == 0 && spr > 0,
+                    "peer: int64 [W * 6] device table and slots per rank");
     check(mid.numel() >= int64_t(p.routes) * p.I, "mid too small");
     check(w13.size(2) * 2 == p.H, "w13 / x hidden mismatch");
     c10::cuda::CUDAGuard g(x.device());
@@ -184,9 +189,13 @@ void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const 
 void moe_down(const Tensor &mid, const Tensor &slots, const Tensor &w, const Tensor &w2, const Tensor &s2,
               const Tensor &g2, const std::optional<Tensor> &add, const Tensor &out,
               const std::optional<Tensor> &out_f32, const std::optional<Tensor> &gpu_part, int64_t fmt,
-              int64_t mailbox) {
+              int64_t mailbox, const std::optional<Tensor> &peer, int64_t spr) {
     cuda_contig(w2, "w2");
     DownParams p{};
+    p.peer = peer ? reinterpret_cast<const unsigned long long *>(peer->data_ptr<int64_t>()) : nullptr;
+    p.spr = int(spr);
+    if (peer) check(peer->is_cuda() && peer->scalar_type() == at::kLong && peer->numel() % 6 == 0 && spr > 0,
+                    "peer: int64 [W * 6] device table and slots per rank");
     p.mid = ptr<const float>(mid);
     p.slots = ptr<const int32_t>(slots);
     p.w = ptr<const float>(w);
@@ -595,9 +604,9 @@ TORCH_LIBRARY(xtier, m) {
     m.def("ag_gemm(Tensor a_shard, Tensor b, Tensor peer, int local_base, Tensor(a!) state, Tensor(b!) out, "
           "Tensor(c!) err, int W, int rank, int[] offsets, float timeout_s) -> ()");
     m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
-          "float limit, float alpha, float beta) -> ()");
+          "float limit, float alpha, float beta, Tensor? peer=None, int spr=0) -> ()");
     m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
-          "Tensor(b!)? out_f32, Tensor(c!)? gpu_part, int fmt, int mailbox) -> ()");
+          "Tensor(b!)? out_f32, Tensor(c!)? gpu_part, int fmt, int mailbox, Tensor? peer=None, int spr=0) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(xtier, CUDA, m) {

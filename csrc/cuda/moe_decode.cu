@@ -379,9 +379,19 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams
     load_x_bf16<LPR, CH>(p.x + size_t(t) * p.H, q, xr);
     const int bs = p.fmt == 0 ? 16 : 32;
     const size_t wrow = p.H / 2, srow = p.H / bs;
-    const uint8_t *W = p.w13 + size_t(slot) * 2 * p.I * wrow;
-    const uint8_t *S = p.s13 + size_t(slot) * 2 * p.I * srow;
-    const float gg = p.g13[2 * slot], gu = p.g13[2 * slot + 1];
+    const uint8_t *w13 = p.w13, *s13 = p.s13;
+    const float *g13 = p.g13;
+    int ls = slot;
+    if (p.peer) {   // the slot's owner: this GPU or a peer (NVLink loads)
+        const int o = slot / p.spr;
+        ls = slot - o * p.spr;
+        w13 = reinterpret_cast<const uint8_t *>(p.peer[o * 6 + 0]);
+        s13 = reinterpret_cast<const uint8_t *>(p.peer[o * 6 + 1]);
+        g13 = reinterpret_cast<const float *>(p.peer[o * 6 + 2]);
+    }
+    const uint8_t *W = w13 + size_t(ls) * 2 * p.I * wrow;
+    const uint8_t *S = s13 + size_t(ls) * 2 * p.I * srow;
+    const float gg = g13[2 * ls], gu = g13[2 * ls + 1];
     const int rows_per_cta = GU_WARPS * RPW;
     const int j_raw = blockIdx.y * rows_per_cta + warp * RPW + sub;
     const int j = min(j_raw, p.I - 1);   // every lane takes part in the group shuffles; out-of-range rows store nothing
@@ -417,8 +427,18 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
     const int r = t * p.kk + j;
     const int slot = p.slots[r];
     if (slot >= 0) {   // warp-uniform
-        const uint8_t *W = p.w2 + size_t(slot) * p.H * wrow;
-        const uint8_t *S = p.s2 + size_t(slot) * p.H * srow;
+        const uint8_t *w2 = p.w2, *s2 = p.s2;
+        const float *g2 = p.g2;
+        int ls = slot;
+        if (p.peer) {
+            const int o = slot / p.spr;
+            ls = slot - o * p.spr;
+            w2 = reinterpret_cast<const uint8_t *>(p.peer[o * 6 + 3]);
+            s2 = reinterpret_cast<const uint8_t *>(p.peer[o * 6 + 4]);
+            g2 = reinterpret_cast<const float *>(p.peer[o * 6 + 5]);
+        }
+        const uint8_t *W = w2 + size_t(ls) * p.H * wrow;
+        const uint8_t *S = s2 + size_t(ls) * p.H * srow;
         uint4 wv[U][CH];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -428,7 +448,7 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
         }
         __half2 xr[CH][16];
         load_x_f32<LPR, CH>(p.mid + size_t(r) * p.I, q, xr);
-        const float wt = p.w[r] * p.g2[slot];
+        const float wt = p.w[r] * g2[ls];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int h = min(hb + u * RPW + sub, p.H - 1);

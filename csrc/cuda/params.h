@@ -37,6 +37,10 @@ struct GateUpParams {
     float *mid;               // [m*kk, I] fp32
     int routes, kk, H, I, fmt;
     float limit, alpha, beta;
+    // slot pools of the peer GPUs (may be null): [W][6] base addresses (w13, s13, g13, w2, s2, g2) of every rank's
+    // pool; a slot then names rank slot / spr, local slot slot % spr, read over NVLink when the rank is another GPU
+    const unsigned long long *peer;
+    int spr;
 };
 
 struct DownParams {
@@ -51,6 +55,8 @@ struct DownParams {
     float *out_f32;           // [m, H] optional FP32 copy of the GPU part (tests), may be null
     float *gpu_part;          // [m, H] scratch: the GPU part while a CPU part is pending (mailbox calls)
     int kk, H, I, fmt;
+    const unsigned long long *peer;   // as in GateUpParams (may be null)
+    int spr;
 };
 
 struct RopeParams {

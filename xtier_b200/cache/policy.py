@@ -69,6 +69,8 @@ class AdaptivePolicy:
         for layer in self.layers:
             if budget <= 0:
                 break
+            if getattr(layer, 'peer', None) is not None:   # peer mode: other GPUs read this pool, no swaps
+                continue
             counts, _ = self.mailbox.layer_stats(layer.layer, layer.E)
             for inc, vic in self.plan_layer(layer, counts, budget):
                 if vic is None:

@@ -34,7 +34,8 @@ class TieredMoE:
                  hot: list[int] | None = None, shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1,
                  topk_group: int = 1, renorm: bool = True, scale: float = 1.0, router_bias: torch.Tensor | None = None,
                  corr_bias: torch.Tensor | None = None, limit: float = 0.0, mailbox=None, engine=None,
-                 device='cuda', max_tokens: int = MAX_DECODE_TOKENS, host_experts: ExpertWeights | None = None):
+                 device='cuda', max_tokens: int = MAX_DECODE_TOKENS, host_experts: ExpertWeights | None = None,
+                 pool_storage: dict | None = None):
         self.layer = layer
         self.device = torch.device(device)
         self.E, self.H, self.I = experts.experts, experts.hidden, experts.inter
@@ -58,10 +59,20 @@ class TieredMoE:
         if shared is not None:
             parts.append(shared.to(self.device))
         if parts:
-            self.pool = ExpertWeights(self.fmt, *[torch.cat([getattr(p, f) for p in parts]).contiguous()
-                                                  for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
-            self.pool.g13 = self.pool.g13.float().contiguous()
-            self.pool.g2 = self.pool.g2.float().contiguous()
+            fields = ('w13', 'w2', 's13', 's2', 'g13', 'g2')
+            if pool_storage is not None:   # preallocated (e.g. symmetric peer memory): copy the slots in
+                for f in fields:
+                    o = 0
+                    for part in parts:
+                        src = getattr(part, f)
+                        pool_storage[f][o:o + src.shape[0]].copy_(src)
+                        o += src.shape[0]
+                self.pool = ExpertWeights(self.fmt, *[pool_storage[f] for f in fields])
+            else:
+                self.pool = ExpertWeights(self.fmt, *[torch.cat([getattr(p, f) for p in parts]).contiguous()
+                                                      for f in fields])
+                self.pool.g13 = self.pool.g13.float().contiguous()
+                self.pool.g2 = self.pool.g2.float().contiguous()
         else:
             self.pool = None
         table = torch.full((self.E,), -1, dtype=torch.int32)
@@ -77,6 +88,10 @@ class TieredMoE:
             self.mailbox.register(layer, engine)
         self.kk = self.k + self.n_shared
         self.elastic = None       # ElasticSlots (cache/elastic.py) when the layer has extra slots
+        # peer mode (cache/peer.py): `table` / `shared_slots` hold global slot names read through `peer`; prefill
+        # routes with the local names
+        self.peer, self.spr = None, 0
+        self.table_local, self.shared_local = self.table, self.shared_slots
         self._alloc(max_tokens)
 
     def _make_bufs(self, m: int) -> dict:
@@ -110,14 +125,33 @@ class TieredMoE:
         return len(self.hot) == self.E
 
     # ------------------------------------------------------------------ decode (graph capturable)
-    def route(self, x: torch.Tensor, use_mailbox: bool, active: torch.Tensor | None = None):
+    def use_peers(self, peer_table: torch.Tensor, spr: int, rank: int, sets: list[list[int]]):
+        """Peer mode: routes to experts held by another GPU's pool (sets[r]: rank r's hot experts, slot = index) read
+        them over NVLink; only experts no GPU holds go to the CPU tier. Swaps are off in this mode (other GPUs read
+        this pool)."""
+        from .peer import owners
+        own = owners(sets, rank)
+        table = torch.full((self.E,), -1, dtype=torch.int32)
+        for e, (r, s) in own.items():
+            table[e] = r * spr + s
+        self.table = table.to(self.device)
+        self.peer, self.spr = peer_table, spr
+        if self.n_shared:
+            S = len(self.hot)
+            self.shared_slots = torch.arange(S, S + self.n_shared, dtype=torch.int32, device=self.device) + rank * spr
+        self.peer_sets = sets
+
+    def route(self, x: torch.Tensor, use_mailbox: bool, active: torch.Tensor | None = None, local: bool = False):
+        """local: route with this GPU's slot names only (the grouped prefill reads the local pool)."""
         m = x.shape[0]
         logits = None
         if m > MAX_DECODE_TOKENS and not use_mailbox:
             # prefill-sized call: the router GEMM on the tensor cores (FP32 out), then per-token selection
             logits = ops.gemm_f32(x, self.router_w, self.ws_logits[:m])
+        table = self.table_local if local else self.table
+        shared = self.shared_local if local else self.shared_slots
         ops.moe_route(x, self.router_w, self.router_bias, self.corr_bias,
-                      None if self.all_hot else self.table, self.shared_slots,
+                      None if self.all_hot else table, shared,
                       self.ids[:m], self.w[:m], self.slots[:m], self.ws_logits, self.ws_count, self.k, self.mode,
                       self.n_group, self.topk_group,
                       self.renorm, self.scale, self.layer,
@@ -128,11 +162,11 @@ class TieredMoE:
         m = x.shape[0]
         if self.pool is not None:
             ops.moe_gate_up(x, self.slots[:m], self.pool.w13, self.pool.s13, self.pool.g13, self.mid[:m * self.kk],
-                            self.fmt_code, self.limit)
+                            self.fmt_code, self.limit, peer=self.peer, spr=self.spr)
             ops.moe_down(self.mid[:m * self.kk], self.slots[:m], self.w[:m], self.pool.w2, self.pool.s2, self.pool.g2,
                          add, out, out_f32, self.fmt_code,
                          self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0,
-                         gpu_part=self.gpu_part[:m])
+                         gpu_part=self.gpu_part[:m], peer=self.peer, spr=self.spr)
         else:   # no GPU slots at all: every route on the CPU
             raise NotImplementedError('a layer without GPU slots needs at least the shared/hot pool')
 
@@ -214,7 +248,7 @@ class TieredMoE:
         is read once per call instead of once per 8 tokens by the CPU engine)."""
         from .prefill import combine, grouped_routes
         m = x.shape[0]
-        self.route(x, False)
+        self.route(x, False, local=True)
         slots, w = self.slots[:m], self.w[:m]
         parts = [grouped_routes(x, slots, w, self.pool)]
         if not self.all_hot:
@@ -280,6 +314,8 @@ class TieredMoE:
     # ------------------------------------------------------------------ residency changes
     def swap(self, incoming: int, victim: int):
         """Replaces hot expert `victim` by `incoming` (stream-ordered with every kernel launched so far/after)."""
+        if self.peer is not None:
+            raise RuntimeError('swaps are off in peer mode (other GPUs read this pool)')
         slot = int(self.table_host[victim])
         if slot < 0 or int(self.table_host[incoming]) >= 0:
             raise ValueError(f'swap {incoming} <- {victim}: bad residency')
@@ -307,6 +343,8 @@ class TieredMoE:
         """Puts a non-resident expert into an empty elastic slot (stream-ordered like `swap`). Experts in elastic
         slots keep their prefill staging index, since their slot can be released again."""
         slot = None if self.elastic is None else self.elastic.free_slot()
+        if self.peer is not None:
+            raise RuntimeError('elastic slots are off in peer mode')
         if slot is None or int(self.table_host[incoming]) >= 0:
             raise ValueError(f'fill {incoming}: no free elastic slot or already resident')
         for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):

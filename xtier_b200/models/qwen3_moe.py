@@ -94,7 +94,9 @@ def zipf_bias(E: int, s: float, gen: torch.Generator, tau: float = 1.0) -> torch
 class Qwen3MoeModel:
     def __init__(self, cfg: Qwen3MoeConfig, device='cuda', seed: int = 0, hot_fraction: float = 1.0,
                  engine_threads: int | None = None, mailbox=None, synthetic_experts: bool = True,
-                 hot_sets: list[list[int]] | None = None):
+                 hot_sets: list[list[int]] | None = None, peer: bool = False):
+        """peer: spread the hot slots over the ranks of the process group (cache/peer.py): every rank holds the same
+        model (same seed), its slot pool in symmetric memory, and reads the experts other GPUs hold over NVLink."""
         self.cfg = cfg
         self.device = torch.device(device)
         g = torch.Generator(device='cpu').manual_seed(seed)
@@ -114,6 +116,16 @@ class Qwen3MoeModel:
         self.mailbox = mailbox
         self.engines = []
         self.cold = None
+        self.peers = None
+        prank, pworld = 0, 1
+        if peer and n_hot < cfg.experts:
+            from ..parallel import dist as xdist
+            env = xdist.init()
+            prank, pworld = env.rank, env.world
+            if pworld > 1:
+                from ..cache.peer import PeerPools
+                bs = 16 if cfg.fmt == formats.NVFP4 else 32
+                self.peers = PeerPools([(n_hot, H, cfg.inter, bs)] * cfg.layers, dev)
         if config.get('XTIER_COLD') and n_hot < cfg.experts:
             from ..cache.cold import ColdPool
             if not config.get('XTIER_COLD_DIR'):
@@ -138,8 +150,13 @@ class Qwen3MoeModel:
                 ew = formats.synthetic_experts(cfg.experts, H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
             else:
                 ew = formats.random_experts(cfg.experts, H, cfg.inter, cfg.fmt, std=cfg.std, seed=seed_l)
+            sets = None
             if hot_sets is not None:
                 hot = hot_sets[li]
+            elif self.peers is not None:
+                from ..cache.peer import plan_sets
+                sets = plan_sets(cfg.experts, n_hot, pworld, bias.cpu())
+                hot = sets[prank]
             elif n_hot < cfg.experts:
                 hot = torch.argsort(bias, descending=True)[:n_hot].tolist()   # most popular first (a profile)
             else:
@@ -157,10 +174,17 @@ class Qwen3MoeModel:
                     engine = CpuEngine(host, threads=engine_threads)
                 self.engines.append(engine)
             L['moe'] = TieredMoE(li, router, ew, cfg.top_k, hot=hot, router_bias=bias, mailbox=mailbox,
-                                 engine=engine, device=dev, host_experts=host)
+                                 engine=engine, device=dev, host_experts=host,
+                                 pool_storage=self.peers.storage(li) if self.peers is not None else None)
+            if sets is not None:
+                L['moe'].use_peers(self.peers.table(li), n_hot, prank, sets)
             L['moe'].prepare_prefill()
             del ew
             self.layers.append(L)
+        if self.peers is not None:   # every rank's pool is filled before any rank reads a peer's
+            torch.cuda.synchronize()
+            from ..parallel import dist as xdist
+            xdist.barrier()
         # adaptive hot-slot swaps (AdaptivePolicy) and elastic extra slots (Governor), stepped between decode steps by
         # the runtime (runtime/decode.py Generator)
         self.policy = None

@@ -173,12 +173,16 @@ def l2_prefetch(ptrs, sizes, ctas: int = 16):
     _ops().l2_prefetch(ptrs, sizes, ctas)
 
 
-def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0):
-    _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta)
+def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0,
+                peer=None, spr: int = 0):
+    """`peer` (int64 [W * 6] on the device, with `spr` slots per rank): every rank's pool base addresses; slots then
+    name (rank, local slot) and a peer's slot is read over NVLink."""
+    _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta, peer, spr)
 
 
-def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0, gpu_part=None):
-    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, gpu_part, fmt, mailbox)
+def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0, gpu_part=None,
+             peer=None, spr: int = 0):
+    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, gpu_part, fmt, mailbox, peer, spr)
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:

@@ -50,6 +50,9 @@ def init(backend: str | None = None, timeout_s: float = 300.0) -> DistEnv:
         dist.init_process_group(**kw)
         cpu_group = dist.new_group(backend='gloo', timeout=timedelta(seconds=timeout_s)) if be == 'nccl' else \
             dist.group.WORLD
+    elif world > 1:   # the caller made the process group: host exchanges still need a gloo group (collective call)
+        cpu_group = dist.new_group(backend='gloo', timeout=timedelta(seconds=timeout_s)) \
+            if dist.get_backend() == 'nccl' else dist.group.WORLD
     _env = DistEnv(rank, world, local, device, cpu_group)
     return _env
 
