@@ -3,7 +3,7 @@
     python -m xtier_b200.serve --model qwen3-moe [--layers 48] [--hot 0.4] [--max-len 8192] --port 18180
 
 Endpoints: GET /health ({"ready": true} once the model is built and its decode step captured), GET /metrics (decode
-counters and mailbox statistics), POST /v1/generate {"prompt_ids": [...], "max_new_tokens": n} -> {"ids": [...],
+counters, mailbox statistics, per-layer hit rates; /metrics/prometheus: the same in the Prometheus text format), POST /v1/generate {"prompt_ids": [...], "max_new_tokens": n} -> {"ids": [...],
 "decode_tok_s": ...}. One request at a time (batch 1 decode, the CUDA graph of the tiered MoE model).
 """
 from __future__ import annotations
@@ -49,10 +49,18 @@ def make_handler(state):
         def do_GET(self):
             if self.path == '/health':
                 return self._json(200, {'ready': state['ready']})
-            if self.path == '/metrics':
-                mb = state.get('mailbox')
-                return self._json(200, {'requests': state['requests'], 'tokens': state['tokens'],
-                                        'mailbox': mb.stats() if mb is not None else None})
+            if self.path in ('/metrics', '/metrics/prometheus'):
+                from .utils.metrics import prometheus_text, snapshot
+                snap = snapshot(state.get('model'), state.get('mailbox'), state)
+                if self.path == '/metrics':
+                    return self._json(200, snap)
+                data = prometheus_text(snap).encode()
+                self.send_response(200)
+                self.send_header('Content-Type', 'text/plain; version=0.0.4')
+                self.send_header('Content-Length', str(len(data)))
+                self.end_headers()
+                self.wfile.write(data)
+                return
             self._json(404, {'error': 'not found'})
 
         def do_POST(self):
