@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(AD_WARPS * 32) attn_decode_kernel(AttnDecodePa
     float *l_run = m_run + G, *alpha = l_run + G;
     float(&wsplit)[AD_MAX_SPLITS][G] = *reinterpret_cast<float(*)[AD_MAX_SPLITS][G]>(alpha + G);
     __shared__ bool last;
+    pdl_wait();
+    pdl_trigger();
 
     const size_t head_off = (size_t(b) * p.Hkv + kvh) * p.L;
     const __nv_bfloat16 *K = p.kc + head_off * AD_D;
@@ -378,6 +380,8 @@ __global__ void __launch_bounds__(AM_WARPS * 32) attn_decode_mma_kernel(AttnDeco
                                                                               ? AmSmem<G>::O
                                                                               : AmSmem<G>::MERGE));
     __shared__ bool last;
+    pdl_wait();
+    pdl_trigger();
 
     const size_t head_off = (size_t(b) * p.Hkv + kvh) * p.L;
     const __nv_bfloat16 *K = p.kc + head_off * AD_D;
@@ -567,7 +571,8 @@ extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t st
                                      smem);                                                                        \
                 attr = true;                                                                                       \
             }                                                                                                      \
-            attn_decode_mma_kernel<GG><<<grid, AM_WARPS * 32, smem, stream>>>(p);                                  \
+            if (xt_launch(attn_decode_mma_kernel<GG>, grid, dim3(AM_WARPS * 32), smem, stream, p) != cudaSuccess)  \
+                return -1;                                                                                         \
         }
         if (G == 8) XT_AM(8) else XT_AM(16)
 #undef XT_AM
@@ -581,7 +586,8 @@ extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t st
             cudaFuncSetAttribute(attn_decode_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);       \
             attr = true;                                                                                           \
         }                                                                                                          \
-        attn_decode_kernel<GG><<<grid, AD_WARPS * 32, smem, stream>>>(p);                                          \
+        if (xt_launch(attn_decode_kernel<GG>, grid, dim3(AD_WARPS * 32), smem, stream, p) != cudaSuccess)           \
+            return -1;                                                                                             \
         break;                                                                                                     \
     }
     switch (G) {

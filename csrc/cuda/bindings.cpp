@@ -167,7 +167,8 @@ void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const 
     p.w13 = ptr<const uint8_t>(w13);
     p.s13 = ptr<const uint8_t>(s13);
     p.g13 = ptr<const float>(g13);
-    p.mid = ptr<float>(mid);
+    check(mid.scalar_type() == at::kHalf, "moe_gate_up: mid must be float16");
+    p.mid = ptr<__half>(mid);
     p.routes = int(slots.numel());
     p.kk = int(slots.size(-1));
     p.H = int(x.size(-1));
@@ -196,7 +197,8 @@ void moe_down(const Tensor &mid, const Tensor &slots, const Tensor &w, const Ten
     p.spr = int(spr);
     if (peer) check(peer->is_cuda() && peer->scalar_type() == at::kLong && peer->numel() % 6 == 0 && spr > 0,
                     "peer: int64 [W * 6] device table and slots per rank");
-    p.mid = ptr<const float>(mid);
+    check(mid.scalar_type() == at::kHalf, "moe_down: mid must be float16");
+    p.mid = ptr<const __half>(mid);
     p.slots = ptr<const int32_t>(slots);
     p.w = ptr<const float>(w);
     p.w2 = ptr<const uint8_t>(w2);

@@ -7,7 +7,42 @@
 
 #define XT_DEV __device__ __forceinline__
 
+#include <stdlib.h>
+#include <utility>
+
 namespace xt {
+
+// Programmatic dependent launch (PDL). A kernel started by xt_launch may begin while its predecessor in the stream
+// still runs: before pdl_wait() it may only read data no earlier kernel writes (weights); pdl_wait() returns once the
+// predecessor grid has completed and its memory is visible (a no-op for a kernel launched without the attribute);
+// pdl_trigger() lets the successor start launching. Every kernel launched by xt_launch calls pdl_wait() before its
+// first dependent read and before any global write, so a chain of such kernels stays ordered.
+XT_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+XT_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+inline bool pdl_enabled() {   // XTIER_PDL=0 turns the overlap off
+    static const bool on = [] {
+        const char *v = getenv("XTIER_PDL");
+        return !v || atoi(v) != 0;
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t xt_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 XT_DEV float warp_sum(float v) {
 #pragma unroll

@@ -22,9 +22,23 @@ __global__ void __launch_bounds__(GV_WARPS * 32) gemv_bf16_kernel(const __nv_bfl
     extern __shared__ uint4 xs[];   // [M][K/8]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int kc = K / 8;
+    const int row0 = (blockIdx.x * GV_WARPS + warp) * GV_ROWS;
+    // the first K segment's weights are in flight before the wait for the previous kernel (they do not depend on it)
+    uint4 w[GV_ROWS][GV_SEG];
+#pragma unroll
+    for (int r = 0; r < GV_ROWS; ++r) {
+        const int row = min(row0 + r, N - 1);
+        const uint4 *wr = reinterpret_cast<const uint4 *>(W + size_t(row) * K);
+#pragma unroll
+        for (int c = 0; c < GV_SEG; ++c) {
+            const int ci = c * 32 + lane;
+            w[r][c] = (row0 < N && ci < kc) ? ldg_nc_v4(wr + ci) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
     for (int i = threadIdx.x; i < M * kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4 *>(x)[i];
     __syncthreads();
-    const int row0 = (blockIdx.x * GV_WARPS + warp) * GV_ROWS;
     if (row0 >= N) return;
     float acc[GV_ROWS][M];
 #pragma unroll
@@ -32,15 +46,16 @@ __global__ void __launch_bounds__(GV_WARPS * 32) gemv_bf16_kernel(const __nv_bfl
 #pragma unroll
         for (int t = 0; t < M; ++t) acc[r][t] = 0.f;
     for (int seg = 0; seg < kc; seg += 32 * GV_SEG) {
-        uint4 w[GV_ROWS][GV_SEG];
+        if (seg > 0) {
 #pragma unroll
-        for (int r = 0; r < GV_ROWS; ++r) {
-            const int row = min(row0 + r, N - 1);
-            const uint4 *wr = reinterpret_cast<const uint4 *>(W + size_t(row) * K);
+            for (int r = 0; r < GV_ROWS; ++r) {
+                const int row = min(row0 + r, N - 1);
+                const uint4 *wr = reinterpret_cast<const uint4 *>(W + size_t(row) * K);
 #pragma unroll
-            for (int c = 0; c < GV_SEG; ++c) {
-                const int ci = seg + c * 32 + lane;
-                w[r][c] = ci < kc ? ldg_nc_v4(wr + ci) : make_uint4(0, 0, 0, 0);
+                for (int c = 0; c < GV_SEG; ++c) {
+                    const int ci = seg + c * 32 + lane;
+                    w[r][c] = ci < kc ? ldg_nc_v4(wr + ci) : make_uint4(0, 0, 0, 0);
+                }
             }
         }
 #pragma unroll
@@ -100,7 +115,9 @@ extern "C" int xt_gemv_bf16(const void *x, const void *W, const void *add, void 
             cudaFuncSetAttribute(gemv_bf16_kernel<MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
             attr = true;                                                                                     \
         }                                                                                                    \
-        gemv_bf16_kernel<MM><<<grid, GV_WARPS * 32, smem, stream>>>(X, Wp, A, Y, N, K);                      \
+        if (xt_launch(gemv_bf16_kernel<MM>, grid, dim3(GV_WARPS * 32), smem, stream, X, Wp, A, Y, N, K) !=     \
+            cudaSuccess)                                                                                     \
+            return -1;                                                                                       \
         break;                                                                                               \
     }
     switch (m) {

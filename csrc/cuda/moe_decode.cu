@@ -191,6 +191,17 @@ __global__ void __cluster_dims__(ROUTE_CLUSTER, 1, 1) __launch_bounds__(ROUTE_TH
     // every CTA of the cluster must have started before the leader's shared memory is written remotely: arrive now,
     // wait just before the first remote store (the row loads overlap the barrier)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+    const int gw = int(rank) * ROUTE_WARPS + warp;
+    // this warp's first router row (weights: independent of the previous kernel) is in flight before the wait
+    uint4 r0[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int c = i * 32 + lane;
+        r0[i] = (gw < p.E && c < chunks) ? ldg_nc_v4(reinterpret_cast<const uint4 *>(p.wr + size_t(gw) * p.H) + c)
+                                         : make_uint4(0, 0, 0, 0);
+    }
+    pdl_wait();
+    pdl_trigger();
     if (rank == 0) {
         if (use_mb) {   // PCIe writes overlap the logits; published below by this CTA
             uint4 *mbx = reinterpret_cast<uint4 *>(mb.x + size_t(t) * p.H);
@@ -203,17 +214,17 @@ __global__ void __cluster_dims__(ROUTE_CLUSTER, 1, 1) __launch_bounds__(ROUTE_TH
         }
         if (tid == 0) any_cpu = 0;
     }
-    const int gw = int(rank) * ROUTE_WARPS + warp;
     bool waited = false;
     for (int e = gw; e < p.E; e += ROUTE_CLUSTER * ROUTE_WARPS) {
         const uint4 *we = reinterpret_cast<const uint4 *>(p.wr + size_t(e) * p.H);
         float acc = 0.f;
         for (int c0 = 0; c0 < chunks; c0 += 32 * 8) {
             uint4 r[8], xv[8];
+            const bool pre = e == gw && c0 == 0;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int c = c0 + i * 32 + lane;
-                r[i] = c < chunks ? ldg_nc_v4(we + c) : make_uint4(0, 0, 0, 0);
+                r[i] = pre ? r0[i] : (c < chunks ? ldg_nc_v4(we + c) : make_uint4(0, 0, 0, 0));
                 xv[i] = c < chunks ? xg[c] : make_uint4(0, 0, 0, 0);
             }
 #pragma unroll
@@ -334,6 +345,21 @@ XT_DEV void load_x_bf16(const __nv_bfloat16 *x, int q, __half2 (&xr)[CH][16]) {
 }
 
 template <int LPR, int CH>
+XT_DEV void load_x_f16(const __half *x, int q, __half2 (&xr)[CH][16]) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + size_t(c * LPR + q) * 32);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            const uint4 u = src[v];
+            const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xr[c][v * 4 + i] = h[i];
+        }
+    }
+}
+
+template <int LPR, int CH>
 XT_DEV void load_x_f32(const float *x, int q, __half2 (&xr)[CH][16]) {
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
@@ -364,10 +390,26 @@ XT_DEV float row_dot(const uint8_t *wrow, const uint8_t *srow, int fmt, int q, c
 }
 
 
+// Dot of a row whose chunks are already in registers (see gate_up: every row's loads are issued first).
+template <int LPR, int CH>
+XT_DEV float row_dot_loaded(const uint4 (&wv)[CH], const uint8_t *srow, int fmt, int q, const __half2 (&xr)[CH][16]) {
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int chunk = c * LPR + q;
+        const uint8_t *sp = fmt == 0 ? srow + chunk * 2 : srow + chunk;
+        acc += chunk_dot(wv[c], xr[c], sp, fmt);
+    }
+    return group_sum<LPR>(acc);
+}
+
 constexpr int GU_WARPS = 8;
+constexpr int GU_U = 2;   // gate/up row pairs per warp step: 2 * GU_U rows of loads in flight per lane
 
 template <int LPR, int CH>
 __global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x;
     const int slot = p.slots[r];
     if (slot < 0) return;
@@ -392,19 +434,32 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams
     const uint8_t *W = w13 + size_t(ls) * 2 * p.I * wrow;
     const uint8_t *S = s13 + size_t(ls) * 2 * p.I * srow;
     const float gg = g13[2 * ls], gu = g13[2 * ls + 1];
-    const int rows_per_cta = GU_WARPS * RPW;
-    const int j_raw = blockIdx.y * rows_per_cta + warp * RPW + sub;
-    const int j = min(j_raw, p.I - 1);   // every lane takes part in the group shuffles; out-of-range rows store nothing
-    float g = row_dot<LPR, CH>(W + j * wrow, S + j * srow, p.fmt, q, xr) * gg;
-    float u = row_dot<LPR, CH>(W + (p.I + j) * wrow, S + (p.I + j) * srow, p.fmt, q, xr) * gu;
-    if (q == 0 && j_raw < p.I) {
-        if (p.limit > 0.f) {
-            g = fminf(g, p.limit);
-            u = fmaxf(-p.limit, fminf(u, p.limit));
+    const int rows_per_cta = GU_WARPS * RPW * GU_U;
+    int jr[GU_U], jj[GU_U];
+    uint4 wg[GU_U][CH], wu[GU_U][CH];
+#pragma unroll
+    for (int u = 0; u < GU_U; ++u) {
+        jr[u] = blockIdx.y * rows_per_cta + (warp * GU_U + u) * RPW + sub;
+        jj[u] = min(jr[u], p.I - 1);   // every lane takes part in the group shuffles; out-of-range rows store nothing
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            wg[u][c] = ldg_nc_v4(W + jj[u] * wrow + size_t(c * LPR + q) * 16);
+            wu[u][c] = ldg_nc_v4(W + (p.I + jj[u]) * wrow + size_t(c * LPR + q) * 16);
         }
-        float h = (p.alpha == 1.f && p.beta == 0.f) ? g / (1.f + __expf(-g)) * u
-                                                     : g / (1.f + __expf(-p.alpha * g)) * (u + p.beta);
-        p.mid[size_t(r) * p.I + j] = h;
+    }
+#pragma unroll
+    for (int u = 0; u < GU_U; ++u) {
+        float g = row_dot_loaded<LPR, CH>(wg[u], S + jj[u] * srow, p.fmt, q, xr) * gg;
+        float v = row_dot_loaded<LPR, CH>(wu[u], S + (p.I + jj[u]) * srow, p.fmt, q, xr) * gu;
+        if (q == 0 && jr[u] < p.I) {
+            if (p.limit > 0.f) {
+                g = fminf(g, p.limit);
+                v = fmaxf(-p.limit, fminf(v, p.limit));
+            }
+            const float h = (p.alpha == 1.f && p.beta == 0.f) ? g / (1.f + __expf(-g)) * v
+                                                                : g / (1.f + __expf(-p.alpha * g)) * (v + p.beta);
+            p.mid[size_t(r) * p.I + jj[u]] = __float2half_rn(h);
+        }
     }
 }
 
@@ -418,6 +473,8 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
     constexpr int ROWS = RPW * U;
     static_assert(ROWS % 4 == 0, "the epilogue writes four rows per thread");
     __shared__ float part[XT_MB_MAX_ROUTES][ROWS];
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     const int lane = threadIdx.x & 31, j = threadIdx.x >> 5;   // warp j = route j
     const int q = lane % LPR, sub = lane / LPR;
@@ -447,7 +504,7 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
             for (int c = 0; c < CH; ++c) wv[u][c] = ldg_nc_v4(W + h * wrow + size_t(c * LPR + q) * 16);
         }
         __half2 xr[CH][16];
-        load_x_f32<LPR, CH>(p.mid + size_t(r) * p.I, q, xr);
+        load_x_f16<LPR, CH>(p.mid + size_t(r) * p.I, q, xr);
         const float wt = p.w[r] * g2[ls];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -505,6 +562,7 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
 // the token's FP32 CPU row from mapped host memory in 16-byte pieces.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const float *gpu_part, const __nv_bfloat16 *add,
                                                           __nv_bfloat16 *out, int H, XtMailbox mb) {
+    pdl_wait();
     if (!mb.dev->pending) return;
     __shared__ int ok;
     const int t = blockIdx.x;
@@ -575,19 +633,26 @@ static int pick_lpr(int row_bytes, int *ch) {
 
 #define XT_GU_CASE(L, C)                                                                        \
     if (lpr == L && ch == C) {                                                                  \
-        constexpr int rows = GU_WARPS * (32 / L);                                               \
+        constexpr int rows = GU_WARPS * (32 / L) * GU_U;                                        \
         dim3 grid(p.routes, (p.I + rows - 1) / rows);                                           \
-        moe_gate_up_kernel<L, C><<<grid, GU_WARPS * 32, 0, stream>>>(p);                        \
-        return cudaGetLastError() == cudaSuccess ? 0 : -1;                                      \
+        return xt_launch(moe_gate_up_kernel<L, C>, grid, dim3(GU_WARPS * 32), 0, stream, p) ==   \
+                       cudaSuccess                                                              \
+                   ? 0                                                                          \
+                   : -1;                                                                        \
     }
 
 #define XT_DN_CASE(L, C, U)                                                                     \
     if (lpr == L && ch == C) {                                                                  \
         constexpr int rows = (32 / L) * U;                                                      \
         dim3 grid(m, (p.H + rows - 1) / rows);                                                  \
-        moe_down_kernel<L, C, U><<<grid, 32 * p.kk, 0, stream>>>(p, mb, use_mb);                \
-        if (use_mb) moe_combine_kernel<<<m, 256, 0, stream>>>(p.gpu_part, p.add, p.out, p.H, mb); \
-        return cudaGetLastError() == cudaSuccess ? 0 : -1;                                      \
+        if (xt_launch(moe_down_kernel<L, C, U>, grid, dim3(32 * p.kk), 0, stream, p, mb, use_mb) !=  \
+            cudaSuccess)                                                                        \
+            return -1;                                                                          \
+        if (use_mb && xt_launch(moe_combine_kernel, dim3(m), dim3(256), 0, stream, p.gpu_part,    \
+                                static_cast<const __nv_bfloat16 *>(p.add), p.out, p.H, mb) !=   \
+                          cudaSuccess)                                                          \
+            return -1;                                                                          \
+        return 0;                                                                               \
     }
 
 extern "C" {
@@ -602,7 +667,9 @@ int xt_moe_route(const RouteParams *p, const XtMailbox *mb, int use_mb, cudaStre
         route_select_kernel<<<(p->m + SEL_WARPS - 1) / SEL_WARPS, SEL_WARPS * 32, 0, stream>>>(*p);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
-    moe_route_kernel<<<dim3(ROUTE_CLUSTER, p->m), ROUTE_THREADS, 0, stream>>>(*p, use_mb ? *mb : empty, use_mb);
+    if (xt_launch(moe_route_kernel, dim3(ROUTE_CLUSTER, p->m), dim3(ROUTE_THREADS), 0, stream, *p,
+                  use_mb ? *mb : empty, use_mb) != cudaSuccess)
+        return -1;
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -627,7 +694,7 @@ int xt_moe_down(const DownParams *pp, const XtMailbox *mbp, int use_mb, int m, c
     if (use_mb && !p.gpu_part) return -5;
     XT_DN_CASE(32, 1, 8) XT_DN_CASE(32, 2, 8) XT_DN_CASE(32, 3, 4) XT_DN_CASE(32, 4, 4) XT_DN_CASE(32, 5, 4)
     XT_DN_CASE(32, 6, 4) XT_DN_CASE(32, 7, 4) XT_DN_CASE(32, 8, 4) XT_DN_CASE(16, 1, 8) XT_DN_CASE(16, 3, 4)
-    XT_DN_CASE(16, 5, 2) XT_DN_CASE(16, 7, 2) XT_DN_CASE(8, 1, 8) XT_DN_CASE(8, 3, 4) XT_DN_CASE(8, 5, 2)
+    XT_DN_CASE(16, 5, 2) XT_DN_CASE(16, 7, 2) XT_DN_CASE(8, 1, 8) XT_DN_CASE(8, 3, 2) XT_DN_CASE(8, 5, 2)
     XT_DN_CASE(8, 7, 2) XT_DN_CASE(4, 1, 4) XT_DN_CASE(4, 3, 2) XT_DN_CASE(4, 5, 2) XT_DN_CASE(4, 7, 1)
     return -4;
 }

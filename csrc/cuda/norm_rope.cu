@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(const __nv_bf
     const __nv_bfloat16 *xr = x + size_t(t) * H;
     __nv_bfloat16 *rr = residual ? residual + size_t(t) * H : nullptr;
     __shared__ float red[NORM_THREADS / 32];
+    pdl_wait();
+    pdl_trigger();
     float ss = 0.f;
     // pass 1: sum (and store the new residual)
     for (int i = threadIdx.x * 8; i < H; i += NORM_THREADS * 8) {
@@ -69,6 +71,8 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(const __nv_bf
 
 // D == 128: lane l owns dims 2l, 2l+1 (first half) and 64+2l, 65+2l (second half)
 __global__ void qk_norm_rope_kv_kernel(RopeParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int heads = p.Hq + 2 * p.Hkv;
@@ -126,18 +130,19 @@ extern "C" {
 int xt_add_rmsnorm(const void *x, void *residual, const void *w, void *out, int T, int H, float eps,
                    cudaStream_t stream) {
     if (H % 8) return -2;
-    add_rmsnorm_kernel<<<T, NORM_THREADS, 0, stream>>>(
-        static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(residual),
-        static_cast<const __nv_bfloat16 *>(w), static_cast<__nv_bfloat16 *>(out), H, eps);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    const cudaError_t e = xt_launch(add_rmsnorm_kernel, dim3(T), dim3(NORM_THREADS), 0, stream,
+                                    static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(residual),
+                                    static_cast<const __nv_bfloat16 *>(w), static_cast<__nv_bfloat16 *>(out), H, eps);
+    return e == cudaSuccess ? 0 : -1;
 }
 
 int xt_qk_norm_rope_kv(const RopeParams *p, cudaStream_t stream) {
     if (p->D != 128) return -2;
     const int warps = p->T * (p->Hq + 2 * p->Hkv);
     const int threads = 256;
-    qk_norm_rope_kv_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, stream>>>(*p);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    const cudaError_t e = xt_launch(qk_norm_rope_kv_kernel, dim3((warps * 32 + threads - 1) / threads),
+                                    dim3(threads), 0, stream, *p);
+    return e == cudaSuccess ? 0 : -1;
 }
 
 }  // extern "C"

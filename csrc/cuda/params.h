@@ -34,7 +34,7 @@ struct GateUpParams {
     const uint8_t *w13;       // [S, 2I, H/2]
     const uint8_t *s13;       // [S, 2I, H/bs]
     const float *g13;         // [S, 2]
-    float *mid;               // [m*kk, I] fp32
+    __half *mid;              // [m*kk, I] f16 (the down kernel's FP4 x f16 products take it as is)
     int routes, kk, H, I, fmt;
     float limit, alpha, beta;
     // slot pools of the peer GPUs (may be null): [W][6] base addresses (w13, s13, g13, w2, s2, g2) of every rank's
@@ -44,7 +44,7 @@ struct GateUpParams {
 };
 
 struct DownParams {
-    const float *mid;         // [m*kk, I]
+    const __half *mid;        // [m*kk, I] f16
     const int32_t *slots;     // [m, kk]
     const float *w;           // [m, kk]
     const uint8_t *w2;        // [S, H, I/2]

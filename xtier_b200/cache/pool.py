@@ -99,7 +99,7 @@ class TieredMoE:
         return dict(ids=torch.empty(m, self.kk, dtype=torch.int32, device=dev),
                     w=torch.empty(m, self.kk, dtype=torch.float32, device=dev),
                     slots=torch.empty(m, self.kk, dtype=torch.int32, device=dev),
-                    mid=torch.empty(m * self.kk, self.I, dtype=torch.float32, device=dev),
+                    mid=torch.empty(m * self.kk, self.I, dtype=torch.float16, device=dev),
                     ws_logits=torch.empty(m, self.E, dtype=torch.float32, device=dev),
                     ws_count=torch.zeros(m, dtype=torch.int32, device=dev),
                     gpu_part=torch.empty(m, self.H, dtype=torch.float32, device=dev))

@@ -130,7 +130,7 @@ class _SharedExperts:
         self.fmt_code = 0 if shared.fmt == NVFP4 else 1
         self.slots = torch.arange(n, dtype=torch.int32, device=device).repeat(max_tokens, 1).contiguous()
         self.w = torch.ones(max_tokens, n, dtype=torch.float32, device=device)
-        self.mid = torch.empty(max_tokens * n, shared.inter, dtype=torch.float32, device=device)
+        self.mid = torch.empty(max_tokens * n, shared.inter, dtype=torch.float16, device=device)
         self.out = torch.empty(max_tokens, shared.hidden, dtype=torch.bfloat16, device=device)
 
     def __call__(self, x, add=None):
@@ -166,7 +166,7 @@ def nccl_ep_moe(x, ids, w, local: ExpertWeights, E: int, group=None):
     if n:
         slots = r_meta[:, 0:1].contiguous()
         wt = r_meta[:, 1:2].contiguous().view(torch.float32)
-        mid = torch.empty(n, local.inter, dtype=torch.float32, device=x.device)
+        mid = torch.empty(n, local.inter, dtype=torch.float16, device=x.device)
         fmt = 0 if local.fmt == NVFP4 else 1
         ops.moe_gate_up(r_rows, slots, local.w13, local.s13, local.g13, mid, fmt)
         ops.moe_down(mid, slots, wt, local.w2, local.s2, local.g2, None, y, fmt=fmt)

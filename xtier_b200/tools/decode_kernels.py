@@ -1,6 +1,6 @@
 """Device time of the decode-step kernels of the flagship shape in isolation (hidden 2048, GQA 32/4
 with head dim 128, 128 experts top-8): GQA decode attention at several context lengths and split counts, and the
-router (8-CTA cluster per token) with and without the CPU-tier mailbox.
+router (8-CTA cluster per token), and the hot-expert gate/up and down kernels of one token's 8 routes.
 
     python -m xtier_b200.tools.decode_kernels [--contexts 2084,8000,32768] [--iters 48]
 
@@ -80,6 +80,19 @@ def main(argv=None):
         print('ok')
         return
     res['route_m1_us'] = round(_graph_us(fr, a.iters), 2)
+    # the hot experts of one token (8 routes, all on this GPU): gate/up and down on the routes above
+    layer.route(x, False)
+    out = torch.empty_like(x)
+    fg = lambda: ops.moe_gate_up(x, layer.slots[:1], layer.pool.w13, layer.pool.s13, layer.pool.g13,
+                                 layer.mid[:k_], 0)
+    fd = lambda: ops.moe_down(layer.mid[:k_], layer.slots[:1], layer.w[:1], layer.pool.w2, layer.pool.s2,
+                              layer.pool.g2, None, out, None, 0)
+    gu_us, dn_us = _graph_us(fg, a.iters), _graph_us(fd, a.iters)
+    res['gate_up_us'] = round(gu_us, 2)
+    res['down_us'] = round(dn_us, 2)
+    res['gate_up_gbs'] = round(k_ * 2 * I * H * (0.5 + 1 / 16) / gu_us / 1e3, 1)
+    res['down_gbs'] = round(k_ * H * I * (0.5 + 1 / 16) / dn_us / 1e3, 1)
+    res['moe_layer_us'] = round(_graph_us(lambda: layer.forward(x, out=out), a.iters), 2)
     print(json.dumps(res), flush=True)
 
 
