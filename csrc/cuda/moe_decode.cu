@@ -404,7 +404,7 @@ XT_DEV float row_dot_loaded(const uint4 (&wv)[CH], const uint8_t *srow, int fmt,
 }
 
 constexpr int GU_WARPS = 8;
-constexpr int GU_U = 4;   // gate/up row pairs per warp step: 2 * GU_U rows of loads in flight per lane
+constexpr int GU_U = 2;   // gate/up row pairs per warp step: 2 * GU_U rows of loads in flight per lane
 
 template <int LPR, int CH>
 __global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams p) {
