@@ -126,13 +126,15 @@ def main():
         from datetime import timedelta
         dist.init_process_group('nccl', timeout=timedelta(seconds=600), device_id=torch.device('cuda', local))
 
-    # CPU partition of this rank: workers, then the main thread, then the mailbox dispatcher
-    cpus = sorted(os.sched_getaffinity(0))
-    per = max(3, len(cpus) // max(1, torch.cuda.device_count() if world == 1 else world))
-    mine = cpus[local * per:(local + 1) * per] if world > 1 else cpus
+    # CPU partition of this rank (NUMA node of its GPU when the node has enough of them): engine workers, the main
+    # thread, the mailbox dispatcher (xtier_b200/engine/placement.py)
+    from xtier_b200.engine import placement
+    place = placement.for_rank(local, world, spare_siblings=False)
+    mine = sorted(set(place.workers) | {place.main, place.dispatcher})
     os.sched_setaffinity(0, mine)
-    threads = args.threads or max(1, len(mine) - 2)
-    os.environ["XTIER_DISPATCH_CPU"] = str(mine[-1])
+    threads = args.threads or len(place.workers)
+    os.environ["XTIER_DISPATCH_CPU"] = str(place.dispatcher)
+    os.environ["XTIER_WORKER_CPUS"] = ','.join(map(str, place.workers))
     os.environ.setdefault("XTIER_SPIN_US", "5000")   # decode calls come every few hundred microseconds: keep workers hot
     torch.set_num_threads(1)
 
@@ -149,8 +151,8 @@ def main():
     model = Qwen3MoeModel(cfg, device='cuda', seed=1234, hot_fraction=args.hot, engine_threads=threads,
                           mailbox=mailbox, peer=peer)
     if mailbox is not None:
-        mailbox.start(cpu=mine[-1])
-    os.sched_setaffinity(0, [mine[-2]] if len(mine) >= 2 else mine)   # main thread off the workers' CPUs
+        mailbox.start(cpu=place.dispatcher)
+    os.sched_setaffinity(0, [place.main])   # main thread off the workers' CPUs
     build_s = time.time() - t0
     max_len = args.prompt + args.warmup + 2 * args.steps + 16
     gen = Generator(model, batch=1, max_len=max_len)

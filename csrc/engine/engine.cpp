@@ -93,7 +93,12 @@ static Topology read_topology() {
     Topology t;
     cpu_set_t allowed;
     CPU_ZERO(&allowed);
-    sched_getaffinity(0, sizeof allowed, &allowed);
+    const char *wc = getenv("XTIER_WORKER_CPUS");   // a placement's worker CPUs (else the process's affinity)
+    if (wc && *wc) {
+        for (int c : parse_cpulist(wc))
+            if (c >= 0 && c < CPU_SETSIZE) CPU_SET(c, &allowed);
+    }
+    if (CPU_COUNT(&allowed) == 0) sched_getaffinity(0, sizeof allowed, &allowed);
     for (int n = 0; n < 64; ++n) {
         std::string s = read_file("/sys/devices/system/node/node" + std::to_string(n) + "/cpulist");
         if (s.empty()) continue;
