@@ -116,7 +116,8 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
                const std::optional<Tensor> &table, const std::optional<Tensor> &shared_slots, const Tensor &ids,
                const Tensor &w, const Tensor &slots, const Tensor &ws_logits, const Tensor &ws_count, int64_t k,
                int64_t mode, int64_t n_group, int64_t topk_group, bool renorm, double scale, int64_t layer,
-               int64_t mailbox, const std::optional<Tensor> &active, const std::optional<Tensor> &logits_in) {
+               int64_t mailbox, const std::optional<Tensor> &active, const std::optional<Tensor> &logits_in,
+               const std::optional<Tensor> &cold_index, int64_t share_min, int64_t host_base) {
     cuda_contig(x, "x");
     cuda_contig(wr, "router weight");
     RouteParams p{};
@@ -128,6 +129,11 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
     p.shared_slots = optr<const int32_t>(shared_slots);
     p.active = optr<const int32_t>(active);
     p.logits_in = optr<const float>(logits_in);
+    p.cold_index = optr<const int32_t>(cold_index);
+    p.share_min = int(share_min);
+    p.host_base = int(host_base);
+    if (cold_index) check(cold_index->scalar_type() == at::kInt && cold_index->numel() >= wr.size(0) && host_base > 0,
+                          "cold_index: int32 [E] and a positive host_base");
     if (logits_in)
         check(logits_in->scalar_type() == at::kFloat && logits_in->numel() >= x.size(0) * wr.size(0) && mailbox == 0,
               "logits_in: fp32 [m, E], no mailbox");
@@ -158,7 +164,8 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
 
 void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const Tensor &s13, const Tensor &g13,
                  const Tensor &mid, int64_t fmt, double limit, double alpha, double beta,
-                 const std::optional<Tensor> &peer, int64_t spr) {
+                 const std::optional<Tensor> &peer, int64_t spr, const std::optional<Tensor> &host,
+                 int64_t host_base) {
     cuda_contig(w13, "w13");
     cuda_contig(s13, "s13");
     GateUpParams p{};
@@ -181,6 +188,10 @@ void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const 
     p.spr = int(spr);
     if (peer) check(peer->is_cuda() && peer->scalar_type() == at::kLong && peer->numel() % 6 == 0 && spr > 0,
                     "peer: int64 [W * 6] device table and slots per rank");
+    p.host = host ? reinterpret_cast<const unsigned long long *>(host->data_ptr<int64_t>()) : nullptr;
+    p.host_base = int(host_base);
+    if (host) check(host->is_cuda() && host->scalar_type() == at::kLong && host->numel() == 6 && host_base > 0,
+                    "host: int64 [6] device table of the pinned host pool and a positive host_base");
     check(mid.numel() >= int64_t(p.routes) * p.I, "mid too small");
     check(w13.size(2) * 2 == p.H, "w13 / x hidden mismatch");
     c10::cuda::CUDAGuard g(x.device());
@@ -190,11 +201,16 @@ void moe_gate_up(const Tensor &x, const Tensor &slots, const Tensor &w13, const 
 void moe_down(const Tensor &mid, const Tensor &slots, const Tensor &w, const Tensor &w2, const Tensor &s2,
               const Tensor &g2, const std::optional<Tensor> &add, const Tensor &out,
               const std::optional<Tensor> &out_f32, const std::optional<Tensor> &gpu_part, int64_t fmt,
-              int64_t mailbox, const std::optional<Tensor> &peer, int64_t spr) {
+              int64_t mailbox, const std::optional<Tensor> &peer, int64_t spr, const std::optional<Tensor> &host,
+              int64_t host_base) {
     cuda_contig(w2, "w2");
     DownParams p{};
     p.peer = peer ? reinterpret_cast<const unsigned long long *>(peer->data_ptr<int64_t>()) : nullptr;
     p.spr = int(spr);
+    p.host = host ? reinterpret_cast<const unsigned long long *>(host->data_ptr<int64_t>()) : nullptr;
+    p.host_base = int(host_base);
+    if (host) check(host->is_cuda() && host->scalar_type() == at::kLong && host->numel() == 6 && host_base > 0,
+                    "host: int64 [6] device table of the pinned host pool and a positive host_base");
     if (peer) check(peer->is_cuda() && peer->scalar_type() == at::kLong && peer->numel() % 6 == 0 && spr > 0,
                     "peer: int64 [W * 6] device table and slots per rank");
     check(mid.scalar_type() == at::kHalf, "moe_down: mid must be float16");
@@ -576,7 +592,7 @@ TORCH_LIBRARY(xtier, m) {
     m.def("moe_route(Tensor x, Tensor wr, Tensor? bias, Tensor? corr, Tensor? table, Tensor? shared_slots, "
           "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, Tensor(d!) ws_logits, Tensor(e!) ws_count, int k, int mode, "
           "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox, Tensor? active=None, "
-          "Tensor? logits_in=None) -> ()");
+          "Tensor? logits_in=None, Tensor? cold_index=None, int share_min=0, int host_base=0) -> ()");
     m.def("gemv(Tensor x, Tensor w, Tensor? add, Tensor(a!) out) -> ()");
     m.def("fp8_rows(Tensor tab, Tensor scales, Tensor? ids, int lo, int hi, int blk, Tensor(a!) out) -> ()");
     m.def("gemv_fp8(Tensor x, Tensor w, Tensor s, Tensor? add, Tensor(a!) out) -> ()");
@@ -606,9 +622,11 @@ TORCH_LIBRARY(xtier, m) {
     m.def("ag_gemm(Tensor a_shard, Tensor b, Tensor peer, int local_base, Tensor(a!) state, Tensor(b!) out, "
           "Tensor(c!) err, int W, int rank, int[] offsets, float timeout_s) -> ()");
     m.def("moe_gate_up(Tensor x, Tensor slots, Tensor w13, Tensor s13, Tensor g13, Tensor(a!) mid, int fmt, "
-          "float limit, float alpha, float beta, Tensor? peer=None, int spr=0) -> ()");
+          "float limit, float alpha, float beta, Tensor? peer=None, int spr=0, Tensor? host=None, "
+          "int host_base=0) -> ()");
     m.def("moe_down(Tensor mid, Tensor slots, Tensor w, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(a!) out, "
-          "Tensor(b!)? out_f32, Tensor(c!)? gpu_part, int fmt, int mailbox, Tensor? peer=None, int spr=0) -> ()");
+          "Tensor(b!)? out_f32, Tensor(c!)? gpu_part, int fmt, int mailbox, Tensor? peer=None, int spr=0, "
+          "Tensor? host=None, int host_base=0) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(xtier, CUDA, m) {

@@ -50,3 +50,18 @@ int xt_ipc_alloc(size_t bytes, void **ptr) {
 int xt_ipc_free(void *ptr) { return int(cudaFree(ptr)); }
 
 }  // extern "C"
+
+extern "C" {
+
+// 1 when `ptr` is page-locked host memory that kernels can read through the same address (mapped under unified
+// addressing), else 0: the check before a kernel is given a host pointer.
+int xt_host_ptr_mapped(const void *ptr) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return (a.type == cudaMemoryTypeHost && a.devicePointer == ptr) ? 1 : 0;
+}
+
+}  // extern "C"

@@ -257,6 +257,13 @@ __global__ void __cluster_dims__(ROUTE_CLUSTER, 1, 1) __launch_bounds__(ROUTE_TH
         float wv;
         route_select(p, t, logits, sel, chosen, chosen_w, lane, p.table ? table_s : nullptr, p.corr ? corr_s : nullptr,
                      e, wv, slot);
+        if (p.share_min > 0 && p.cold_index) {   // miss share: the first CPU route goes to the GPU (host memory)
+            const unsigned cm = __ballot_sync(0xffffffffu, lane < p.k && slot < 0 && e >= 0);
+            if (__popc(cm) >= p.share_min && lane == __ffs(cm) - 1) {
+                const int ci = p.cold_index[e];
+                if (ci >= 0) slot = p.host_base + ci;
+            }
+        }
         if (lane < kk) {
             const size_t o = size_t(t) * kk + lane;
             p.ids[o] = e;
@@ -390,6 +397,13 @@ XT_DEV float row_dot(const uint8_t *wrow, const uint8_t *srow, int fmt, int q, c
 }
 
 
+// 16-byte load through the coherent path (pinned host memory read over PCIe)
+XT_DEV uint4 ld_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
 // Dot of a row whose chunks are already in registers (see gate_up: every row's loads are issued first).
 template <int LPR, int CH>
 XT_DEV float row_dot_loaded(const uint4 (&wv)[CH], const uint8_t *srow, int fmt, int q, const __half2 (&xr)[CH][16]) {
@@ -424,7 +438,13 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams
     const uint8_t *w13 = p.w13, *s13 = p.s13;
     const float *g13 = p.g13;
     int ls = slot;
-    if (p.peer) {   // the slot's owner: this GPU or a peer (NVLink loads)
+    const bool hostw = p.host && slot >= p.host_base;   // a CPU-tier expert shared with the GPU (PCIe loads)
+    if (hostw) {
+        ls = slot - p.host_base;
+        w13 = reinterpret_cast<const uint8_t *>(p.host[0]);
+        s13 = reinterpret_cast<const uint8_t *>(p.host[1]);
+        g13 = reinterpret_cast<const float *>(p.host[2]);
+    } else if (p.peer) {   // the slot's owner: this GPU or a peer (NVLink loads)
         const int o = slot / p.spr;
         ls = slot - o * p.spr;
         w13 = reinterpret_cast<const uint8_t *>(p.peer[o * 6 + 0]);
@@ -443,8 +463,10 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_gate_up_kernel(GateUpParams
         jj[u] = min(jr[u], p.I - 1);   // every lane takes part in the group shuffles; out-of-range rows store nothing
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
-            wg[u][c] = ldg_nc_v4(W + jj[u] * wrow + size_t(c * LPR + q) * 16);
-            wu[u][c] = ldg_nc_v4(W + (p.I + jj[u]) * wrow + size_t(c * LPR + q) * 16);
+            const uint8_t *pg = W + jj[u] * wrow + size_t(c * LPR + q) * 16;
+            const uint8_t *pu = W + (p.I + jj[u]) * wrow + size_t(c * LPR + q) * 16;
+            wg[u][c] = hostw ? ld_v4(pg) : ldg_nc_v4(pg);
+            wu[u][c] = hostw ? ld_v4(pu) : ldg_nc_v4(pu);
         }
     }
 #pragma unroll
@@ -487,7 +509,13 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
         const uint8_t *w2 = p.w2, *s2 = p.s2;
         const float *g2 = p.g2;
         int ls = slot;
-        if (p.peer) {
+        const bool hostw = p.host && slot >= p.host_base;
+        if (hostw) {
+            ls = slot - p.host_base;
+            w2 = reinterpret_cast<const uint8_t *>(p.host[3]);
+            s2 = reinterpret_cast<const uint8_t *>(p.host[4]);
+            g2 = reinterpret_cast<const float *>(p.host[5]);
+        } else if (p.peer) {
             const int o = slot / p.spr;
             ls = slot - o * p.spr;
             w2 = reinterpret_cast<const uint8_t *>(p.peer[o * 6 + 3]);
@@ -501,7 +529,10 @@ __global__ void __launch_bounds__(XT_MB_MAX_ROUTES * 32) moe_down_kernel(DownPar
         for (int u = 0; u < U; ++u) {
             const int h = min(hb + u * RPW + sub, p.H - 1);
 #pragma unroll
-            for (int c = 0; c < CH; ++c) wv[u][c] = ldg_nc_v4(W + h * wrow + size_t(c * LPR + q) * 16);
+            for (int c = 0; c < CH; ++c) {
+                const uint8_t *pw = W + h * wrow + size_t(c * LPR + q) * 16;
+                wv[u][c] = hostw ? ld_v4(pw) : ldg_nc_v4(pw);
+            }
         }
         __half2 xr[CH][16];
         load_x_f16<LPR, CH>(p.mid + size_t(r) * p.I, q, xr);

@@ -19,6 +19,10 @@ struct RouteParams {
     const int32_t *shared_slots;   // [n_shared]
     const int32_t *active;    // [m] token flags (may be null): a token with flag 0 skips its routed experts
     const float *logits_in;   // [m, E] precomputed FP32 router logits (prefill; may be null): selection only
+    // miss share (may be null / 0): a token with at least share_min routes on the CPU tier sends its first one to the
+    // GPU instead, which reads that expert from pinned host memory (slot = host_base + cold_index[expert])
+    const int32_t *cold_index;
+    int share_min, host_base;
     int32_t *ids;             // [m, kk] original expert ids (-1 for shared)
     float *w;                 // [m, kk]
     int32_t *slots;           // [m, kk] GPU slot or -1
@@ -41,6 +45,10 @@ struct GateUpParams {
     // pool; a slot then names rank slot / spr, local slot slot % spr, read over NVLink when the rank is another GPU
     const unsigned long long *peer;
     int spr;
+    // pinned host pool of the CPU tier's experts (may be null): [6] base addresses (w13, s13, g13, w2, s2, g2); a slot
+    // >= host_base names host expert slot - host_base, read over PCIe
+    const unsigned long long *host;
+    int host_base;
 };
 
 struct DownParams {
@@ -57,6 +65,8 @@ struct DownParams {
     int kk, H, I, fmt;
     const unsigned long long *peer;   // as in GateUpParams (may be null)
     int spr;
+    const unsigned long long *host;   // as in GateUpParams (may be null)
+    int host_base;
 };
 
 struct RopeParams {

@@ -92,6 +92,8 @@ class TieredMoE:
         # routes with the local names
         self.peer, self.spr = None, 0
         self.table_local, self.shared_local = self.table, self.shared_slots
+        # miss share (XTIER_DECODE_MISS_GPU): the pinned host pool's base addresses for the decode kernels
+        self.host_table, self.share_min = None, 0
         self._alloc(max_tokens)
 
     def _make_bufs(self, m: int) -> dict:
@@ -155,18 +157,22 @@ class TieredMoE:
                       self.ids[:m], self.w[:m], self.slots[:m], self.ws_logits, self.ws_count, self.k, self.mode,
                       self.n_group, self.topk_group,
                       self.renorm, self.scale, self.layer,
-                      self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0, active, logits)
+                      self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0, active, logits,
+                      *((self._cold_index, self.share_min, self.HOST_BASE)
+                        if (self.host_table is not None and use_mailbox and not local) else (None, 0, 0)))
 
     def experts_gpu(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None, use_mailbox: bool,
                     out_f32: torch.Tensor | None = None):
         m = x.shape[0]
         if self.pool is not None:
+            hb = self.HOST_BASE if self.host_table is not None else 0
             ops.moe_gate_up(x, self.slots[:m], self.pool.w13, self.pool.s13, self.pool.g13, self.mid[:m * self.kk],
-                            self.fmt_code, self.limit, peer=self.peer, spr=self.spr)
+                            self.fmt_code, self.limit, peer=self.peer, spr=self.spr, host=self.host_table,
+                            host_base=hb)
             ops.moe_down(self.mid[:m * self.kk], self.slots[:m], self.w[:m], self.pool.w2, self.pool.s2, self.pool.g2,
                          add, out, out_f32, self.fmt_code,
                          self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0,
-                         gpu_part=self.gpu_part[:m], peer=self.peer, spr=self.spr)
+                         gpu_part=self.gpu_part[:m], peer=self.peer, spr=self.spr, host=self.host_table, host_base=hb)
         else:   # no GPU slots at all: every route on the CPU
             raise NotImplementedError('a layer without GPU slots needs at least the shared/hot pool')
 
@@ -281,10 +287,32 @@ class TieredMoE:
 
     def prepare_prefill(self):
         """Pinned host copy of the layer's cold experts (the source of the prefill uploads); done at model build so
-        the first prefill does not pay for page-locking."""
+        the first prefill does not pay for page-locking. With XTIER_DECODE_MISS_GPU it is also the pool the decode
+        kernels read a shared CPU-tier expert from."""
         if self.all_hot or self.host is None or getattr(self, '_host_cold', None) is not None:
             return
         self._upload_cold(copy=False)
+        self._setup_miss_share()
+
+    HOST_BASE = 1 << 24   # slot names at and above this are experts of the pinned host pool
+
+    def _setup_miss_share(self):
+        import ctypes as C
+        import math
+        share = config.get('XTIER_DECODE_MISS_GPU')
+        if share <= 0 or self.peer is not None or self.device.type != 'cuda':
+            return
+        hc = self._host_cold
+        fields = ('w13', 's13', 'g13', 'w2', 's2', 'g2')
+        ptrs = [getattr(hc, f).data_ptr() for f in fields]
+        L = ops.cdll()
+        L.xt_host_ptr_mapped.argtypes = [C.c_void_p]
+        if not all(L.xt_host_ptr_mapped(C.c_void_p(p)) for p in ptrs):
+            import logging
+            logging.getLogger('xtier_b200').warning('XTIER_DECODE_MISS_GPU: the host pool is not device-mapped; off')
+            return
+        self.host_table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.share_min = max(1, math.ceil(0.5 / share))
 
     def _upload_cold(self, copy: bool = True) -> ExpertWeights:
         """The layer's cold experts in a staging pool on the GPU (shared by the layers of one shape), copied from a

@@ -48,6 +48,8 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_CACHE_DECAY', 'float', 0.7, 'decay of the route counts per round'),
     _S('XTIER_CACHE_MIN_GAIN', 'float', 1.5, 'minimum count advantage of an incoming expert over its victim'),
     _S('XTIER_CACHE_LOG', 'int', 0, 'log the cache statistics every N policy rounds (0: off)'),
+    _S('XTIER_DECODE_MISS_GPU', 'float', 0.0, 'share of a token\'s CPU-tier routes the GPU computes from pinned host '
+       'memory over PCIe (one per token at most; 0: off)'),
     _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in VMM-backed memory that prefills take back'),
     _S('XTIER_CACHE_ELASTIC_MAX', 'float', 2.0, 'address space per layer, as a multiple of its base hot slots'),
     _S('XTIER_CACHE_ELASTIC_RESERVE_GIB', 'float', 2.0, 'free device memory never given to extra slots'),

@@ -66,12 +66,13 @@ def attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits
 
 def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k: int, mode: int = 0,
               n_group: int = 1, topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0,
-              mailbox: int = 0, active=None, logits_in=None):
+              mailbox: int = 0, active=None, logits_in=None, cold_index=None, share_min: int = 0,
+              host_base: int = 0):
     """`active` (int32 [m], optional): token flags; a token with flag 0 skips its routed experts (GPU and CPU),
     e.g. a verify token after a truncated draft. `logits_in` (fp32 [m, E], prefill): precomputed router logits; the
     kernel only selects (one CTA per token)."""
     _ops().moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k, mode, n_group,
-                     topk_group, renorm, scale, layer, mailbox, active, logits_in)
+                     topk_group, renorm, scale, layer, mailbox, active, logits_in, cold_index, share_min, host_base)
 
 
 def gemm_f32(a, b, out=None):
@@ -174,15 +175,16 @@ def l2_prefetch(ptrs, sizes, ctas: int = 16):
 
 
 def moe_gate_up(x, slots, w13, s13, g13, mid, fmt: int, limit: float = 0.0, alpha: float = 1.0, beta: float = 0.0,
-                peer=None, spr: int = 0):
+                peer=None, spr: int = 0, host=None, host_base: int = 0):
     """`peer` (int64 [W * 6] on the device, with `spr` slots per rank): every rank's pool base addresses; slots then
-    name (rank, local slot) and a peer's slot is read over NVLink."""
-    _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta, peer, spr)
+    name (rank, local slot) and a peer's slot is read over NVLink. `host` (int64 [6]): the pinned host pool of the CPU
+    tier's experts; a slot >= host_base names one of them (read over PCIe, the miss share)."""
+    _ops().moe_gate_up(x, slots, w13, s13, g13, mid, fmt, limit, alpha, beta, peer, spr, host, host_base)
 
 
 def moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32=None, fmt: int = 0, mailbox: int = 0, gpu_part=None,
-             peer=None, spr: int = 0):
-    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, gpu_part, fmt, mailbox, peer, spr)
+             peer=None, spr: int = 0, host=None, host_base: int = 0):
+    _ops().moe_down(mid, slots, w, w2, s2, g2, add, out, out_f32, gpu_part, fmt, mailbox, peer, spr, host, host_base)
 
 
 def attn_decode_splits(batch: int, kv_heads: int, max_len: int, sms: int = 148) -> int:
