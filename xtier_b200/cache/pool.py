@@ -192,7 +192,7 @@ class TieredMoE:
     # ------------------------------------------------------------------ prefill (hybrid: GPU hot || CPU rest)
     def prefill(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None = None, chunk: int = 1024):
         grouped = (x.shape[0] >= config.get('XTIER_GPU_PREFILL_MIN') and self.pool is not None
-                   and (self.all_hot or self.host is not None))
+                   and (self.all_hot or self.host is not None or getattr(self, '_host_cold', None) is not None))
         if grouped:   # every expert on the GPU: cold ones uploaded once for the whole call, larger chunks
             stage = None if self.all_hot else self._staged()
             chunk = 8192
@@ -267,7 +267,7 @@ class TieredMoE:
     def upload_async(self, stream: torch.cuda.Stream, after: torch.cuda.Event | None = None):
         """Starts this layer's cold-expert upload on `stream` (after `after`, e.g. the previous user of the staging
         buffer being done); the next prefill call of the layer waits for it instead of copying itself."""
-        if self.all_hot or self.host is None:
+        if self.all_hot or (self.host is None and getattr(self, '_host_cold', None) is None):
             return
         with torch.cuda.stream(stream):
             if after is not None:

@@ -170,15 +170,24 @@ class Qwen3MoeModel:
                     from ..cache.cold import cold_engine
                     engine = cold_engine(li, host, self.cold, config.get('XTIER_COLD_FRACTION'), bias.cpu(), hot,
                                          threads=engine_threads)
+                elif sets is not None:   # peer mode: the CPU tier holds only the experts no GPU's slots hold
+                    covered = set().union(*map(set, sets))
+                    uncovered = [e for e in range(cfg.experts) if e not in covered]
+                    engine = (CpuEngine(host, threads=engine_threads, slots=len(uncovered), resident=uncovered)
+                              if uncovered else None)
                 else:
                     engine = CpuEngine(host, threads=engine_threads)
-                self.engines.append(engine)
+                if engine is not None:
+                    self.engines.append(engine)
             L['moe'] = TieredMoE(li, router, ew, cfg.top_k, hot=hot, router_bias=bias, mailbox=mailbox,
                                  engine=engine, device=dev, host_experts=host,
                                  pool_storage=self.peers.storage(li) if self.peers is not None else None)
             if sets is not None:
                 L['moe'].use_peers(self.peers.table(li), n_hot, prank, sets)
             L['moe'].prepare_prefill()
+            if sets is not None:   # no swaps in peer mode: the pinned staging copy is all the host copy is kept for
+                L['moe'].host = None
+                host = None
             del ew
             self.layers.append(L)
         if self.peers is not None:   # every rank's pool is filled before any rank reads a peer's
