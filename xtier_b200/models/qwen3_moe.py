@@ -391,14 +391,21 @@ class Qwen3MoeModel:
             w, ids = p.topk(cfg.top_k, -1)
             w = w / w.sum(-1, keepdim=True)
             out = torch.zeros_like(x)
-            ew = moe.host if moe.host is not None else moe.pool
-            slot_of = {e: e for e in range(moe.E)} if moe.host is not None else {e: s for s, e in enumerate(moe.hot)}
+            if moe.host is not None:
+                src = {e: (moe.host, e) for e in range(moe.E)}
+            else:   # this GPU's slots, and the pinned staging copy of the others (peer mode keeps no full copy)
+                src = {e: (moe.pool, s) for s, e in enumerate(moe.hot)}
+                hc = getattr(moe, '_host_cold', None)
+                if hc is not None:
+                    ci = moe._cold_index.cpu()
+                    src.update({e: (hc, int(ci[e])) for e in range(moe.E) if e not in src and int(ci[e]) >= 0})
             cache = {}
             for t in range(T):
                 for j in range(cfg.top_k):
                     e = int(ids[t, j])
                     if e not in cache:
-                        w1, w3, w2 = ew.dequant(slot_of[e])
+                        ew, i = src[e]
+                        w1, w3, w2 = ew.dequant(i)
                         cache[e] = (w1.to(dev), w3.to(dev), w2.to(dev))
                     w1, w3, w2 = cache[e]
                     g = h[t] @ w1.t()
