@@ -1,4 +1,4 @@
-"""Headline benchmark: decode tokens/s of the tiered MoE model (BASELINE config 2 at one request per GPU).
+"""Headline benchmark: decode tokens/s of the tiered MoE model (the Qwen3-style 48-layer config at one request per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -30,7 +30,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-BASELINE_TOKS = 139.5   # Qwen3.8 decode with the reference, packs off (tok/s, bs=1, RTX PRO 5000)
+BASELINE_TOKS = 139.5   # the reference's published Qwen3.8 decode, packs off (tok/s, bs=1, RTX PRO 5000)
 METRIC = 'decode tok/s (bs=1 per GPU)'
 
 
@@ -258,7 +258,7 @@ def main():
                    'l2': 'inputs larger than L2: each step streams > 1.8 GB of weights',
                    'weights': 'random-init, experts as random NVFP4 codes and block scales',
                    'baseline': 'vs_baseline divides by 139.5 tok/s, the reference\'s Qwen3.8 bs=1 decode '
-                               '(BASELINE.md, RTX PRO 5000; a different model and machine)'},
+                               '(published, RTX PRO 5000; a different model and machine)'},
         'clocks': clocks.summary(), 'e2e': e2e, 'gpu_launches': launches_per_step * args.steps,
         'mailbox': {'calls': mb_stats.get('calls'), 'mean_us': round(mb_stats.get('mean_us', 0) or 0, 2)},
         'setup_s': {'build': round(build_s, 1), 'prefill': round(prefill_s, 2)},

@@ -1,4 +1,4 @@
-"""Console entry: the DeepSeek-V3-shaped model with its experts split over 8 B200s (EP=8).
+"""Console entry: the DeepSeek-V3-shaped model (61 layers, 256 MXFP4 experts) with its experts split over 8 B200s (EP=8).
 Listed for the EP benchmark tool; the generation server for this model is not wired yet (launches the EP layer
 benchmark instead)."""
 

@@ -1,4 +1,4 @@
-"""Console entry: the Qwen3-style MoE on one B200 with the CPU tier through the mailbox."""
+"""Console entry: the Qwen3-style MoE (48 layers, 128 NVFP4 experts, 40 % hot) on one B200 with the CPU tier through the mailbox."""
 
 MODEL = {
     'id': 'qwen3-moe', 'order': 10, 'name': 'Qwen3-style MoE 48L (config 2)', 'port': 18180, 'ready_timeout': 900,

@@ -1,4 +1,4 @@
-"""DeepSeek-V3-shaped MoE language model.
+"""DeepSeek-V3-shaped MoE language model (the EP decode, long-prefill and three-tier benchmark shapes).
 
 Shape by default: hidden 7168, 61 layers (the first 3 dense, intermediate 18432), MLA attention with 128 heads,
 q_lora 1536, kv_lora 512, qk_nope 128, qk_rope 64, v_head 128; 256 routed MXFP4 experts (intermediate 2048) plus one

@@ -1,6 +1,6 @@
 """Qwen3-style MoE language model (GQA attention with per-head Q/K RMSNorm, RoPE, routed SwiGLU experts).
 
-BASELINE config 2 shape by default: hidden 2048, 48 layers, 32 query / 4 KV heads of dim 128, RoPE theta 1e6,
+The flagship decode shape by default: hidden 2048, 48 layers, 32 query / 4 KV heads of dim 128, RoPE theta 1e6,
 128 experts top-8 of intermediate 768 (NVFP4), vocab 151936, random-init N(0, 0.02) weights, and a per-layer router
 bias that follows a Zipf(1.1) expert popularity so that hot experts exist.
 

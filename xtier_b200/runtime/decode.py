@@ -5,7 +5,7 @@ replayed per token. Inside the graph the step also advances itself (next token -
 device-timed loop is pure replays. `generate()` is the end-to-end path a user calls: per step it copies the input
 token from pinned host memory, replays the graph and reads the next token back to the host.
 
-Reference parity: the reference relies on SGLang's CUDA-graph runner and scheduler (SURVEY 3.2); this is the
+Reference parity: the reference relies on SGLang's CUDA-graph runner and scheduler; this is the
 framework's own minimal runner for the named configs.
 """
 from __future__ import annotations

@@ -1,4 +1,4 @@
-"""Device time of the decode-step kernels of the flagship shape in isolation (BASELINE config 2: hidden 2048, GQA 32/4
+"""Device time of the decode-step kernels of the flagship shape in isolation (hidden 2048, GQA 32/4
 with head dim 128, 128 experts top-8): GQA decode attention at several context lengths and split counts, and the
 router (8-CTA cluster per token), and the hot-expert gate/up and down kernels of one token's 8 routes.
 

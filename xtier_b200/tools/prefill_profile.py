@@ -1,4 +1,4 @@
-"""Time to first token of a long prompt on the flagship model (BASELINE config 2 shape), and where it goes.
+"""Time to first token of a long prompt on the flagship model (Qwen3-style, 48 layers, 128 NVFP4 experts), and where it goes.
 
     python -m xtier_b200.tools.prefill_profile [--tokens 65536] [--layers 48] [--hot 0.4] [--threads 12]
 
