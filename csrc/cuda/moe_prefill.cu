@@ -25,11 +25,14 @@ namespace xt {
 constexpr int GP_BM = 128, GP_BN = 128, GP_BK = 64, GP_STAGES = 4, GP_THREADS = 448;
 constexpr int GP_DQ_WARPS = 8;   // dequantization warps (6..13)
 
+constexpr int GP_MT = 2;   // m-tiles of 128 rows per work item: every dequantized weight tile feeds GP_MT MMAs
+
 struct GpSmem {
-    static constexpr int A = GP_BM * GP_BK * 2;          // 16 KB
+    static constexpr int A1 = GP_BM * GP_BK * 2;         // 16 KB: one m-tile of activations
+    static constexpr int A = GP_MT * A1;                  // 32 KB
     static constexpr int RAW = GP_BN * GP_BK / 2;         // 4 KB of codes
     static constexpr int B = GP_BN * GP_BK * 2;           // 16 KB of BF16 weights
-    static constexpr int STAGE = A + B + RAW;             // A and B 1024-aligned, RAW after them
+    static constexpr int STAGE = A + B + RAW;             // A tiles and B 1024-aligned, RAW after them
     static constexpr int BYTES = GP_STAGES * STAGE + 1024 + 1024;
 };
 
@@ -79,7 +82,7 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
         tc::prefetch_tmap(&tma_w);
     }
     if (warp == 1) {
-        tc::tmem_alloc(tmem_slot, 2 * GP_BN);
+        tc::tmem_alloc(tmem_slot, 2 * GP_MT * GP_BN);   // two accumulator sets (double buffer) of GP_MT m-tiles
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
@@ -99,6 +102,7 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
             for (int t = blockIdx.x; t < p.T && !abort_flag; t += gridDim.x) {
                 const int4 tl = reinterpret_cast<const int4 *>(p.tiles)[t];
                 const int slot = tl.x, row0 = tl.y, nt = tl.z;
+                const bool second = tl.w > GP_BM;   // the work item's second m-tile has rows
                 const int wrow0 = GATE_UP ? slot * p.N_rows + nt * (GP_BN / 2) : slot * p.N_rows + nt * GP_BN;
                 const int wrow1 = GATE_UP ? slot * p.N_rows + p.I + nt * (GP_BN / 2) : wrow0 + GP_BN / 2;
                 for (int kb = 0; kb < kblocks; ++kb) {
@@ -108,8 +112,9 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                     }
                     uint8_t *st = smem + stage * GpSmem::STAGE;
                     uint8_t *raw = st + GpSmem::A + GpSmem::B;
-                    tc::mbar_arrive_expect_tx(&full[stage], GpSmem::A + GpSmem::RAW);
+                    tc::mbar_arrive_expect_tx(&full[stage], (second ? 2 : 1) * GpSmem::A1 + GpSmem::RAW);
                     tc::tma_load_2d(st, &tma_x, &full[stage], kb * GP_BK, row0);
+                    if (second) tc::tma_load_2d(st + GpSmem::A1, &tma_x, &full[stage], kb * GP_BK, row0 + GP_BM);
                     tc::tma_load_2d(raw, &tma_w, &full[stage], kb * (GP_BK / 2), wrow0);
                     tc::tma_load_2d(raw + GpSmem::RAW / 2, &tma_w, &full[stage], kb * (GP_BK / 2), wrow1);
                     issued = min(issued + 1, GP_STAGES);
@@ -202,7 +207,8 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                     break;
                 }
                 tc::tc_fence_after();
-                const uint32_t d = tmem + uint32_t(acc * GP_BN);
+                const uint32_t d = tmem + uint32_t(acc * GP_MT * GP_BN);
+                const bool second = reinterpret_cast<const int4 *>(p.tiles)[t].w > GP_BM;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!tc::mbar_wait(&full[stage], phase) || !tc::mbar_wait(&ready[stage], phase)) {
                         fail();
@@ -211,9 +217,14 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                     tc::tc_fence_after();
                     const uint32_t sa = tc::smem_u32(smem + stage * GpSmem::STAGE);
                     const uint64_t ad = tc::sw128_kmajor_desc(sa), bd = tc::sw128_kmajor_desc(sa + GpSmem::A);
+                    const uint64_t ad1 = tc::sw128_kmajor_desc(sa + GpSmem::A1);
 #pragma unroll
-                    for (int k = 0; k < GP_BK / 16; ++k)
+                    for (int k = 0; k < GP_BK / 16; ++k) {
                         tc::mma_f16(d, ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        if (second)
+                            tc::mma_f16(d + GP_BN, ad1 + uint64_t(2 * k), bd + uint64_t(2 * k), idesc,
+                                        (kb > 0 || k > 0) ? 1u : 0u);
+                    }
                     tc::mma_commit(&empty[stage]);
                     if (++stage == GP_STAGES) {
                         stage = 0;
@@ -242,54 +253,58 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
             }
             __syncwarp();
             tc::tc_fence_after();
-            const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * GP_BN);
-            const int row = row0 + rit;
-            if (GATE_UP) {
-                const float gg = p.gscale[2 * slot], gu = p.gscale[2 * slot + 1];
+            for (int mt = 0; mt < GP_MT; ++mt) {
+                if (mt > 0 && valid <= mt * GP_BM) break;
+                const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * GP_MT * GP_BN + mt * GP_BN);
+                const int row = row0 + mt * GP_BM + rit;
+                const int vrows = valid - mt * GP_BM;   // rows of this m-tile that hold routes
+                if (GATE_UP) {
+                    const float gg = p.gscale[2 * slot], gu = p.gscale[2 * slot + 1];
 #pragma unroll 1
-                for (int c0 = 0; c0 < 64; c0 += 32) {
-                    uint32_t g[32], u[32];
-                    tc::tmem_ld32(base + uint32_t(c0), g);
-                    tc::tmem_ld32(base + uint32_t(64 + c0), u);
-                    tc::tmem_ld_wait();
-                    if (rit < valid) {
-                        __nv_bfloat16 *dst = p.mid + size_t(row) * p.out_cols + nt * 64 + c0;
+                    for (int c0 = 0; c0 < 64; c0 += 32) {
+                        uint32_t g[32], u[32];
+                        tc::tmem_ld32(base + uint32_t(c0), g);
+                        tc::tmem_ld32(base + uint32_t(64 + c0), u);
+                        tc::tmem_ld_wait();
+                        if (rit < vrows) {
+                            __nv_bfloat16 *dst = p.mid + size_t(row) * p.out_cols + nt * 64 + c0;
 #pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            uint4 o;
-                            __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+                            for (int v = 0; v < 4; ++v) {
+                                uint4 o;
+                                __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                float h[2];
+                                for (int i = 0; i < 4; ++i) {
+                                    float h[2];
 #pragma unroll
-                                for (int e = 0; e < 2; ++e) {
-                                    const float a = __uint_as_float(g[v * 8 + 2 * i + e]) * gg;
-                                    const float b = __uint_as_float(u[v * 8 + 2 * i + e]) * gu;
-                                    h[e] = a / (1.f + __expf(-a)) * b;
+                                    for (int e = 0; e < 2; ++e) {
+                                        const float a = __uint_as_float(g[v * 8 + 2 * i + e]) * gg;
+                                        const float b = __uint_as_float(u[v * 8 + 2 * i + e]) * gu;
+                                        h[e] = a / (1.f + __expf(-a)) * b;
+                                    }
+                                    o2[i] = __floats2bfloat162_rn(h[0], h[1]);
                                 }
-                                o2[i] = __floats2bfloat162_rn(h[0], h[1]);
+                                reinterpret_cast<uint4 *>(dst)[v] = o;
                             }
-                            reinterpret_cast<uint4 *>(dst)[v] = o;
+                        }
+                    }
+                } else {
+                    const float scale = rit < vrows ? p.route_w[row] * p.gscale[slot] : 0.f;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < GP_BN; c0 += 32) {
+                        uint32_t r[32];
+                        tc::tmem_ld32(base + uint32_t(c0), r);
+                        tc::tmem_ld_wait();
+                        if (rit < vrows) {
+                            float *dst = p.y + size_t(row) * p.out_cols + nt * GP_BN + c0;
+#pragma unroll
+                            for (int v = 0; v < 8; ++v)
+                                reinterpret_cast<float4 *>(dst)[v] =
+                                    make_float4(__uint_as_float(r[4 * v]) * scale, __uint_as_float(r[4 * v + 1]) * scale,
+                                                __uint_as_float(r[4 * v + 2]) * scale, __uint_as_float(r[4 * v + 3]) * scale);
                         }
                     }
                 }
-            } else {
-                const float scale = rit < valid ? p.route_w[row] * p.gscale[slot] : 0.f;
-#pragma unroll 1
-                for (int c0 = 0; c0 < GP_BN; c0 += 32) {
-                    uint32_t r[32];
-                    tc::tmem_ld32(base + uint32_t(c0), r);
-                    tc::tmem_ld_wait();
-                    if (rit < valid) {
-                        float *dst = p.y + size_t(row) * p.out_cols + nt * GP_BN + c0;
-#pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            reinterpret_cast<float4 *>(dst)[v] =
-                                make_float4(__uint_as_float(r[4 * v]) * scale, __uint_as_float(r[4 * v + 1]) * scale,
-                                            __uint_as_float(r[4 * v + 2]) * scale, __uint_as_float(r[4 * v + 3]) * scale);
-                    }
-                }
-            }
+            }   // m-tiles
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&tempty[acc]);
@@ -299,7 +314,7 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
     __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 2 * GP_BN);
+        tc::tmem_dealloc(tmem, 2 * GP_MT * GP_BN);
     }
 }
 

@@ -41,14 +41,18 @@ def plan(slots: torch.Tensor):
     return order, rows, R, runs
 
 
+WORK_ROWS = 2 * TILE   # rows of one work item of the kernel: two 128-row m-tiles share each dequantized weight tile
+
+
 def _tiles(runs: torch.Tensor, n_tiles: int, device) -> torch.Tensor:
-    """[T, 4] int32 (slot, first row, n-tile, valid rows) for every 128-row block of every run x every n-tile."""
-    mt = (runs[:, 2] + TILE - 1) // TILE
+    """[T, 4] int32 (slot, first row, n-tile, valid rows <= 256) for every 256-row block of every run x every n-tile
+    (rows past a run's end in its last block are computed and dropped by the kernel's epilogue)."""
+    mt = (runs[:, 2] + WORK_ROWS - 1) // WORK_ROWS
     run = torch.repeat_interleave(torch.arange(runs.shape[0]), mt)
     first_block = torch.cumsum(mt, 0) - mt
     blk = torch.arange(run.numel()) - first_block[run]
-    row0 = runs[run, 1] + blk * TILE
-    valid = torch.clamp(runs[run, 2] - blk * TILE, max=TILE)
+    row0 = runs[run, 1] + blk * WORK_ROWS
+    valid = torch.clamp(runs[run, 2] - blk * WORK_ROWS, max=WORK_ROWS)
     slot = runs[run, 0]
     T = run.numel()
     t = torch.stack([slot.repeat_interleave(n_tiles), row0.repeat_interleave(n_tiles),
