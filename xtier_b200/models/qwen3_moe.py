@@ -117,6 +117,7 @@ class Qwen3MoeModel:
         self.engines = []
         self.cold = None
         self.peers = None
+        self.bigram = None   # tables.engram.BigramTable (attach_bigram)
         prank, pworld = 0, 1
         if peer and n_hot < cfg.experts:
             from ..parallel import dist as xdist
@@ -205,6 +206,11 @@ class Qwen3MoeModel:
                 from ..cache.elastic import Governor, install
                 self.governor = Governor(install(self))
 
+    def attach_bigram(self, table):
+        """Adds a hashed-bigram NVMe embedding table (tables/engram.py) to the token embeddings, in prefill and inside
+        the decode graph. Attach before capturing the decode step."""
+        self.bigram = table
+
     # ------------------------------------------------------------------ state
     def alloc_state(self, batch: int, max_len: int) -> dict:
         cfg = self.cfg
@@ -243,6 +249,7 @@ class Qwen3MoeModel:
         H = cfg.hidden
         return dict(
             tokens=torch.zeros(batch, dtype=torch.int64, device=dev),
+            prev=torch.zeros(batch, dtype=torch.int64, device=dev),   # the previous input (hashed n-gram rows)
             pos=torch.zeros(batch, dtype=torch.int32, device=dev),
             seqlens=torch.zeros(batch, dtype=torch.int32, device=dev),
             rows=torch.arange(batch, dtype=torch.int32, device=dev),
@@ -266,6 +273,8 @@ class Qwen3MoeModel:
         main = torch.cuda.current_stream(self.device) if side is not None else None
         torch.add(buf['pos'], 1, out=buf['seqlens'])
         torch.index_select(self.embed, 0, buf['tokens'], out=buf['residual'])
+        if self.bigram is not None:   # NVMe hashed-bigram rows, looked up inside the graph
+            self.bigram.add_decode(buf['residual'], buf['prev'], buf['tokens'])
         scale = 1.0 / math.sqrt(cfg.head_dim)
         for li, L in enumerate(self.layers):
             if li == 0:
@@ -287,6 +296,7 @@ class Qwen3MoeModel:
         ops.add_rmsnorm(buf['moe_out'], buf['residual'], self.final_norm, buf['h'], cfg.eps)
         ops.gemv(buf['h'], self.lm_head, buf['logits'])
         torch.argmax(buf['logits'], dim=-1, out=buf['next'])
+        buf['prev'].copy_(buf['tokens'])
         if side is not None:
             main.wait_stream(side)
         return buf['next']
@@ -304,6 +314,10 @@ class Qwen3MoeModel:
         pos = torch.arange(start, start + T, dtype=torch.int32, device=dev)
         rows = torch.full((T,), row, dtype=torch.int32, device=dev)
         residual = self.embed.index_select(0, tokens.to(dev)).contiguous()
+        if self.bigram is not None:
+            last = st.setdefault('last_token', {})
+            self.bigram.add_prefill(residual, tokens, prev0=last.get(row, 0) if start > 0 else 0)
+            last[row] = int(tokens[-1])
         h = torch.empty_like(residual)
         moe_out = torch.empty_like(residual)
         q = torch.empty(T, cfg.heads, D, dtype=torch.bfloat16, device=dev)
@@ -370,6 +384,10 @@ class Qwen3MoeModel:
             return torch.cat([a * cos - b * sin, b * cos + a * sin], -1)
 
         x = self.embed.index_select(0, tokens.to(dev)).to(f)
+        if self.bigram is not None:
+            t = tokens.detach().cpu().long()
+            r = self.bigram.rows_host(torch.cat([torch.tensor([0]), t[:-1]]), t).to(dev, f)
+            x = x + (r @ self.bigram.proj.to(f).t() if self.bigram.proj is not None else r)
         mask = torch.ones(T, T, device=dev, dtype=torch.bool).tril()
         for L in self.layers:
             h = rms(x, L['in_norm'])

@@ -37,8 +37,7 @@ class Generator:
 
     def capture(self, warmup: int = 2):
         """Captures one self-advancing decode step. Warm-up runs rewrite the current position only."""
-        pos0 = self.buf['pos'].clone()
-        tok0 = self.buf['tokens'].clone()
+        saved = {k: self.buf[k].clone() for k in ('pos', 'tokens', 'prev') if k in self.buf}
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -50,8 +49,8 @@ class Generator:
         with torch.cuda.graph(self.graph):
             self._step_body()
         torch.cuda.synchronize()
-        self.buf['pos'].copy_(pos0)
-        self.buf['tokens'].copy_(tok0)
+        for k, v in saved.items():
+            self.buf[k].copy_(v)
         self.check()
 
     def step(self):
@@ -65,6 +64,9 @@ class Generator:
         mb = getattr(self.model, 'mailbox', None)
         if mb is not None:
             mb.check()
+        bg = getattr(self.model, 'bigram', None)
+        if bg is not None:
+            bg.check()
 
     # ------------------------------------------------------------------ public API
     def prefill(self, prompts: torch.Tensor):
@@ -85,6 +87,8 @@ class Generator:
             first.append(gov.guarded(self.model.prefill, self.state, ids, row=b))
             gov.after_forward(T, T, before, torch.cuda.max_memory_allocated())
         self.buf['tokens'].copy_(torch.cat(first).view(-1))
+        if 'prev' in self.buf:   # the last prompt token precedes the first decode input
+            self.buf['prev'].copy_(prompts[:, -1].to(self.buf['prev'].device))
         self.buf['pos'].fill_(T)
         torch.cuda.synchronize()
         self.check()

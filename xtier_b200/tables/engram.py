@@ -1,0 +1,97 @@
+"""Hashed bigram embedding rows from an NVMe row table, added to the residual stream (the lookup of DeepSeek V4's
+Engram memory, and of the three-tier benchmark's 32 GiB table).
+
+Each token t at a position with previous token p reads row hash(p, t) mod rows of the table: the 64-bit key
+(p << 32) | t goes through the SplitMix64 finalizer (Steele, Lea and Flood, "Fast splittable pseudorandom number
+generators", 2014: xor-shift 30, multiply, xor-shift 27, multiply, xor-shift 31), computed on the device in int64
+with logical shifts, so the ids never leave the GPU before the lookup. The BF16 rows [dim] come from `RowStore` (page
+cache, NVMe with O_DIRECT, row cache); in decode the lookup runs inside the CUDA
+graph (`GraphLookup`: device->host ids, a host-function node running the C++ lookup, host->device rows) and the rows
+are projected to the hidden size when the table's width differs (a BF16 [hidden, dim] matrix) and added to the
+token's embedding. Prefill looks its rows up directly.
+(Reference parity: xtier/tables/lookup.py:47-93 and xtier/packs/deepseek_v4/__init__.py (Engram `_init`,
+`_owned_rows`, `_prefetch`): rows of an NVMe table looked up inside the graph with a row cache.)
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+_M1 = -4658895280553007687    # 0xbf58476d1ce4e5b9 as a signed 64-bit integer
+_M2 = -7723592293110705685    # 0x94d049bb133111eb
+
+
+def _lsr(x: torch.Tensor, k: int) -> torch.Tensor:
+    """Logical right shift of int64 lanes."""
+    return (x >> k) & ((1 << (64 - k)) - 1)
+
+
+def bigram_rows(prev: torch.Tensor, cur: torch.Tensor, rows: int, seed: int = 0) -> torch.Tensor:
+    """Row ids (int64) of the (previous, current) token pairs: SplitMix64 finalizer of (prev << 32 | cur) ^ seed."""
+    z = (prev.long() << 32) | (cur.long() & 0xFFFFFFFF)
+    z = z ^ seed
+    z = (z ^ _lsr(z, 30)) * _M1
+    z = (z ^ _lsr(z, 27)) * _M2
+    z = z ^ _lsr(z, 31)
+    return (z & 0x7FFFFFFFFFFFFFFF) % rows
+
+
+def bigram_rows_reference(prev, cur, rows: int, seed: int = 0) -> np.ndarray:
+    """The same hash in Python integers (the tests' oracle)."""
+    out = []
+    mask = (1 << 64) - 1
+    for p, c in zip(np.asarray(prev).tolist(), np.asarray(cur).tolist()):
+        z = (((p << 32) | (c & 0xFFFFFFFF)) ^ seed) & mask
+        z = ((z ^ (z >> 30)) * 0xbf58476d1ce4e5b9) & mask
+        z = ((z ^ (z >> 27)) * 0x94d049bb133111eb) & mask
+        z = z ^ (z >> 31)
+        out.append((z & 0x7FFFFFFFFFFFFFFF) % rows)
+    return np.asarray(out, dtype=np.int64)
+
+
+class BigramTable:
+    """An NVMe table of `rows` BF16 rows of width `dim`, added (through `proj` [hidden, dim] when dim != hidden) to
+    the embeddings of `batch` decode tokens inside the graph, and of whole prompts in prefill."""
+
+    def __init__(self, store, rows: int, dim: int, hidden: int, batch: int = 1, device='cuda', seed: int = 0,
+                 proj: torch.Tensor | None = None):
+        from .lookup import GraphLookup
+        if store.row_bytes != dim * 2 or store.scale_bytes:
+            raise ValueError('BigramTable: BF16 rows of width dim expected')
+        if dim != hidden and proj is None:
+            raise ValueError('BigramTable: a [hidden, dim] projection is needed when dim != hidden')
+        self.store, self.rows, self.dim, self.hidden, self.seed = store, rows, dim, hidden, seed
+        self.device = torch.device(device)
+        self.proj = None if proj is None else proj.to(self.device, torch.bfloat16).contiguous()
+        self.lookup = GraphLookup(store, batch, self.device)
+        self.ids = torch.zeros(batch, dtype=torch.int64, device=self.device)
+        self.delta = torch.empty(batch, hidden, dtype=torch.bfloat16, device=self.device)
+
+    def _project(self, r: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        from .. import ops
+        if self.proj is None:
+            return r if out is None else out.copy_(r)
+        return ops.linear(r, self.proj, out=out)
+
+    def add_decode(self, x: torch.Tensor, prev: torch.Tensor, cur: torch.Tensor):
+        """x [batch, hidden] += rows of (prev, cur); graph-capturable."""
+        self.ids.copy_(bigram_rows(prev, cur, self.rows, self.seed))
+        raw = self.lookup.fetch(self.ids)
+        r = raw.view(torch.bfloat16).view(-1, self.dim)
+        x.add_(self._project(r, self.delta))
+
+    def rows_host(self, prev, cur) -> torch.Tensor:
+        """BF16 [n, dim] rows of the pairs, looked up directly (prefill, reference)."""
+        ids = bigram_rows(torch.as_tensor(prev).cpu(), torch.as_tensor(cur).cpu(), self.rows, self.seed)
+        raw = self.store.lookup(ids.numpy())
+        return torch.from_numpy(np.ascontiguousarray(raw)).view(torch.bfloat16).view(-1, self.dim)
+
+    def add_prefill(self, x: torch.Tensor, tokens: torch.Tensor, prev0: int = 0):
+        """x [T, hidden] += rows of the prompt's pairs (the first token's previous one is prev0)."""
+        t = tokens.detach().cpu().long()
+        prev = torch.cat([torch.tensor([prev0]), t[:-1]])
+        r = self.rows_host(prev, t).to(x.device)
+        x.add_(self._project(r))
+
+    def check(self):
+        self.lookup.check()
