@@ -61,7 +61,8 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_CACHE_ELASTIC_EXTRAPOLATE', 'float', 2.0, 'how far a learnt need is scaled up to bound a larger one'),
     _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in memory only a prefill needs (VMM granules)'),
     _S('XTIER_CACHE_ELASTIC_RESERVE_GIB', 'float', 2.0, 'memory the elastic slots always leave free'),
-    _S('XTIER_GPU2_SLOTS', 'str', '', 'hot slots on peer GPUs read over NVLink: N per layer, or auto'),
+    _S('XTIER_GPU2_SLOTS', 'str', '', 'auto / on: the hot slots of all GPUs of the process group form one pool, '
+       'read over NVLink'),
     _S('XTIER_EP', 'int', 0, 'expert-parallel ranks of the hot-slot pool (0: the world size)'),
     _S('XTIER_COLD', 'flag', False, 'cold experts in NVMe relayout files, read on demand with O_DIRECT'),
     _S('XTIER_COLD_DIR', 'str', '', 'directories (one per drive, comma separated) of the cold-expert store'),

@@ -94,9 +94,12 @@ def zipf_bias(E: int, s: float, gen: torch.Generator, tau: float = 1.0) -> torch
 class Qwen3MoeModel:
     def __init__(self, cfg: Qwen3MoeConfig, device='cuda', seed: int = 0, hot_fraction: float = 1.0,
                  engine_threads: int | None = None, mailbox=None, synthetic_experts: bool = True,
-                 hot_sets: list[list[int]] | None = None, peer: bool = False):
+                 hot_sets: list[list[int]] | None = None, peer: bool | None = None):
         """peer: spread the hot slots over the ranks of the process group (cache/peer.py): every rank holds the same
-        model (same seed), its slot pool in symmetric memory, and reads the experts other GPUs hold over NVLink."""
+        model (same seed), its slot pool in symmetric memory, and reads the experts other GPUs hold over NVLink
+        (None: XTIER_GPU2_SLOTS=auto / on turns it on)."""
+        if peer is None:
+            peer = str(config.get('XTIER_GPU2_SLOTS')).strip().lower() in ('auto', '1', 'on', 'true', 'yes')
         self.cfg = cfg
         self.device = torch.device(device)
         g = torch.Generator(device='cpu').manual_seed(seed)
