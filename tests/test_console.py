@@ -1,6 +1,5 @@
 """Console on the CPU: every option value of every card builds a command, the page renders, the API answers, POSTs
 without the console header are refused, and a launch starts and stops a (stand-in) server process group."""
-import itertools
 import json
 import threading
 import urllib.error

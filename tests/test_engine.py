@@ -1,6 +1,5 @@
 """CPU expert engine vs the FP32 dequant reference (the single-layer CPU config: H 2048, 64 routed experts of I 768 plus one
 shared expert, NVFP4, softmax top-8 with renormalized weights, 16 bf16 tokens ~ N(0,1), seed 0)."""
-import numpy as np
 import pytest
 import torch
 

@@ -16,7 +16,6 @@ from __future__ import annotations
 import argparse
 import concurrent.futures as cf
 import os
-import shutil
 import subprocess
 import sys
 import sysconfig

@@ -21,7 +21,7 @@ import threading
 import torch
 
 from .. import config, ops
-from ..formats import MXFP4, NVFP4, ExpertWeights
+from ..formats import NVFP4, ExpertWeights
 
 MAX_DECODE_TOKENS = 16
 _STAGING: dict = {}   # (cold experts, H, I, fmt, device) -> staging ExpertWeights shared by the layers
