@@ -151,13 +151,18 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                 const int wr = GATE_UP ? (r < 64 ? nt * 64 + r : p.I + nt * 64 + (r - 64)) : nt * GP_BN + r;
                 sp[i] = p.scales + (size_t(slot) * p.N_rows + wr) * srow;
             }
-            for (int kb = 0; kb < kblocks; ++kb) {
-                float sf[4];
+            // block scales one k-block ahead: the next k-block's loads are in flight while this one is converted
+            auto load_sf = [&](int kb, float (&out)[4]) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int kel = kb * GP_BK + ((dt + i * 256) & 7) * 8;
-                    sf[i] = p.fmt == 0 ? e4m3_to_f(sp[i][kel / 16]) : ue8m0_to_f(sp[i][kel / 32]);
+                    out[i] = p.fmt == 0 ? e4m3_to_f(sp[i][kel / 16]) : ue8m0_to_f(sp[i][kel / 32]);
                 }
+            };
+            float sf[4], sfn[4];
+            load_sf(0, sf);
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (kb + 1 < kblocks) load_sf(kb + 1, sfn);
                 bool ok = true;
                 if (lane == 0) ok = tc::mbar_wait(&full[stage], phase);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -191,6 +196,8 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                     stage = 0;
                     phase ^= 1;
                 }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sf[i] = sfn[i];
             }
         }
     } else if (warp == 1) {
