@@ -306,8 +306,8 @@ struct Plan {
     double tail_stats[3] = {0, 0, 0};
     // cold
     void *cold = nullptr;
-    std::vector<int> cold_file;
-    std::vector<long long> cold_off;
+    std::vector<int> cold_file;           // per (expert, node, piece): drive file of the piece (-1: no record)
+    std::vector<long long> cold_off;      // and its byte offset there
     std::vector<float> score;
     float decay = 1.f;
     double cold_stats[4] = {0, 0, 0, 0};
@@ -703,7 +703,7 @@ static int cold_ensure(Plan *p, const std::vector<int> &need, bool decode) {
     for (int e : need) used[e] = 1;
     double t0 = now_us();
     for (int e : missing) {
-        if (p->cold_file[size_t(e) * p->nodes] < 0) {
+        if (p->cold_file[size_t(e) * p->nodes * 6] < 0) {
             set_error("engine: expert " + std::to_string(e) + " is not in RAM and has no cold record");
             return -1;
         }
@@ -723,20 +723,22 @@ static int cold_ensure(Plan *p, const std::vector<int> &need, bool decode) {
             set_error("engine: no free RAM slot for a cold expert (all slots used by this call or pinned)");
             return -1;
         }
+        // every piece of every node's shard is one read job (the pieces of a record may sit on different drives)
+        const int jobs = p->nodes * 6;
+        std::vector<void *> dst(jobs);
+        std::vector<size_t> sz(jobs);
         for (int n = 0; n < p->nodes; ++n) {
             const Shard &sh = p->shards[n];
-            void *dst[6];
-            size_t sz[6];
             for (int q = 0; q < 6; ++q) {
-                dst[q] = sh.piece(victim, q);
-                sz[q] = (sh.piece_bytes[q] + 511) & ~size_t(511);
+                dst[n * 6 + q] = sh.piece(victim, q);
+                sz[n * 6 + q] = (sh.piece_bytes[q] + 511) & ~size_t(511);
             }
-            int f = p->cold_file[size_t(e) * p->nodes + n];
-            long long off = p->cold_off[size_t(e) * p->nodes + n];
-            if (xt_cold_read(p->cold, 1, &f, &off, dst, sz, 6) != 0) {
-                set_error("engine: cold read of expert " + std::to_string(e) + " failed");
-                return -1;
-            }
+        }
+        const int *f = p->cold_file.data() + size_t(e) * jobs;
+        const long long *off = p->cold_off.data() + size_t(e) * jobs;
+        if (xt_cold_read(p->cold, jobs, f, off, dst.data(), sz.data(), 1) != 0) {
+            set_error("engine: cold read of expert " + std::to_string(e) + " failed");
+            return -1;
         }
         int old = p->expert_of[victim];
         if (old >= 0) p->slot_of[old] = -1;
@@ -952,16 +954,36 @@ int xt_engine_nodes(void *plan) {
     return p ? p->nodes : -1;
 }
 
+int xt_engine_cold_attach_pieces(void *plan, void *store, const int32_t *files, const long long *offsets,
+                                 const float *scores, float half_life) {
+    Plan *p = static_cast<Plan *>(plan);
+    if (!p || !store) return -1;
+    p->cold = store;
+    p->cold_file.assign(files, files + size_t(p->E) * p->nodes * 6);
+    p->cold_off.assign(offsets, offsets + size_t(p->E) * p->nodes * 6);
+    if (scores) p->score.assign(scores, scores + p->E);
+    p->decay = half_life > 0 ? powf(0.5f, 1.f / half_life) : 1.f;
+    return 0;
+}
+
+// Whole records: the six pieces of (expert, node) follow each other from the record's offset, each padded to 512 B.
 int xt_engine_cold_attach(void *plan, void *store, const int32_t *files, const long long *offsets, const float *scores,
                           float half_life) {
     Plan *p = static_cast<Plan *>(plan);
     if (!p || !store) return -1;
-    p->cold = store;
-    p->cold_file.assign(files, files + size_t(p->E) * p->nodes);
-    p->cold_off.assign(offsets, offsets + size_t(p->E) * p->nodes);
-    if (scores) p->score.assign(scores, scores + p->E);
-    p->decay = half_life > 0 ? powf(0.5f, 1.f / half_life) : 1.f;
-    return 0;
+    const size_t recs = size_t(p->E) * p->nodes;
+    std::vector<int32_t> pf(recs * 6);
+    std::vector<long long> po(recs * 6);
+    for (size_t r = 0; r < recs; ++r) {
+        const Shard &sh = p->shards[r % p->nodes];
+        long long o = offsets[r];
+        for (int q = 0; q < 6; ++q) {
+            pf[r * 6 + q] = files[r];
+            po[r * 6 + q] = o;
+            o += (long long)((sh.piece_bytes[q] + 511) & ~size_t(511));
+        }
+    }
+    return xt_engine_cold_attach_pieces(plan, store, pf.data(), po.data(), scores, half_life);
 }
 
 void xt_engine_cold_stats(void *plan, double *o) {

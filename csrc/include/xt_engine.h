@@ -63,6 +63,10 @@ int xt_engine_nodes(void *plan);
 // files/offsets [experts * nodes]: record of expert e's node part n (file -1: never cold). scores: initial use counts.
 int xt_engine_cold_attach(void *plan, void *store, const int32_t *files, const long long *offsets, const float *scores,
                           float half_life);
+// The same with one location per piece: files / offsets [experts * nodes * 6] (pieces of a record may sit on different
+// drives, e.g. records split into units).
+int xt_engine_cold_attach_pieces(void *plan, void *store, const int32_t *files, const long long *offsets,
+                                 const float *scores, float half_life);
 // out[4]: forwards, experts read from NVMe, seconds waited for reads, decode forwards.
 void xt_engine_cold_stats(void *plan, double *out4);
 // CPUs the workers would bind to for `threads`.

@@ -56,6 +56,7 @@ def lib():
         L.xt_engine_slot_pieces.argtypes = [_P, _I, _I, _P, _P]
         L.xt_engine_nodes.argtypes = [_P]
         L.xt_engine_cold_attach.argtypes = [_P, _P, _P, _P, _P, _F]
+        L.xt_engine_cold_attach_pieces.argtypes = [_P, _P, _P, _P, _P, _F]
         L.xt_engine_cold_stats.argtypes = [_P, _P]
         L.xt_engine_worker_cpus.argtypes = [_I, _P, _I]
         L.xt_engine_isa.restype = C.c_char_p
@@ -225,6 +226,17 @@ class CpuEngine:
         s = None if scores is None else np.ascontiguousarray(scores, dtype=np.float32)
         rc = lib().xt_engine_cold_attach(self.plan, store.handle, f.ctypes.data, o.ctypes.data,
                                          None if s is None else s.ctypes.data, half_life)
+        if rc != 0:
+            raise RuntimeError('xtier_b200 engine: cold attach failed')
+        self._cold = (store, f, o, s)
+
+    def attach_cold_pieces(self, store: 'ColdStore', files, offsets, scores=None, half_life: float = 64.0):
+        """As attach_cold with one (file, offset) per piece: arrays [experts * nodes * 6]."""
+        f = np.ascontiguousarray(files, dtype=np.int32)
+        o = np.ascontiguousarray(offsets, dtype=np.int64)
+        s = None if scores is None else np.ascontiguousarray(scores, dtype=np.float32)
+        rc = lib().xt_engine_cold_attach_pieces(self.plan, store.handle, f.ctypes.data, o.ctypes.data,
+                                                None if s is None else s.ctypes.data, half_life)
         if rc != 0:
             raise RuntimeError('xtier_b200 engine: cold attach failed')
         self._cold = (store, f, o, s)
