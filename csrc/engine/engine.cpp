@@ -804,7 +804,7 @@ void *xt_engine_create(int hidden, int inter, int experts, int shared, int slots
         p->pins.assign(slots, 0);
         p->score.assign(experts, 0.f);
         for (int s = 0; s < slots; ++s) {
-            int e = resident ? resident[s] : s;
+            int e = resident ? resident[s] : (w13 ? s : -1);   // unfilled slots hold no expert unless named
             if (e >= 0 && e < experts) {
                 p->expert_of[s] = e;
                 p->slot_of[e] = s;
@@ -903,10 +903,14 @@ int xt_engine_slot_table(void *plan, int32_t *table) {
 
 int xt_engine_place(void *plan, int expert, int slot) {
     Plan *p = static_cast<Plan *>(plan);
-    if (!p || expert < 0 || expert >= p->E || slot < 0 || slot >= p->slots) return -2;
+    if (!p || expert < -1 || expert >= p->E || slot < 0 || slot >= p->slots) return -2;
     if (p->busy.load()) return -3;
     int old = p->expert_of[slot];
     if (old >= 0) p->slot_of[old] = -1;
+    if (expert < 0) {          // vacate the slot
+        p->expert_of[slot] = -1;
+        return old;
+    }
     int prev = p->slot_of[expert];
     if (prev >= 0) p->expert_of[prev] = -1;
     p->expert_of[slot] = expert;

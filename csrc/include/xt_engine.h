@@ -47,7 +47,8 @@ void xt_engine_last_timings(void *plan, double *out2);
 void xt_engine_tail_stats(void *plan, double *out3);
 // Slot of every routed expert (-1 if not in RAM): table[experts]. Returns slots.
 int xt_engine_slot_table(void *plan, int32_t *table);
-// Mark `expert` as held by `slot` after its weights were written there. Returns the previous expert of the slot or -1;
+// Mark `expert` as held by `slot` after its weights were written there (expert -1: the slot holds nothing). Returns
+// the previous expert of the slot or -1;
 // -2 bad arguments, -3 a forward in progress.
 int xt_engine_place(void *plan, int expert, int slot);
 // Global scales of every routed expert (g13 [E, 2], g2 [E]); from then on a slot takes the scales of the expert placed

@@ -99,6 +99,58 @@ def test_engine_reads_misses_from_the_store(tmp_path, fmt):
     pool.close()
 
 
+def test_three_unit_records_dealt_by_bytes(tmp_path):
+    """Records cut into gate / up / rest units: each unit is dealt to a drive on its own, the engine reads the pieces
+    of one record from several drives, and start-up fill, CRC checks and relayout work per unit."""
+    from xtier_b200.tools.cold_relayout import relayout
+    ew = _experts(formats.NVFP4, seed=9)
+    full = CpuEngine(ew, threads=2)
+    N = full.nodes()
+    dirs = [tmp_path / 'a', tmp_path / 'b', tmp_path / 'c']
+    pool = cold.ColdPool(dirs, units=3)
+    pool.write_layer(0, ew, N)
+    ent = pool.entry(0)
+    assert ent['units'] == 3 and len(ent['loc']) == E * N * 3
+    assert sum(ent['unit_bytes']) == ent['record']
+    per_drive = [0, 0, 0]
+    for i, (d, _) in enumerate(ent['loc']):
+        per_drive[d] += ent['unit_bytes'][i % 3]
+    assert max(per_drive) - min(per_drive) <= max(ent['unit_bytes'])          # bytes dealt evenly
+    assert any(len({ent['loc'][r * 3 + u][0] for u in range(3)}) > 1 for r in range(E * N))   # records span drives
+    assert pool.layer_ok(0, H, I, ew.fmt, N, E)
+    assert not cold.ColdPool(dirs, units=1).layer_ok(0, H, I, ew.fmt, N, E)   # another unit count: rewrite
+    back = pool.load_layer(0)
+    assert torch.equal(back.w13, ew.w13) and torch.equal(back.s13, ew.s13) and torch.equal(back.w2, ew.w2)
+    assert torch.equal(back.s2, ew.s2)
+    # a bad unit is reported by its own index
+    d, off = ent['loc'][7]
+    with open(pool.files[d], 'r+b') as f:
+        f.seek(off + 3)
+        f.write(b'\x5a' * 2)
+    assert pool.check_layer(0) == [7]
+    pool.write_layer(0, ew, N)
+    assert pool.check_layer(0) == []
+    # misses come from three drives; start-up fill reads per piece
+    eng = CpuEngine(ew, threads=2, slots=4, fill=False)
+    pool.fill_engine(eng, 0, [1, 4, -1, -1])
+    pool.attach(eng, 0)
+    for i in range(4):
+        x, ids, w = _routes(1, 3, seed=30 + i)
+        assert torch.equal(eng.forward(x, ids, w), full.forward(x, ids, w)), i
+    assert eng.cold_stats()['reads'] > 0
+    eng.close()
+    full.close()
+    pool.close()
+    # relayout back to whole-shard records on one drive, and to 3 units again
+    rep = relayout(','.join(map(str, dirs)), str(tmp_path / 'one'), units=1, log=lambda s: None)
+    assert rep[0]['units'] == E * N
+    rep = relayout(str(tmp_path / 'one'), str(tmp_path / 'three'), units=3, log=lambda s: None)
+    assert rep[0]['units'] == E * N * 3
+    p3 = cold.ColdPool(tmp_path / 'three', units=3)
+    assert torch.equal(p3.load_layer(0).w13, ew.w13)
+    p3.close()
+
+
 def test_fill_engine_from_store(tmp_path):
     ew = _experts(seed=7)
     pool = cold.ColdPool([tmp_path / 'a'])

@@ -11,8 +11,9 @@ Files: `<dir>/<key>.xtc` on every drive directory; the manifest `<first dir>/<ke
 
     {"version": 1, "key": ..., "drives": [...], "parts": [...], "end": [next free byte per drive],
      "layers": {"<layer>": {"shape": [H, I, fmt, nodes], "experts": E, "record": bytes,
-                            "loc": [[drive, offset] for expert-major (expert, node)],
-                            "crc": [[crc32 of the first 4 KiB, of the last 4 KiB] per record],
+                            "units": 1 or 3, "unit_bytes": [...],
+                            "loc": [[drive, offset] for every (expert, node, unit), in that order],
+                            "crc": [[crc32 of the first 4 KiB, of the last 4 KiB] per unit],
                             "source": [[name, size, mtime_ns] per checkpoint file], "g13": [...], "g2": [...]}}}
 
 The manifest is rewritten (temporary file + rename) only after a layer's records are on the drives: the store
@@ -22,8 +23,9 @@ per layer, where each expert tensor sits in the checkpoint file it was loaded fr
 
 Reference parity: docs/design-cold-experts.md (record = the engine slot's six pieces per NUMA shard, shards dealt over
 drives by XTIER_COLD_PARTS, KEY.json with per-record CRC of the first / last 4 KiB and the checkpoint source id,
-KEY.ranges, fill RAM slots from the store at start, decayed-use victim choice), xtier/cache/cold.py:142-240 (manifest
-reuse), :248 LayerPlan, :454 attach. The whole-shard records (no 3-unit split) and the JSON fields are this project's.
+KEY.ranges, fill RAM slots from the store at start, decayed-use victim choice, XTIER_COLD_UNITS=3 records cut into
+gate / up / rest units dealt over the drives), xtier/cache/cold.py:142-240 (manifest reuse), :248 LayerPlan, :454
+attach. The byte-weighted dealing and the JSON fields are this project's.
 """
 from __future__ import annotations
 
@@ -54,6 +56,25 @@ def piece_bytes(H: int, I: int, fmt: str, nodes: int) -> list[int]:
 
 def record_bytes(H: int, I: int, fmt: str, nodes: int) -> int:
     return sum(_pad(b) for b in piece_bytes(H, I, fmt, nodes))
+
+
+# A record can be cut into units dealt to drives of their own: 1 unit (the whole shard) or 3 (gate rows, up rows, the
+# scales and down rows: about a third each), for drive sets whose speeds or count do not divide the shards evenly.
+UNIT_GROUPS = {1: [[0, 1, 2, 3, 4, 5]], 3: [[0], [1], [2, 3, 4, 5]]}
+
+
+def _dir_list(dirs) -> list:
+    """Drive directories from a comma separated string, one path, or a list of paths."""
+    if isinstance(dirs, str):
+        return [d for d in dirs.split(',') if d]
+    if isinstance(dirs, os.PathLike):
+        return [dirs]
+    return list(dirs)
+
+
+def unit_bytes(H: int, I: int, fmt: str, nodes: int, units: int) -> list[int]:
+    pb = piece_bytes(H, I, fmt, nodes)
+    return [sum(_pad(pb[q]) for q in g) for g in UNIT_GROUPS[units]]
 
 
 def shard_pieces(ew: ExpertWeights, e: int, n: int, nodes: int) -> list[np.ndarray]:
@@ -99,9 +120,15 @@ def parse_parts(spec: str | None, drives: int) -> list[float]:
 class ColdPool:
     """The cold-expert store of a model: record files on `dirs` (one per drive) and their manifest."""
 
-    def __init__(self, dirs, key: str = 'xtier-cold', parts=None, threads: int = 4):
+    def __init__(self, dirs, key: str = 'xtier-cold', parts=None, threads: int = 4, units: int | None = None):
         from ..engine import ColdStore
-        self.dirs = [Path(d) for d in (dirs.split(',') if isinstance(dirs, str) else dirs)]
+        if units is None:
+            from .. import config
+            units = config.get('XTIER_COLD_UNITS')
+        if units not in UNIT_GROUPS:
+            raise ValueError(f'cold store: units must be one of {sorted(UNIT_GROUPS)}, got {units}')
+        self.units = units
+        self.dirs = [Path(d) for d in _dir_list(dirs)]
         if not self.dirs:
             raise ValueError('cold store: no directories')
         for d in self.dirs:
@@ -120,8 +147,7 @@ class ColdPool:
 
     @staticmethod
     def files_for(dirs, key: str) -> list[str]:
-        dirs = dirs.split(',') if isinstance(dirs, str) else dirs
-        return [str(Path(d) / f'{key}.xtc') for d in dirs]
+        return [str(Path(d) / f'{key}.xtc') for d in _dir_list(dirs)]
 
     # ---------------------------------------------------------------- manifest
     def _load_manifest(self):
@@ -145,28 +171,33 @@ class ColdPool:
         return self.manifest['layers'][str(layer)]
 
     # ---------------------------------------------------------------- layout
-    def _deal(self, E: int, nodes: int) -> list[int]:
-        """Drive of every (expert, node) record: the drive furthest below its weighted share takes the next one."""
+    def _deal(self, E: int, nodes: int, usizes: list[int]) -> list[int]:
+        """Drive of every (expert, node, unit): the drive that stays furthest below its weighted share of the bytes
+        takes the next unit."""
         load = [0.0] * len(self.files)
         out = []
         for _ in range(E * nodes):
-            d = min(range(len(self.files)), key=lambda i: (load[i] / self.parts[i], i))
-            load[d] += 1.0
-            out.append(d)
+            for b in usizes:
+                d = min(range(len(self.files)), key=lambda i: ((load[i] + b) / self.parts[i], i))
+                load[d] += b
+                out.append(d)
         return out
 
-    def _allocate(self, layer: int, E: int, nodes: int, rec: int) -> list[list[int]]:
+    def _allocate(self, layer: int, E: int, nodes: int, usizes: list[int]) -> list[list[int]]:
         old = self.manifest['layers'].get(str(layer))
-        drives = self._deal(E, nodes)
-        if old is not None and old['record'] == rec and len(old['loc']) == E * nodes and \
-                [d for d, _ in old['loc']] == drives:
-            return [list(x) for x in old['loc']]     # same size and dealing: rewrite in place
-        step = _pad(rec, ALIGN)
+        drives = self._deal(E, nodes, usizes)
+        if old is not None and old.get('unit_bytes', [old['record']]) == usizes and len(old['loc']) == len(drives) \
+                and [d for d, _ in old['loc']] == drives:
+            return [list(x) for x in old['loc']]     # same sizes and dealing: rewrite in place
         loc = []
-        for d in drives:
+        for i, d in enumerate(drives):
             loc.append([d, self.manifest['end'][d]])
-            self.manifest['end'][d] += step
+            self.manifest['end'][d] += _pad(usizes[i % len(usizes)], ALIGN)
         return loc
+
+    @staticmethod
+    def _units_of(ent: dict) -> tuple[int, list[int]]:
+        return ent.get('units', 1), ent.get('unit_bytes', [ent['record']])
 
     # ---------------------------------------------------------------- write / check
     def write_layer(self, layer: int, ew: ExpertWeights, nodes: int, source=None, checkpoint: str | None = None,
@@ -174,21 +205,26 @@ class ColdPool:
         """Writes every record of the layer, then the manifest entry (and the checkpoint ranges when given)."""
         E, H, I = ew.experts, ew.hidden, ew.inter
         rec = record_bytes(H, I, ew.fmt, nodes)
-        loc = self._allocate(layer, E, nodes, rec)
+        usizes = unit_bytes(H, I, ew.fmt, nodes, self.units)
+        groups = UNIT_GROUPS[self.units]
+        loc = self._allocate(layer, E, nodes, usizes)
         crc = []
         for e in range(E):
             for n in range(nodes):
-                d, off = loc[e * nodes + n]
                 pieces = shard_pieces(ew, e, n, nodes)
-                self.store.write(d, off, pieces)
-                buf = np.zeros(rec, dtype=np.uint8)
-                o = 0
-                for p in pieces:
-                    buf[o:o + p.size] = p
-                    o += _pad(p.size)
-                crc.append(_crc_pair(buf))
+                for u, g in enumerate(groups):
+                    d, off = loc[(e * nodes + n) * len(groups) + u]
+                    ps = [pieces[q] for q in g]
+                    self.store.write(d, off, ps)
+                    buf = np.zeros(usizes[u], dtype=np.uint8)
+                    o = 0
+                    for p in ps:
+                        buf[o:o + p.size] = p
+                        o += _pad(p.size)
+                    crc.append(_crc_pair(buf))
         self.manifest['layers'][str(layer)] = dict(
-            shape=[H, I, ew.fmt, nodes], experts=E, record=rec, loc=loc, crc=crc, source=source or [],
+            shape=[H, I, ew.fmt, nodes], experts=E, record=rec, units=self.units, unit_bytes=usizes, loc=loc,
+            crc=crc, source=source or [],
             g13=ew.g13.detach().float().cpu().reshape(-1).tolist(), g2=ew.g2.detach().float().cpu().reshape(-1).tolist())
         self._save_manifest()
         if checkpoint is not None and tensor_ranges is not None:
@@ -211,25 +247,35 @@ class ColdPool:
             return {}
 
     def read_record(self, layer: int, e: int, n: int) -> np.ndarray:
+        """The whole (expert, node) record (its units put back together in piece order)."""
         ent = self.entry(layer)
         N = ent['shape'][3]
-        d, off = ent['loc'][e * N + n]
+        U, usizes = self._units_of(ent)
         buf = _aligned(ent['record'])
-        self.store.read([d], [off], [buf.ctypes.data], [ent['record']], 1)
+        files, offs, dst = [], [], []
+        o = 0
+        for u in range(U):
+            d, off = ent['loc'][(e * N + n) * U + u]
+            files.append(d)
+            offs.append(off)
+            dst.append(buf[o:].ctypes.data)
+            o += usizes[u]
+        self.store.read(files, offs, dst, usizes, 1)
         return buf
 
     def check_layer(self, layer: int) -> list[int]:
-        """Indices (expert * nodes + node) of the records whose first / last 4 KiB do not match their CRCs."""
+        """Indices ((expert * nodes + node) * units + unit) of the units whose first / last 4 KiB do not match their
+        CRCs."""
         ent = self.entry(layer)
-        rec = ent['record']
-        k = min(ALIGN, rec)
+        U, usizes = self._units_of(ent)
+        ks = [min(ALIGN, usizes[i % U]) for i in range(len(ent['loc']))]
         bad = []
-        heads = [_aligned(k) for _ in ent['loc']]
-        tails = [_aligned(k) for _ in ent['loc']]
+        heads = [_aligned(k) for k in ks]
+        tails = [_aligned(k) for k in ks]
         files = [d for d, _ in ent['loc']] * 2
-        offs = [o for _, o in ent['loc']] + [o + rec - k for _, o in ent['loc']]
+        offs = [o for _, o in ent['loc']] + [o + usizes[i % U] - ks[i] for i, (_, o) in enumerate(ent['loc'])]
         try:
-            self.store.read(files, offs, [b.ctypes.data for b in heads + tails], [k] * len(files), 1)
+            self.store.read(files, offs, [b.ctypes.data for b in heads + tails], ks + ks, 1)
         except OSError:
             return list(range(len(ent['loc'])))
         for i, (h, t) in enumerate(zip(heads, tails)):
@@ -243,9 +289,12 @@ class ColdPool:
             return False
         if ent['record'] != record_bytes(H, I, fmt, nodes):
             return False
+        U, usizes = self._units_of(ent)
+        if U != self.units or usizes != unit_bytes(H, I, fmt, nodes, U):
+            return False
         if source is not None and ent['source'] != source:
             return False
-        if [d for d, _ in ent['loc']] != self._deal(E, nodes):
+        if [d for d, _ in ent['loc']] != self._deal(E, nodes, usizes):
             return False
         return not self.check_layer(layer)
 
@@ -261,8 +310,19 @@ class ColdPool:
 
     # ---------------------------------------------------------------- engine side
     def locations(self, layer: int) -> tuple[np.ndarray, np.ndarray]:
-        loc = np.asarray(self.entry(layer)['loc'], dtype=np.int64).reshape(-1, 2)
-        return loc[:, 0].astype(np.int32), loc[:, 1]
+        """(file, offset) of every piece, [experts * nodes * 6] in (expert, node, piece) order."""
+        ent = self.entry(layer)
+        H, I, fmt, N = ent['shape']
+        U, _ = self._units_of(ent)
+        pb = piece_bytes(H, I, fmt, N)
+        files, offs = [], []
+        for i, (d, off) in enumerate(ent['loc']):
+            o = off
+            for q in UNIT_GROUPS[U][i % U]:
+                files.append(d)
+                offs.append(o)
+                o += _pad(pb[q])
+        return np.asarray(files, dtype=np.int32), np.asarray(offs, dtype=np.int64)
 
     def scales(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
         ent = self.entry(layer)
@@ -278,27 +338,29 @@ class ColdPool:
         g13, g2 = self.scales(layer)
         engine.set_expert_scales(g13, g2)
         files, offs = self.locations(layer)
-        engine.attach_cold(self.store, files, offs, scores, half_life)
+        engine.attach_cold_pieces(self.store, files, offs, scores, half_life)
 
     def fill_engine(self, engine, layer: int, resident):
         """Reads the resident experts' records straight into the engine's RAM slots (start-up without the
         checkpoint's expert tensors): slot s <- expert resident[s]."""
         ent = self.entry(layer)
         N = ent['shape'][3]
+        pf, po = self.locations(layer)
         files, offs, dst, sizes = [], [], [], []
         for s, e in enumerate(resident):
             if e < 0:
+                engine.place(-1, s)
                 continue
             engine.place(int(e), s)
             for n in range(N):
                 ptrs, szs = engine.slot_pieces(s, n)
-                d, off = ent['loc'][int(e) * N + n]
-                files.append(d)
-                offs.append(off)
+                base = (int(e) * N + n) * 6
+                files += pf[base:base + 6].tolist()
+                offs += po[base:base + 6].tolist()
                 dst += ptrs
                 sizes += [_pad(b) for b in szs]
         if files:
-            self.store.read(files, offs, dst, sizes, 6)
+            self.store.read(files, offs, dst, sizes, 1)
 
     def load_layer(self, layer: int) -> ExpertWeights:
         """The layer's experts rebuilt from the records (the only copy once the checkpoint's tensors are punched)."""

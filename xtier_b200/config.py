@@ -69,6 +69,7 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_COLD_FRACTION', 'float', 0.0, 'share of each layer\'s experts kept cold (not in RAM)'),
     _S('XTIER_COLD_THREADS', 'int', 4, 'reader threads per cold-store file'),
     _S('XTIER_COLD_PARTS', 'str', '', 'cold records dealt over the drives by these weights, e.g. 5:5:2 (default equal)'),
+    _S('XTIER_COLD_UNITS', 'int', 1, 'units per cold record (1: whole NUMA shards; 3: gate / up / rest dealt apart)'),
     _S('XTIER_COLD_HALF_LIFE', 'float', 50.0, 'half life (engine calls) of the use counts that pick cold victims'),
     _S('XTIER_FAST_LOAD', 'flag', False, 'read expert tensors straight from safetensors into engine shards (O_DIRECT)'),
     _S('XTIER_LOAD_DIGEST', 'flag', False, 'log a digest of every loaded layer'),

@@ -183,6 +183,7 @@ class CpuEngine:
         return t
 
     def place(self, expert: int, slot: int) -> int:
+        """Slot `slot` now holds `expert` (-1: nothing); returns the expert it held before (-1: none)."""
         return lib().xt_engine_place(self.plan, expert, slot)
 
     def set_expert_scales(self, g13: torch.Tensor, g2: torch.Tensor):
