@@ -151,6 +151,86 @@ def test_three_unit_records_dealt_by_bytes(tmp_path):
     p3.close()
 
 
+def _offset_stage(n, fmt, shift):
+    """Host staging tensors whose rows start `shift` bytes past a 4 KiB boundary (exercises the bounce reads)."""
+    bs = 16 if fmt == formats.NVFP4 else 32
+    shapes = [(n, 2 * I, H // 2), (n, H, I // 2), (n, 2 * I, H // bs), (n, H, I // bs)]
+    out = []
+    for sh in shapes:
+        raw = cold._aligned(int(np.prod(sh)) + 8192)
+        out.append(torch.from_numpy(raw[shift:shift + int(np.prod(sh))]).view(sh))
+    return formats.ExpertWeights(fmt, *out, torch.empty(n, 2), torch.empty(n))
+
+
+@pytest.mark.parametrize('units', [1, 3])
+def test_cold_prefill_staging_from_ram_and_drives(tmp_path, units):
+    """The GPU prefill's host staging of a cold-backed layer: experts in the engine's RAM slots are copied from the
+    slots, the others read from the drives; bytes and global scales equal the layer's; a threaded fill waits for the
+    previous upload out of the same buffer."""
+    ew = _experts(formats.NVFP4, seed=11)
+    pool = cold.ColdPool([tmp_path / 'a', tmp_path / 'b'], units=units)
+    gpu_hot = [0, 5]
+    eng = cold.cold_engine(2, ew, pool, 0.5, popularity=torch.arange(E, 0, -1).float(), gpu_hot=gpu_hot, threads=2)
+    non_gpu = [e for e in range(E) if e not in gpu_hot]
+    cp = cold.ColdPrefill(pool, 2, eng, non_gpu)
+    want = ew.select(torch.tensor(non_gpu))
+    st = cp.stage()                                        # no read-ahead started: fills now
+    for f in ('w13', 'w2', 's13', 's2'):
+        assert torch.equal(getattr(st, f), getattr(want, f)), f
+    assert torch.equal(st.g13, want.g13.float()) and torch.equal(st.g2, want.g2.float())
+    assert cp.stats['from_ram'] > 0 and cp.stats['from_drive'] > 0
+    assert cp.stats['from_ram'] + cp.stats['from_drive'] == len(non_gpu)
+
+    class Ev:          # the upload out of the buffer: the next fill of the same parity must wait for it
+        done = False
+
+        def synchronize(self):
+            Ev.done = True
+    cp.uploaded(Ev())
+    st.w13.zero_()
+    cp.start()
+    st = cp.stage()
+    assert Ev.done and torch.equal(st.w13, want.w13)
+    # unaligned destinations go through bounce buffers; a subset in any order
+    sub = [non_gpu[3], non_gpu[0]]
+    st2 = _offset_stage(2, formats.NVFP4, 64)
+    cp.fill(st2, sub)
+    got = cp.read_experts(sub)
+    ref = ew.select(torch.tensor(sub))
+    for f in ('w13', 'w2', 's13', 's2'):
+        assert torch.equal(getattr(st2, f), getattr(ref, f)) and torch.equal(getattr(got, f), getattr(ref, f)), f
+    eng.close()
+    pool.close()
+
+
+def test_cold_mode_swap_sources_the_store(tmp_path):
+    """A GPU-slot swap in cold mode (no host copy of the layer): the incoming expert comes from the engine or the
+    drives, and the victim takes the incoming expert's place in the prefill staging."""
+    from xtier_b200.cache.pool import TieredMoE
+    ew = _experts(formats.NVFP4, seed=12)
+    pool = cold.ColdPool([tmp_path / 'a'])
+    hot = [1, 2]
+    eng = cold.cold_engine(0, ew, pool, 0.5, popularity=torch.arange(E, 0, -1).float(), gpu_hot=hot, threads=2)
+    router = torch.randn(E, H)
+    moe = TieredMoE(0, router, ew, 2, hot=hot, engine=eng, device='cpu', host_experts=None)
+    assert not moe.can_refill
+    moe.attach_cold_prefill(cold.ColdPrefill(pool, 0, eng, [e for e in range(E) if e not in hot]))
+    assert moe.can_refill
+    incoming, victim = 6, 2
+    idx = int(moe._cold_index[incoming])
+    moe.swap(incoming, victim)
+    slot = int(moe.table_host[incoming])
+    assert slot == 1 and int(moe.table_host[victim]) == -1
+    for f in ('w13', 'w2', 's13', 's2'):
+        assert torch.equal(getattr(moe.pool, f)[slot], getattr(ew, f)[incoming]), f
+    assert float(moe.pool.g2[slot]) == float(ew.g2[incoming])
+    assert int(moe._cold_index[victim]) == idx and int(moe._cold_index[incoming]) == -1
+    st = moe.cold_prefill.stage()
+    assert torch.equal(st.w13[idx], ew.w13[victim])
+    eng.close()
+    pool.close()
+
+
 def test_fill_engine_from_store(tmp_path):
     ew = _experts(seed=7)
     pool = cold.ColdPool([tmp_path / 'a'])

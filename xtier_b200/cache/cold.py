@@ -400,6 +400,170 @@ class ColdPool:
             self.store = None
 
 
+_HOST_STAGE: dict = {}   # (experts, H, I, fmt, parity, pinned) -> [host staging, event of its last upload or None]
+
+
+class ColdPrefill:
+    """The host side of a GPU prefill of a layer whose CPU-tier experts live in a cold-backed engine (RAM slots plus
+    the drive store), so that no full host copy of the layer is kept.
+
+    The layer's non-GPU experts (`cold`, in staging order) are gathered into a host staging buffer in the expert
+    layout the GPU staging pool uses: an expert in one of the engine's RAM slots is copied from the slot (pinned
+    while it is copied, so a concurrent miss cannot evict it), any other one is read from its records with O_DIRECT
+    straight into its rows (through a bounce buffer when a piece is not a whole number of 512-byte blocks). Two host
+    buffers per shape are shared by all layers (layer parity); a fill first waits until the previous upload out of
+    its buffer is done. `start()` runs the fill on a thread (the next layer's read-ahead while this layer computes);
+    `stage()` waits for it (or fills now) and returns the buffer.
+    (Reference parity: xtier/cache/cold.py:646-790 PrefillCold -- cold experts read into a pinned staging by layer
+    parity, the next layer read ahead; here RAM-slot experts come from the engine, and every non-GPU expert is staged
+    since the routes of the next layer are not known yet.)
+    """
+
+    def __init__(self, pool: ColdPool, layer: int, engine, cold):
+        ent = pool.entry(layer)
+        self.H, self.I, self.fmt, self.N = ent['shape']
+        self.pool, self.layer, self.engine = pool, layer, engine
+        self.cold = [int(e) for e in cold]
+        self.K = len(self.cold)
+        self.bs = 16 if self.fmt == NVFP4 else 32
+        self.files, self.offs = pool.locations(layer)
+        self.g13, self.g2 = pool.scales(layer)     # every expert's global scales
+        self.pb = piece_bytes(self.H, self.I, self.fmt, self.N)
+        self.pinned = torch.cuda.is_available()
+        self._thread = None
+        self._box: dict = {}
+        self.stats = dict(fills=0, from_ram=0, from_drive=0, bytes_read=0, wait_s=0.0)
+
+    # ------------------------------------------------------------------ buffers
+    def _key(self):
+        return (self.K, self.H, self.I, self.fmt, self.layer % 2, self.pinned)
+
+    def _buffer(self) -> list:
+        cur = _HOST_STAGE.get(self._key())
+        if cur is None:
+            K, H, I, bs = self.K, self.H, self.I, self.bs
+            shapes = [('w13', (K, 2 * I, H // 2), torch.uint8), ('w2', (K, H, I // 2), torch.uint8),
+                      ('s13', (K, 2 * I, H // bs), torch.uint8), ('s2', (K, H, I // bs), torch.uint8),
+                      ('g13', (K, 2), torch.float32), ('g2', (K,), torch.float32)]
+            sizes = [_pad(int(np.prod(sh)) * torch.tensor([], dtype=dt).element_size(), ALIGN) for _, sh, dt in shapes]
+            raw = torch.empty(sum(sizes) + ALIGN, dtype=torch.uint8, pin_memory=self.pinned)
+            o = (-raw.data_ptr()) % ALIGN
+            fields = {}
+            for (name, sh, dt), n in zip(shapes, sizes):
+                nb = int(np.prod(sh)) * torch.tensor([], dtype=dt).element_size()
+                fields[name] = raw[o:o + nb].view(dt).view(sh)
+                o += n
+            cur = _HOST_STAGE[self._key()] = [ExpertWeights(self.fmt, *(fields[f] for f in
+                                                                         ('w13', 'w2', 's13', 's2', 'g13', 'g2'))),
+                                              None]
+        return cur
+
+    def uploaded(self, event):
+        """The upload out of this layer's host buffer was enqueued; `event` completes with it."""
+        self._buffer()[1] = event
+
+    # ------------------------------------------------------------------ fill
+    def _dests(self, st: ExpertWeights, i: int, n: int) -> list[int]:
+        """Addresses of staging row i's six pieces for node n (the rows a node shard covers are contiguous)."""
+        H, I, N, bs = self.H, self.I, self.N, self.bs
+        gr, dr = I // N, H // N
+        w13, s13, w2, s2 = st.w13.data_ptr(), st.s13.data_ptr(), st.w2.data_ptr(), st.s2.data_ptr()
+        return [w13 + (i * 2 * I + n * gr) * (H // 2), w13 + (i * 2 * I + I + n * gr) * (H // 2),
+                s13 + (i * 2 * I + n * gr) * (H // bs), s13 + (i * 2 * I + I + n * gr) * (H // bs),
+                w2 + (i * H + n * dr) * (I // 2), s2 + (i * H + n * dr) * (I // bs)]
+
+    def fill(self, st: ExpertWeights, experts=None):
+        """Gathers `experts` (default: every non-GPU expert, in staging order) into rows 0.. of `st` (synchronous)."""
+        import ctypes
+        experts = list(self.cold) if experts is None else [int(e) for e in experts]
+        files, offs, dst, sizes, bounce = [], [], [], [], []
+        for i, e in enumerate(experts):
+            slot = self.engine.pin(e) if self.engine is not None else -1
+            try:
+                if slot >= 0:
+                    for n in range(self.N):
+                        ptrs, szs = self.engine.slot_pieces(slot, n)
+                        for d, sp, b in zip(self._dests(st, i, n), ptrs, szs):
+                            ctypes.memmove(d, sp, b)
+                    self.stats['from_ram'] += 1
+                    continue
+            finally:
+                if slot >= 0:
+                    self.engine.unpin(slot)
+            for n in range(self.N):
+                base = (e * self.N + n) * 6
+                for q, d in enumerate(self._dests(st, i, n)):
+                    b = self.pb[q]
+                    files.append(int(self.files[base + q]))
+                    offs.append(int(self.offs[base + q]))
+                    if b % 512 == 0 and d % 512 == 0:
+                        dst.append(d)
+                    else:   # a ragged piece: read its padded bytes aside, copy the piece
+                        buf = _aligned(_pad(b))
+                        bounce.append((d, buf, b))
+                        dst.append(buf.ctypes.data)
+                    sizes.append(_pad(b))
+            self.stats['from_drive'] += 1
+        if files:
+            self.pool.store.read(files, offs, dst, sizes, 1)
+            self.stats['bytes_read'] += sum(sizes)
+        for d, buf, b in bounce:
+            ctypes.memmove(d, buf.ctypes.data, b)
+        idx = torch.tensor(experts, dtype=torch.long)
+        st.g13[:len(experts)].copy_(self.g13[idx])
+        st.g2[:len(experts)].copy_(self.g2[idx])
+        self.stats['fills'] += 1
+
+    def read_experts(self, experts) -> ExpertWeights:
+        """The given experts gathered into fresh host tensors (e.g. the source of a GPU slot swap)."""
+        n, H, I, bs = len(experts), self.H, self.I, self.bs
+        st = ExpertWeights(self.fmt, torch.empty(n, 2 * I, H // 2, dtype=torch.uint8),
+                           torch.empty(n, H, I // 2, dtype=torch.uint8),
+                           torch.empty(n, 2 * I, H // bs, dtype=torch.uint8),
+                           torch.empty(n, H, I // bs, dtype=torch.uint8),
+                           torch.empty(n, 2, dtype=torch.float32), torch.empty(n, dtype=torch.float32))
+        self.fill(st, experts)
+        return st
+
+    def _run(self, cur: list):
+        import time
+        t0 = time.perf_counter()
+        try:
+            st, ev = cur
+            if ev is not None:   # the previous layer of this parity has its upload out of the buffer done
+                dev = getattr(ev, 'device', None)
+                if dev is not None:
+                    torch.cuda.set_device(dev)   # this thread's current device is the event's
+                ev.synchronize()
+            self.fill(st)
+        except BaseException as ex:   # re-raised by stage()
+            self._box['err'] = ex
+        self._box['s'] = time.perf_counter() - t0
+
+    def start(self):
+        """Starts the fill on a thread (no-op while one runs)."""
+        import threading
+        if self._thread is None:
+            self._box = {}
+            cur = list(self._buffer())   # allocated (pinned) on the caller's thread and device
+            self._thread = threading.Thread(target=self._run, args=(cur,), daemon=True,
+                                            name=f'xtier-cold-prefill-{self.layer}')
+            self._thread.start()
+
+    def stage(self) -> ExpertWeights:
+        """The filled host buffer: waits for a started fill, or fills now."""
+        import time
+        t0 = time.perf_counter()
+        if self._thread is None:
+            self.start()
+        self._thread.join()
+        self._thread = None
+        self.stats['wait_s'] += time.perf_counter() - t0
+        if 'err' in self._box:
+            raise self._box['err']
+        return self._buffer()[0]
+
+
 def open_layer(pool: ColdPool, layer: int, path, nodes: int, prefix: str = 'experts.') -> ExpertWeights:
     """One layer's experts for a cold-backed engine: read from its checkpoint file (the records are written or
     checked against it and the tensor ranges kept for punching), or, once the file's expert tensors were punched out,

@@ -25,7 +25,7 @@ class AdaptivePolicy:
     def __init__(self, layers, mailbox, every: int | None = None, swaps: int | None = None,
                  min_gain: float | None = None, log_every: int | None = None):
         """layers: TieredMoE layers sharing `mailbox` (those with a CPU part)."""
-        self.layers = [l for l in layers if l.mailbox is not None and l.host is not None]
+        self.layers = [l for l in layers if l.mailbox is not None and l.can_refill]
         self.mailbox = mailbox
         self.every = every or config.get('XTIER_CACHE_EVERY')
         self.swaps = swaps or config.get('XTIER_CACHE_SWAPS')

@@ -94,6 +94,9 @@ class TieredMoE:
         self.table_local, self.shared_local = self.table, self.shared_slots
         # miss share (XTIER_DECODE_MISS_GPU): the pinned host pool's base addresses for the decode kernels
         self.host_table, self.share_min = None, 0
+        # cold-backed CPU tier (cache/cold.py ColdPrefill): the prefill staging is gathered from the engine's RAM
+        # slots and the drive store instead of a host copy of the layer
+        self.cold_prefill = None
         self._alloc(max_tokens)
 
     def _make_bufs(self, m: int) -> dict:
@@ -192,7 +195,8 @@ class TieredMoE:
     # ------------------------------------------------------------------ prefill (hybrid: GPU hot || CPU rest)
     def prefill(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None = None, chunk: int = 1024):
         grouped = (x.shape[0] >= config.get('XTIER_GPU_PREFILL_MIN') and self.pool is not None
-                   and (self.all_hot or self.host is not None or getattr(self, '_host_cold', None) is not None))
+                   and (self.all_hot or self.host is not None or getattr(self, '_host_cold', None) is not None
+                        or self.cold_prefill is not None))
         if grouped:   # every expert on the GPU: cold ones uploaded once for the whole call, larger chunks
             stage = None if self.all_hot else self._staged()
             chunk = 8192
@@ -267,6 +271,10 @@ class TieredMoE:
     def upload_async(self, stream: torch.cuda.Stream, after: torch.cuda.Event | None = None):
         """Starts this layer's cold-expert upload on `stream` (after `after`, e.g. the previous user of the staging
         buffer being done); the next prefill call of the layer waits for it instead of copying itself."""
+        if self.cold_prefill is not None:   # the drive reads start now; the copy is enqueued when they are done
+            self.cold_prefill.start()
+            self._pending = ('cold', stream, after)
+            return
         if self.all_hot or (self.host is None and getattr(self, '_host_cold', None) is None):
             return
         with torch.cuda.stream(stream):
@@ -279,17 +287,60 @@ class TieredMoE:
 
     def _staged(self) -> ExpertWeights:
         pending = getattr(self, '_pending', None)
+        self._pending = None
+        if self.cold_prefill is not None:
+            return self._upload_cold_prefill(*(pending[1:] if pending is not None else (None, None)))
         if pending is not None:
-            self._pending = None
             torch.cuda.current_stream(self.device).wait_event(pending[1])
             return pending[0]
         return self._upload_cold()
+
+    def attach_cold_prefill(self, cp):
+        """Prefill staging from a cold-backed CPU tier (cache/cold.py ColdPrefill over this layer's non-GPU experts,
+        in staging order)."""
+        cold = [e for e in range(self.E) if self.table_host[e] < 0]
+        if list(cp.cold) != cold:
+            raise ValueError(f'layer {self.layer}: the cold prefill covers other experts than the non-GPU ones')
+        idx = torch.full((self.E,), -1, dtype=torch.int32)
+        idx[cold] = torch.arange(len(cold), dtype=torch.int32)
+        self._cold_index = idx.to(self.device)
+        self.cold_prefill = cp
+
+    def _gpu_stage(self, like: ExpertWeights) -> ExpertWeights:
+        """The GPU staging pool for `like`'s shape (shared by the layers of one shape, two by layer parity)."""
+        key = (like.experts, self.H, self.I, self.fmt, self.device, self.layer % 2)
+        stage = _STAGING.get(key)
+        if stage is None:
+            stage = ExpertWeights(self.fmt, *[torch.empty_like(getattr(like, f), device=self.device)
+                                              for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
+            _STAGING[key] = stage
+        return stage
+
+    def _upload_cold_prefill(self, stream=None, after=None) -> ExpertWeights:
+        """Waits for the host staging of the cold-backed tier and copies it to the GPU staging on `stream` (after
+        `after`); the current stream waits for the copy."""
+        hc = self.cold_prefill.stage()
+        stage = self._gpu_stage(hc)
+        cur = torch.cuda.current_stream(self.device)
+        stream = cur if stream is None else stream
+        with torch.cuda.stream(stream):
+            if after is not None:
+                stream.wait_event(after)
+            for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+                getattr(stage, f).copy_(getattr(hc, f), non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        if stream != cur:
+            cur.wait_event(ev)
+        self.cold_prefill.uploaded(ev)
+        return stage
 
     def prepare_prefill(self):
         """Pinned host copy of the layer's cold experts (the source of the prefill uploads); done at model build so
         the first prefill does not pay for page-locking. With XTIER_DECODE_MISS_GPU it is also the pool the decode
         kernels read a shared CPU-tier expert from."""
-        if self.all_hot or self.host is None or getattr(self, '_host_cold', None) is not None:
+        if (self.all_hot or self.host is None or getattr(self, '_host_cold', None) is not None
+                or self.cold_prefill is not None):
             return
         self._upload_cold(copy=False)
         self._setup_miss_share()
@@ -328,18 +379,27 @@ class TieredMoE:
             self._host_cold.g13 = self._host_cold.g13.float().pin_memory()
             self._host_cold.g2 = self._host_cold.g2.float().pin_memory()
         hc = self._host_cold
-        key = (hc.experts, self.H, self.I, self.fmt, self.device, self.layer % 2)   # two buffers: layer parity
-        stage = _STAGING.get(key)
-        if stage is None:
-            stage = ExpertWeights(self.fmt, *[torch.empty_like(getattr(hc, f), device=self.device)
-                                              for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
-            _STAGING[key] = stage
+        stage = self._gpu_stage(hc)
         if copy:
             for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
                 getattr(stage, f).copy_(getattr(hc, f), non_blocking=True)
         return stage
 
     # ------------------------------------------------------------------ residency changes
+    @property
+    def can_refill(self) -> bool:
+        """Whether GPU slots can take other experts: a host copy or a cold-backed tier is their source, and no other
+        GPU reads this pool."""
+        return self.peer is None and (self.host is not None or self.cold_prefill is not None)
+
+    def _expert_host(self, e: int) -> ExpertWeights:
+        """Expert e on the host ([1, ...] fields): from the host copy, or gathered from the cold-backed tier."""
+        if self.host is not None:
+            return self.host.select([e])
+        if self.cold_prefill is not None:
+            return self.cold_prefill.read_experts([e])
+        raise RuntimeError(f'layer {self.layer}: no host source for expert {e}')
+
     def swap(self, incoming: int, victim: int):
         """Replaces hot expert `victim` by `incoming` (stream-ordered with every kernel launched so far/after)."""
         if self.peer is not None:
@@ -347,10 +407,11 @@ class TieredMoE:
         slot = int(self.table_host[victim])
         if slot < 0 or int(self.table_host[incoming]) >= 0:
             raise ValueError(f'swap {incoming} <- {victim}: bad residency')
+        src = self._expert_host(incoming)
         self.table[victim] = -1
         self.table_host[victim] = -1
         for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
-            getattr(self.pool, f)[slot].copy_(getattr(self.host, f)[incoming], non_blocking=True)
+            getattr(self.pool, f)[slot].copy_(getattr(src, f)[0], non_blocking=True)
         self.table[incoming] = slot
         self.table_host[incoming] = slot
         if slot >= len(self.hot):   # an elastic slot: both experts keep their prefill staging index
@@ -366,6 +427,11 @@ class TieredMoE:
             for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
                 getattr(self._host_cold, f)[idx].copy_(getattr(self.host, f)[victim])
             self._pending = None
+        elif self.cold_prefill is not None:   # the cold-backed staging gathers the victim in the incoming's place
+            idx = int(self._cold_index[incoming])
+            self._cold_index[victim] = idx
+            self._cold_index[incoming] = -1
+            self.cold_prefill.cold[idx] = victim
 
     def fill(self, incoming: int):
         """Puts a non-resident expert into an empty elastic slot (stream-ordered like `swap`). Experts in elastic
@@ -375,8 +441,9 @@ class TieredMoE:
             raise RuntimeError('elastic slots are off in peer mode')
         if slot is None or int(self.table_host[incoming]) >= 0:
             raise ValueError(f'fill {incoming}: no free elastic slot or already resident')
+        src = self._expert_host(incoming)
         for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
-            getattr(self.pool, f)[slot].copy_(getattr(self.host, f)[incoming], non_blocking=True)
+            getattr(self.pool, f)[slot].copy_(getattr(src, f)[0], non_blocking=True)
         self.table[incoming] = slot
         self.table_host[incoming] = slot
         self.elastic.occupant[slot - self.elastic.first] = incoming

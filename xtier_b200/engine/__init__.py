@@ -182,6 +182,13 @@ class CpuEngine:
         lib().xt_engine_slot_table(self.plan, t.ctypes.data)
         return t
 
+    def pin(self, expert: int) -> int:
+        """Keeps `expert` in its RAM slot (no miss evicts it) until `unpin`; returns the slot, -1 when not in RAM."""
+        return lib().xt_engine_slot_pin(self.plan, expert)
+
+    def unpin(self, slot: int):
+        lib().xt_engine_slot_unpin(self.plan, slot)
+
     def place(self, expert: int, slot: int) -> int:
         """Slot `slot` now holds `expert` (-1: nothing); returns the expert it held before (-1: none)."""
         return lib().xt_engine_place(self.plan, expert, slot)

@@ -188,8 +188,16 @@ class Qwen3MoeModel:
                                  pool_storage=self.peers.storage(li) if self.peers is not None else None)
             if sets is not None:
                 L['moe'].use_peers(self.peers.table(li), n_hot, prank, sets)
+            if self.cold is not None and engine is not None:
+                # prefill stages the CPU tier's experts from the engine's RAM slots and the drives; no host copy
+                from ..cache.cold import ColdPrefill
+                moe = L['moe']
+                moe.attach_cold_prefill(ColdPrefill(self.cold, li, engine,
+                                                    [e for e in range(cfg.experts) if int(moe.table_host[e]) < 0]))
             L['moe'].prepare_prefill()
-            if sets is not None:   # no swaps in peer mode: the pinned staging copy is all the host copy is kept for
+            if sets is not None or L['moe'].cold_prefill is not None:
+                # peer mode: no swaps, the pinned staging copy is all the host copy is kept for; cold mode: swaps
+                # and prefill read the engine and the drives
                 L['moe'].host = None
                 host = None
             del ew
@@ -392,7 +400,7 @@ class Qwen3MoeModel:
             r = self.bigram.rows_host(torch.cat([torch.tensor([0]), t[:-1]]), t).to(dev, f)
             x = x + (r @ self.bigram.proj.to(f).t() if self.bigram.proj is not None else r)
         mask = torch.ones(T, T, device=dev, dtype=torch.bool).tril()
-        for L in self.layers:
+        for li_ref, L in enumerate(self.layers):
             h = rms(x, L['in_norm'])
             qkv = (h @ L['qkv'].to(f).t()).view(T, Hq + 2 * Hkv, D)
             q = rope(rms(qkv[:, :Hq], L['q_norm']))
@@ -414,6 +422,9 @@ class Qwen3MoeModel:
             out = torch.zeros_like(x)
             if moe.host is not None:
                 src = {e: (moe.host, e) for e in range(moe.E)}
+            elif moe.cold_prefill is not None:   # cold mode: the layer rebuilt from the store's records
+                full = moe.cold_prefill.pool.load_layer(li_ref)
+                src = {e: (full, e) for e in range(moe.E)}
             else:   # this GPU's slots, and the pinned staging copy of the others (peer mode keeps no full copy)
                 src = {e: (moe.pool, s) for s, e in enumerate(moe.hot)}
                 hc = getattr(moe, '_host_cold', None)
