@@ -1,0 +1,180 @@
+"""The generation server's HTTP behaviour and the bench tools, against a stand-in backend on the CPU: validation,
+streaming, scoring, aborts, the queue limit; speed, perplexity / KL / token stability, abuse and interleave probes,
+and the verbatim-copy test."""
+import math
+import random
+import time
+
+import numpy as np
+import pytest
+
+from xtier_b200 import serve
+from xtier_b200.bench import copy_test, quality, robustness, speed
+from xtier_b200.bench.client import Client, ServerError
+
+V = 1000
+
+
+class Fake:
+    """A deterministic model: next token = (31 * last + 7) % vocab; position logits a fixed function of the token."""
+
+    def __init__(self, vocab=V, max_len=4096, delay=0.0005, shift=0.0, tokenizer=None, corrupt=False):
+        self.vocab, self.max_len, self.delay, self.shift = vocab, max_len, delay, shift
+        self.tokenizer, self.corrupt = tokenizer, corrupt
+        self.queue = None
+
+    def prefill(self, ids):
+        time.sleep(self.delay * (1 + len(ids) / 256))
+        self.last = ids[-1]
+        if self.tokenizer is not None:      # echo what sits between <src> and </src>
+            text = self.tokenizer.decode(ids)
+            a, b = text.index('<src>\n') + 6, text.index('\n</src>')
+            body = text[a:b]
+            if self.corrupt:
+                body = body.replace('e', 'E', 1)
+            self.queue = self.tokenizer.encode(body) + [self.tokenizer.eos_token_id]
+            return self.queue.pop(0)
+        return self.decode(sleep=False)
+
+    def decode(self, sleep=True):
+        if sleep:
+            time.sleep(self.delay)
+        if self.queue is not None:
+            return self.queue.pop(0) if self.queue else self.tokenizer.eos_token_id
+        self.last = (31 * self.last + 7) % self.vocab
+        return self.last
+
+    def _lp(self, t):
+        x = np.sin(np.arange(self.vocab) * (t + 1) * 0.01) * 3.0 + self.shift * np.cos(np.arange(self.vocab) * 0.37)
+        x = x - x.max()
+        return x - np.log(np.exp(x).sum())
+
+    def logprobs(self, ids, top):
+        nll, tops = [], []
+        for i in range(len(ids) - 1):
+            lp = self._lp(ids[i])
+            nll.append(float(-lp[ids[i + 1]]))
+            if top:
+                idx = np.argsort(-lp)[:top]
+                tops.append([(int(j), float(lp[j])) for j in idx])
+        return nll, tops
+
+    def check(self):
+        pass
+
+
+class CharTok:
+    eos_token_id = 3
+
+    def encode(self, s, add_special_tokens=False):
+        return [ord(c) for c in s]
+
+    def decode(self, ids, skip_special_tokens=False):
+        return ''.join(chr(t) for t in ids if t != self.eos_token_id)
+
+    def apply_chat_template(self, msgs, add_generation_prompt=True, tokenize=True, **kw):
+        return [1] + self.encode('user: ' + msgs[0]['content'] + '\nassistant: ')
+
+
+@pytest.fixture
+def server():
+    made = []
+
+    def make(backend, max_queue=8):
+        s = serve.Server(backend, max_queue)
+        srv = serve.serve(s, '127.0.0.1', 0)
+        made.append(srv)
+        return s, Client(f'http://127.0.0.1:{srv.server_address[1]}', timeout=60)
+    yield make
+    for srv in made:
+        srv.shutdown()
+        srv.server_close()
+
+
+def test_endpoints_validation_and_streaming(server):
+    s, cl = server(Fake())
+    st, h = cl.request('GET', '/health')
+    assert st == 200 and h['ready'] and h['vocab'] == V and h['max_len'] == 4096
+    full = cl.generate([5, 6, 7], 10)
+    assert len(full['ids']) == 10 and full['prompt_tokens'] == 3 and full['decode_tok_s'] > 0
+    x = cl.stream([5, 6, 7], 10)
+    assert x['ids'] == full['ids'] and x['server']['done'] and x['ttft_s'] > 0
+    stop = full['ids'][3]
+    assert cl.generate([5, 6, 7], 10, stop_ids=[stop])['ids'] == full['ids'][:4]
+    r = cl.logprobs(list(range(20)), top=3)
+    assert len(r['nll']) == 19 and len(r['top']) == 19 and len(r['top'][0]) == 3
+    assert cl.flush() == {'ok': True}
+    for body, code in [({'prompt_ids': [1] * 4090, 'max_new_tokens': 8}, 400), ({'prompt_ids': [V]}, 400),
+                       ({'prompt_ids': [1], 'max_new_tokens': True}, 400), ({'prompt': 'text'}, 400),
+                       ({'prompt_ids': 'abc'}, 400)]:
+        assert cl.request('POST', '/v1/generate', body)[0] == code, body
+    assert cl.request('GET', '/nowhere')[0] == 404
+    m = cl.metrics()
+    assert m['requests'] == 4 and m['tokens'] == 24
+    _, cl0 = server(Fake(), max_queue=0)
+    with pytest.raises(ServerError) as e:
+        cl0.generate([1, 2], 2)
+    assert e.value.status == 503
+
+
+def test_speed_tools(server):
+    _, cl = server(Fake())
+    quiet = dict(log=lambda s: None)
+    d = speed.decode_speed(cl, tokens=16, prompt_len=8, concurrency=2, rounds=1, **quiet)
+    assert d['rounds'][0]['aggregate_tok_s'] > 0 and d['decode_tok_s'] > 0
+    t = speed.ttft(cl, lengths=[16, 64, 5000], repeat=2, **quiet)
+    assert [r['tokens'] for r in t['rows']] == [16, 64] and all(r['ttft_s'] > 0 for r in t['rows'])
+    c = speed.context_speed(cl, contexts=[256], output=8, warmup=32, repeats=1, **quiet)
+    assert c['rows'][0]['prefill_tok_s'] > 0 and c['rows'][0]['answers'] == 2
+
+
+def test_ppl_kl_and_flip(server):
+    _, ref = server(Fake())
+    _, test = server(Fake(shift=0.3))
+    quiet = dict(log=lambda s: None)
+    r1, d1 = quality.ppl(ref, 'ref', segments=3, tokens=64, top=8, **quiet)
+    r2, d2 = quality.ppl(test, 'test', segments=3, tokens=64, top=8, **quiet)
+    assert r1['summary']['all']['segments'] == 3 and r1['summary']['all']['ppl'] > 1
+    assert [r['seg'] for r in r1['rows']] == [r['seg'] for r in r2['rows']]    # the same segments
+    same = quality.kl_compare(d1, d1)
+    assert same['kl_mean'] == 0 and same['top1_changed'] == 0 and same['nll_diff'] == 0
+    diff = quality.kl_compare(d1, d2)
+    assert diff['kl_mean'] > 0 and diff['positions'] == 3 * 63
+    assert abs(diff['nll_diff'] - (r2['summary']['all']['nll'] - r1['summary']['all']['nll'])) < 1e-3
+    f = quality.flip(ref, cycles=3, prompt_len=32, tokens=8, **quiet)
+    assert f['identical']
+
+
+def test_kl_lower_bound_never_exceeds_the_full_kl():
+    rng = random.Random(0)
+    for _ in range(200):
+        n = 30
+        p = [rng.random() ** 3 for _ in range(n)]
+        q = [rng.random() ** 3 for _ in range(n)]
+        sp, sq = sum(p), sum(q)
+        p, q = [x / sp for x in p], [x / sq for x in q]
+        full = sum(a * math.log(a / b) for a, b in zip(p, q))
+        top = 5
+        pt = sorted(range(n), key=lambda i: -p[i])[:top]
+        qt = sorted(range(n), key=lambda i: -q[i])[:top]
+        lb = quality.kl_lower_bound([[i, math.log(p[i])] for i in pt], [[i, math.log(q[i])] for i in qt])
+        assert lb <= full + 1e-9
+
+
+def test_abuse_and_interleave(server):
+    _, cl = server(Fake(delay=0.001))
+    res = robustness.abuse(cl, quick=True, log=lambda s: None)
+    assert res['failed'] == 0, res['failures']
+    it = robustness.interleave(cl, tokens=128, delay=0.05, answer=80, log=lambda s: None)
+    assert it['b_waited_for_a'] and it['a_tokens'] == 80
+
+
+def test_copy_test(server):
+    src = '\n'.join(f'def f{i}(x):\n    return x + {i}' for i in range(40))
+    tok = CharTok()
+    _, good = server(Fake(vocab=70000, tokenizer=tok))
+    res = copy_test.run(good, tok, src, chunks=3, lines=20, log=lambda s: None)
+    assert res['windows'] == 3 and res['differ'] == 0
+    _, bad = server(Fake(vocab=70000, tokenizer=tok, corrupt=True))
+    res = copy_test.run(bad, tok, src, chunks=3, lines=20, log=lambda s: None)
+    assert res['differ'] == 3

@@ -34,6 +34,7 @@ class Qwen3MoeConfig:
     fmt: str = formats.NVFP4
     zipf_s: float = 1.1
     std: float = 0.02
+    norm_topk: bool = True     # renormalize the top-k routing weights to sum to 1 (Qwen3's norm_topk_prob)
 
     @staticmethod
     def tiny(**kw):
@@ -94,10 +95,15 @@ def zipf_bias(E: int, s: float, gen: torch.Generator, tau: float = 1.0) -> torch
 class Qwen3MoeModel:
     def __init__(self, cfg: Qwen3MoeConfig, device='cuda', seed: int = 0, hot_fraction: float = 1.0,
                  engine_threads: int | None = None, mailbox=None, synthetic_experts: bool = True,
-                 hot_sets: list[list[int]] | None = None, peer: bool | None = None):
+                 hot_sets: list[list[int]] | None = None, peer: bool | None = None, weights=None,
+                 popularity: torch.Tensor | None = None):
         """peer: spread the hot slots over the ranks of the process group (cache/peer.py): every rank holds the same
         model (same seed), its slot pool in symmetric memory, and reads the experts other GPUs hold over NVLink
-        (None: XTIER_GPU2_SLOTS=auto / on turns it on)."""
+        (None: XTIER_GPU2_SLOTS=auto / on turns it on).
+        weights: a weight source (models/hf.py HFWeights: embed(), lm_head(), final_norm(), layer(li)) instead of
+        random init; such a model has no router bias. popularity [layers, experts]: measured route shares (a planner
+        profile) that choose the hot and RAM-resident experts when hot_sets is not given; without it the random
+        model's Zipf bias does, and a loaded model takes the lowest expert ids."""
         if peer is None:
             peer = str(config.get('XTIER_GPU2_SLOTS')).strip().lower() in ('auto', '1', 'on', 'true', 'yes')
         self.cfg = cfg
@@ -111,9 +117,14 @@ class Qwen3MoeModel:
             return t.normal_(0.0, cfg.std, generator=torch.Generator(device=dev).manual_seed(
                 int(torch.randint(0, 2 ** 31 - 1, (1,), generator=g))))
 
-        self.embed = randn(cfg.vocab, H)
-        self.lm_head = randn(cfg.vocab, H)
-        self.final_norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        if weights is not None:
+            self.embed = weights.embed().to(dev).contiguous()
+            self.lm_head = weights.lm_head().to(dev).contiguous()
+            self.final_norm = weights.final_norm().to(dev).contiguous()
+        else:
+            self.embed = randn(cfg.vocab, H)
+            self.lm_head = randn(cfg.vocab, H)
+            self.final_norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
         self.layers = []
         n_hot = cfg.experts if hot_fraction >= 1.0 else max(1, int(round(hot_fraction * cfg.experts)))
         self.mailbox = mailbox
@@ -137,32 +148,44 @@ class Qwen3MoeModel:
             self.cold = ColdPool(config.get('XTIER_COLD_DIR'), parts=config.get('XTIER_COLD_PARTS') or None,
                                  threads=config.get('XTIER_COLD_THREADS'))
         # router logits are N(0, (std * sqrt(H))^2) for RMS-normalized hidden states
-        self.zipf_tau = zipf_temperature(cfg.experts, cfg.top_k, cfg.zipf_s, cfg.std * H ** 0.5)
+        self.zipf_tau = (zipf_temperature(cfg.experts, cfg.top_k, cfg.zipf_s, cfg.std * H ** 0.5)
+                         if weights is None else 0.0)
         for li in range(cfg.layers):
-            L = dict(
-                in_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
-                post_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
-                qkv=randn((cfg.heads + 2 * cfg.kv_heads) * D, H),
-                q_norm=torch.ones(D, dtype=torch.bfloat16, device=dev),
-                k_norm=torch.ones(D, dtype=torch.bfloat16, device=dev),
-                o=randn(H, cfg.heads * D),
-            )
-            router = randn(cfg.experts, H)
-            bias = zipf_bias(cfg.experts, cfg.zipf_s, g, self.zipf_tau)
-            seed_l = seed * 1000 + li
-            if synthetic_experts:   # random codes generated on the GPU (fast), copied to the host for the CPU tier
-                ew = formats.synthetic_experts(cfg.experts, H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
+            if weights is not None:
+                src = weights.layer(li)
+                L = {k: src[k].to(dev).contiguous() for k in ('in_norm', 'post_norm', 'qkv', 'q_norm', 'k_norm', 'o')}
+                router = src['router'].to(dev).contiguous()
+                bias = None
+                ew = src['experts']
+                del src
             else:
-                ew = formats.random_experts(cfg.experts, H, cfg.inter, cfg.fmt, std=cfg.std, seed=seed_l)
+                L = dict(
+                    in_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
+                    post_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
+                    qkv=randn((cfg.heads + 2 * cfg.kv_heads) * D, H),
+                    q_norm=torch.ones(D, dtype=torch.bfloat16, device=dev),
+                    k_norm=torch.ones(D, dtype=torch.bfloat16, device=dev),
+                    o=randn(H, cfg.heads * D),
+                )
+                router = randn(cfg.experts, H)
+                bias = zipf_bias(cfg.experts, cfg.zipf_s, g, self.zipf_tau)
+                seed_l = seed * 1000 + li
+                if synthetic_experts:   # random codes generated on the GPU (fast), copied to the host for the CPU tier
+                    ew = formats.synthetic_experts(cfg.experts, H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
+                else:
+                    ew = formats.random_experts(cfg.experts, H, cfg.inter, cfg.fmt, std=cfg.std, seed=seed_l)
+            # expert popularity of this layer: a measured profile, the random model's bias, or none (id order)
+            pop = (popularity[li].float().cpu() if popularity is not None else
+                   bias.float().cpu() if bias is not None else torch.zeros(cfg.experts))
             sets = None
             if hot_sets is not None:
                 hot = hot_sets[li]
             elif self.peers is not None:
                 from ..cache.peer import plan_sets
-                sets = plan_sets(cfg.experts, n_hot, pworld, bias.cpu())
+                sets = plan_sets(cfg.experts, n_hot, pworld, pop)
                 hot = sets[prank]
             elif n_hot < cfg.experts:
-                hot = torch.argsort(bias, descending=True)[:n_hot].tolist()   # most popular first (a profile)
+                hot = sorted(range(cfg.experts), key=lambda e: (-float(pop[e]), e))[:n_hot]   # most popular first
             else:
                 hot = None
             engine = None
@@ -172,7 +195,7 @@ class Qwen3MoeModel:
                 host = ew.to('cpu')
                 if self.cold is not None:   # RAM slots for part of the experts, the rest read from the drives
                     from ..cache.cold import cold_engine
-                    engine = cold_engine(li, host, self.cold, config.get('XTIER_COLD_FRACTION'), bias.cpu(), hot,
+                    engine = cold_engine(li, host, self.cold, config.get('XTIER_COLD_FRACTION'), pop, hot,
                                          threads=engine_threads)
                 elif sets is not None:   # peer mode: the CPU tier holds only the experts no GPU's slots hold
                     covered = set().union(*map(set, sets))
@@ -183,7 +206,8 @@ class Qwen3MoeModel:
                     engine = CpuEngine(host, threads=engine_threads)
                 if engine is not None:
                     self.engines.append(engine)
-            L['moe'] = TieredMoE(li, router, ew, cfg.top_k, hot=hot, router_bias=bias, mailbox=mailbox,
+            L['moe'] = TieredMoE(li, router, ew, cfg.top_k, hot=hot, router_bias=bias, renorm=cfg.norm_topk,
+                                 mailbox=mailbox,
                                  engine=engine, device=dev, host_experts=host,
                                  pool_storage=self.peers.storage(li) if self.peers is not None else None)
             if sets is not None:
@@ -216,6 +240,18 @@ class Qwen3MoeModel:
             if config.get('XTIER_CACHE_ELASTIC'):
                 from ..cache.elastic import Governor, install
                 self.governor = Governor(install(self))
+
+    @classmethod
+    def from_pretrained(cls, path, device='cuda', hot_fraction: float = 1.0, fmt: str | None = None, **kw):
+        """A model built from a Hugging Face qwen3_moe checkpoint directory (models/hf.py: BF16, ModelOpt NVFP4,
+        compressed-tensors NVFP4 or MXFP4 experts; `fmt` (default XTIER_CKPT_FORMAT) for unquantized experts)."""
+        from .hf import HFWeights
+        dev = torch.device(device)
+        w = HFWeights(path, fmt=fmt, quant_device=dev if dev.type == 'cuda' else 'cpu')
+        try:
+            return cls(w.cfg, device=device, hot_fraction=hot_fraction, weights=w, **kw)
+        finally:
+            w.close()
 
     def attach_bigram(self, table):
         """Adds a hashed-bigram NVMe embedding table (tables/engram.py) to the token embeddings, in prefill and inside
@@ -418,7 +454,8 @@ class Qwen3MoeModel:
             logits = h @ moe.router_w.to(f).t() + (moe.router_bias if moe.router_bias is not None else 0)
             p = logits.softmax(-1)
             w, ids = p.topk(cfg.top_k, -1)
-            w = w / w.sum(-1, keepdim=True)
+            if cfg.norm_topk:
+                w = w / w.sum(-1, keepdim=True)
             out = torch.zeros_like(x)
             if moe.host is not None:
                 src = {e: (moe.host, e) for e in range(moe.E)}

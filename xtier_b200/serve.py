@@ -1,10 +1,28 @@
-"""Minimal generation server over the framework's public API (the process the console launches).
+"""Generation server over the framework's public API (the process the console launches, and what xtier_b200.bench
+measures).
 
     python -m xtier_b200.serve --model qwen3-moe [--layers 48] [--hot 0.4] [--max-len 8192] --port 18180
+    python -m xtier_b200.serve --checkpoint DIR [--hot 0.4] ...       # a Hugging Face qwen3_moe checkpoint
 
-Endpoints: GET /health ({"ready": true} once the model is built and its decode step captured), GET /metrics (decode
-counters, mailbox statistics, per-layer hit rates; /metrics/prometheus: the same in the Prometheus text format), POST /v1/generate {"prompt_ids": [...], "max_new_tokens": n} -> {"ids": [...],
-"decode_tok_s": ...}. One request at a time (batch 1 decode, the CUDA graph of the tiered MoE model).
+Endpoints
+  GET  /health               {"ready": true, "vocab": V, "max_len": L, "tokenizer": bool} once the model is built and its
+                             decode step captured
+  GET  /metrics              decode counters, mailbox statistics, per-layer hit rates (JSON);
+                             /metrics/prometheus: the same in the Prometheus text format
+  POST /flush_cache          {"ok": true}; nothing is cached between requests (every prompt is a cold prefill)
+  POST /v1/generate          {"prompt_ids": [...] | "prompt": "text" (with a tokenizer), "max_new_tokens": n,
+                              "stream": false, "stop_ids": [...]}
+                             -> {"ids": [...], "text": ..., "prompt_tokens": T, "ttft_s": ..., "decode_tok_s": ...};
+                             with "stream": true, newline-delimited JSON in a chunked response: {"id": t, "text": s}
+                             per token, then {"done": true, ...the summary above}. A client that goes away ends the
+                             decode at the next token.
+  POST /v1/logprobs          {"prompt_ids": [...], "top": N} -> {"nll": [-log p(ids[i+1] | ids[:i+1])],
+                             "top": [[[id, logprob], ...] per position]} (fixed-text perplexity, A/B of configurations)
+
+Requests run one at a time on the model (batch 1 decode, the CUDA graph of the tiered MoE model); at most --max-queue
+wait, the next ones get 503. Bad requests get 400 with the reason, unknown paths 404, bodies over 64 MiB 413.
+(Reference parity: the reference serves through SGLang's HTTP server; the endpoints its bench tools use -- streamed
+generation, /flush_cache, prompt logprobs, /metrics -- have these counterparts.)
 """
 from __future__ import annotations
 
@@ -14,101 +32,345 @@ import threading
 import time
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 
-import torch
-
 MODELS = ('qwen3-moe',)
+MAX_BODY = 64 << 20
+
+
+class BadRequest(ValueError):
+    pass
+
+
+class GenBackend:
+    """The model and its decode runner behind the server: prefill a prompt, decode one token, score a text."""
+
+    def __init__(self, model, gen, tokenizer=None, mailbox=None):
+        self.model, self.gen, self.tokenizer, self.mailbox = model, gen, tokenizer, mailbox
+        self.vocab = model.cfg.vocab
+        self.max_len = gen.max_len
+
+    def prefill(self, ids: list[int]) -> int:
+        import torch
+        gen = self.gen
+        gen.prefill(torch.tensor([ids]))
+        if gen.graph is None and gen.use_graph:
+            gen.capture()
+        gen.host_tokens.copy_(gen.buf['tokens'].cpu())
+        return int(gen.host_tokens[0])
+
+    def decode(self) -> int:
+        t = int(self.gen.decode_one()[0])
+        self.gen.between_steps()
+        return t
+
+    def logprobs(self, ids: list[int], top: int):
+        import torch
+        m = self.model
+        st = self.gen.state
+        _, logits = m.prefill(st, torch.tensor(ids, device=m.device), all_logits=True)
+        nll, tops = [], []
+        tgt = torch.tensor(ids[1:], device=m.device)
+        for s in range(0, len(ids) - 1, 512):
+            lp = torch.log_softmax(logits[s:min(s + 512, len(ids) - 1)].float(), dim=-1)
+            nll += (-lp.gather(1, tgt[s:s + lp.shape[0], None])[:, 0]).tolist()
+            if top > 0:
+                v, i = lp.topk(top, dim=-1)
+                tops += [list(zip(a, b)) for a, b in zip(i.tolist(), v.tolist())]
+        return nll, tops
+
+    def check(self):
+        self.gen.check()
+
+    def snapshot(self, state) -> dict:
+        from .utils.metrics import snapshot
+        return snapshot(self.model, self.mailbox, state)
+
+
+class Server:
+    """Request handling of the HTTP endpoints over a backend (GenBackend, or a stand-in in the tests)."""
+
+    def __init__(self, backend=None, max_queue: int = 8):
+        self.backend = backend
+        self.lock = threading.Lock()      # one request at a time on the model
+        self.qlock = threading.Lock()     # the queue count
+        self.max_queue = max_queue
+        self.waiting = 0
+        self.state = {'ready': backend is not None, 'requests': 0, 'tokens': 0, 'aborted': 0, 'rejected': 0,
+                      'prompt_tokens': 0}
+
+    def set_backend(self, backend):
+        self.backend = backend
+        self.state['ready'] = True
+
+    # ------------------------------------------------------------------ validation
+    def _ids(self, req: dict) -> list[int]:
+        be = self.backend
+        if 'prompt_ids' in req:
+            ids = req['prompt_ids']
+            if not isinstance(ids, list) or not all(isinstance(t, int) and not isinstance(t, bool) for t in ids):
+                raise BadRequest('prompt_ids must be a list of integers')
+        elif 'prompt' in req:
+            tok = getattr(be, 'tokenizer', None)
+            if tok is None:
+                raise BadRequest('this server has no tokenizer: send prompt_ids')
+            if not isinstance(req['prompt'], str):
+                raise BadRequest('prompt must be a string')
+            ids = tok.encode(req['prompt'], add_special_tokens=False)
+        else:
+            raise BadRequest('prompt_ids (or prompt) is required')
+        if not ids:
+            raise BadRequest('empty prompt')
+        bad = [t for t in ids if t < 0 or t >= be.vocab]
+        if bad:
+            raise BadRequest(f'token id {bad[0]} outside the vocabulary [0, {be.vocab})')
+        return ids
+
+    def parse_generate(self, req: dict):
+        if not isinstance(req, dict):
+            raise BadRequest('the body must be a JSON object')
+        ids = self._ids(req)
+        n = req.get('max_new_tokens', 16)
+        if not isinstance(n, int) or isinstance(n, bool) or n < 1:
+            raise BadRequest('max_new_tokens must be a positive integer')
+        if len(ids) + n + 8 > self.backend.max_len:
+            raise BadRequest(f'prompt ({len(ids)}) + max_new_tokens ({n}) exceed the server max length '
+                             f'{self.backend.max_len}')
+        stop = req.get('stop_ids', [])
+        if not isinstance(stop, list) or not all(isinstance(t, int) for t in stop):
+            raise BadRequest('stop_ids must be a list of integers')
+        return ids, n, set(stop), bool(req.get('stream', False))
+
+    # ------------------------------------------------------------------ work
+    def enter(self) -> bool:
+        """Takes a place in the queue (False: full)."""
+        with self.qlock:
+            if self.waiting >= self.max_queue:
+                self.state['rejected'] += 1
+                return False
+            self.waiting += 1
+            return True
+
+    def _started(self):
+        with self.qlock:
+            self.waiting -= 1
+
+    def generate(self, ids, n, stop, emit=None) -> dict:
+        """Runs one request; emit(token) per new token returns False when the client is gone."""
+        be = self.backend
+        with self.lock:
+            self._started()
+            t0 = time.perf_counter()
+            tok = be.prefill(ids)
+            t_first = time.perf_counter()
+            out, aborted = [tok], False
+            if emit is not None and emit(tok) is False:
+                aborted = True
+            t_last = t_first
+            while not aborted and len(out) < n and tok not in stop:
+                tok = be.decode()
+                out.append(tok)
+                t_last = time.perf_counter()
+                if emit is not None and emit(tok) is False:
+                    aborted = True
+            be.check()
+            self.state['requests'] += 1
+            self.state['tokens'] += len(out)
+            self.state['prompt_tokens'] += len(ids)
+            if aborted:
+                self.state['aborted'] += 1
+        dec = t_last - t_first
+        res = {'ids': out, 'prompt_tokens': len(ids), 'completion_tokens': len(out), 'ttft_s': t_first - t0,
+               'decode_s': dec, 'decode_tok_s': (len(out) - 1) / dec if dec > 0 and len(out) > 1 else None,
+               'aborted': aborted}
+        tokz = getattr(be, 'tokenizer', None)
+        if tokz is not None:
+            res['text'] = tokz.decode(out)
+        return res
+
+    def parse_logprobs(self, req: dict):
+        if not isinstance(req, dict):
+            raise BadRequest('the body must be a JSON object')
+        ids = self._ids(req)
+        top = req.get('top', 0)
+        if not isinstance(top, int) or isinstance(top, bool) or top < 0 or top > 100:
+            raise BadRequest('top must be an integer in [0, 100]')
+        if len(ids) < 2:
+            raise BadRequest('scoring needs at least two tokens')
+        if len(ids) + 8 > self.backend.max_len:
+            raise BadRequest(f'{len(ids)} tokens exceed the server max length {self.backend.max_len}')
+        return ids, top
+
+    def logprobs(self, ids, top) -> dict:
+        with self.lock:
+            self._started()
+            nll, tops = self.backend.logprobs(ids, top)
+            self.backend.check()
+            self.state['requests'] += 1
+            self.state['prompt_tokens'] += len(ids)
+        return {'nll': nll, 'top': tops, 'prompt_tokens': len(ids)}
+
+
+def make_handler(server: Server):
+    class Handler(BaseHTTPRequestHandler):
+        server_version = 'xtier-b200'
+        protocol_version = 'HTTP/1.1'
+
+        def log_message(self, fmt, *a):
+            pass
+
+        def _send(self, code, data: bytes, ctype='application/json'):
+            self.send_response(code)
+            self.send_header('Content-Type', ctype)
+            self.send_header('Content-Length', str(len(data)))
+            self.end_headers()
+            self.wfile.write(data)
+
+        def _json(self, code, obj):
+            self._send(code, json.dumps(obj).encode())
+
+        def do_GET(self):
+            if self.path == '/health':
+                be = server.backend
+                info = {'ready': server.state['ready']}
+                if be is not None and server.state['ready']:
+                    info.update(vocab=be.vocab, max_len=be.max_len, tokenizer=getattr(be, 'tokenizer', None) is not None)
+                return self._json(200, info)
+            if self.path in ('/metrics', '/metrics/prometheus'):
+                from .utils.metrics import prometheus_text
+                be = server.backend
+                snap = be.snapshot(server.state) if be is not None and hasattr(be, 'snapshot') else {}
+                snap.update({k: server.state[k] for k in ('requests', 'tokens', 'aborted', 'rejected',
+                                                          'prompt_tokens')})
+                if self.path == '/metrics':
+                    return self._json(200, snap)
+                return self._send(200, prometheus_text(snap).encode(), 'text/plain; version=0.0.4')
+            self._json(404, {'error': 'not found'})
+
+        def _body(self):
+            try:
+                n = int(self.headers.get('Content-Length', '0'))
+            except ValueError:
+                raise BadRequest('bad Content-Length')
+            if n > MAX_BODY:
+                return None
+            raw = self.rfile.read(n) if n else b''
+            try:
+                return json.loads(raw or b'{}')
+            except ValueError as e:
+                raise BadRequest(f'body is not JSON: {e}')
+
+        def do_POST(self):
+            if self.path == '/flush_cache':
+                self.rfile.read(int(self.headers.get('Content-Length', '0') or 0))
+                return self._json(200, {'ok': True})
+            if self.path not in ('/v1/generate', '/v1/logprobs'):
+                return self._json(404, {'error': 'not found'})
+            if not server.state['ready']:
+                return self._json(503, {'error': 'loading'})
+            try:
+                req = self._body()
+                if req is None:
+                    self.close_connection = True
+                    return self._json(413, {'error': 'body too large'})
+                if self.path == '/v1/logprobs':
+                    ids, top = server.parse_logprobs(req)
+                else:
+                    ids, n, stop, stream = server.parse_generate(req)
+            except BadRequest as e:
+                return self._json(400, {'error': str(e)})
+            if not server.enter():
+                return self._json(503, {'error': 'queue full'})
+            if self.path == '/v1/logprobs':
+                try:
+                    return self._json(200, server.logprobs(ids, top))
+                except Exception as e:   # noqa: BLE001 -- reported to the client, the server stays up
+                    return self._json(500, {'error': f'{type(e).__name__}: {e}'})
+            if not stream:
+                try:
+                    res = server.generate(ids, n, stop)
+                except Exception as e:   # noqa: BLE001 -- reported to the client, the server stays up
+                    return self._json(500, {'error': f'{type(e).__name__}: {e}'})
+                return self._json(200, res)
+            self.send_response(200)
+            self.send_header('Content-Type', 'application/x-ndjson')
+            self.send_header('Transfer-Encoding', 'chunked')
+            self.end_headers()
+            tokz = getattr(server.backend, 'tokenizer', None)
+
+            def chunk(obj) -> bool:
+                data = (json.dumps(obj) + '\n').encode()
+                try:
+                    self.wfile.write(b'%x\r\n%s\r\n' % (len(data), data))
+                    self.wfile.flush()
+                    return True
+                except (BrokenPipeError, ConnectionResetError, OSError):
+                    return False
+
+            def emit(t):
+                return chunk({'id': t, 'text': tokz.decode([t]) if tokz is not None else None})
+            try:
+                res = server.generate(ids, n, stop, emit)
+                res['done'] = True
+                if chunk(res):
+                    self.wfile.write(b'0\r\n\r\n')
+            except Exception as e:   # noqa: BLE001
+                chunk({'done': True, 'error': f'{type(e).__name__}: {e}'})
+            self.close_connection = True
+
+    return Handler
 
 
 def build(args):
     from .engine.mailbox import Mailbox
     from .models.qwen3_moe import Qwen3MoeConfig, Qwen3MoeModel
     from .runtime.decode import Generator
-    cfg = Qwen3MoeConfig(layers=args.layers)
-    mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
-    model = Qwen3MoeModel(cfg, device='cuda', seed=args.seed, hot_fraction=args.hot, mailbox=mailbox)
+    tok = None
+    if args.checkpoint:
+        from .models.hf import HFWeights
+        cfg = HFWeights(args.checkpoint).cfg
+        mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
+        model = Qwen3MoeModel.from_pretrained(args.checkpoint, device='cuda', hot_fraction=args.hot, mailbox=mailbox)
+        try:
+            from transformers import AutoTokenizer
+            tok = AutoTokenizer.from_pretrained(args.tokenizer or args.checkpoint)
+        except Exception as e:   # noqa: BLE001 -- a checkpoint without tokenizer files serves token ids only
+            print(f'[xtier_b200] no tokenizer ({type(e).__name__}); prompt_ids only', flush=True)
+    else:
+        cfg = Qwen3MoeConfig(layers=args.layers)
+        mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
+        model = Qwen3MoeModel(cfg, device='cuda', seed=args.seed, hot_fraction=args.hot, mailbox=mailbox)
     if mailbox is not None:
         mailbox.start()
-    return model, Generator(model, batch=1, max_len=args.max_len), mailbox
+    gen = Generator(model, batch=1, max_len=args.max_len)
+    be = GenBackend(model, gen, tok, mailbox)
+    be.prefill([0])        # captures the decode graph before the server says it is ready
+    return be
 
 
-def make_handler(state):
-    class Handler(BaseHTTPRequestHandler):
-        server_version = 'xtier-b200'
-
-        def log_message(self, fmt, *a):
-            pass
-
-        def _json(self, code, obj):
-            data = json.dumps(obj).encode()
-            self.send_response(code)
-            self.send_header('Content-Type', 'application/json')
-            self.send_header('Content-Length', str(len(data)))
-            self.end_headers()
-            self.wfile.write(data)
-
-        def do_GET(self):
-            if self.path == '/health':
-                return self._json(200, {'ready': state['ready']})
-            if self.path in ('/metrics', '/metrics/prometheus'):
-                from .utils.metrics import prometheus_text, snapshot
-                snap = snapshot(state.get('model'), state.get('mailbox'), state)
-                if self.path == '/metrics':
-                    return self._json(200, snap)
-                data = prometheus_text(snap).encode()
-                self.send_response(200)
-                self.send_header('Content-Type', 'text/plain; version=0.0.4')
-                self.send_header('Content-Length', str(len(data)))
-                self.end_headers()
-                self.wfile.write(data)
-                return
-            self._json(404, {'error': 'not found'})
-
-        def do_POST(self):
-            if self.path != '/v1/generate':
-                return self._json(404, {'error': 'not found'})
-            if not state['ready']:
-                return self._json(503, {'error': 'loading'})
-            try:
-                req = json.loads(self.rfile.read(int(self.headers.get('Content-Length', '0'))) or b'{}')
-                ids = [int(t) for t in req['prompt_ids']]
-                n = int(req.get('max_new_tokens', 16))
-            except (KeyError, ValueError, TypeError) as e:
-                return self._json(400, {'error': f'bad request: {e}'})
-            with state['lock']:
-                gen = state['gen']
-                if len(ids) + n + 8 > gen.max_len:
-                    return self._json(400, {'error': 'prompt + max_new_tokens exceed the server max length'})
-                gen.prefill(torch.tensor([ids]))
-                if gen.graph is None:
-                    gen.capture()
-                gen.host_tokens.copy_(gen.buf['tokens'].cpu())
-                t0 = time.perf_counter()
-                out = [int(gen.decode_one()[0]) for _ in range(n)]
-                dt = time.perf_counter() - t0
-                gen.check()
-                state['requests'] += 1
-                state['tokens'] += n
-            self._json(200, {'ids': out, 'decode_tok_s': n / dt if dt > 0 else None})
-
-    return Handler
+def serve(server: Server, host: str, port: int) -> ThreadingHTTPServer:
+    """Starts the HTTP server on a thread; returns it (its server_address has the bound port)."""
+    srv = ThreadingHTTPServer((host, port), make_handler(server))
+    srv.daemon_threads = True
+    threading.Thread(target=srv.serve_forever, daemon=True).start()
+    return srv
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument('--model', default='qwen3-moe', choices=MODELS)
+    ap.add_argument('--checkpoint', default=None, help='a Hugging Face qwen3_moe checkpoint directory')
+    ap.add_argument('--tokenizer', default=None, help='tokenizer directory (default: the checkpoint)')
     ap.add_argument('--layers', type=int, default=48)
     ap.add_argument('--hot', type=float, default=0.4)
     ap.add_argument('--max-len', type=int, default=8192)
+    ap.add_argument('--max-queue', type=int, default=8)
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--host', default='127.0.0.1')
     ap.add_argument('--port', type=int, default=18180)
     args = ap.parse_args(argv)
-    state = {'ready': False, 'lock': threading.Lock(), 'requests': 0, 'tokens': 0}
-    srv = ThreadingHTTPServer((args.host, args.port), make_handler(state))
-    threading.Thread(target=srv.serve_forever, daemon=True).start()
-    print(f'[xtier_b200] loading {args.model} ...', flush=True)
-    model, gen, mailbox = build(args)
-    state.update(model=model, gen=gen, mailbox=mailbox, ready=True)
+    server = Server(None, args.max_queue)
+    serve(server, args.host, args.port)
+    print(f'[xtier_b200] loading {args.checkpoint or args.model} ...', flush=True)
+    server.set_backend(build(args))
     print(f'[xtier_b200] ready on http://{args.host}:{args.port}', flush=True)
     try:
         threading.Event().wait()
