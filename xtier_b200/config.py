@@ -34,6 +34,9 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_SPIN_US', 'int', 200, 'engine workers spin this long before sleeping on a futex'),
     _S('XTIER_MAIN_CPUS', 'str', '', 'CPUs of the other threads of the process (auto: all but the workers)'),
     _S('XTIER_DISPATCH_CPU', 'int', -1, 'CPU the mailbox dispatcher thread is pinned to (-1: last CPU)'),
+    _S('XTIER_WORKER_CPUS', 'list', '', 'CPUs the engine workers are pinned to (empty: every allowed CPU; set by placement)'),
+    _S('XTIER_PDL', 'flag', True, 'programmatic dependent launch between the decode kernels (0: plain stream order)'),
+    _S('XTIER_ATTN_CUDA_CORES', 'flag', False, 'decode attention on the CUDA-core kernel for every group size'),
     _S('XTIER_DECODE_MAX', 'int', 64, 'calls of up to this many tokens use the mailbox decode path (graph capturable)'),
     _S('XTIER_SLOT_TOKENS', 'int', 16, 'tokens of one mailbox decode slot at the most'),
     _S('XTIER_CPU_TIMEOUT_S', 'float', 60.0, 'a mailbox request unanswered for this long fails the step (bounded wait)'),
