@@ -1,0 +1,517 @@
+"""Recall: a persistent record of the token ids a server has read and written, and copy drafts from it for speculative
+decoding (the target model verifies every copied token, so the output is the same with Recall on or off).
+
+`Record` keeps token ids only: chunks of up to 2^20 int32 ids (on disk: `chunk-NNNNNNNN.ids` files, 0600, in a 0700
+directory with an `identity.json` naming the tokenizer and a `lock` file; or in memory). A separator id (-1) ends
+every added run, so no match crosses two unrelated texts. Every window of 16 consecutive ids is indexed by a 64-bit
+hash (a polynomial over the ids, then the SplitMix64 finalizer of Steele, Lea and Flood, 2014): each chunk's index is
+a few sorted runs of (hash, position) numpy arrays -- one per add, merged into one when the chunk fills -- searched with
+binary search, so a lookup costs a few dozen `searchsorted` calls and no Python dictionary of millions of entries.
+Adding a text skips stretches of 128 or more ids the record already holds (keeping 32 ids at each edge, so windows
+across the cut stay indexed): a request sent twice adds nothing new. Past the id budget the oldest chunk goes first;
+with less than `min_free_gib` on the record's file system nothing is added. One process holds the lock and writes;
+the others open the record read-only and `refresh()` to see new chunks.
+
+`RecallEngine` makes the copy decisions per stream: a stream's own context is asked first (a per-stream index) and
+wins ties, then the record; a candidate is the continuation after the longest match (16 ids or more, extended back up
+to 128) of the stream's last 16 ids. Expected landed tokens are kept per source and match tier (16-31, 32-63, 64+
+ids) as decayed means with a prior; a copy is offered when its expectation reaches the stream's own draft yield (or
+`min_n`). A stream whose copy landed nothing leaves copies alone for `cooldown` rounds; a source whose expectation
+fell below the bar is only probed, rarer after every probe that misses.
+
+(Reference parity: xtier/packs/deepseek_v4/recall/core.py -- RecallRecord (ids-only chunk files, identity, lock,
+dedup of repeated runs, FIFO budget, min free space, read-only refresh) and RecallEngine (own context first, match tiers,
+cooldown after a miss, probes) and the proposal broadcast to the tensor-parallel ranks (`sync_proposal`). The index
+layout, hash and expectation rule here are this project's own. Not built:
+the heat-ordered eviction with its hot zone, the prompt-hash reply store, the GPU-resident id store and tree drafts.)
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+import shutil
+from pathlib import Path
+
+import numpy as np
+
+WINDOW = 16
+SENTINEL = -1
+CHUNK_IDS = 1 << 20
+DEDUP_RUN = 128
+OVERLAP = 32
+MAX_BACK = 128
+MAX_RUNS = 8            # sorted index runs per chunk before they are merged
+_P = np.uint64(0x100000001B3)          # odd multiplier of the polynomial window hash
+_M1 = np.uint64(0xBF58476D1CE4E5B9)    # SplitMix64 finalizer constants
+_M2 = np.uint64(0x94D049BB133111EB)
+
+
+def window_hashes(a: np.ndarray, w: int = WINDOW) -> tuple[np.ndarray, np.ndarray]:
+    """(hashes uint64, start offsets) of every window of `w` ids of `a` that contains no separator."""
+    a = np.asarray(a, dtype=np.int64)
+    n = a.shape[0] - w + 1
+    if n <= 0:
+        return np.zeros(0, np.uint64), np.zeros(0, np.int64)
+    with np.errstate(over='ignore'):
+        v = (a & 0xFFFFFFFF).astype(np.uint64)
+        h = np.zeros(n, np.uint64)
+        for k in range(w):
+            h = h * _P + v[k:k + n]
+        h ^= h >> np.uint64(30)
+        h *= _M1
+        h ^= h >> np.uint64(27)
+        h *= _M2
+        h ^= h >> np.uint64(31)
+    bad = np.convolve((a == SENTINEL).astype(np.int64), np.ones(w, np.int64), 'valid') > 0
+    keep = ~bad
+    return h[keep], np.nonzero(keep)[0].astype(np.int64)
+
+
+class _Chunk:
+    def __init__(self, seq: int, ids: np.ndarray | None = None):
+        self.seq = seq
+        self.ids = np.empty(CHUNK_IDS, np.int32)
+        self.n = 0
+        self.runs: list[tuple[np.ndarray, np.ndarray]] = []   # sorted (hashes, global window starts)
+        if ids is not None:
+            self.ids[:ids.shape[0]] = ids
+            self.n = ids.shape[0]
+
+    @property
+    def base(self) -> int:
+        return self.seq * CHUNK_IDS
+
+    def index(self, lo: int, hi: int):
+        """Indexes the windows starting in [lo, hi) (offsets in this chunk; a window may not leave the chunk)."""
+        seg = self.ids[max(0, lo):min(self.n, hi + WINDOW - 1)]
+        h, off = window_hashes(seg)
+        if h.shape[0] == 0:
+            return
+        order = np.argsort(h, kind='stable')
+        self.runs.append((h[order], off[order] + max(0, lo) + self.base))
+        if len(self.runs) > MAX_RUNS:
+            self.merge()
+
+    def merge(self):
+        if len(self.runs) > 1:
+            h = np.concatenate([r[0] for r in self.runs])
+            p = np.concatenate([r[1] for r in self.runs])
+            order = np.argsort(h, kind='stable')
+            self.runs = [(h[order], p[order])]
+
+    def find(self, h: int) -> list[int]:
+        key = np.uint64(h)
+        out = []
+        for hs, ps in self.runs:
+            i = int(np.searchsorted(hs, key))
+            while i < hs.shape[0] and hs[i] == key:
+                out.append(int(ps[i]))
+                i += 1
+        return out
+
+    def contains(self, hs: np.ndarray) -> np.ndarray:
+        """For every hash of `hs`, whether this chunk indexes it."""
+        found = np.zeros(hs.shape[0], bool)
+        for rh, _ in self.runs:
+            i = np.searchsorted(rh, hs)
+            i = np.minimum(i, rh.shape[0] - 1)
+            found |= rh[i] == hs
+        return found
+
+
+class Record:
+    """Token ids with a 16-id window index; `path` None keeps everything in memory."""
+
+    def __init__(self, path=None, identity: dict | None = None, budget_ids: int = 1 << 24, min_free_gib: float = 1.0,
+                 dedup: bool = True):
+        self.path = Path(path) if path is not None else None
+        self.identity = identity or {}
+        self.budget_ids = max(CHUNK_IDS, int(budget_ids))
+        self.min_free_gib = min_free_gib
+        self.dedup = dedup
+        self.chunks: list[_Chunk] = []
+        self.writer = True
+        self._lock = None
+        self.added = self.skipped = self.evicted = 0
+        if self.path is not None:
+            self._open_dir()
+
+    # ------------------------------------------------------------------ disk
+    def _open_dir(self):
+        p = self.path
+        p.mkdir(parents=True, exist_ok=True)
+        os.chmod(p, 0o700)
+        ident = p / 'identity.json'
+        if ident.exists():
+            have = json.loads(ident.read_text())
+            if self.identity and have != self.identity:
+                raise RuntimeError(f'recall record {p} belongs to another tokenizer: {have} != {self.identity}')
+            self.identity = have
+        else:
+            fd = os.open(ident, os.O_WRONLY | os.O_CREAT | os.O_TRUNC, 0o600)
+            with os.fdopen(fd, 'w') as f:
+                f.write(json.dumps(self.identity))
+        import fcntl
+        self._lock = open(p / 'lock', 'a+')
+        try:
+            fcntl.flock(self._lock.fileno(), fcntl.LOCK_EX | fcntl.LOCK_NB)
+        except OSError:
+            self.writer = False
+        self.refresh()
+
+    def _chunk_file(self, seq: int) -> Path:
+        return self.path / f'chunk-{seq:08d}.ids'
+
+    def refresh(self) -> int:
+        """Reads chunks (and growth of the last one) other processes wrote; returns ids read."""
+        if self.path is None:
+            return 0
+        seqs = sorted(int(f.name[6:14]) for f in self.path.glob('chunk-*.ids'))
+        have = {c.seq: c for c in self.chunks}
+        self.chunks = [have[s] for s in seqs if s in have]   # chunks evicted elsewhere go
+        read = 0
+        for s in seqs:
+            data = np.fromfile(self._chunk_file(s), dtype='<i4')
+            c = have.get(s)
+            if c is None:
+                c = _Chunk(s, data.astype(np.int32))
+                c.index(0, c.n)
+                c.merge()
+                self.chunks.append(c)
+                read += c.n
+            elif data.shape[0] > c.n:
+                lo = c.n
+                c.ids[lo:data.shape[0]] = data[lo:]
+                c.n = data.shape[0]
+                c.index(lo - WINDOW + 1, c.n)
+                read += c.n - lo
+        self.chunks.sort(key=lambda c: c.seq)
+        return read
+
+    # ------------------------------------------------------------------ add
+    @property
+    def size(self) -> int:
+        return sum(c.n for c in self.chunks)
+
+    def _seen(self, a: np.ndarray) -> np.ndarray:
+        """Per id of `a`: whether it lies in a run of >= DEDUP_RUN ids whose windows the record already indexes,
+        keeping OVERLAP ids at each edge of the run."""
+        h, off = window_hashes(a)
+        if h.shape[0] == 0 or not self.chunks:
+            return np.zeros(a.shape[0], bool)
+        known = np.zeros(h.shape[0], bool)
+        for c in self.chunks:
+            known |= c.contains(h)
+        win = np.zeros(a.shape[0] - WINDOW + 1, bool)
+        win[off] = known
+        skip = np.zeros(a.shape[0], bool)
+        i, n = 0, win.shape[0]
+        while i < n:
+            if not win[i]:
+                i += 1
+                continue
+            j = i
+            while j < n and win[j]:
+                j += 1
+            lo, hi = i, j - 1 + WINDOW          # ids [lo, hi) are covered by known windows
+            if hi - lo >= DEDUP_RUN:            # keep OVERLAP ids where the run meets new text, none at the ends
+                skip[lo + (OVERLAP if lo > 0 else 0):hi - (OVERLAP if hi < a.shape[0] else 0)] = True
+            i = j
+        return skip
+
+    def _append(self, seg: np.ndarray, sep: bool = True):
+        seg = np.asarray(seg, np.int32)
+        if sep:
+            seg = np.concatenate([seg, np.array([SENTINEL], np.int32)])
+        while seg.shape[0]:
+            if not self.chunks or self.chunks[-1].n == CHUNK_IDS:
+                if self.chunks:
+                    self.chunks[-1].merge()
+                self.chunks.append(_Chunk(self.chunks[-1].seq + 1 if self.chunks else 0))
+            c = self.chunks[-1]
+            k = min(seg.shape[0], CHUNK_IDS - c.n)
+            lo = c.n
+            c.ids[lo:lo + k] = seg[:k]
+            c.n += k
+            if self.path is not None:
+                fd = os.open(self._chunk_file(c.seq), os.O_WRONLY | os.O_CREAT | os.O_APPEND, 0o600)
+                with os.fdopen(fd, 'ab') as f:
+                    f.write(seg[:k].astype('<i4').tobytes())
+            c.index(lo - WINDOW + 1, c.n)
+            seg = seg[k:]
+
+    def _evict(self):
+        while len(self.chunks) > 1 and self.size > self.budget_ids:
+            c = self.chunks.pop(0)
+            self.evicted += c.n
+            if self.path is not None:
+                self._chunk_file(c.seq).unlink(missing_ok=True)
+
+    def add(self, ids) -> int:
+        """Adds a text; returns the ids stored (0 when read-only, short of disk space, or all already held)."""
+        if not self.writer:
+            return 0
+        if self.path is not None and shutil.disk_usage(self.path).free < self.min_free_gib * (1 << 30):
+            return 0
+        a = np.asarray(ids, dtype=np.int64)
+        a = a[a >= 0]
+        if a.shape[0] < WINDOW:
+            return 0
+        skip = self._seen(a) if self.dedup else np.zeros(a.shape[0], bool)
+        stored = 0
+        i = 0
+        while i < a.shape[0]:     # the kept stretches, each ended by a separator
+            if skip[i]:
+                i += 1
+                continue
+            j = i
+            while j < a.shape[0] and not skip[j]:
+                j += 1
+            if j - i >= WINDOW:
+                self._append(a[i:j])
+                stored += j - i
+            i = j
+        self.added += stored
+        self.skipped += int(skip.sum())
+        self._evict()
+        return stored
+
+    # ------------------------------------------------------------------ lookup
+    def _ids(self, g0: int, g1: int) -> np.ndarray | None:
+        """Ids of global positions [g0, g1) if they are still held (one chunk or two)."""
+        out = []
+        for c in self.chunks:
+            lo, hi = max(g0, c.base), min(g1, c.base + c.n)
+            if lo < hi:
+                out.append(c.ids[lo - c.base:hi - c.base])
+        if not out:
+            return None
+        r = np.concatenate(out)
+        return r if r.shape[0] == g1 - g0 else None
+
+    def lookup(self, tail, max_back: int = MAX_BACK):
+        """(match length, position after the match) of the longest match of `tail`'s last ids (>= WINDOW), newest
+        first on ties; None without one."""
+        t = np.asarray(tail, dtype=np.int64)
+        if t.shape[0] < WINDOW:
+            return None
+        h, off = window_hashes(t[-WINDOW:])
+        if h.shape[0] == 0:
+            return None
+        best = None
+        for c in reversed(self.chunks):
+            for p in sorted(c.find(int(h[0])), reverse=True):
+                w = self._ids(p, p + WINDOW)
+                if w is None or not np.array_equal(w, t[-WINDOW:]):
+                    continue                              # a hash collision
+                back = 0
+                lim = min(max_back, t.shape[0] - WINDOW)
+                if lim > 0:
+                    g0 = max(self.chunks[0].base, p - lim)
+                    prev = self._ids(g0, p)
+                    if prev is not None:
+                        mine = t[-WINDOW - (p - g0):-WINDOW] if p > g0 else t[:0]
+                        eq = prev[::-1] == mine[::-1]
+                        back = int(np.argmin(eq)) if not eq.all() else eq.shape[0]
+                m = WINDOW + back
+                if best is None or m > best[0]:
+                    best = (m, p + WINDOW)
+        return best
+
+    def continuation(self, pos: int, n: int) -> np.ndarray:
+        """Up to n ids from global position `pos`, stopping at a separator."""
+        ids = self._ids(pos, pos + n)
+        if ids is None:
+            for k in range(n - 1, 0, -1):
+                ids = self._ids(pos, pos + k)
+                if ids is not None:
+                    break
+            else:
+                return np.zeros(0, np.int32)
+        stop = np.nonzero(ids == SENTINEL)[0]
+        return ids[:stop[0]] if stop.shape[0] else ids
+
+    def stats(self) -> dict:
+        return dict(ids=self.size, chunks=len(self.chunks), added=self.added, skipped=self.skipped,
+                    evicted=self.evicted, writer=self.writer)
+
+    def clear(self):
+        if not self.writer:
+            return
+        for c in self.chunks:
+            if self.path is not None:
+                self._chunk_file(c.seq).unlink(missing_ok=True)
+        self.chunks = []
+
+    def close(self):
+        if self._lock is not None:
+            self._lock.close()
+            self._lock = None
+
+
+def tier_of(match: int) -> int:
+    return 0 if match < 32 else (1 if match < 64 else 2)
+
+
+@dataclasses.dataclass
+class Proposal:
+    source: str          # 'own' or 'record'
+    ids: list[int]
+    match: int
+    tier: int
+    probe: bool = False
+
+
+class _Stream:
+    def __init__(self, prompt):
+        self.own = Record(None, dedup=False)
+        self.ids: list[int] = list(prompt)
+        self.indexed = 0
+        self.cooldown = 0
+        self.own_yield = 0.0     # tokens the stream's own draft model lands per round (0: none)
+        self.last: Proposal | None = None
+        self.prompt_len = len(prompt)
+
+
+class RecallEngine:
+    SOURCES = ('own', 'record')
+
+    def __init__(self, record: Record | None, gamma: int = 16, min_n: float = 2.0, cooldown: int = 4,
+                 prior: float = 0.5, prior_weight: float = 2.0, decay: float = 0.98, probe_start: int = 16,
+                 probe_max: int = 4096):
+        self.record = record
+        self.gamma = gamma
+        self.min_n = min_n
+        self.cooldown = cooldown
+        self.prior, self.prior_w, self.decay = prior * gamma, prior_weight, decay
+        self.sums = {(s, t): [0.0, 0.0] for s in self.SOURCES for t in range(3)}   # decayed (landed, offers)
+        self.probe_iv = {s: probe_start for s in self.SOURCES}
+        self.probe_left = {s: probe_start for s in self.SOURCES}
+        self.probe_start, self.probe_max = probe_start, probe_max
+        self.streams: dict = {}
+        self.offers = self.probes = self.landed = 0
+
+    # ------------------------------------------------------------------ streams
+    def begin_stream(self, rid, prompt_ids):
+        self.streams[rid] = _Stream([int(t) for t in prompt_ids])
+
+    def extend_stream(self, rid, ids):
+        self.streams[rid].ids += [int(t) for t in ids]
+
+    def end_stream(self, rid, add: bool = True):
+        st = self.streams.pop(rid)
+        if add and self.record is not None:
+            self.record.add(st.ids)
+
+    def observe_own(self, rid, landed: float, alpha: float = 0.25):
+        """The stream's own draft model landed `landed` tokens this round (the bar a copy must reach)."""
+        st = self.streams[rid]
+        st.own_yield = (1 - alpha) * st.own_yield + alpha * landed
+
+    # ------------------------------------------------------------------ decisions
+    def expect(self, source: str, tier: int) -> float:
+        landed, offers = self.sums[(source, tier)]
+        return (self.prior * self.prior_w + landed) / (self.prior_w + offers)
+
+    def _own_candidate(self, st: _Stream):
+        if len(st.ids) - st.indexed >= WINDOW:    # index the stream's history except its last window
+            hi = len(st.ids) - 1
+            st.own._append(np.asarray(st.ids[st.indexed:hi], np.int64), sep=False)   # one continuous text
+            st.indexed = hi
+        m = st.own.lookup(st.ids)
+        if m is None:
+            return None
+        cont = st.own.continuation(m[1], self.gamma)
+        return (m[0], cont) if cont.shape[0] else None
+
+    def _record_candidate(self, st: _Stream):
+        if self.record is None:
+            return None
+        m = self.record.lookup(st.ids)
+        if m is None:
+            return None
+        cont = self.record.continuation(m[1], self.gamma)
+        return (m[0], cont) if cont.shape[0] else None
+
+    def propose(self, rid) -> Proposal | None:
+        st = self.streams[rid]
+        if st.cooldown > 0:
+            st.cooldown -= 1
+            return None
+        cands = []
+        for src, cand in (('own', self._own_candidate(st)), ('record', self._record_candidate(st))):
+            if cand is not None:
+                cands.append((self.expect(src, tier_of(cand[0])), src == 'own', src, cand))
+        if not cands:
+            return None
+        cands.sort(key=lambda c: (c[0], c[1]), reverse=True)    # best expectation, own context on ties
+        e, _, src, (match, cont) = cands[0]
+        bar = max(self.min_n, st.own_yield)
+        probe = False
+        if e < bar:                    # below the bar: only a probe now and then
+            self.probe_left[src] -= 1
+            if self.probe_left[src] > 0:
+                return None
+            probe = True
+            self.probe_left[src] = self.probe_iv[src]
+        p = Proposal(src, [int(t) for t in cont], match, tier_of(match), probe)
+        st.last = p
+        self.offers += 1
+        self.probes += probe
+        return p
+
+    def feedback(self, rid, landed: int):
+        """The target accepted `landed` tokens of the last proposal."""
+        st = self.streams[rid]
+        p, st.last = st.last, None
+        if p is None:
+            return
+        for k in self.sums:
+            self.sums[k][0] *= self.decay
+            self.sums[k][1] *= self.decay
+        s = self.sums[(p.source, p.tier)]
+        s[0] += landed
+        s[1] += 1
+        self.landed += landed
+        if landed == 0:
+            st.cooldown = self.cooldown
+        if p.probe:
+            self.probe_iv[p.source] = (self.probe_start if landed > 0 else
+                                       min(self.probe_max, self.probe_iv[p.source] * 2))
+
+    def stats(self) -> dict:
+        return dict(offers=self.offers, probes=self.probes, landed=self.landed,
+                    expect={f'{s}/{t}': round(self.expect(s, t), 3) for s, t in self.sums},
+                    record=self.record.stats() if self.record is not None else None)
+
+
+def sync_proposal(prop: Proposal | None, group=None, src: int = 0) -> Proposal | None:
+    """Every rank of `group` takes rank `src`'s proposal (tensor-parallel ranks must verify the same drafts; only
+    `src` keeps a record and an engine). One broadcast of a small int64 tensor: [count, match, tier, probe, source,
+    ids...] padded to a fixed length."""
+    import torch
+    import torch.distributed as dist
+    cap = 64
+    buf = torch.full((5 + cap,), -1, dtype=torch.int64)
+    if dist.get_rank(group) == src if group is not None else dist.get_rank() == src:
+        if prop is not None and prop.ids:
+            ids = prop.ids[:cap]
+            buf[:5] = torch.tensor([len(ids), prop.match, prop.tier, int(prop.probe), int(prop.source == 'own')])
+            buf[5:5 + len(ids)] = torch.tensor(ids)
+        else:
+            buf[0] = 0
+    dist.broadcast(buf, src=src if group is None else dist.get_global_rank(group, src), group=group)
+    n = int(buf[0])
+    if n <= 0:
+        return None
+    return Proposal('own' if int(buf[4]) else 'record', buf[5:5 + n].tolist(), int(buf[1]), int(buf[2]),
+                    bool(buf[3]))
+
+
+def tokenizer_identity(tokenizer, model_name: str = '') -> dict:
+    """What a record's ids mean: the tokenizer's class, vocabulary size and a digest of its vocabulary."""
+    import hashlib
+    vocab = tokenizer.get_vocab() if hasattr(tokenizer, 'get_vocab') else {}
+    digest = hashlib.sha256(json.dumps(sorted(vocab.items())).encode()).hexdigest()[:16] if vocab else ''
+    return dict(tokenizer=type(tokenizer).__name__, vocab=len(vocab), digest=digest, model=model_name)

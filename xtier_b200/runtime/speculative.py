@@ -76,21 +76,43 @@ def verify_chain(p: torch.Tensor, q: torch.Tensor, drafts: torch.Tensor, generat
 
 class SpeculativeDecoder:
     """Chain speculative decoding of one sequence (row 0) of `target` with `draft` (both models with the
-    `prefill(st, tokens, start=..., all_logits=...)` interface and their own KV state)."""
+    `prefill(st, tokens, start=..., all_logits=...)` interface and their own KV state) and/or copy drafts from a
+    `recall` engine (xtier_b200.recall.RecallEngine: continuations of the stream's own context or of the record; a
+    copy is a point-mass draft, verified by the same rule). Without a draft model, rounds with no copy are plain
+    target steps."""
 
-    def __init__(self, target, draft, steps: int = 4, threshold: float = 0.2, temperature: float = 0.0,
-                 max_len: int = 4096, seed: int = 0):
-        self.target, self.draft = target, draft
+    def __init__(self, target, draft=None, steps: int = 4, threshold: float = 0.2, temperature: float = 0.0,
+                 max_len: int = 4096, seed: int = 0, recall=None):
+        if draft is None and recall is None:
+            raise ValueError('speculative decoding needs a draft model or a recall engine')
+        self.target, self.draft, self.recall = target, draft, recall
         self.S, self.th, self.temp = steps, threshold, temperature
         self.st_t = target.alloc_state(1, max_len)
-        self.st_d = draft.alloc_state(1, max_len)
+        self.st_d = draft.alloc_state(1, max_len) if draft is not None else None
         self.gen = torch.Generator().manual_seed(seed)
-        self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0)
+        self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0, copies=0, copied=0, copy_landed=0, plain=0)
 
     def _probs(self, logits: torch.Tensor) -> torch.Tensor:
         if self.temp <= 0:
             return torch.nn.functional.one_hot(torch.argmax(logits, -1), logits.shape[-1]).float()
         return torch.softmax(logits.float() / self.temp, dim=-1)
+
+    def _verify(self, pos: int, last: int, drafts: list[int], q: torch.Tensor, active=None,
+                keep: int | None = None) -> list[int]:
+        """Target forward of [last, drafts...] from `pos` (`active`: the token flags of truncated drafts); the first
+        `keep` drafts (default all) are verified against q [keep, V]: the accepted ones plus one corrected / bonus
+        token."""
+        dev = self.target.device
+        keep = len(drafts) if keep is None else keep
+        vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
+        _, logits = self.target.prefill(self.st_t, vt[0], start=pos, all_logits=True, active=active)
+        return verify_chain(self._probs(logits)[:keep + 1], q[:keep], torch.tensor(drafts[:keep]), self.gen,
+                            self.temp <= 0)
+
+    def _sample(self, logits: torch.Tensor) -> int:
+        if self.temp <= 0:
+            return int(torch.argmax(logits))
+        return int(torch.multinomial(self._probs(logits).cpu(), 1, generator=self.gen))
 
     def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> list[int]:
         """Up to `max_new_tokens` new tokens after `prompt` [T]."""
@@ -99,40 +121,70 @@ class SpeculativeDecoder:
         T = prompt.shape[0]
         greedy = self.temp <= 0
         _, lt = self.target.prefill(self.st_t, prompt, return_logits=True)
-        first = (int(torch.argmax(lt)) if greedy else
-                 int(torch.multinomial(self._probs(lt).cpu(), 1, generator=self.gen)))
+        first = self._sample(lt)
         seq = prompt.tolist() + [first]
-        if T > 1:
+        rid = object()
+        if self.recall is not None:
+            self.recall.begin_stream(rid, seq)
+        if self.draft is not None and T > 1:
             self.draft.prefill(self.st_d, prompt[:-1])
         pos = T            # position of the last accepted token; the target holds KV for positions < pos
         dpos = T - 1       # the draft holds KV for positions < dpos
-        while len(seq) - T < max_new_tokens:
-            if dpos < pos:   # the draft catches up on accepted tokens it has not seen
-                self.draft.prefill(self.st_d, torch.tensor(seq[dpos:pos], device=dev), start=dpos)
-                dpos = pos
-            last = seq[pos]
-            drafts, qs, cur = [], [], last
-            for j in range(self.S):
-                _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
-                                           return_logits=True)
-                qj = self._probs(ld)
-                d = int(torch.argmax(qj)) if greedy else int(torch.multinomial(qj.cpu(), 1, generator=self.gen))
-                drafts.append(d)
-                qs.append(qj)
-                cur = d
-            q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
-            vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
-            flags = truncate(q, vt, self.th, greedy=greedy)
-            _, logits = self.target.prefill(self.st_t, vt[0], start=pos, all_logits=True, active=flags[0])
-            keep = int(flags[0].sum()) - 1
-            acc = verify_chain(self._probs(logits)[:keep + 1], q[0, :keep], torch.tensor(drafts[:keep]), self.gen,
-                               greedy)
-            self.stats['rounds'] += 1
-            self.stats['drafted'] += self.S
-            self.stats['kept'] += keep
-            self.stats['accepted'] += len(acc) - 1
-            seq.extend(acc)
-            # the draft fed last, d_1..d_{S-1} at pos..pos+S-1: valid up to the accepted ones
-            dpos = pos + min(len(acc), self.S)
-            pos = len(seq) - 1
+        try:
+            while len(seq) - T < max_new_tokens:
+                last = seq[pos]
+                prop = self.recall.propose(rid) if self.recall is not None else None
+                if prop is not None and prop.ids:
+                    drafts = prop.ids[:max(1, max_new_tokens - (len(seq) - T))]
+                    V = self.target_vocab(dev)
+                    q = torch.zeros(len(drafts), V)
+                    q[torch.arange(len(drafts)), torch.tensor(drafts)] = 1.0     # a copy is a point mass
+                    acc = self._verify(pos, last, drafts, q)
+                    self.recall.feedback(rid, len(acc) - 1)
+                    self.stats['copies'] += 1
+                    self.stats['copied'] += len(drafts)
+                    self.stats['copy_landed'] += len(acc) - 1
+                elif self.draft is None:      # a plain target step
+                    _, lg = self.target.prefill(self.st_t, torch.tensor([last], device=dev), start=pos,
+                                                return_logits=True)
+                    acc = [self._sample(lg)]
+                    self.stats['plain'] += 1
+                else:
+                    if dpos < pos:   # the draft catches up on accepted tokens it has not seen
+                        self.draft.prefill(self.st_d, torch.tensor(seq[dpos:pos], device=dev), start=dpos)
+                        dpos = pos
+                    drafts, qs, cur = [], [], last
+                    for j in range(self.S):
+                        _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
+                                                   return_logits=True)
+                        qj = self._probs(ld)
+                        d = (int(torch.argmax(qj)) if greedy else
+                             int(torch.multinomial(qj.cpu(), 1, generator=self.gen)))
+                        drafts.append(d)
+                        qs.append(qj)
+                        cur = d
+                    q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
+                    vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
+                    flags = truncate(q, vt, self.th, greedy=greedy)
+                    keep = int(flags[0].sum()) - 1
+                    acc = self._verify(pos, last, drafts, q[0], active=flags[0], keep=keep)
+                    self.stats['rounds'] += 1
+                    self.stats['drafted'] += self.S
+                    self.stats['kept'] += keep
+                    self.stats['accepted'] += len(acc) - 1
+                    if self.recall is not None:
+                        self.recall.observe_own(rid, len(acc) - 1)
+                    # the draft fed last, d_1..d_{S-1} at pos..pos+S-1: valid up to the accepted ones
+                    dpos = pos + min(len(acc), self.S)
+                seq.extend(acc)
+                if self.recall is not None:
+                    self.recall.extend_stream(rid, acc)
+                pos = len(seq) - 1
+        finally:
+            if self.recall is not None:
+                self.recall.end_stream(rid)
         return seq[T:T + max_new_tokens]
+
+    def target_vocab(self, dev) -> int:
+        cfg = getattr(self.target, 'cfg', None)
+        return cfg.vocab if cfg is not None else int(self.target.vocab)
