@@ -75,6 +75,8 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_COLD_UNITS', 'int', 1, 'units per cold record (1: whole NUMA shards; 3: gate / up / rest dealt apart)'),
     _S('XTIER_COLD_HALF_LIFE', 'float', 50.0, 'half life (engine calls) of the use counts that pick cold victims'),
     _S('XTIER_FAST_LOAD', 'flag', False, 'read expert tensors straight from safetensors into engine shards (O_DIRECT)'),
+    _S('XTIER_SPEC_TRUNCATE_Q', 'float', 0.2, 'speculative verify truncated after the first draft with q < this (0: off)'),
+    _S('XTIER_SPEC_DRAFT_TEMP_SCALE', 'float', 0.8, 'a sampled request\'s draft runs at its temperature x this'),
     _S('XTIER_CKPT_FORMAT', 'str', 'nvfp4', 'expert format unquantized (BF16) checkpoints are quantized to: nvfp4 or mxfp4'),
     _S('XTIER_LOAD_DIGEST', 'flag', False, 'log a digest of every loaded layer'),
     _S('XTIER_TAIL_SKIP', 'str', '', 'K/N: decode calls of top-N skip experts outside every token\'s K largest routes'),

@@ -81,21 +81,43 @@ class SpeculativeDecoder:
     copy is a point-mass draft, verified by the same rule). Without a draft model, rounds with no copy are plain
     target steps."""
 
-    def __init__(self, target, draft=None, steps: int = 4, threshold: float = 0.2, temperature: float = 0.0,
-                 max_len: int = 4096, seed: int = 0, recall=None):
+    def __init__(self, target, draft=None, steps: int = 4, threshold: float | None = None, temperature: float = 0.0,
+                 max_len: int = 4096, seed: int = 0, recall=None, hot_ids: torch.Tensor | None = None,
+                 draft_temp_scale: float | None = None):
+        """threshold: verify truncation at draft confidence (default XTIER_SPEC_TRUNCATE_Q; 0: off). hot_ids [Vd]:
+        the target ids of a draft model whose head covers only a hot vocabulary (its q is scattered into the target
+        vocabulary before verification: zero where the draft can never propose, so the accept test and the residual
+        stay exact). draft_temp_scale: the draft samples at temperature x this (default XTIER_SPEC_DRAFT_TEMP_SCALE);
+        lossless for any scale, since verification uses the q the draft sampled from."""
+        from .. import config
         if draft is None and recall is None:
             raise ValueError('speculative decoding needs a draft model or a recall engine')
         self.target, self.draft, self.recall = target, draft, recall
-        self.S, self.th, self.temp = steps, threshold, temperature
+        self.S, self.temp = steps, temperature
+        self.th = config.get('XTIER_SPEC_TRUNCATE_Q') if threshold is None else threshold
+        self.draft_scale = (config.get('XTIER_SPEC_DRAFT_TEMP_SCALE') if draft_temp_scale is None
+                            else draft_temp_scale)
+        self.hot_ids = None if hot_ids is None else torch.as_tensor(hot_ids, dtype=torch.long).cpu()
         self.st_t = target.alloc_state(1, max_len)
         self.st_d = draft.alloc_state(1, max_len) if draft is not None else None
         self.gen = torch.Generator().manual_seed(seed)
         self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0, copies=0, copied=0, copy_landed=0, plain=0)
 
-    def _probs(self, logits: torch.Tensor) -> torch.Tensor:
-        if self.temp <= 0:
+    def _probs(self, logits: torch.Tensor, temp: float | None = None) -> torch.Tensor:
+        temp = self.temp if temp is None else temp
+        if temp <= 0:
             return torch.nn.functional.one_hot(torch.argmax(logits, -1), logits.shape[-1]).float()
-        return torch.softmax(logits.float() / self.temp, dim=-1)
+        return torch.softmax(logits.float() / temp, dim=-1)
+
+    def draft_probs(self, logits: torch.Tensor, V: int) -> torch.Tensor:
+        """The draft's proposal distribution over the target vocabulary: at the scaled temperature, and scattered
+        from the hot vocabulary when the draft's head covers only that."""
+        q = self._probs(logits, self.temp * self.draft_scale if self.temp > 0 else 0.0).float().cpu()
+        if self.hot_ids is None:
+            return q
+        full = torch.zeros(*q.shape[:-1], V)
+        full[..., self.hot_ids] = q
+        return full
 
     def _verify(self, pos: int, last: int, drafts: list[int], q: torch.Tensor, active=None,
                 keep: int | None = None) -> list[int]:
@@ -154,20 +176,26 @@ class SpeculativeDecoder:
                         self.draft.prefill(self.st_d, torch.tensor(seq[dpos:pos], device=dev), start=dpos)
                         dpos = pos
                     drafts, qs, cur = [], [], last
+                    V = self.target_vocab(dev)
                     for j in range(self.S):
                         _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
                                                    return_logits=True)
-                        qj = self._probs(ld)
+                        qj = self.draft_probs(ld, V)
                         d = (int(torch.argmax(qj)) if greedy else
-                             int(torch.multinomial(qj.cpu(), 1, generator=self.gen)))
+                             int(torch.multinomial(qj, 1, generator=self.gen)))
                         drafts.append(d)
                         qs.append(qj)
                         cur = d
                     q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
-                    vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
-                    flags = truncate(q, vt, self.th, greedy=greedy)
-                    keep = int(flags[0].sum()) - 1
-                    acc = self._verify(pos, last, drafts, q[0], active=flags[0], keep=keep)
+                    if self.th > 0:
+                        q = q.to(dev)
+                        vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
+                        flags = truncate(q, vt, self.th, greedy=greedy)
+                        keep = int(flags[0].sum()) - 1
+                        active = flags[0]
+                    else:                      # no truncation: every draft is verified
+                        keep, active = self.S, None
+                    acc = self._verify(pos, last, drafts, q[0], active=active, keep=keep)
                     self.stats['rounds'] += 1
                     self.stats['drafted'] += self.S
                     self.stats['kept'] += keep
