@@ -178,3 +178,43 @@ def test_copy_test(server):
     _, bad = server(Fake(vocab=70000, tokenizer=tok, corrupt=True))
     res = copy_test.run(bad, tok, src, chunks=3, lines=20, log=lambda s: None)
     assert res['differ'] == 3
+
+
+def test_speculative_serving_with_recall(server):
+    """A --recall server: one target forward per step, several tokens when a copy lands; the tokens equal the
+    target's greedy ones; repeated prompts copy from the record."""
+    import torch
+    from xtier_b200 import recall
+
+    class Bigram:
+        def __init__(self, V=64):
+            self.W = torch.randn(V, V, generator=torch.Generator().manual_seed(0)) * 4
+            self.vocab, self.device = V, torch.device('cpu')
+
+        def alloc_state(self, b, n):
+            return {}
+
+        def prefill(self, st, tokens, start=0, return_logits=False, all_logits=False, active=None):
+            lg = self.W[tokens.long()]
+            nxt = torch.argmax(lg, -1)
+            if all_logits:
+                return nxt, lg
+            return (nxt[-1:], lg[-1]) if return_logits else nxt[-1:]
+
+    tgt = Bigram()
+    be = serve.SpecBackend(tgt, recall.RecallEngine(recall.Record(), gamma=8, min_n=1.0), max_len=512)
+    _, cl = server(be)
+    prompt = [3, 9, 27, 17, 40]
+    want, t = [], prompt[-1]
+    for _ in range(40):
+        t = int(torch.argmax(tgt.W[t]))
+        want.append(t)
+    assert cl.generate(prompt, 40)['ids'] == want
+    x = cl.stream(prompt, 40)
+    assert x['ids'] == want
+    res = speed.spec_steps(cl, tokens=32, prompts=2, rounds=2, prompt_len=24, log=lambda s: None)
+    assert res['rounds'][1]['tokens_per_step'] > 1.0
+    m = cl.metrics()
+    assert m['spec_copy_landed'] > 0 and m['recall_record_ids'] > 0
+    r = cl.logprobs(prompt + want[:5], top=2)
+    assert len(r['nll']) == 9

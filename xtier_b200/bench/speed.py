@@ -5,6 +5,7 @@ long-context prefill + decode.
     python -m xtier_b200.bench.speed ttft    --url URL [--lengths 70,500,1000,2000,4096,8192] [--repeat 3]
     python -m xtier_b200.bench.speed context --url URL [--contexts 8192,65536] [--output 256] [--warmup 2048]
         [--repeats 3]
+    python -m xtier_b200.bench.speed spec    --url URL [--tokens 256] [--prompts 8] [--rounds 2]   (--recall servers)
     common: [--tokenizer DIR --corpus FILE] (prompts cut from a text; default: seeded ids) [--out FILE]
 
 decode: streamed requests with fixed prompts; per request decode tok/s from the first to the last streamed token, per
@@ -13,8 +14,9 @@ of each length, one output token, median of --repeat. context: per context lengt
 prompt tokens / time to the first token) and an answer of --output tokens, then --repeats more answers to the same
 prompt; decode tok/s is the median over the answers. A first request of --warmup tokens takes one-time costs.
 Every line printed is JSON; the last one is the summary, also written to --out.
-(Reference parity: bench/decode_speed.py, bench/ttft_probe.py, bench/context_speed.py -- the same measures against
-this framework's server.)
+spec: per request of a speculative server, target forwards, ms per forward and tokens per forward.
+(Reference parity: bench/decode_speed.py, bench/ttft_probe.py, bench/context_speed.py, bench/verify_step_bench.py --
+the same measures against this framework's server.)
 """
 from __future__ import annotations
 
@@ -98,9 +100,39 @@ def context_speed(cl: Client, contexts=(8192, 65536), output: int = 256, warmup:
     return dict(test='context_speed', output=output, rows=rows)
 
 
+def spec_steps(cl: Client, tokens: int = 256, prompts: int = 8, rounds: int = 2, prompt_len: int = 64, tok=None,
+               corpus_path=None, log=print) -> dict:
+    """Cost of one speculative step of a server started with --recall (or a draft model): per request the target
+    forwards it took (the `spec_forwards` metric), ms per forward = decode time / forwards, tokens per forward. The
+    same prompts run every round, so later rounds can copy from what earlier ones wrote."""
+    info = _info(cl)
+    rows = []
+    for r in range(rounds):
+        for i in range(prompts):
+            f0 = cl.metrics().get('spec_forwards')
+            if f0 is None:
+                raise SystemExit('the server does not report spec_forwards: start it with --recall')
+            x = cl.stream(corpus.prompt(prompt_len, info['vocab'], tok, corpus_path, salt=3000 + i), tokens)
+            fw = cl.metrics()['spec_forwards'] - f0
+            n = len(x['ids'])
+            rows.append(dict(round=r, request=i, tokens=n, forwards=fw,
+                             ms_per_step=round(1000.0 * x['decode_s'] / fw, 3) if fw else None,
+                             tokens_per_step=round((n - 1) / fw, 3) if fw else None))
+            log(json.dumps(rows[-1]))
+    summary = []
+    for r in range(rounds):
+        sel = [x for x in rows if x['round'] == r and x['forwards']]
+        fw = sum(x['forwards'] for x in sel)
+        summary.append(dict(round=r, forwards=fw, tokens_per_step=round(sum(x['tokens'] - 1 for x in sel) / fw, 3)
+                            if fw else None,
+                            ms_per_step=round(statistics.median(x['ms_per_step'] for x in sel), 3) if sel else None))
+    return dict(test='spec_steps', rounds=summary, rows=rows)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split('\n\n')[0])
-    ap.add_argument('mode', choices=('decode', 'ttft', 'context'))
+    ap.add_argument('mode', choices=('decode', 'ttft', 'context', 'spec'))
+    ap.add_argument('--prompts', type=int, default=8)
     ap.add_argument('--url', default='http://127.0.0.1:18180')
     ap.add_argument('--tokenizer')
     ap.add_argument('--corpus')
@@ -122,6 +154,8 @@ def main(argv=None):
         res = decode_speed(cl, a.tokens, a.prompt_len, a.concurrency, a.rounds, tok, a.corpus)
     elif a.mode == 'ttft':
         res = ttft(cl, [int(x) for x in a.lengths.split(',')], a.repeat, tok, a.corpus)
+    elif a.mode == 'spec':
+        res = spec_steps(cl, a.tokens, a.prompts, a.rounds, a.prompt_len, tok, a.corpus)
     else:
         res = context_speed(cl, [int(x) for x in a.contexts.split(',')], a.output, a.warmup, a.repeats, tok,
                             a.corpus)

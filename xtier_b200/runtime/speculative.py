@@ -101,7 +101,7 @@ class SpeculativeDecoder:
         self.st_t = target.alloc_state(1, max_len)
         self.st_d = draft.alloc_state(1, max_len) if draft is not None else None
         self.gen = torch.Generator().manual_seed(seed)
-        self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0, copies=0, copied=0, copy_landed=0, plain=0)
+        self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0, copies=0, copied=0, copy_landed=0, plain=0, forwards=0)
 
     def _probs(self, logits: torch.Tensor, temp: float | None = None) -> torch.Tensor:
         temp = self.temp if temp is None else temp
@@ -136,82 +136,101 @@ class SpeculativeDecoder:
             return int(torch.argmax(logits))
         return int(torch.multinomial(self._probs(logits).cpu(), 1, generator=self.gen))
 
-    def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> list[int]:
-        """Up to `max_new_tokens` new tokens after `prompt` [T]."""
+    # ------------------------------------------------------------------ one stream, step by step
+    def begin(self, prompt: torch.Tensor) -> int:
+        """Prefills `prompt` [T] (target and draft); returns the first new token."""
         dev = self.target.device
-        prompt = prompt.to(dev)
+        prompt = torch.as_tensor(prompt).to(dev)
         T = prompt.shape[0]
-        greedy = self.temp <= 0
         _, lt = self.target.prefill(self.st_t, prompt, return_logits=True)
         first = self._sample(lt)
-        seq = prompt.tolist() + [first]
-        rid = object()
+        self.seq = prompt.tolist() + [first]
+        self.rid = object()
         if self.recall is not None:
-            self.recall.begin_stream(rid, seq)
+            self.recall.begin_stream(self.rid, self.seq)
         if self.draft is not None and T > 1:
             self.draft.prefill(self.st_d, prompt[:-1])
-        pos = T            # position of the last accepted token; the target holds KV for positions < pos
-        dpos = T - 1       # the draft holds KV for positions < dpos
-        try:
-            while len(seq) - T < max_new_tokens:
-                last = seq[pos]
-                prop = self.recall.propose(rid) if self.recall is not None else None
-                if prop is not None and prop.ids:
-                    drafts = prop.ids[:max(1, max_new_tokens - (len(seq) - T))]
-                    V = self.target_vocab(dev)
-                    q = torch.zeros(len(drafts), V)
-                    q[torch.arange(len(drafts)), torch.tensor(drafts)] = 1.0     # a copy is a point mass
-                    acc = self._verify(pos, last, drafts, q)
-                    self.recall.feedback(rid, len(acc) - 1)
-                    self.stats['copies'] += 1
-                    self.stats['copied'] += len(drafts)
-                    self.stats['copy_landed'] += len(acc) - 1
-                elif self.draft is None:      # a plain target step
-                    _, lg = self.target.prefill(self.st_t, torch.tensor([last], device=dev), start=pos,
-                                                return_logits=True)
-                    acc = [self._sample(lg)]
-                    self.stats['plain'] += 1
-                else:
-                    if dpos < pos:   # the draft catches up on accepted tokens it has not seen
-                        self.draft.prefill(self.st_d, torch.tensor(seq[dpos:pos], device=dev), start=dpos)
-                        dpos = pos
-                    drafts, qs, cur = [], [], last
-                    V = self.target_vocab(dev)
-                    for j in range(self.S):
-                        _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
-                                                   return_logits=True)
-                        qj = self.draft_probs(ld, V)
-                        d = (int(torch.argmax(qj)) if greedy else
-                             int(torch.multinomial(qj, 1, generator=self.gen)))
-                        drafts.append(d)
-                        qs.append(qj)
-                        cur = d
-                    q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
-                    if self.th > 0:
-                        q = q.to(dev)
-                        vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
-                        flags = truncate(q, vt, self.th, greedy=greedy)
-                        keep = int(flags[0].sum()) - 1
-                        active = flags[0]
-                    else:                      # no truncation: every draft is verified
-                        keep, active = self.S, None
-                    acc = self._verify(pos, last, drafts, q[0], active=active, keep=keep)
-                    self.stats['rounds'] += 1
-                    self.stats['drafted'] += self.S
-                    self.stats['kept'] += keep
-                    self.stats['accepted'] += len(acc) - 1
-                    if self.recall is not None:
-                        self.recall.observe_own(rid, len(acc) - 1)
-                    # the draft fed last, d_1..d_{S-1} at pos..pos+S-1: valid up to the accepted ones
-                    dpos = pos + min(len(acc), self.S)
-                seq.extend(acc)
-                if self.recall is not None:
-                    self.recall.extend_stream(rid, acc)
-                pos = len(seq) - 1
-        finally:
+        self.pos = T            # position of the last accepted token; the target holds KV for positions < pos
+        self.dpos = T - 1       # the draft holds KV for positions < dpos
+        return first
+
+    def step(self, limit: int | None = None) -> list[int]:
+        """One target forward: the accepted drafts plus one corrected / bonus token (a plain step without a draft).
+        `limit` caps the copy length (tokens still wanted)."""
+        dev = self.target.device
+        greedy = self.temp <= 0
+        pos, seq = self.pos, self.seq
+        last = seq[pos]
+        prop = self.recall.propose(self.rid) if self.recall is not None else None
+        if prop is not None and prop.ids:
+            drafts = prop.ids[:max(1, limit)] if limit is not None else prop.ids
+            V = self.target_vocab(dev)
+            q = torch.zeros(len(drafts), V)
+            q[torch.arange(len(drafts)), torch.tensor(drafts)] = 1.0     # a copy is a point mass
+            acc = self._verify(pos, last, drafts, q)
+            self.recall.feedback(self.rid, len(acc) - 1)
+            self.stats['copies'] += 1
+            self.stats['copied'] += len(drafts)
+            self.stats['copy_landed'] += len(acc) - 1
+        elif self.draft is None:      # a plain target step
+            _, lg = self.target.prefill(self.st_t, torch.tensor([last], device=dev), start=pos, return_logits=True)
+            acc = [self._sample(lg)]
+            self.stats['plain'] += 1
+        else:
+            if self.dpos < pos:   # the draft catches up on accepted tokens it has not seen
+                self.draft.prefill(self.st_d, torch.tensor(seq[self.dpos:pos], device=dev), start=self.dpos)
+                self.dpos = pos
+            drafts, qs, cur = [], [], last
+            V = self.target_vocab(dev)
+            for j in range(self.S):
+                _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
+                                           return_logits=True)
+                qj = self.draft_probs(ld, V)
+                d = int(torch.argmax(qj)) if greedy else int(torch.multinomial(qj, 1, generator=self.gen))
+                drafts.append(d)
+                qs.append(qj)
+                cur = d
+            q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
+            if self.th > 0:
+                q = q.to(dev)
+                vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
+                flags = truncate(q, vt, self.th, greedy=greedy)
+                keep = int(flags[0].sum()) - 1
+                active = flags[0]
+            else:                      # no truncation: every draft is verified
+                keep, active = self.S, None
+            acc = self._verify(pos, last, drafts, q[0], active=active, keep=keep)
+            self.stats['rounds'] += 1
+            self.stats['drafted'] += self.S
+            self.stats['kept'] += keep
+            self.stats['accepted'] += len(acc) - 1
             if self.recall is not None:
-                self.recall.end_stream(rid)
-        return seq[T:T + max_new_tokens]
+                self.recall.observe_own(self.rid, len(acc) - 1)
+            # the draft fed last, d_1..d_{S-1} at pos..pos+S-1: valid up to the accepted ones
+            self.dpos = pos + min(len(acc), self.S)
+        self.stats['forwards'] += 1
+        seq.extend(acc)
+        if self.recall is not None:
+            self.recall.extend_stream(self.rid, acc)
+        self.pos = len(seq) - 1
+        return acc
+
+    def end(self, add: bool = True):
+        """Ends the stream (its ids go to the recall record unless add=False)."""
+        if self.recall is not None and getattr(self, 'rid', None) is not None:
+            self.recall.end_stream(self.rid, add)
+        self.rid = None
+
+    def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> list[int]:
+        """Up to `max_new_tokens` new tokens after `prompt` [T]."""
+        T = torch.as_tensor(prompt).shape[0]
+        self.begin(prompt)
+        try:
+            while len(self.seq) - T < max_new_tokens:
+                self.step(max_new_tokens - (len(self.seq) - T))
+        finally:
+            self.end()
+        return self.seq[T:T + max_new_tokens]
 
     def target_vocab(self, dev) -> int:
         cfg = getattr(self.target, 'cfg', None)

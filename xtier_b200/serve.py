@@ -3,6 +3,8 @@ measures).
 
     python -m xtier_b200.serve --model qwen3-moe [--layers 48] [--hot 0.4] [--max-len 8192] --port 18180
     python -m xtier_b200.serve --checkpoint DIR [--hot 0.4] ...       # a Hugging Face qwen3_moe checkpoint
+    ... [--recall DIR|memory]        # speculative serving: Recall copy drafts verified by the target (one forward
+                                     # per step, several tokens when a copy lands)
 
 Endpoints
   GET  /health               {"ready": true, "vocab": V, "max_len": L, "tokenizer": bool} once the model is built and its
@@ -63,19 +65,7 @@ class GenBackend:
         return t
 
     def logprobs(self, ids: list[int], top: int):
-        import torch
-        m = self.model
-        st = self.gen.state
-        _, logits = m.prefill(st, torch.tensor(ids, device=m.device), all_logits=True)
-        nll, tops = [], []
-        tgt = torch.tensor(ids[1:], device=m.device)
-        for s in range(0, len(ids) - 1, 512):
-            lp = torch.log_softmax(logits[s:min(s + 512, len(ids) - 1)].float(), dim=-1)
-            nll += (-lp.gather(1, tgt[s:s + lp.shape[0], None])[:, 0]).tolist()
-            if top > 0:
-                v, i = lp.topk(top, dim=-1)
-                tops += [list(zip(a, b)) for a, b in zip(i.tolist(), v.tolist())]
-        return nll, tops
+        return score(self.model, self.gen.state, ids, top)
 
     def check(self):
         self.gen.check()
@@ -83,6 +73,75 @@ class GenBackend:
     def snapshot(self, state) -> dict:
         from .utils.metrics import snapshot
         return snapshot(self.model, self.mailbox, state)
+
+
+def score(model, state, ids: list[int], top: int):
+    """(-log p(ids[i+1] | ids[:i+1]) per position, the `top` most likely (id, logprob) per position) from one
+    forward of `model` over `ids` with every position's logits."""
+    import torch
+    dev = model.device
+    _, logits = model.prefill(state, torch.tensor(ids, device=dev), all_logits=True)
+    nll, tops = [], []
+    tgt = torch.tensor(ids[1:], device=dev)
+    for s in range(0, len(ids) - 1, 512):
+        lp = torch.log_softmax(logits[s:min(s + 512, len(ids) - 1)].float(), dim=-1)
+        nll += (-lp.gather(1, tgt[s:s + lp.shape[0], None])[:, 0]).tolist()
+        if top > 0:
+            v, i = lp.topk(top, dim=-1)
+            tops += [list(zip(a, b)) for a, b in zip(i.tolist(), v.tolist())]
+    return nll, tops
+
+
+class SpecBackend:
+    """Speculative serving: each step is one target forward that verifies copy drafts from a Recall engine (and / or
+    a draft model's chain); a step yields one or more tokens. The stream's text goes to the recall record when the
+    request ends."""
+
+    def __init__(self, model, recall=None, draft=None, max_len: int = 8192, tokenizer=None, temperature: float = 0.0,
+                 mailbox=None):
+        from .runtime.speculative import SpeculativeDecoder
+        self.model, self.recall, self.tokenizer, self.mailbox = model, recall, tokenizer, mailbox
+        cfg = getattr(model, 'cfg', None)
+        self.vocab = cfg.vocab if cfg is not None else int(model.vocab)
+        self.max_len = max_len
+        self.dec = SpeculativeDecoder(model, draft, recall=recall, max_len=max_len, temperature=temperature)
+        self.active = False
+
+    def prefill(self, ids: list[int]) -> int:
+        import torch
+        if self.active:
+            self.dec.end()
+        self.active = True
+        return self.dec.begin(torch.tensor(ids))
+
+    def decode(self) -> list[int]:
+        return self.dec.step()
+
+    def finish(self):
+        if self.active:
+            self.dec.end()
+            self.active = False
+
+    def logprobs(self, ids: list[int], top: int):
+        return score(self.model, self.dec.st_t, ids, top)
+
+    def check(self):
+        mb = self.mailbox or getattr(self.model, 'mailbox', None)
+        if mb is not None:
+            mb.check()
+
+    def snapshot(self, state) -> dict:
+        snap = {}
+        if self.mailbox is not None:
+            from .utils.metrics import snapshot
+            snap = snapshot(self.model, self.mailbox, state)
+        snap.update({f'spec_{k}': v for k, v in self.dec.stats.items()})
+        if self.recall is not None:
+            st = self.recall.stats()
+            snap.update(recall_offers=st['offers'], recall_landed=st['landed'], recall_probes=st['probes'])
+            if st['record'] is not None:
+                snap['recall_record_ids'] = st['record']['ids']
+        return snap
 
 
 class Server:
@@ -165,12 +224,20 @@ class Server:
             if emit is not None and emit(tok) is False:
                 aborted = True
             t_last = t_first
-            while not aborted and len(out) < n and tok not in stop:
-                tok = be.decode()
-                out.append(tok)
-                t_last = time.perf_counter()
-                if emit is not None and emit(tok) is False:
-                    aborted = True
+            try:
+                while not aborted and len(out) < n and out[-1] not in stop:
+                    got = be.decode()          # one token, or several (a speculative step)
+                    for tok in (got if isinstance(got, list) else [got]):
+                        if len(out) >= n or out[-1] in stop:
+                            break
+                        out.append(tok)
+                        if emit is not None and emit(tok) is False:
+                            aborted = True
+                            break
+                    t_last = time.perf_counter()
+            finally:
+                if hasattr(be, 'finish'):
+                    be.finish()
             be.check()
             self.state['requests'] += 1
             self.state['tokens'] += len(out)
@@ -340,6 +407,14 @@ def build(args):
         model = Qwen3MoeModel(cfg, device='cuda', seed=args.seed, hot_fraction=args.hot, mailbox=mailbox)
     if mailbox is not None:
         mailbox.start()
+    if args.recall:
+        from . import recall
+        ident = (recall.tokenizer_identity(tok, args.checkpoint or args.model) if tok is not None
+                 else {'model': args.checkpoint or f'{args.model}-seed{args.seed}', 'vocab': model.cfg.vocab})
+        rec = recall.Record(None if args.recall == 'memory' else args.recall, identity=ident,
+                            budget_ids=int(args.recall_gib * (1 << 28)))
+        eng = recall.RecallEngine(rec, gamma=args.recall_gamma)
+        return SpecBackend(model, eng, max_len=args.max_len, tokenizer=tok, mailbox=mailbox)
     gen = Generator(model, batch=1, max_len=args.max_len)
     be = GenBackend(model, gen, tok, mailbox)
     be.prefill([0])        # captures the decode graph before the server says it is ready
@@ -363,6 +438,10 @@ def main(argv=None):
     ap.add_argument('--hot', type=float, default=0.4)
     ap.add_argument('--max-len', type=int, default=8192)
     ap.add_argument('--max-queue', type=int, default=8)
+    ap.add_argument('--recall', default=None,
+                    help='serve with Recall copy drafts verified by the target: a record directory, or "memory"')
+    ap.add_argument('--recall-gib', type=float, default=1.0 / 16, help='record size budget (GiB of int32 ids)')
+    ap.add_argument('--recall-gamma', type=int, default=16, help='longest copy draft')
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--host', default='127.0.0.1')
     ap.add_argument('--port', type=int, default=18180)
