@@ -218,3 +218,67 @@ def test_speculative_serving_with_recall(server):
     assert m['spec_copy_landed'] > 0 and m['recall_record_ids'] > 0
     r = cl.logprobs(prompt + want[:5], top=2)
     assert len(r['nll']) == 9
+
+
+class Canned:
+    """A backend that answers every prompt with the same text, then its end-of-turn id."""
+
+    def __init__(self, reply, tok):
+        self.tokenizer, self.vocab, self.max_len = tok, 70000, 4096
+        self.reply = tok.encode(reply) + [tok.eos_token_id]
+
+    def prefill(self, ids):
+        self.i = 0
+        return self.decode()
+
+    def decode(self):
+        t = self.reply[min(self.i, len(self.reply) - 1)]
+        self.i += 1
+        return t
+
+    def check(self):
+        pass
+
+
+def _sse(cl, body):
+    import http.client
+    import json
+    c = http.client.HTTPConnection(cl.host, cl.port, timeout=30)
+    c.request('POST', '/v1/chat/completions', json.dumps(body).encode(), {'Content-Type': 'application/json'})
+    r = c.getresponse()
+    assert r.status == 200 and r.getheader('Content-Type') == 'text/event-stream'
+    events = [line[6:] for line in r.read().decode().split('\n') if line.startswith('data: ')]
+    c.close()
+    return events
+
+
+def test_chat_completions(server):
+    import json
+    tok = CharTok()
+    reply = 'Hello <tool_call>\n{"name": "read_file", "arguments": {"path": "a.py"}}\n</tool_call>'
+    _, cl = server(Canned(reply, tok))
+    msgs = [{'role': 'user', 'content': 'read a.py'}]
+    tools = [{'type': 'function', 'function': {'name': 'read_file', 'parameters': {}}}]
+    st, r = cl.request('POST', '/v1/chat/completions', {'messages': msgs, 'tools': tools})
+    assert st == 200 and r['object'] == 'chat.completion'
+    ch = r['choices'][0]
+    assert ch['message']['content'] == 'Hello' and ch['finish_reason'] == 'tool_calls'
+    call = ch['message']['tool_calls'][0]['function']
+    assert call['name'] == 'read_file' and json.loads(call['arguments']) == {'path': 'a.py'}
+    assert r['usage']['completion_tokens'] == len(reply) and r['usage']['prompt_tokens'] > 0
+    st, r = cl.request('POST', '/v1/chat/completions', {'messages': msgs})          # no tools: plain text
+    assert r['choices'][0]['message']['content'] == reply and r['choices'][0]['finish_reason'] == 'stop'
+    st, r = cl.request('POST', '/v1/chat/completions', {'messages': msgs, 'max_tokens': 3})
+    assert r['choices'][0]['message']['content'] == 'Hel' and r['choices'][0]['finish_reason'] == 'length'
+    ev = _sse(cl, {'messages': msgs, 'stream': True, 'stream_options': {'include_usage': True}})
+    assert ev[-1] == '[DONE]'
+    chunks = [json.loads(e) for e in ev[:-1]]
+    text = ''.join(c['choices'][0]['delta'].get('content', '') for c in chunks if c['choices'])
+    assert text == reply
+    assert chunks[-2]['choices'][0]['finish_reason'] == 'stop' and chunks[-1]['usage']['completion_tokens'] == len(reply)
+    for body in ({'messages': msgs, 'temperature': 0.7}, {'messages': []}, {'messages': msgs, 'max_tokens': 0}):
+        st, r = cl.request('POST', '/v1/chat/completions', body)
+        assert st == 400 and 'message' in r['error'], body
+    assert cl.request('GET', '/v1/models')[1]['data'][0]['id'] == 'xtier-b200'
+    _, plain = server(Fake())
+    assert plain.request('POST', '/v1/chat/completions', {'messages': msgs})[0] == 400     # no tokenizer

@@ -18,6 +18,10 @@ Endpoints
                              with "stream": true, newline-delimited JSON in a chunked response: {"id": t, "text": s}
                              per token, then {"done": true, ...the summary above}. A client that goes away ends the
                              decode at the next token.
+  POST /v1/chat/completions  OpenAI chat format (with a tokenizer that has a chat template): messages, max_tokens,
+                             stream (server-sent events, stream_options.include_usage), tools (Qwen-style
+                             <tool_call> blocks in the reply come back as tool_calls), chat_template_kwargs; GET
+                             /v1/models lists the one model
   POST /v1/logprobs          {"prompt_ids": [...], "top": N} -> {"nll": [-log p(ids[i+1] | ids[:i+1])],
                              "top": [[[id, logprob], ...] per position]} (fixed-text perplexity, A/B of configurations)
 
@@ -30,6 +34,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import re
 import threading
 import time
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
@@ -198,6 +203,47 @@ class Server:
             raise BadRequest('stop_ids must be a list of integers')
         return ids, n, set(stop), bool(req.get('stream', False))
 
+    def parse_chat(self, req: dict):
+        """OpenAI chat request -> (prompt ids, max tokens, stop ids, stream, include usage, tools given)."""
+        if not isinstance(req, dict):
+            raise BadRequest('the body must be a JSON object')
+        tok = getattr(self.backend, 'tokenizer', None)
+        if tok is None or not hasattr(tok, 'apply_chat_template'):
+            raise BadRequest('this server has no tokenizer with a chat template: use /v1/generate with prompt_ids')
+        msgs = req.get('messages')
+        if not isinstance(msgs, list) or not msgs or not all(isinstance(m, dict) and 'role' in m for m in msgs):
+            raise BadRequest('messages must be a non-empty list of {"role": ..., "content": ...}')
+        temp = req.get('temperature')
+        if temp not in (None, 0, 0.0) and not getattr(self.backend, 'sampling', False):
+            raise BadRequest('this server decodes greedily: send temperature 0 or none')
+        n = req.get('max_completion_tokens', req.get('max_tokens', 512))
+        if not isinstance(n, int) or isinstance(n, bool) or n < 1:
+            raise BadRequest('max_tokens must be a positive integer')
+        tools = req.get('tools')
+        kw = dict(req.get('chat_template_kwargs') or {})
+        try:
+            ids = tok.apply_chat_template(msgs, tools=tools, add_generation_prompt=True, tokenize=True, **kw)
+        except TypeError:
+            ids = tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True)
+        except Exception as e:   # noqa: BLE001 -- a template that refuses the messages
+            raise BadRequest(f'chat template: {type(e).__name__}: {e}')
+        ids = list(ids['input_ids'] if isinstance(ids, dict) else ids)
+        n = min(n, self.backend.max_len - len(ids) - 8)
+        if n < 1:
+            raise BadRequest(f'the prompt ({len(ids)} tokens) leaves no room under the server max length')
+        stop = set()
+        for t in (getattr(tok, 'eos_token_id', None), ):
+            if isinstance(t, int):
+                stop.add(t)
+        conv = getattr(tok, 'convert_tokens_to_ids', None)
+        if conv is not None:
+            for name in ('<|im_end|>', '<|endoftext|>', '<|eot_id|>'):
+                t = conv(name)
+                if isinstance(t, int) and t >= 0 and t != getattr(tok, 'unk_token_id', None):
+                    stop.add(t)
+        opts = req.get('stream_options') or {}
+        return ids, n, stop, bool(req.get('stream', False)), bool(opts.get('include_usage')), bool(tools)
+
     # ------------------------------------------------------------------ work
     def enter(self) -> bool:
         """Takes a place in the queue (False: full)."""
@@ -276,6 +322,28 @@ class Server:
         return {'nll': nll, 'top': tops, 'prompt_tokens': len(ids)}
 
 
+_TOOL_CALL = re.compile(r'<tool_call>\s*(\{.*?\})\s*</tool_call>', re.S)
+
+
+def split_tool_calls(text: str):
+    """(content without the <tool_call>{json}</tool_call> blocks or None, OpenAI tool_calls) of a reply; a block
+    whose JSON does not parse stays in the content."""
+    calls = []
+
+    def take(m):
+        try:
+            obj = json.loads(m.group(1))
+            name = obj['name']
+        except (ValueError, KeyError, TypeError):
+            return m.group(0)
+        args = obj.get('arguments', {})
+        calls.append({'id': f'call_{len(calls)}', 'type': 'function',
+                      'function': {'name': name, 'arguments': args if isinstance(args, str) else json.dumps(args)}})
+        return ''
+    rest = _TOOL_CALL.sub(take, text).strip()
+    return (rest or None) if calls else text, calls
+
+
 def make_handler(server: Server):
     class Handler(BaseHTTPRequestHandler):
         server_version = 'xtier-b200'
@@ -294,7 +362,99 @@ def make_handler(server: Server):
         def _json(self, code, obj):
             self._send(code, json.dumps(obj).encode())
 
+        def _chat(self):
+            if not server.state['ready']:
+                return self._json(503, {'error': {'message': 'loading'}})
+            try:
+                req = self._body()
+                if req is None:
+                    self.close_connection = True
+                    return self._json(413, {'error': {'message': 'body too large'}})
+                ids, n, stop, stream, usage, tools = server.parse_chat(req)
+            except BadRequest as e:
+                return self._json(400, {'error': {'message': str(e), 'type': 'invalid_request_error'}})
+            if not server.enter():
+                return self._json(503, {'error': {'message': 'queue full'}})
+            tok = server.backend.tokenizer
+            model = req.get('model') or 'xtier-b200'
+            cid = f'chatcmpl-{time.time_ns():x}'
+            created = int(time.time())
+
+            def finish_reason(res):
+                if res['ids'] and res['ids'][-1] in stop:
+                    return 'stop'
+                return 'length' if len(res['ids']) >= n else 'stop'
+
+            def text_of(out):
+                return tok.decode([t for t in out if t not in stop], skip_special_tokens=True)
+
+            if not stream:
+                try:
+                    res = server.generate(ids, n, stop)
+                except Exception as e:   # noqa: BLE001
+                    return self._json(500, {'error': {'message': f'{type(e).__name__}: {e}'}})
+                text = text_of(res['ids'])
+                content, calls = split_tool_calls(text) if tools else (text, [])
+                msg = {'role': 'assistant', 'content': content}
+                if calls:
+                    msg['tool_calls'] = calls
+                done = len([t for t in res['ids'] if t not in stop])
+                return self._json(200, {
+                    'id': cid, 'object': 'chat.completion', 'created': created, 'model': model,
+                    'choices': [{'index': 0, 'message': msg,
+                                 'finish_reason': 'tool_calls' if calls else finish_reason(res)}],
+                    'usage': {'prompt_tokens': len(ids), 'completion_tokens': done,
+                              'total_tokens': len(ids) + done}})
+            self.send_response(200)
+            self.send_header('Content-Type', 'text/event-stream')
+            self.send_header('Cache-Control', 'no-cache')
+            self.send_header('Transfer-Encoding', 'chunked')
+            self.end_headers()
+
+            def event(obj) -> bool:
+                data = b'data: ' + (obj if isinstance(obj, bytes) else json.dumps(obj).encode()) + b'\n\n'
+                try:
+                    self.wfile.write(b'%x\r\n%s\r\n' % (len(data), data))
+                    self.wfile.flush()
+                    return True
+                except (BrokenPipeError, ConnectionResetError, OSError):
+                    return False
+
+            def chunk(delta, reason=None):
+                return {'id': cid, 'object': 'chat.completion.chunk', 'created': created, 'model': model,
+                        'choices': [{'index': 0, 'delta': delta, 'finish_reason': reason}]}
+            out, sent = [], ['']
+
+            def emit(t):
+                out.append(t)
+                text = text_of(out)
+                if text.endswith('\ufffd'):      # an incomplete multi-byte character: wait for the next token
+                    return True
+                piece, sent[0] = text[len(sent[0]):], text
+                return event(chunk({'content': piece})) if piece else True
+            try:
+                if not event(chunk({'role': 'assistant', 'content': ''})):
+                    return None
+                res = server.generate(ids, n, stop, emit)
+                ok = event(chunk({}, finish_reason(res)))
+                if ok and usage:
+                    done = len([t for t in res['ids'] if t not in stop])
+                    u = chunk({})
+                    u['choices'] = []
+                    u['usage'] = {'prompt_tokens': len(ids), 'completion_tokens': done,
+                                  'total_tokens': len(ids) + done}
+                    ok = event(u)
+                if ok and event(b'[DONE]'):
+                    self.wfile.write(b'0\r\n\r\n')
+            except Exception as e:   # noqa: BLE001
+                event({'error': {'message': f'{type(e).__name__}: {e}'}})
+            self.close_connection = True
+            return None
+
         def do_GET(self):
+            if self.path == '/v1/models':
+                return self._json(200, {'object': 'list', 'data': [{'id': 'xtier-b200', 'object': 'model',
+                                                                    'owned_by': 'xtier-b200'}]})
             if self.path == '/health':
                 be = server.backend
                 info = {'ready': server.state['ready']}
@@ -329,6 +489,8 @@ def make_handler(server: Server):
             if self.path == '/flush_cache':
                 self.rfile.read(int(self.headers.get('Content-Length', '0') or 0))
                 return self._json(200, {'ok': True})
+            if self.path == '/v1/chat/completions':
+                return self._chat()
             if self.path not in ('/v1/generate', '/v1/logprobs'):
                 return self._json(404, {'error': 'not found'})
             if not server.state['ready']:
