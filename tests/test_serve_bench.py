@@ -282,3 +282,70 @@ def test_chat_completions(server):
     assert cl.request('GET', '/v1/models')[1]['data'][0]['id'] == 'xtier-b200'
     _, plain = server(Fake())
     assert plain.request('POST', '/v1/chat/completions', {'messages': msgs})[0] == 400     # no tokenizer
+
+
+class JsonChatTok(CharTok):
+    """Chat template: the messages as ASCII JSON, one id per character."""
+
+    def apply_chat_template(self, msgs, add_generation_prompt=True, tokenize=True, **kw):
+        import json
+        return self.encode(json.dumps(msgs))
+
+
+class Scripted:
+    """Answers the n-th request with the n-th scripted reply."""
+
+    def __init__(self, replies, tok):
+        self.tokenizer, self.vocab, self.max_len = tok, 70000, 1 << 20
+        self.replies = [tok.encode(r) + [tok.eos_token_id] for r in replies]
+        self.n = -1
+
+    def prefill(self, ids):
+        self.n += 1
+        self.cur = self.replies[min(self.n, len(self.replies) - 1)]
+        self.i = 0
+        return self.decode()
+
+    def decode(self):
+        t = self.cur[min(self.i, len(self.cur) - 1)]
+        self.i += 1
+        return t
+
+    def check(self):
+        pass
+
+
+def test_agent_bench_session(server):
+    import json
+    from pathlib import Path
+    from xtier_b200.bench import agent
+    src = Path(agent.__file__).resolve().parents[1]
+    before = (src / 'bench' / 'corpus.py').read_text()
+
+    def call(name, **args):
+        return '<tool_call>\n' + json.dumps({'name': name, 'arguments': args}) + '\n</tool_call>'
+    replies = ['Reading. ' + call('read_file', path='bench/corpus.py', start_line=1, end_line=5),
+               call('edit_file', path='bench/corpus.py', old_string='def tokenizer(path: str | None):',
+                    new_string='def tokenizer(path: str | None):  # edited'),
+               call('check_python', path='bench/corpus.py') + call('grep', pattern='edited', path='bench'),
+               'Done: the function is edited and the file checks.']
+    _, cl = server(Scripted(replies, JsonChatTok()))
+    res = agent.run_session(cl, 'tiny', (500, 'Edit the corpus module.', ['bench/corpus.py']), src, steps=6,
+                            count=len, run_id='t1', context_limit=1 << 24, log=lambda s: None)
+    rows = res['requests']
+    assert [r['tools'] for r in rows] == [['read_file'], ['edit_file'], ['check_python', 'grep'], []]
+    assert rows[0]['prefill_tps'] > 0 and all(r['output_tokens'] > 0 for r in rows)
+    assert (src / 'bench' / 'corpus.py').read_text() == before          # the edit stayed in the sandbox
+    t = agent.table([{'sessions': [res]}])
+    assert t['all']['requests'] == 4 and t['sessions']['tiny']['cold_prefill_tps'] > 0
+    sb = agent.Sandbox(src)
+    try:
+        assert 'outside' in sb.call('read_file', {'path': '../../etc/passwd'})
+        assert sb.call('edit_file', {'path': 'bench/corpus.py', 'old_string': 'import', 'new_string': 'x'}).startswith(
+            'error: old_string occurs')
+        assert sb.call('write_file', {'path': 'new/x.py', 'content': 'def f(:\n'}).startswith('ok')
+        assert sb.call('check_python', {'path': 'new/x.py'}).startswith('syntax error')
+        assert sb.call('nope', {}) == 'error: no tool nope'
+    finally:
+        sb.close()
+    assert not sb.root.exists()

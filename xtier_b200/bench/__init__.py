@@ -6,6 +6,7 @@ or seeded ids for a random-init model):
     quality.py      fixed-text perplexity with top-N dumps, the KL lower bound between two dumps, token stability across
                     recomputed prompts
     copy_test.py    verbatim copy of source windows (a real instruction-tuned checkpoint)
+    agent.py        coding-agent sessions over the chat API with sandboxed tools, sized to target contexts
     robustness.py   aborted streams, refused requests, concurrent requests; a long prompt beside a decoding request
 
 `bench.py` at the repository root is the driver's throughput benchmark; these measure a served model as a client sees
