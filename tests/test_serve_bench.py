@@ -349,3 +349,23 @@ def test_agent_bench_session(server):
     finally:
         sb.close()
     assert not sb.root.exists()
+
+
+def test_sampling_parameters(server):
+    class Sampler(Fake):
+        sampling = True
+
+        def set_sampling(self, t, p):
+            self.seen = (t, p)
+
+    be = Sampler()
+    _, cl = server(be)
+    cl.request('POST', '/v1/generate', {'prompt_ids': [1, 2], 'max_new_tokens': 2, 'temperature': 0.7, 'top_p': 0.9})
+    assert be.seen == (0.7, 0.9)
+    cl.generate([1, 2], 2)
+    assert be.seen == (0.0, 1.0)
+    for bad in ({'temperature': -1}, {'top_p': 0}, {'top_p': 1.5}, {'temperature': 'hot'}):
+        assert cl.request('POST', '/v1/generate', {'prompt_ids': [1], **bad})[0] == 400, bad
+    _, greedy = server(Fake())
+    st, r = greedy.request('POST', '/v1/generate', {'prompt_ids': [1], 'temperature': 0.5})
+    assert st == 400 and 'greedily' in r['error']

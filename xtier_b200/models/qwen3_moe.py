@@ -310,6 +310,8 @@ class Qwen3MoeModel:
             o=torch.empty(batch, H, dtype=torch.bfloat16, device=dev),
             logits=torch.empty(batch, cfg.vocab, dtype=torch.bfloat16, device=dev),
             next=torch.zeros(batch, dtype=torch.int64, device=dev),
+            temp=torch.zeros(batch, dtype=torch.float32, device=dev),     # per row; 0: greedy (runtime/sampling.py)
+            top_p=torch.ones(batch, dtype=torch.float32, device=dev),
         )
 
     def decode_step(self, st: dict, buf: dict):
@@ -342,7 +344,11 @@ class Qwen3MoeModel:
             L['moe'].forward(buf['h'], out=buf['moe_out'])
         ops.add_rmsnorm(buf['moe_out'], buf['residual'], self.final_norm, buf['h'], cfg.eps)
         ops.gemv(buf['h'], self.lm_head, buf['logits'])
-        torch.argmax(buf['logits'], dim=-1, out=buf['next'])
+        if getattr(self, 'sampling', False):   # temperature / top-p per row, decided on the device
+            from ..runtime.sampling import sample
+            sample(buf['logits'], buf['temp'], buf['top_p'], out=buf['next'])
+        else:
+            torch.argmax(buf['logits'], dim=-1, out=buf['next'])
         buf['prev'].copy_(buf['tokens'])
         if side is not None:
             main.wait_stream(side)

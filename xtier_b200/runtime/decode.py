@@ -15,8 +15,12 @@ import torch
 
 class Generator:
     def __init__(self, model, batch: int = 1, max_len: int = 4096, use_graph: bool = True, policy=None,
-                 governor=None):
+                 governor=None, sampling: bool = False):
+        """sampling: the decode step draws each row's token with that row's temperature and top-p
+        (`set_sampling`; temperature 0 stays greedy) instead of taking the argmax. Decided before capture."""
         self.model = model
+        self.sampling = sampling
+        model.sampling = sampling
         # between decode steps: adaptive hot-slot swaps and the elastic cache's sizing (the model's, unless given)
         self.policy = policy if policy is not None else getattr(model, 'policy', None)
         self.governor = governor if governor is not None else getattr(model, 'governor', None)
@@ -68,6 +72,14 @@ class Generator:
         if bg is not None:
             bg.check()
 
+    def set_sampling(self, temperature, top_p=1.0):
+        """Per-row (or one for all rows) temperature and top-p of the following steps (device buffers the captured
+        step reads; no recapture)."""
+        if not self.sampling and torch.any(torch.as_tensor(temperature, dtype=torch.float32) > 0):
+            raise ValueError('this Generator decodes greedily: create it with sampling=True')
+        self.buf['temp'].copy_(torch.as_tensor(temperature, dtype=torch.float32).expand(self.batch))
+        self.buf['top_p'].copy_(torch.as_tensor(top_p, dtype=torch.float32).expand(self.batch))
+
     # ------------------------------------------------------------------ public API
     def prefill(self, prompts: torch.Tensor):
         """prompts [batch, T] token ids (host or device): fills the KV cache, sets the first decode input."""
@@ -75,16 +87,23 @@ class Generator:
         first = []
         T = prompts.shape[1]
         gov = self.governor
+        def run(ids, b):
+            if not self.sampling:
+                return self.model.prefill(self.state, ids, row=b)
+            from .sampling import sample     # the first token is drawn like the decode step's
+            _, lg = self.model.prefill(self.state, ids, row=b, return_logits=True)
+            return sample(lg[None], self.buf['temp'][b:b + 1], self.buf['top_p'][b:b + 1])
+
         for b in range(self.batch):
             ids = prompts[b].to(self.model.device)
             if gov is None:
-                first.append(self.model.prefill(self.state, ids, row=b))
+                first.append(run(ids, b))
                 continue
             gov.before_alloc(T, T)     # extra slots go back until the predicted need fits
             torch.cuda.synchronize()
             before = torch.cuda.memory_allocated()
             torch.cuda.reset_peak_memory_stats()
-            first.append(gov.guarded(self.model.prefill, self.state, ids, row=b))
+            first.append(gov.guarded(run, ids, b))
             gov.after_forward(T, T, before, torch.cuda.max_memory_allocated())
         self.buf['tokens'].copy_(torch.cat(first).view(-1))
         if 'prev' in self.buf:   # the last prompt token precedes the first decode input

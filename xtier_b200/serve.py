@@ -13,7 +13,8 @@ Endpoints
                              /metrics/prometheus: the same in the Prometheus text format
   POST /flush_cache          {"ok": true}; nothing is cached between requests (every prompt is a cold prefill)
   POST /v1/generate          {"prompt_ids": [...] | "prompt": "text" (with a tokenizer), "max_new_tokens": n,
-                              "stream": false, "stop_ids": [...]}
+                              "stream": false, "stop_ids": [...], "temperature": 0, "top_p": 1 (a server started
+                              with --sampling draws tokens; otherwise a temperature is refused)}
                              -> {"ids": [...], "text": ..., "prompt_tokens": T, "ttft_s": ..., "decode_tok_s": ...};
                              with "stream": true, newline-delimited JSON in a chunked response: {"id": t, "text": s}
                              per token, then {"done": true, ...the summary above}. A client that goes away ends the
@@ -54,6 +55,10 @@ class GenBackend:
         self.model, self.gen, self.tokenizer, self.mailbox = model, gen, tokenizer, mailbox
         self.vocab = model.cfg.vocab
         self.max_len = gen.max_len
+        self.sampling = gen.sampling
+
+    def set_sampling(self, temperature: float, top_p: float):
+        self.gen.set_sampling(temperature, top_p)
 
     def prefill(self, ids: list[int]) -> int:
         import torch
@@ -201,7 +206,24 @@ class Server:
         stop = req.get('stop_ids', [])
         if not isinstance(stop, list) or not all(isinstance(t, int) for t in stop):
             raise BadRequest('stop_ids must be a list of integers')
+        self.sampling_of(req)
         return ids, n, set(stop), bool(req.get('stream', False))
+
+    def sampling_of(self, req: dict) -> tuple[float, float]:
+        """(temperature, top_p) of a request; 400 when the backend decodes greedily and a temperature is asked."""
+        temp = req.get('temperature', 0.0)
+        top_p = req.get('top_p', 1.0)
+        if temp is None:
+            temp = 0.0
+        if top_p is None:
+            top_p = 1.0
+        if not isinstance(temp, (int, float)) or isinstance(temp, bool) or not 0 <= temp <= 10:
+            raise BadRequest('temperature must be a number in [0, 10]')
+        if not isinstance(top_p, (int, float)) or isinstance(top_p, bool) or not 0 < top_p <= 1:
+            raise BadRequest('top_p must be a number in (0, 1]')
+        if temp > 0 and not getattr(self.backend, 'sampling', False):
+            raise BadRequest('this server decodes greedily (start it with --sampling): send temperature 0 or none')
+        return float(temp), float(top_p)
 
     def parse_chat(self, req: dict):
         """OpenAI chat request -> (prompt ids, max tokens, stop ids, stream, include usage, tools given)."""
@@ -213,9 +235,7 @@ class Server:
         msgs = req.get('messages')
         if not isinstance(msgs, list) or not msgs or not all(isinstance(m, dict) and 'role' in m for m in msgs):
             raise BadRequest('messages must be a non-empty list of {"role": ..., "content": ...}')
-        temp = req.get('temperature')
-        if temp not in (None, 0, 0.0) and not getattr(self.backend, 'sampling', False):
-            raise BadRequest('this server decodes greedily: send temperature 0 or none')
+        self.sampling_of(req)
         n = req.get('max_completion_tokens', req.get('max_tokens', 512))
         if not isinstance(n, int) or isinstance(n, bool) or n < 1:
             raise BadRequest('max_tokens must be a positive integer')
@@ -258,11 +278,14 @@ class Server:
         with self.qlock:
             self.waiting -= 1
 
-    def generate(self, ids, n, stop, emit=None) -> dict:
-        """Runs one request; emit(token) per new token returns False when the client is gone."""
+    def generate(self, ids, n, stop, emit=None, sampling=(0.0, 1.0)) -> dict:
+        """Runs one request; emit(token) per new token returns False when the client is gone; sampling:
+        (temperature, top_p)."""
         be = self.backend
         with self.lock:
             self._started()
+            if hasattr(be, 'set_sampling'):
+                be.set_sampling(*sampling)
             t0 = time.perf_counter()
             tok = be.prefill(ids)
             t_first = time.perf_counter()
@@ -390,7 +413,7 @@ def make_handler(server: Server):
 
             if not stream:
                 try:
-                    res = server.generate(ids, n, stop)
+                    res = server.generate(ids, n, stop, sampling=server.sampling_of(req))
                 except Exception as e:   # noqa: BLE001
                     return self._json(500, {'error': {'message': f'{type(e).__name__}: {e}'}})
                 text = text_of(res['ids'])
@@ -435,7 +458,7 @@ def make_handler(server: Server):
             try:
                 if not event(chunk({'role': 'assistant', 'content': ''})):
                     return None
-                res = server.generate(ids, n, stop, emit)
+                res = server.generate(ids, n, stop, emit, sampling=server.sampling_of(req))
                 ok = event(chunk({}, finish_reason(res)))
                 if ok and usage:
                     done = len([t for t in res['ids'] if t not in stop])
@@ -515,7 +538,7 @@ def make_handler(server: Server):
                     return self._json(500, {'error': f'{type(e).__name__}: {e}'})
             if not stream:
                 try:
-                    res = server.generate(ids, n, stop)
+                    res = server.generate(ids, n, stop, sampling=server.sampling_of(req))
                 except Exception as e:   # noqa: BLE001 -- reported to the client, the server stays up
                     return self._json(500, {'error': f'{type(e).__name__}: {e}'})
                 return self._json(200, res)
@@ -537,7 +560,7 @@ def make_handler(server: Server):
             def emit(t):
                 return chunk({'id': t, 'text': tokz.decode([t]) if tokz is not None else None})
             try:
-                res = server.generate(ids, n, stop, emit)
+                res = server.generate(ids, n, stop, emit, sampling=server.sampling_of(req))
                 res['done'] = True
                 if chunk(res):
                     self.wfile.write(b'0\r\n\r\n')
@@ -577,7 +600,7 @@ def build(args):
                             budget_ids=int(args.recall_gib * (1 << 28)))
         eng = recall.RecallEngine(rec, gamma=args.recall_gamma)
         return SpecBackend(model, eng, max_len=args.max_len, tokenizer=tok, mailbox=mailbox)
-    gen = Generator(model, batch=1, max_len=args.max_len)
+    gen = Generator(model, batch=1, max_len=args.max_len, sampling=args.sampling)
     be = GenBackend(model, gen, tok, mailbox)
     be.prefill([0])        # captures the decode graph before the server says it is ready
     return be
@@ -600,6 +623,8 @@ def main(argv=None):
     ap.add_argument('--hot', type=float, default=0.4)
     ap.add_argument('--max-len', type=int, default=8192)
     ap.add_argument('--max-queue', type=int, default=8)
+    ap.add_argument('--sampling', action='store_true',
+                    help='temperature / top-p sampling in the decode step (requests without a temperature stay greedy)')
     ap.add_argument('--recall', default=None,
                     help='serve with Recall copy drafts verified by the target: a record directory, or "memory"')
     ap.add_argument('--recall-gib', type=float, default=1.0 / 16, help='record size budget (GiB of int32 ids)')
