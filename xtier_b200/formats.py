@@ -137,6 +137,23 @@ class ExpertWeights:
         return ExpertWeights(self.fmt, *(getattr(self, f).contiguous()
                                          for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')))
 
+    def tp_slice(self, rank: int, world: int) -> 'ExpertWeights':
+        """This tensor-parallel rank's share of every expert: intermediate units [rank * I / world, (rank + 1) * I /
+        world) -- those gate and up rows, the same columns of the down projection (codes and block scales), the global
+        scales unchanged. SwiGLU acts per intermediate unit and the down projection is linear in them, so the ranks'
+        outputs sum to the whole expert's. I / world must be a multiple of the block size."""
+        I, bs = self.inter, BLOCK[self.fmt]
+        if I % world or (I // world) % bs:
+            raise ValueError(f'tp_slice: {I} intermediate units do not split into {world} shares of whole '
+                             f'{bs}-blocks')
+        n = I // world
+        a, b = rank * n, (rank + 1) * n
+        w13 = torch.cat([self.w13[:, a:b], self.w13[:, I + a:I + b]], 1).contiguous()
+        s13 = torch.cat([self.s13[:, a:b], self.s13[:, I + a:I + b]], 1).contiguous()
+        w2 = self.w2[:, :, a // 2:b // 2].contiguous()
+        s2 = self.s2[:, :, a // bs:b // bs].contiguous()
+        return ExpertWeights(self.fmt, w13, w2, s13, s2, self.g13.clone(), self.g2.clone())
+
     def dequant(self, e: int):
         """(w1 [I,H], w3 [I,H], w2 [H,I]) float32 of expert e."""
         I = self.inter
