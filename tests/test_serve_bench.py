@@ -369,3 +369,55 @@ def test_sampling_parameters(server):
     _, greedy = server(Fake())
     st, r = greedy.request('POST', '/v1/generate', {'prompt_ids': [1], 'temperature': 0.5})
     assert st == 400 and 'greedily' in r['error']
+
+
+def test_prefix_reuse_across_requests(server):
+    """A prompt that starts with the previous request's prompt and reply prefills only the rest; a flush or a
+    different prompt starts from the first token."""
+    import torch
+
+    class FakeGen:
+        sampling, use_graph, max_len = False, False, 4096
+
+        def __init__(self):
+            self.graph, self.starts, self.state = 'captured', [], {}
+            self.buf = {'tokens': torch.zeros(1, dtype=torch.int64)}
+            self.host_tokens = torch.zeros(1, dtype=torch.int64)
+
+        def prefill(self, prompts, start=0):
+            self.starts.append(start)
+            self.buf['tokens'].fill_(int(prompts[0, -1]) + 1)
+
+        def decode_one(self):
+            self.host_tokens += 1
+            return self.host_tokens
+
+        def between_steps(self):
+            pass
+
+        def check(self):
+            pass
+
+    class FakeModel:
+        class cfg:
+            vocab = 1000
+        bigram = None
+
+    gen = FakeGen()
+    _, cl = server(serve.GenBackend(FakeModel(), gen))
+    p = [5, 6, 7, 8]
+    out = cl.generate(p, 4)['ids']
+    assert out == [9, 10, 11, 12] and gen.starts == [0]
+    cl.generate(p + out + [40, 41], 2)            # the cache holds p and the reply's first three tokens
+    assert gen.starts[-1] == len(p) + len(out) - 1
+    cl.generate(p, 2)                             # a prefix of the cache: all but the last id reused
+    assert gen.starts[-1] == len(p) - 1
+    cl.generate([1, 2, 3], 2)
+    assert gen.starts[-1] == 0
+    cl.flush()
+    cl.generate([1, 2, 3], 2)
+    assert gen.starts[-1] == 0
+    assert cl.metrics()['prefix_reused_tokens'] == (len(p) + len(out) - 1) + (len(p) - 1)
+    be = serve.GenBackend(FakeModel(), FakeGen(), prefix_cache=False)
+    be.cached = [1, 2, 3]
+    assert be.reusable([1, 2, 3, 4]) == 0

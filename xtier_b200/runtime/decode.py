@@ -81,30 +81,35 @@ class Generator:
         self.buf['top_p'].copy_(torch.as_tensor(top_p, dtype=torch.float32).expand(self.batch))
 
     # ------------------------------------------------------------------ public API
-    def prefill(self, prompts: torch.Tensor):
-        """prompts [batch, T] token ids (host or device): fills the KV cache, sets the first decode input."""
+    def prefill(self, prompts: torch.Tensor, start: int = 0):
+        """prompts [batch, T] token ids (host or device): fills the KV cache, sets the first decode input. start > 0:
+        the cache already holds the KV of prompts[:, :start] (the same ids at the same positions, e.g. a previous
+        request's prefix); only the rest is computed."""
         prompts = torch.as_tensor(prompts)
         first = []
         T = prompts.shape[1]
+        if not 0 <= start < T:
+            raise ValueError(f'prefill: start {start} outside [0, {T})')
         gov = self.governor
+
         def run(ids, b):
             if not self.sampling:
-                return self.model.prefill(self.state, ids, row=b)
+                return self.model.prefill(self.state, ids, row=b, start=start)
             from .sampling import sample     # the first token is drawn like the decode step's
-            _, lg = self.model.prefill(self.state, ids, row=b, return_logits=True)
+            _, lg = self.model.prefill(self.state, ids, row=b, start=start, return_logits=True)
             return sample(lg[None], self.buf['temp'][b:b + 1], self.buf['top_p'][b:b + 1])
 
         for b in range(self.batch):
-            ids = prompts[b].to(self.model.device)
+            ids = prompts[b, start:].to(self.model.device)
             if gov is None:
                 first.append(run(ids, b))
                 continue
-            gov.before_alloc(T, T)     # extra slots go back until the predicted need fits
+            gov.before_alloc(T - start, T)     # extra slots go back until the predicted need fits
             torch.cuda.synchronize()
             before = torch.cuda.memory_allocated()
             torch.cuda.reset_peak_memory_stats()
             first.append(gov.guarded(run, ids, b))
-            gov.after_forward(T, T, before, torch.cuda.max_memory_allocated())
+            gov.after_forward(T - start, T, before, torch.cuda.max_memory_allocated())
         self.buf['tokens'].copy_(torch.cat(first).view(-1))
         if 'prev' in self.buf:   # the last prompt token precedes the first decode input
             self.buf['prev'].copy_(prompts[:, -1].to(self.buf['prev'].device))

@@ -11,7 +11,9 @@ Endpoints
                              decode step captured
   GET  /metrics              decode counters, mailbox statistics, per-layer hit rates (JSON);
                              /metrics/prometheus: the same in the Prometheus text format
-  POST /flush_cache          {"ok": true}; nothing is cached between requests (every prompt is a cold prefill)
+  POST /flush_cache          {"ok": true}; forgets the cached prefix (the next prompt is a cold prefill). A request whose
+                             prompt starts with ids of the previous request (its prompt and reply) prefills only the
+                             rest (--no-prefix-cache: never)
   POST /v1/generate          {"prompt_ids": [...] | "prompt": "text" (with a tokenizer), "max_new_tokens": n,
                               "stream": false, "stop_ids": [...], "temperature": 0, "top_p": 1 (a server started
                               with --sampling draws tokens; otherwise a temperature is refused)}
@@ -51,38 +53,69 @@ class BadRequest(ValueError):
 class GenBackend:
     """The model and its decode runner behind the server: prefill a prompt, decode one token, score a text."""
 
-    def __init__(self, model, gen, tokenizer=None, mailbox=None):
+    def __init__(self, model, gen, tokenizer=None, mailbox=None, prefix_cache: bool = True):
         self.model, self.gen, self.tokenizer, self.mailbox = model, gen, tokenizer, mailbox
         self.vocab = model.cfg.vocab
         self.max_len = gen.max_len
         self.sampling = gen.sampling
+        # hashed n-gram rows read the previous token of a prefill's first one, which a reused prefix does not keep
+        self.prefix_cache = prefix_cache and getattr(model, 'bigram', None) is None
+        self.cached: list[int] = []      # ids whose KV sits in the cache at positions 0.. (the last request's)
+        self.reused = 0                  # prompt tokens not computed again, over all requests
 
     def set_sampling(self, temperature: float, top_p: float):
-        self.gen.set_sampling(temperature, top_p)
+        if self.sampling:                # a greedy generator has nothing to set (temperatures were refused)
+            self.gen.set_sampling(temperature, top_p)
+
+    def reusable(self, ids: list[int]) -> int:
+        """How many leading ids of a prompt the cache already holds (at least one id is always computed)."""
+        if not self.prefix_cache:
+            return 0
+        n = 0
+        for a, b in zip(self.cached, ids):
+            if a != b:
+                break
+            n += 1
+        return min(n, len(ids) - 1)
 
     def prefill(self, ids: list[int]) -> int:
         import torch
         gen = self.gen
-        gen.prefill(torch.tensor([ids]))
+        start = self.reusable(ids)
+        self.cached = []                 # invalid until this prefill is done
+        gen.prefill(torch.tensor([ids]), start=start)
         if gen.graph is None and gen.use_graph:
             gen.capture()
         gen.host_tokens.copy_(gen.buf['tokens'].cpu())
-        return int(gen.host_tokens[0])
+        self.reused += start
+        self.cached = list(ids)
+        self.last = int(gen.host_tokens[0])
+        return self.last
 
     def decode(self) -> int:
         t = int(self.gen.decode_one()[0])
+        self.cached.append(self.last)    # the step wrote the KV of the token it was fed
+        self.last = t
         self.gen.between_steps()
         return t
 
+    def flush(self):
+        self.cached = []
+
     def logprobs(self, ids: list[int], top: int):
-        return score(self.model, self.gen.state, ids, top)
+        self.cached = []
+        out = score(self.model, self.gen.state, ids, top)
+        self.cached = list(ids)          # the scoring forward left the KV of exactly these ids
+        return out
 
     def check(self):
         self.gen.check()
 
     def snapshot(self, state) -> dict:
         from .utils.metrics import snapshot
-        return snapshot(self.model, self.mailbox, state)
+        snap = snapshot(self.model, self.mailbox, state)
+        snap['prefix_reused_tokens'] = self.reused
+        return snap
 
 
 def score(model, state, ids: list[int], top: int):
@@ -511,6 +544,10 @@ def make_handler(server: Server):
         def do_POST(self):
             if self.path == '/flush_cache':
                 self.rfile.read(int(self.headers.get('Content-Length', '0') or 0))
+                be = server.backend
+                if be is not None and hasattr(be, 'flush'):
+                    with server.lock:
+                        be.flush()
                 return self._json(200, {'ok': True})
             if self.path == '/v1/chat/completions':
                 return self._chat()
@@ -601,7 +638,7 @@ def build(args):
         eng = recall.RecallEngine(rec, gamma=args.recall_gamma)
         return SpecBackend(model, eng, max_len=args.max_len, tokenizer=tok, mailbox=mailbox)
     gen = Generator(model, batch=1, max_len=args.max_len, sampling=args.sampling)
-    be = GenBackend(model, gen, tok, mailbox)
+    be = GenBackend(model, gen, tok, mailbox, prefix_cache=not args.no_prefix_cache)
     be.prefill([0])        # captures the decode graph before the server says it is ready
     return be
 
@@ -623,6 +660,7 @@ def main(argv=None):
     ap.add_argument('--hot', type=float, default=0.4)
     ap.add_argument('--max-len', type=int, default=8192)
     ap.add_argument('--max-queue', type=int, default=8)
+    ap.add_argument('--no-prefix-cache', action='store_true', help='prefill every prompt from its first token')
     ap.add_argument('--sampling', action='store_true',
                     help='temperature / top-p sampling in the decode step (requests without a temperature stay greedy)')
     ap.add_argument('--recall', default=None,
