@@ -216,7 +216,8 @@ class Server:
                 raise BadRequest('this server has no tokenizer: send prompt_ids')
             if not isinstance(req['prompt'], str):
                 raise BadRequest('prompt must be a string')
-            ids = tok.encode(req['prompt'], add_special_tokens=False)
+            from .utils.tokenize import parallel_encode
+            ids = parallel_encode(tok, req['prompt'])
         else:
             raise BadRequest('prompt_ids (or prompt) is required')
         if not ids:
@@ -274,12 +275,15 @@ class Server:
             raise BadRequest('max_tokens must be a positive integer')
         tools = req.get('tools')
         kw = dict(req.get('chat_template_kwargs') or {})
-        try:
-            ids = tok.apply_chat_template(msgs, tools=tools, add_generation_prompt=True, tokenize=True, **kw)
+        try:   # rendered to text, then encoded (in parallel slices when long)
+            ids = tok.apply_chat_template(msgs, tools=tools, add_generation_prompt=True, tokenize=False, **kw)
         except TypeError:
-            ids = tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True)
+            ids = tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=False)
         except Exception as e:   # noqa: BLE001 -- a template that refuses the messages
             raise BadRequest(f'chat template: {type(e).__name__}: {e}')
+        if isinstance(ids, str):
+            from .utils.tokenize import parallel_encode
+            ids = parallel_encode(tok, ids)
         ids = list(ids['input_ids'] if isinstance(ids, dict) else ids)
         n = min(n, self.backend.max_len - len(ids) - 8)
         if n < 1:
