@@ -11,6 +11,11 @@ MODEL = {
         {'key': 'adapt', 'label': 'adaptive hot slots', 'default': 'on', 'choices': [['on', 'on'], ['off', 'off']]},
         {'key': 'trace', 'label': 'route trace', 'default': 'off',
          'choices': [['off', 'off'], ['on', 'write /tmp/xtier-route-trace.bin (planner input)']]},
+        {'key': 'decode', 'label': 'token choice', 'default': 'greedy',
+         'choices': [['greedy', 'greedy (temperatures refused)'], ['sampling', 'temperature / top-p per request'],
+                     ['recall', 'greedy + Recall copy drafts (speculative, in-memory record)']]},
+        {'key': 'prefix', 'label': 'prefix reuse', 'default': 'on',
+         'choices': [['on', 'a prompt extending the previous request reuses its KV'], ['off', 'every prompt cold']]},
     ],
 }
 
@@ -18,6 +23,12 @@ MODEL = {
 def build(options, port):
     """(argv, env) of the server process for the chosen options."""
     argv = ['python', '-m', 'xtier_b200.serve', '--model', 'qwen3-moe', '--hot', options['hot'], '--port', str(port)]
+    if options['decode'] == 'sampling':
+        argv.append('--sampling')
+    elif options['decode'] == 'recall':
+        argv += ['--recall', 'memory']
+    if options['prefix'] == 'off':
+        argv.append('--no-prefix-cache')
     env = {'XTIER_THREADS': options['threads'], 'XTIER_CACHE_ADAPT': '1' if options['adapt'] == 'on' else '0'}
     if options['trace'] == 'on':
         env['XTIER_ROUTE_TRACE'] = '/tmp/xtier-route-trace.bin'
