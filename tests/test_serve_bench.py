@@ -421,3 +421,71 @@ def test_prefix_reuse_across_requests(server):
     be = serve.GenBackend(FakeModel(), FakeGen(), prefix_cache=False)
     be.cached = [1, 2, 3]
     assert be.reusable([1, 2, 3, 4]) == 0
+
+
+def test_continuous_batching(server):
+    """Concurrent requests share decode steps (at most `rows` at once); each gets exactly its own sequence; an
+    aborted stream frees its row."""
+    import threading
+    import time as _t
+
+    class FakeBatch:
+        vocab, max_len, rows, tokenizer, sampling = 1000, 4096, 3, None, False
+
+        def __init__(self):
+            self.last, self.steps, self.max_active = {}, 0, 0
+
+        def prefill_row(self, row, ids):
+            self.last[row] = sum(ids) % 1000
+            return self.last[row]
+
+        def step(self, active):
+            _t.sleep(0.003)
+            self.steps += 1
+            self.max_active = max(self.max_active, len(active))
+            out = [0] * self.rows
+            for r in active:
+                self.last[r] = (31 * self.last[r] + 7) % 1000
+                out[r] = self.last[r]
+            return out
+
+        def check(self):
+            pass
+
+    def expect(ids, n):
+        t = sum(ids) % 1000
+        seq = [t]
+        while len(seq) < n:
+            t = (31 * t + 7) % 1000
+            seq.append(t)
+        return seq
+
+    be = FakeBatch()
+    srv = serve.BatchServer(be, max_queue=16)
+    hs = serve.serve(srv, '127.0.0.1', 0)
+    try:
+        cl = Client(f'http://127.0.0.1:{hs.server_address[1]}', timeout=60)
+        prompts = [[i + 1, 2 * i + 5, 7] for i in range(6)]
+        res = [None] * 6
+
+        def one(i):
+            res[i] = cl.generate(prompts[i], 20 + i)['ids']
+        th = [threading.Thread(target=one, args=(i,)) for i in range(6)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        for i in range(6):
+            assert res[i] == expect(prompts[i], 20 + i), i
+        assert 1 < be.max_active <= 3
+        assert be.steps < sum(20 + i for i in range(6)) - 6          # steps were shared
+        x = cl.stream([9, 9, 9], 200, abort_after=2)
+        assert x['aborted']
+        assert cl.generate([1, 2, 3], 5)['ids'] == expect([1, 2, 3], 5)
+        t_end = _t.time() + 10
+        while cl.metrics()['aborted'] < 1 and _t.time() < t_end:
+            _t.sleep(0.05)
+        assert cl.metrics()['aborted'] == 1
+    finally:
+        hs.shutdown()
+        hs.server_close()

@@ -28,8 +28,9 @@ Endpoints
   POST /v1/logprobs          {"prompt_ids": [...], "top": N} -> {"nll": [-log p(ids[i+1] | ids[:i+1])],
                              "top": [[[id, logprob], ...] per position]} (fixed-text perplexity, A/B of configurations)
 
-Requests run one at a time on the model (batch 1 decode, the CUDA graph of the tiered MoE model); at most --max-queue
-wait, the next ones get 503. Bad requests get 400 with the reason, unknown paths 404, bodies over 64 MiB 413.
+Requests run one at a time on the model (batch 1 decode, the CUDA graph of the tiered MoE model), or with --batch N
+share the decode steps of N rows (continuous batching: a new request is prefilled into a free row between two steps);
+at most --max-queue wait, the next ones get 503. Bad requests get 400 with the reason, unknown paths 404, bodies over 64 MiB 413.
 (Reference parity: the reference serves through SGLang's HTTP server; the endpoints its bench tools use -- streamed
 generation, /flush_cache, prompt logprobs, /metrics -- have these counterparts.)
 """
@@ -382,6 +383,186 @@ class Server:
         return {'nll': nll, 'top': tops, 'prompt_tokens': len(ids)}
 
 
+class BatchBackend:
+    """Continuous batching over a Generator of `gen.batch` decode rows: a request is prefilled into a free row while
+    the others keep their KV; one replay of the captured decode step advances every row. Rows without a request decode
+    a throw-away token at position 0 of their own KV row."""
+
+    def __init__(self, model, gen, tokenizer=None, mailbox=None):
+        import torch
+        self.model, self.gen, self.tokenizer, self.mailbox = model, gen, tokenizer, mailbox
+        self.vocab, self.max_len, self.rows = model.cfg.vocab, gen.max_len, gen.batch
+        self.sampling = False
+        pin = torch.cuda.is_available()
+        self.host_pos = torch.zeros(self.rows, dtype=torch.int32, pin_memory=pin)
+        self.score_state = None
+
+    def capture(self):
+        if self.gen.use_graph and self.gen.graph is None:
+            self.gen.capture()
+
+    def prefill_row(self, row: int, ids: list[int]) -> int:
+        import torch
+        g = self.gen
+        t = int(self.model.prefill(g.state, torch.tensor(ids, device=self.model.device), row=row)[0])
+        g.host_tokens[row] = t
+        if 'prev' in g.buf:
+            g.buf['prev'][row] = ids[-1]
+        self.host_pos[row] = len(ids)
+        return t
+
+    def step(self, active: list[int]) -> list[int]:
+        """One decode step of every row; the next token of each row (rows not in `active` are parked at 0)."""
+        g = self.gen
+        for r in range(self.rows):
+            if r not in active:
+                self.host_pos[r] = 0
+        g.buf['pos'].copy_(self.host_pos, non_blocking=True)
+        nxt = g.decode_one().tolist()
+        for r in active:
+            self.host_pos[r] += 1
+        g.between_steps()
+        return nxt
+
+    def logprobs(self, ids: list[int], top: int):
+        if self.score_state is None:
+            self.score_state = self.model.alloc_state(1, self.max_len)
+        return score(self.model, self.score_state, ids, top)
+
+    def check(self):
+        self.gen.check()
+
+    def snapshot(self, state) -> dict:
+        from .utils.metrics import snapshot
+        return snapshot(self.model, self.mailbox, state)
+
+
+class _Req:
+    def __init__(self, ids, n, stop):
+        import queue
+        self.ids, self.n, self.stop = ids, n, stop
+        self.q = queue.Queue()
+        self.count, self.last, self.aborted, self.error, self.done = 0, None, False, None, False
+
+
+class BatchServer(Server):
+    """Server whose requests share the decode steps of a BatchBackend: a scheduler thread admits waiting requests
+    into free rows (their prefill runs between two decode steps) and hands every step's tokens to the requests."""
+
+    def __init__(self, backend=None, max_queue: int = 8):
+        import collections
+        super().__init__(backend, max_queue)
+        self.cond = threading.Condition()
+        self.pending = collections.deque()
+        self.rows: dict = {}
+        self.gpu = threading.Lock()
+        self.thread = None
+        if backend is not None:
+            self._start()
+
+    def set_backend(self, backend):
+        super().set_backend(backend)
+        self._start()
+
+    def _start(self):
+        if self.thread is None:
+            self.thread = threading.Thread(target=self._loop, daemon=True, name='xtier-batch')
+            self.thread.start()
+
+    def _finish(self, row):
+        req = self.rows.pop(row)
+        req.done = True
+        req.q.put(None)
+
+    def _give(self, row, t):
+        req = self.rows[row]
+        req.count += 1
+        req.last = t
+        req.q.put(t)
+        if req.count >= req.n or t in req.stop:
+            self._finish(row)
+
+    def _loop(self):
+        be = self.backend
+        while True:
+            with self.cond:
+                while not self.pending and not self.rows:
+                    self.cond.wait()
+                admit = []
+                while self.pending and len(self.rows) < be.rows:
+                    req = self.pending.popleft()
+                    row = next(r for r in range(be.rows) if r not in self.rows)
+                    self.rows[row] = req
+                    admit.append((row, req))
+            for row, req in admit:
+                self._started()
+                try:
+                    with self.gpu:
+                        t = be.prefill_row(row, req.ids)
+                except Exception as e:   # noqa: BLE001 -- the request fails, the server goes on
+                    req.error = e
+                    self._finish(row)
+                    continue
+                self._give(row, t)
+            for row in [r for r, q in self.rows.items() if q.aborted]:
+                self._finish(row)
+            active = sorted(self.rows)
+            if not active:
+                continue
+            try:
+                with self.gpu:
+                    toks = be.step(active)
+                    be.check()
+            except Exception as e:   # noqa: BLE001 -- every running request fails with the step
+                for row in active:
+                    self.rows[row].error = e
+                    self._finish(row)
+                continue
+            for row in active:
+                self._give(row, toks[row])
+
+    def generate(self, ids, n, stop, emit=None, sampling=(0.0, 1.0)) -> dict:
+        req = _Req(ids, n, stop)
+        t0 = time.perf_counter()
+        with self.cond:
+            self.pending.append(req)
+            self.cond.notify()
+        out, times = [], []
+        while True:
+            t = req.q.get()
+            if t is None:
+                break
+            out.append(t)
+            times.append(time.perf_counter())
+            if emit is not None and emit(t) is False:
+                req.aborted = True
+                break
+        if req.error is not None:
+            raise req.error
+        with self.qlock:
+            self.state['requests'] += 1
+            self.state['tokens'] += len(out)
+            self.state['prompt_tokens'] += len(ids)
+            self.state['aborted'] += int(req.aborted)
+        dec = times[-1] - times[0] if len(times) > 1 else 0.0
+        res = {'ids': out, 'prompt_tokens': len(ids), 'completion_tokens': len(out),
+               'ttft_s': (times[0] - t0) if times else None, 'decode_s': dec,
+               'decode_tok_s': (len(out) - 1) / dec if dec > 0 else None, 'aborted': req.aborted}
+        tokz = getattr(self.backend, 'tokenizer', None)
+        if tokz is not None:
+            res['text'] = tokz.decode(out)
+        return res
+
+    def logprobs(self, ids, top) -> dict:
+        self._started()
+        with self.gpu:
+            nll, tops = self.backend.logprobs(ids, top)
+        with self.qlock:
+            self.state['requests'] += 1
+            self.state['prompt_tokens'] += len(ids)
+        return {'nll': nll, 'top': tops, 'prompt_tokens': len(ids)}
+
+
 _TOOL_CALL = re.compile(r'<tool_call>\s*(\{.*?\})\s*</tool_call>', re.S)
 
 
@@ -641,6 +822,10 @@ def build(args):
                             budget_ids=int(args.recall_gib * (1 << 28)))
         eng = recall.RecallEngine(rec, gamma=args.recall_gamma)
         return SpecBackend(model, eng, max_len=args.max_len, tokenizer=tok, mailbox=mailbox)
+    if args.batch > 1:
+        be = BatchBackend(model, Generator(model, batch=args.batch, max_len=args.max_len), tok, mailbox)
+        be.capture()
+        return be
     gen = Generator(model, batch=1, max_len=args.max_len, sampling=args.sampling)
     be = GenBackend(model, gen, tok, mailbox, prefix_cache=not args.no_prefix_cache)
     be.prefill([0])        # captures the decode graph before the server says it is ready
@@ -665,6 +850,8 @@ def main(argv=None):
     ap.add_argument('--max-len', type=int, default=8192)
     ap.add_argument('--max-queue', type=int, default=8)
     ap.add_argument('--no-prefix-cache', action='store_true', help='prefill every prompt from its first token')
+    ap.add_argument('--batch', type=int, default=1,
+                    help='decode rows shared by concurrent requests (continuous batching; greedy, no prefix reuse)')
     ap.add_argument('--sampling', action='store_true',
                     help='temperature / top-p sampling in the decode step (requests without a temperature stay greedy)')
     ap.add_argument('--recall', default=None,
@@ -675,7 +862,7 @@ def main(argv=None):
     ap.add_argument('--host', default='127.0.0.1')
     ap.add_argument('--port', type=int, default=18180)
     args = ap.parse_args(argv)
-    server = Server(None, args.max_queue)
+    server = (BatchServer if args.batch > 1 else Server)(None, args.max_queue)
     serve(server, args.host, args.port)
     print(f'[xtier_b200] loading {args.checkpoint or args.model} ...', flush=True)
     server.set_backend(build(args))
