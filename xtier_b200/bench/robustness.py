@@ -11,7 +11,8 @@ answered in full. After every group a small request must still be answered. One 
 when any case failed.
 interleave: request A streams a long answer; --delay seconds in, request B sends a cold prompt of --tokens ids.
 Reported: B's time to its first token, A's longest wait between two tokens while B is read, A's token rate before,
-during and after. This server runs one request at a time, so B waits for A (and A is never paused by B).
+during and after. A server started with --batch 1 runs one request at a time, so B waits for A (and A is never paused
+by B); with --batch N > 1, B's prefill runs between two of A's decode steps, and A's longest wait is its cost.
 (Reference parity: bench/abuse_test.py and bench/interleave_probe.py.)
 """
 from __future__ import annotations
