@@ -35,3 +35,22 @@ def test_prefill_rows_from_the_table(tmp_path):
     t.add_prefill(x, tokens)
     assert torch.equal(x, bf[torch.from_numpy(ids)])
     store.close()
+
+
+def test_chunk_look_ahead_rows_match_direct_lookup(tmp_path):
+    """prefetch_rows (a chunked prefill's read-ahead of the next chunk) gives the rows add_prefill would read."""
+    from xtier_b200.tables.engram import BigramTable
+    rows, dim = 4096, 64
+    bf = (torch.arange(rows * dim, dtype=torch.float32).reshape(rows, dim) % 251 / 251.0).bfloat16()
+    segs = write_table(tmp_path / 'bigram', bf.view(torch.uint8).numpy().reshape(rows, dim * 2), None, segments=2)
+    store = RowStore(segs, dim * 2, 0, io_threads=2, cache_rows=64)
+    bt = BigramTable.__new__(BigramTable)
+    bt.store, bt.rows, bt.dim, bt.hidden, bt.seed, bt.proj = store, rows, dim, dim, 0, None
+    toks = torch.randint(0, 1000, (300,), generator=torch.Generator().manual_seed(1))
+    fut = bt.prefetch_rows(toks[100:], int(toks[99]))
+    direct = bt.rows_host(toks[99:-1], toks[100:])
+    assert torch.equal(fut.result(), direct)
+    x = torch.zeros(200, dim, dtype=torch.bfloat16)
+    bt.add_prefill(x, toks[100:], prev0=int(toks[99]), rows=fut.result())
+    assert torch.equal(x, direct)
+    store.close()

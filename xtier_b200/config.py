@@ -84,6 +84,7 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_GPU_PREFILL_MIN', 'int', 1024, 'prefill calls of at least this many tokens run every expert on the GPU'),
     _S('XTIER_HYBRID_PREFILL_MAX', 'int', 2560, 'partly cached prefill below this: GPU hot routes || CPU the rest'),
     _S('XTIER_PREFILL_CHUNK', 'int', 8, 'experts uploaded per chunk of the host-resident GPU prefill'),
+    _S('XTIER_LONG_PREFILL_CHUNK', 'int', 0, 'tokens per chunk of a long prompt\'s prefill (0: one piece)'),
     _S('XTIER_PREFILL_SLOTS', 'int', 4, 'staging slots of the prefill upload ring'),
     _S('XTIER_ROUTE_TRACE', 'str', '', 'binary route trace of the CPU decode calls (planner input)'),
     _S('XTIER_TIMING', 'flag', False, 'log synchronized MoE time per forward'),

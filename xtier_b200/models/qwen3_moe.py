@@ -355,6 +355,29 @@ class Qwen3MoeModel:
         return buf['next']
 
     # ------------------------------------------------------------------ prefill (one sequence)
+    def prefill_chunked(self, st: dict, tokens: torch.Tensor, row: int = 0, start: int = 0, chunk: int = 0,
+                        return_logits: bool = False):
+        """`prefill` of a long prompt in chunks of `chunk` tokens (0: XTIER_LONG_PREFILL_CHUNK, whose default 0 means
+        one piece), each continuing after the KV of the ones before, so activations stay bounded by the chunk;
+        with a hashed n-gram table the next chunk's rows are read from the drive on a thread while this chunk
+        computes. Returns what the last chunk's prefill returns."""
+        chunk = chunk or config.get('XTIER_LONG_PREFILL_CHUNK')
+        T = tokens.shape[0]
+        if chunk <= 0 or T <= chunk:
+            return self.prefill(st, tokens, row=row, start=start, return_logits=return_logits)
+        bounds = list(range(0, T, chunk)) + [T]
+        ahead = None
+        res = None
+        for i, (a, b) in enumerate(zip(bounds, bounds[1:])):
+            if self.bigram is not None:
+                rows = ahead.result() if ahead is not None else None
+                if b < T:      # the next chunk's rows, read while this one computes
+                    ahead = self.bigram.prefetch_rows(tokens[b:bounds[i + 2]], int(tokens[b - 1]))
+                st.setdefault('bigram_rows', {})[row] = rows
+            res = self.prefill(st, tokens[a:b], row=row, start=start + a,
+                               return_logits=return_logits and b == T)
+        return res
+
     def prefill(self, st: dict, tokens: torch.Tensor, row: int = 0, start: int = 0, return_logits: bool = False,
                 all_logits: bool = False, active: torch.Tensor | None = None):
         """Runs `tokens` [T] of sequence `row` from position `start`; fills the KV cache; returns the next token
@@ -369,7 +392,8 @@ class Qwen3MoeModel:
         residual = self.embed.index_select(0, tokens.to(dev)).contiguous()
         if self.bigram is not None:
             last = st.setdefault('last_token', {})
-            self.bigram.add_prefill(residual, tokens, prev0=last.get(row, 0) if start > 0 else 0)
+            rows = st.get('bigram_rows', {}).pop(row, None)     # read ahead by prefill_chunked
+            self.bigram.add_prefill(residual, tokens, prev0=last.get(row, 0) if start > 0 else 0, rows=rows)
             last[row] = int(tokens[-1])
         h = torch.empty_like(residual)
         moe_out = torch.empty_like(residual)

@@ -92,11 +92,16 @@ class Generator:
             raise ValueError(f'prefill: start {start} outside [0, {T})')
         gov = self.governor
 
+        from .. import config
+        chunked = getattr(self.model, 'prefill_chunked', None) if config.get('XTIER_LONG_PREFILL_CHUNK') > 0 else None
+        prefill = chunked or self.model.prefill
+        kw = {'start': start} if start else {}
+
         def run(ids, b):
             if not self.sampling:
-                return self.model.prefill(self.state, ids, row=b, start=start)
+                return prefill(self.state, ids, row=b, **kw)
             from .sampling import sample     # the first token is drawn like the decode step's
-            _, lg = self.model.prefill(self.state, ids, row=b, start=start, return_logits=True)
+            _, lg = prefill(self.state, ids, row=b, return_logits=True, **kw)
             return sample(lg[None], self.buf['temp'][b:b + 1], self.buf['top_p'][b:b + 1])
 
         for b in range(self.batch):

@@ -86,12 +86,24 @@ class BigramTable:
         raw = self.store.lookup(ids.numpy())
         return torch.from_numpy(np.ascontiguousarray(raw)).view(torch.bfloat16).view(-1, self.dim)
 
-    def add_prefill(self, x: torch.Tensor, tokens: torch.Tensor, prev0: int = 0):
-        """x [T, hidden] += rows of the prompt's pairs (the first token's previous one is prev0)."""
+    def prefetch_rows(self, tokens: torch.Tensor, prev0: int):
+        """Starts reading the rows of a later prompt chunk on a thread (the look-ahead of a chunked prefill); returns a
+        future whose result `add_prefill(..., rows=)` takes."""
+        import concurrent.futures as cf
+        if not hasattr(self, '_ahead'):
+            self._ahead = cf.ThreadPoolExecutor(1, thread_name_prefix='xtier-engram-ahead')
         t = tokens.detach().cpu().long()
         prev = torch.cat([torch.tensor([prev0]), t[:-1]])
-        r = self.rows_host(prev, t).to(x.device)
-        x.add_(self._project(r))
+        return self._ahead.submit(self.rows_host, prev, t)
+
+    def add_prefill(self, x: torch.Tensor, tokens: torch.Tensor, prev0: int = 0, rows: torch.Tensor | None = None):
+        """x [T, hidden] += rows of the prompt's pairs (the first token's previous one is prev0); `rows`: the BF16
+        rows already read (prefetch_rows)."""
+        if rows is None:
+            t = tokens.detach().cpu().long()
+            prev = torch.cat([torch.tensor([prev0]), t[:-1]])
+            rows = self.rows_host(prev, t)
+        x.add_(self._project(rows.to(x.device)))
 
     def check(self):
         self.lookup.check()
