@@ -84,3 +84,26 @@ def test_layer_slots_from_env(monkeypatch, tmp_path):
     monkeypatch.setenv('XTIER_CACHE_FULL', '4')
     assert planner.layer_slots(4, 64) == 64
     planner._plan_cache.clear()
+
+
+def test_model_takes_per_layer_slots_and_the_route_profile(tmp_path, monkeypatch):
+    """A slot plan gives each layer its own hot count; a route profile picks which experts are hot."""
+    import json
+    from xtier_b200.models.qwen3_moe import Qwen3MoeConfig, Qwen3MoeModel
+    plan = tmp_path / 'plan.json'
+    plan.write_text(json.dumps({'slots': {'0': 3, '1': 8}}))
+    prof = tmp_path / 'profile.json'
+    p0 = [0.01, 0.3, 0.02, 0.25, 0.05, 0.2, 0.1, 0.07]
+    prof.write_text(json.dumps({'tokens': {'0': 100}, 'layers': {'0': p0}}))
+    monkeypatch.setenv('XTIER_CACHE_PLAN', str(plan))
+    monkeypatch.setenv('XTIER_CACHE_PROFILE', str(prof))
+    monkeypatch.setenv('XTIER_GPU2_SLOTS', 'off')
+    from xtier_b200 import planner
+    planner._plan_cache.clear()
+    cfg = Qwen3MoeConfig.tiny(layers=2, experts=8)
+    model = Qwen3MoeModel(cfg, device='cpu', seed=0, hot_fraction=0.5, engine_threads=2, synthetic_experts=False)
+    l0, l1 = model.layers[0]['moe'], model.layers[1]['moe']
+    assert l0.hot == [1, 3, 5] and l1.all_hot                 # the profile's three most routed experts
+    assert len(model.engines) == 1
+    for e in model.engines:
+        e.close()

@@ -374,10 +374,11 @@ class TieredMoE:
             idx[cold] = torch.arange(len(cold), dtype=torch.int32)
             self._cold_index = idx.to(self.device)
             hc = self.host.select(torch.tensor(cold))
-            self._host_cold = ExpertWeights(self.fmt, *[getattr(hc, f).contiguous().pin_memory()
+            pin = (lambda t: t.pin_memory()) if torch.cuda.is_available() else (lambda t: t)   # pinned for fast H2D
+            self._host_cold = ExpertWeights(self.fmt, *[pin(getattr(hc, f).contiguous())
                                                         for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
-            self._host_cold.g13 = self._host_cold.g13.float().pin_memory()
-            self._host_cold.g2 = self._host_cold.g2.float().pin_memory()
+            self._host_cold.g13 = pin(self._host_cold.g13.float())
+            self._host_cold.g2 = pin(self._host_cold.g2.float())
         hc = self._host_cold
         stage = self._gpu_stage(hc)
         if copy:

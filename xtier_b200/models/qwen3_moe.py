@@ -126,22 +126,30 @@ class Qwen3MoeModel:
             self.lm_head = randn(cfg.vocab, H)
             self.final_norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
         self.layers = []
-        n_hot = cfg.experts if hot_fraction >= 1.0 else max(1, int(round(hot_fraction * cfg.experts)))
+        from .. import planner
+        if planner.configured():   # per-layer slots from the planner's switches (plan file, fraction, slots, ...)
+            hot_counts = [planner.layer_slots(li, cfg.experts, cfg.layers) for li in range(cfg.layers)]
+        else:
+            n = cfg.experts if hot_fraction >= 1.0 else max(1, int(round(hot_fraction * cfg.experts)))
+            hot_counts = [n] * cfg.layers
+        partial = any(h < cfg.experts for h in hot_counts)
+        if popularity is None and config.get('XTIER_CACHE_PROFILE'):   # a measured route profile fills the slots
+            popularity = planner.profile_popularity(config.get('XTIER_CACHE_PROFILE'), cfg.layers, cfg.experts)
         self.mailbox = mailbox
         self.engines = []
         self.cold = None
         self.peers = None
         self.bigram = None   # tables.engram.BigramTable (attach_bigram)
         prank, pworld = 0, 1
-        if peer and n_hot < cfg.experts:
+        if peer and partial:
             from ..parallel import dist as xdist
             env = xdist.init()
             prank, pworld = env.rank, env.world
             if pworld > 1:
                 from ..cache.peer import PeerPools
                 bs = 16 if cfg.fmt == formats.NVFP4 else 32
-                self.peers = PeerPools([(n_hot, H, cfg.inter, bs)] * cfg.layers, dev)
-        if config.get('XTIER_COLD') and n_hot < cfg.experts:
+                self.peers = PeerPools([(h, H, cfg.inter, bs) for h in hot_counts], dev)
+        if config.get('XTIER_COLD') and partial:
             from ..cache.cold import ColdPool
             if not config.get('XTIER_COLD_DIR'):
                 raise ValueError('XTIER_COLD=1 needs XTIER_COLD_DIR (one directory per drive, comma separated)')
@@ -151,6 +159,7 @@ class Qwen3MoeModel:
         self.zipf_tau = (zipf_temperature(cfg.experts, cfg.top_k, cfg.zipf_s, cfg.std * H ** 0.5)
                          if weights is None else 0.0)
         for li in range(cfg.layers):
+            n_hot = hot_counts[li]
             if weights is not None:
                 src = weights.layer(li)
                 L = {k: src[k].to(dev).contiguous() for k in ('in_norm', 'post_norm', 'qkv', 'q_norm', 'k_norm', 'o')}
@@ -234,7 +243,7 @@ class Qwen3MoeModel:
         # the runtime (runtime/decode.py Generator)
         self.policy = None
         self.governor = None
-        if mailbox is not None and n_hot < cfg.experts:
+        if mailbox is not None and partial:
             from ..cache.policy import AdaptivePolicy
             self.policy = AdaptivePolicy([L['moe'] for L in self.layers], mailbox)
             if config.get('XTIER_CACHE_ELASTIC'):

@@ -42,3 +42,25 @@ def layer_slots(layer: int, experts: int, layers: int = 0, bytes_per_expert: int
         return max(1, min(experts, int(round(frac * experts))))
     slots = config.get('XTIER_CACHE_SLOTS')
     return experts if slots < 0 else min(experts, slots)
+
+
+def configured() -> bool:
+    """Whether any of the per-layer slot switches is set (then they, not a model's single hot fraction, decide)."""
+    return bool(config.get('XTIER_CACHE_PLAN') or config.get('XTIER_CACHE_FRACTION') > 0
+                or config.get('XTIER_CACHE_SLOTS') >= 0 or config.get('XTIER_CACHE_FULL')
+                or str(config.get('XTIER_LAYERS')).strip() not in ('', 'all'))
+
+
+def profile_popularity(path, layers: int, experts: int):
+    """[layers, experts] route probabilities of a route profile ({"layers": {layer: [p_e]}}, tools/plan_trace.py);
+    layers it does not cover are zero (id order decides there)."""
+    import torch
+    with open(path) as f:
+        prof = json.load(f)
+    out = torch.zeros(layers, experts)
+    for k, v in prof.get('layers', {}).items():
+        if int(k) < layers:
+            row = torch.tensor(v[:experts], dtype=torch.float32)
+            out[int(k), :row.numel()] = row
+    return out
+
