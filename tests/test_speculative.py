@@ -112,3 +112,16 @@ def test_hot_vocab_verify_matches_target_distribution():
         out = verify_chain(p, q, d, g)
         first[out[0]] += 1
     assert float((first / N - p[0]).abs().max()) < 0.015
+
+
+def test_top_p_nucleus_in_verification_probs():
+    from xtier_b200.runtime.sampling import nucleus_probs
+    from xtier_b200.runtime.speculative import SpeculativeDecoder
+    g = torch.Generator().manual_seed(3)
+    W = torch.randn(16, 16, generator=g) * 2
+    sd = SpeculativeDecoder(_Bigram(W), _Bigram(W), threshold=0.0, temperature=0.9)
+    sd.top_p = 0.7
+    logits = torch.randn(3, 16, generator=g)
+    got = sd._probs(logits)
+    for r in range(3):
+        assert torch.allclose(got[r].double(), nucleus_probs(logits[r], 0.9, 0.7), atol=1e-6)

@@ -104,10 +104,20 @@ class SpeculativeDecoder:
         self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0, copies=0, copied=0, copy_landed=0, plain=0, forwards=0)
 
     def _probs(self, logits: torch.Tensor, temp: float | None = None) -> torch.Tensor:
+        """Target (or draft) distribution per row: one-hot argmax at temperature 0, else softmax(logits / temp)
+        restricted to the top-p nucleus (`self.top_p`, 1: all) and renormalized."""
         temp = self.temp if temp is None else temp
         if temp <= 0:
             return torch.nn.functional.one_hot(torch.argmax(logits, -1), logits.shape[-1]).float()
-        return torch.softmax(logits.float() / temp, dim=-1)
+        p = torch.softmax(logits.float() / temp, dim=-1)
+        top_p = getattr(self, 'top_p', 1.0)
+        if top_p < 1.0:
+            ps, idx = torch.sort(p, dim=-1, descending=True)
+            drop = (torch.cumsum(ps, -1) - ps) >= top_p      # mass ranked above reaches top_p: outside the nucleus
+            drop[..., 0] = False
+            p = p.scatter(-1, idx, ps.masked_fill(drop, 0.0))
+            p = p / p.sum(-1, keepdim=True)
+        return p
 
     def draft_probs(self, logits: torch.Tensor, V: int) -> torch.Tensor:
         """The draft's proposal distribution over the target vocabulary: at the scaled temperature, and scattered

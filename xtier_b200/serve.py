@@ -150,6 +150,10 @@ class SpecBackend:
         self.max_len = max_len
         self.dec = SpeculativeDecoder(model, draft, recall=recall, max_len=max_len, temperature=temperature)
         self.active = False
+        self.sampling = True             # verification is lossless at any temperature / top-p
+
+    def set_sampling(self, temperature: float, top_p: float):
+        self.dec.temp, self.dec.top_p = float(temperature), float(top_p)
 
     def prefill(self, ids: list[int]) -> int:
         import torch
