@@ -178,3 +178,16 @@ def test_config_mapping_and_refusals():
         with pytest.raises(NotImplementedError):
             hf.config_from_hf(bad)
     json.dumps(base)
+
+
+def test_bf16_experts_quantized_to_the_chosen_format(tmp_path):
+    """Unquantized experts follow `fmt` (XTIER_CKPT_FORMAT): MXFP4 here, dequantizing close to the BF16 weights."""
+    m = _hf_model(seed=6)
+    m.save_pretrained(tmp_path)
+    w = hf.HFWeights(tmp_path, fmt=formats.MXFP4)
+    ew = w.layer(1)['experts']
+    assert ew.fmt == formats.MXFP4 and ew.s13.shape[-1] == H // 32
+    src = w.st.get('model.layers.1.mlp.experts.2.gate_proj.weight').float()
+    w1, _, _ = ew.dequant(2)
+    assert float((w1 - src).norm() / src.norm()) < 0.2
+    w.close()
