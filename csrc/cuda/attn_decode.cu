@@ -564,13 +564,8 @@ extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t st
     if (!legacy && (G == 8 || G == 16)) {
 #define XT_AM(GG)                                                                                                  \
         {                                                                                                          \
-            static bool attr = false;                                                                              \
             const int smem = int(AmSmem<GG>::BYTES);                                                               \
-            if (!attr) {                                                                                           \
-                cudaFuncSetAttribute(attn_decode_mma_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
-                                     smem);                                                                        \
-                attr = true;                                                                                       \
-            }                                                                                                      \
+            xt_smem_optin(attn_decode_mma_kernel<GG>, smem);                                                       \
             if (xt_launch(attn_decode_mma_kernel<GG>, grid, dim3(AM_WARPS * 32), smem, stream, p) != cudaSuccess)  \
                 return -1;                                                                                         \
         }
@@ -580,12 +575,8 @@ extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t st
     }
 #define XT_AD(GG)                                                                                                  \
     case GG: {                                                                                                     \
-        static bool attr = false;                                                                                  \
         const int smem = int(AdSmem<GG>::BYTES);                                                                   \
-        if (!attr) {                                                                                               \
-            cudaFuncSetAttribute(attn_decode_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);       \
-            attr = true;                                                                                           \
-        }                                                                                                          \
+        xt_smem_optin(attn_decode_kernel<GG>, smem);                                                               \
         if (xt_launch(attn_decode_kernel<GG>, grid, dim3(AD_WARPS * 32), smem, stream, p) != cudaSuccess)           \
             return -1;                                                                                             \
         break;                                                                                                     \
@@ -621,9 +612,7 @@ extern "C" int xt_attn_decode(const AttnDecodeParams *pp, int B, cudaStream_t st
 #include <mutex>
 #include <string>
 
-#define XT_AD_NOALLOC_FLOATS (512 * 1024)
-#define XT_AD_NOALLOC_COUNTERS 4096
-#define XT_AD_NOALLOC_TOO_BIG (-6)
+#include "../include/xt_attn.h"
 
 static __device__ __align__(256) float xt_ad_noalloc_scratch[XT_AD_NOALLOC_FLOATS];
 static __device__ __align__(256) uint32_t xt_ad_noalloc_counters[XT_AD_NOALLOC_COUNTERS];
@@ -680,6 +669,10 @@ int xt_attn_decode_noalloc(const void *q, const void *k_cache, const void *v_cac
         return -2;
     }
     const int G = Hq / Hkv;
+    if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) {
+        g_noalloc_err = "attn_decode_noalloc: Hq / Hkv must be 1, 2, 4, 8 or 16";
+        return -2;
+    }
     const size_t units = size_t(B) * Hkv * splits * G;
     if (units * (AD_D + 2) > size_t(XT_AD_NOALLOC_FLOATS)) {
         g_noalloc_err = "attn_decode_noalloc: B * Hkv * splits * (Hq / Hkv) * 130 = " +
@@ -693,8 +686,13 @@ int xt_attn_decode_noalloc(const void *q, const void *k_cache, const void *v_cac
         return XT_AD_NOALLOC_TOO_BIG;
     }
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
         g_noalloc_err = "attn_decode_noalloc: no current device";
+        return -2;
+    }
+    if (dev >= kMaxDevices) {
+        g_noalloc_err = "attn_decode_noalloc: device index " + std::to_string(dev) + " exceeds the " +
+                        std::to_string(kMaxDevices) + " devices of the fixed address table";
         return -2;
     }
     const int rc = noalloc_setup(dev);
@@ -728,7 +726,7 @@ int xt_attn_decode_noalloc(const void *q, const void *k_cache, const void *v_cac
         case 4: attn_decode_kernel<4><<<grid, AD_WARPS * 32, AdSmem<4>::BYTES, stream>>>(p); break;
         case 8: attn_decode_kernel<8><<<grid, AD_WARPS * 32, AdSmem<8>::BYTES, stream>>>(p); break;
         case 16: attn_decode_kernel<16><<<grid, AD_WARPS * 32, AdSmem<16>::BYTES, stream>>>(p); break;
-        default: g_noalloc_err = "attn_decode_noalloc: Hq / Hkv must be 1, 2, 4, 8 or 16"; return -2;
+        default: return -2;   // unreachable: G was checked before anything was enqueued
     }
     if (cudaGetLastError() != cudaSuccess) {
         g_noalloc_err = "attn_decode_noalloc: launch failed";

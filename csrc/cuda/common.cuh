@@ -8,6 +8,7 @@
 #define XT_DEV __device__ __forceinline__
 
 #include <stdlib.h>
+#include <mutex>
 #include <utility>
 
 namespace xt {
@@ -42,6 +43,34 @@ inline cudaError_t xt_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Opts a kernel into `bytes` of dynamic shared memory on the current device. The attribute belongs to the device's
+// context, so a process that drives several GPUs must set it once per device: the flag kept here is a bit per device
+// (devices 0-63) per kernel, and a device beyond that sets the attribute on every call.
+inline cudaError_t xt_smem_optin(const void *func, int bytes) {
+    struct Entry { const void *f; int bytes; uint64_t devs; };
+    static Entry table[256];
+    static int used = 0;
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    Entry *hit = nullptr;
+    for (int i = 0; i < used; ++i)
+        if (table[i].f == func && table[i].bytes == bytes) hit = &table[i];
+    if (hit && dev < 64 && (hit->devs >> dev & 1)) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    if (!hit && used < 256) hit = &table[used++], *hit = Entry{func, bytes, 0};
+    if (hit && dev < 64) hit->devs |= uint64_t(1) << dev;
+    return cudaSuccess;
+}
+
+template <typename... KArgs>
+inline cudaError_t xt_smem_optin(void (*kernel)(KArgs...), int bytes) {
+    return xt_smem_optin(reinterpret_cast<const void *>(kernel), bytes);
 }
 
 XT_DEV float warp_sum(float v) {

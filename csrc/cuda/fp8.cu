@@ -179,11 +179,7 @@ extern "C" int xt_gemv_fp8(const void *x, const void *W, const float *S, const v
     auto Y = static_cast<__nv_bfloat16 *>(y);
 #define XT_G8(MM)                                                                                             \
     case MM: {                                                                                               \
-        static bool attr = false;                                                                            \
-        if (!attr) {                                                                                         \
-            cudaFuncSetAttribute(gemv_fp8_kernel<MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
-            attr = true;                                                                                     \
-        }                                                                                                    \
+        xt_smem_optin(gemv_fp8_kernel<MM>, 200 * 1024);                                                      \
         gemv_fp8_kernel<MM><<<grid, G8_WARPS * 32, smem, stream>>>(X, Wp, S, A, Y, N, K);                    \
         break;                                                                                               \
     }

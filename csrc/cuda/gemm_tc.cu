@@ -467,13 +467,7 @@ int launch(const void *A, const void *B, void *Dp, const void *R, int M, int N, 
     CUtensorMap ma, mb;
     if (!make_map(&ma, A, M, K, TC_BM) || !make_map(&mb, B, N, K, BN)) return -3;
     const int smem = TcSmem<BN>::BYTES;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(gemm_tc_kernel<BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
-            return -4;
-        attr = true;
-    }
+    if (xt_smem_optin(gemm_tc_kernel<BN, F32>, smem) != cudaSuccess) return -4;
     const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
     gemm_tc_kernel<BN, F32><<<grid, TC_THREADS, smem, stream>>>(ma, mb, static_cast<__nv_bfloat16 *>(Dp),
@@ -487,13 +481,7 @@ int launch_pair(const void *A, const void *B, void *Dp, const void *R, int M, in
     CUtensorMap ma, mb;
     if (!make_map(&ma, A, M, K, TC_BM) || !make_map(&mb, B, N, K, BN / 2)) return -3;
     const int smem = Tc2Smem<BN>::BYTES;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(gemm_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
-            return -4;
-        attr = true;
-    }
+    if (xt_smem_optin(gemm_tc2_kernel<BN>, smem) != cudaSuccess) return -4;
     const int tiles = ((M + 2 * TC_BM - 1) / (2 * TC_BM)) * ((N + BN - 1) / BN);
     int pairs = num_sms() / 2;
     if (tiles < pairs) pairs = tiles;

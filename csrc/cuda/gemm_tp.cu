@@ -393,13 +393,7 @@ template <int BN, int MODE>
 int tp_launch(const CUtensorMap &ma0, const CUtensorMap &ma1, const CUtensorMap &mb, const CUtensorMap &ml,
               const TpParams &p, cudaStream_t stream) {
     const int smem = TpSmem<BN>::BYTES;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(gemm_tp_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
-            return -4;
-        attr = true;
-    }
+    if (xt_smem_optin(gemm_tp_kernel<BN, MODE>, smem) != cudaSuccess) return -4;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -110,11 +110,7 @@ extern "C" int xt_gemv_bf16(const void *x, const void *W, const void *add, void 
     auto Y = static_cast<__nv_bfloat16 *>(y);
 #define XT_GV(MM)                                                                                             \
     case MM: {                                                                                               \
-        static bool attr = false;                                                                            \
-        if (!attr) {                                                                                         \
-            cudaFuncSetAttribute(gemv_bf16_kernel<MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
-            attr = true;                                                                                     \
-        }                                                                                                    \
+        xt_smem_optin(gemv_bf16_kernel<MM>, 200 * 1024);                                                     \
         if (xt_launch(gemv_bf16_kernel<MM>, grid, dim3(GV_WARPS * 32), smem, stream, X, Wp, A, Y, N, K) !=     \
             cudaSuccess)                                                                                     \
             return -1;                                                                                       \

@@ -459,13 +459,7 @@ int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void
         !mla_map(&mk, Kg, uint64_t(Q) * nsel, MLA_D, MLA_NB) ||
         !mla_map(&mv, Vt, uint64_t(Q) * MLA_L, uint64_t(nsel), 256))
         return -3;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(mla_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MlaSmem::BYTES) !=
-            cudaSuccess)
-            return -4;
-        attr = true;
-    }
+    if (xt_smem_optin(mla_attend_kernel, int(MlaSmem::BYTES)) != cudaSuccess) return -4;
     const int nblk = nsel / MLA_NB;
     dim3 ga(nblk, Q);
     mla_attend_kernel<<<ga, MLA_THREADS, MlaSmem::BYTES, stream>>>(mq, mk, mv, idx, nsel,

@@ -1030,16 +1030,13 @@ extern "C" int xt_ep_moe(const EpParams *pp, int phase, cudaStream_t stream) {
         ep_combine_kernel<<<p.T, 256, 0, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
-    static bool attr = false;
-    if (!attr) {
+    {
         const void *fns[4] = {reinterpret_cast<const void *>(ep_gate_up_stream<4>),
                               reinterpret_cast<const void *>(ep_gate_up_stream<8>),
                               reinterpret_cast<const void *>(ep_down_stream<4>),
                               reinterpret_cast<const void *>(ep_down_stream<8>)};
         for (const void *f : fns)
-            if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, fs::SMEM_BYTES) != cudaSuccess)
-                return -5;
-        attr = true;
+            if (xt_smem_optin(f, int(fs::SMEM_BYTES)) != cudaSuccess) return -5;
     }
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

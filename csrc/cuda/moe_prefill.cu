@@ -391,13 +391,10 @@ int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int
     p.y = y;
     p.out_cols = out_cols;
     p.error = error;
-    static bool attr[2] = {false, false};
-    if (!attr[gate_up ? 1 : 0]) {
+    {
         const void *f = gate_up ? reinterpret_cast<const void *>(moe_grouped_kernel<true>)
                                 : reinterpret_cast<const void *>(moe_grouped_kernel<false>);
-        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, GpSmem::BYTES) != cudaSuccess)
-            return -4;
-        attr[gate_up ? 1 : 0] = true;
+        if (xt_smem_optin(f, int(GpSmem::BYTES)) != cudaSuccess) return -4;
     }
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

@@ -379,10 +379,10 @@ class Qwen3MoeModel:
         res = None
         for i, (a, b) in enumerate(zip(bounds, bounds[1:])):
             if self.bigram is not None:
-                rows = ahead.result() if ahead is not None else None
+                ahead_rows = ahead.result() if ahead is not None else None
                 if b < T:      # the next chunk's rows, read while this one computes
                     ahead = self.bigram.prefetch_rows(tokens[b:bounds[i + 2]], int(tokens[b - 1]))
-                st.setdefault('bigram_rows', {})[row] = rows
+                st.setdefault('bigram_rows', {})[row] = ahead_rows
             res = self.prefill(st, tokens[a:b], row=row, start=start + a,
                                return_logits=return_logits and b == T)
         return res
@@ -401,8 +401,8 @@ class Qwen3MoeModel:
         residual = self.embed.index_select(0, tokens.to(dev)).contiguous()
         if self.bigram is not None:
             last = st.setdefault('last_token', {})
-            rows = st.get('bigram_rows', {}).pop(row, None)     # read ahead by prefill_chunked
-            self.bigram.add_prefill(residual, tokens, prev0=last.get(row, 0) if start > 0 else 0, rows=rows)
+            ahead_rows = st.get('bigram_rows', {}).pop(row, None)     # read ahead by prefill_chunked
+            self.bigram.add_prefill(residual, tokens, prev0=last.get(row, 0) if start > 0 else 0, rows=ahead_rows)
             last[row] = int(tokens[-1])
         h = torch.empty_like(residual)
         moe_out = torch.empty_like(residual)
