@@ -370,13 +370,17 @@ void ep_moe(const Tensor &x, const Tensor &ids, const Tensor &w, const Tensor &p
             const Tensor &mid, const Tensor &w13, const Tensor &s13, const Tensor &g13, const Tensor &w2,
             const Tensor &s2, const Tensor &g2, const std::optional<Tensor> &add, const Tensor &out, const Tensor &err,
             int64_t W, int64_t rank, int64_t E, int64_t fmt, int64_t R, std::vector<int64_t> offsets, double timeout_s,
-            int64_t phases) {
+            int64_t phases, const std::optional<Tensor> &slots, int64_t spr, int64_t mailbox) {
     cuda_contig(x, "x");
     xt::EpParams p{};
     p.W = int(W);
     p.rank = int(rank);
     p.E = int(E);
-    p.El = int(E / W);
+    p.El = slots.has_value() && slots->defined() ? int(spr) : int(E / W);
+    p.slots = optr<const int32_t>(slots);
+    if (p.slots) check(spr > 0 && slots->scalar_type() == at::kInt && slots->is_contiguous(), "ep slots");
+    p.mb = mailbox_view(mailbox);
+    p.use_mb = mailbox ? 1 : 0;
     p.H = int(x.size(1));
     p.I = int(w13.size(1) / 2);
     p.k = int(ids.size(1));
@@ -583,8 +587,72 @@ extern "C" int xt_launch_host_fn(void *stream, void (*fn)(void *), void *arg) {
     return cudaLaunchHostFunc(static_cast<cudaStream_t>(stream), fn, arg) == cudaSuccess ? 0 : -1;
 }
 
+void mla_prep(const Tensor &in, int64_t q_lora, const Tensor &q_norm, const Tensor &kv_norm, const Tensor &pos,
+              const Tensor &slot, double eps, double theta, const Tensor &q_out, const Tensor &codes,
+              const Tensor &scales, const Tensor &rope, const std::optional<Tensor> &lat_out) {
+    check(in.is_cuda() && in.dim() == 2 && in.stride(1) == 1 && in.scalar_type() == at::kBFloat16, "mla_prep input");
+    check(pos.scalar_type() == at::kInt && slot.scalar_type() == at::kLong, "mla_prep: pos int32, slot int64");
+    cuda_contig(q_out, "q_out");
+    cuda_contig(codes, "codes");
+    cuda_contig(scales, "scales");
+    cuda_contig(rope, "rope");
+    const int T = int(in.size(0));
+    check(pos.numel() >= T && slot.numel() >= T && q_out.numel() >= int64_t(T) * q_lora, "mla_prep sizes");
+    c10::cuda::CUDAGuard g(in.device());
+    check_rc(xt_mla_prep(in.data_ptr(), int(in.stride(0)), int(q_lora), q_norm.data_ptr(), kv_norm.data_ptr(),
+                         ptr<const int32_t>(pos), ptr<const int64_t>(slot), float(eps), float(theta), q_out.data_ptr(),
+                         codes.data_ptr(), scales.data_ptr(), rope.data_ptr(), optr<void>(lat_out), T, stream()),
+             "mla_prep");
+}
+
+void head_gemm(const Tensor &x, const Tensor &w, const Tensor &y, const std::optional<Tensor> &pos, int64_t rope_x,
+               int64_t rope_y, int64_t rope_dims, double theta) {
+    // x [T, heads, >= K] (last stride 1), w [heads, K, N], y [T, heads, >= N]
+    check(x.is_cuda() && x.dim() == 3 && x.stride(2) == 1 && y.dim() == 3 && y.stride(2) == 1, "head_gemm layouts");
+    cuda_contig(w, "w");
+    check(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
+          "head_gemm wants bf16");
+    xt::HeadGemmParams p{};
+    p.x = ptr<const __nv_bfloat16>(x);
+    p.w = ptr<const __nv_bfloat16>(w);
+    p.y = ptr<__nv_bfloat16>(y);
+    p.xs_t = x.stride(0);
+    p.xs_h = x.stride(1);
+    p.ys_t = y.stride(0);
+    p.ys_h = y.stride(1);
+    p.T = int(x.size(0));
+    p.K = int(w.size(1));
+    p.N = int(w.size(2));
+    check(x.size(1) == w.size(0) && y.size(1) == w.size(0), "head_gemm heads");
+    p.pos = optr<const int32_t>(pos);
+    p.rope_x = int(rope_x);
+    p.rope_y = int(rope_y);
+    p.rope_dims = int(rope_dims);
+    p.theta = float(theta);
+    if (p.rope_dims) check(p.pos && pos->scalar_type() == at::kInt, "head_gemm: int32 positions for the rotary part");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_head_gemm(&p, int(w.size(0)), stream()), "head_gemm");
+}
+
+void silu_mul(const Tensor &in, const Tensor &out) {
+    cuda_contig(in, "in");
+    cuda_contig(out, "out");
+    check(in.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16, "silu_mul wants bf16");
+    const int I = int(out.size(-1));
+    const int T = int(out.numel() / I);
+    check(in.numel() == int64_t(T) * 2 * I, "silu_mul shapes");
+    c10::cuda::CUDAGuard g(in.device());
+    check_rc(xt_silu_mul(in.data_ptr(), out.data_ptr(), T, I, stream()), "silu_mul");
+}
+
 TORCH_LIBRARY(xtier, m) {
     m.def("add_rmsnorm(Tensor x, Tensor(a!)? residual, Tensor w, Tensor(b!) out, float eps) -> ()");
+    m.def("mla_prep(Tensor inp, int q_lora, Tensor q_norm, Tensor kv_norm, Tensor pos, Tensor slot, float eps, "
+          "float theta, Tensor(a!) q_out, Tensor(b!) codes, Tensor(c!) scales, Tensor(d!) rope, Tensor(e!)? lat_out) "
+          "-> ()");
+    m.def("head_gemm(Tensor x, Tensor w, Tensor(a!) y, Tensor? pos, int rope_x, int rope_y, int rope_dims, "
+          "float theta) -> ()");
+    m.def("silu_mul(Tensor inp, Tensor(a!) out) -> ()");
     m.def("qk_norm_rope_kv(Tensor qkv, Tensor? q_norm, Tensor? k_norm, Tensor pos, Tensor batch, Tensor(a!) q, "
           "Tensor(b!) k_cache, Tensor(c!) v_cache, int hq, int hkv, float theta, float eps) -> ()");
     m.def("attn_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seqlens, Tensor(a!) out, Tensor(b!) ws_o, "
@@ -604,7 +672,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("gemm_tc(Tensor a, Tensor b, Tensor? residual, Tensor(a!) out, Tensor(b!) err) -> ()");
     m.def("ep_moe(Tensor x, Tensor ids, Tensor w, Tensor peer, Tensor(a!) state, Tensor(b!) mid, Tensor w13, "
           "Tensor s13, Tensor g13, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(c!) out, Tensor(d!) err, "
-          "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases) -> ()");
+          "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases, Tensor? slots=None, "
+          "int spr=0, int mailbox=0) -> ()");
     m.def("l2_prefetch(Tensor ptrs, Tensor bytes, int ctas) -> ()");
     m.def("dsa_key_write(Tensor k, Tensor slot, Tensor(a!) codes, Tensor(b!) kscale) -> ()");
     m.def("dsa_index_decode(Tensor q, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, "
@@ -631,6 +700,9 @@ TORCH_LIBRARY(xtier, m) {
 
 TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("add_rmsnorm", &add_rmsnorm);
+    m.impl("mla_prep", &mla_prep);
+    m.impl("head_gemm", &head_gemm);
+    m.impl("silu_mul", &silu_mul);
     m.impl("qk_norm_rope_kv", &qk_norm_rope_kv);
     m.impl("attn_decode", &attn_decode);
     m.impl("moe_route", &moe_route);

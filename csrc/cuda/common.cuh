@@ -144,6 +144,20 @@ XT_DEV uint64_t globaltimer_ns() {
     return t;
 }
 
+// float -> E4M3 byte (round to nearest even, saturating at 448)
+XT_DEV uint8_t f32_to_e4m3(float v) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;\n" : "=h"(r) : "f"(0.f), "f"(v));
+    return uint8_t(r & 0xFF);
+}
+
+// two floats -> one byte of two E2M1 codes (a in the low nibble), round to nearest even, saturating at 6
+XT_DEV uint8_t f32x2_to_e2m1(float a, float b) {
+    uint16_t r;
+    asm("{\n .reg .b8 t;\n cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n cvt.u16.u8 %0, t;\n}\n" : "=h"(r) : "f"(a), "f"(b));
+    return uint8_t(r);
+}
+
 XT_DEV float bf16_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 
 }  // namespace xt

@@ -36,19 +36,6 @@ constexpr int MLA_STAGES = 4;
 constexpr int MLA_THREADS = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 softmax / epilogue
 
 // ------------------------------------------------------------------------------------------------ cache write
-__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
-    uint16_t r;
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;\n" : "=h"(r) : "f"(0.f), "f"(v));
-    return uint8_t(r & 0xFF);
-}
-
-// two floats -> one byte of two E2M1 codes (a in the low nibble), round to nearest even, saturating at 6
-__device__ __forceinline__ uint8_t f32x2_to_e2m1(float a, float b) {
-    uint16_t r;
-    asm("{\n .reg .b8 t;\n cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n cvt.u16.u8 %0, t;\n}\n" : "=h"(r) : "f"(a), "f"(b));
-    return uint8_t(r);
-}
-
 __global__ void __launch_bounds__(256) mla_kv_write_kernel(const __nv_bfloat16 *__restrict__ lat, const int64_t *slot,
                                                            uint8_t *codes, uint8_t *scales, __nv_bfloat16 *rope,
                                                            int T) {

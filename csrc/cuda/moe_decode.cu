@@ -763,7 +763,10 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
     __shared__ bool last;
     const int n = p.T * p.k;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) dest[i] = p.ids[i] / p.El;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int s = p.slots ? p.slots[i] : p.ids[i];
+        dest[i] = s < 0 ? -1 : s / p.El;   // -1: the CPU tier computes this route (not dispatched)
+    }
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         int c = 0;
@@ -773,6 +776,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
     __syncthreads();
     for (int i = blockIdx.x * nw + warp; i < n; i += gridDim.x * nw) {
         const int d = dest[i], t = i / p.k;
+        if (d < 0) continue;
         uint8_t *base = ep_buf(p, d);
         const size_t slot = size_t(p.rank) * p.R + pos[i];
         uint4 *dst = reinterpret_cast<uint4 *>(base + p.off_rx + slot * p.H * 2);
@@ -787,7 +791,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
             dst[c] = o;
         }
         if (lane == 0) {
-            int4 m = make_int4(p.ids[i] % p.El, t, i % p.k, __float_as_int(p.w[i]));
+            int4 m = make_int4((p.slots ? p.slots[i] : p.ids[i]) % p.El, t, i % p.k, __float_as_int(p.w[i]));
             *reinterpret_cast<int4 *>(base + p.off_meta + slot * 16) = m;
         }
     }
@@ -992,7 +996,8 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_down_stream(EpParams p, fs:
 }
 
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
-    __shared__ int ok;
+    __shared__ int ok, cpu_ok;
+    __shared__ unsigned gpu_mask;
     const int t = blockIdx.x;
     const uint32_t epoch = p.state[0];
     if (threadIdx.x == 0) {
@@ -1003,13 +1008,43 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
                                 p.timeout_ns);
         if (!good) atomicExch(p.error, 1);
         ok = good;
+        unsigned mask = 0;   // routes computed on a GPU (the others went to the CPU tier and have no return row)
+        for (int j = 0; j < p.k; ++j)
+            if (!p.slots || p.slots[size_t(t) * p.k + j] >= 0) mask |= 1u << j;
+        gpu_mask = mask;
+        // the CPU tier's rows of this call: a bounded wait for the dispatcher's answer (a timeout sets the error
+        // words and leaves the CPU part out)
+        int got = 0;
+        if (p.use_mb && p.mb.dev->pending) {
+            const unsigned seq = p.mb.dev->seq;
+            const uint64_t t0 = globaltimer_ns();
+            for (;;) {
+                if (ld_acquire_sys(&p.mb.hdr->resp) == seq) {
+                    got = 1;
+                    break;
+                }
+                if (globaltimer_ns() - t0 > p.mb.timeout_ns) {
+                    atomicExch(&p.mb.dev->error, 1u);
+                    p.mb.hdr->gpu_error = 1;
+                    break;
+                }
+            }
+        }
+        cpu_ok = got;
     }
     __syncthreads();
     const float *ret = reinterpret_cast<const float *>(ep_buf(p, p.rank) + p.off_ret);
+    const unsigned mask = gpu_mask;
     for (int h = threadIdx.x; h < p.H; h += blockDim.x) {
         float v = 0.f;
         if (ok)
-            for (int j = 0; j < p.k; ++j) v += __ldcv(ret + (size_t(t) * p.k + j) * p.H + h);
+            for (int j = 0; j < p.k; ++j)
+                if (mask >> j & 1) v += __ldcv(ret + (size_t(t) * p.k + j) * p.H + h);
+        if (cpu_ok) {
+            float c;
+            asm volatile("ld.volatile.global.f32 %0, [%1];\n" : "=f"(c) : "l"(p.mb.y + size_t(t) * p.H + h));
+            v += c;
+        }
         if (p.add) v += __bfloat162float(p.add[size_t(t) * p.H + h]);
         p.out[size_t(t) * p.H + h] = __float2bfloat16(v);
     }
@@ -1019,7 +1054,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
 
 extern "C" int xt_ep_moe(const EpParams *pp, int phase, cudaStream_t stream) {
     EpParams p = *pp;
-    if (p.W > EP_MAX_W || p.T * p.k > EP_MAX_ROUTES || p.H % 256 || p.I % 16) return -2;
+    if (p.W > EP_MAX_W || p.T * p.k > EP_MAX_ROUTES || p.H % 256 || p.I % 16 || p.k > 32) return -2;
+    if (p.use_mb && p.T > XT_MB_MAX_TOKENS) return -2;
     if (phase == 0) {
         const int n = p.T * p.k;
         const int grid = n < 8 ? 1 : (n + 63) / 64 > 64 ? 64 : (n + 63) / 64;

@@ -141,6 +141,25 @@ struct EpParams {
     __nv_bfloat16 *out;          // [T, H]
     unsigned long long timeout_ns;
     int *error;
+    // tiers (may be null / 0): slots [T, k] as the router wrote them -- rank * El + slot in the owner's GPU pool, or
+    // -1 for a route the CPU tier computes; such routes are not dispatched, and the combine adds the mailbox's CPU
+    // rows (a bounded wait for the dispatcher's answer) instead
+    const int32_t *slots;
+    XtMailbox mb;
+    int use_mb;
+};
+
+// Per-head small GEMM of the MLA decode step (csrc/cuda/mla_proj.cu).
+struct HeadGemmParams {
+    const __nv_bfloat16 *x;   // X[t, h, k] at x + t * xs_t + h * xs_h + k
+    const __nv_bfloat16 *w;   // [heads, K, N]
+    __nv_bfloat16 *y;         // Y[t, h, n] at y + t * ys_t + h * ys_h + n
+    long long xs_t, xs_h, ys_t, ys_h;
+    int T, K, N;
+    // optional rotary part (rope_dims > 0): Y[t, h, rope_y + i] = NeoX rotation of X[t, h, rope_x + i]
+    const int32_t *pos;
+    int rope_x, rope_y, rope_dims;
+    float theta;
 };
 }  // namespace xt
 
@@ -181,6 +200,11 @@ int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int
 int xt_gather_rows(const void *x, const int32_t *src, void *X, int R, int H, cudaStream_t stream);
 int xt_route_combine(const float *Ya, const int32_t *da, int ka, const float *Yb, const int32_t *db, int kb,
                      const void *add, void *out, int out_f32, int m, int H, cudaStream_t stream);
+int xt_mla_prep(const void *in, int ld, int q_lora, const void *q_norm, const void *kv_norm, const int32_t *pos,
+                const int64_t *slot, float eps, float theta, void *q_out, void *codes, void *scales, void *rope,
+                void *lat_out, int T, cudaStream_t stream);
+int xt_head_gemm(const xt::HeadGemmParams *p, int heads, cudaStream_t stream);
+int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream);
 int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
                   const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,
                   int *error, cudaStream_t stream);

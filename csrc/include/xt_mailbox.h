@@ -10,7 +10,7 @@
 #pragma once
 #include <stdint.h>
 
-#define XT_MB_MAX_TOKENS 16
+#define XT_MB_MAX_TOKENS 32
 #define XT_MB_MAX_ROUTES 16   // per token (top-k plus shared experts)
 
 struct XtMailboxHeader {

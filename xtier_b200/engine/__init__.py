@@ -96,27 +96,39 @@ class CpuEngine:
 
     `experts` holds the routed experts (ids 0..E-1); `shared` optional shared experts applied to every token with
     weight 1. With `slots` < E only `resident` experts are in RAM; the others must come from an attached cold store.
+    With `total_experts`, `experts` holds exactly the `resident` experts in slot order (ids of a larger set of
+    `total_experts`), so the caller never materializes the experts this engine does not keep.
     """
 
     def __init__(self, experts: ExpertWeights, shared: ExpertWeights | None = None, threads: int | None = None,
-                 limit: float = 0.0, slots: int | None = None, resident=None, fill: bool = True):
+                 limit: float = 0.0, slots: int | None = None, resident=None, fill: bool = True,
+                 total_experts: int | None = None):
         L = lib()
-        self.H, self.I, self.E = experts.hidden, experts.inter, experts.experts
+        self.H, self.I = experts.hidden, experts.inter
+        self.E = experts.experts if total_experts is None else total_experts
         self.fmt = experts.fmt
         self.shared = 0 if shared is None else shared.experts
         self.slots = self.E if slots is None else slots
         ew = experts.to('cpu')
         if resident is not None:
             res = torch.as_tensor(resident, dtype=torch.int32).contiguous()
-            src = ew.select(res.clamp_min(0).long()) if fill else None
+            if total_experts is not None:
+                if len(res) != experts.experts or self.slots < len(res):
+                    raise ValueError('engine: the given experts must be the resident ones, one per slot')
+                src = ew if fill else None
+            else:
+                src = ew.select(res.clamp_min(0).long()) if fill else None
         else:
             res = None
             src = ew.select(torch.arange(self.slots)) if self.slots < self.E else ew
         arrays = None
         if fill:
             parts = [src] + ([shared.to('cpu')] if shared is not None else [])
-            arrays = [torch.cat([getattr(p, f) for p in parts]).contiguous()
-                      for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')]
+            fields = ('w13', 'w2', 's13', 's2', 'g13', 'g2')
+            if len(parts) == 1:   # no concatenation copy
+                arrays = [getattr(src, f).contiguous() for f in fields]
+            else:
+                arrays = [torch.cat([getattr(p, f) for p in parts]).contiguous() for f in fields]
             arrays[4] = arrays[4].float().contiguous()
             arrays[5] = arrays[5].float().contiguous()
         self._keep = arrays

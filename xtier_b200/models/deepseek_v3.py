@@ -5,11 +5,23 @@ q_lora 1536, kv_lora 512, qk_nope 128, qk_rope 64, v_head 128; 256 routed MXFP4 
 shared expert, grouped top-8 routing (8 groups, top-4 groups, sigmoid scores with a selection bias, renormalized,
 routed scale 2.5); vocab 129280; random-init N(0, 0.02) weights.
 
-MLA keeps a latent cache: per token the normalized 512-dim compressed KV and the 64-dim rotary key, 576 BF16 values
-shared by all heads. Decode uses the absorbed form (queries projected into the latent space, attention over the
-latent rows, values projected back per head); prefill expands keys and values per head and runs causal attention.
-The MoE layers are `TieredMoE` (one GPU, hot slots + CPU engine) or `EPMoE` (experts split over the ranks, NVLink
-peer exchange) — attention is data parallel across ranks (each rank serves its own requests).
+MLA keeps a latent cache: per token the normalized 512-dim compressed KV and the 64-dim rotary key, shared by all
+heads (NVFP4 latent + BF16 rotary key, 416 bytes per token, for the tensor-core kernels; BF16 for the plain PyTorch
+path). Decode uses the absorbed form: the queries are projected into the latent space (q_nope . W_uk), attention
+runs over the latent rows, and the latent output is projected back per head (. W_uv^T); prefill expands keys and
+values per head and runs causal attention.
+
+Two ways to hold the MoE layers:
+  * `TieredMoE` (default, one GPU, every expert in the GPU pool): the small test shapes.
+  * expert parallelism (`ep=True`): the group's ranks own E / W experts each (`parallel/ep.py` EPMoE); when the GPUs
+    cannot hold them all (`gpu_experts`), every owner keeps part of its range in its GPU pool and the rest form a CPU
+    tier computed by each rank's CPU engine through the mailbox. Attention is data parallel (each rank serves its own
+    requests), so one decode step of the group runs `batch` requests per rank.
+
+The batched decode step (`decode_buffers` / `decode_step`, captured into one CUDA graph by runtime/decode.py
+Generator) runs per layer: fused [q_a | kv_a] GEMV, mla_prep (both RMSNorms, RoPE, NVFP4 cache write), q_b GEMV, query
+absorption + RoPE (head_gemm), the tcgen05 MLA attention over every cached position, value un-absorption (head_gemm),
+o GEMV, MoE (route + EP exchange + expert streams + combine, CPU tier through the mailbox) or the dense MLP.
 
 Reference parity: the reference runs DeepSeek V4.1 through SGLang with its MoE method (xtier/backend/method.py) and
 the DeepSeek pack (xtier/packs/deepseek_v4); this model is the framework's own runner of the named shape.
@@ -62,6 +74,26 @@ class DeepSeekV3Config:
         base.update(kw)
         return DeepSeekV3Config(**base)
 
+    def expert_bytes(self) -> int:
+        """Bytes of one routed expert (codes + block scales, gate/up and down)."""
+        bs = formats.BLOCK[self.fmt]
+        return 3 * self.inter * self.hidden // 2 + 3 * self.inter * self.hidden // bs
+
+    def moe_layers(self) -> int:
+        return self.layers - self.dense_layers
+
+    def dense_bytes(self) -> int:
+        """Bytes of everything but the routed experts (BF16 attention, dense MLPs, embeddings, shared experts,
+        routers, norms)."""
+        H = self.hidden
+        qk = self.qk_nope + self.qk_rope
+        attn = (H * (self.q_lora + self.kv_lora + self.qk_rope) + self.heads * qk * self.q_lora +
+                self.heads * self.qk_nope * self.kv_lora + self.heads * self.kv_lora * self.v_head +
+                H * self.heads * self.v_head) * 2
+        mlp = 3 * H * self.dense_inter * 2
+        moe = self.shared * self.expert_bytes() + self.experts * H * 2
+        return self.layers * attn + self.dense_layers * mlp + self.moe_layers() * moe + 2 * self.vocab * H * 2
+
 
 def _rope(x: torch.Tensor, pos: torch.Tensor, theta: float) -> torch.Tensor:
     """NeoX-style rotation of the last dim of x [..., T, d] at positions pos [T] (FP32 math)."""
@@ -73,15 +105,77 @@ def _rope(x: torch.Tensor, pos: torch.Tensor, theta: float) -> torch.Tensor:
     return torch.cat([a * cos - b * sin, b * cos + a * sin], -1).to(x.dtype)
 
 
+def _fill_random_codes(t: torch.Tensor, gen: torch.Generator):
+    """Uniform random bytes into a uint8 tensor (in chunks, so no large temporary)."""
+    flat = t.view(-1)
+    step = 1 << 28
+    for s in range(0, flat.numel(), step):
+        torch.randint(0, 256, (min(step, flat.numel() - s),), dtype=torch.uint8, device=t.device, generator=gen,
+                      out=flat[s:s + step])
+
+
+def synthetic_into(ew: formats.ExpertWeights, gen: torch.Generator, std: float):
+    """Random experts written in place into preallocated tensors (the generator of formats.synthetic_experts without
+    its full-size temporaries): uniform E2M1 codes and one block scale giving roughly N(0, std)-sized weights."""
+    _fill_random_codes(ew.w13, gen)
+    _fill_random_codes(ew.w2, gen)
+    if ew.fmt == formats.NVFP4:
+        sv = torch.tensor([std * 2.5 / 6.0], device=ew.s13.device).to(torch.float8_e4m3fn).view(torch.uint8)
+    else:
+        sv = torch.tensor([127 + round(math.log2(std * 2.5 / 4.0))], dtype=torch.uint8, device=ew.s13.device)
+    ew.s13.copy_(sv.expand_as(ew.s13))
+    ew.s2.copy_(sv.expand_as(ew.s2))
+    ew.g13.fill_(1.0)
+    ew.g2.fill_(1.0)
+
+
+def empty_experts(n: int, H: int, I: int, fmt: str, device, pin: bool = False) -> formats.ExpertWeights:
+    bs = formats.BLOCK[fmt]
+    kw = dict(device=device, pin_memory=pin) if str(device) == 'cpu' else dict(device=device)
+    return formats.ExpertWeights(fmt, torch.empty(n, 2 * I, H // 2, dtype=torch.uint8, **kw),
+                                 torch.empty(n, H, I // 2, dtype=torch.uint8, **kw),
+                                 torch.empty(n, 2 * I, H // bs, dtype=torch.uint8, **kw),
+                                 torch.empty(n, H, I // bs, dtype=torch.uint8, **kw),
+                                 torch.empty(n, 2, dtype=torch.float32, **kw),
+                                 torch.empty(n, dtype=torch.float32, **kw))
+
+
+def ep_layout(E: int, world: int, gpu_per_rank: int, seed: int):
+    """Expert placement of one MoE layer over `world` ranks: owner r holds experts [r * El, (r + 1) * El); the
+    first `gpu_per_rank` of its range in a seeded order sit in its GPU pool (slot order), the rest in the CPU tier.
+    Returns (table [E] int32: owner * gpu_per_rank + slot or -1, per-rank lists of pool experts, CPU-tier experts)."""
+    El = E // world
+    g = torch.Generator().manual_seed(seed)
+    table = torch.full((E,), -1, dtype=torch.int32)
+    pools, cpu = [], []
+    for r in range(world):
+        order = (torch.randperm(El, generator=g) + r * El).tolist()
+        pool = sorted(order[:gpu_per_rank])
+        for s, e in enumerate(pool):
+            table[e] = r * gpu_per_rank + s
+        pools.append(pool)
+        cpu += order[gpu_per_rank:]
+    return table, pools, sorted(cpu)
+
+
 class DeepSeekV3Model:
-    def __init__(self, cfg: DeepSeekV3Config, device='cuda', seed: int = 0, moe_factory=None, max_tokens: int = 64):
+    def __init__(self, cfg: DeepSeekV3Config, device='cuda', seed: int = 0, moe_factory=None, max_tokens: int = 64,
+                 ep: bool = False, gpu_experts: int | None = None, mailbox=None, engine_threads: int | None = None,
+                 decode_tokens: int = 16, ep_timeout_s: float = 30.0):
         """moe_factory(layer, router_w, corr_bias, experts_fn, shared_experts) -> an MoE layer with .forward(x, out);
-        experts_fn(rank_slice) generates the quantized experts (synthetic MXFP4 bytes) of the given expert ids.
-        Default: every expert on this GPU (TieredMoE, all hot)."""
+        experts_fn(ids) generates the quantized experts (synthetic MXFP4 bytes) of the given expert ids.
+        Default: every expert on this GPU (TieredMoE, all hot).
+        ep: expert parallelism over the process group (world 1 allowed); `gpu_experts` pool slots per rank and MoE
+        layer (default: every owned expert), the rest in the CPU tier through `mailbox` (required then) with
+        `engine_threads` workers; `decode_tokens` tokens per rank and step."""
         self.cfg = cfg
         dev = self.device = torch.device(device)
         g = torch.Generator(device='cpu').manual_seed(seed)
         H = cfg.hidden
+        self.mailbox = mailbox
+        self.engines = []
+        self.ep = None
+        self.decode_tokens = decode_tokens
 
         def randn(*shape):
             t = torch.empty(*shape, dtype=torch.bfloat16, device=dev)
@@ -93,12 +187,25 @@ class DeepSeekV3Model:
         self.lm_head = randn(cfg.vocab, H)
         self.final_norm = ones(H)
         qk = cfg.qk_nope + cfg.qk_rope
+        stage = None
+        if ep:
+            from ..parallel import dist as xdist
+            from ..parallel.ep import EPComm
+            env = xdist.init()
+            El = cfg.experts // env.world
+            self.gpu_per_rank = El if gpu_experts is None else max(1, min(El, int(gpu_experts)))
+            if self.gpu_per_rank < El and mailbox is None:
+                raise ValueError('a CPU tier (gpu_experts < experts per rank) needs a mailbox')
+            self.ep = EPComm(H, cfg.inter, cfg.experts, cfg.top_k, decode_tokens, dev, timeout_s=ep_timeout_s,
+                             slots_per_rank=self.gpu_per_rank)
+            self.ep_rank, self.ep_world = env.rank, env.world
         self.layers = []
         for li in range(cfg.layers):
             L = dict(in_norm=ones(H), post_norm=ones(H),
-                     q_a=randn(cfg.q_lora, H), q_a_norm=ones(cfg.q_lora), q_b=randn(cfg.heads * qk, cfg.q_lora),
-                     kv_a=randn(cfg.kv_lora + cfg.qk_rope, H), kv_a_norm=ones(cfg.kv_lora),
-                     kv_b=randn(cfg.heads * (cfg.qk_nope + cfg.v_head), cfg.kv_lora),
+                     qkv_a=randn(cfg.q_lora + cfg.kv_lora + cfg.qk_rope, H), q_a_norm=ones(cfg.q_lora),
+                     q_b=randn(cfg.heads * qk, cfg.q_lora), kv_a_norm=ones(cfg.kv_lora),
+                     w_uk=randn(cfg.heads, cfg.qk_nope, cfg.kv_lora),      # [h, nope, lora]
+                     w_uvT=randn(cfg.heads, cfg.kv_lora, cfg.v_head),      # [h, lora, v] (W_uv transposed)
                      o=randn(H, cfg.heads * cfg.v_head))
             if cfg.attn == 'dsa':   # own seeds: the other weights are the same with and without the indexer
                 gi = torch.Generator(device=dev).manual_seed(seed * 7919 + li)
@@ -106,9 +213,6 @@ class DeepSeekV3Model:
                               * cfg.std).bfloat16()
                 L['idx_k'] = (torch.randn(cfg.index_dim, H, device=dev, generator=gi) * cfg.std).bfloat16()
                 L['idx_w'] = (torch.randn(cfg.index_heads, H, device=dev, generator=gi) * cfg.std).bfloat16()
-            kvb = L['kv_b'].view(cfg.heads, cfg.qk_nope + cfg.v_head, cfg.kv_lora)
-            L['w_uk'] = kvb[:, :cfg.qk_nope].contiguous()          # [h, nope, lora]
-            L['w_uv'] = kvb[:, cfg.qk_nope:].contiguous()          # [h, v, lora]
             if li < cfg.dense_layers:
                 L['gate_up'] = randn(2 * cfg.dense_inter, H)
                 L['down'] = randn(H, cfg.dense_inter)
@@ -118,12 +222,13 @@ class DeepSeekV3Model:
                 seed_l = seed * 1000 + li
 
                 def experts_fn(ids, seed_l=seed_l):
-                    full = formats.synthetic_experts(len(ids), H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
-                    return full
+                    return formats.synthetic_experts(len(ids), H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
 
                 shared = formats.synthetic_experts(cfg.shared, H, cfg.inter, cfg.fmt, dev, seed=seed_l + 500,
                                                    std=cfg.std) if cfg.shared else None
-                if moe_factory is None:
+                if ep:
+                    L['moe'], stage = self._ep_layer(li, router, corr, shared, seed_l, engine_threads, stage)
+                elif moe_factory is None:
                     from ..cache.pool import TieredMoE
                     L['moe'] = TieredMoE(li, router, experts_fn(list(range(cfg.experts))), cfg.top_k, shared=shared,
                                          mode=1, n_group=cfg.n_group, topk_group=cfg.topk_group, renorm=True,
@@ -131,6 +236,46 @@ class DeepSeekV3Model:
                 else:
                     L['moe'] = moe_factory(li, router, corr, experts_fn, shared)
             self.layers.append(L)
+        del stage
+        if ep:
+            from ..parallel import dist as xdist
+            torch.cuda.synchronize()
+            xdist.barrier()   # every rank's pools are filled before any rank's dispatch reads them
+
+    def _ep_layer(self, li, router, corr, shared, seed_l, threads, stage):
+        """One MoE layer under expert parallelism: this rank's pool generated on the GPU, the CPU tier's experts
+        generated on the GPU in chunks and copied into a pinned staging buffer for this rank's engine."""
+        from ..parallel.ep import EPMoE
+        cfg = self.cfg
+        H, I, E = cfg.hidden, cfg.inter, cfg.experts
+        table, pools, cpu_ids = ep_layout(E, self.ep_world, self.gpu_per_rank, seed_l)
+        gen = torch.Generator(device=self.device).manual_seed(seed_l * 31 + self.ep_rank)
+        local = empty_experts(len(pools[self.ep_rank]), H, I, cfg.fmt, self.device)
+        synthetic_into(local, gen, cfg.std)
+        engine = None
+        if cpu_ids:
+            from ..engine import CpuEngine
+            n = len(cpu_ids)
+            if stage is None or stage.experts < n:
+                stage = empty_experts(n, H, I, cfg.fmt, 'cpu', pin=True)
+            host = formats.ExpertWeights(cfg.fmt, *(getattr(stage, f)[:n] for f in
+                                                    ('w13', 'w2', 's13', 's2', 'g13', 'g2')))
+            # the CPU tier's bytes are the same on every rank (every rank's engine holds all of them)
+            gc = torch.Generator(device=self.device).manual_seed(seed_l * 31 + 7777)
+            chunk = 16
+            for s in range(0, n, chunk):
+                e = min(n, s + chunk)
+                tmp = empty_experts(e - s, H, I, cfg.fmt, self.device)
+                synthetic_into(tmp, gc, cfg.std)
+                for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+                    getattr(host, f)[s:e].copy_(getattr(tmp, f))
+                del tmp
+            engine = CpuEngine(host, threads=threads, slots=n, resident=cpu_ids, total_experts=E)
+            self.engines.append(engine)
+        moe = EPMoE(li, self.ep, router, local, cfg.top_k, shared=shared, mode=1, n_group=cfg.n_group,
+                    topk_group=cfg.topk_group, renorm=True, scale=cfg.routed_scale, corr_bias=corr,
+                    table=table if cpu_ids else None, mailbox=self.mailbox, engine=engine)
+        return moe, stage
 
     # ------------------------------------------------------------------ state
     def kernel_attention(self) -> bool:
@@ -141,13 +286,17 @@ class DeepSeekV3Model:
             raise ValueError('the MLA kernels need 128 heads, kv_lora 512 and qk_rope 64')
         return cfg.attn in ('mla', 'dsa') or (cfg.attn == 'auto' and fits)
 
-    def alloc_state(self, batch: int, max_len: int) -> dict:
+    def alloc_state(self, batch: int, max_len: int, bf16_cache: bool = False) -> dict:
+        """KV state of `batch` sequences of up to max_len tokens. The BF16 latent cache (the plain PyTorch decode, and
+        the prefill of a continuation) is kept when the kernels do not attend or bf16_cache is set."""
         cfg = self.cfg
+        kern = self.kernel_attention()
         st = dict(batch=batch, max_len=max_len,
-                  cache=[torch.zeros(batch, max_len, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16,
-                                     device=self.device) for _ in self.layers],
                   lengths=torch.zeros(batch, dtype=torch.int32, device=self.device))
-        if self.kernel_attention():
+        if bf16_cache or not kern:
+            st['cache'] = [torch.zeros(batch, max_len, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16,
+                                       device=self.device) for _ in self.layers]
+        if kern:
             from ..attention.mla import BLOCK, LatentCache, MlaWorkspace
             st['latent'] = [LatentCache(batch, max_len, self.device) for _ in self.layers]
             nsel = cfg.index_topk if cfg.attn == 'dsa' else (max_len + BLOCK - 1) // BLOCK * BLOCK
@@ -157,24 +306,43 @@ class DeepSeekV3Model:
                 st['index'] = [IndexCache(batch, max_len, self.device) for _ in self.layers]
         return st
 
+    def fill_synthetic_cache(self, st: dict, length: int, seed: int = 0):
+        """Writes random latent rows (N(0, 1) latent values, rotary keys) for positions [0, length) of every row
+        of every layer and sets the lengths: the state a `length`-token prompt leaves, for decode benchmarks whose
+        prompts are random ids (their prefill is measured on its own)."""
+        cfg = self.cfg
+        B = st['batch']
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        slots = (torch.arange(B, device=self.device)[:, None] * st['max_len'] +
+                 torch.arange(length, device=self.device)[None]).reshape(-1)
+        for li in range(len(self.layers)):
+            for s in range(0, slots.numel(), 1 << 16):
+                sl = slots[s:s + (1 << 16)]
+                lat = torch.randn(sl.numel(), cfg.kv_lora + cfg.qk_rope, device=self.device, generator=g).bfloat16()
+                if 'latent' in st:
+                    st['latent'][li].write(lat, sl)
+                if 'cache' in st:
+                    st['cache'][li].view(-1, cfg.kv_lora + cfg.qk_rope)[sl] = lat
+        st['lengths'].fill_(length)
+
     # ------------------------------------------------------------------ blocks
     def _mla_project(self, L, h, pos):
         """Queries [T, heads, nope+rope] and the latent cache rows [T, kv_lora + rope] of h [T, H]."""
         cfg = self.cfg
         T = h.shape[0]
-        q_a = ops.linear(h, L['q_a'])
-        q_a = ops.rmsnorm(q_a.contiguous(), L['q_a_norm'], cfg.eps)
+        qkv = ops.linear(h, L['qkv_a'])
+        q_a = ops.rmsnorm(qkv[:, :cfg.q_lora].contiguous(), L['q_a_norm'], cfg.eps)
         self._q_a = q_a
         q = ops.linear(q_a, L['q_b']).view(T, cfg.heads, cfg.qk_nope + cfg.qk_rope)
         q_pe = _rope(q[..., cfg.qk_nope:].transpose(0, 1), pos, cfg.rope_theta).transpose(0, 1)
         q = torch.cat([q[..., :cfg.qk_nope], q_pe], -1)
-        kv = ops.linear(h, L['kv_a'])
+        kv = qkv[:, cfg.q_lora:]
         c = ops.rmsnorm(kv[:, :cfg.kv_lora].contiguous(), L['kv_a_norm'], cfg.eps)
         k_pe = _rope(kv[:, cfg.kv_lora:], pos, cfg.rope_theta)
         return q, torch.cat([c, k_pe], -1)
 
     def _mla_decode(self, L, q, cache, lengths):
-        """Absorbed MLA over the latent cache: q [B, heads, nope+rope] -> [B, heads * v]."""
+        """Absorbed MLA over the latent cache (plain PyTorch, FP32): q [B, heads, nope+rope] -> [B, heads * v]."""
         cfg = self.cfg
         B = q.shape[0]
         q_lat = torch.einsum('bhn,hnl->bhl', q[..., :cfg.qk_nope].float(), L['w_uk'].float())   # [B, h, lora]
@@ -187,18 +355,19 @@ class DeepSeekV3Model:
             s = (qf[b] @ kv.t()) * scale                    # [h, n]
             p = torch.softmax(s, -1)
             o_lat = p @ kv[:, :cfg.kv_lora]                 # [h, lora]
-            out[b] = torch.einsum('hl,hvl->hv', o_lat, L['w_uv'].float())
+            out[b] = torch.einsum('hl,hlv->hv', o_lat, L['w_uvT'].float())
         return out.to(torch.bfloat16).view(B, -1)
 
     def _mla_decode_kernel(self, li, L, st, q, h, q_a, rows, lens):
         """Absorbed MLA decode on the tensor cores over the NVFP4 latent cache: every cached position (dense) or the
-        DSA indexer's top-k (sparse). q [B, heads, nope+rope] -> [B, heads * v]."""
+        DSA indexer's top-k (sparse). q [B, heads, nope+rope] (rotated) -> [B, heads * v]."""
         from ..attention import dsa
         from ..attention.mla import mla_decode
         cfg = self.cfg
         B = q.shape[0]
-        q_lat = torch.einsum('bhn,hnl->bhl', q[..., :cfg.qk_nope].float(), L['w_uk'].float())
-        qf = torch.cat([q_lat, q[..., cfg.qk_nope:].float()], -1).to(torch.bfloat16).contiguous()
+        qf = torch.empty(B, cfg.heads, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16, device=q.device)
+        ops.head_gemm(q.contiguous(), L['w_uk'], qf)
+        qf[..., cfg.kv_lora:] = q[..., cfg.qk_nope:]
         lc = st['latent'][li]
         if cfg.attn == 'dsa':
             qi = ops.linear(q_a, L['idx_q']).view(B, cfg.index_heads, cfg.index_dim)
@@ -210,8 +379,9 @@ class DeepSeekV3Model:
             pos = torch.arange(nsel, device=q.device, dtype=torch.int32)[None]
             idx = torch.where(pos < lens[:, None], pos + rows[:, None] * st['max_len'], -1).int()
         o_lat = mla_decode(qf, idx, lc, st['mla_ws'], 1.0 / math.sqrt(cfg.qk_nope + cfg.qk_rope))
-        out = torch.einsum('bhl,hvl->bhv', o_lat.float(), L['w_uv'].float())
-        return out.to(torch.bfloat16).reshape(B, -1)
+        out = torch.empty(B, cfg.heads, cfg.v_head, dtype=torch.bfloat16, device=q.device)
+        ops.head_gemm(o_lat, L['w_uvT'], out)
+        return out.reshape(B, -1)
 
     def _mla_prefill(self, L, q, lat, start):
         """Expanded MLA (causal) for one sequence: q [T, h, nope+rope], lat [start+T, lora+rope] -> [T, h*v]."""
@@ -219,7 +389,7 @@ class DeepSeekV3Model:
         T = q.shape[0]
         c, k_pe = lat[:, :cfg.kv_lora], lat[:, cfg.kv_lora:]
         k_nope = torch.einsum('nl,hdl->hnd', c.float(), L['w_uk'].float()).to(torch.bfloat16)   # [h, n, nope]
-        v = torch.einsum('nl,hdl->hnd', c.float(), L['w_uv'].float()).to(torch.bfloat16)        # [h, n, v]
+        v = torch.einsum('nl,hld->hnd', c.float(), L['w_uvT'].float()).to(torch.bfloat16)       # [h, n, v]
         k = torch.cat([k_nope, k_pe.unsqueeze(0).expand(cfg.heads, -1, -1)], -1)
         qq = q.transpose(0, 1)
         mask = None
@@ -232,9 +402,9 @@ class DeepSeekV3Model:
 
     def _mlp(self, L, h, out):
         g = ops.linear(h, L['gate_up'])
-        I = g.shape[-1] // 2
-        a = (torch.nn.functional.silu(g[..., :I].float()) * g[..., I:].float()).to(torch.bfloat16)
-        out.copy_(ops.linear(a.contiguous(), L['down']))
+        a = torch.empty(h.shape[0], g.shape[-1] // 2, dtype=torch.bfloat16, device=h.device)
+        ops.silu_mul(g, a)
+        ops.linear(a, L['down'], out=out)
 
     # ------------------------------------------------------------------ forward
     def forward(self, st: dict, tokens: torch.Tensor, rows: torch.Tensor, pos: torch.Tensor, decode: bool):
@@ -251,8 +421,8 @@ class DeepSeekV3Model:
             else:
                 ops.add_rmsnorm(blk, residual, L['in_norm'], h, cfg.eps)
             q, lat = self._mla_project(L, h, pos)
-            cache = st['cache'][li]
-            cache[rows.long(), pos.long()] = lat
+            if 'cache' in st:
+                st['cache'][li][rows.long(), pos.long()] = lat
             if 'latent' in st:
                 slots = rows.long() * st['max_len'] + pos.long()
                 st['latent'][li].write(lat, slots)
@@ -263,10 +433,13 @@ class DeepSeekV3Model:
                 if 'latent' in st:
                     a = self._mla_decode_kernel(li, L, st, q, h, self._q_a, rows, lens)
                 else:
-                    a = self._mla_decode(L, q, cache[rows.long()], lens)
+                    a = self._mla_decode(L, q, st['cache'][li][rows.long()], lens)
             else:
                 start = int(pos[0])
-                a = self._mla_prefill(L, q, cache[int(rows[0]), :start + T], start)
+                if start and 'cache' not in st:
+                    raise ValueError('a continuation prefill needs the BF16 latent cache (alloc_state(bf16_cache))')
+                prefix = st['cache'][li][int(rows[0]), :start + T] if 'cache' in st else lat
+                a = self._mla_prefill(L, q, prefix, start)
             o = ops.linear(a.contiguous(), L['o'])
             ops.add_rmsnorm(o, residual, L['post_norm'], h, cfg.eps)
             if 'moe' in L:
@@ -285,8 +458,95 @@ class DeepSeekV3Model:
         st['lengths'][row] = T
         return logits.argmax(-1)
 
-    def decode_step(self, st, tokens, rows):
+    def decode_tokens_step(self, st, tokens, rows):
+        """Eager decode of one token per row (plain forward); returns the greedy next tokens."""
         pos = st['lengths'][rows.long()].clone()
         logits = self.forward(st, tokens, rows, pos, decode=True)
         st['lengths'][rows.long()] += 1
         return logits.argmax(-1)
+
+    # ------------------------------------------------------------------ batched decode step (graph capturable)
+    def decode_buffers(self, batch: int) -> dict:
+        cfg = self.cfg
+        dev = self.device
+        H = cfg.hidden
+        B = batch
+        e = lambda *s: torch.empty(*s, dtype=torch.bfloat16, device=dev)
+        return dict(
+            tokens=torch.zeros(B, dtype=torch.int64, device=dev),
+            pos=torch.zeros(B, dtype=torch.int32, device=dev),
+            rows=torch.arange(B, dtype=torch.int32, device=dev),
+            slot=torch.zeros(B, dtype=torch.int64, device=dev),
+            lens=torch.zeros(B, dtype=torch.int32, device=dev),
+            residual=e(B, H), h=e(B, H), blk=e(B, H), o=e(B, H),
+            qkv_a=e(B, cfg.q_lora + cfg.kv_lora + cfg.qk_rope), q_a=e(B, cfg.q_lora),
+            q=e(B, cfg.heads, cfg.qk_nope + cfg.qk_rope), qf=e(B, cfg.heads, cfg.kv_lora + cfg.qk_rope),
+            o_lat=e(B, cfg.heads, cfg.kv_lora), a=e(B, cfg.heads, cfg.v_head),
+            gu=e(B, 2 * cfg.dense_inter), act=e(B, cfg.dense_inter),
+            logits=e(B, cfg.vocab), next=torch.zeros(B, dtype=torch.int64, device=dev),
+        )
+
+    def decode_step(self, st: dict, buf: dict):
+        """One token per row: reads buf['tokens'], buf['pos'] (device), writes buf['next'] (greedy). Every op is a
+        kernel of this package; nothing synchronizes with the host, so the step captures into one CUDA graph."""
+        cfg = self.cfg
+        if 'latent' not in st:
+            raise ValueError('the batched decode step runs on the MLA kernels (NVFP4 latent cache)')
+        if cfg.attn == 'dsa':
+            raise ValueError('the batched decode step attends densely (attn="mla")')
+        B = buf['tokens'].shape[0]
+        ws = st['mla_ws']
+        nsel = ws.nsel
+        scale = 1.0 / math.sqrt(cfg.qk_nope + cfg.qk_rope)
+        # per step: cache slots of the new tokens and the dense key list of every row (the same for all layers)
+        if 'idx' not in buf or buf['idx'].shape[1] != nsel:
+            buf['idx'] = torch.empty(B, nsel, dtype=torch.int32, device=self.device)
+            buf['ar'] = torch.arange(nsel, dtype=torch.int32, device=self.device)[None].expand(B, nsel).contiguous()
+            buf['rowbase'] = (buf['rows'][:, None] * st['max_len']).contiguous()
+            buf['minus1'] = torch.full((B, nsel), -1, dtype=torch.int32, device=self.device)
+        torch.add(buf['rows'].long() * st['max_len'], buf['pos'].long(), out=buf['slot'])
+        torch.add(buf['pos'], 1, out=buf['lens'])
+        torch.where(buf['ar'] < buf['lens'][:, None], buf['ar'] + buf['rowbase'], buf['minus1'], out=buf['idx'])
+        torch.index_select(self.embed, 0, buf['tokens'], out=buf['residual'])
+        for li, L in enumerate(self.layers):
+            if li == 0:
+                ops.add_rmsnorm(buf['residual'], None, L['in_norm'], buf['h'], cfg.eps)
+            else:
+                ops.add_rmsnorm(buf['blk'], buf['residual'], L['in_norm'], buf['h'], cfg.eps)
+            ops.linear(buf['h'], L['qkv_a'], out=buf['qkv_a'])
+            lc = st['latent'][li]
+            ops.mla_prep(buf['qkv_a'], cfg.q_lora, L['q_a_norm'], L['kv_a_norm'], buf['pos'], buf['slot'], cfg.eps,
+                         cfg.rope_theta, buf['q_a'], lc.codes, lc.scales, lc.rope)
+            ops.linear(buf['q_a'], L['q_b'], out=buf['q'].view(B, -1))
+            ops.head_gemm(buf['q'], L['w_uk'], buf['qf'], buf['pos'], cfg.qk_nope, cfg.kv_lora, cfg.qk_rope,
+                          cfg.rope_theta)
+            torch.ops.xtier.mla_decode(buf['qf'], buf['idx'], lc.codes, lc.scales, lc.rope, ws.kg, ws.vt, ws.part_o,
+                                       ws.part_ml, buf['o_lat'], float(scale), ws.err)
+            ops.head_gemm(buf['o_lat'], L['w_uvT'], buf['a'])
+            ops.linear(buf['a'].view(B, -1), L['o'], out=buf['o'])
+            ops.add_rmsnorm(buf['o'], buf['residual'], L['post_norm'], buf['h'], cfg.eps)
+            if 'moe' in L:
+                L['moe'].forward(buf['h'], out=buf['blk'])
+            else:
+                ops.linear(buf['h'], L['gate_up'], out=buf['gu'])
+                ops.silu_mul(buf['gu'], buf['act'])
+                ops.linear(buf['act'], L['down'], out=buf['blk'])
+        ops.add_rmsnorm(buf['blk'], buf['residual'], self.final_norm, buf['h'], cfg.eps)
+        ops.linear(buf['h'], self.lm_head, out=buf['logits'])
+        torch.argmax(buf['logits'], dim=-1, out=buf['next'])
+        return buf['next']
+
+    def check(self):
+        """Raises when a bounded wait of the last steps ran out (EP exchange, mailbox, MLA)."""
+        if self.ep is not None:
+            self.ep.check()
+        if self.mailbox is not None:
+            self.mailbox.check()
+
+    def close(self):
+        for e in self.engines:
+            e.close()
+        self.engines = []
+        if self.ep is not None:
+            self.ep.close()
+            self.ep = None

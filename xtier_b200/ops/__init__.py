@@ -155,18 +155,47 @@ def gemm(a, b, out=None, residual=None):
 
 
 def linear(x, w, out=None):
-    """x @ w^T in BF16: the weight-streaming GEMV for decode-sized inputs (<= 16 rows), the tcgen05 GEMM for larger
-    ones (cuBLAS only for shapes TMA cannot describe: K not a multiple of 8 or unaligned rows)."""
+    """x @ w^T in BF16: the weight-streaming GEMV for decode-sized inputs (at most two passes over the weights, each
+    of <= 16 rows whose activations fit the kernel's shared memory), the tcgen05 GEMM for larger ones (cuBLAS only for
+    shapes TMA cannot describe: K not a multiple of 8 or unaligned rows)."""
     m = x.numel() // x.shape[-1]
     K = x.shape[-1]
-    if m <= 16 and K * m * 2 <= 200 * 1024 and x.is_contiguous():
+    per = min(16, (200 * 1024) // (K * 2))
+    if per >= 1 and m <= 2 * per and x.is_contiguous() and x.dtype == torch.bfloat16:
         out = torch.empty(*x.shape[:-1], w.shape[0], dtype=x.dtype, device=x.device) if out is None else out
-        _ops().gemv(x, w, None, out)
+        if m <= per:
+            _ops().gemv(x, w, None, out)
+            return out
+        x2, o2 = x.reshape(m, K), out.view(m, w.shape[0])
+        _ops().gemv(x2[:per], w, None, o2[:per])
+        _ops().gemv(x2[per:], w, None, o2[per:])
         return out
     if (x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.is_contiguous() and w.is_contiguous()
             and K % 8 == 0 and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0 and x.is_cuda):
         return gemm(x, w, out)
     return torch.matmul(x, w.t(), out=out) if out is not None else torch.matmul(x, w.t())
+
+
+def mla_prep(inp, q_lora: int, q_norm, kv_norm, pos, slot, eps: float, theta: float, q_out, codes, scales, rope,
+             lat_out=None):
+    """The fused [q_a | kv_a] projection rows inp [T, >= q_lora + 576] -> q_out [T, q_lora] = RMSNorm(q_a) and the
+    NVFP4 latent cache at `slot` (int64 [T]): RMSNorm of the compressed KV and RoPE of the rotary key at `pos`
+    (int32 [T]); lat_out [T, 576] (optional) receives the BF16 latent rows."""
+    _ops().mla_prep(inp, q_lora, q_norm, kv_norm, pos, slot, eps, theta, q_out, codes, scales, rope, lat_out)
+    return q_out
+
+
+def head_gemm(x, w, y, pos=None, rope_x: int = 0, rope_y: int = 0, rope_dims: int = 0, theta: float = 0.0):
+    """Per head h: y[t, h, :N] = x[t, h, :K] . w[h] (w [heads, K, N]); with rope_dims, also
+    y[t, h, rope_y:rope_y + rope_dims] = NeoX RoPE of x[t, h, rope_x:rope_x + rope_dims] at pos[t]."""
+    _ops().head_gemm(x, w, y, pos, rope_x, rope_y, rope_dims, theta)
+    return y
+
+
+def silu_mul(inp, out):
+    """inp [T, 2I] (gate then up) -> out [T, I] = SiLU(gate) * up."""
+    _ops().silu_mul(inp, out)
+    return out
 
 
 def l2_prefetch(ptrs, sizes, ctas: int = 16):

@@ -7,6 +7,12 @@ weighted result straight back into the source rank's return buffer from the down
 each token's routes in route order. Flags carry a per-call epoch, so a CUDA graph replays the exchange with no host
 work, and every wait is bounded (a timeout sets the error word and the call's output lacks the missing parts).
 
+Tiers: when the GPUs of the group cannot hold every expert, each owner keeps only part of its range in its GPU pool
+(`table`: expert -> owner * slots_per_rank + pool slot, or -1) and the others live in a CPU tier. The router then
+marks those routes -1 and hands them to this rank's mailbox (the CPU engine of every rank holds all CPU-tier experts,
+so such a route never leaves its source); the dispatch skips them and the combine adds the engine's rows after a
+bounded wait. With one rank this is the single-GPU tiered MoE on the EP kernels.
+
 `EPComm` is shared by all MoE layers of a model (the layers run one after another): one symmetric buffer, the epoch
 state and the scratch. `nccl_ep_moe()` is the baseline the fused path is measured against: all_to_all_single of the
 routed rows and metadata, the same expert kernels locally, all_to_all_single back.
@@ -26,13 +32,15 @@ from .symm import SymmetricBuffer
 
 class EPComm:
     def __init__(self, hidden: int, inter: int, experts: int, top_k: int, max_tokens: int, device=None,
-                 timeout_s: float = 10.0):
+                 timeout_s: float = 10.0, slots_per_rank: int | None = None):
+        """slots_per_rank: pool slots of every rank when the pools hold only part of the experts (tiers)."""
         env = xdist.get()
         self.W, self.rank = env.world, env.rank
         self.H, self.I, self.E, self.k, self.T = hidden, inter, experts, top_k, max_tokens
         if experts % self.W:
             raise ValueError(f'{experts} experts do not split over {self.W} ranks')
         self.El = experts // self.W
+        self.spr = slots_per_rank or self.El
         self.R = max_tokens * top_k   # worst case: every route of a source goes to one rank
         self.device = device or env.device
         W, R, H = self.W, self.R, hidden
@@ -67,11 +75,16 @@ class EPComm:
 
 
 class EPMoE:
-    """One MoE layer's routed experts split over the ranks (+ shared experts computed locally)."""
+    """One MoE layer's routed experts split over the ranks (+ shared experts computed locally).
+
+    `local`: this rank's GPU pool (all of its El experts in id order, or with `table` the pool slots' experts).
+    `table` (int32 [E], optional): expert -> owner * slots_per_rank + pool slot, -1 for the CPU tier, whose routes go
+    through `mailbox` to `engine` (this rank's CPU engine of every CPU-tier expert)."""
 
     def __init__(self, layer: int, comm: EPComm, router_w: torch.Tensor, local: ExpertWeights, top_k: int,
                  shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1, topk_group: int = 1,
-                 renorm: bool = True, scale: float = 1.0, router_bias=None, corr_bias=None):
+                 renorm: bool = True, scale: float = 1.0, router_bias=None, corr_bias=None, table=None,
+                 mailbox=None, engine=None):
         self.comm = comm
         self.layer = layer
         self.k = top_k
@@ -79,26 +92,38 @@ class EPMoE:
         self.local.g13 = self.local.g13.float().contiguous()
         self.local.g2 = self.local.g2.float().contiguous()
         self.fmt_code = 0 if local.fmt == NVFP4 else 1
+        self.table = None if table is None else torch.as_tensor(table, dtype=torch.int32).to(comm.device)
+        self.mailbox = mailbox if (engine is not None and self.table is not None) else None
+        if self.mailbox is not None:
+            self.mailbox.register(layer, engine)
+        self.engine = engine
         self.router = _Router(router_w, comm.E, top_k, mode, n_group, topk_group, renorm, scale, router_bias,
-                              corr_bias, comm.device, comm.T)
+                              corr_bias, comm.device, comm.T, table=self.table, layer=layer, mailbox=self.mailbox)
         self.shared = _SharedExperts(shared, comm.device, comm.T) if shared is not None else None
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None):
         c = self.comm
         T = x.shape[0]
+        if T > c.T:
+            raise ValueError(f'EP MoE: {T} tokens exceed the {c.T} per rank the exchange buffers were sized for')
         out = torch.empty_like(x) if out is None else out
         ids, w = self.router(x)
         extra = add
         if self.shared is not None:
             extra = self.shared(x, add)
+        tiered = self.table is not None
         torch.ops.xtier.ep_moe(x, ids, w, c.buf.peer_table, c.state, c.mid, self.local.w13, self.local.s13,
                                self.local.g13, self.local.w2, self.local.s2, self.local.g2, extra, out, c.err, c.W,
-                               c.rank, c.E, self.fmt_code, c.R, c.offsets, c.timeout_s, 0xF)
+                               c.rank, c.E, self.fmt_code, c.R, c.offsets, c.timeout_s, 0xF,
+                               self.router.slots[:T] if tiered else None, c.spr if tiered else 0,
+                               self.mailbox.handle if self.mailbox is not None else 0)
         return out
 
 
 class _Router:
-    def __init__(self, router_w, E, k, mode, n_group, topk_group, renorm, scale, bias, corr, device, max_tokens):
+    def __init__(self, router_w, E, k, mode, n_group, topk_group, renorm, scale, bias, corr, device, max_tokens,
+                 table=None, layer: int = 0, mailbox=None):
+        self.table, self.layer, self.mailbox = table, layer, mailbox
         self.w = router_w.to(device, torch.bfloat16).contiguous()
         self.E, self.k = E, k
         self.mode, self.n_group, self.topk_group, self.renorm, self.scale = mode, n_group, topk_group, renorm, scale
@@ -112,9 +137,9 @@ class _Router:
 
     def __call__(self, x):
         T = x.shape[0]
-        ops.moe_route(x, self.w, self.bias, self.corr, None, None, self.ids[:T], self.wt[:T], self.slots[:T],
+        ops.moe_route(x, self.w, self.bias, self.corr, self.table, None, self.ids[:T], self.wt[:T], self.slots[:T],
                       self.ws_logits, self.ws_count, self.k, self.mode, self.n_group, self.topk_group, self.renorm,
-                      self.scale)
+                      self.scale, self.layer, self.mailbox.handle if self.mailbox is not None else 0)
         return self.ids[:T], self.wt[:T]
 
 
