@@ -1,16 +1,24 @@
-"""Headline benchmark: decode tokens/s of the tiered MoE model (the Qwen3-style 48-layer config at one request per GPU).
+"""Headline benchmark of BASELINE.json: 32-way decode tokens/s of the DeepSeek-V3-shaped model (config 3) at N GPUs of
+one node, device-timed, max over ranks.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 3|2]
 
-Per GPU: the Qwen3-style 48-layer MoE (hidden 2048, GQA 32/4 x 128, 128 NVFP4 experts top-8 of I 768, vocab 151936,
-random-init weights, Zipf(1.1) router bias) with only 40% of each layer's experts in GPU hot slots; the other 60% run
-on the C++ CPU engine through the mailbox inside the CUDA graph. A 2048-token random prompt is prefilled, then W
-untimed and K timed greedy decode steps (batch 1) are replayed from the captured graph; the K steps are bracketed by a
-barrier and a device synchronize on both sides and timed with CUDA events; the job time is the max over ranks. With
-N > 1 every rank runs its own request (data parallel, weak scaling: per-GPU work fixed) and `value` is the total
-tokens/s of the job. Each step streams > 1.8 GB of weights (more than the 126 MB L2), so no L2 flush is needed.
-`e2e` repeats the measurement through the public API (`Generator.decode_one`: pinned H2D of the input token, graph
-replay, D2H read of the next token, every step), wall-clock, max over ranks.
+Config 3 (default): the 61-layer DeepSeek-V3 shape (MLA 128 heads, 256 MXFP4 experts top-8 with grouped sigmoid
+routing, one shared expert, first 3 layers dense, vocab 129280), random-init weights, 32 concurrent requests of a
+4096-token random prompt and 256 decode tokens. The requests are split over the N ranks (attention data parallel,
+32 / N requests per rank); the routed experts are split over the ranks (expert parallelism: rank r owns experts
+[r * 256 / N, (r + 1) * 256 / N), tokens reach their experts' owners and come back through in-kernel NVLink peer
+stores). When the N GPUs cannot hold all 347 GB of experts (N = 1, 2), every owner keeps as many of its experts in HBM
+as fit and the rest form a CPU tier on the C++ engine, reached through the mailbox inside the captured step -- the
+tiered product. The KV cache of the prompts is filled with random latent rows (the prompt ids are random; prefill is
+measured on its own) up to the middle of the 256 decode positions, so the timed steps see the average context. W
+untimed and K timed decode steps (one token for every request) are replayed from one captured CUDA graph, bracketed by
+a barrier and a device synchronize, timed with CUDA events; the job time is the max over ranks. Each step streams
+tens of GB of weights (far more than the 126 MB L2), so no L2 flush is needed. `e2e` repeats the K steps through the
+public API (`Generator.decode_one`: pinned H2D of the step's input tokens, replay, D2H of the next tokens).
+
+Config 2 (--config 2): the Qwen3-style 48-layer model of round one's flagship (one request per GPU, 40 % of the
+experts in HBM, the rest on the CPU tier).
 
 The reference arm (--impl reference) would run the unmodified reference from baseline/_ref; it is an SGLang plugin
 and SGLang is not installed in this image, so that arm reports itself unavailable.
@@ -30,12 +38,13 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-BASELINE_TOKS = 139.5   # the reference's published Qwen3.8 decode, packs off (tok/s, bs=1, RTX PRO 5000)
-METRIC = 'decode tok/s (bs=1 per GPU)'
+METRIC = 'decode tok/s (bs=1, 32-way) & 64K-prefill TTFT at 1/2/4/8 B200, max over ranks'
+QWEN_BASELINE_TOKS = 139.5   # the reference's published Qwen3.8 decode, packs off (tok/s, bs=1, RTX PRO 5000)
+GB = 1e9
 
 
 class ClockSampler:
-    """nvidia-smi samples of this rank's GPU during the timed region."""
+    """nvidia-smi samples of this rank's GPU (every 50 ms) while the timed work runs."""
 
     def __init__(self, gpu: int):
         self.gpu = gpu
@@ -48,10 +57,11 @@ class ClockSampler:
                 ['nvidia-smi', '-i', str(self.gpu), '--query-gpu=clocks.sm,clocks.max.sm,power.draw,'
                  'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
                  'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap',
-                 '--format=csv,noheader,nounits', '-lms', '200'],
+                 '--format=csv,noheader,nounits', '-lms', '50'],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            time.sleep(0.3)   # the first sample is in before the timed work starts
         except FileNotFoundError:
             self.proc = None
         return self
@@ -81,6 +91,16 @@ class ClockSampler:
                 'reasons': reasons, 'samples': len(self.samples)}
 
 
+def cpu_model() -> str:
+    try:
+        for line in open('/proc/cpuinfo'):
+            if line.startswith('model name'):
+                return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    return 'unknown'
+
+
 def reference_arm(args):
     line = {'impl': 'reference',
             'unavailable': 'the reference is an SGLang plugin (entry point xtier.plugin:load) and SGLang is not '
@@ -90,77 +110,242 @@ def reference_arm(args):
         print(json.dumps(line), flush=True)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=256)
-    ap.add_argument('--warmup', type=int, default=4)
-    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--prompt', type=int, default=2048)
-    ap.add_argument('--hot', type=float, default=0.4, help='fraction of each layer\'s experts in GPU hot slots')
-    ap.add_argument('--layers', type=int, default=48)
-    ap.add_argument('--threads', type=int, default=0, help='CPU engine workers per rank (0: auto)')
-    ap.add_argument('--no-e2e', action='store_true')
-    ap.add_argument('--no-peer', action='store_true',
-                    help='N > 1: keep every GPU\'s hot slots to itself (default: the hot slots of all GPUs form one pool '
-                         'read over NVLink)')
-    ap.add_argument('--long-prefill', type=int, default=65536,
-                    help='also time a warm prefill of this many random tokens (0: skip)')
-    ap.add_argument('--profile', type=int, default=0, help='print per-kernel device time of N graph replays and exit')
-    args = ap.parse_args()
-    if args.impl == 'reference':
-        return reference_arm(args)
-    if args.warmup < 3:
-        raise SystemExit('bench: at least 3 warm-up steps')
+class Ctx:
+    """Per-rank plumbing shared by the configs: process group, CPU placement, timing helpers."""
 
-    import torch
-    import torch.distributed as dist
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get('WORLD_SIZE', '1'))
+        self.rank = int(os.environ.get('RANK', '0'))
+        self.local = int(os.environ.get('LOCAL_RANK', '0'))
+        if self.world != args.gpus:
+            raise SystemExit(f'bench: --gpus {args.gpus} but WORLD_SIZE={self.world}')
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group('nccl', timeout=timedelta(seconds=600),
+                                    device_id=torch.device('cuda', self.local))
+        # CPU partition of this rank (NUMA node of its GPU when the node has enough of them): engine workers, the
+        # main thread, the mailbox dispatcher (xtier_b200/engine/placement.py)
+        from xtier_b200.engine import placement
+        self.place = placement.for_rank(self.local, self.world, spare_siblings=False)
+        mine = sorted(set(self.place.workers) | {self.place.main, self.place.dispatcher})
+        os.sched_setaffinity(0, mine)
+        self.threads = args.threads or len(self.place.workers)
+        os.environ["XTIER_DISPATCH_CPU"] = str(self.place.dispatcher)
+        os.environ["XTIER_WORKER_CPUS"] = ','.join(map(str, self.place.workers))
+        os.environ.setdefault("XTIER_SPIN_US", "5000")   # decode calls come every few hundred microseconds
+        torch.set_num_threads(1)
 
-    world = int(os.environ.get('WORLD_SIZE', '1'))
-    rank = int(os.environ.get('RANK', '0'))
-    local = int(os.environ.get('LOCAL_RANK', '0'))
-    if world != args.gpus:
-        raise SystemExit(f'bench: --gpus {args.gpus} but WORLD_SIZE={world}')
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group('nccl', timeout=timedelta(seconds=600), device_id=torch.device('cuda', local))
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
 
-    # CPU partition of this rank (NUMA node of its GPU when the node has enough of them): engine workers, the main
-    # thread, the mailbox dispatcher (xtier_b200/engine/placement.py)
-    from xtier_b200.engine import placement
-    place = placement.for_rank(local, world, spare_siblings=False)
-    mine = sorted(set(place.workers) | {place.main, place.dispatcher})
-    os.sched_setaffinity(0, mine)
-    threads = args.threads or len(place.workers)
-    os.environ["XTIER_DISPATCH_CPU"] = str(place.dispatcher)
-    os.environ["XTIER_WORKER_CPUS"] = ','.join(map(str, place.workers))
-    os.environ.setdefault("XTIER_SPIN_US", "5000")   # decode calls come every few hundred microseconds: keep workers hot
-    torch.set_num_threads(1)
+    def max_over_ranks(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device='cuda')
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
 
+    def sum_over_ranks(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device='cuda')
+        self.dist.all_reduce(t)
+        return float(t.item())
+
+    def timed_decode(self, gen, args):
+        """W warm-up replays, then K replays between barriers timed by CUDA events (max over ranks), then K steps
+        through the public API (wall clock, max over ranks). Clocks are sampled over both timed loops."""
+        torch = self.torch
+        for _ in range(args.warmup):
+            gen.step()
+        torch.cuda.synchronize()
+        gen.check()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(self.local) as clocks:
+            self.barrier()
+            start.record()
+            for _ in range(args.steps):
+                gen.step()
+            end.record()
+            self.barrier()
+            gen.check()
+            ms = self.max_over_ranks(start.elapsed_time(end))
+            e2e_s = None
+            if not args.no_e2e:
+                self.barrier()
+                t2 = time.perf_counter()
+                for _ in range(args.steps):
+                    gen.decode_one()
+                e2e_s = self.max_over_ranks(time.perf_counter() - t2)
+                gen.check()
+        return ms, e2e_s, clocks.summary()
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def graph_launches(gen) -> dict:
+    from xtier_b200.runtime.decode import graph_kernels, own_kernel_launches
+    try:
+        counts = graph_kernels(gen.graph)
+    except Exception as e:   # the count is a claim only when it was read from the graph
+        return {'error': f'{type(e).__name__}: {e}'}
+    return {'own_per_step': own_kernel_launches(counts), 'all_per_step': sum(counts.values()),
+            'own_kernels': len([k for k in counts if k.startswith('_ZN2xt')])}
+
+
+def plan_config3(cfg, world: int, B: int, max_len: int, torch, reserve_gb: float):
+    """HBM pool slots per rank and MoE layer: what fits beside the dense weights, the KV cache and the workspaces."""
+    free, _ = torch.cuda.mem_get_info()
+    nsel = (max_len + 127) // 128 * 128
+    kv = B * max_len * 416 * cfg.layers
+    ws = B * nsel * 1088 * 2 + B * (nsel // 128) * 128 * 514 * 4
+    spare = free - cfg.dense_bytes() - kv - ws - int(reserve_gb * GB)
+    El = cfg.experts // world
+    n = max(0, spare // (cfg.expert_bytes() * cfg.moe_layers()))
+    return int(min(El, n)), free
+
+
+def run_config3(args, ctx: Ctx) -> dict:
+    torch = ctx.torch
+    from xtier_b200.engine.mailbox import Mailbox
+    from xtier_b200.models.deepseek_v3 import DeepSeekV3Config, DeepSeekV3Model
+    from xtier_b200.runtime.decode import Generator
+    world, rank = ctx.world, ctx.rank
+    cfg = DeepSeekV3Config(layers=args.layers, attn='mla')
+    if args.requests % world:
+        raise SystemExit(f'bench: {args.requests} requests do not split over {world} ranks')
+    B = args.requests // world
+    # the timed steps straddle the middle of the 256 decode positions (the average context of the decode)
+    fill = max(args.prompt, args.prompt + args.gen // 2 - args.warmup - args.steps // 2)
+    max_len = (fill + args.warmup + 2 * args.steps + 8 + 127) // 128 * 128
+    El = cfg.experts // world
+    gpu_per_rank, free = plan_config3(cfg, world, B, max_len, torch, args.reserve_gb)
+    if gpu_per_rank < 1:
+        raise SystemExit('bench: the dense weights and the KV cache leave no HBM for routed experts')
+    cpu_per_layer = world * (El - gpu_per_rank)
+    cpu_bytes = cpu_per_layer * cfg.moe_layers() * cfg.expert_bytes()
+    if cpu_per_layer:
+        import psutil
+        avail = psutil.virtual_memory().available / max(1, world)
+        need = cpu_bytes + 6 * GB   # + the process itself, the pinned bounce buffer and slack
+        if need > avail:
+            raise SystemExit(f'bench: the CPU tier needs {need / GB:.1f} GB of host memory per rank, '
+                             f'{avail / GB:.1f} GB is available')
+    mailbox = Mailbox(cfg.hidden) if cpu_per_layer else None
+    if rank == 0:
+        print(f'bench: config 3 at {world} GPU(s): {B} requests per rank, {gpu_per_rank} of {El} experts per rank and '
+              f'layer in HBM ({free / GB:.1f} GB free), CPU tier {cpu_per_layer} experts per layer '
+              f'({cpu_bytes / GB:.1f} GB per rank)', file=sys.stderr, flush=True)
+    t0 = time.time()
+    model = DeepSeekV3Model(cfg, device='cuda', seed=1234, ep=True, gpu_experts=gpu_per_rank, mailbox=mailbox,
+                            engine_threads=ctx.threads, decode_tokens=B)
+    if mailbox is not None:
+        mailbox.start(cpu=ctx.place.dispatcher)
+    os.sched_setaffinity(0, [ctx.place.main])   # main thread off the workers' CPUs
+    build_s = time.time() - t0
+    if rank == 0:
+        print(f'bench: model built in {build_s:.1f} s', file=sys.stderr, flush=True)
+    gen = Generator(model, batch=B, max_len=max_len)
+    model.fill_synthetic_cache(gen.state, fill, seed=rank)
+    toks = torch.randint(0, cfg.vocab, (B,), generator=torch.Generator().manual_seed(100 + rank))
+    gen.buf['tokens'].copy_(toks)
+    gen.host_tokens.copy_(toks)
+    gen.buf['pos'].fill_(fill)
+    gen.capture(keep_graph=True)
+    launches = graph_launches(gen)
+    if args.profile:
+        return profile_steps(gen, args, ctx)
+    ms, e2e_s, clocks = ctx.timed_decode(gen, args)
+    ms_per_step = ms / args.steps
+    value = args.requests * args.steps / (ms / 1000.0)
+    e2e = None
+    if e2e_s is not None:
+        e2e = {'value': round(args.requests * args.steps / e2e_s, 2), 'unit': 'tok/s',
+               'h2d_bytes_per_step': gen.h2d_bytes_per_step * world, 'd2h_bytes_per_step': gen.d2h_bytes_per_step * world,
+               'api': 'Generator.decode_one (each rank: pinned H2D of its requests\' tokens, replay, D2H of the next)'}
+    mb = mailbox.stats() if mailbox is not None else {}
+    gpu_experts_bytes = gpu_per_rank * cfg.moe_layers() * cfg.expert_bytes()
+    line = {
+        'metric': METRIC, 'value': round(value, 2), 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': round(ms_per_step, 4), 'higher_is_better': True, 'scaling': 'strong',
+        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+        'config': {
+            'model': 'DeepSeek-V3-shaped 61L H7168 MLA-128h 256 MXFP4 experts top-8 (grouped sigmoid) + 1 shared, '
+                     'I2048, 3 dense layers I18432, vocab 129280 (BASELINE config 3)',
+            'global_batch': args.requests, 'seq_len': args.prompt + args.gen, 'prompt': args.prompt,
+            'decode_tokens': args.gen, 'context_at_timed_steps': fill,
+            'parallelism': f'ep{world} (experts) + dp{world} (attention, {B} requests per rank)',
+            'layers': cfg.layers,
+            'experts_in_hbm_per_rank_and_layer': gpu_per_rank, 'experts_per_rank_and_layer': El,
+            'cpu_tier_experts_per_layer': cpu_per_layer, 'cpu_tier_gb_per_rank': round(cpu_bytes / GB, 1),
+            'hbm_expert_gb_per_rank': round(gpu_experts_bytes / GB, 1),
+            'cpu_engine_threads': ctx.threads if cpu_per_layer else 0, 'cpu': cpu_model(), 'cpus': os.cpu_count(),
+            'kv': 'NVFP4 latent cache filled with random latent rows for the random prompts (prefill measured '
+                  'separately)',
+            'l2': 'inputs larger than L2: each step streams tens of GB of weights',
+            'weights': 'random-init; experts as random MXFP4 codes with block scales',
+            'baseline': 'no published number of the reference for this model and machine (vs_baseline null)'},
+        'clocks': clocks, 'e2e': e2e,
+        'gpu_launches': (launches['own_per_step'] * args.steps) if 'own_per_step' in launches else None,
+        'graph_kernels': launches,
+        'mailbox': {'calls': mb.get('calls'), 'mean_us': round(mb.get('mean_us', 0) or 0, 2)},
+        'setup_s': {'build': round(build_s, 1)},
+        'ttft_64k': None,
+    }
+    gen.graph = None
+    if mailbox is not None:
+        mailbox.stop()
+    model.close()
+    return line
+
+
+def profile_steps(gen, args, ctx):
+    from torch.profiler import ProfilerActivity, profile
+    torch = ctx.torch
+    for _ in range(args.warmup):
+        gen.step()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(args.profile):
+            gen.step()
+        torch.cuda.synchronize()
+    if ctx.rank == 0:
+        print(prof.key_averages().table(sort_by='cuda_time_total', row_limit=30, max_name_column_width=70))
+    gen.graph = None
+    return None
+
+
+def run_config2(args, ctx: Ctx) -> dict:
+    torch = ctx.torch
     from xtier_b200.engine.mailbox import Mailbox
     from xtier_b200.models.qwen3_moe import Qwen3MoeConfig, Qwen3MoeModel
     from xtier_b200.runtime.decode import Generator
-
+    world, rank = ctx.world, ctx.rank
     cfg = Qwen3MoeConfig(layers=args.layers)
     mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
     t0 = time.time()
     peer = world > 1 and not args.no_peer
     # data parallel replicas of one model (same weights on every GPU); with peer slots each GPU keeps its 40 % budget
     # of hot slots and reads the experts held by the other GPUs' slots over NVLink
-    model = Qwen3MoeModel(cfg, device='cuda', seed=1234, hot_fraction=args.hot, engine_threads=threads,
+    model = Qwen3MoeModel(cfg, device='cuda', seed=1234, hot_fraction=args.hot, engine_threads=ctx.threads,
                           mailbox=mailbox, peer=peer)
     if mailbox is not None:
-        mailbox.start(cpu=place.dispatcher)
-    os.sched_setaffinity(0, [place.main])   # main thread off the workers' CPUs
+        mailbox.start(cpu=ctx.place.dispatcher)
+    os.sched_setaffinity(0, [ctx.place.main])
     build_s = time.time() - t0
     max_len = args.prompt + args.warmup + 2 * args.steps + 16
     gen = Generator(model, batch=1, max_len=max_len)
     prompt = torch.randint(0, cfg.vocab, (1, args.prompt), generator=torch.Generator().manual_seed(rank))
-    t1 = time.time()
     gen.prefill(prompt)
-    prefill_s = time.time() - t1
-    # time to first token of a warm prefill of the same prompt (device time; rewrites the same KV entries)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record()
@@ -168,112 +353,78 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     ttft_ms = e0.elapsed_time(e1)
-    gen.capture()
-    for _ in range(args.warmup):
-        gen.step()
-    torch.cuda.synchronize()
-    gen.check()
-
+    gen.capture(keep_graph=True)
+    launches = graph_launches(gen)
     if args.profile:
-        from torch.profiler import ProfilerActivity, profile
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            for _ in range(args.profile):
-                gen.step()
-            torch.cuda.synchronize()
-        if rank == 0:
-            print(prof.key_averages().table(sort_by='cuda_time_total', row_limit=25, max_name_column_width=70))
-        gen.graph = None
-        if mailbox is not None:
-            mailbox.stop()
-        return
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device='cuda')
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        barrier()
-        start.record()
-        for _ in range(args.steps):
-            gen.step()
-        end.record()
-        barrier()
-    gen.check()
-    ms = max_over_ranks(start.elapsed_time(end))
-    ms_per_step = ms / args.steps
-    value = world * 1 * args.steps / (ms / 1000.0)
-
+        return profile_steps(gen, args, ctx)
+    ms, e2e_s, clocks = ctx.timed_decode(gen, args)
+    value = world * args.steps / (ms / 1000.0)
     e2e = None
-    if not args.no_e2e:
-        barrier()
-        t2 = time.perf_counter()
-        for _ in range(args.steps):
-            gen.decode_one()
-        e2e_s = max_over_ranks(time.perf_counter() - t2)
-        gen.check()
-        e2e = {'value': world * args.steps / e2e_s, 'unit': 'tok/s', 'h2d_bytes_per_step': gen.h2d_bytes_per_step,
-               'd2h_bytes_per_step': gen.d2h_bytes_per_step, 'api': 'Generator.decode_one'}
-
-    long_prefill = None
-    if args.long_prefill:
-        # time to first token of a long prompt: a fresh KV state, one untimed run (allocations, upload buffers,
-        # kernel selection), then one timed by device events between barriers, max over ranks
-        st2 = model.alloc_state(1, args.long_prefill + 8)
-        ids = torch.randint(0, cfg.vocab, (args.long_prefill,), generator=torch.Generator().manual_seed(7 + rank))
-        ids = ids.cuda()
-        model.prefill(st2, ids)
-        barrier()
-        e0.record()
-        model.prefill(st2, ids)
-        e1.record()
-        barrier()
-        t_long = max_over_ranks(e0.elapsed_time(e1))
-        long_prefill = {'tokens': args.long_prefill, 'ttft_ms': round(t_long, 1),
-                        'tok_s': round(world * args.long_prefill / t_long * 1e3, 1),
-                        'timing': 'warm, device events, max over ranks', 'scaling': 'weak (one prompt per GPU)'}
-        del st2
-        torch.cuda.empty_cache()
-
-    mb_stats = mailbox.stats() if mailbox is not None else {}
-    launches_per_step = 7 * cfg.layers + 1   # norms x2, rope+kv, attention, route, gate/up, down per layer; final norm
+    if e2e_s is not None:
+        e2e = {'value': round(world * args.steps / e2e_s, 2), 'unit': 'tok/s',
+               'h2d_bytes_per_step': gen.h2d_bytes_per_step * world, 'd2h_bytes_per_step': gen.d2h_bytes_per_step * world,
+               'api': 'Generator.decode_one'}
+    mb = mailbox.stats() if mailbox is not None else {}
     line = {
-        'metric': METRIC, 'value': round(value, 2), 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
-        'warmup': args.warmup, 'ms_per_step': round(ms_per_step, 4), 'higher_is_better': True, 'scaling': 'weak',
-        'vs_baseline': round(value / BASELINE_TOKS, 3), 'dtype': 'bf16', 'data': 'synthetic',
+        'metric': 'decode tok/s (bs=1 per GPU)', 'value': round(value, 2), 'unit': 'tok/s', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms / args.steps, 4),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': round(value / QWEN_BASELINE_TOKS, 3),
+        'dtype': 'bf16', 'data': 'synthetic',
         'config': {'model': 'qwen3-style MoE 48L H2048 GQA32/4 128E top-8 I768 NVFP4 (BASELINE config 2)',
                    'global_batch': world, 'seq_len': args.prompt + args.warmup + args.steps,
                    'prompt': args.prompt, 'parallelism': f'dp{world}', 'hot_fraction': args.hot,
                    'hot_slots': ('each GPU holds hot_fraction of the experts; the GPUs\' slots form one pool read '
                                  'over NVLink peer memory' if peer else 'per GPU'),
-                   'cpu_engine_threads': threads, 'layers': cfg.layers,
+                   'cpu_engine_threads': ctx.threads, 'cpu': cpu_model(), 'layers': cfg.layers,
                    'l2': 'inputs larger than L2: each step streams > 1.8 GB of weights',
                    'weights': 'random-init, experts as random NVFP4 codes and block scales',
                    'baseline': 'vs_baseline divides by 139.5 tok/s, the reference\'s Qwen3.8 bs=1 decode '
                                '(published, RTX PRO 5000; a different model and machine)'},
-        'clocks': clocks.summary(), 'e2e': e2e, 'gpu_launches': launches_per_step * args.steps,
-        'mailbox': {'calls': mb_stats.get('calls'), 'mean_us': round(mb_stats.get('mean_us', 0) or 0, 2)},
-        'setup_s': {'build': round(build_s, 1), 'prefill': round(prefill_s, 2)},
-        'prefill': {'tokens': args.prompt, 'ttft_ms': round(ttft_ms, 1),
-                    'tok_s': round(args.prompt / ttft_ms * 1e3, 1), 'timing': 'warm, device events'},
-        'prefill_long': long_prefill,
+        'clocks': clocks, 'e2e': e2e,
+        'gpu_launches': (launches['own_per_step'] * args.steps) if 'own_per_step' in launches else None,
+        'graph_kernels': launches,
+        'mailbox': {'calls': mb.get('calls'), 'mean_us': round(mb.get('mean_us', 0) or 0, 2)},
+        'setup_s': {'build': round(build_s, 1)},
+        'prefill': {'tokens': args.prompt, 'ttft_ms': round(ttft_ms, 1), 'timing': 'warm, device events'},
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     gen.graph = None
     if mailbox is not None:
         mailbox.stop()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=4)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--config', type=int, default=3, choices=[2, 3])
+    ap.add_argument('--requests', type=int, default=32, help='config 3: concurrent requests of the whole job')
+    ap.add_argument('--prompt', type=int, default=None, help='prompt tokens (config 3: 4096, config 2: 2048)')
+    ap.add_argument('--gen', type=int, default=256, help='config 3: decode tokens per request')
+    ap.add_argument('--layers', type=int, default=None, help='layers (config 3: 61, config 2: 48)')
+    ap.add_argument('--reserve-gb', type=float, default=3.0,
+                    help='config 3: HBM kept free beside the dense weights, KV and workspaces')
+    ap.add_argument('--hot', type=float, default=0.4, help='config 2: fraction of each layer\'s experts in HBM')
+    ap.add_argument('--threads', type=int, default=0, help='CPU engine workers per rank (0: auto)')
+    ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-peer', action='store_true', help='config 2, N > 1: no node-wide slot pool')
+    ap.add_argument('--profile', type=int, default=0, help='print per-kernel device time of N graph replays and exit')
+    args = ap.parse_args()
+    if args.impl == 'reference':
+        return reference_arm(args)
+    if args.warmup < 3:
+        raise SystemExit('bench: at least 3 warm-up steps')
+    if args.prompt is None:
+        args.prompt = 4096 if args.config == 3 else 2048
+    if args.layers is None:
+        args.layers = 61 if args.config == 3 else 48
+    ctx = Ctx(args)
+    line = run_config3(args, ctx) if args.config == 3 else run_config2(args, ctx)
+    if line is not None and ctx.rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
 
 
 if __name__ == '__main__':

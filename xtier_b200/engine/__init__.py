@@ -113,7 +113,7 @@ class CpuEngine:
         if resident is not None:
             res = torch.as_tensor(resident, dtype=torch.int32).contiguous()
             if total_experts is not None:
-                if len(res) != experts.experts or self.slots < len(res):
+                if (fill and len(res) != experts.experts) or self.slots < len(res):
                     raise ValueError('engine: the given experts must be the resident ones, one per slot')
                 src = ew if fill else None
             else:
@@ -236,9 +236,10 @@ class CpuEngine:
             pieces = [w13[n * gr:(n + 1) * gr], w13[I + n * gr:I + (n + 1) * gr], s13[n * gr:(n + 1) * gr],
                       s13[I + n * gr:I + (n + 1) * gr], w2[n * dr:(n + 1) * dr], s2[n * dr:(n + 1) * dr]]
             for p, ptr, sz in zip(pieces, ptrs, sizes):
-                b = p.contiguous().numpy().tobytes()
-                assert len(b) == sz
-                C.memmove(ptr, b, sz)
+                p = p.contiguous()
+                if p.numel() * p.element_size() != sz:
+                    raise ValueError(f'engine slot piece: {p.numel() * p.element_size()} bytes, slot holds {sz}')
+                C.memmove(ptr, p.data_ptr(), sz)
 
     def attach_cold(self, store: 'ColdStore', files, offsets, scores=None, half_life: float = 64.0):
         f = np.ascontiguousarray(files, dtype=np.int32)

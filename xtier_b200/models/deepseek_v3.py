@@ -256,21 +256,22 @@ class DeepSeekV3Model:
         if cpu_ids:
             from ..engine import CpuEngine
             n = len(cpu_ids)
-            if stage is None or stage.experts < n:
-                stage = empty_experts(n, H, I, cfg.fmt, 'cpu', pin=True)
-            host = formats.ExpertWeights(cfg.fmt, *(getattr(stage, f)[:n] for f in
-                                                    ('w13', 'w2', 's13', 's2', 'g13', 'g2')))
-            # the CPU tier's bytes are the same on every rank (every rank's engine holds all of them)
-            gc = torch.Generator(device=self.device).manual_seed(seed_l * 31 + 7777)
             chunk = 16
+            if stage is None:   # pinned bounce buffer of one chunk, shared by the layers
+                stage = empty_experts(chunk, H, I, cfg.fmt, 'cpu', pin=True)
+            # slots filled chunk by chunk (no host copy of a whole layer); the CPU tier's bytes are the same on every
+            # rank (every rank's engine holds all of them)
+            engine = CpuEngine(stage, threads=threads, slots=n, resident=cpu_ids, total_experts=E, fill=False)
+            gc = torch.Generator(device=self.device).manual_seed(seed_l * 31 + 7777)
             for s in range(0, n, chunk):
                 e = min(n, s + chunk)
                 tmp = empty_experts(e - s, H, I, cfg.fmt, self.device)
                 synthetic_into(tmp, gc, cfg.std)
                 for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
-                    getattr(host, f)[s:e].copy_(getattr(tmp, f))
+                    getattr(stage, f)[:e - s].copy_(getattr(tmp, f))
                 del tmp
-            engine = CpuEngine(host, threads=threads, slots=n, resident=cpu_ids, total_experts=E)
+                for j in range(e - s):
+                    engine.write_slot(s + j, stage, j)
             self.engines.append(engine)
         moe = EPMoE(li, self.ep, router, local, cfg.top_k, shared=shared, mode=1, n_group=cfg.n_group,
                     topk_group=cfg.topk_group, renorm=True, scale=cfg.routed_scale, corr_bias=corr,

@@ -39,8 +39,9 @@ class Generator:
         self.buf['tokens'].copy_(self.buf['next'])
         self.buf['pos'].add_(1)
 
-    def capture(self, warmup: int = 2):
-        """Captures one self-advancing decode step. Warm-up runs rewrite the current position only."""
+    def capture(self, warmup: int = 2, keep_graph: bool = False):
+        """Captures one self-advancing decode step. Warm-up runs rewrite the current position only. keep_graph keeps
+        the graph's node list for inspection (`graph_kernels`)."""
         saved = {k: self.buf[k].clone() for k in ('pos', 'tokens', 'prev') if k in self.buf}
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -49,9 +50,11 @@ class Generator:
                 self.model.decode_step(self.state, self.buf)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
-        self.graph = torch.cuda.CUDAGraph()
+        self.graph = torch.cuda.CUDAGraph(keep_graph=keep_graph)
         with torch.cuda.graph(self.graph):
             self._step_body()
+        if keep_graph:
+            self.graph.instantiate()
         torch.cuda.synchronize()
         for k, v in saved.items():
             self.buf[k].copy_(v)
@@ -159,3 +162,29 @@ class Generator:
     @property
     def d2h_bytes_per_step(self) -> int:
         return self.host_next.numel() * self.host_next.element_size()
+
+
+def graph_kernels(graph: torch.cuda.CUDAGraph) -> dict[str, int]:
+    """Kernel nodes of a captured graph (captured with keep_graph), counted by (mangled) kernel name: what one replay
+    launches."""
+    from cuda.bindings import driver as d
+    g = d.CUgraph(graph.raw_cuda_graph())
+    err, _, n = d.cuGraphGetNodes(g, 0)
+    err, nodes, n = d.cuGraphGetNodes(g, n)
+    if err != d.CUresult.CUDA_SUCCESS:
+        raise RuntimeError(f'cuGraphGetNodes: {err}')
+    counts: dict[str, int] = {}
+    for nd in nodes[:n]:
+        err, t = d.cuGraphNodeGetType(nd)
+        if t != d.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+            continue
+        err, prm = d.cuGraphKernelNodeGetParams(nd)
+        err, name = d.cuFuncGetName(prm.func)
+        name = name.decode() if isinstance(name, (bytes, bytearray)) else str(name)
+        counts[name] = counts.get(name, 0) + 1
+    return counts
+
+
+def own_kernel_launches(counts: dict[str, int]) -> int:
+    """Launches of this package's kernels (namespace xt) in a graph_kernels() count."""
+    return sum(v for k, v in counts.items() if k.startswith('_ZN2xt') or 'xt::' in k)
