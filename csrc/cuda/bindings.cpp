@@ -381,6 +381,11 @@ void ep_moe(const Tensor &x, const Tensor &ids, const Tensor &w, const Tensor &p
     if (p.slots) check(spr > 0 && slots->scalar_type() == at::kInt && slots->is_contiguous(), "ep slots");
     p.mb = mailbox_view(mailbox);
     p.use_mb = mailbox ? 1 : 0;
+    static const int by_expert = [] {   // XTIER_EP_ORDER=0: the expert streams take the routes in arrival order
+        const char *v = getenv("XTIER_EP_ORDER");
+        return v && *v == '0' ? 0 : 1;
+    }();
+    p.by_expert = by_expert;
     p.H = int(x.size(1));
     p.I = int(w13.size(1) / 2);
     p.k = int(ids.size(1));

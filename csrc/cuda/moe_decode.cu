@@ -845,6 +845,94 @@ XT_DEV void ep_locate(const EpParams &p, const int *off, int r, int &s, int &slo
     slot = s * p.R + (r - off[s]);
 }
 
+// Item order of the expert streams. The received routes are ordered by pool slot (a counting sort of their meta words
+// in every CTA's shared memory) and a slot's routes take turns block by block: items (group g, row block b, member m)
+// in that order. A block of weights is then copied for every route of its expert one after another by the same CTA,
+// so the copies after the first hit L2 and each expert's weights cross HBM about once per call, however many tokens
+// chose it. More routes than EP_MAX_SORT, or pools wider than EP_MAX_POOL: arrival order.
+constexpr int EP_MAX_SORT = 2048;
+constexpr int EP_MAX_POOL = 256;
+
+struct EpSort {
+    int ord[EP_MAX_SORT];        // received index of the i-th route in slot order
+    int gstart[EP_MAX_POOL];     // first sorted index of group g
+    int gsize[EP_MAX_POOL];      // routes of group g
+    int ng;                      // groups (0: arrival order)
+};
+
+XT_DEV void ep_sort(const EpParams &p, const int *off, EpSort &S) {
+    __shared__ int cnt[EP_MAX_POOL];
+    const int n = off[p.W];
+    const bool on = p.by_expert && n <= EP_MAX_SORT && p.El <= EP_MAX_POOL && n > 0;
+    const uint8_t *me = ep_buf(p, p.rank);
+    if (on) {
+        for (int e = threadIdx.x; e < p.El; e += blockDim.x) cnt[e] = 0;
+        __syncthreads();
+        for (int r = threadIdx.x; r < n; r += blockDim.x) {
+            int s, slot;
+            ep_locate(p, off, r, s, slot);
+            atomicAdd(&cnt[reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x], 1);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {   // groups: the non-empty slots; cnt becomes each slot's next free sorted index
+            int acc = 0, g = 0;
+            for (int e = 0; e < p.El; ++e) {
+                const int c = cnt[e];
+                if (c) {
+                    S.gstart[g] = acc;
+                    S.gsize[g] = c;
+                    ++g;
+                }
+                cnt[e] = acc;
+                acc += c;
+            }
+            S.ng = g;
+        }
+        __syncthreads();
+        // placement in arrival order within a slot (every CTA must derive the same item order): warp 0 walks the
+        // routes 32 at a time; lanes with the same slot rank themselves by lane, the lowest one advances the slot
+        if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            const unsigned below = (1u << lane) - 1u;
+            for (int base = 0; base < n; base += 32) {
+                const int r = base + lane;
+                int e = -1;
+                if (r < n) {
+                    int s, slot;
+                    ep_locate(p, off, r, s, slot);
+                    e = reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x;
+                }
+                const unsigned same = __match_any_sync(0xffffffffu, e);
+                if (r < n) S.ord[cnt[e] + __popc(same & below)] = r;
+                __syncwarp();
+                if (r < n && (same & below) == 0) cnt[e] += __popc(same);
+                __syncwarp();
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        S.ng = 0;
+    }
+    __syncthreads();
+}
+
+// item -> (received route, row block)
+XT_DEV void ep_item(const EpSort &S, int it, int nrb, int &r, int &rb) {
+    if (S.ng == 0) {
+        r = it / nrb;
+        rb = it % nrb;
+        return;
+    }
+    int lo = 0, hi = S.ng - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (S.gstart[mid] * nrb <= it) lo = mid;
+        else hi = mid - 1;
+    }
+    const int local = it - S.gstart[lo] * nrb, sz = S.gsize[lo];
+    rb = local / sz;
+    r = S.ord[S.gstart[lo] + local % sz];
+}
+
 // Phase 1, persistent: items = (received route, R/2 rows of gate and the same R/2 rows of up) streamed through the
 // shared-memory ring of fp4_stream.cuh; row group rs owns gate rows [rs*RPW/2, (rs+1)*RPW/2) and the matching up rows,
 // so SwiGLU is applied where the sums meet. Each CTA takes a contiguous range of items (few route changes, so the
@@ -854,8 +942,10 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_gate_up_stream(EpParams p, 
     extern __shared__ uint8_t smem_raw[];
     __shared__ int off[EP_MAX_W + 1];
     __shared__ volatile int abort_flag;
+    __shared__ EpSort S;
     const uint32_t epoch = p.state[0];
     if (!ep_gather_counts(p, epoch, off)) return;
+    ep_sort(p, off, S);
     const fs::Ring ring = fs::ring_init(smem_raw, geo, &abort_flag, p.error);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int half = geo.R / 2;
@@ -869,7 +959,8 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_gate_up_stream(EpParams p, 
         uint32_t filled = 0;
         int cur = -1, e = 0;
         for (int it = it0; it < it1; ++it) {
-            const int r = it / nrb, rb = it % nrb;
+            int r, rb;
+            ep_item(S, it, nrb, r, rb);
             if (r != cur) {
                 int s, slot;
                 ep_locate(p, off, r, s, slot);
@@ -895,7 +986,8 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_gate_up_stream(EpParams p, 
     int cur = -1, slot = 0;
     float gg = 0.f, gu = 0.f;
     for (int it = it0; it < it1; ++it) {
-        const int r = it / nrb, rb = it % nrb;
+        int r, rb;
+        ep_item(S, it, nrb, r, rb);
         if (r != cur) {
             int s;
             ep_locate(p, off, r, s, slot);
@@ -927,8 +1019,10 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_down_stream(EpParams p, fs:
     __shared__ int off[EP_MAX_W + 1];
     __shared__ volatile int abort_flag;
     __shared__ bool last;
+    __shared__ EpSort S;
     const uint32_t epoch = p.state[0];
     if (!ep_gather_counts(p, epoch, off)) return;
+    ep_sort(p, off, S);
     const fs::Ring ring = fs::ring_init(smem_raw, geo, &abort_flag, p.error);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nrb = p.H / geo.R;
@@ -941,7 +1035,8 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_down_stream(EpParams p, fs:
         uint32_t filled = 0;
         int cur = -1, e = 0;
         for (int it = it0; it < it1; ++it) {
-            const int r = it / nrb, hb = it % nrb;
+            int r, hb;
+            ep_item(S, it, nrb, r, hb);
             if (r != cur) {
                 int s, slot;
                 ep_locate(p, off, r, s, slot);
@@ -963,7 +1058,8 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_down_stream(EpParams p, fs:
         float wt = 0.f;
         float *dst_row = nullptr;
         for (int it = it0; it < it1; ++it) {
-            const int r = it / nrb, hb = it % nrb;
+            int r, hb;
+            ep_item(S, it, nrb, r, hb);
             if (r != cur) {
                 int s, slot;
                 ep_locate(p, off, r, s, slot);

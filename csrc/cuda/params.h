@@ -147,6 +147,7 @@ struct EpParams {
     const int32_t *slots;
     XtMailbox mb;
     int use_mb;
+    int by_expert;   // expert streams visit the received routes grouped by pool slot (0: arrival order)
 };
 
 // Per-head small GEMM of the MLA decode step (csrc/cuda/mla_proj.cu).

@@ -191,3 +191,29 @@ def test_batched_decode_step_matches_forward(cuda_ops):
     finally:
         mb.stop()
         model.close()
+
+
+def test_ep_shared_expert_in_pool(cuda_ops):
+    """Shared experts as routes to the last pool slots of every rank: the EP kernels at world 1 against the fp32
+    dequant reference with the shared expert added at weight 1."""
+    from xtier_b200.parallel import dist as xdist
+    from xtier_b200.parallel.ep import EPComm, EPMoE
+    xdist.init()
+    H, I, E, k, T = 1024, 512, 16, 4, 9
+    ex = formats.random_experts(E, H, I, formats.MXFP4, seed=15, std=0.05)
+    sh = formats.random_experts(1, H, I, formats.MXFP4, seed=16, std=0.05)
+    router = (torch.randn(E, H, generator=torch.Generator().manual_seed(17)) * 0.02).bfloat16()
+    comm = EPComm(H, I, E, k, 16, torch.device('cuda'), timeout_s=5.0, n_shared=1)
+    layer = EPMoE(0, comm, router, ex, k, shared=sh, mode=1, n_group=4, topk_group=2, renorm=True, scale=2.5)
+    try:
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(18)).bfloat16().cuda()
+        add = torch.randn(T, H, generator=torch.Generator().manual_seed(19)).bfloat16().cuda()
+        out = layer.forward(x, add=add)
+        torch.cuda.synchronize()
+        comm.check()
+        ids, w = layer.router.ids[:T].cpu(), layer.router.wt[:T].cpu()
+        assert bool((ids[:, k:] == -1).all()) and bool((w[:, k:] == 1).all())
+        ref = formats.reference_moe(x.cpu(), ids[:, :k], w[:, :k], ex, shared=sh) + add.cpu().float()
+        assert _rel(out.cpu(), ref) < 2e-2, _rel(out.cpu(), ref)
+    finally:
+        comm.close()

@@ -140,10 +140,12 @@ def empty_experts(n: int, H: int, I: int, fmt: str, device, pin: bool = False) -
                                  torch.empty(n, dtype=torch.float32, **kw))
 
 
-def ep_layout(E: int, world: int, gpu_per_rank: int, seed: int):
+def ep_layout(E: int, world: int, gpu_per_rank: int, seed: int, stride: int | None = None):
     """Expert placement of one MoE layer over `world` ranks: owner r holds experts [r * El, (r + 1) * El); the
     first `gpu_per_rank` of its range in a seeded order sit in its GPU pool (slot order), the rest in the CPU tier.
-    Returns (table [E] int32: owner * gpu_per_rank + slot or -1, per-rank lists of pool experts, CPU-tier experts)."""
+    Returns (table [E] int32: owner * stride + slot or -1, per-rank lists of pool experts, CPU-tier experts); stride
+    is the pool width (default gpu_per_rank; more when shared experts follow the routed ones)."""
+    stride = gpu_per_rank if stride is None else stride
     El = E // world
     g = torch.Generator().manual_seed(seed)
     table = torch.full((E,), -1, dtype=torch.int32)
@@ -152,7 +154,7 @@ def ep_layout(E: int, world: int, gpu_per_rank: int, seed: int):
         order = (torch.randperm(El, generator=g) + r * El).tolist()
         pool = sorted(order[:gpu_per_rank])
         for s, e in enumerate(pool):
-            table[e] = r * gpu_per_rank + s
+            table[e] = r * stride + s
         pools.append(pool)
         cpu += order[gpu_per_rank:]
     return table, pools, sorted(cpu)
@@ -197,7 +199,7 @@ class DeepSeekV3Model:
             if self.gpu_per_rank < El and mailbox is None:
                 raise ValueError('a CPU tier (gpu_experts < experts per rank) needs a mailbox')
             self.ep = EPComm(H, cfg.inter, cfg.experts, cfg.top_k, decode_tokens, dev, timeout_s=ep_timeout_s,
-                             slots_per_rank=self.gpu_per_rank)
+                             slots_per_rank=self.gpu_per_rank + cfg.shared, n_shared=cfg.shared)
             self.ep_rank, self.ep_world = env.rank, env.world
         self.layers = []
         for li in range(cfg.layers):
@@ -248,7 +250,7 @@ class DeepSeekV3Model:
         from ..parallel.ep import EPMoE
         cfg = self.cfg
         H, I, E = cfg.hidden, cfg.inter, cfg.experts
-        table, pools, cpu_ids = ep_layout(E, self.ep_world, self.gpu_per_rank, seed_l)
+        table, pools, cpu_ids = ep_layout(E, self.ep_world, self.gpu_per_rank, seed_l, stride=self.ep.spr)
         gen = torch.Generator(device=self.device).manual_seed(seed_l * 31 + self.ep_rank)
         local = empty_experts(len(pools[self.ep_rank]), H, I, cfg.fmt, self.device)
         synthetic_into(local, gen, cfg.std)
@@ -275,7 +277,7 @@ class DeepSeekV3Model:
             self.engines.append(engine)
         moe = EPMoE(li, self.ep, router, local, cfg.top_k, shared=shared, mode=1, n_group=cfg.n_group,
                     topk_group=cfg.topk_group, renorm=True, scale=cfg.routed_scale, corr_bias=corr,
-                    table=table if cpu_ids else None, mailbox=self.mailbox, engine=engine)
+                    table=table, mailbox=self.mailbox, engine=engine)
         return moe, stage
 
     # ------------------------------------------------------------------ state

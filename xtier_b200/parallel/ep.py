@@ -32,15 +32,20 @@ from .symm import SymmetricBuffer
 
 class EPComm:
     def __init__(self, hidden: int, inter: int, experts: int, top_k: int, max_tokens: int, device=None,
-                 timeout_s: float = 10.0, slots_per_rank: int | None = None):
-        """slots_per_rank: pool slots of every rank when the pools hold only part of the experts (tiers)."""
+                 timeout_s: float = 10.0, slots_per_rank: int | None = None, n_shared: int = 0):
+        """slots_per_rank: pool slots of every rank (routed experts in HBM plus the shared experts; default every
+        owned expert plus the shared ones). n_shared: shared experts per token, computed as routes to the local pool's
+        last slots."""
         env = xdist.get()
         self.W, self.rank = env.world, env.rank
-        self.H, self.I, self.E, self.k, self.T = hidden, inter, experts, top_k, max_tokens
+        self.H, self.I, self.E, self.T = hidden, inter, experts, max_tokens
+        self.k = top_k + n_shared     # routes per token on the wire (routed + shared)
+        self.n_shared = n_shared
         if experts % self.W:
             raise ValueError(f'{experts} experts do not split over {self.W} ranks')
         self.El = experts // self.W
-        self.spr = slots_per_rank or self.El
+        self.spr = slots_per_rank or (self.El + n_shared)
+        top_k = self.k
         self.R = max_tokens * top_k   # worst case: every route of a source goes to one rank
         self.device = device or env.device
         W, R, H = self.W, self.R, hidden
@@ -75,11 +80,12 @@ class EPComm:
 
 
 class EPMoE:
-    """One MoE layer's routed experts split over the ranks (+ shared experts computed locally).
+    """One MoE layer's routed experts split over the ranks; the shared experts are routes to the last slots of the
+    local pool, so they stream through the same kernels (one weight pass for all of a rank's tokens).
 
-    `local`: this rank's GPU pool (all of its El experts in id order, or with `table` the pool slots' experts).
-    `table` (int32 [E], optional): expert -> owner * slots_per_rank + pool slot, -1 for the CPU tier, whose routes go
-    through `mailbox` to `engine` (this rank's CPU engine of every CPU-tier expert)."""
+    `local`: this rank's GPU pool of routed experts (all of its El experts in id order, or with `table` the pool
+    slots' experts). `table` (int32 [E], optional): expert -> owner * slots_per_rank + pool slot, -1 for the CPU tier,
+    whose routes go through `mailbox` to `engine` (this rank's CPU engine of every CPU-tier expert)."""
 
     def __init__(self, layer: int, comm: EPComm, router_w: torch.Tensor, local: ExpertWeights, top_k: int,
                  shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1, topk_group: int = 1,
@@ -88,18 +94,37 @@ class EPMoE:
         self.comm = comm
         self.layer = layer
         self.k = top_k
-        self.local = local.to(comm.device).contiguous()
+        n_sh = 0 if shared is None else shared.experts
+        if n_sh != comm.n_shared or top_k + n_sh != comm.k:
+            raise ValueError('EP MoE: routes per token differ from the exchange buffers (top_k / n_shared)')
+        nl = local.experts
+        if nl + n_sh != comm.spr:
+            raise ValueError(f'EP MoE: {nl} pool experts + {n_sh} shared != {comm.spr} slots per rank')
+        parts = [local] + ([shared] if shared is not None else [])
+        fields = ('w13', 'w2', 's13', 's2', 'g13', 'g2')
+        self.local = ExpertWeights(local.fmt, *[torch.cat([getattr(q, f).to(comm.device) for q in parts]).contiguous()
+                                                for f in fields])
         self.local.g13 = self.local.g13.float().contiguous()
         self.local.g2 = self.local.g2.float().contiguous()
         self.fmt_code = 0 if local.fmt == NVFP4 else 1
-        self.table = None if table is None else torch.as_tensor(table, dtype=torch.int32).to(comm.device)
-        self.mailbox = mailbox if (engine is not None and self.table is not None) else None
+        if table is None:   # every owned expert in its owner's pool, in id order
+            if nl != comm.El:
+                raise ValueError('EP MoE: without a table the pool holds every owned expert')
+            e = torch.arange(comm.E, dtype=torch.int32)
+            table = (e // comm.El) * comm.spr + e % comm.El
+            tiered = False
+        else:
+            tiered = True
+        self.table = torch.as_tensor(table, dtype=torch.int32).to(comm.device)
+        self.shared_slots = (torch.arange(nl, nl + n_sh, dtype=torch.int32, device=comm.device) + comm.rank * comm.spr
+                             if n_sh else None)
+        self.mailbox = mailbox if (engine is not None and tiered) else None
         if self.mailbox is not None:
             self.mailbox.register(layer, engine)
         self.engine = engine
         self.router = _Router(router_w, comm.E, top_k, mode, n_group, topk_group, renorm, scale, router_bias,
-                              corr_bias, comm.device, comm.T, table=self.table, layer=layer, mailbox=self.mailbox)
-        self.shared = _SharedExperts(shared, comm.device, comm.T) if shared is not None else None
+                              corr_bias, comm.device, comm.T, table=self.table, layer=layer, mailbox=self.mailbox,
+                              shared_slots=self.shared_slots)
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None):
         c = self.comm
@@ -108,63 +133,36 @@ class EPMoE:
             raise ValueError(f'EP MoE: {T} tokens exceed the {c.T} per rank the exchange buffers were sized for')
         out = torch.empty_like(x) if out is None else out
         ids, w = self.router(x)
-        extra = add
-        if self.shared is not None:
-            extra = self.shared(x, add)
-        tiered = self.table is not None
         torch.ops.xtier.ep_moe(x, ids, w, c.buf.peer_table, c.state, c.mid, self.local.w13, self.local.s13,
-                               self.local.g13, self.local.w2, self.local.s2, self.local.g2, extra, out, c.err, c.W,
+                               self.local.g13, self.local.w2, self.local.s2, self.local.g2, add, out, c.err, c.W,
                                c.rank, c.E, self.fmt_code, c.R, c.offsets, c.timeout_s, 0xF,
-                               self.router.slots[:T] if tiered else None, c.spr if tiered else 0,
+                               self.router.slots[:T], c.spr,
                                self.mailbox.handle if self.mailbox is not None else 0)
         return out
 
 
 class _Router:
     def __init__(self, router_w, E, k, mode, n_group, topk_group, renorm, scale, bias, corr, device, max_tokens,
-                 table=None, layer: int = 0, mailbox=None):
-        self.table, self.layer, self.mailbox = table, layer, mailbox
+                 table=None, layer: int = 0, mailbox=None, shared_slots=None):
+        self.table, self.layer, self.mailbox, self.shared_slots = table, layer, mailbox, shared_slots
+        kk = k + (0 if shared_slots is None else shared_slots.numel())
         self.w = router_w.to(device, torch.bfloat16).contiguous()
         self.E, self.k = E, k
         self.mode, self.n_group, self.topk_group, self.renorm, self.scale = mode, n_group, topk_group, renorm, scale
         self.bias = None if bias is None else bias.to(device, torch.float32).contiguous()
         self.corr = None if corr is None else corr.to(device, torch.float32).contiguous()
-        self.ids = torch.empty(max_tokens, k, dtype=torch.int32, device=device)
-        self.wt = torch.empty(max_tokens, k, dtype=torch.float32, device=device)
-        self.slots = torch.empty(max_tokens, k, dtype=torch.int32, device=device)
+        self.ids = torch.empty(max_tokens, kk, dtype=torch.int32, device=device)
+        self.wt = torch.empty(max_tokens, kk, dtype=torch.float32, device=device)
+        self.slots = torch.empty(max_tokens, kk, dtype=torch.int32, device=device)
         self.ws_logits = torch.empty(max_tokens, E, dtype=torch.float32, device=device)
         self.ws_count = torch.zeros(max_tokens, dtype=torch.int32, device=device)
 
     def __call__(self, x):
         T = x.shape[0]
-        ops.moe_route(x, self.w, self.bias, self.corr, self.table, None, self.ids[:T], self.wt[:T], self.slots[:T],
+        ops.moe_route(x, self.w, self.bias, self.corr, self.table, self.shared_slots, self.ids[:T], self.wt[:T], self.slots[:T],
                       self.ws_logits, self.ws_count, self.k, self.mode, self.n_group, self.topk_group, self.renorm,
                       self.scale, self.layer, self.mailbox.handle if self.mailbox is not None else 0)
         return self.ids[:T], self.wt[:T]
-
-
-class _SharedExperts:
-    """Shared experts of a layer on every rank: the decode expert kernels with one route per token per shared
-    expert, weight 1."""
-
-    def __init__(self, shared: ExpertWeights, device, max_tokens: int):
-        self.p = shared.to(device).contiguous()
-        self.p.g13 = self.p.g13.float().contiguous()
-        self.p.g2 = self.p.g2.float().contiguous()
-        n = shared.experts
-        self.fmt_code = 0 if shared.fmt == NVFP4 else 1
-        self.slots = torch.arange(n, dtype=torch.int32, device=device).repeat(max_tokens, 1).contiguous()
-        self.w = torch.ones(max_tokens, n, dtype=torch.float32, device=device)
-        self.mid = torch.empty(max_tokens * n, shared.inter, dtype=torch.float16, device=device)
-        self.out = torch.empty(max_tokens, shared.hidden, dtype=torch.bfloat16, device=device)
-
-    def __call__(self, x, add=None):
-        T = x.shape[0]
-        ops.moe_gate_up(x, self.slots[:T], self.p.w13, self.p.s13, self.p.g13, self.mid[:T * self.slots.shape[1]],
-                        self.fmt_code)
-        ops.moe_down(self.mid[:T * self.slots.shape[1]], self.slots[:T], self.w[:T], self.p.w2, self.p.s2, self.p.g2,
-                     add, self.out[:T], fmt=self.fmt_code)
-        return self.out[:T]
 
 
 def nccl_ep_moe(x, ids, w, local: ExpertWeights, E: int, group=None):
