@@ -13,16 +13,17 @@ namespace xt {
 constexpr int GV_WARPS = 8;
 constexpr int GV_ROWS = 2;        // rows per warp
 constexpr int GV_SEG = 8;         // 16-byte chunks per lane per row per segment (K segment = 2048 elements)
+constexpr int GV_MAX_WARPS = 16;  // a CTA whose activations fill most of an SM's shared memory runs 16 warps
 
-template <int M>
-__global__ void __launch_bounds__(GV_WARPS * 32) gemv_bf16_kernel(const __nv_bfloat16 *__restrict__ x,
+template <int M, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) gemv_bf16_kernel(const __nv_bfloat16 *__restrict__ x,
                                                                  const __nv_bfloat16 *__restrict__ W,
                                                                  const __nv_bfloat16 *__restrict__ add,
                                                                  __nv_bfloat16 *__restrict__ y, int N, int K) {
     extern __shared__ uint4 xs[];   // [M][K/8]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int kc = K / 8;
-    const int row0 = (blockIdx.x * GV_WARPS + warp) * GV_ROWS;
+    const int row0 = (blockIdx.x * WARPS + warp) * GV_ROWS;
     // the first K segment's weights are in flight before the wait for the previous kernel (they do not depend on it)
     uint4 w[GV_ROWS][GV_SEG];
 #pragma unroll
@@ -102,25 +103,37 @@ extern "C" int xt_gemv_bf16(const void *x, const void *W, const void *add, void 
     if (K % 8 || m < 1 || m > 16) return -2;
     const size_t smem = size_t(m) * K * 2;
     if (smem > 200 * 1024) return -3;
-    const int rows_per_cta = GV_WARPS * GV_ROWS;
+    // activations over 64 KB leave room for one or two CTAs per SM: those run 16 warps (up to 8 tokens, whose
+    // registers fit 512 threads), so as many weight loads stay in flight as several 8-warp CTAs would keep
+    const int warps = smem > 64 * 1024 && m <= 8 ? GV_MAX_WARPS : GV_WARPS;
+    const int rows_per_cta = warps * GV_ROWS;
     dim3 grid((N + rows_per_cta - 1) / rows_per_cta);
     auto X = static_cast<const __nv_bfloat16 *>(x);
     auto Wp = static_cast<const __nv_bfloat16 *>(W);
     auto A = static_cast<const __nv_bfloat16 *>(add);
     auto Y = static_cast<__nv_bfloat16 *>(y);
-#define XT_GV(MM)                                                                                             \
-    case MM: {                                                                                               \
-        xt_smem_optin(gemv_bf16_kernel<MM>, 200 * 1024);                                                     \
-        if (xt_launch(gemv_bf16_kernel<MM>, grid, dim3(GV_WARPS * 32), smem, stream, X, Wp, A, Y, N, K) !=     \
+#define XT_GV_LAUNCH(MM, WW)                                                                                  \
+    {                                                                                                        \
+        xt_smem_optin(gemv_bf16_kernel<MM, WW>, 200 * 1024);                                                 \
+        if (xt_launch(gemv_bf16_kernel<MM, WW>, grid, dim3(WW * 32), smem, stream, X, Wp, A, Y, N, K) !=       \
             cudaSuccess)                                                                                     \
             return -1;                                                                                       \
-        break;                                                                                               \
     }
+#define XT_GV(MM)                                                                                             \
+    case MM:                                                                                                 \
+        if (warps == GV_MAX_WARPS) XT_GV_LAUNCH(MM, GV_MAX_WARPS) else XT_GV_LAUNCH(MM, GV_WARPS)            \
+        break;
+#define XT_GV8(MM)                                                                                            \
+    case MM:                                                                                                 \
+        XT_GV_LAUNCH(MM, GV_WARPS)                                                                           \
+        break;
     switch (m) {
         XT_GV(1) XT_GV(2) XT_GV(3) XT_GV(4) XT_GV(5) XT_GV(6) XT_GV(7) XT_GV(8)
-        XT_GV(9) XT_GV(10) XT_GV(11) XT_GV(12) XT_GV(13) XT_GV(14) XT_GV(15) XT_GV(16)
+        XT_GV8(9) XT_GV8(10) XT_GV8(11) XT_GV8(12) XT_GV8(13) XT_GV8(14) XT_GV8(15) XT_GV8(16)
         default: return -2;
     }
 #undef XT_GV
+#undef XT_GV8
+#undef XT_GV_LAUNCH
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

@@ -9,8 +9,8 @@
 //                position, BF16 into the cache; and optionally the BF16 latent row itself.
 //   silu_mul     the dense MLP's activation: [T, 2I] (gate rows then up rows of the fused projection) ->
 //                SiLU(gate) * up in FP32, BF16 out [T, I].
-//   head_gemm    per head: Y[t, h, :N] = X[t, h, :K] . W[h] (W[h] is [K, N] row-major), grid (heads, N / 64); the
-//                query absorption (q_nope . W_uk, K 128 -> N 512, with the query's rotary dims rotated by an extra
+//   head_gemm    per head: Y[t, h, :N] = X[t, h, :K] . W[h] (W[h] is [K, N] row-major), grid (heads, N / 64), K split
+//                over the warps; the query absorption (q_nope . W_uk, K 128 -> N 512, with the query's rotary dims rotated by an extra
 //                column block of CTAs) and the value un-absorption (o_latent . W_uv^T, K 512 -> N 128).
 //
 // Reference parity: the reference runs these steps inside SGLang's DeepSeek model code (FlashMLA decode with the
@@ -24,7 +24,7 @@ namespace xt {
 
 constexpr int MP_THREADS = 256;
 constexpr int HG_COLS = 64;      // output columns per CTA
-constexpr int HG_TOK = 32;       // tokens per pass (shared-memory chunk)
+constexpr int HG_TOK = 16;       // tokens per pass (registers and shared-memory chunk)
 
 // NeoX rotation of the pair (a, b) = (x[i], x[i + d/2]) at position pos, frequency index i of d rotary dims
 XT_DEV float2 rope_pair(float a, float b, float pos, int i, int d, float theta) {
@@ -118,11 +118,15 @@ __global__ void __launch_bounds__(MP_THREADS) mla_prep_kernel(const __nv_bfloat1
         for (int i = tid; i < L; i += MP_THREADS) lat_out[size_t(t) * (L + R) + i] = __float2bfloat16(lat[i]);
 }
 
-// grid (heads, N / 64 [+ 1 rotary block]); thread (token group g = tid / 32, column pair c = tid % 32)
+// grid (heads, N / 64 [+ 1 rotary block]). The 8 warps split K; lane c owns columns n0 + 2c, n0 + 2c + 1 and keeps
+// the sums of up to HG_TOK tokens in registers, so every weight is loaded once per CTA (eight loads in flight per lane);
+// the warps' partial sums meet in shared memory and are added in warp order.
 __global__ void __launch_bounds__(MP_THREADS) head_gemm_kernel(HeadGemmParams p) {
     extern __shared__ __align__(16) uint8_t hg_smem[];
-    __nv_bfloat16 *xs = reinterpret_cast<__nv_bfloat16 *>(hg_smem);   // [HG_TOK][K]
-    const int h = blockIdx.x, tid = threadIdx.x;
+    constexpr int NW = MP_THREADS / 32;
+    __nv_bfloat16 *xs = reinterpret_cast<__nv_bfloat16 *>(hg_smem);                        // [HG_TOK][K]
+    float *red = reinterpret_cast<float *>(hg_smem + size_t(HG_TOK) * p.K * 2);           // [NW][HG_TOK][64]
+    const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, c = tid & 31;
     const int nblk = p.N / HG_COLS;
     pdl_wait();
     pdl_trigger();
@@ -140,44 +144,57 @@ __global__ void __launch_bounds__(MP_THREADS) head_gemm_kernel(HeadGemmParams p)
         return;
     }
     const int n0 = blockIdx.y * HG_COLS;
-    const int c = tid & 31, g = tid >> 5;   // columns n0 + 2c, n0 + 2c + 1; tokens g, g + 8, g + 16, g + 24
+    const int kw = p.K / NW;                 // this warp's K slice (K % 64 == 0)
+    const int k0w = warp * kw;
     const __nv_bfloat16 *W = p.w + size_t(h) * p.K * p.N + n0 + 2 * c;
     for (int t0 = 0; t0 < p.T; t0 += HG_TOK) {
         const int nt = min(HG_TOK, p.T - t0);
         __syncthreads();
-        // this head's rows of the token chunk into shared memory (16-byte pieces; K % 8 == 0)
         for (int i = tid; i < nt * (p.K / 8); i += MP_THREADS) {
             const int t = i / (p.K / 8), kc = i % (p.K / 8);
             reinterpret_cast<uint4 *>(xs + size_t(t) * p.K)[kc] =
                 *reinterpret_cast<const uint4 *>(p.x + (t0 + t) * p.xs_t + h * p.xs_h + kc * 8);
         }
         __syncthreads();
-        float acc[4][2] = {};
-        for (int k0 = 0; k0 < p.K; k0 += 8) {
-            __nv_bfloat162 wv[8];
+        float acc[HG_TOK][2];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) wv[u] = *reinterpret_cast<const __nv_bfloat162 *>(W + size_t(k0 + u) * p.N);
+        for (int t = 0; t < HG_TOK; ++t) acc[t][0] = acc[t][1] = 0.f;
+        for (int k0 = k0w; k0 < k0w + kw; k0 += 8) {
+            float2 wf[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int t = g + 8 * j;
+            for (int u = 0; u < 8; ++u)
+                wf[u] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(W + size_t(k0 + u) * p.N));
+#pragma unroll
+            for (int t = 0; t < HG_TOK; ++t) {
                 if (t >= nt) break;
                 const uint4 xv = *reinterpret_cast<const uint4 *>(xs + size_t(t) * p.K + k0);
                 const __nv_bfloat162 *x2 = reinterpret_cast<const __nv_bfloat162 *>(&xv);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float2 xf = __bfloat1622float2(x2[u]);
-                    const float2 w0 = __bfloat1622float2(wv[2 * u]), w1 = __bfloat1622float2(wv[2 * u + 1]);
-                    acc[j][0] = fmaf(xf.x, w0.x, fmaf(xf.y, w1.x, acc[j][0]));
-                    acc[j][1] = fmaf(xf.x, w0.y, fmaf(xf.y, w1.y, acc[j][1]));
+                    acc[t][0] = fmaf(xf.x, wf[2 * u].x, fmaf(xf.y, wf[2 * u + 1].x, acc[t][0]));
+                    acc[t][1] = fmaf(xf.x, wf[2 * u].y, fmaf(xf.y, wf[2 * u + 1].y, acc[t][1]));
                 }
             }
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int t = g + 8 * j;
+        for (int t = 0; t < HG_TOK; ++t) {
             if (t >= nt) break;
-            *reinterpret_cast<__nv_bfloat162 *>(p.y + (t0 + t) * p.ys_t + h * p.ys_h + n0 + 2 * c) =
-                __floats2bfloat162_rn(acc[j][0], acc[j][1]);
+            *reinterpret_cast<float2 *>(red + (size_t(warp) * HG_TOK + t) * HG_COLS + 2 * c) =
+                make_float2(acc[t][0], acc[t][1]);
+        }
+        __syncthreads();
+        for (int i = tid; i < nt * 32; i += MP_THREADS) {   // (token, column pair): the warps' sums in warp order
+            const int t = i / 32, cc = i % 32;
+            float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float2 v = *reinterpret_cast<const float2 *>(red + (size_t(w) * HG_TOK + t) * HG_COLS + 2 * cc);
+                s.x += v.x;
+                s.y += v.y;
+            }
+            *reinterpret_cast<__nv_bfloat162 *>(p.y + (t0 + t) * p.ys_t + h * p.ys_h + n0 + 2 * cc) =
+                __floats2bfloat162_rn(s.x, s.y);
         }
     }
 }
@@ -233,9 +250,9 @@ int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream) {
 int xt_head_gemm(const HeadGemmParams *pp, int heads, cudaStream_t stream) {
     const HeadGemmParams &p = *pp;
     if (p.T <= 0) return 0;
-    if (p.N % HG_COLS || p.K % 8 || p.K > 1024 || p.xs_t % 8 || p.xs_h % 8 || p.ys_h % 2 || p.ys_t % 2) return -2;
+    if (p.N % HG_COLS || p.K % 64 || p.K > 1024 || p.xs_t % 8 || p.xs_h % 8 || p.ys_h % 2 || p.ys_t % 2) return -2;
     if (p.rope_dims && (!p.pos || p.rope_dims % 2)) return -2;
-    const int smem = HG_TOK * p.K * 2;
+    const int smem = HG_TOK * p.K * 2 + (MP_THREADS / 32) * HG_TOK * HG_COLS * 4;
     if (xt_smem_optin(head_gemm_kernel, smem) != cudaSuccess) return -4;
     dim3 grid(heads, p.N / HG_COLS + (p.rope_dims ? 1 : 0));
     const cudaError_t e = xt_launch(head_gemm_kernel, grid, dim3(MP_THREADS), size_t(smem), stream, p);

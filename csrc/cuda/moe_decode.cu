@@ -768,10 +768,12 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
         dest[i] = s < 0 ? -1 : s / p.El;   // -1: the CPU tier computes this route (not dispatched)
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    // slot of route i in its destination's region for this source (route order); only this CTA's routes
+    for (int i = blockIdx.x * nw + (threadIdx.x >> 5); i < n; i += gridDim.x * nw) {
         int c = 0;
-        for (int j = 0; j < i; ++j) c += dest[j] == dest[i];
-        pos[i] = c;   // slot of route i in its destination's region for this source (route order)
+        for (int j = lane; j < i; j += 32) c += dest[j] == dest[i];
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (lane == 0) pos[i] = c;
     }
     __syncthreads();
     for (int i = blockIdx.x * nw + warp; i < n; i += gridDim.x * nw) {
@@ -1131,19 +1133,41 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
     __syncthreads();
     const float *ret = reinterpret_cast<const float *>(ep_buf(p, p.rank) + p.off_ret);
     const unsigned mask = gpu_mask;
-    for (int h = threadIdx.x; h < p.H; h += blockDim.x) {
-        float v = 0.f;
-        if (ok)
-            for (int j = 0; j < p.k; ++j)
-                if (mask >> j & 1) v += __ldcv(ret + (size_t(t) * p.k + j) * p.H + h);
-        if (cpu_ok) {
-            float c;
-            asm volatile("ld.volatile.global.f32 %0, [%1];\n" : "=f"(c) : "l"(p.mb.y + size_t(t) * p.H + h));
-            v += c;
-        }
-        if (p.add) v += __bfloat162float(p.add[size_t(t) * p.H + h]);
-        p.out[size_t(t) * p.H + h] = __float2bfloat16(v);
+    const int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4;   // four consecutive outputs per thread
+    if (h >= p.H) return;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ok)
+        for (int j = 0; j < p.k; ++j)
+            if (mask >> j & 1) {
+                const float4 r = __ldcv(reinterpret_cast<const float4 *>(ret + (size_t(t) * p.k + j) * p.H + h));
+                v.x += r.x;
+                v.y += r.y;
+                v.z += r.z;
+                v.w += r.w;
+            }
+    const size_t o = size_t(t) * p.H + h;
+    if (cpu_ok) {
+        float4 c;
+        asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+                     : "=f"(c.x), "=f"(c.y), "=f"(c.z), "=f"(c.w)
+                     : "l"(p.mb.y + o));
+        v.x += c.x;
+        v.y += c.y;
+        v.z += c.z;
+        v.w += c.w;
     }
+    if (p.add) {
+        const uint2 a = *reinterpret_cast<const uint2 *>(p.add + o);
+        const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.x));
+        const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.y));
+        v.x += a0.x;
+        v.y += a0.y;
+        v.z += a1.x;
+        v.w += a1.y;
+    }
+    const __nv_bfloat162 r0 = __floats2bfloat162_rn(v.x, v.y), r1 = __floats2bfloat162_rn(v.z, v.w);
+    *reinterpret_cast<uint2 *>(p.out + o) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&r0), *reinterpret_cast<const uint32_t *>(&r1));
 }
 
 }  // namespace xt
@@ -1154,12 +1178,12 @@ extern "C" int xt_ep_moe(const EpParams *pp, int phase, cudaStream_t stream) {
     if (p.use_mb && p.T > XT_MB_MAX_TOKENS) return -2;
     if (phase == 0) {
         const int n = p.T * p.k;
-        const int grid = n < 8 ? 1 : (n + 63) / 64 > 64 ? 64 : (n + 63) / 64;
+        const int grid = (n + 7) / 8;   // one warp per route
         ep_dispatch_kernel<<<grid, 256, 0, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
     if (phase == 3) {
-        ep_combine_kernel<<<p.T, 256, 0, stream>>>(p);
+        ep_combine_kernel<<<dim3(p.T, (p.H / 4 + 255) / 256), 256, 0, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
     {
