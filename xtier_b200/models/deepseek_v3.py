@@ -82,9 +82,9 @@ class DeepSeekV3Config:
     def moe_layers(self) -> int:
         return self.layers - self.dense_layers
 
-    def dense_bytes(self) -> int:
+    def dense_bytes(self, indexer: bool = False) -> int:
         """Bytes of everything but the routed experts (BF16 attention, dense MLPs, embeddings, shared experts,
-        routers, norms)."""
+        routers, norms; with `indexer`, the DSA indexer's projections)."""
         H = self.hidden
         qk = self.qk_nope + self.qk_rope
         attn = (H * (self.q_lora + self.kv_lora + self.qk_rope) + self.heads * qk * self.q_lora +
@@ -92,7 +92,9 @@ class DeepSeekV3Config:
                 H * self.heads * self.v_head) * 2
         mlp = 3 * H * self.dense_inter * 2
         moe = self.shared * self.expert_bytes() + self.experts * H * 2
-        return self.layers * attn + self.dense_layers * mlp + self.moe_layers() * moe + 2 * self.vocab * H * 2
+        idx = (self.index_heads * self.index_dim * self.q_lora + self.index_dim * H + self.index_heads * H) * 2
+        return (self.layers * (attn + (idx if indexer else 0)) + self.dense_layers * mlp + self.moe_layers() * moe +
+                2 * self.vocab * H * 2)
 
 
 def _rope(x: torch.Tensor, pos: torch.Tensor, theta: float) -> torch.Tensor:
@@ -163,13 +165,14 @@ def ep_layout(E: int, world: int, gpu_per_rank: int, seed: int, stride: int | No
 class DeepSeekV3Model:
     def __init__(self, cfg: DeepSeekV3Config, device='cuda', seed: int = 0, moe_factory=None, max_tokens: int = 64,
                  ep: bool = False, gpu_experts: int | None = None, mailbox=None, engine_threads: int | None = None,
-                 decode_tokens: int = 16, ep_timeout_s: float = 30.0):
+                 decode_tokens: int = 16, ep_timeout_s: float = 30.0, indexer: bool = False):
         """moe_factory(layer, router_w, corr_bias, experts_fn, shared_experts) -> an MoE layer with .forward(x, out);
         experts_fn(ids) generates the quantized experts (synthetic MXFP4 bytes) of the given expert ids.
         Default: every expert on this GPU (TieredMoE, all hot).
         ep: expert parallelism over the process group (world 1 allowed); `gpu_experts` pool slots per rank and MoE
         layer (default: every owned expert), the rest in the CPU tier through `mailbox` (required then) with
-        `engine_threads` workers; `decode_tokens` tokens per rank and step."""
+        `engine_threads` workers; `decode_tokens` tokens per rank and step. indexer: build the DSA indexer's
+        projections whatever the decode attention (the sparse prefill needs them)."""
         self.cfg = cfg
         dev = self.device = torch.device(device)
         g = torch.Generator(device='cpu').manual_seed(seed)
@@ -209,7 +212,7 @@ class DeepSeekV3Model:
                      w_uk=randn(cfg.heads, cfg.qk_nope, cfg.kv_lora),      # [h, nope, lora]
                      w_uvT=randn(cfg.heads, cfg.kv_lora, cfg.v_head),      # [h, lora, v] (W_uv transposed)
                      o=randn(H, cfg.heads * cfg.v_head))
-            if cfg.attn == 'dsa':   # own seeds: the other weights are the same with and without the indexer
+            if cfg.attn == 'dsa' or indexer:   # own seeds: the other weights are the same with and without it
                 gi = torch.Generator(device=dev).manual_seed(seed * 7919 + li)
                 L['idx_q'] = (torch.randn(cfg.index_heads * cfg.index_dim, cfg.q_lora, device=dev, generator=gi)
                               * cfg.std).bfloat16()
