@@ -125,7 +125,7 @@ class Ctx:
         torch.cuda.set_device(self.local)
         if self.world > 1:
             from datetime import timedelta
-            dist.init_process_group('nccl', timeout=timedelta(seconds=600),
+            dist.init_process_group('nccl', timeout=timedelta(seconds=300),
                                     device_id=torch.device('cuda', self.local))
         # CPU partition of this rank (NUMA node of its GPU when the node has enough of them): engine workers, the
         # main thread, the mailbox dispatcher (xtier_b200/engine/placement.py)
@@ -186,6 +186,14 @@ class Ctx:
                 gen.check()
         return ms, e2e_s, clocks.summary()
 
+    def gather_tokens(self, t) -> list[int]:
+        torch = self.torch
+        if self.world == 1:
+            return t.cpu().tolist()
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        self.dist.all_gather(out, t.contiguous())
+        return torch.cat(out).cpu().tolist()
+
     def close(self):
         if self.world > 1:
             self.dist.barrier()
@@ -241,13 +249,14 @@ def run_config3(args, ctx: Ctx) -> dict:
             raise SystemExit(f'bench: the CPU tier needs {need / GB:.1f} GB of host memory per rank, '
                              f'{avail / GB:.1f} GB is available')
     mailbox = Mailbox(cfg.hidden) if cpu_per_layer else None
+    with_ttft = args.ttft and not cpu_per_layer   # the sparse prefill needs every expert in some GPU's HBM
     if rank == 0:
         print(f'bench: config 3 at {world} GPU(s): {B} requests per rank, {gpu_per_rank} of {El} experts per rank and '
               f'layer in HBM ({free / GB:.1f} GB free), CPU tier {cpu_per_layer} experts per layer '
               f'({cpu_bytes / GB:.1f} GB per rank)', file=sys.stderr, flush=True)
     t0 = time.time()
     model = DeepSeekV3Model(cfg, device='cuda', seed=1234, ep=True, gpu_experts=gpu_per_rank, mailbox=mailbox,
-                            engine_threads=ctx.threads, decode_tokens=B)
+                            engine_threads=ctx.threads, decode_tokens=B, indexer=with_ttft)
     if mailbox is not None:
         mailbox.start(cpu=ctx.place.dispatcher)
     os.sched_setaffinity(0, [ctx.place.main])   # main thread off the workers' CPUs
@@ -255,8 +264,10 @@ def run_config3(args, ctx: Ctx) -> dict:
     if rank == 0:
         print(f'bench: model built in {build_s:.1f} s', file=sys.stderr, flush=True)
     gen = Generator(model, batch=B, max_len=max_len)
-    model.fill_synthetic_cache(gen.state, fill, seed=rank)
-    toks = torch.randint(0, cfg.vocab, (B,), generator=torch.Generator().manual_seed(100 + rank))
+    # the 32 requests (input tokens and caches) do not depend on N: rank r serves requests r * B .. r * B + B - 1
+    model.fill_synthetic_cache(gen.state, fill, seed=11, first_request=rank * B)
+    toks = torch.randint(0, cfg.vocab, (args.requests,), generator=torch.Generator().manual_seed(100))
+    toks = toks[rank * B:(rank + 1) * B].contiguous()
     gen.buf['tokens'].copy_(toks)
     gen.host_tokens.copy_(toks)
     gen.buf['pos'].fill_(fill)
@@ -264,6 +275,10 @@ def run_config3(args, ctx: Ctx) -> dict:
     launches = graph_launches(gen)
     if args.profile:
         return profile_steps(gen, args, ctx)
+    # the first step's next token of every request, gathered: the same job at every N gives the same tokens (up to
+    # the CPU tier's FP32 arithmetic at 1 and 2 GPUs)
+    gen.step()
+    first_tokens = ctx.gather_tokens(gen.buf['next'])
     ms, e2e_s, clocks = ctx.timed_decode(gen, args)
     ms_per_step = ms / args.steps
     value = args.requests * args.steps / (ms / 1000.0)
@@ -274,6 +289,17 @@ def run_config3(args, ctx: Ctx) -> dict:
                'api': 'Generator.decode_one (each rank: pinned H2D of its requests\' tokens, replay, D2H of the next)'}
     mb = mailbox.stats() if mailbox is not None else {}
     gpu_experts_bytes = gpu_per_rank * cfg.moe_layers() * cfg.expert_bytes()
+    gen.graph = None
+    if with_ttft:
+        del gen
+        torch.cuda.empty_cache()
+        ttft = time_ttft(args, ctx, model)
+    elif args.ttft:
+        ttft = {'tokens': args.ttft_tokens,
+                'unavailable': f'the prefill computes every expert on a GPU; at {world} GPU(s) '
+                               f'{cpu_per_layer} experts per layer live in host RAM (the decode CPU tier)'}
+    else:
+        ttft = None
     line = {
         'metric': METRIC, 'value': round(value, 2), 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(ms_per_step, 4), 'higher_is_better': True, 'scaling': 'strong',
@@ -299,13 +325,48 @@ def run_config3(args, ctx: Ctx) -> dict:
         'graph_kernels': launches,
         'mailbox': {'calls': mb.get('calls'), 'mean_us': round(mb.get('mean_us', 0) or 0, 2)},
         'setup_s': {'build': round(build_s, 1)},
-        'ttft_64k': None,
+        'first_step_tokens': first_tokens,
+        'ttft_64k': ttft,
     }
-    gen.graph = None
     if mailbox is not None:
         mailbox.stop()
     model.close()
     return line
+
+
+def time_ttft(args, ctx: Ctx, model) -> dict:
+    """time to first token of one random-id prompt of --ttft-tokens tokens with DSA sparse
+    attention (index top-2048) over the group (models/deepseek_prefill.py). One untimed run (allocations), then one
+    timed by CUDA events between barriers, max over ranks."""
+    torch = ctx.torch
+    from xtier_b200.models.deepseek_prefill import SparsePrefill
+    T = args.ttft_tokens
+    try:
+        sp = SparsePrefill(model, T, q_chunk=args.ttft_q_chunk, attn_chunk=128, moe_chunk=4096)
+        ids = torch.randint(0, model.cfg.vocab, (T,), generator=torch.Generator().manual_seed(77))
+        mine = ids[ctx.rank * sp.Tl:(ctx.rank + 1) * sp.Tl].cuda()
+        t0 = time.time()
+        first = sp.run(mine)
+        ctx.barrier()
+        warm_s = time.time() - t0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx.barrier()
+        e0.record()
+        first = sp.run(mine)
+        e1.record()
+        ctx.barrier()
+        sp.check()
+        ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+        tok = int(ctx.max_over_ranks(float(first[0])))
+    except Exception as e:   # reported in the line; the decode measurement above stands
+        return {'tokens': T, 'error': f'{type(e).__name__}: {e}'[:300]}
+    return {'tokens': T, 'ttft_ms': round(ms, 1), 'tok_s': round(T / ms * 1e3, 1), 'first_token': tok,
+            'untimed_first_run_s': round(warm_s, 1),
+            'parallelism': f'sequence-parallel attention over {ctx.world} rank(s) (latent + index caches all-gathered), '
+                           f'expert-parallel MoE (all-to-all, grouped FP4 tcgen05 GEMM)',
+            'attention': f'DSA: FP8 lightning indexer (64 heads x 128), top-{sp.topk} keys per query, tcgen05 MLA '
+                         f'over the NVFP4 latent cache',
+            'timing': 'warm (second run), device events, max over ranks'}
 
 
 def profile_steps(gen, args, ctx):
@@ -411,6 +472,10 @@ def main():
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-peer', action='store_true', help='config 2, N > 1: no node-wide slot pool')
     ap.add_argument('--profile', type=int, default=0, help='print per-kernel device time of N graph replays and exit')
+    ap.add_argument('--no-ttft', dest='ttft', action='store_false',
+                    help='config 3: skip the 64K-prefill time to first token (config 4, same model)')
+    ap.add_argument('--ttft-tokens', type=int, default=65536)
+    ap.add_argument('--ttft-q-chunk', type=int, default=1024, help='queries per indexer / attention chunk')
     args = ap.parse_args()
     if args.impl == 'reference':
         return reference_arm(args)

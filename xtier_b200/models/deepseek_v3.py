@@ -131,6 +131,17 @@ def synthetic_into(ew: formats.ExpertWeights, gen: torch.Generator, std: float):
     ew.g2.fill_(1.0)
 
 
+def synthetic_experts_by_id(ew: formats.ExpertWeights, ids, seed: int, std: float):
+    """Random experts in place, expert ew[i] drawn from a generator seeded by (seed, ids[i]): the bytes of an expert do
+    not depend on where it is placed (which rank's pool, the GPU or the CPU tier), so a model is the same at any GPU
+    count."""
+    synthetic_into(ew, torch.Generator(device=ew.w13.device).manual_seed(seed), std)   # scales
+    for i, e in enumerate(ids):
+        g = torch.Generator(device=ew.w13.device).manual_seed(seed * 1000003 + int(e))
+        _fill_random_codes(ew.w13[i], g)
+        _fill_random_codes(ew.w2[i], g)
+
+
 def empty_experts(n: int, H: int, I: int, fmt: str, device, pin: bool = False) -> formats.ExpertWeights:
     bs = formats.BLOCK[fmt]
     kw = dict(device=device, pin_memory=pin) if str(device) == 'cpu' else dict(device=device)
@@ -254,9 +265,8 @@ class DeepSeekV3Model:
         cfg = self.cfg
         H, I, E = cfg.hidden, cfg.inter, cfg.experts
         table, pools, cpu_ids = ep_layout(E, self.ep_world, self.gpu_per_rank, seed_l, stride=self.ep.spr)
-        gen = torch.Generator(device=self.device).manual_seed(seed_l * 31 + self.ep_rank)
         local = empty_experts(len(pools[self.ep_rank]), H, I, cfg.fmt, self.device)
-        synthetic_into(local, gen, cfg.std)
+        synthetic_experts_by_id(local, pools[self.ep_rank], seed_l, cfg.std)
         engine = None
         if cpu_ids:
             from ..engine import CpuEngine
@@ -267,11 +277,10 @@ class DeepSeekV3Model:
             # slots filled chunk by chunk (no host copy of a whole layer); the CPU tier's bytes are the same on every
             # rank (every rank's engine holds all of them)
             engine = CpuEngine(stage, threads=threads, slots=n, resident=cpu_ids, total_experts=E, fill=False)
-            gc = torch.Generator(device=self.device).manual_seed(seed_l * 31 + 7777)
             for s in range(0, n, chunk):
                 e = min(n, s + chunk)
                 tmp = empty_experts(e - s, H, I, cfg.fmt, self.device)
-                synthetic_into(tmp, gc, cfg.std)
+                synthetic_experts_by_id(tmp, cpu_ids[s:e], seed_l, cfg.std)
                 for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
                     getattr(stage, f)[:e - s].copy_(getattr(tmp, f))
                 del tmp
@@ -312,19 +321,19 @@ class DeepSeekV3Model:
                 st['index'] = [IndexCache(batch, max_len, self.device) for _ in self.layers]
         return st
 
-    def fill_synthetic_cache(self, st: dict, length: int, seed: int = 0):
+    def fill_synthetic_cache(self, st: dict, length: int, seed: int = 0, first_request: int = 0):
         """Writes random latent rows (N(0, 1) latent values, rotary keys) for positions [0, length) of every row
         of every layer and sets the lengths: the state a `length`-token prompt leaves, for decode benchmarks whose
-        prompts are random ids (their prefill is measured on its own)."""
+        prompts are random ids (their prefill is measured on its own). Row b holds request first_request + b, whose
+        rows are drawn from (seed, layer, request) alone, so a request's cache is the same on any rank."""
         cfg = self.cfg
         B = st['batch']
-        g = torch.Generator(device=self.device).manual_seed(seed)
-        slots = (torch.arange(B, device=self.device)[:, None] * st['max_len'] +
-                 torch.arange(length, device=self.device)[None]).reshape(-1)
+        pos = torch.arange(length, device=self.device)
         for li in range(len(self.layers)):
-            for s in range(0, slots.numel(), 1 << 16):
-                sl = slots[s:s + (1 << 16)]
-                lat = torch.randn(sl.numel(), cfg.kv_lora + cfg.qk_rope, device=self.device, generator=g).bfloat16()
+            for b in range(B):
+                g = torch.Generator(device=self.device).manual_seed((seed * 1009 + li) * 100003 + first_request + b)
+                lat = torch.randn(length, cfg.kv_lora + cfg.qk_rope, device=self.device, generator=g).bfloat16()
+                sl = b * st['max_len'] + pos
                 if 'latent' in st:
                     st['latent'][li].write(lat, sl)
                 if 'cache' in st:
