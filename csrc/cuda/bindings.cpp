@@ -510,6 +510,27 @@ void mla_decode(const Tensor &q, const Tensor &idx, const Tensor &codes, const T
              "mla_decode");
 }
 
+void mla_flash(const Tensor &q, const Tensor &idx, const Tensor &codes, const Tensor &scales, const Tensor &rope,
+               const std::optional<Tensor> &part_o, const std::optional<Tensor> &part_ml, const Tensor &out,
+               double scale, int64_t splits, const Tensor &err) {
+    cuda_contig(q, "q");
+    cuda_contig(idx, "idx");
+    cuda_contig(out, "out");
+    const int64_t Q = q.size(0), nsel = idx.size(1);
+    check(q.size(1) == 128 && q.size(2) == 576 && idx.size(0) == Q && idx.scalar_type() == at::kInt && nsel % 64 == 0,
+          "mla_flash q [Q, 128, 576] bf16, idx [Q, nsel] int32 (nsel % 64 == 0)");
+    check(out.numel() == Q * 128 * 512, "mla_flash out [Q, 128, 512]");
+    const int64_t nblk = nsel / 64, bps = (nblk + splits - 1) / splits, eff = (nblk + bps - 1) / bps;
+    if (eff > 1)
+        check(part_o && part_ml && part_o->numel() >= Q * eff * 128 * 512 && part_ml->numel() >= Q * eff * 128 * 2,
+              "mla_flash: split partials too small");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_mla_flash(q.data_ptr(), ptr<const int32_t>(idx), int(Q), int(nsel), codes.data_ptr(), scales.data_ptr(),
+                          rope.data_ptr(), optr<float>(part_o), optr<float>(part_ml), out.data_ptr(), float(scale),
+                          int(splits), ptr<int>(err), stream()),
+             "mla_flash");
+}
+
 void dsa_key_write(const Tensor &k, const Tensor &slot, const Tensor &codes, const Tensor &kscale) {
     cuda_contig(k, "k");
     check(k.size(-1) == 128 && slot.scalar_type() == at::kLong && slot.numel() == k.size(0) &&
@@ -689,6 +710,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("dsa_index_tc(Tensor q8, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, Tensor(a!) scores, "
           "int nq, Tensor(b!) err) -> ()");
     m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");
+    m.def("mla_flash(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!)? part_o, "
+          "Tensor(b!)? part_ml, Tensor(c!) out, float scale, int splits, Tensor(d!) err) -> ()");
     m.def("mla_decode(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!) kg, Tensor(b!) vt, "
           "Tensor(c!) part_o, Tensor(d!) part_ml, Tensor(e!) out, float scale, Tensor(f!) err) -> ()");
     m.def("gemm_rs(Tensor a, Tensor b, Tensor peer, Tensor(a!) state, Tensor? residual, Tensor(b!) out, "
@@ -728,6 +751,7 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("l2_prefetch", &l2_prefetch);
     m.impl("mla_kv_write", &mla_kv_write);
     m.impl("mla_decode", &mla_decode);
+    m.impl("mla_flash", &mla_flash);
     m.impl("dsa_key_write", &dsa_key_write);
     m.impl("dsa_index_decode", &dsa_index_decode);
     m.impl("topk_rows", &topk_rows);

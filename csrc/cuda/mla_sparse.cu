@@ -355,6 +355,391 @@ __global__ void __launch_bounds__(MLA_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------------------------------------ flash attention
+// mla_flash: the selected keys of a query in one pass, online softmax, O accumulated in TMEM. One CTA per (value half
+// j, key split s, query q); 320 threads:
+//   warp 0      MMA issuer (lane 0). Per 64-key block b: S = Q.K^T over the other value half's four k-blocks and the
+//               rotary one (ring tiles), then O += P.V of block b - 1, then S over this half's four k-blocks (the V
+//               tile, read as K^T here and in place through an MN-major descriptor by P.V: no transposed copy)
+//   warp 1      TMEM owner (512 columns: O half at 0..255, S buffers at 256..319 and 320..383)
+//   warps 2-5   producers: TMA of the query's nine k-blocks once (the query stays in shared memory), and the gather
+//               of every block's latent rows (NVFP4 -> BF16, rotary part BF16) into 128-byte-swizzled K-major tiles;
+//               a block's rows are loaded into registers while the previous block is written
+//   warps 6-9   softmax, one head row per thread: block max, lazy correction of O (only when the running max grows by
+//               more than 2^8; then O and the row sum are rescaled in TMEM), P = exp2(S - m) in BF16 into shared
+//               memory, and the epilogue (O / l, or the unnormalized split partial with m and l for mla_merge)
+// Every wait is bounded; a wait that runs out sets the error word, raises the CTA's abort flag and every role winds
+// down (the output of that query is then meaningless and the caller raises).
+constexpr int MF_NB = 64;
+constexpr int MF_STAGES = 3;
+constexpr int MF_THREADS = 320;
+constexpr float MF_TAU = 8.f;   // log2 of the growth of the running max tolerated before O is rescaled
+
+struct MfSmem {
+    static constexpr int QKB = MLA_H * 64 * 2;     // 16 KB: a query k-block [128 heads x 64 dims]
+    static constexpr int Q = 9 * QKB;              // the whole query, resident
+    static constexpr int KKB = MF_NB * 64 * 2;     // 8 KB: a key k-block [64 keys x 64 dims]
+    static constexpr int VBUF = 4 * KKB;           // the value half's four k-blocks of one key block
+    static constexpr int P_BYTES = MLA_H * MF_NB * 2;
+    static constexpr int BYTES = Q + MF_STAGES * KKB + VBUF + P_BYTES + 1024 + 1024;
+};
+
+// k-block of position i (0..8) in a block's order: the other half's four, the rotary one, then this half's four (the
+// ones the V tile keeps)
+XT_DEV int mf_kb(int i, int j) { return i < 4 ? 4 * (1 - j) + i : i == 4 ? 8 : 4 * j + (i - 5); }
+
+__global__ void __launch_bounds__(MF_THREADS, 1)
+    mla_flash_kernel(const __grid_constant__ CUtensorMap tma_q, const int32_t *__restrict__ idx, int nsel, int bps,
+                     int nblk, const uint8_t *__restrict__ codes, const uint8_t *__restrict__ scales,
+                     const __nv_bfloat16 *__restrict__ rope, float scale_log2, __nv_bfloat16 *__restrict__ out,
+                     float *__restrict__ part_o, float *__restrict__ part_ml, int *error) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *qs = smem;                                   // [9][128 x 64]
+    uint8_t *ring = qs + MfSmem::Q;                       // [STAGES][64 x 64]
+    uint8_t *vbuf = ring + MF_STAGES * MfSmem::KKB;       // [4][64 x 64]
+    uint8_t *ps = vbuf + MfSmem::VBUF;
+    uint64_t *full = reinterpret_cast<uint64_t *>(ps + MfSmem::P_BYTES);
+    uint64_t *empty = full + MF_STAGES;
+    uint64_t *qfull = empty + MF_STAGES;
+    uint64_t *vfull = qfull + 1;
+    uint64_t *vfree = vfull + 1;
+    uint64_t *sfull = vfree + 1;           // [2]
+    uint64_t *sfree = sfull + 2;           // [2]
+    uint64_t *pfull = sfree + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfull + 1);
+    __shared__ volatile int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j = blockIdx.x, split = blockIdx.y, q = blockIdx.z, splits = gridDim.y;
+    const int b0 = split * bps, b1 = min(nblk, b0 + bps), nb = b1 - b0;
+    const int32_t *qidx = idx + size_t(q) * nsel;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < MF_STAGES; ++s) {
+            tc::mbar_init(&full[s], 4);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(qfull, 1);
+        tc::mbar_init(vfull, 4);
+        tc::mbar_init(vfree, 1);
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&sfull[s], 1);
+            tc::mbar_init(&sfree[s], 4);
+        }
+        tc::mbar_init(pfull, 4);
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tma_q);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto fail = [&]() {
+        abort_flag = 1;
+        atomicExch(error, 1);
+    };
+
+    if (warp == 0) {
+        if (lane == 0 && nb > 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            const uint32_t idesc_s = tc::idesc_bf16_f32(MLA_H, MF_NB);
+            const uint32_t idesc_o = tc::idesc_bf16_f32(MLA_H, 256) | (1u << 16);   // B (V) MN-major
+            const uint32_t qa = tc::smem_u32(qs), va = tc::smem_u32(vbuf);
+            bool ok = tc::mbar_wait(qfull, 0);
+            auto pv = [&](int bi) {   // O (+)= P . V of block bi (the V tile still holds block bi)
+                if (!(ok = tc::mbar_wait(pfull, uint32_t(bi & 1)))) return;
+                tc::tc_fence_after();
+                const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_u32(ps));
+#pragma unroll
+                for (int k = 0; k < MF_NB / 16; ++k)
+                    tc::mma_f16(tmem, ad + uint64_t(2 * k),
+                                tc::sw128_mnmajor_desc(va + uint32_t(k * 2048), MfSmem::KKB, 1024), idesc_o,
+                                (bi > 0 || k > 0) ? 1u : 0u);
+                tc::mma_commit(vfree);
+            };
+            auto s_kb = [&](uint32_t sb, int kb, uint32_t baddr, bool first) {
+                const uint64_t ad = tc::sw128_kmajor_desc(qa + uint32_t(kb * MfSmem::QKB));
+                const uint64_t bd = tc::sw128_kmajor_desc(baddr);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    tc::mma_f16(sb, ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc_s, (!first || k > 0) ? 1u : 0u);
+            };
+            for (int bi = 0; bi < nb && ok && !abort_flag; ++bi) {
+                const uint32_t sb = tmem + 256u + uint32_t((bi & 1) * MF_NB);
+                if (!(ok = tc::mbar_wait(&sfree[bi & 1], uint32_t(((bi >> 1) & 1) ^ 1)))) break;
+                tc::tc_fence_after();
+                for (int i = 0; i < 5 && ok; ++i) {   // the ring's k-blocks
+                    if (!(ok = tc::mbar_wait(&full[stage], phase))) break;
+                    tc::tc_fence_after();
+                    s_kb(sb, mf_kb(i, j), tc::smem_u32(ring + stage * MfSmem::KKB), i == 0);
+                    tc::mma_commit(&empty[stage]);
+                    if (++stage == MF_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                if (bi > 0) {   // frees the V tile for this block's own k-blocks
+                    pv(bi - 1);
+                    if (!ok) break;
+                }
+                if (!(ok = tc::mbar_wait(vfull, uint32_t(bi & 1)))) break;
+                tc::tc_fence_after();
+#pragma unroll 1
+                for (int t = 0; t < 4; ++t) s_kb(sb, 4 * j + t, va + uint32_t(t * MfSmem::KKB), false);
+                tc::mma_commit(&sfull[bi & 1]);
+            }
+            if (ok && !abort_flag) pv(nb - 1);
+            if (!ok) fail();
+        }
+    } else if (warp >= 2 && warp < 6) {
+        const int w = warp - 2;
+        const int kk = w * 16 + (lane >> 1), half = lane & 1;   // key of the block, 32-dim half of a k-block
+        if (w == 0 && lane == 0 && nb > 0) {   // the query, once
+            tc::mbar_arrive_expect_tx(qfull, MfSmem::Q);
+            for (int kb = 0; kb < 9; ++kb) tc::tma_load_2d(qs + kb * MfSmem::QKB, &tma_q, qfull, kb * 64, q * MLA_H);
+        }
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        uint4 ncw[8], nrp[4];
+        uint16_t nsc[8];
+        auto load_block = [&](int bi) {   // this key's codes and scales of its half of every latent k-block (in the
+                                          // CTA's order), and its half of the rotary part
+            const int slot = qidx[size_t(b0 + bi) * MF_NB + kk];
+#pragma unroll
+            for (int i = 0; i < 9; ++i) {
+                if (i == 4) continue;
+                const int kb = mf_kb(i, j), r = i < 4 ? i : i - 1;
+                ncw[r] = make_uint4(0, 0, 0, 0);
+                nsc[r] = 0;
+                if (slot >= 0) {
+                    ncw[r] = *reinterpret_cast<const uint4 *>(codes + size_t(slot) * (MLA_L / 2) + kb * 32 + half * 16);
+                    nsc[r] =
+                        *reinterpret_cast<const uint16_t *>(scales + size_t(slot) * (MLA_L / 16) + kb * 4 + half * 2);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                nrp[t] = slot >= 0 ? reinterpret_cast<const uint4 *>(rope + size_t(slot) * MLA_R + half * 32)[t]
+                                   : make_uint4(0, 0, 0, 0);
+        };
+        auto write_kb = [&](uint8_t *dst, const uint4 &cw, uint16_t sc) {   // 32 dims of one latent k-block row
+            const float s0 = e4m3_to_f(uint8_t(sc & 0xFF)), s1 = e4m3_to_f(uint8_t(sc >> 8));
+            const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+            uint8_t *rowp = dst + kk * 128;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                __half2 hh[4];
+                e2m1x8_to_h2(words[t], hh);
+                const float sf = t < 2 ? s0 : s1;
+                __nv_bfloat162 o[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float2 f = __half22float2(hh[u]);
+                    o[u] = __floats2bfloat162_rn(f.x * sf, f.y * sf);
+                }
+                const int c = half * 4 + t;
+                *reinterpret_cast<uint4 *>(rowp + ((c ^ (kk & 7)) << 4)) = *reinterpret_cast<uint4 *>(o);
+            }
+        };
+        if (nb > 0) load_block(0);
+        for (int bi = 0; bi < nb && ok && !abort_flag; ++bi) {
+            uint4 cw[8], rp[4];
+            uint16_t sc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                cw[i] = ncw[i];
+                sc[i] = nsc[i];
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) rp[t] = nrp[t];
+            if (bi + 1 < nb) load_block(bi + 1);
+            // the ring's k-blocks: the other value half's four, then the rotary one
+#pragma unroll
+            for (int i = 0; i < 5; ++i) {
+                int good = 1;
+                if (lane == 0) good = tc::mbar_wait(&empty[stage], phase ^ 1);
+                good = __shfl_sync(0xffffffffu, good, 0);
+                if (!good || abort_flag) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *dst = ring + stage * MfSmem::KKB;
+                if (i < 4) {
+                    write_kb(dst, cw[i], sc[i]);
+                } else {
+                    uint8_t *rowp = dst + kk * 128;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const int c = half * 4 + t;
+                        *reinterpret_cast<uint4 *>(rowp + ((c ^ (kk & 7)) << 4)) = rp[t];
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&full[stage]);
+                if (++stage == MF_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (!ok) break;
+            // this half's four k-blocks into the V tile, once the previous block's P.V has read it
+            int good = 1;
+            if (lane == 0 && bi > 0) good = tc::mbar_wait(vfree, uint32_t((bi - 1) & 1));
+            good = __shfl_sync(0xffffffffu, good, 0);
+            if (!good || abort_flag) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) write_kb(vbuf + t * MfSmem::KKB, cw[4 + t], sc[4 + t]);
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(vfull);
+        }
+        if (!ok && lane == 0) fail();
+    } else if (warp >= 6) {
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;   // head
+        const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        int ilo = nb > 0 ? qidx[size_t(b0) * MF_NB + lane] : -1;
+        int ihi = nb > 0 ? qidx[size_t(b0) * MF_NB + 32 + lane] : -1;
+        for (int bi = 0; bi < nb && ok; ++bi) {
+            // S(bi) complete; it was issued after P.V of bi - 1, so O is also final for the correction below
+            int good = 1;
+            if (lane == 0) good = tc::mbar_wait(&sfull[bi & 1], uint32_t((bi >> 1) & 1));
+            good = __shfl_sync(0xffffffffu, good, 0);
+            if (!good || abort_flag) {
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            float sv[MF_NB];
+#pragma unroll
+            for (int c = 0; c < MF_NB / 32; ++c) {
+                uint32_t r[32];
+                tc::tmem_ld32(lane_base + 256u + uint32_t((bi & 1) * MF_NB + c * 32), r);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&sfree[bi & 1]);
+            const unsigned vlo = __ballot_sync(0xffffffffu, ilo >= 0);
+            const unsigned vhi = __ballot_sync(0xffffffffu, ihi >= 0);
+            if (bi + 1 < nb) {   // the next block's slots, in flight while this block is processed
+                ilo = qidx[size_t(b0 + bi + 1) * MF_NB + lane];
+                ihi = qidx[size_t(b0 + bi + 1) * MF_NB + 32 + lane];
+            }
+            float bm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < MF_NB; ++i) {
+                const bool v = i < 32 ? (vlo >> i) & 1 : (vhi >> (i - 32)) & 1;
+                sv[i] = v ? sv[i] * scale_log2 : -INFINITY;
+                bm = fmaxf(bm, sv[i]);
+            }
+            const float m_new = fmaxf(m, bm);
+            const bool need = m_new > -INFINITY && (m == -INFINITY || m_new > m + MF_TAU);
+            float factor = 1.f;
+            if (need) {
+                factor = m == -INFINITY ? 0.f : exp2f(m - m_new);
+                m = m_new;
+                l *= factor;
+            }
+            if (bi > 0 && __ballot_sync(0xffffffffu, need)) {
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t r[32];
+                    tc::tmem_ld32(lane_base + uint32_t(c * 32), r);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+                    tc::tmem_st32(lane_base + uint32_t(c * 32), r);
+                }
+                tc::tmem_st_wait();
+            }
+            uint8_t *rowp = ps + row * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                __nv_bfloat162 pv[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int k0 = c * 8 + 2 * t;
+                    const float p0 = m == -INFINITY ? 0.f : exp2f(sv[k0] - m);
+                    const float p1 = m == -INFINITY ? 0.f : exp2f(sv[k0 + 1] - m);
+                    pv[t] = __floats2bfloat162_rn(p0, p1);
+                    const float2 back = __bfloat1622float2(pv[t]);
+                    l += back.x + back.y;
+                }
+                *reinterpret_cast<uint4 *>(rowp + ((c ^ (row & 7)) << 4)) = *reinterpret_cast<uint4 *>(pv);
+            }
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(pfull);
+        }
+        int good = ok ? 1 : 0;
+        if (ok && nb > 0 && lane == 0) good = tc::mbar_wait(vfree, uint32_t((nb - 1) & 1));   // the last P.V
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good && lane == 0) fail();
+        tc::tc_fence_after();
+        const size_t pbase = (size_t(q) * splits + split) * MLA_H + row;
+        if (good && nb > 0 && !abort_flag) {
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {
+                uint32_t r[32];
+                tc::tmem_ld32(lane_base + uint32_t(c * 32), r);
+                tc::tmem_ld_wait();
+                if (splits == 1) {
+                    __nv_bfloat16 *dst = out + (size_t(q) * MLA_H + row) * MLA_L + j * 256 + c * 32;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        __nv_bfloat162 o[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            o[u] = __floats2bfloat162_rn(__uint_as_float(r[8 * v + 2 * u]) * inv,
+                                                         __uint_as_float(r[8 * v + 2 * u + 1]) * inv);
+                        reinterpret_cast<uint4 *>(dst)[v] = *reinterpret_cast<uint4 *>(o);
+                    }
+                } else {
+                    float *dst = part_o + pbase * MLA_L + j * 256 + c * 32;
+#pragma unroll
+                    for (int v = 0; v < 8; ++v)
+                        reinterpret_cast<float4 *>(dst)[v] =
+                            make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                        __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                }
+            }
+        } else if (splits > 1) {
+            for (int c = 0; c < 256; ++c) part_o[pbase * MLA_L + j * 256 + c] = 0.f;
+            m = -INFINITY;
+            l = 0.f;
+        }
+        if (splits > 1 && j == 0) {
+            part_ml[pbase * 2] = (good && nb > 0) ? m : -INFINITY;
+            part_ml[pbase * 2 + 1] = (good && nb > 0) ? l : 0.f;
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ merge
 // grid (heads, queries), 128 threads: thread t -> dims 4t..4t+3
 __global__ void __launch_bounds__(128) mla_merge_kernel(const float *__restrict__ part_o,
@@ -455,6 +840,32 @@ int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void
     dim3 gm(MLA_H, Q);
     mla_merge_kernel<<<gm, 128, 0, stream>>>(part_o, part_ml, nblk, static_cast<__nv_bfloat16 *>(out));
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Flash form of xt_mla_decode: the same inputs, no gather scratch. part_o [Q, splits, 128, 512] f32 and part_ml [Q,
+// splits, 128, 2] are used only when splits > 1 (the splits' partials, merged by mla_merge). nsel % 64 == 0.
+int xt_mla_flash(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
+                 const void *rope, float *part_o, float *part_ml, void *out, float scale, int splits, int *error,
+                 cudaStream_t stream) {
+    if (Q <= 0 || Q > 65535 || nsel <= 0 || nsel % MF_NB || splits < 1) return -2;
+    const int nblk = nsel / MF_NB;
+    const int bps = (nblk + splits - 1) / splits;
+    splits = (nblk + bps - 1) / bps;
+    if (splits > 1 && (!part_o || !part_ml)) return -2;
+    CUtensorMap mq;
+    if (!mla_map(&mq, q, uint64_t(Q) * MLA_H, MLA_D, MLA_H)) return -3;
+    if (xt_smem_optin(mla_flash_kernel, int(MfSmem::BYTES)) != cudaSuccess) return -4;
+    mla_flash_kernel<<<dim3(2, splits, Q), MF_THREADS, MfSmem::BYTES, stream>>>(
+        mq, idx, nsel, bps, nblk, static_cast<const uint8_t *>(codes), static_cast<const uint8_t *>(scales),
+        static_cast<const __nv_bfloat16 *>(rope), scale * 1.4426950408889634f, static_cast<__nv_bfloat16 *>(out),
+        part_o, part_ml, error);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    if (splits > 1) {
+        mla_merge_kernel<<<dim3(MLA_H, Q), 128, 0, stream>>>(part_o, part_ml, splits,
+                                                             static_cast<__nv_bfloat16 *>(out));
+        if (cudaGetLastError() != cudaSuccess) return -1;
+    }
+    return 0;
 }
 
 }  // extern "C"

@@ -206,6 +206,9 @@ int xt_mla_prep(const void *in, int ld, int q_lora, const void *q_norm, const vo
                 void *lat_out, int T, cudaStream_t stream);
 int xt_head_gemm(const xt::HeadGemmParams *p, int heads, cudaStream_t stream);
 int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream);
+int xt_mla_flash(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
+                 const void *rope, float *part_o, float *part_ml, void *out, float scale, int splits, int *error,
+                 cudaStream_t stream);
 int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
                   const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,
                   int *error, cudaStream_t stream);

@@ -101,6 +101,20 @@ XT_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 XT_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
+// 32 consecutive FP32 columns into this thread's TMEM lane.
+XT_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+XT_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
 // Grouped rasterization of a tiles_m x tiles_n grid: runs of `gm` tile rows are walked across all tile columns before
 // the next run starts, so the A rows and B columns that the CTAs in flight touch stay resident in L2 (walking whole
 // column panels would stream all of A from DRAM once per panel).
@@ -186,6 +200,21 @@ XT_DEV uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
     d |= uint64_t(1024 >> 4) << 32;             // stride byte offset [32,46)
     d |= uint64_t(1) << 46;                     // version [46,48)
     d |= uint64_t(2) << 61;                     // layout: SWIZZLE_128B [61,64)
+    return d;
+}
+
+// Shared-memory descriptor of an MN-major operand in 128-byte-swizzle atoms (64 BF16 values of the MN dimension per
+// 128-byte row, 8 rows of K per 1024-byte atom): `lbo` bytes between consecutive 64-value MN chunks, `sbo` bytes
+// between consecutive 8-row K groups. A K-major SW128 tile of [rows x 64] values is, byte for byte, the MN-major SW128
+// tile of its transpose, so one gathered tile serves as the B operand of both S = Q.K^T (K-major) and O = P.V
+// (MN-major).
+XT_DEV uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= uint64_t((smem_addr >> 4) & 0x3FFF);
+    d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+    d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(2) << 61;
     return d;
 }
 

@@ -56,11 +56,11 @@ def test_sparse_prefill_matches_dense_when_topk_covers(cuda_ops):
     try:
         T = 256
         ids = torch.randint(0, cfg.vocab, (T,), generator=torch.Generator().manual_seed(6)).cuda()
-        sp = SparsePrefill(model, T, q_chunk=128, attn_chunk=64, moe_chunk=128)
+        sp = SparsePrefill(model, T, q_chunk=128, moe_chunk=128)
         lg = sp.run(ids, return_logits=True).float()
         torch.cuda.synchronize()
         sp.check()
-        dn = SparsePrefill(model, T, q_chunk=128, attn_chunk=64, moe_chunk=128, dense=True)
+        dn = SparsePrefill(model, T, q_chunk=128, moe_chunk=128, dense=True)
         lg_d = dn.run(ids, return_logits=True).float()
         assert _rel(lg, lg_d) < 3e-2, _rel(lg, lg_d)
     finally:
@@ -78,7 +78,7 @@ def test_sparse_prefill_topk_below_length_runs(cuda_ops):
     try:
         T = 384
         ids = torch.randint(0, cfg.vocab, (T,), generator=torch.Generator().manual_seed(8)).cuda()
-        sp = SparsePrefill(model, T, q_chunk=128, attn_chunk=64, moe_chunk=256)
+        sp = SparsePrefill(model, T, q_chunk=128, moe_chunk=256)
         lg = sp.run(ids, return_logits=True).float()
         torch.cuda.synchronize()
         sp.check()

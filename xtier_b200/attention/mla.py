@@ -76,6 +76,43 @@ def mla_decode(q: torch.Tensor, idx: torch.Tensor, cache: LatentCache, ws: MlaWo
     return out
 
 
+class FlashWorkspace:
+    """Split partials of mla_flash for up to `queries` queries and `splits` key splits (none needed at one split)."""
+
+    def __init__(self, queries: int, splits: int, device='cuda'):
+        self.Q, self.splits = queries, splits
+        n = queries * splits * 128 if splits > 1 else 0
+        self.part_o = torch.empty(n * LATENT, dtype=torch.float32, device=device) if n else None
+        self.part_ml = torch.empty(n * 2, dtype=torch.float32, device=device) if n else None
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+
+
+FLASH_BLOCK = 64
+
+
+def flash_splits(queries: int, nsel: int, sms: int = 148) -> int:
+    """Key splits of mla_flash: enough CTAs (2 value halves x splits x queries) to cover the SMs, at least four 64-key
+    blocks per split."""
+    nblk = max(1, nsel // FLASH_BLOCK)
+    want = max(1, -(-sms // (2 * queries)))
+    return max(1, min(want, nblk // 4 if nblk >= 8 else 1))
+
+
+def mla_flash(q: torch.Tensor, idx: torch.Tensor, cache: LatentCache, scale: float, splits: int = 1,
+              ws: FlashWorkspace | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """mla_decode in one pass (csrc/cuda/mla_sparse.cu mla_flash): q [Q, 128, 576] BF16 (absorbed), idx [Q, nsel]
+    int32 cache slots (-1: none; nsel % 64 == 0) -> latent output [Q, 128, 512]. splits > 1 splits every query's keys
+    over that many CTAs (short query batches) and merges their partials from `ws`."""
+    Q = q.shape[0]
+    out = torch.empty(Q, 128, LATENT, dtype=torch.bfloat16, device=q.device) if out is None else out
+    if ws is None:
+        ws = FlashWorkspace(Q, splits, q.device)
+    ops.load()
+    torch.ops.xtier.mla_flash(q.contiguous(), idx.to(torch.int32).contiguous(), cache.codes, cache.scales,
+                              cache.rope, ws.part_o, ws.part_ml, out, float(scale), int(splits), ws.err)
+    return out
+
+
 def reference_decode(q: torch.Tensor, idx: torch.Tensor, cache: LatentCache, scale: float) -> torch.Tensor:
     """fp32 oracle: per query, softmax(scale * q . k) over its valid slots, times the latent values."""
     outs = []

@@ -9,9 +9,9 @@ dense parts of every layer on its own slice. Per layer:
     position. The two caches of the layer (416 + 132 bytes per token) are then all-gathered, so every rank holds the
     keys of the whole prompt (27 MB + 8.6 MB per layer at 64K tokens: small next to the weights).
   * attention, per chunk of queries: the lightning indexer scores every earlier key on the tensor cores (FP8,
-    `attention/dsa.py`), a radix select keeps each query's top `index_topk` positions, and the tcgen05 MLA kernel
-    attends over exactly those latent rows (`attention/mla.py`); the queries enter absorbed (q_nope . W_uk) and the
-    latent output leaves through W_uv.
+    `attention/dsa.py`), a radix select keeps each query's top `index_topk` positions, and the one-pass tcgen05 MLA
+    kernel (`attention/mla.py` mla_flash) attends over exactly those latent rows; the queries enter absorbed
+    (q_nope . W_uk) and the latent output leaves through W_uv.
   * the MoE, expert parallel: each token's routes (top-8 + the shared expert) are sorted by owner rank, the token rows
     and route weights cross with one all-to-all, the owner runs its pool's experts as grouped FP4 tcgen05 GEMMs
     (`cache/prefill.py`, weights read once per 128 routed tokens), the weighted rows come back with a second
@@ -33,7 +33,7 @@ import torch.distributed as dist
 
 from .. import ops
 from ..attention import dsa
-from ..attention.mla import BLOCK, LatentCache, MlaWorkspace
+from ..attention.mla import BLOCK, FlashWorkspace, LatentCache
 from ..cache.prefill import grouped_routes
 from ..parallel import dist as xdist
 from .deepseek_v3 import DeepSeekV3Model, _rope
@@ -119,8 +119,8 @@ class SparsePrefill:
     dense=True replaces the indexer + sparse attention by causal attention over every earlier key (the expanded form
     of `DeepSeekV3Model._mla_prefill`), the oracle of the tests."""
 
-    def __init__(self, model: DeepSeekV3Model, total: int, q_chunk: int = 1024, attn_chunk: int = 128,
-                 moe_chunk: int = 4096, dense: bool = False):
+    def __init__(self, model: DeepSeekV3Model, total: int, q_chunk: int = 1024, moe_chunk: int = 4096,
+                 dense: bool = False):
         cfg = model.cfg
         env = xdist.get()
         self.model, self.cfg = model, cfg
@@ -128,13 +128,13 @@ class SparsePrefill:
         if total % self.W:
             raise ValueError(f'{total} tokens do not split over {self.W} ranks')
         self.total, self.Tl = total, total // self.W
-        self.q_chunk, self.attn_chunk = q_chunk, attn_chunk
+        self.q_chunk = q_chunk
         self.dense = dense
         self.topk = min(cfg.index_topk, (total + BLOCK - 1) // BLOCK * BLOCK)
         dev = model.device
         self.latent = [LatentCache(1, total, dev) for _ in model.layers]
         self.index = [dsa.IndexCache(1, total, dev) for _ in model.layers]
-        self.ws = MlaWorkspace(attn_chunk, self.topk, dev)
+        self.ws = FlashWorkspace(q_chunk, 1, dev)
         self.moe = EPPrefillMoE(moe_chunk)
         self.scores = torch.empty(q_chunk, total, dtype=torch.float32, device=dev)
         self.idx_err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -181,11 +181,8 @@ class SparsePrefill:
                                   per_cta=2 if C % 2 == 0 else 1)
             idx = dsa.topk(sc, self.topk)
             o_lat = torch.empty(C, cfg.heads, cfg.kv_lora, dtype=torch.bfloat16, device=q.device)
-            for a0 in range(0, C, self.attn_chunk):
-                a1 = min(C, a0 + self.attn_chunk)
-                torch.ops.xtier.mla_decode(qf[a0:a1], idx[a0:a1], lc.codes, lc.scales, lc.rope, self.ws.kg,
-                                           self.ws.vt, self.ws.part_o, self.ws.part_ml, o_lat[a0:a1], float(scale),
-                                           self.ws.err)
+            torch.ops.xtier.mla_flash(qf, idx, lc.codes, lc.scales, lc.rope, None, None, o_lat, float(scale), 1,
+                                      self.ws.err)
             out[c0:c1] = torch.matmul(o_lat.transpose(0, 1), L['w_uvT']).transpose(0, 1).reshape(C, -1)
         return out
 

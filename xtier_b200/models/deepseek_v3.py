@@ -312,10 +312,12 @@ class DeepSeekV3Model:
             st['cache'] = [torch.zeros(batch, max_len, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16,
                                        device=self.device) for _ in self.layers]
         if kern:
-            from ..attention.mla import BLOCK, LatentCache, MlaWorkspace
+            from ..attention.mla import FLASH_BLOCK, FlashWorkspace, LatentCache, flash_splits
             st['latent'] = [LatentCache(batch, max_len, self.device) for _ in self.layers]
-            nsel = cfg.index_topk if cfg.attn == 'dsa' else (max_len + BLOCK - 1) // BLOCK * BLOCK
-            st['mla_ws'] = MlaWorkspace(batch, nsel, self.device)
+            nsel = cfg.index_topk if cfg.attn == 'dsa' else (max_len + FLASH_BLOCK - 1) // FLASH_BLOCK * FLASH_BLOCK
+            st['nsel'] = nsel
+            st['mla_splits'] = flash_splits(batch, nsel)
+            st['mla_ws'] = FlashWorkspace(batch, st['mla_splits'], self.device)
             if cfg.attn == 'dsa':
                 from ..attention.dsa import IndexCache
                 st['index'] = [IndexCache(batch, max_len, self.device) for _ in self.layers]
@@ -377,7 +379,7 @@ class DeepSeekV3Model:
         """Absorbed MLA decode on the tensor cores over the NVFP4 latent cache: every cached position (dense) or the
         DSA indexer's top-k (sparse). q [B, heads, nope+rope] (rotated) -> [B, heads * v]."""
         from ..attention import dsa
-        from ..attention.mla import mla_decode
+        from ..attention.mla import mla_flash
         cfg = self.cfg
         B = q.shape[0]
         qf = torch.empty(B, cfg.heads, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16, device=q.device)
@@ -390,10 +392,10 @@ class DeepSeekV3Model:
             scores = dsa.index_scores(qi, w, st['index'][li], rows, lens)
             idx = dsa.select_slots(scores, rows, cfg.index_topk, st['max_len'])
         else:
-            nsel = st['mla_ws'].nsel
+            nsel = st['nsel']
             pos = torch.arange(nsel, device=q.device, dtype=torch.int32)[None]
             idx = torch.where(pos < lens[:, None], pos + rows[:, None] * st['max_len'], -1).int()
-        o_lat = mla_decode(qf, idx, lc, st['mla_ws'], 1.0 / math.sqrt(cfg.qk_nope + cfg.qk_rope))
+        o_lat = mla_flash(qf, idx, lc, 1.0 / math.sqrt(cfg.qk_nope + cfg.qk_rope), st['mla_splits'], st['mla_ws'])
         out = torch.empty(B, cfg.heads, cfg.v_head, dtype=torch.bfloat16, device=q.device)
         ops.head_gemm(o_lat, L['w_uvT'], out)
         return out.reshape(B, -1)
@@ -511,7 +513,7 @@ class DeepSeekV3Model:
             raise ValueError('the batched decode step attends densely (attn="mla")')
         B = buf['tokens'].shape[0]
         ws = st['mla_ws']
-        nsel = ws.nsel
+        nsel = st['nsel']
         scale = 1.0 / math.sqrt(cfg.qk_nope + cfg.qk_rope)
         # per step: cache slots of the new tokens and the dense key list of every row (the same for all layers)
         if 'idx' not in buf or buf['idx'].shape[1] != nsel:
@@ -535,8 +537,8 @@ class DeepSeekV3Model:
             ops.linear(buf['q_a'], L['q_b'], out=buf['q'].view(B, -1))
             ops.head_gemm(buf['q'], L['w_uk'], buf['qf'], buf['pos'], cfg.qk_nope, cfg.kv_lora, cfg.qk_rope,
                           cfg.rope_theta)
-            torch.ops.xtier.mla_decode(buf['qf'], buf['idx'], lc.codes, lc.scales, lc.rope, ws.kg, ws.vt, ws.part_o,
-                                       ws.part_ml, buf['o_lat'], float(scale), ws.err)
+            torch.ops.xtier.mla_flash(buf['qf'], buf['idx'], lc.codes, lc.scales, lc.rope, ws.part_o, ws.part_ml,
+                                      buf['o_lat'], float(scale), st['mla_splits'], ws.err)
             ops.head_gemm(buf['o_lat'], L['w_uvT'], buf['a'])
             ops.linear(buf['a'].view(B, -1), L['o'], out=buf['o'])
             ops.add_rmsnorm(buf['o'], buf['residual'], L['post_norm'], buf['h'], cfg.eps)
@@ -551,8 +553,10 @@ class DeepSeekV3Model:
         torch.argmax(buf['logits'], dim=-1, out=buf['next'])
         return buf['next']
 
-    def check(self):
-        """Raises when a bounded wait of the last steps ran out (EP exchange, mailbox, MLA)."""
+    def check(self, st: dict | None = None):
+        """Raises when a bounded wait of the last steps ran out (EP exchange, mailbox, MLA of state `st`)."""
+        if st is not None and 'mla_ws' in st and int(st['mla_ws'].err.item()):
+            raise RuntimeError('MLA attention: a bounded wait ran out')
         if self.ep is not None:
             self.ep.check()
         if self.mailbox is not None:
