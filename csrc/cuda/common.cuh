@@ -117,6 +117,20 @@ XT_DEV float2 e4m3x2_to_f2(uint16_t v) {
 
 XT_DEV float e4m3_to_f(uint8_t b) { return e4m3x2_to_f2(uint16_t(b)).x; }
 
+// Two E4M3 bytes (low byte first) -> f16 pair (exact: every E4M3 value is an f16 value)
+XT_DEV __half2 e4m3x2_to_h2(uint16_t v) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;\n" : "=r"(r) : "h"(v));
+    return *reinterpret_cast<__half2 *>(&r);
+}
+
+// 2^x, hardware approximation (results below 2^-126 flush to zero)
+XT_DEV float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 XT_DEV float ue8m0_to_f(uint8_t b) { return b ? __uint_as_float(uint32_t(b) << 23) : 5.877471754e-39f; }
 
 XT_DEV uint4 ldg_nc_v4(const void *p) {

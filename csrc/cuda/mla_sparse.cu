@@ -356,37 +356,59 @@ __global__ void __launch_bounds__(MLA_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ flash attention
-// mla_flash: the selected keys of a query in one pass, online softmax, O accumulated in TMEM. One CTA per (value half
-// j, key split s, query q); 320 threads:
-//   warp 0      MMA issuer (lane 0). Per 64-key block b: S = Q.K^T over the other value half's four k-blocks and the
-//               rotary one (ring tiles), then O += P.V of block b - 1, then S over this half's four k-blocks (the V
-//               tile, read as K^T here and in place through an MN-major descriptor by P.V: no transposed copy)
-//   warp 1      TMEM owner (512 columns: O half at 0..255, S buffers at 256..319 and 320..383)
-//   warps 2-5   producers: TMA of the query's nine k-blocks once (the query stays in shared memory), and the gather
-//               of every block's latent rows (NVFP4 -> BF16, rotary part BF16) into 128-byte-swizzled K-major tiles;
-//               a block's rows are loaded into registers while the previous block is written
-//   warps 6-9   softmax, one head row per thread: block max, lazy correction of O (only when the running max grows by
-//               more than 2^8; then O and the row sum are rescaled in TMEM), P = exp2(S - m) in BF16 into shared
-//               memory, and the epilogue (O / l, or the unnormalized split partial with m and l for mla_merge)
-// Every wait is bounded; a wait that runs out sets the error word, raises the CTA's abort flag and every role winds
-// down (the output of that query is then meaningless and the caller raises).
+// mla_flash: the selected keys of a query in one pass, online softmax, O accumulated in TMEM, FP16 operands. One CTA
+// per (value half j, key split s, query q); 320 threads:
+//   warp 0      MMA issuer (lane 0). Per 64-key block b: S = Q.K^T over the ring's five k-blocks (the other value
+//               half and the rotary one) and this half's four (the V tile of b), then O += P.V of block b - 1 with P
+//               read from TMEM and V read in place through an MN-major descriptor (no transposed copy)
+//   warp 1      TMEM owner (512 columns: O half at 0..255, S buffers at 256 and 320, P buffers at 384 and 416)
+//   warps 2-5   producers: TMA of the query's nine k-blocks once, and the gather of every block's latent rows into
+//               128-byte-swizzled K-major FP16 tiles (E2M1 -> f16 by the hardware conversion, times the block's E4M3
+//               scale in f16: exact, every product has at most six significant bits and lies in f16's normal range;
+//               the rotary part BF16 -> f16); a block's rows are loaded while the previous block is written, and the
+//               slots one block further ahead
+//   warps 6-9   first the query: BF16 -> f16 in place, scaled by the power of two 2^e that puts its largest magnitude
+//               in [2^14, 2^15) (so the conversion is exact down to 2^-28 of the largest element), 2^-e folded into
+//               the softmax scale. Then softmax, one head row per thread: block max, lazy correction of O (only when
+//               the running max grows by more than 2^8; then O and the row sum are rescaled in TMEM once P.V of the
+//               previous block is done), P = 2^(S - m) in f16 into TMEM, the row sum over the rounded P, and the
+//               epilogue (O / l, or the unnormalized split partial with m and l for mla_merge)
+// V is double-buffered, so S of block b does not wait for P.V of block b - 1: the tensor core computes S of b while
+// the softmax warps work on b - 1. Every wait is bounded; a wait that runs out sets the error word, raises the CTA's
+// abort flag and every role winds down (the output of that query is then meaningless and the caller raises).
 constexpr int MF_NB = 64;
-constexpr int MF_STAGES = 3;
+constexpr int MF_STAGES = 2;
 constexpr int MF_THREADS = 320;
-constexpr float MF_TAU = 8.f;   // log2 of the growth of the running max tolerated before O is rescaled
+constexpr float MF_TAU = 8.f;      // log2 of the growth of the running max tolerated before O is rescaled
+constexpr uint32_t MF_TS = 256;    // TMEM column of the S buffers (2 x 64)
+constexpr uint32_t MF_TP = 384;    // TMEM column of the P buffers (2 x 32: 64 f16 per row)
 
 struct MfSmem {
     static constexpr int QKB = MLA_H * 64 * 2;     // 16 KB: a query k-block [128 heads x 64 dims]
     static constexpr int Q = 9 * QKB;              // the whole query, resident
     static constexpr int KKB = MF_NB * 64 * 2;     // 8 KB: a key k-block [64 keys x 64 dims]
-    static constexpr int VBUF = 4 * KKB;           // the value half's four k-blocks of one key block
-    static constexpr int P_BYTES = MLA_H * MF_NB * 2;
-    static constexpr int BYTES = Q + MF_STAGES * KKB + VBUF + P_BYTES + 1024 + 1024;
+    static constexpr int VBUF = 4 * KKB;           // this value half's four k-blocks of one key block
+    static constexpr int BYTES = Q + MF_STAGES * KKB + 2 * VBUF + 1024 + 1024;
 };
+static_assert(MfSmem::BYTES <= 232448, "mla_flash shared memory");
 
-// k-block of position i (0..8) in a block's order: the other half's four, the rotary one, then this half's four (the
-// ones the V tile keeps)
-XT_DEV int mf_kb(int i, int j) { return i < 4 ? 4 * (1 - j) + i : i == 4 ? 8 : 4 * j + (i - 5); }
+// k-block of ring position i (0..4): the other value half's four, then the rotary one
+XT_DEV int mf_kb(int i, int j) { return i < 4 ? 4 * (1 - j) + i : 8; }
+
+// 32 dims (four 16-byte chunks c0..c0+3 of a 128-byte swizzled row) of one NVFP4 latent k-block row -> f16
+XT_DEV void mf_write_kb(uint8_t *rowp, int kk, int c0, const uint4 &cw, uint16_t sc) {
+    const __half2 s2 = e4m3x2_to_h2(sc);
+    const __half2 s0 = __low2half2(s2), s1 = __high2half2(s2);
+    const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        __half2 hh[4];
+        e2m1x8_to_h2(words[t], hh);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) hh[u] = __hmul2(hh[u], t < 2 ? s0 : s1);
+        *reinterpret_cast<uint4 *>(rowp + (((c0 + t) ^ (kk & 7)) << 4)) = *reinterpret_cast<uint4 *>(hh);
+    }
+}
 
 __global__ void __launch_bounds__(MF_THREADS, 1)
     mla_flash_kernel(const __grid_constant__ CUtensorMap tma_q, const int32_t *__restrict__ idx, int nsel, int bps,
@@ -397,18 +419,19 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *qs = smem;                                   // [9][128 x 64]
     uint8_t *ring = qs + MfSmem::Q;                       // [STAGES][64 x 64]
-    uint8_t *vbuf = ring + MF_STAGES * MfSmem::KKB;       // [4][64 x 64]
-    uint8_t *ps = vbuf + MfSmem::VBUF;
-    uint64_t *full = reinterpret_cast<uint64_t *>(ps + MfSmem::P_BYTES);
+    uint8_t *vbuf = ring + MF_STAGES * MfSmem::KKB;       // [2][4][64 x 64]
+    uint64_t *full = reinterpret_cast<uint64_t *>(vbuf + 2 * MfSmem::VBUF);
     uint64_t *empty = full + MF_STAGES;
     uint64_t *qfull = empty + MF_STAGES;
-    uint64_t *vfull = qfull + 1;
-    uint64_t *vfree = vfull + 1;
-    uint64_t *sfull = vfree + 1;           // [2]
+    uint64_t *qready = qfull + 1;
+    uint64_t *vfull = qready + 1;          // [2]
+    uint64_t *vfree = vfull + 2;           // [2]: P.V of the buffer's block done (V tile and P buffer free)
+    uint64_t *sfull = vfree + 2;           // [2]
     uint64_t *sfree = sfull + 2;           // [2]
-    uint64_t *pfull = sfree + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfull + 1);
+    uint64_t *pfull = sfree + 2;           // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfull + 2);
     __shared__ volatile int abort_flag;
+    __shared__ float red[4];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j = blockIdx.x, split = blockIdx.y, q = blockIdx.z, splits = gridDim.y;
@@ -421,13 +444,14 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
             tc::mbar_init(&empty[s], 1);
         }
         tc::mbar_init(qfull, 1);
-        tc::mbar_init(vfull, 4);
-        tc::mbar_init(vfree, 1);
+        tc::mbar_init(qready, 4);
         for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&vfull[s], 4);
+            tc::mbar_init(&vfree[s], 1);
             tc::mbar_init(&sfull[s], 1);
             tc::mbar_init(&sfree[s], 4);
+            tc::mbar_init(&pfull[s], 4);
         }
-        tc::mbar_init(pfull, 4);
         tc::fence_barrier_init();
         tc::prefetch_tmap(&tma_q);
     }
@@ -443,25 +467,32 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
         abort_flag = 1;
         atomicExch(error, 1);
     };
+    // one lane waits, the warp follows; false once the wait ran out or another role failed
+    auto warp_wait = [&](uint64_t *bar, uint32_t parity) {
+        int good = 1;
+        if (lane == 0) good = tc::mbar_wait(bar, parity);
+        good = __shfl_sync(0xffffffffu, good, 0);
+        return good && !abort_flag;
+    };
 
     if (warp == 0) {
         if (lane == 0 && nb > 0) {
             int stage = 0;
             uint32_t phase = 0;
-            const uint32_t idesc_s = tc::idesc_bf16_f32(MLA_H, MF_NB);
-            const uint32_t idesc_o = tc::idesc_bf16_f32(MLA_H, 256) | (1u << 16);   // B (V) MN-major
+            const uint32_t idesc_s = tc::idesc_f16_f32(MLA_H, MF_NB);
+            const uint32_t idesc_o = tc::idesc_f16_f32(MLA_H, 256) | (1u << 16);   // B (V) MN-major
             const uint32_t qa = tc::smem_u32(qs), va = tc::smem_u32(vbuf);
-            bool ok = tc::mbar_wait(qfull, 0);
-            auto pv = [&](int bi) {   // O (+)= P . V of block bi (the V tile still holds block bi)
-                if (!(ok = tc::mbar_wait(pfull, uint32_t(bi & 1)))) return;
+            bool ok = tc::mbar_wait(qready, 0);
+            auto pv = [&](int b) {   // O (+)= P . V of block b; its completion frees the V tile and P buffer of b
+                if (!(ok = tc::mbar_wait(&pfull[b & 1], uint32_t((b >> 1) & 1)))) return;
                 tc::tc_fence_after();
-                const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_u32(ps));
+                const uint32_t pa = tmem + MF_TP + uint32_t((b & 1) * 32);
+                const uint32_t vb = va + uint32_t((b & 1) * MfSmem::VBUF);
 #pragma unroll
                 for (int k = 0; k < MF_NB / 16; ++k)
-                    tc::mma_f16(tmem, ad + uint64_t(2 * k),
-                                tc::sw128_mnmajor_desc(va + uint32_t(k * 2048), MfSmem::KKB, 1024), idesc_o,
-                                (bi > 0 || k > 0) ? 1u : 0u);
-                tc::mma_commit(vfree);
+                    tc::mma_f16_ts(tmem, pa + uint32_t(8 * k), tc::sw128_mnmajor_desc(vb + uint32_t(k * 2048), MfSmem::KKB, 1024),
+                                   idesc_o, (b > 0 || k > 0) ? 1u : 0u);
+                tc::mma_commit(&vfree[b & 1]);
             };
             auto s_kb = [&](uint32_t sb, int kb, uint32_t baddr, bool first) {
                 const uint64_t ad = tc::sw128_kmajor_desc(qa + uint32_t(kb * MfSmem::QKB));
@@ -470,9 +501,9 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                 for (int k = 0; k < 4; ++k)
                     tc::mma_f16(sb, ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc_s, (!first || k > 0) ? 1u : 0u);
             };
-            for (int bi = 0; bi < nb && ok && !abort_flag; ++bi) {
-                const uint32_t sb = tmem + 256u + uint32_t((bi & 1) * MF_NB);
-                if (!(ok = tc::mbar_wait(&sfree[bi & 1], uint32_t(((bi >> 1) & 1) ^ 1)))) break;
+            for (int b = 0; b < nb && ok && !abort_flag; ++b) {
+                const uint32_t sb = tmem + MF_TS + uint32_t((b & 1) * MF_NB);
+                if (!(ok = tc::mbar_wait(&sfree[b & 1], uint32_t(((b >> 1) & 1) ^ 1)))) break;
                 tc::tc_fence_after();
                 for (int i = 0; i < 5 && ok; ++i) {   // the ring's k-blocks
                     if (!(ok = tc::mbar_wait(&full[stage], phase))) break;
@@ -485,15 +516,13 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                     }
                 }
                 if (!ok) break;
-                if (bi > 0) {   // frees the V tile for this block's own k-blocks
-                    pv(bi - 1);
-                    if (!ok) break;
-                }
-                if (!(ok = tc::mbar_wait(vfull, uint32_t(bi & 1)))) break;
+                if (!(ok = tc::mbar_wait(&vfull[b & 1], uint32_t((b >> 1) & 1)))) break;
                 tc::tc_fence_after();
+                const uint32_t vb = va + uint32_t((b & 1) * MfSmem::VBUF);
 #pragma unroll 1
-                for (int t = 0; t < 4; ++t) s_kb(sb, 4 * j + t, va + uint32_t(t * MfSmem::KKB), false);
-                tc::mma_commit(&sfull[bi & 1]);
+                for (int t = 0; t < 4; ++t) s_kb(sb, 4 * j + t, vb + uint32_t(t * MfSmem::KKB), false);
+                tc::mma_commit(&sfull[b & 1]);
+                if (b > 0) pv(b - 1);
             }
             if (ok && !abort_flag) pv(nb - 1);
             if (!ok) fail();
@@ -510,13 +539,14 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
         bool ok = true;
         uint4 ncw[8], nrp[4];
         uint16_t nsc[8];
-        auto load_block = [&](int bi) {   // this key's codes and scales of its half of every latent k-block (in the
-                                          // CTA's order), and its half of the rotary part
-            const int slot = qidx[size_t(b0 + bi) * MF_NB + kk];
+        int pslot = nb > 0 ? qidx[size_t(b0) * MF_NB + kk] : -1;
+        auto load_block = [&](int b) {   // this key's codes and scales of its half of every latent k-block (other
+                                         // value half first), and its half of the rotary part
+            const int slot = pslot;
+            if (b + 1 < nb) pslot = qidx[size_t(b0 + b + 1) * MF_NB + kk];
 #pragma unroll
-            for (int i = 0; i < 9; ++i) {
-                if (i == 4) continue;
-                const int kb = mf_kb(i, j), r = i < 4 ? i : i - 1;
+            for (int r = 0; r < 8; ++r) {
+                const int kb = r < 4 ? 4 * (1 - j) + r : 4 * j + (r - 4);
                 ncw[r] = make_uint4(0, 0, 0, 0);
                 nsc[r] = 0;
                 if (slot >= 0) {
@@ -530,27 +560,8 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                 nrp[t] = slot >= 0 ? reinterpret_cast<const uint4 *>(rope + size_t(slot) * MLA_R + half * 32)[t]
                                    : make_uint4(0, 0, 0, 0);
         };
-        auto write_kb = [&](uint8_t *dst, const uint4 &cw, uint16_t sc) {   // 32 dims of one latent k-block row
-            const float s0 = e4m3_to_f(uint8_t(sc & 0xFF)), s1 = e4m3_to_f(uint8_t(sc >> 8));
-            const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
-            uint8_t *rowp = dst + kk * 128;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                __half2 hh[4];
-                e2m1x8_to_h2(words[t], hh);
-                const float sf = t < 2 ? s0 : s1;
-                __nv_bfloat162 o[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float2 f = __half22float2(hh[u]);
-                    o[u] = __floats2bfloat162_rn(f.x * sf, f.y * sf);
-                }
-                const int c = half * 4 + t;
-                *reinterpret_cast<uint4 *>(rowp + ((c ^ (kk & 7)) << 4)) = *reinterpret_cast<uint4 *>(o);
-            }
-        };
         if (nb > 0) load_block(0);
-        for (int bi = 0; bi < nb && ok && !abort_flag; ++bi) {
+        for (int b = 0; b < nb && ok && !abort_flag; ++b) {
             uint4 cw[8], rp[4];
             uint16_t sc[8];
 #pragma unroll
@@ -560,26 +571,23 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
             }
 #pragma unroll
             for (int t = 0; t < 4; ++t) rp[t] = nrp[t];
-            if (bi + 1 < nb) load_block(bi + 1);
-            // the ring's k-blocks: the other value half's four, then the rotary one
+            if (b + 1 < nb) load_block(b + 1);
+            // the ring: the other value half's four k-blocks, then the rotary one
 #pragma unroll
             for (int i = 0; i < 5; ++i) {
-                int good = 1;
-                if (lane == 0) good = tc::mbar_wait(&empty[stage], phase ^ 1);
-                good = __shfl_sync(0xffffffffu, good, 0);
-                if (!good || abort_flag) {
-                    ok = false;
-                    break;
-                }
-                uint8_t *dst = ring + stage * MfSmem::KKB;
+                if (!(ok = warp_wait(&empty[stage], phase ^ 1))) break;
+                uint8_t *rowp = ring + stage * MfSmem::KKB + kk * 128;
                 if (i < 4) {
-                    write_kb(dst, cw[i], sc[i]);
+                    mf_write_kb(rowp, kk, half * 4, cw[i], sc[i]);
                 } else {
-                    uint8_t *rowp = dst + kk * 128;
 #pragma unroll
                     for (int t = 0; t < 4; ++t) {
+                        const __nv_bfloat162 *bp = reinterpret_cast<const __nv_bfloat162 *>(&rp[t]);
+                        __half2 hh[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) hh[u] = __float22half2_rn(__bfloat1622float2(bp[u]));
                         const int c = half * 4 + t;
-                        *reinterpret_cast<uint4 *>(rowp + ((c ^ (kk & 7)) << 4)) = rp[t];
+                        *reinterpret_cast<uint4 *>(rowp + ((c ^ (kk & 7)) << 4)) = *reinterpret_cast<uint4 *>(hh);
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
@@ -591,73 +599,101 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                 }
             }
             if (!ok) break;
-            // this half's four k-blocks into the V tile, once the previous block's P.V has read it
-            int good = 1;
-            if (lane == 0 && bi > 0) good = tc::mbar_wait(vfree, uint32_t((bi - 1) & 1));
-            good = __shfl_sync(0xffffffffu, good, 0);
-            if (!good || abort_flag) {
-                ok = false;
-                break;
-            }
+            // this half's four k-blocks into V tile b & 1, once P.V of block b - 2 has read it
+            if (b >= 2 && !(ok = warp_wait(&vfree[b & 1], uint32_t(((b >> 1) & 1) ^ 1)))) break;
+            uint8_t *vrow = vbuf + (b & 1) * MfSmem::VBUF + kk * 128;
 #pragma unroll
-            for (int t = 0; t < 4; ++t) write_kb(vbuf + t * MfSmem::KKB, cw[4 + t], sc[4 + t]);
+            for (int t = 0; t < 4; ++t) mf_write_kb(vrow + t * MfSmem::KKB, kk, half * 4, cw[4 + t], sc[4 + t]);
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(vfull);
+            if (lane == 0) tc::mbar_arrive(&vfull[b & 1]);
         }
         if (!ok && lane == 0) fail();
     } else if (warp >= 6) {
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;   // head
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
+        float m = -INFINITY, l = 0.f, sl = scale_log2;
+        bool ok = nb == 0 || warp_wait(qfull, 0);
+        if (nb > 0) {   // the query to f16, scaled by 2^e (every thread takes part in the named barrier)
+            const int t = threadIdx.x - 192;
+            float amax = 0.f;
+            if (ok)
+                for (int i = t; i < MfSmem::Q / 16; i += 128) {
+                    const uint4 v = reinterpret_cast<const uint4 *>(qs)[i];
+                    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float2 f = __bfloat1622float2(h[u]);
+                        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+                    }
+                }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            if (lane == 0) red[quarter] = amax;
+            asm volatile("bar.sync 1, 128;\n" ::: "memory");
+            amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+            const int ex = int((__float_as_uint(amax) >> 23) & 0xFF);
+            const int e = amax > 0.f ? max(-126, min(126, 141 - ex)) : 0;   // amax * 2^e in [2^14, 2^15)
+            const float qf = __uint_as_float(uint32_t(127 + e) << 23);
+            sl = scale_log2 * __uint_as_float(uint32_t(127 - e) << 23);
+            if (ok)
+                for (int i = t; i < MfSmem::Q / 16; i += 128) {
+                    uint4 v = reinterpret_cast<const uint4 *>(qs)[i];
+                    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&v);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float2 f = __bfloat1622float2(h[u]);
+                        const __half2 hv = __floats2half2_rn(f.x * qf, f.y * qf);
+                        h[u] = *reinterpret_cast<const __nv_bfloat162 *>(&hv);
+                    }
+                    reinterpret_cast<uint4 *>(qs)[i] = v;
+                }
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(qready);
+        }
         int ilo = nb > 0 ? qidx[size_t(b0) * MF_NB + lane] : -1;
         int ihi = nb > 0 ? qidx[size_t(b0) * MF_NB + 32 + lane] : -1;
-        for (int bi = 0; bi < nb && ok; ++bi) {
-            // S(bi) complete; it was issued after P.V of bi - 1, so O is also final for the correction below
-            int good = 1;
-            if (lane == 0) good = tc::mbar_wait(&sfull[bi & 1], uint32_t((bi >> 1) & 1));
-            good = __shfl_sync(0xffffffffu, good, 0);
-            if (!good || abort_flag) {
-                ok = false;
-                break;
-            }
+        for (int b = 0; b < nb && ok; ++b) {
+            if (!(ok = warp_wait(&sfull[b & 1], uint32_t((b >> 1) & 1)))) break;
             tc::tc_fence_after();
             float sv[MF_NB];
 #pragma unroll
             for (int c = 0; c < MF_NB / 32; ++c) {
                 uint32_t r[32];
-                tc::tmem_ld32(lane_base + 256u + uint32_t((bi & 1) * MF_NB + c * 32), r);
+                tc::tmem_ld32(lane_base + MF_TS + uint32_t((b & 1) * MF_NB + c * 32), r);
                 tc::tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
             }
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&sfree[bi & 1]);
+            if (lane == 0) tc::mbar_arrive(&sfree[b & 1]);
             const unsigned vlo = __ballot_sync(0xffffffffu, ilo >= 0);
             const unsigned vhi = __ballot_sync(0xffffffffu, ihi >= 0);
-            if (bi + 1 < nb) {   // the next block's slots, in flight while this block is processed
-                ilo = qidx[size_t(b0 + bi + 1) * MF_NB + lane];
-                ihi = qidx[size_t(b0 + bi + 1) * MF_NB + 32 + lane];
+            if (b + 1 < nb) {   // the next block's slots, in flight while this block is processed
+                ilo = qidx[size_t(b0 + b + 1) * MF_NB + lane];
+                ihi = qidx[size_t(b0 + b + 1) * MF_NB + 32 + lane];
             }
             float bm = -INFINITY;
 #pragma unroll
             for (int i = 0; i < MF_NB; ++i) {
                 const bool v = i < 32 ? (vlo >> i) & 1 : (vhi >> (i - 32)) & 1;
-                sv[i] = v ? sv[i] * scale_log2 : -INFINITY;
+                sv[i] = v ? sv[i] * sl : -INFINITY;
                 bm = fmaxf(bm, sv[i]);
             }
             const float m_new = fmaxf(m, bm);
             const bool need = m_new > -INFINITY && (m == -INFINITY || m_new > m + MF_TAU);
             float factor = 1.f;
             if (need) {
-                factor = m == -INFINITY ? 0.f : exp2f(m - m_new);
+                factor = m == -INFINITY ? 0.f : ex2_approx(m - m_new);
                 m = m_new;
                 l *= factor;
             }
-            if (bi > 0 && __ballot_sync(0xffffffffu, need)) {
+            if (b > 0 && __ballot_sync(0xffffffffu, need)) {   // O complete up to block b - 1, then rescaled
+                if (!(ok = warp_wait(&vfree[(b - 1) & 1], uint32_t(((b - 1) >> 1) & 1)))) break;
+                tc::tc_fence_after();
 #pragma unroll 1
                 for (int c = 0; c < 8; ++c) {
                     uint32_t r[32];
@@ -669,28 +705,29 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                 }
                 tc::tmem_st_wait();
             }
-            uint8_t *rowp = ps + row * 128;
+            uint32_t pr[32];
+            float lacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                __nv_bfloat162 pv[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int k0 = c * 8 + 2 * t;
-                    const float p0 = m == -INFINITY ? 0.f : exp2f(sv[k0] - m);
-                    const float p1 = m == -INFINITY ? 0.f : exp2f(sv[k0 + 1] - m);
-                    pv[t] = __floats2bfloat162_rn(p0, p1);
-                    const float2 back = __bfloat1622float2(pv[t]);
-                    l += back.x + back.y;
-                }
-                *reinterpret_cast<uint4 *>(rowp + ((c ^ (row & 7)) << 4)) = *reinterpret_cast<uint4 *>(pv);
+            for (int c = 0; c < 32; ++c) {
+                const float p0 = m == -INFINITY ? 0.f : ex2_approx(sv[2 * c] - m);
+                const float p1 = m == -INFINITY ? 0.f : ex2_approx(sv[2 * c + 1] - m);
+                const __half2 h = __floats2half2_rn(p0, p1);
+                const float2 back = __half22float2(h);
+                lacc[c & 3] += back.x + back.y;
+                pr[c] = *reinterpret_cast<const uint32_t *>(&h);
             }
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            l += (lacc[0] + lacc[1]) + (lacc[2] + lacc[3]);
+            // P buffer b & 1 was last read by P.V of block b - 2
+            if (b >= 2 && !(ok = warp_wait(&vfree[b & 1], uint32_t(((b >> 1) & 1) ^ 1)))) break;
+            tc::tc_fence_after();
+            tc::tmem_st32(lane_base + MF_TP + uint32_t((b & 1) * 32), pr);
+            tc::tmem_st_wait();
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(pfull);
+            if (lane == 0) tc::mbar_arrive(&pfull[b & 1]);
         }
         int good = ok ? 1 : 0;
-        if (ok && nb > 0 && lane == 0) good = tc::mbar_wait(vfree, uint32_t((nb - 1) & 1));   // the last P.V
+        if (ok && nb > 0 && lane == 0) good = tc::mbar_wait(&vfree[(nb - 1) & 1], uint32_t(((nb - 1) >> 1) & 1));
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good && lane == 0) fail();
         tc::tc_fence_after();

@@ -81,6 +81,16 @@ XT_DEV void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t id
         : "memory");
 }
 
+// D (+)= A . B with A [M x K] in tensor memory (row m in lane m, two 16-bit elements per 32-bit column, element 2c in
+// the low half of column c) and B through a shared-memory descriptor.
+XT_DEV void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrives on `bar` once every tcgen05 operation issued so far by this thread has completed.
 XT_DEV void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
@@ -223,6 +233,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
     return (1u << 4)                    // D format F32
            | (1u << 7)                  // A format BF16
            | (1u << 10)                 // B format BF16
+           | (uint32_t(N >> 3) << 17)   // N / 8
+           | (uint32_t(M >> 4) << 24);  // M / 16
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+    return (1u << 4)                    // D format F32 (A and B formats 0: F16)
            | (uint32_t(N >> 3) << 17)   // N / 8
            | (uint32_t(M >> 4) << 24);  // M / 16
 }
