@@ -362,18 +362,19 @@ __global__ void __launch_bounds__(MLA_THREADS, 1)
 //               half and the rotary one) and this half's four (the V tile of b), then O += P.V of block b - 1 with P
 //               read from TMEM and V read in place through an MN-major descriptor (no transposed copy)
 //   warp 1      TMEM owner (512 columns: O half at 0..255, S buffers at 256 and 320, P buffers at 384 and 416)
-//   warps 2-5   producers: TMA of the query's nine k-blocks once, and the gather of every block's latent rows into
+//   warps 2-5   producers: TMA of the query's nine k-blocks once (converted to f16 by warps 2-9 together, below),
+//               and the gather of every block's latent rows into
 //               128-byte-swizzled K-major FP16 tiles (E2M1 -> f16 by the hardware conversion, times the block's E4M3
 //               scale in f16: exact, every product has at most six significant bits and lies in f16's normal range;
 //               the rotary part BF16 -> f16); a block's rows are loaded while the previous block is written, and the
 //               slots one block further ahead
-//   warps 6-9   first the query: BF16 -> f16 in place, scaled by the power of two 2^e that puts its largest magnitude
-//               in [2^14, 2^15) (so the conversion is exact down to 2^-28 of the largest element), 2^-e folded into
-//               the softmax scale. Then softmax, one head row per thread: block max, lazy correction of O (only when
+//   warps 6-9   softmax, one head row per thread: block max, lazy correction of O (only when
 //               the running max grows by more than 2^8; then O and the row sum are rescaled in TMEM once P.V of the
 //               previous block is done), P = 2^(S - m) in f16 into TMEM, the row sum over the rounded P, and the
 //               epilogue (O / l, or the unnormalized split partial with m and l for mla_merge)
-// V is double-buffered, so S of block b does not wait for P.V of block b - 1: the tensor core computes S of b while
+// The query is converted once, in place: each head row BF16 -> f16 scaled by the power of two 2^e that puts the row's
+// largest magnitude in [2^14, 2^15) (exact down to 2^-28 of that magnitude); 2^-e is folded into the row's softmax
+// scale. V is double-buffered, so S of block b does not wait for P.V of block b - 1: the tensor core computes S of b while
 // the softmax warps work on b - 1. Every wait is bounded; a wait that runs out sets the error word, raises the CTA's
 // abort flag and every role winds down (the output of that query is then meaningless and the caller raises).
 constexpr int MF_NB = 64;
@@ -410,6 +411,48 @@ XT_DEV void mf_write_kb(uint8_t *rowp, int kk, int c0, const uint4 &cw, uint16_t
     }
 }
 
+// Largest magnitude of k-blocks [k0, k1) of query row `row` (BF16, 128 bytes per row and k-block)
+XT_DEV float mf_row_amax(const uint8_t *qs, int row, int k0, int k1) {
+    float a = 0.f;
+    for (int kb = k0; kb < k1; ++kb) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(qs + kb * MfSmem::QKB + row * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {   // chunk order rotated by the row: the lanes of a warp hit distinct banks
+            const uint4 v = p[c ^ (row & 7)];
+            const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float2 f = __bfloat1622float2(h[u]);
+                a = fmaxf(a, fmaxf(fabsf(f.x), fabsf(f.y)));
+            }
+        }
+    }
+    return a;
+}
+
+// The same k-blocks BF16 -> f16 in place, times qf (a power of two)
+XT_DEV void mf_row_to_f16(uint8_t *qs, int row, int k0, int k1, float qf) {
+    for (int kb = k0; kb < k1; ++kb) {
+        uint4 *p = reinterpret_cast<uint4 *>(qs + kb * MfSmem::QKB + row * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 v = p[c ^ (row & 7)];
+            auto cv = [qf](uint32_t w) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
+                const __half2 hv = __floats2half2_rn(f.x * qf, f.y * qf);
+                return *reinterpret_cast<const uint32_t *>(&hv);
+            };
+            p[c ^ (row & 7)] = make_uint4(cv(v.x), cv(v.y), cv(v.z), cv(v.w));
+        }
+    }
+}
+
+// 2^e with e chosen so that amax * 2^e lies in [2^14, 2^15) (1 for amax 0)
+XT_DEV int mf_row_exp(float amax) {
+    const int ex = int((__float_as_uint(amax) >> 23) & 0xFF);
+    return amax > 0.f ? max(-126, min(126, 141 - ex)) : 0;
+}
+
 __global__ void __launch_bounds__(MF_THREADS, 1)
     mla_flash_kernel(const __grid_constant__ CUtensorMap tma_q, const int32_t *__restrict__ idx, int nsel, int bps,
                      int nblk, const uint8_t *__restrict__ codes, const uint8_t *__restrict__ scales,
@@ -431,7 +474,9 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
     uint64_t *pfull = sfree + 2;           // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfull + 2);
     __shared__ volatile int abort_flag;
-    __shared__ float red[4];
+    // the query rows' largest magnitudes over k-blocks 0-4 and 5-8, exchanged once at the start in V tile 1 (first
+    // written for block 1, which the MMA issuer starts only after every converting warp has arrived on qready)
+    float (*row_amax)[MLA_H] = reinterpret_cast<float (*)[MLA_H]>(vbuf + MfSmem::VBUF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j = blockIdx.x, split = blockIdx.y, q = blockIdx.z, splits = gridDim.y;
@@ -444,7 +489,7 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
             tc::mbar_init(&empty[s], 1);
         }
         tc::mbar_init(qfull, 1);
-        tc::mbar_init(qready, 4);
+        tc::mbar_init(qready, 8);
         for (int s = 0; s < 2; ++s) {
             tc::mbar_init(&vfull[s], 4);
             tc::mbar_init(&vfree[s], 1);
@@ -538,7 +583,7 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
         uint32_t phase = 0;
         bool ok = true;
         uint4 ncw[8], nrp[4];
-        uint16_t nsc[8];
+        uint32_t nsc[4];   // the E4M3 scale pairs of k-blocks r and r + 4 (low and high half)
         int pslot = nb > 0 ? qidx[size_t(b0) * MF_NB + kk] : -1;
         auto load_block = [&](int b) {   // this key's codes and scales of its half of every latent k-block (other
                                          // value half first), and its half of the rotary part
@@ -547,27 +592,47 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
                 const int kb = r < 4 ? 4 * (1 - j) + r : 4 * j + (r - 4);
-                ncw[r] = make_uint4(0, 0, 0, 0);
-                nsc[r] = 0;
-                if (slot >= 0) {
-                    ncw[r] = *reinterpret_cast<const uint4 *>(codes + size_t(slot) * (MLA_L / 2) + kb * 32 + half * 16);
-                    nsc[r] =
-                        *reinterpret_cast<const uint16_t *>(scales + size_t(slot) * (MLA_L / 16) + kb * 4 + half * 2);
-                }
+                ncw[r] = slot >= 0 ? *reinterpret_cast<const uint4 *>(codes + size_t(slot) * (MLA_L / 2) + kb * 32 +
+                                                                      half * 16)
+                                   : make_uint4(0, 0, 0, 0);
+            }
+            // the key's 32 scales in two loads; this thread's pair of k-block kb is 16-bit half `half` of word kb
+            uint4 sw[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+            if (slot >= 0) {
+                sw[0] = reinterpret_cast<const uint4 *>(scales + size_t(slot) * (MLA_L / 16))[0];
+                sw[1] = reinterpret_cast<const uint4 *>(scales + size_t(slot) * (MLA_L / 16))[1];
+            }
+            const uint32_t lo[4] = {sw[0].x, sw[0].y, sw[0].z, sw[0].w}, hi[4] = {sw[1].x, sw[1].y, sw[1].z, sw[1].w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {   // k-blocks 4 (1 - j) + r and 4 j + r
+                const uint32_t a = j ? lo[r] : hi[r], c = j ? hi[r] : lo[r];
+                nsc[r] = half ? __byte_perm(a, c, 0x7632) : __byte_perm(a, c, 0x5410);
             }
 #pragma unroll
             for (int t = 0; t < 4; ++t)
                 nrp[t] = slot >= 0 ? reinterpret_cast<const uint4 *>(rope + size_t(slot) * MLA_R + half * 32)[t]
                                    : make_uint4(0, 0, 0, 0);
         };
-        if (nb > 0) load_block(0);
+        if (nb > 0) {
+            load_block(0);
+            // k-blocks 0-4 of the query row this thread shares with a softmax thread (which takes 5-8)
+            const int qrow = (warp & 3) * 32 + lane;
+            ok = warp_wait(qfull, 0);
+            row_amax[0][qrow] = ok ? mf_row_amax(qs, qrow, 0, 5) : 0.f;
+            asm volatile("bar.sync 1, 256;\n" ::: "memory");
+            const int e = mf_row_exp(fmaxf(row_amax[0][qrow], row_amax[1][qrow]));
+            if (ok) mf_row_to_f16(qs, qrow, 0, 5, __uint_as_float(uint32_t(127 + e) << 23));
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(qready);
+        }
         for (int b = 0; b < nb && ok && !abort_flag; ++b) {
             uint4 cw[8], rp[4];
             uint16_t sc[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 cw[i] = ncw[i];
-                sc[i] = nsc[i];
+                sc[i] = uint16_t(nsc[i & 3] >> (i < 4 ? 0 : 16));
             }
 #pragma unroll
             for (int t = 0; t < 4; ++t) rp[t] = nrp[t];
@@ -614,41 +679,14 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
         const int row = quarter * 32 + lane;   // head
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         float m = -INFINITY, l = 0.f, sl = scale_log2;
-        bool ok = nb == 0 || warp_wait(qfull, 0);
-        if (nb > 0) {   // the query to f16, scaled by 2^e (every thread takes part in the named barrier)
-            const int t = threadIdx.x - 192;
-            float amax = 0.f;
-            if (ok)
-                for (int i = t; i < MfSmem::Q / 16; i += 128) {
-                    const uint4 v = reinterpret_cast<const uint4 *>(qs)[i];
-                    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float2 f = __bfloat1622float2(h[u]);
-                        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-                    }
-                }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            if (lane == 0) red[quarter] = amax;
-            asm volatile("bar.sync 1, 128;\n" ::: "memory");
-            amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-            const int ex = int((__float_as_uint(amax) >> 23) & 0xFF);
-            const int e = amax > 0.f ? max(-126, min(126, 141 - ex)) : 0;   // amax * 2^e in [2^14, 2^15)
-            const float qf = __uint_as_float(uint32_t(127 + e) << 23);
+        bool ok = true;
+        if (nb > 0) {   // k-blocks 5-8 of this head row of the query (a producer thread takes 0-4)
+            ok = warp_wait(qfull, 0);
+            row_amax[1][row] = ok ? mf_row_amax(qs, row, 5, 9) : 0.f;
+            asm volatile("bar.sync 1, 256;\n" ::: "memory");
+            const int e = mf_row_exp(fmaxf(row_amax[0][row], row_amax[1][row]));
+            if (ok) mf_row_to_f16(qs, row, 5, 9, __uint_as_float(uint32_t(127 + e) << 23));
             sl = scale_log2 * __uint_as_float(uint32_t(127 - e) << 23);
-            if (ok)
-                for (int i = t; i < MfSmem::Q / 16; i += 128) {
-                    uint4 v = reinterpret_cast<const uint4 *>(qs)[i];
-                    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&v);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float2 f = __bfloat1622float2(h[u]);
-                        const __half2 hv = __floats2half2_rn(f.x * qf, f.y * qf);
-                        h[u] = *reinterpret_cast<const __nv_bfloat162 *>(&hv);
-                    }
-                    reinterpret_cast<uint4 *>(qs)[i] = v;
-                }
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(qready);
