@@ -595,15 +595,36 @@ void moe_grouped(const Tensor &x, const Tensor &codes, const Tensor &scales, con
              "moe_grouped");
 }
 
-void topk_rows(const Tensor &scores, int64_t K, const Tensor &out) {
+void topk_rows(const Tensor &scores, int64_t K, const Tensor &out, const std::optional<Tensor> &len) {
     cuda_contig(scores, "scores");
     check(scores.scalar_type() == at::kFloat && out.scalar_type() == at::kInt && out.size(0) == scores.size(0) &&
               out.size(1) == K,
           "topk_rows shapes");
+    if (len.has_value())
+        check(len->scalar_type() == at::kInt && len->is_contiguous() && len->numel() == scores.size(0),
+              "topk_rows: len int32 [rows]");
     c10::cuda::CUDAGuard g(scores.device());
     check_rc(xt_topk_rows(ptr<const float>(scores), int(scores.size(0)), int(scores.size(1)), int(K),
-                          ptr<int32_t>(out), stream()),
+                          optr<const int32_t>(len), ptr<int32_t>(out), stream()),
              "topk_rows");
+}
+
+void dsa_index_pf(const Tensor &q8, const Tensor &w, const Tensor &codes, const Tensor &kscale, int64_t row_base,
+                  const Tensor &len, const Tensor &scores, int64_t splits, const Tensor &err) {
+    cuda_contig(q8, "q8");
+    cuda_contig(w, "w");
+    cuda_contig(len, "len");
+    cuda_contig(scores, "scores");
+    check(q8.scalar_type() == at::kByte && q8.size(1) == 64 && q8.size(2) == 128 && codes.size(-1) == 128 &&
+              w.scalar_type() == at::kFloat && scores.scalar_type() == at::kFloat && len.scalar_type() == at::kInt &&
+              len.numel() == q8.size(0) && scores.size(0) >= q8.size(0),
+          "dsa_index_pf shapes");
+    check(row_base >= 0 && row_base + scores.size(1) <= codes.size(0), "dsa_index_pf: row outside the cache");
+    c10::cuda::CUDAGuard g(q8.device());
+    check_rc(xt_dsa_index_pf(q8.data_ptr(), ptr<const float>(w), codes.data_ptr(), codes.size(0),
+                             ptr<const float>(kscale), row_base, ptr<const int32_t>(len), ptr<float>(scores),
+                             int(q8.size(0)), int(scores.size(1)), int(splits), ptr<int>(err), stream()),
+             "dsa_index_pf");
 }
 
 }  // namespace
@@ -704,7 +725,9 @@ TORCH_LIBRARY(xtier, m) {
     m.def("dsa_key_write(Tensor k, Tensor slot, Tensor(a!) codes, Tensor(b!) kscale) -> ()");
     m.def("dsa_index_decode(Tensor q, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, "
           "Tensor(a!) scores) -> ()");
-    m.def("topk_rows(Tensor scores, int K, Tensor(a!) out) -> ()");
+    m.def("topk_rows(Tensor scores, int K, Tensor(a!) out, Tensor? len=None) -> ()");
+    m.def("dsa_index_pf(Tensor q8, Tensor w, Tensor codes, Tensor kscale, int row_base, Tensor len, "
+          "Tensor(a!) scores, int splits, Tensor(b!) err) -> ()");
     m.def("moe_grouped(Tensor x, Tensor codes, Tensor scales, Tensor gscale, Tensor tiles, bool gate_up, int I, "
           "int fmt, Tensor? route_w, Tensor(a!) out, Tensor(b!) err) -> ()");
     m.def("dsa_index_tc(Tensor q8, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, Tensor(a!) scores, "
@@ -757,4 +780,5 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("topk_rows", &topk_rows);
     m.impl("moe_grouped", &moe_grouped);
     m.impl("dsa_index_tc", &dsa_index_tc);
+    m.impl("dsa_index_pf", &dsa_index_pf);
 }

@@ -201,6 +201,180 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
+// ------------------------------------------------------------------------------------------------ prefill indexer
+// The queries of a prefill chunk share one cache row. One CTA per (4 queries, key split): the 4 queries' FP8 Q
+// [256 = 4 x 64 heads, 128] stays in shared memory, the split's 128-key tiles stream through a TMA ring, and each tile
+// is one D[128 keys, 256] = K8 . Q8^T on tcgen05 (4 MMAs of K = 32 bytes) into one of two TMEM accumulators, so the
+// epilogue of tile t overlaps the MMAs of tile t + 1. 576 threads:
+//   warp 0      TMA producer (lane 0)
+//   warp 1      TMEM owner (512 columns) and MMA issuer (lane 0)
+//   warps 2-17  epilogue, one warp per (query of the group, 32-lane quarter of the accumulator): each thread owns one
+//               key and reduces score[q, key] = kscale[key] * sum_h w[q, h] * relu(D[key, q * 64 + h]); keys at or
+//               past the query's length get -inf up to the end of the last tile, nothing beyond it (top-k reads each
+//               row only up to its length)
+// Every wait is bounded; a wait that runs out sets the error word and the CTA winds down.
+constexpr int IP_NQ = 4;
+constexpr int IP_N = IDX_HEADS * IP_NQ;   // 256
+constexpr int IP_STAGES = 6;
+constexpr int IP_THREADS = 576;
+
+struct IpSmem {
+    static constexpr int Q = IP_N * 128;   // 32 KB
+    static constexpr int KT = 128 * 128;   // 16 KB: a key tile
+    static constexpr int BYTES = Q + IP_STAGES * KT + 1024;
+};
+
+__global__ void __launch_bounds__(IP_THREADS, 1)
+    dsa_index_pf_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constant__ CUtensorMap tma_q,
+                        const float *__restrict__ w, const float *__restrict__ kscale, int64_t row_base,
+                        const int32_t *__restrict__ len, float *__restrict__ scores, int Q, int max_len, int *error) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *qs = smem;
+    uint8_t *ring = smem + IpSmem::Q;
+    __shared__ uint64_t full[IP_STAGES], empty[IP_STAGES], qfull, accf[2], acce[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ __align__(16) float ws[IP_NQ][IDX_HEADS];
+    __shared__ volatile int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.y * IP_NQ, split = blockIdx.x, splits = gridDim.x;
+    int nmax = 0;
+    for (int i = 0; i < IP_NQ; ++i)
+        if (q0 + i < Q) nmax = max(nmax, min(len[q0 + i], max_len));
+    const int ntile = (nmax + 127) / 128, per = (ntile + splits - 1) / splits;
+    const int t0 = split * per, nt = min(ntile, t0 + per) - t0;
+    for (int i = threadIdx.x; i < IP_NQ * IDX_HEADS; i += blockDim.x) {
+        const int qi = q0 + i / IDX_HEADS;
+        ws[i / IDX_HEADS][i % IDX_HEADS] = qi < Q ? w[size_t(qi) * IDX_HEADS + i % IDX_HEADS] : 0.f;
+    }
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < IP_STAGES; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(&qfull, 1);
+        for (int a = 0; a < 2; ++a) {
+            tc::mbar_init(&accf[a], 1);
+            tc::mbar_init(&acce[a], 16);
+        }
+        tc::fence_barrier_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    auto fail = [&]() {
+        abort_flag = 1;
+        atomicExch(error, 1);
+    };
+
+    if (nt > 0) {
+        if (warp == 0) {
+            if (lane == 0) {
+                tc::prefetch_tmap(&tma_k);
+                tc::mbar_arrive_expect_tx(&qfull, IpSmem::Q);
+                tc::tma_load_2d(qs, &tma_q, &qfull, 0, q0 * IDX_HEADS);
+                int stage = 0;
+                uint32_t phase = 0;
+                for (int t = 0; t < nt && !abort_flag; ++t) {
+                    if (!tc::mbar_wait(&empty[stage], phase ^ 1)) {
+                        fail();
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&full[stage], IpSmem::KT);
+                    tc::tma_load_2d(ring + stage * IpSmem::KT, &tma_k, &full[stage], 0,
+                                    int(row_base + int64_t(t0 + t) * 128));
+                    if (++stage == IP_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        } else if (warp == 1) {
+            if (lane == 0) {
+                // kind::f8f6f4: D F32 (bit 4), A and B E4M3 (format 0), N / 8, M / 16
+                const uint32_t idesc = (1u << 4) | (uint32_t(IP_N >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+                const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_u32(qs));
+                bool ok = tc::mbar_wait(&qfull, 0);
+                int stage = 0;
+                uint32_t phase = 0;
+                for (int t = 0; t < nt && ok && !abort_flag; ++t) {
+                    const int a = t & 1;
+                    if (!(ok = tc::mbar_wait(&acce[a], uint32_t(((t >> 1) & 1) ^ 1)))) break;
+                    if (!(ok = tc::mbar_wait(&full[stage], phase))) break;
+                    tc::tc_fence_after();
+                    const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_u32(ring + stage * IpSmem::KT));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)   // K = 32 bytes per MMA
+                        asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                     " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+                                         tmem + uint32_t(a * IP_N)),
+                                     "l"(ad + uint64_t(2 * k)), "l"(bd + uint64_t(2 * k)), "r"(idesc),
+                                     "r"(k > 0 ? 1u : 0u)
+                                     : "memory");
+                    tc::mma_commit(&empty[stage]);
+                    tc::mma_commit(&accf[a]);
+                    if (++stage == IP_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) fail();
+            }
+        } else {
+            const int qq = (warp - 2) >> 2, quarter = warp & 3;
+            const int qi = q0 + qq;
+            const int L = qi < Q ? min(len[qi], max_len) : 0;
+            const float4 *wq = reinterpret_cast<const float4 *>(ws[qq]);
+            for (int t = 0; t < nt; ++t) {
+                const int a = t & 1;
+                int good = 1;
+                if (lane == 0) good = tc::mbar_wait(&accf[a], uint32_t((t >> 1) & 1));
+                good = __shfl_sync(0xffffffffu, good, 0);
+                if (!good || abort_flag) {
+                    if (!good && lane == 0) fail();
+                    break;
+                }
+                tc::tc_fence_after();
+                uint32_t r[2][32];
+                const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(a * IP_N + qq * IDX_HEADS);
+                tc::tmem_ld32(base, r[0]);
+                tc::tmem_ld32(base + 32u, r[1]);
+                tc::tmem_ld_wait();
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&acce[a]);
+                const int key = (t0 + t) * 128 + quarter * 32 + lane;
+                float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int h4 = 0; h4 < 8; ++h4) {
+                        const float4 wv = wq[c * 8 + h4];
+                        acc0 += wv.x * fmaxf(__uint_as_float(r[c][4 * h4]), 0.f);
+                        acc1 += wv.y * fmaxf(__uint_as_float(r[c][4 * h4 + 1]), 0.f);
+                        acc0 += wv.z * fmaxf(__uint_as_float(r[c][4 * h4 + 2]), 0.f);
+                        acc1 += wv.w * fmaxf(__uint_as_float(r[c][4 * h4 + 3]), 0.f);
+                    }
+                if (qi < Q && key < max_len)
+                    scores[size_t(qi) * max_len + key] = key < L ? (acc0 + acc1) * kscale[row_base + key] : -INFINITY;
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
 // order-preserving image of a float: larger float -> larger unsigned (NaN never occurs here)
 __device__ __forceinline__ uint32_t fkey(float f) {
     const uint32_t u = __float_as_uint(f);
@@ -236,16 +410,19 @@ __device__ int block_scan(int v, int *warp_sums, int *tot) {
     return before;
 }
 
-__global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(const float *__restrict__ scores, int n, int K,
+// Rows of stride `stride`; row r holds len[r] scores (all `stride` when len is null).
+__global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(const float *__restrict__ scores, int stride, int K,
+                                                               const int32_t *__restrict__ len,
                                                                int32_t *__restrict__ out) {
     __shared__ int hist[256];
     __shared__ int warp_sums[32];
     __shared__ uint32_t prefix_s;
     __shared__ int need_s, finite_s;
     const int row = blockIdx.x;
-    const float *x = scores + size_t(row) * n;
+    const float *x = scores + size_t(row) * stride;
+    const int n = len ? max(0, min(stride, len[row])) : stride;
     int32_t *o = out + size_t(row) * K;
-    const bool vec = (n % 4) == 0;   // rows 16-byte aligned
+    const bool vec = (stride % 4) == 0;   // rows 16-byte aligned
     // radix select of the K-th largest key among finite scores (pass 0 also counts them)
     uint32_t prefix = 0;
     int need = K;
@@ -426,9 +603,32 @@ int xt_dsa_index_tc(const void *q8, const float *w, const void *codes, int64_t s
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int xt_topk_rows(const float *scores, int rows, int n, int K, int32_t *out, cudaStream_t stream) {
+// Prefill indexer: the Q queries share the cache row starting at slot row_base; query i scores keys
+// [0, len[i]) of it (scores [Q, max_len], -inf from len[i] to the end of its last key tile). splits key ranges per
+// group of 4 queries (0: chosen here).
+int xt_dsa_index_pf(const void *q8, const float *w, const void *codes, int64_t slots, const float *kscale,
+                    int64_t row_base, const int32_t *len, float *scores, int Q, int max_len, int splits, int *error,
+                    cudaStream_t stream) {
+    if (Q <= 0 || max_len <= 0 || splits < 0) return -2;
+    CUtensorMap mk, mq;
+    if (!dsa_map(&mk, codes, uint64_t(slots), 128) || !dsa_map(&mq, q8, uint64_t(Q) * IDX_HEADS, IP_N)) return -3;
+    const int groups = (Q + IP_NQ - 1) / IP_NQ;
+    if (groups > 65535) return -2;
+    if (splits == 0) {   // about four CTAs per SM over the chunk, at least 8 key tiles per CTA
+        int sms = 148, dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int tiles = (max_len + 127) / 128;
+        splits = max(1, min((4 * sms + groups - 1) / groups, tiles / 8));
+    }
+    if (xt_smem_optin(dsa_index_pf_kernel, IpSmem::BYTES) != cudaSuccess) return -4;
+    dsa_index_pf_kernel<<<dim3(splits, groups), IP_THREADS, IpSmem::BYTES, stream>>>(mk, mq, w, kscale, row_base, len,
+                                                                                  scores, Q, max_len, error);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int xt_topk_rows(const float *scores, int rows, int n, int K, const int32_t *len, int32_t *out, cudaStream_t stream) {
     if (rows <= 0 || n <= 0 || K <= 0) return -2;
-    topk_rows_kernel<<<rows, TK_THREADS, 0, stream>>>(scores, n, K, out);
+    topk_rows_kernel<<<rows, TK_THREADS, 0, stream>>>(scores, n, K, len, out);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -194,7 +194,10 @@ int xt_dsa_index_decode(const void *q, const float *w, const void *codes, const 
 int xt_dsa_index_tc(const void *q8, const float *w, const void *codes, int64_t slots, const float *kscale,
                     const int64_t *base, const int32_t *len, float *scores, int Q, int max_len, int nq, int *error,
                     cudaStream_t stream);
-int xt_topk_rows(const float *scores, int rows, int n, int K, int32_t *out, cudaStream_t stream);
+int xt_topk_rows(const float *scores, int rows, int n, int K, const int32_t *len, int32_t *out, cudaStream_t stream);
+int xt_dsa_index_pf(const void *q8, const float *w, const void *codes, int64_t slots, const float *kscale,
+                    int64_t row_base, const int32_t *len, float *scores, int Q, int max_len, int splits, int *error,
+                    cudaStream_t stream);
 int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int32_t *tiles, int T, int gate_up,
                    int K, int N_rows, int I, int fmt, const void *scales, const float *gscale, const float *route_w,
                    void *mid, float *y, int out_cols, int *error, cudaStream_t stream);

@@ -51,6 +51,44 @@ def test_index_scores_and_topk(cuda_ops):
     assert (idx[2] >= 0).sum() == 700                  # short row: every finite score, then -1
 
 
+@pytest.mark.parametrize('Q,splits', [(6, 1), (9, 3), (64, 0)])
+def test_prefill_indexer_and_length_topk(cuda_ops, Q, splits):
+    """Pipelined prefill indexer (4 queries per CTA, key splits, a partial last group) against the FP8-query oracle
+    over each query's causal length, and top-k that reads each row only up to its length."""
+    from xtier_b200.attention import dsa
+    g = torch.Generator(device='cuda').manual_seed(11 + Q)
+    rows, max_len = 2, 5000
+    cache = dsa.IndexCache(rows, max_len)
+    cache.write(torch.randn(rows * max_len, 128, device='cuda', generator=g).bfloat16(),
+                torch.arange(rows * max_len, device='cuda'))
+    q = torch.randn(Q, 64, 128, device='cuda', generator=g).bfloat16()
+    w = torch.rand(Q, 64, device='cuda', generator=g)
+    lens = torch.randint(1, max_len + 1, (Q,), device='cuda', generator=g).int()
+    lens[0] = max_len
+    err = torch.zeros(1, dtype=torch.int32, device='cuda')
+    out = torch.full((Q, max_len), float('nan'), device='cuda')
+    sc = dsa.index_scores_prefill(q, w, cache, 1, lens, out=out, err=err, splits=splits)
+    ref = dsa.reference_scores(q, w, cache, torch.ones(Q, dtype=torch.long, device='cuda'), lens, fp8_queries=True)
+    assert int(err) == 0
+    for i in range(Q):
+        n = int(lens[i])
+        assert float((sc[i, :n] - ref[i, :n]).abs().max() / ref[i, :n].abs().max()) < 1e-3, i
+        end = min(max_len, (n + 127) // 128 * 128)
+        assert bool(torch.isneginf(sc[i, n:end]).all()), i
+    K = 2048
+    idx = dsa.topk(sc, K, lengths=lens)
+    masked = sc.clone()
+    for i in range(Q):
+        masked[i, int(lens[i]):] = float('-inf')
+    want = dsa.reference_topk(masked, K)
+    for i in range(Q):
+        row = idx[i].tolist()
+        got = [j for j in row if j >= 0]
+        assert got == sorted(got) and set(got) == want[i], i
+        assert len(got) == min(K, int(lens[i])), i
+        assert all(j == -1 for j in row[len(got):]), i
+
+
 def test_sparse_decode_chain(cuda_ops):
     from xtier_b200.attention import dsa
     from xtier_b200.attention.mla import LatentCache, MlaWorkspace, default_scale, mla_decode, reference_decode

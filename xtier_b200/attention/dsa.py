@@ -63,11 +63,31 @@ def index_scores(q: torch.Tensor, w: torch.Tensor, cache: IndexCache, rows: torc
     return out
 
 
-def topk(scores: torch.Tensor, k: int, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Indices of the k largest finite scores per row, ascending; -1 padding. int32 [rows, k]."""
+def index_scores_prefill(q: torch.Tensor, w: torch.Tensor, cache: IndexCache, row: int, lengths: torch.Tensor,
+                         out: torch.Tensor | None = None, err: torch.Tensor | None = None,
+                         splits: int = 0) -> torch.Tensor:
+    """Indexer scores of queries that share cache row `row` (a prefill chunk of one sequence): q [Q, 64, 128] BF16,
+    w [Q, 64] fp32, lengths [Q] -> scores [Q, max_len] fp32, valid in [0, lengths[i]) of row i (then -inf up to the
+    end of the last 128-key tile, unwritten beyond: pass the same lengths to topk). FP8 queries (E4M3 x E4M3 MMA),
+    4 queries per CTA over a pipelined key stream; `splits` key ranges per query group (0: chosen by the launcher)."""
+    Q = q.shape[0]
+    out = torch.empty(Q, cache.max_len, dtype=torch.float32, device=q.device) if out is None else out
+    ops.load()
+    q8, w8 = quantize_queries(q, w)
+    err = torch.zeros(1, dtype=torch.int32, device=q.device) if err is None else err
+    torch.ops.xtier.dsa_index_pf(q8, w8, cache.codes, cache.scale, int(row) * cache.max_len,
+                                 lengths.int().contiguous(), out, int(splits), err)
+    return out
+
+
+def topk(scores: torch.Tensor, k: int, out: torch.Tensor | None = None,
+         lengths: torch.Tensor | None = None) -> torch.Tensor:
+    """Indices of the k largest finite scores per row, ascending; -1 padding. int32 [rows, k]. With lengths, row i
+    is read only in [0, lengths[i])."""
     out = torch.empty(scores.shape[0], k, dtype=torch.int32, device=scores.device) if out is None else out
     ops.load()
-    torch.ops.xtier.topk_rows(scores.contiguous(), k, out)
+    torch.ops.xtier.topk_rows(scores.contiguous(), k, out,
+                              None if lengths is None else lengths.to(torch.int32).contiguous())
     return out
 
 

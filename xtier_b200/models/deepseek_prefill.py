@@ -176,10 +176,9 @@ class SparsePrefill:
             # indexer: top-k earlier positions of every query (slot = position: one sequence)
             qi = ops.linear(q_a[c0:c1], L['idx_q']).view(C, cfg.index_heads, cfg.index_dim)
             wi = ops.linear(h[c0:c1], L['idx_w']).float() * cfg.index_heads ** -0.5
-            zero = torch.zeros(C, dtype=torch.int32, device=q.device)
-            sc = dsa.index_scores(qi, wi, self.index[li], zero, pc + 1, out=self.scores[:C], err=self.idx_err,
-                                  per_cta=2 if C % 2 == 0 else 1)
-            idx = dsa.topk(sc, self.topk)
+            lens = pc + 1
+            sc = dsa.index_scores_prefill(qi, wi, self.index[li], 0, lens, out=self.scores[:C], err=self.idx_err)
+            idx = dsa.topk(sc, self.topk, lengths=lens)
             o_lat = torch.empty(C, cfg.heads, cfg.kv_lora, dtype=torch.bfloat16, device=q.device)
             torch.ops.xtier.mla_flash(qf, idx, lc.codes, lc.scales, lc.rope, None, None, o_lat, float(scale), 1,
                                       self.ws.err)
