@@ -342,7 +342,7 @@ def time_ttft(args, ctx: Ctx, model) -> dict:
     from xtier_b200.models.deepseek_prefill import SparsePrefill
     T = args.ttft_tokens
     try:
-        sp = SparsePrefill(model, T, q_chunk=args.ttft_q_chunk, moe_chunk=4096)
+        sp = SparsePrefill(model, T, q_chunk=args.ttft_q_chunk, moe_chunk=16384)
         ids = torch.randint(0, model.cfg.vocab, (T,), generator=torch.Generator().manual_seed(77))
         mine = ids[ctx.rank * sp.Tl:(ctx.rank + 1) * sp.Tl].cuda()
         t0 = time.time()

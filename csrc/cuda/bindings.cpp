@@ -571,7 +571,7 @@ void dsa_index_tc(const Tensor &q8, const Tensor &w, const Tensor &codes, const 
 
 void moe_grouped(const Tensor &x, const Tensor &codes, const Tensor &scales, const Tensor &gscale,
                  const Tensor &tiles, bool gate_up, int64_t I, int64_t fmt, const std::optional<Tensor> &route_w,
-                 const Tensor &out, const Tensor &err) {
+                 const Tensor &out, const Tensor &err, const std::optional<Tensor> &dst_rows) {
     cuda_contig(x, "x");
     cuda_contig(codes, "codes");
     cuda_contig(scales, "scales");
@@ -584,13 +584,18 @@ void moe_grouped(const Tensor &x, const Tensor &codes, const Tensor &scales, con
         check(out.scalar_type() == at::kBFloat16 && out.size(0) == R && out.size(1) == I && N_rows == 2 * I,
               "moe_grouped gate_up: mid [R, I] bf16");
     else
-        check(out.scalar_type() == at::kFloat && out.size(0) == R && out.size(1) == N_rows && route_w.has_value(),
-              "moe_grouped down: y [R, H] f32 and route weights");
+        check(out.scalar_type() == at::kFloat && (dst_rows.has_value() || out.size(0) == R) &&
+                  out.size(1) == N_rows && route_w.has_value(),
+              "moe_grouped down: y [R, H] f32 (any row count with dst_rows) and route weights");
+    if (dst_rows.has_value())
+        check(!gate_up && dst_rows->scalar_type() == at::kInt && dst_rows->is_contiguous() && dst_rows->numel() == R,
+              "moe_grouped: dst_rows int32 [R] (down only)");
     c10::cuda::CUDAGuard g(x.device());
     check_rc(xt_moe_grouped(x.data_ptr(), int(R), codes.data_ptr(), int(slots), ptr<const int32_t>(tiles),
                             int(tiles.size(0)), gate_up ? 1 : 0, int(K), int(N_rows), int(I), int(fmt),
                             scales.data_ptr(), ptr<const float>(gscale), optr<const float>(route_w),
-                            gate_up ? out.data_ptr() : nullptr, gate_up ? nullptr : ptr<float>(out),
+                            optr<const int32_t>(dst_rows), gate_up ? out.data_ptr() : nullptr,
+                            gate_up ? nullptr : ptr<float>(out),
                             int(out.size(1)), ptr<int>(err), stream()),
              "moe_grouped");
 }
@@ -729,7 +734,7 @@ TORCH_LIBRARY(xtier, m) {
     m.def("dsa_index_pf(Tensor q8, Tensor w, Tensor codes, Tensor kscale, int row_base, Tensor len, "
           "Tensor(a!) scores, int splits, Tensor(b!) err) -> ()");
     m.def("moe_grouped(Tensor x, Tensor codes, Tensor scales, Tensor gscale, Tensor tiles, bool gate_up, int I, "
-          "int fmt, Tensor? route_w, Tensor(a!) out, Tensor(b!) err) -> ()");
+          "int fmt, Tensor? route_w, Tensor(a!) out, Tensor(b!) err, Tensor? dst_rows=None) -> ()");
     m.def("dsa_index_tc(Tensor q8, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, Tensor(a!) scores, "
           "int nq, Tensor(b!) err) -> ()");
     m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");

@@ -45,6 +45,7 @@ struct GpParams {
     const uint8_t *scales;    // [slots, N_rows, K / bs]
     const float *gscale;      // GATE_UP: g13 [slots, 2]; DOWN: g2 [slots]
     const float *route_w;     // DOWN: [R] route weight of each row of X
+    const int32_t *dst_row;   // DOWN, optional: [R] the Y row of each row of X (-1: none); null: the same row
     __nv_bfloat16 *mid;       // GATE_UP out: [R, I]
     float *y;                 // DOWN out: [R, H]
     int out_cols;             // I (gate/up) or H (down)
@@ -296,13 +297,14 @@ __global__ void __launch_bounds__(GP_THREADS, 1)
                     }
                 } else {
                     const float scale = rit < vrows ? p.route_w[row] * p.gscale[slot] : 0.f;
+                    const int yrow = rit < vrows ? (p.dst_row ? p.dst_row[row] : row) : -1;
 #pragma unroll 1
                     for (int c0 = 0; c0 < GP_BN; c0 += 32) {
                         uint32_t r[32];
                         tc::tmem_ld32(base + uint32_t(c0), r);
                         tc::tmem_ld_wait();
-                        if (rit < vrows) {
-                            float *dst = p.y + size_t(row) * p.out_cols + nt * GP_BN + c0;
+                        if (yrow >= 0) {
+                            float *dst = p.y + size_t(yrow) * p.out_cols + nt * GP_BN + c0;
 #pragma unroll
                             for (int v = 0; v < 8; ++v)
                                 reinterpret_cast<float4 *>(dst)[v] =
@@ -351,7 +353,7 @@ extern "C" {
 // scales [slots * N_rows, K/bs]. gate_up: mid [R, I] = SwiGLU(...); else y [R, H] = w * g2 * (x . W2^T).
 int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int32_t *tiles, int T, int gate_up,
                    int K, int N_rows, int I, int fmt, const void *scales, const float *gscale, const float *route_w,
-                   void *mid, float *y, int out_cols, int *error, cudaStream_t stream) {
+                   const int32_t *dst_row, void *mid, float *y, int out_cols, int *error, cudaStream_t stream) {
     if (T <= 0) return 0;
     if (K % GP_BK || R % GP_BM || N_rows % (gate_up ? 2 : GP_BN) || (gate_up && I % 64)) return -2;
     auto fn = gp_encode_fn();
@@ -387,6 +389,7 @@ int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int
     p.scales = static_cast<const uint8_t *>(scales);
     p.gscale = gscale;
     p.route_w = route_w;
+    p.dst_row = dst_row;
     p.mid = static_cast<__nv_bfloat16 *>(mid);
     p.y = y;
     p.out_cols = out_cols;

@@ -200,6 +200,7 @@ int xt_dsa_index_pf(const void *q8, const float *w, const void *codes, int64_t s
                     cudaStream_t stream);
 int xt_moe_grouped(const void *x, int R, const void *codes, int slots, const int32_t *tiles, int T, int gate_up,
                    int K, int N_rows, int I, int fmt, const void *scales, const float *gscale, const float *route_w,
+                   const int32_t *dst_row,
                    void *mid, float *y, int out_cols, int *error, cudaStream_t stream);
 int xt_gather_rows(const void *x, const int32_t *src, void *X, int R, int H, cudaStream_t stream);
 int xt_route_combine(const float *Ya, const int32_t *da, int ka, const float *Yb, const int32_t *db, int kb,

@@ -61,11 +61,12 @@ def _tiles(runs: torch.Tensor, n_tiles: int, device) -> torch.Tensor:
 
 
 def grouped_routes(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: ExpertWeights,
-                   err: torch.Tensor | None = None):
+                   err: torch.Tensor | None = None, route_rows: bool = False, out: torch.Tensor | None = None):
     """x [m, H] BF16, slots [m, k] GPU slot per route (-1 skips), w [m, k] route weights -> (Y [R, H] FP32: every
     computed route's w * MoE_expert(x) row, dest [m * k] int32: the Y row of each route or -1); (None, None) when no
     route has a slot. Token rows are gathered into the padded per-expert runs by a kernel (csrc/cuda/moe_prefill.cu
-    gather_rows); the down GEMM's epilogue applies the route weight."""
+    gather_rows); the down GEMM's epilogue applies the route weight. route_rows=True: Y [m * k, H] indexed by route
+    (t * k + j), written there directly by the down GEMM's epilogue (into `out` when given)."""
     m, k = slots.shape
     H, I = pool.hidden, pool.inter
     dev = x.device
@@ -86,11 +87,18 @@ def grouped_routes(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: 
     mid = torch.empty(R, I, dtype=torch.bfloat16, device=dev)
     torch.ops.xtier.moe_grouped(X, pool.w13, pool.s13, pool.g13.float().contiguous(), _tiles(runs, I // 64, dev), True,
                                 I, fmt, None, mid, err)
-    Y = torch.empty(R, H, dtype=torch.float32, device=dev)
-    torch.ops.xtier.moe_grouped(mid, pool.w2, pool.s2, pool.g2.float().contiguous(), _tiles(runs, H // 128, dev),
-                                False, I, fmt, rw, Y, err)
     dest = torch.full((m * k,), -1, dtype=torch.int32, device=dev)
-    dest[order] = rows.int()
+    if route_rows:
+        Y = torch.empty(m * k, H, dtype=torch.float32, device=dev) if out is None else out
+        dst = torch.full((R,), -1, dtype=torch.int32, device=dev)
+        dst[rows] = order.int()
+        dest[order] = order.int()
+    else:
+        Y = torch.empty(R, H, dtype=torch.float32, device=dev)
+        dst = None
+        dest[order] = rows.int()
+    torch.ops.xtier.moe_grouped(mid, pool.w2, pool.s2, pool.g2.float().contiguous(), _tiles(runs, H // 128, dev),
+                                False, I, fmt, rw, Y, err, dst)
     return Y, dest
 
 

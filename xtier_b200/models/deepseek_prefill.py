@@ -50,7 +50,7 @@ class EPPrefillMoE:
     """Prefill-sized calls of an EPMoE layer (every expert in some rank's HBM): route, all-to-all to the owners,
     grouped GEMMs on the owner's pool, all-to-all back, route-ordered combine."""
 
-    def __init__(self, chunk: int = 4096):
+    def __init__(self, chunk: int = 16384):
         self.chunk = chunk
         self.err = None
         self.count = None
@@ -59,6 +59,7 @@ class EPPrefillMoE:
         c = moe.comm
         W, kk, spr = c.W, c.k, c.spr
         dev = x.device
+        H = x.shape[1]
         if self.err is None:
             self.err = torch.zeros(1, dtype=torch.int32, device=dev)
             self.count = torch.zeros(self.chunk, dtype=torch.int32, device=dev)
@@ -77,9 +78,15 @@ class EPPrefillMoE:
             flat = slots.flatten().long()
             if bool((flat < 0).any()):
                 raise RuntimeError('EP prefill: a route has no GPU slot (the CPU tier is a decode path)')
+            add_c = None if add is None else add[s:e].contiguous()
+            if W == 1:   # every route is local: grouped GEMMs straight from the chunk, rows written in route order
+                Y, dest = grouped_routes(xc, slots, wt, moe.local, self.err, route_rows=True)
+                torch.ops.xtier.route_combine(Y, dest, None, None, add_c, out[s:e])
+                self.last = (ids, wt)
+                continue
             owner = flat // spr
             n = flat.numel()
-            order = torch.sort(owner * n + torch.arange(n, device=dev)).indices   # by owner, route order inside
+            order = torch.sort(owner, stable=True).indices   # by owner, route order inside
             send = torch.bincount(owner, minlength=W)
             recv = torch.empty_like(send)
             _a2a(recv, send, [1] * W, [1] * W)
@@ -87,27 +94,22 @@ class EPPrefillMoE:
             rows = xc.index_select(0, order // kk)
             meta = torch.stack([(flat % spr)[order].int(), wt.flatten()[order].view(torch.int32)], 1).contiguous()
             nr = sum(rc)
-            r_rows = torch.empty(nr, xc.shape[1], dtype=xc.dtype, device=dev)
+            r_rows = torch.empty(nr, H, dtype=xc.dtype, device=dev)
             r_meta = torch.empty(nr, 2, dtype=torch.int32, device=dev)
             _a2a(r_rows, rows, rc, sc)
             _a2a(r_meta, meta, rc, sc)
             del rows
-            y = torch.empty(nr, xc.shape[1], dtype=torch.float32, device=dev)
-            if nr:
+            y = torch.empty(nr, H, dtype=torch.float32, device=dev)
+            if nr:   # the received routes' rows, written in received order by the down GEMM
                 r_w = r_meta[:, 1:].contiguous().view(torch.float32)
-                Y, dest = grouped_routes(r_rows, r_meta[:, :1].contiguous(), r_w, moe.local, self.err)
-                y.copy_(Y.index_select(0, dest.long()))
-                del Y
+                grouped_routes(r_rows, r_meta[:, :1].contiguous(), r_w, moe.local, self.err, route_rows=True, out=y)
             del r_rows
-            back = torch.empty(n, xc.shape[1], dtype=torch.float32, device=dev)
+            back = torch.empty(n, H, dtype=torch.float32, device=dev)
             _a2a(back, y, sc, rc)
             del y
-            Ysrc = torch.empty_like(back)
-            Ysrc[order] = back
-            del back
-            da = torch.arange(n, dtype=torch.int32, device=dev)
-            torch.ops.xtier.route_combine(Ysrc, da, None, None, None if add is None else add[s:e].contiguous(),
-                                          out[s:e])
+            inv = torch.empty(n, dtype=torch.int32, device=dev)   # route -> its row of `back`
+            inv[order] = torch.arange(n, dtype=torch.int32, device=dev)
+            torch.ops.xtier.route_combine(back, inv, None, None, add_c, out[s:e])
             self.last = (ids, wt)   # the last chunk's routes (tests)
         return out
 
@@ -119,7 +121,7 @@ class SparsePrefill:
     dense=True replaces the indexer + sparse attention by causal attention over every earlier key (the expanded form
     of `DeepSeekV3Model._mla_prefill`), the oracle of the tests."""
 
-    def __init__(self, model: DeepSeekV3Model, total: int, q_chunk: int = 1024, moe_chunk: int = 4096,
+    def __init__(self, model: DeepSeekV3Model, total: int, q_chunk: int = 1024, moe_chunk: int = 16384,
                  dense: bool = False):
         cfg = model.cfg
         env = xdist.get()
