@@ -510,23 +510,34 @@ void mla_decode(const Tensor &q, const Tensor &idx, const Tensor &codes, const T
              "mla_decode");
 }
 
+// q [Q, 128, 576] (latent then rotary values), or with q_rope: q [Q, 128, 512] and q_rope [Q, 128, 64]; q, q_rope and
+// out [Q, 128, 512] may be strided views (unit stride along the last dim).
 void mla_flash(const Tensor &q, const Tensor &idx, const Tensor &codes, const Tensor &scales, const Tensor &rope,
                const std::optional<Tensor> &part_o, const std::optional<Tensor> &part_ml, const Tensor &out,
-               double scale, int64_t splits, const Tensor &err) {
-    cuda_contig(q, "q");
+               double scale, int64_t splits, const Tensor &err, const std::optional<Tensor> &q_rope) {
     cuda_contig(idx, "idx");
-    cuda_contig(out, "out");
+    auto rows_ok = [](const Tensor &t, int64_t d) {
+        return t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 3 && t.size(1) == 128 && t.size(2) == d &&
+               t.stride(2) == 1;
+    };
     const int64_t Q = q.size(0), nsel = idx.size(1);
-    check(q.size(1) == 128 && q.size(2) == 576 && idx.size(0) == Q && idx.scalar_type() == at::kInt && nsel % 64 == 0,
-          "mla_flash q [Q, 128, 576] bf16, idx [Q, nsel] int32 (nsel % 64 == 0)");
-    check(out.numel() == Q * 128 * 512, "mla_flash out [Q, 128, 512]");
+    check(rows_ok(q, q_rope ? 512 : 576) && (!q_rope || (rows_ok(*q_rope, 64) && q_rope->size(0) == Q)),
+          "mla_flash: q [Q, 128, 576] bf16, or q [Q, 128, 512] and q_rope [Q, 128, 64] (unit stride along the last dim)");
+    check(idx.size(0) == Q && idx.scalar_type() == at::kInt && nsel % 64 == 0,
+          "mla_flash idx [Q, nsel] int32 (nsel % 64 == 0)");
+    check(rows_ok(out, 512) && out.size(0) == Q, "mla_flash out [Q, 128, 512] bf16 (unit stride along the last dim)");
     const int64_t nblk = nsel / 64, bps = (nblk + splits - 1) / splits, eff = (nblk + bps - 1) / bps;
     if (eff > 1)
-        check(part_o && part_ml && part_o->numel() >= Q * eff * 128 * 512 && part_ml->numel() >= Q * eff * 128 * 2,
-              "mla_flash: split partials too small");
+        check(part_o && part_ml && part_o->numel() >= Q * eff * 128 * 512 && part_ml->numel() >= Q * eff * 128 * 2 &&
+                  out.is_contiguous(),
+              "mla_flash: split partials too small, or a strided out with splits");
+    const auto *qp = static_cast<const __nv_bfloat16 *>(q.data_ptr());
+    const void *qr = q_rope ? q_rope->data_ptr() : static_cast<const void *>(qp + 512);
+    const int64_t qr_ts = q_rope ? q_rope->stride(0) : q.stride(0), qr_hs = q_rope ? q_rope->stride(1) : q.stride(1);
     c10::cuda::CUDAGuard g(q.device());
-    check_rc(xt_mla_flash(q.data_ptr(), ptr<const int32_t>(idx), int(Q), int(nsel), codes.data_ptr(), scales.data_ptr(),
-                          rope.data_ptr(), optr<float>(part_o), optr<float>(part_ml), out.data_ptr(), float(scale),
+    check_rc(xt_mla_flash(qp, q.stride(0), q.stride(1), qr, qr_ts, qr_hs, ptr<const int32_t>(idx), int(Q), int(nsel),
+                          codes.data_ptr(), scales.data_ptr(), rope.data_ptr(), optr<float>(part_o),
+                          optr<float>(part_ml), out.data_ptr(), out.stride(0), out.stride(1), float(scale),
                           int(splits), ptr<int>(err), stream()),
              "mla_flash");
 }
@@ -686,6 +697,35 @@ void head_gemm(const Tensor &x, const Tensor &w, const Tensor &y, const std::opt
     check_rc(xt_head_gemm(&p, int(w.size(0)), stream()), "head_gemm");
 }
 
+void rope_heads(const Tensor &x, const Tensor &pos, double theta, const Tensor &out) {
+    // x [T, H, d] and out [T, H, d] bf16 views with unit stride along d; pos int32 [T]
+    check(x.is_cuda() && x.dim() == 3 && x.stride(2) == 1 && out.dim() == 3 && out.stride(2) == 1 &&
+              x.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
+              x.sizes() == out.sizes() && pos.scalar_type() == at::kInt && pos.is_contiguous() &&
+              pos.numel() == x.size(0),
+          "rope_heads: x, out [T, H, d] bf16 (unit stride along d), pos int32 [T]");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_rope_heads(x.data_ptr(), x.stride(0), x.stride(1), ptr<const int32_t>(pos), float(theta),
+                           out.data_ptr(), out.stride(0), out.stride(1), int(x.size(0)), int(x.size(1)),
+                           int(x.size(2)), stream()),
+             "rope_heads");
+}
+
+void dsa_quant_q(const Tensor &q, const Tensor &w, double w_scale, const Tensor &q8, const Tensor &w8) {
+    cuda_contig(q, "q");
+    cuda_contig(w, "w");
+    cuda_contig(q8, "q8");
+    cuda_contig(w8, "w8");
+    check(q.scalar_type() == at::kBFloat16 && q.size(-1) == 128 && w.scalar_type() == at::kBFloat16 &&
+              w.numel() * 128 == q.numel() && q8.scalar_type() == at::kByte && q8.numel() == q.numel() &&
+              w8.scalar_type() == at::kFloat && w8.numel() == w.numel(),
+          "dsa_quant_q: q [..., 128] bf16, w bf16 (one per row), q8 u8, w8 f32");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_dsa_quant_q(q.data_ptr(), w.data_ptr(), float(w_scale), q8.data_ptr(), ptr<float>(w8),
+                            int(w.numel()), stream()),
+             "dsa_quant_q");
+}
+
 void silu_mul(const Tensor &in, const Tensor &out) {
     cuda_contig(in, "in");
     cuda_contig(out, "out");
@@ -702,6 +742,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("mla_prep(Tensor inp, int q_lora, Tensor q_norm, Tensor kv_norm, Tensor pos, Tensor slot, float eps, "
           "float theta, Tensor(a!) q_out, Tensor(b!) codes, Tensor(c!) scales, Tensor(d!) rope, Tensor(e!)? lat_out) "
           "-> ()");
+    m.def("rope_heads(Tensor x, Tensor pos, float theta, Tensor(a!) out) -> ()");
+    m.def("dsa_quant_q(Tensor q, Tensor w, float w_scale, Tensor(a!) q8, Tensor(b!) w8) -> ()");
     m.def("head_gemm(Tensor x, Tensor w, Tensor(a!) y, Tensor? pos, int rope_x, int rope_y, int rope_dims, "
           "float theta) -> ()");
     m.def("silu_mul(Tensor inp, Tensor(a!) out) -> ()");
@@ -739,7 +781,7 @@ TORCH_LIBRARY(xtier, m) {
           "int nq, Tensor(b!) err) -> ()");
     m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");
     m.def("mla_flash(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!)? part_o, "
-          "Tensor(b!)? part_ml, Tensor(c!) out, float scale, int splits, Tensor(d!) err) -> ()");
+          "Tensor(b!)? part_ml, Tensor(c!) out, float scale, int splits, Tensor(d!) err, Tensor? q_rope=None) -> ()");
     m.def("mla_decode(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!) kg, Tensor(b!) vt, "
           "Tensor(c!) part_o, Tensor(d!) part_ml, Tensor(e!) out, float scale, Tensor(f!) err) -> ()");
     m.def("gemm_rs(Tensor a, Tensor b, Tensor peer, Tensor(a!) state, Tensor? residual, Tensor(b!) out, "
@@ -758,6 +800,8 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("add_rmsnorm", &add_rmsnorm);
     m.impl("mla_prep", &mla_prep);
     m.impl("head_gemm", &head_gemm);
+    m.impl("rope_heads", &rope_heads);
+    m.impl("dsa_quant_q", &dsa_quant_q);
     m.impl("silu_mul", &silu_mul);
     m.impl("qk_norm_rope_kv", &qk_norm_rope_kv);
     m.impl("attn_decode", &attn_decode);

@@ -375,6 +375,27 @@ __global__ void __launch_bounds__(IP_THREADS, 1)
     }
 }
 
+// Indexer queries to FP8, one warp per (query, head) row of 128: s = max(amax / 448, 1e-12), q8 = E4M3(q / s) (IEEE
+// division, round to nearest even), w8 = (w * w_scale) * s, the head weight carrying the scale (relu commutes with a
+// positive scale). w is BF16 [rows] (one weight per row).
+__global__ void __launch_bounds__(256) dsa_quant_q_kernel(const __nv_bfloat16 *__restrict__ q,
+                                                         const __nv_bfloat16 *__restrict__ w, float w_scale,
+                                                         uint8_t *__restrict__ q8, float *__restrict__ w8, int rows) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const uint2 raw = reinterpret_cast<const uint2 *>(q + size_t(r) * IDX_DIM)[lane];
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&raw.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&raw.y));
+    float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y)));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float sc = fmaxf(m / 448.f, 1e-12f);
+    const uint32_t packed = uint32_t(f32_to_e4m3(a.x / sc)) | (uint32_t(f32_to_e4m3(a.y / sc)) << 8) |
+                            (uint32_t(f32_to_e4m3(b.x / sc)) << 16) | (uint32_t(f32_to_e4m3(b.y / sc)) << 24);
+    reinterpret_cast<uint32_t *>(q8 + size_t(r) * IDX_DIM)[lane] = packed;
+    if (lane == 0) w8[r] = (__bfloat162float(w[r]) * w_scale) * sc;
+}
+
 // order-preserving image of a float: larger float -> larger unsigned (NaN never occurs here)
 __device__ __forceinline__ uint32_t fkey(float f) {
     const uint32_t u = __float_as_uint(f);
@@ -623,6 +644,14 @@ int xt_dsa_index_pf(const void *q8, const float *w, const void *codes, int64_t s
     if (xt_smem_optin(dsa_index_pf_kernel, IpSmem::BYTES) != cudaSuccess) return -4;
     dsa_index_pf_kernel<<<dim3(splits, groups), IP_THREADS, IpSmem::BYTES, stream>>>(mk, mq, w, kscale, row_base, len,
                                                                                   scores, Q, max_len, error);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int xt_dsa_quant_q(const void *q, const void *w, float w_scale, void *q8, float *w8, int rows, cudaStream_t stream) {
+    if (rows <= 0) return 0;
+    dsa_quant_q_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(q),
+                                                          static_cast<const __nv_bfloat16 *>(w), w_scale,
+                                                          static_cast<uint8_t *>(q8), w8, rows);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

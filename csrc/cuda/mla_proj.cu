@@ -220,6 +220,24 @@ __global__ void __launch_bounds__(MP_THREADS) silu_mul_kernel(const __nv_bfloat1
 
 using namespace xt;
 
+// y[t, h, :d] = NeoX RoPE of x[t, h, :d] at pos[t] (strided over tokens and heads); one warp per (token, head)
+__global__ void __launch_bounds__(256) rope_heads_kernel(const __nv_bfloat16 *__restrict__ x, int64_t xs_t, int64_t xs_h,
+                                                        const int32_t *__restrict__ pos, float theta,
+                                                        __nv_bfloat16 *__restrict__ y, int64_t ys_t, int64_t ys_h,
+                                                        int T, int H, int d) {
+    const long long w = blockIdx.x * 8ll + (threadIdx.x >> 5);
+    if (w >= (long long)T * H) return;
+    const int t = int(w / H), h = int(w % H), lane = threadIdx.x & 31;
+    const __nv_bfloat16 *xr = x + t * xs_t + h * xs_h;
+    __nv_bfloat16 *yr = y + t * ys_t + h * ys_h;
+    const int half = d / 2;
+    for (int i = lane; i < half; i += 32) {
+        const float2 r = rope_pair(bf16_to_f(xr[i]), bf16_to_f(xr[i + half]), float(pos[t]), i, d, theta);
+        yr[i] = __float2bfloat16(r.x);
+        yr[i + half] = __float2bfloat16(r.y);
+    }
+}
+
 extern "C" {
 
 int xt_mla_prep(const void *in, int ld, int q_lora, const void *q_norm, const void *kv_norm, const int32_t *pos,
@@ -245,6 +263,17 @@ int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream) {
     const cudaError_t e = xt_launch(silu_mul_kernel, dim3(grid), dim3(MP_THREADS), 0, stream,
                                     static_cast<const __nv_bfloat16 *>(in), static_cast<__nv_bfloat16 *>(out), T, I);
     return e == cudaSuccess ? 0 : -1;
+}
+
+int xt_rope_heads(const void *x, int64_t xs_t, int64_t xs_h, const int32_t *pos, float theta, void *y, int64_t ys_t,
+                  int64_t ys_h, int T, int H, int d, cudaStream_t stream) {
+    if (T <= 0 || H <= 0) return 0;
+    if (d <= 0 || d % 2) return -2;
+    const long long warps = (long long)T * H;
+    rope_heads_kernel<<<unsigned((warps + 7) / 8), 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(x), xs_t, xs_h,
+                                                                     pos, theta, static_cast<__nv_bfloat16 *>(y), ys_t,
+                                                                     ys_h, T, H, d);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 int xt_head_gemm(const HeadGemmParams *pp, int heads, cudaStream_t stream) {

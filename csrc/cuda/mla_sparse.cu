@@ -454,10 +454,11 @@ XT_DEV int mf_row_exp(float amax) {
 }
 
 __global__ void __launch_bounds__(MF_THREADS, 1)
-    mla_flash_kernel(const __grid_constant__ CUtensorMap tma_q, const int32_t *__restrict__ idx, int nsel, int bps,
-                     int nblk, const uint8_t *__restrict__ codes, const uint8_t *__restrict__ scales,
-                     const __nv_bfloat16 *__restrict__ rope, float scale_log2, __nv_bfloat16 *__restrict__ out,
-                     float *__restrict__ part_o, float *__restrict__ part_ml, int *error) {
+    mla_flash_kernel(const __grid_constant__ CUtensorMap tma_ql, const __grid_constant__ CUtensorMap tma_qr,
+                     const int32_t *__restrict__ idx, int nsel, int bps, int nblk, const uint8_t *__restrict__ codes,
+                     const uint8_t *__restrict__ scales, const __nv_bfloat16 *__restrict__ rope, float scale_log2,
+                     __nv_bfloat16 *__restrict__ out, int64_t out_ts, int64_t out_hs, float *__restrict__ part_o,
+                     float *__restrict__ part_ml, int *error) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *qs = smem;                                   // [9][128 x 64]
@@ -498,7 +499,8 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
             tc::mbar_init(&pfull[s], 4);
         }
         tc::fence_barrier_init();
-        tc::prefetch_tmap(&tma_q);
+        tc::prefetch_tmap(&tma_ql);
+        tc::prefetch_tmap(&tma_qr);
     }
     if (warp == 1) {
         tc::tmem_alloc(tmem_slot, 512);
@@ -575,9 +577,10 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
     } else if (warp >= 2 && warp < 6) {
         const int w = warp - 2;
         const int kk = w * 16 + (lane >> 1), half = lane & 1;   // key of the block, 32-dim half of a k-block
-        if (w == 0 && lane == 0 && nb > 0) {   // the query, once
+        if (w == 0 && lane == 0 && nb > 0) {   // the query, once: eight latent k-blocks and the rotary one
             tc::mbar_arrive_expect_tx(qfull, MfSmem::Q);
-            for (int kb = 0; kb < 9; ++kb) tc::tma_load_2d(qs + kb * MfSmem::QKB, &tma_q, qfull, kb * 64, q * MLA_H);
+            for (int kb = 0; kb < 8; ++kb) tc::tma_load_3d(qs + kb * MfSmem::QKB, &tma_ql, qfull, kb * 64, q, 0);
+            tc::tma_load_3d(qs + 8 * MfSmem::QKB, &tma_qr, qfull, 0, q, 0);
         }
         int stage = 0;
         uint32_t phase = 0;
@@ -778,7 +781,7 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                 tc::tmem_ld32(lane_base + uint32_t(c * 32), r);
                 tc::tmem_ld_wait();
                 if (splits == 1) {
-                    __nv_bfloat16 *dst = out + (size_t(q) * MLA_H + row) * MLA_L + j * 256 + c * 32;
+                    __nv_bfloat16 *dst = out + q * out_ts + row * out_hs + j * 256 + c * 32;
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         __nv_bfloat162 o[4];
@@ -872,6 +875,21 @@ bool mla_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, ui
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [Q, 128 heads, d] BF16 view (unit stride along d, element strides ts, hs) as a 3-D map (d, Q, heads) whose box is
+// one query's 128 heads x 64 values: a 128-row 128-byte-swizzled tile
+bool mla_map3(CUtensorMap *map, const void *ptr, int d, int Q, int64_t ts, int64_t hs) {
+    auto fn = mla_encode_fn();
+    if (!fn || ts <= 0 || hs <= 0 || (ts * 2) % 16 || (hs * 2) % 16 || reinterpret_cast<uintptr_t>(ptr) % 16)
+        return false;
+    cuuint64_t dims[3] = {cuuint64_t(d), cuuint64_t(Q), cuuint64_t(MLA_H)};
+    cuuint64_t strides[2] = {cuuint64_t(ts) * 2, cuuint64_t(hs) * 2};
+    cuuint32_t box[3] = {64, 1, MLA_H};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 extern "C" {
@@ -917,23 +935,29 @@ int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-// Flash form of xt_mla_decode: the same inputs, no gather scratch. part_o [Q, splits, 128, 512] f32 and part_ml [Q,
-// splits, 128, 2] are used only when splits > 1 (the splits' partials, merged by mla_merge). nsel % 64 == 0.
-int xt_mla_flash(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
-                 const void *rope, float *part_o, float *part_ml, void *out, float scale, int splits, int *error,
-                 cudaStream_t stream) {
+// Flash form of xt_mla_decode without gather scratch. The query comes as two views of [Q, 128 heads, d] BF16 with
+// unit stride along d and element strides (token, head): the latent part q_lat (d = 512) and the rotary part q_rope
+// (d = 64); out [Q, 128, 512] BF16 likewise (token and head strides out_ts, out_hs). part_o [Q, splits, 128, 512] f32
+// and part_ml [Q, splits, 128, 2] are used only when splits > 1 (the splits' partials, merged by mla_merge, which
+// writes a contiguous out). nsel % 64 == 0.
+int xt_mla_flash(const void *q_lat, int64_t ql_ts, int64_t ql_hs, const void *q_rope, int64_t qr_ts, int64_t qr_hs,
+                 const int32_t *idx, int Q, int nsel, const void *codes, const void *scales, const void *rope,
+                 float *part_o, float *part_ml, void *out, int64_t out_ts, int64_t out_hs, float scale, int splits,
+                 int *error, cudaStream_t stream) {
     if (Q <= 0 || Q > 65535 || nsel <= 0 || nsel % MF_NB || splits < 1) return -2;
     const int nblk = nsel / MF_NB;
     const int bps = (nblk + splits - 1) / splits;
     splits = (nblk + bps - 1) / bps;
     if (splits > 1 && (!part_o || !part_ml)) return -2;
-    CUtensorMap mq;
-    if (!mla_map(&mq, q, uint64_t(Q) * MLA_H, MLA_D, MLA_H)) return -3;
+    if (splits > 1 && (out_ts != int64_t(MLA_H) * MLA_L || out_hs != MLA_L)) return -2;
+    if ((out_ts | out_hs) % 8 || reinterpret_cast<uintptr_t>(out) % 16) return -2;
+    CUtensorMap ml, mr;
+    if (!mla_map3(&ml, q_lat, MLA_L, Q, ql_ts, ql_hs) || !mla_map3(&mr, q_rope, MLA_R, Q, qr_ts, qr_hs)) return -3;
     if (xt_smem_optin(mla_flash_kernel, int(MfSmem::BYTES)) != cudaSuccess) return -4;
     mla_flash_kernel<<<dim3(2, splits, Q), MF_THREADS, MfSmem::BYTES, stream>>>(
-        mq, idx, nsel, bps, nblk, static_cast<const uint8_t *>(codes), static_cast<const uint8_t *>(scales),
+        ml, mr, idx, nsel, bps, nblk, static_cast<const uint8_t *>(codes), static_cast<const uint8_t *>(scales),
         static_cast<const __nv_bfloat16 *>(rope), scale * 1.4426950408889634f, static_cast<__nv_bfloat16 *>(out),
-        part_o, part_ml, error);
+        out_ts, out_hs, part_o, part_ml, error);
     if (cudaGetLastError() != cudaSuccess) return -1;
     if (splits > 1) {
         mla_merge_kernel<<<dim3(MLA_H, Q), 128, 0, stream>>>(part_o, part_ml, splits,

@@ -195,6 +195,9 @@ int xt_dsa_index_tc(const void *q8, const float *w, const void *codes, int64_t s
                     const int64_t *base, const int32_t *len, float *scores, int Q, int max_len, int nq, int *error,
                     cudaStream_t stream);
 int xt_topk_rows(const float *scores, int rows, int n, int K, const int32_t *len, int32_t *out, cudaStream_t stream);
+int xt_dsa_quant_q(const void *q, const void *w, float w_scale, void *q8, float *w8, int rows, cudaStream_t stream);
+int xt_rope_heads(const void *x, int64_t xs_t, int64_t xs_h, const int32_t *pos, float theta, void *y, int64_t ys_t,
+                  int64_t ys_h, int T, int H, int d, cudaStream_t stream);
 int xt_dsa_index_pf(const void *q8, const float *w, const void *codes, int64_t slots, const float *kscale,
                     int64_t row_base, const int32_t *len, float *scores, int Q, int max_len, int splits, int *error,
                     cudaStream_t stream);
@@ -210,9 +213,10 @@ int xt_mla_prep(const void *in, int ld, int q_lora, const void *q_norm, const vo
                 void *lat_out, int T, cudaStream_t stream);
 int xt_head_gemm(const xt::HeadGemmParams *p, int heads, cudaStream_t stream);
 int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream);
-int xt_mla_flash(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
-                 const void *rope, float *part_o, float *part_ml, void *out, float scale, int splits, int *error,
-                 cudaStream_t stream);
+int xt_mla_flash(const void *q_lat, int64_t ql_ts, int64_t ql_hs, const void *q_rope, int64_t qr_ts, int64_t qr_hs,
+                 const int32_t *idx, int Q, int nsel, const void *codes, const void *scales, const void *rope,
+                 float *part_o, float *part_ml, void *out, int64_t out_ts, int64_t out_hs, float scale, int splits,
+                 int *error, cudaStream_t stream);
 int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
                   const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,
                   int *error, cudaStream_t stream);

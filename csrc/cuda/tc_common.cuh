@@ -52,6 +52,15 @@ XT_DEV void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x,
         : "memory");
 }
 
+// 3-D TMA tile load (x innermost, in elements).
+XT_DEV void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];\n" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 XT_DEV void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

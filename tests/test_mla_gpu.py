@@ -95,3 +95,51 @@ def test_mla_flash_growing_scores_rescale(cuda_ops):
     assert int(ws.err) == 0
     ref = reference_decode(q, idx, cache, default_scale())
     assert _rel(out, ref) < 2e-2, _rel(out, ref)
+
+
+def test_mla_flash_strided_query_and_output(cuda_ops):
+    """Flash MLA through head-major views (latent and rotary query parts as separate strided tensors, strided output)
+    equals the contiguous [Q, 128, 576] call bit for bit."""
+    from xtier_b200.attention.mla import LatentCache, default_scale, mla_flash
+    g = torch.Generator(device='cuda').manual_seed(41)
+    Q, n = 5, 1000
+    lc = LatentCache(1, n)
+    lc.write(torch.randn(n, 576, device='cuda', generator=g).bfloat16(), torch.arange(n, device='cuda'))
+    q = (torch.randn(Q, 128, 576, device='cuda', generator=g) * 0.5).bfloat16()
+    idx = torch.stack([torch.randperm(n, device='cuda', generator=g)[:256] for _ in range(Q)]).int()
+    ref = mla_flash(q, idx, lc, default_scale())
+    q_lat = q[..., :512].transpose(0, 1).contiguous()          # [128, Q, 512] head-major
+    q_pe = q[..., 512:].transpose(0, 1).contiguous()           # [128, Q, 64]
+    o = torch.zeros(128, Q, 512, dtype=torch.bfloat16, device='cuda')
+    mla_flash(q_lat.transpose(0, 1), idx, lc, default_scale(), out=o.transpose(0, 1), q_rope=q_pe.transpose(0, 1))
+    assert torch.equal(o.transpose(0, 1), ref)
+
+
+def test_rope_heads_and_fp8_query_quantization(cuda_ops):
+    """RoPE kernel over strided (token, head) views against the fp32 PyTorch rotation; the fused FP8 query
+    quantization against the PyTorch one (the same scales and weights; the E4M3 bytes agree but for rare ties
+    rounded the other way, one code step apart)."""
+    from xtier_b200 import ops
+    from xtier_b200.attention import dsa
+    from xtier_b200.models.deepseek_v3 import _rope
+    g = torch.Generator(device='cuda').manual_seed(42)
+    T, H = 300, 128
+    x = torch.randn(T, H, 192, device='cuda', generator=g).bfloat16()
+    pos = torch.randint(0, 70000, (T,), device='cuda', generator=g).int()
+    ref = _rope(x[..., 128:].transpose(0, 1), pos, 10000.0).transpose(0, 1).float()
+    out = torch.empty(H, T, 64, dtype=torch.bfloat16, device='cuda')
+    ops.rope_heads(x[..., 128:], pos, 10000.0, out.transpose(0, 1))
+    assert float((out.transpose(0, 1).float() - ref).abs().max()) < 0.05
+    assert float((out.transpose(0, 1).float() - ref).norm() / ref.norm()) < 5e-3
+    q = torch.randn(T, 64, 128, device='cuda', generator=g).bfloat16()
+    w = torch.randn(T, 64, device='cuda', generator=g).bfloat16()
+    q8_ref, w8_ref = dsa.quantize_queries(q, w.float() * 0.125)
+    q8 = torch.empty_like(q8_ref)
+    w8 = torch.empty_like(w8_ref)
+    torch.ops.xtier.dsa_quant_q(q, w, 0.125, q8, w8)
+    assert torch.allclose(w8, w8_ref, rtol=1e-6, atol=0)
+    diff = q8 != q8_ref
+    assert float(diff.float().mean()) < 1e-3
+    a = q8.view(torch.float8_e4m3fn).float()
+    b = q8_ref.view(torch.float8_e4m3fn).float()
+    assert bool(((a - b).abs() <= b.abs() * 0.125 + 2 ** -9).all())

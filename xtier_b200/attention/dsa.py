@@ -65,15 +65,21 @@ def index_scores(q: torch.Tensor, w: torch.Tensor, cache: IndexCache, rows: torc
 
 def index_scores_prefill(q: torch.Tensor, w: torch.Tensor, cache: IndexCache, row: int, lengths: torch.Tensor,
                          out: torch.Tensor | None = None, err: torch.Tensor | None = None,
-                         splits: int = 0) -> torch.Tensor:
+                         splits: int = 0, w_scale: float = 1.0) -> torch.Tensor:
     """Indexer scores of queries that share cache row `row` (a prefill chunk of one sequence): q [Q, 64, 128] BF16,
-    w [Q, 64] fp32, lengths [Q] -> scores [Q, max_len] fp32, valid in [0, lengths[i]) of row i (then -inf up to the
-    end of the last 128-key tile, unwritten beyond: pass the same lengths to topk). FP8 queries (E4M3 x E4M3 MMA),
-    4 queries per CTA over a pipelined key stream; `splits` key ranges per query group (0: chosen by the launcher)."""
+    head weights w_scale * w [Q, 64] (BF16: quantized with the queries by one kernel, or fp32), lengths [Q] -> scores
+    [Q, max_len] fp32, valid in [0, lengths[i]) of row i (then -inf up to the end of the last 128-key tile, unwritten
+    beyond: pass the same lengths to topk). FP8 queries (E4M3 x E4M3 MMA), 4 queries per CTA over a pipelined key
+    stream; `splits` key ranges per query group (0: chosen by the launcher)."""
     Q = q.shape[0]
     out = torch.empty(Q, cache.max_len, dtype=torch.float32, device=q.device) if out is None else out
     ops.load()
-    q8, w8 = quantize_queries(q, w)
+    if w.dtype == torch.bfloat16 and q.is_contiguous():   # one kernel: FP8 queries, scales into the head weights
+        q8 = torch.empty(q.shape, dtype=torch.uint8, device=q.device)
+        w8 = torch.empty(w.shape, dtype=torch.float32, device=q.device)
+        torch.ops.xtier.dsa_quant_q(q, w.contiguous(), float(w_scale), q8, w8)
+    else:
+        q8, w8 = quantize_queries(q, w.float() * w_scale)
     err = torch.zeros(1, dtype=torch.int32, device=q.device) if err is None else err
     torch.ops.xtier.dsa_index_pf(q8, w8, cache.codes, cache.scale, int(row) * cache.max_len,
                                  lengths.int().contiguous(), out, int(splits), err)

@@ -99,17 +99,22 @@ def flash_splits(queries: int, nsel: int, sms: int = 148) -> int:
 
 
 def mla_flash(q: torch.Tensor, idx: torch.Tensor, cache: LatentCache, scale: float, splits: int = 1,
-              ws: FlashWorkspace | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+              ws: FlashWorkspace | None = None, out: torch.Tensor | None = None,
+              q_rope: torch.Tensor | None = None) -> torch.Tensor:
     """mla_decode in one pass (csrc/cuda/mla_sparse.cu mla_flash): q [Q, 128, 576] BF16 (absorbed), idx [Q, nsel]
-    int32 cache slots (-1: none; nsel % 64 == 0) -> latent output [Q, 128, 512]. splits > 1 splits every query's keys
-    over that many CTAs (short query batches) and merges their partials from `ws`."""
+    int32 cache slots (-1: none; nsel % 64 == 0) -> latent output [Q, 128, 512]. With q_rope, q is the latent part
+    [Q, 128, 512] and q_rope the rotary part [Q, 128, 64]; q, q_rope and out may be strided views with unit stride
+    along the last dim (e.g. head-major buffers seen through transpose(0, 1)). splits > 1 splits every query's keys
+    over that many CTAs (short query batches) and merges their partials from `ws` (out contiguous then)."""
     Q = q.shape[0]
     out = torch.empty(Q, 128, LATENT, dtype=torch.bfloat16, device=q.device) if out is None else out
     if ws is None:
         ws = FlashWorkspace(Q, splits, q.device)
     ops.load()
-    torch.ops.xtier.mla_flash(q.contiguous(), idx.to(torch.int32).contiguous(), cache.codes, cache.scales,
-                              cache.rope, ws.part_o, ws.part_ml, out, float(scale), int(splits), ws.err)
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    torch.ops.xtier.mla_flash(q, idx.to(torch.int32).contiguous(), cache.codes, cache.scales,
+                              cache.rope, ws.part_o, ws.part_ml, out, float(scale), int(splits), ws.err, q_rope)
     return out
 
 

@@ -164,27 +164,29 @@ class SparsePrefill:
             C = c1 - c0
             qc = q[c0:c1]
             pc = pos[c0:c1]
-            q_pe = _rope(qc[..., cfg.qk_nope:].transpose(0, 1), pc, cfg.rope_theta).transpose(0, 1)
             if self.dense:
+                q_pe = _rope(qc[..., cfg.qk_nope:].transpose(0, 1), pc, cfg.rope_theta).transpose(0, 1)
                 qq = torch.cat([qc[..., :cfg.qk_nope], q_pe], -1)
                 for i in range(C):   # causal, one query at a time (test sizes)
                     p = int(pc[i])
                     out[c0 + i] = self.model._mla_prefill(L, qq[i:i + 1], lat[:p + 1], p)[0]
                 continue
-            # absorbed queries [C, heads, kv_lora + rope]
-            qf = torch.empty(C, cfg.heads, cfg.kv_lora + cfg.qk_rope, dtype=torch.bfloat16, device=q.device)
-            qf[..., :cfg.kv_lora] = torch.matmul(qc[..., :cfg.qk_nope].transpose(0, 1), L['w_uk']).transpose(0, 1)
-            qf[..., cfg.kv_lora:] = q_pe
+            # absorbed queries, head-major: latent part [heads, C, kv_lora] by one batched GEMM, rotary part
+            # [heads, C, rope] by the RoPE kernel; flash MLA reads both through strided views, no [C, heads, 576] copy
+            q_lat = torch.bmm(qc[..., :cfg.qk_nope].transpose(0, 1), L['w_uk'])
+            q_pe = torch.empty(cfg.heads, C, cfg.qk_rope, dtype=torch.bfloat16, device=q.device)
+            ops.rope_heads(qc[..., cfg.qk_nope:], pc, cfg.rope_theta, q_pe.transpose(0, 1))
             # indexer: top-k earlier positions of every query (slot = position: one sequence)
             qi = ops.linear(q_a[c0:c1], L['idx_q']).view(C, cfg.index_heads, cfg.index_dim)
-            wi = ops.linear(h[c0:c1], L['idx_w']).float() * cfg.index_heads ** -0.5
+            wi = ops.linear(h[c0:c1], L['idx_w'])
             lens = pc + 1
-            sc = dsa.index_scores_prefill(qi, wi, self.index[li], 0, lens, out=self.scores[:C], err=self.idx_err)
+            sc = dsa.index_scores_prefill(qi, wi, self.index[li], 0, lens, out=self.scores[:C], err=self.idx_err,
+                                          w_scale=cfg.index_heads ** -0.5)
             idx = dsa.topk(sc, self.topk, lengths=lens)
-            o_lat = torch.empty(C, cfg.heads, cfg.kv_lora, dtype=torch.bfloat16, device=q.device)
-            torch.ops.xtier.mla_flash(qf, idx, lc.codes, lc.scales, lc.rope, None, None, o_lat, float(scale), 1,
-                                      self.ws.err)
-            out[c0:c1] = torch.matmul(o_lat.transpose(0, 1), L['w_uvT']).transpose(0, 1).reshape(C, -1)
+            o_lat = torch.empty(cfg.heads, C, cfg.kv_lora, dtype=torch.bfloat16, device=q.device)
+            torch.ops.xtier.mla_flash(q_lat.transpose(0, 1), idx, lc.codes, lc.scales, lc.rope, None, None,
+                                      o_lat.transpose(0, 1), float(scale), 1, self.ws.err, q_pe.transpose(0, 1))
+            out[c0:c1] = torch.bmm(o_lat, L['w_uvT']).transpose(0, 1).reshape(C, -1)
         return out
 
     @torch.no_grad()

@@ -192,6 +192,13 @@ def head_gemm(x, w, y, pos=None, rope_x: int = 0, rope_y: int = 0, rope_dims: in
     return y
 
 
+def rope_heads(x, pos, theta: float, out):
+    """out[t, h, :] = NeoX RoPE of x[t, h, :] at pos[t] (int32): x and out [T, H, d] BF16 views with unit stride along
+    d (any token and head strides)."""
+    _ops().rope_heads(x, pos, float(theta), out)
+    return out
+
+
 def silu_mul(inp, out):
     """inp [T, 2I] (gate then up) -> out [T, I] = SiLU(gate) * up."""
     _ops().silu_mul(inp, out)
