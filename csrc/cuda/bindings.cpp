@@ -697,6 +697,25 @@ void head_gemm(const Tensor &x, const Tensor &w, const Tensor &y, const std::opt
     check_rc(xt_head_gemm(&p, int(w.size(0)), stream()), "head_gemm");
 }
 
+void skinny_gemm(const Tensor &x, const Tensor &w, const std::optional<Tensor> &add, const Tensor &y,
+                 const std::optional<Tensor> &part, int64_t splits, const Tensor &err) {
+    cuda_contig(x, "x");
+    cuda_contig(w, "w");
+    cuda_contig(y, "y");
+    const int64_t K = x.size(-1), M = x.numel() / K, N = w.size(0);
+    check(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 &&
+              w.size(1) == K && y.numel() == M * N && M >= 1 && M <= 32 && K % 64 == 0,
+          "skinny_gemm: bf16 x [M <= 32, K % 64 == 0], w [N, K], y [M, N]");
+    if (add) check(add->is_contiguous() && add->scalar_type() == at::kBFloat16 && add->numel() == M * N, "skinny add");
+    if (splits > 1)
+        check(part && part->is_contiguous() && part->scalar_type() == at::kFloat && part->numel() >= splits * M * N,
+              "skinny_gemm: part [splits, M, N] f32");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_skinny_gemm(x.data_ptr(), w.data_ptr(), add ? add->data_ptr() : nullptr, y.data_ptr(),
+                            optr<float>(part), int(M), int(N), int(K), int(splits), ptr<int>(err), stream()),
+             "skinny_gemm");
+}
+
 void rope_heads(const Tensor &x, const Tensor &pos, double theta, const Tensor &out) {
     // x [T, H, d] and out [T, H, d] bf16 views with unit stride along d; pos int32 [T]
     check(x.is_cuda() && x.dim() == 3 && x.stride(2) == 1 && out.dim() == 3 && out.stride(2) == 1 &&
@@ -743,6 +762,8 @@ TORCH_LIBRARY(xtier, m) {
           "float theta, Tensor(a!) q_out, Tensor(b!) codes, Tensor(c!) scales, Tensor(d!) rope, Tensor(e!)? lat_out) "
           "-> ()");
     m.def("rope_heads(Tensor x, Tensor pos, float theta, Tensor(a!) out) -> ()");
+    m.def("skinny_gemm(Tensor x, Tensor w, Tensor? add, Tensor(a!) y, Tensor(b!)? part, int splits, Tensor(c!) err) "
+          "-> ()");
     m.def("dsa_quant_q(Tensor q, Tensor w, float w_scale, Tensor(a!) q8, Tensor(b!) w8) -> ()");
     m.def("head_gemm(Tensor x, Tensor w, Tensor(a!) y, Tensor? pos, int rope_x, int rope_y, int rope_dims, "
           "float theta) -> ()");
@@ -801,6 +822,7 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("mla_prep", &mla_prep);
     m.impl("head_gemm", &head_gemm);
     m.impl("rope_heads", &rope_heads);
+    m.impl("skinny_gemm", &skinny_gemm);
     m.impl("dsa_quant_q", &dsa_quant_q);
     m.impl("silu_mul", &silu_mul);
     m.impl("qk_norm_rope_kv", &qk_norm_rope_kv);

@@ -374,9 +374,9 @@ __global__ void __launch_bounds__(MLA_THREADS, 1)
 //               epilogue (O / l, or the unnormalized split partial with m and l for mla_merge)
 // The query is converted once, in place: each head row BF16 -> f16 scaled by the power of two 2^e that puts the row's
 // largest magnitude in [2^14, 2^15) (exact down to 2^-28 of that magnitude); 2^-e is folded into the row's softmax
-// scale. V is double-buffered, so S of block b does not wait for P.V of block b - 1: the tensor core computes S of b while
-// the softmax warps work on b - 1. Every wait is bounded; a wait that runs out sets the error word, raises the CTA's
-// abort flag and every role winds down (the output of that query is then meaningless and the caller raises).
+// scale. V is double-buffered, so S of block b does not wait for P.V of block b - 1: the tensor core computes S of b
+// while the softmax warps work on b - 1. Every wait is bounded; a wait that runs out sets the error word, raises the
+// CTA's abort flag and every role winds down (the output of that query is then meaningless and the caller raises).
 constexpr int MF_NB = 64;
 constexpr int MF_STAGES = 2;
 constexpr int MF_THREADS = 320;
@@ -537,8 +537,9 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                 const uint32_t vb = va + uint32_t((b & 1) * MfSmem::VBUF);
 #pragma unroll
                 for (int k = 0; k < MF_NB / 16; ++k)
-                    tc::mma_f16_ts(tmem, pa + uint32_t(8 * k), tc::sw128_mnmajor_desc(vb + uint32_t(k * 2048), MfSmem::KKB, 1024),
-                                   idesc_o, (b > 0 || k > 0) ? 1u : 0u);
+                    tc::mma_f16_ts(tmem, pa + uint32_t(8 * k),
+                                   tc::sw128_mnmajor_desc(vb + uint32_t(k * 2048), MfSmem::KKB, 1024), idesc_o,
+                                   (b > 0 || k > 0) ? 1u : 0u);
                 tc::mma_commit(&vfree[b & 1]);
             };
             auto s_kb = [&](uint32_t sb, int kb, uint32_t baddr, bool first) {

@@ -108,6 +108,9 @@ int xt_gemm_tc(const void *A, const void *B, void *D, const void *R, int M, int 
                cudaStream_t stream);
 int xt_gemm_tc_f32(const void *A, const void *B, float *D, int M, int N, int K, int *error, cudaStream_t stream);
 int xt_gemv_bf16(const void *x, const void *W, const void *add, void *y, int m, int N, int K, cudaStream_t stream);
+int xt_skinny_splits(int N, int K, int sms);
+int xt_skinny_gemm(const void *x, const void *W, const void *add, void *y, float *part, int M, int N, int K,
+                   int splits, int *error, cudaStream_t stream);
 int xt_fp8_rows(const void *tab, const void *sc, const int64_t *ids, long long lo, long long hi, int n, int dim,
                 int blk, void *out, cudaStream_t stream);
 int xt_gemv_fp8(const void *x, const void *W, const float *S, const void *add, void *y, int m, int N, int K,

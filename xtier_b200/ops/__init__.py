@@ -154,12 +154,47 @@ def gemm(a, b, out=None, residual=None):
     return out
 
 
+_SMS: dict = {}
+
+
+def _sms(device) -> int:
+    key = torch.device(device)
+    if key not in _SMS:
+        _SMS[key] = torch.cuda.get_device_properties(key).multi_processor_count
+    return _SMS[key]
+
+
+def skinny_splits(N: int, K: int, sms: int) -> int:
+    """K splits of skinny_gemm for (N, K): about two CTAs per SM, at least 4 k-blocks of 64 per CTA."""
+    nblk = -(-N // 128)
+    return max(1, min(-(-2 * sms // nblk), (K // 64) // 4))
+
+
+def skinny_gemm(x, w, out=None, add=None):
+    """out[M, N] = x[M, K] . w[N, K]^T (+ add) for M <= 32, K % 64 == 0, on the tcgen05 tensor cores with the weights
+    as the MMA's 128-row operand (csrc/cuda/gemm_skinny.cu); K split over CTAs with FP32 partials reduced in order."""
+    K = x.shape[-1]
+    M, N = x.numel() // K, w.shape[0]
+    out = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device) if out is None else out
+    splits = skinny_splits(N, K, _sms(x.device))
+    part = torch.empty(splits, M, N, dtype=torch.float32, device=x.device) if splits > 1 else None
+    _ops().skinny_gemm(x, w, add, out, part, splits, gemm_error_word(x.device))
+    return out
+
+
 def linear(x, w, out=None):
-    """x @ w^T in BF16: the weight-streaming GEMV for decode-sized inputs (at most two passes over the weights, each
-    of <= 16 rows whose activations fit the kernel's shared memory), the tcgen05 GEMM for larger ones (cuBLAS only for
-    shapes TMA cannot describe: K not a multiple of 8 or unaligned rows)."""
+    """x @ w^T in BF16. Decode-sized inputs (<= 32 rows): the tcgen05 skinny GEMM when K % 64 == 0 and there are three
+    rows or more, else the weight-streaming GEMV (at most two passes over the weights, each of <= 16 rows whose
+    activations fit the kernel's shared memory). Larger inputs: the tcgen05 GEMM (cuBLAS only for shapes TMA cannot
+    describe: K not a multiple of 8 or unaligned rows)."""
     m = x.numel() // x.shape[-1]
     K = x.shape[-1]
+    # the skinny GEMM from 3 rows on (measured faster than the GEMV on every decode projection from 4 rows: the
+    # GEMV's FP32 FMA issue grows with the rows), the GEMV for one or two rows
+    if (3 <= m <= 32 and K % 64 == 0 and x.is_cuda and x.is_contiguous() and w.is_contiguous()
+            and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.data_ptr() % 16 == 0
+            and w.data_ptr() % 16 == 0 and (out is None or out.is_contiguous())):
+        return skinny_gemm(x, w, out)
     per = min(16, (200 * 1024) // (K * 2))
     if per >= 1 and m <= 2 * per and x.is_contiguous() and x.dtype == torch.bfloat16:
         out = torch.empty(*x.shape[:-1], w.shape[0], dtype=x.dtype, device=x.device) if out is None else out
