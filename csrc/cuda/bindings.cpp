@@ -697,6 +697,54 @@ void head_gemm(const Tensor &x, const Tensor &w, const Tensor &y, const std::opt
     check_rc(xt_head_gemm(&p, int(w.size(0)), stream()), "head_gemm");
 }
 
+void mx_quant_rows(const Tensor &x, const std::optional<Tensor> &src, const Tensor &x8, const Tensor &sfx) {
+    cuda_contig(x, "x");
+    cuda_contig(x8, "x8");
+    cuda_contig(sfx, "sfx");
+    const int64_t K = x8.size(-1), R = x8.numel() / K;
+    check(x.scalar_type() == at::kBFloat16 && x.size(-1) == K && x8.scalar_type() == at::kByte &&
+              sfx.scalar_type() == at::kByte && K % 128 == 0 && R % 128 == 0 && sfx.numel() >= R * (K / 32),
+          "mx_quant_rows: x [*, K] bf16, x8 [R, K] u8 (R, K multiples of 128), sfx >= R * K / 32 bytes");
+    if (src) check(src->is_contiguous() && src->scalar_type() == at::kInt && src->numel() == R, "mx_quant_rows src");
+    else check(x.numel() == R * K, "mx_quant_rows: x [R, K] without src");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_mx_quant_rows(x.data_ptr(), optr<const int32_t>(src), int(R), int(K), x8.data_ptr(), sfx.data_ptr(),
+                              stream()),
+             "mx_quant_rows");
+}
+
+void moe_grouped_mx(const Tensor &x8, const Tensor &sfx, const Tensor &codes, const Tensor &scales,
+                    const Tensor &gscale, const Tensor &tiles, bool gate_up, int64_t I,
+                    const std::optional<Tensor> &route_w, const Tensor &out, const Tensor &err,
+                    const std::optional<Tensor> &dst_rows) {
+    cuda_contig(x8, "x8");
+    cuda_contig(sfx, "sfx");
+    cuda_contig(codes, "codes");
+    cuda_contig(scales, "scales");
+    cuda_contig(tiles, "tiles");
+    check(x8.scalar_type() == at::kByte && tiles.scalar_type() == at::kInt && tiles.size(1) == 4,
+          "moe_grouped_mx: u8 x8, int32 tiles [T, 4]");
+    const int64_t R = x8.size(0), K = x8.size(1), slots = codes.size(0), N_rows = codes.size(1);
+    check(codes.size(2) * 2 == K && scales.size(0) == slots && scales.size(1) == N_rows && scales.size(2) * 32 == K,
+          "moe_grouped_mx: MXFP4 codes [slots, N_rows, K/2] and UE8M0 scales [slots, N_rows, K/32]");
+    if (gate_up)
+        check(out.scalar_type() == at::kBFloat16 && out.size(0) == R && out.size(1) == I && N_rows == 2 * I,
+              "moe_grouped_mx gate_up: mid [R, I] bf16");
+    else
+        check(out.scalar_type() == at::kFloat && (dst_rows.has_value() || out.size(0) == R) &&
+                  out.size(1) == N_rows && route_w.has_value(),
+              "moe_grouped_mx down: y f32 and route weights");
+    if (dst_rows.has_value())
+        check(!gate_up && dst_rows->scalar_type() == at::kInt && dst_rows->numel() == R, "moe_grouped_mx dst_rows");
+    c10::cuda::CUDAGuard g(x8.device());
+    check_rc(xt_moe_grouped_mx(x8.data_ptr(), sfx.data_ptr(), int(R), codes.data_ptr(), scales.data_ptr(), int(slots),
+                               ptr<const int32_t>(tiles), int(tiles.size(0)), gate_up ? 1 : 0, int(K), int(N_rows),
+                               int(I), ptr<const float>(gscale), optr<const float>(route_w),
+                               optr<const int32_t>(dst_rows), gate_up ? out.data_ptr() : nullptr,
+                               gate_up ? nullptr : ptr<float>(out), int(out.size(1)), ptr<int>(err), stream()),
+             "moe_grouped_mx");
+}
+
 void skinny_gemm(const Tensor &x, const Tensor &w, const std::optional<Tensor> &add, const Tensor &y,
                  const std::optional<Tensor> &part, int64_t splits, const Tensor &err) {
     cuda_contig(x, "x");
@@ -764,6 +812,9 @@ TORCH_LIBRARY(xtier, m) {
     m.def("rope_heads(Tensor x, Tensor pos, float theta, Tensor(a!) out) -> ()");
     m.def("skinny_gemm(Tensor x, Tensor w, Tensor? add, Tensor(a!) y, Tensor(b!)? part, int splits, Tensor(c!) err) "
           "-> ()");
+    m.def("mx_quant_rows(Tensor x, Tensor? src, Tensor(a!) x8, Tensor(b!) sfx) -> ()");
+    m.def("moe_grouped_mx(Tensor x8, Tensor sfx, Tensor codes, Tensor scales, Tensor gscale, Tensor tiles, "
+          "bool gate_up, int I, Tensor? route_w, Tensor(a!) out, Tensor(b!) err, Tensor? dst_rows=None) -> ()");
     m.def("dsa_quant_q(Tensor q, Tensor w, float w_scale, Tensor(a!) q8, Tensor(b!) w8) -> ()");
     m.def("head_gemm(Tensor x, Tensor w, Tensor(a!) y, Tensor? pos, int rope_x, int rope_y, int rope_dims, "
           "float theta) -> ()");
@@ -823,6 +874,8 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("head_gemm", &head_gemm);
     m.impl("rope_heads", &rope_heads);
     m.impl("skinny_gemm", &skinny_gemm);
+    m.impl("mx_quant_rows", &mx_quant_rows);
+    m.impl("moe_grouped_mx", &moe_grouped_mx);
     m.impl("dsa_quant_q", &dsa_quant_q);
     m.impl("silu_mul", &silu_mul);
     m.impl("qk_norm_rope_kv", &qk_norm_rope_kv);

@@ -108,6 +108,11 @@ int xt_gemm_tc(const void *A, const void *B, void *D, const void *R, int M, int 
                cudaStream_t stream);
 int xt_gemm_tc_f32(const void *A, const void *B, float *D, int M, int N, int K, int *error, cudaStream_t stream);
 int xt_gemv_bf16(const void *x, const void *W, const void *add, void *y, int m, int N, int K, cudaStream_t stream);
+int xt_mx_quant_rows(const void *x, const int32_t *src, int R, int K, void *x8, void *sfx, cudaStream_t stream);
+int xt_moe_grouped_mx(const void *x8, const void *sfx, int R, const void *codes, const void *scales, int slots,
+                      const int32_t *tiles, int T, int gate_up, int K, int N_rows, int I, const float *gscale,
+                      const float *route_w, const int32_t *dst_row, void *mid, float *y, int out_cols, int *error,
+                      cudaStream_t stream);
 int xt_skinny_splits(int N, int K, int sms);
 int xt_skinny_gemm(const void *x, const void *W, const void *add, void *y, float *part, int M, int N, int K,
                    int splits, int *error, cudaStream_t stream);

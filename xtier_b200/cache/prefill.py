@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import torch
 
-from .. import ops
+from .. import config, ops
 from ..formats import NVFP4, ExpertWeights
 
 TILE = 128
@@ -44,9 +44,10 @@ def plan(slots: torch.Tensor):
 WORK_ROWS = 2 * TILE   # rows of one work item of the kernel: two 128-row m-tiles share each dequantized weight tile
 
 
-def _tiles(runs: torch.Tensor, n_tiles: int, device) -> torch.Tensor:
-    """[T, 4] int32 (slot, first row, n-tile, valid rows <= 256) for every 256-row block of every run x every n-tile
-    (rows past a run's end in its last block are computed and dropped by the kernel's epilogue)."""
+def _tiles(runs: torch.Tensor, n_tiles: int, device, work_rows: int = WORK_ROWS) -> torch.Tensor:
+    """[T, 4] int32 (slot, first row, n-tile, valid rows <= work_rows) for every work_rows-row block of every run x
+    every n-tile (rows past a run's end in its last block are computed and dropped by the kernel's epilogue)."""
+    WORK_ROWS = work_rows
     mt = (runs[:, 2] + WORK_ROWS - 1) // WORK_ROWS
     run = torch.repeat_interleave(torch.arange(runs.shape[0]), mt)
     first_block = torch.cumsum(mt, 0) - mt
@@ -60,13 +61,50 @@ def _tiles(runs: torch.Tensor, n_tiles: int, device) -> torch.Tensor:
     return t.to(torch.int32).to(device, non_blocking=True)
 
 
+def _grouped_routes_mx(x, src, w, pool, order, rows, R, runs, m, k, err, route_rows, out):
+    """grouped_routes with MXFP8 activations and the block-scaled MXFP4 kernel (csrc/cuda/moe_prefill_mx.cu): the
+    gathered token rows and the SwiGLU output are quantized to E4M3 with UE8M0 scales per 32 values."""
+    H, I = pool.hidden, pool.inter
+    dev = x.device
+    X8 = torch.empty(R, H, dtype=torch.uint8, device=dev)
+    SFX = torch.empty(R * H // 32, dtype=torch.uint8, device=dev)
+    torch.ops.xtier.mx_quant_rows(x.contiguous(), src, X8, SFX)
+    rw = torch.zeros(R, dtype=torch.float32, device=dev)
+    rw[rows] = w.flatten().float()[order]
+    err = torch.zeros(1, dtype=torch.int32, device=dev) if err is None else err
+    mid = torch.empty(R, I, dtype=torch.bfloat16, device=dev)
+    torch.ops.xtier.moe_grouped_mx(X8, SFX, pool.w13, pool.s13, pool.g13.float().contiguous(),
+                                   _tiles(runs, I // 64, dev, TILE), True, I, None, mid, err)
+    del X8, SFX
+    M8 = torch.empty(R, I, dtype=torch.uint8, device=dev)
+    SFM = torch.empty(R * I // 32, dtype=torch.uint8, device=dev)
+    torch.ops.xtier.mx_quant_rows(mid, None, M8, SFM)
+    del mid
+    dest = torch.full((m * k,), -1, dtype=torch.int32, device=dev)
+    if route_rows:
+        Y = torch.empty(m * k, H, dtype=torch.float32, device=dev) if out is None else out
+        dst = torch.full((R,), -1, dtype=torch.int32, device=dev)
+        dst[rows] = order.int()
+        dest[order] = order.int()
+    else:
+        Y = torch.empty(R, H, dtype=torch.float32, device=dev)
+        dst = None
+        dest[order] = rows.int()
+    torch.ops.xtier.moe_grouped_mx(M8, SFM, pool.w2, pool.s2, pool.g2.float().contiguous(),
+                                   _tiles(runs, H // 128, dev, TILE), False, I, rw, Y, err, dst)
+    return Y, dest
+
+
 def grouped_routes(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: ExpertWeights,
-                   err: torch.Tensor | None = None, route_rows: bool = False, out: torch.Tensor | None = None):
+                   err: torch.Tensor | None = None, route_rows: bool = False, out: torch.Tensor | None = None,
+                   mx: bool | None = None):
     """x [m, H] BF16, slots [m, k] GPU slot per route (-1 skips), w [m, k] route weights -> (Y [R, H] FP32: every
     computed route's w * MoE_expert(x) row, dest [m * k] int32: the Y row of each route or -1); (None, None) when no
     route has a slot. Token rows are gathered into the padded per-expert runs by a kernel (csrc/cuda/moe_prefill.cu
     gather_rows); the down GEMM's epilogue applies the route weight. route_rows=True: Y [m * k, H] indexed by route
-    (t * k + j), written there directly by the down GEMM's epilogue (into `out` when given)."""
+    (t * k + j), written there directly by the down GEMM's epilogue (into `out` when given). mx (default
+    XTIER_PREFILL_MX): MXFP4 pools run with MXFP8 activations on the block-scaled kernel (the reference's prefill
+    numerics) instead of the exact W4A16 one."""
     m, k = slots.shape
     H, I = pool.hidden, pool.inter
     dev = x.device
@@ -78,6 +116,10 @@ def grouped_routes(x: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, pool: 
     ops.load()
     src = torch.full((R,), -1, dtype=torch.int32, device=dev)
     src[rows] = (order // k).int()
+    if mx is None:
+        mx = bool(config.get('XTIER_PREFILL_MX'))
+    if mx and pool.fmt != NVFP4 and H % 128 == 0 and I % 128 == 0:
+        return _grouped_routes_mx(x, src, w, pool, order, rows, R, runs, m, k, err, route_rows, out)
     X = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
     torch.ops.xtier.gather_rows(x.contiguous(), src, X)
     rw = torch.zeros(R, dtype=torch.float32, device=dev)

@@ -67,6 +67,7 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_GPU2_SLOTS', 'str', '', 'auto / on: the hot slots of all GPUs of the process group form one pool, '
        'read over NVLink'),
     _S('XTIER_EP', 'int', 0, 'expert-parallel ranks of the hot-slot pool (0: the world size)'),
+    _S('XTIER_EP_ORDER', 'int', 1, 'EP expert streams take the routes grouped by expert slot (0: arrival order)'),
     _S('XTIER_COLD', 'flag', False, 'cold experts in NVMe relayout files, read on demand with O_DIRECT'),
     _S('XTIER_COLD_DIR', 'str', '', 'directories (one per drive, comma separated) of the cold-expert store'),
     _S('XTIER_COLD_FRACTION', 'float', 0.0, 'share of each layer\'s experts kept cold (not in RAM)'),
@@ -89,6 +90,7 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_ROUTE_TRACE', 'str', '', 'binary route trace of the CPU decode calls (planner input)'),
     _S('XTIER_TIMING', 'flag', False, 'log synchronized MoE time per forward'),
     _S('XTIER_PREFILL_PROFILE', 'flag', False, 'CUDA events per prefill phase'),
+    _S('XTIER_PREFILL_MX', 'flag', False, 'grouped prefill of MXFP4 experts with MXFP8 activations (kind::mxf8f6f4)'),
     _S('XTIER_DEBUG_BOUNDS', 'flag', False, 'bounds-checked kernels: a bad index sets the device error word'),
     _S('XTIER_DEBUG_STALL_US', 'int', 0, 'test only: the mailbox dispatcher stalls this long per request'),
     _S('XTIER_DEBUG_SEQ_START', 'int', 0, 'test only: first sequence number of the swap ring (wrap tests)'),
