@@ -50,8 +50,9 @@ class EPPrefillMoE:
     """Prefill-sized calls of an EPMoE layer (every expert in some rank's HBM): route, all-to-all to the owners,
     grouped GEMMs on the owner's pool, all-to-all back, route-ordered combine."""
 
-    def __init__(self, chunk: int = 16384):
+    def __init__(self, chunk: int = 16384, mx: bool = True):
         self.chunk = chunk
+        self.mx = mx   # MXFP8 activations on the block-scaled FP4 kernel (the reference's prefill numerics)
         self.err = None
         self.count = None
 
@@ -80,7 +81,7 @@ class EPPrefillMoE:
                 raise RuntimeError('EP prefill: a route has no GPU slot (the CPU tier is a decode path)')
             add_c = None if add is None else add[s:e].contiguous()
             if W == 1:   # every route is local: grouped GEMMs straight from the chunk, rows written in route order
-                Y, dest = grouped_routes(xc, slots, wt, moe.local, self.err, route_rows=True)
+                Y, dest = grouped_routes(xc, slots, wt, moe.local, self.err, route_rows=True, mx=self.mx)
                 torch.ops.xtier.route_combine(Y, dest, None, None, add_c, out[s:e])
                 self.last = (ids, wt)
                 continue
@@ -102,7 +103,8 @@ class EPPrefillMoE:
             y = torch.empty(nr, H, dtype=torch.float32, device=dev)
             if nr:   # the received routes' rows, written in received order by the down GEMM
                 r_w = r_meta[:, 1:].contiguous().view(torch.float32)
-                grouped_routes(r_rows, r_meta[:, :1].contiguous(), r_w, moe.local, self.err, route_rows=True, out=y)
+                grouped_routes(r_rows, r_meta[:, :1].contiguous(), r_w, moe.local, self.err, route_rows=True, out=y,
+                               mx=self.mx)
             del r_rows
             back = torch.empty(n, H, dtype=torch.float32, device=dev)
             _a2a(back, y, sc, rc)
@@ -119,10 +121,11 @@ class SparsePrefill:
 
     `model` is a DeepSeekV3Model built with ep=True (world = the group) and `indexer=True`, every expert in HBM.
     dense=True replaces the indexer + sparse attention by causal attention over every earlier key (the expanded form
-    of `DeepSeekV3Model._mla_prefill`), the oracle of the tests."""
+    of `DeepSeekV3Model._mla_prefill`), the oracle of the tests. mx=False runs the experts on the exact W4A16 kernel
+    instead of the block-scaled MXFP4 x MXFP8 one."""
 
     def __init__(self, model: DeepSeekV3Model, total: int, q_chunk: int = 1024, moe_chunk: int = 16384,
-                 dense: bool = False):
+                 dense: bool = False, mx: bool = True):
         cfg = model.cfg
         env = xdist.get()
         self.model, self.cfg = model, cfg
@@ -137,7 +140,7 @@ class SparsePrefill:
         self.latent = [LatentCache(1, total, dev) for _ in model.layers]
         self.index = [dsa.IndexCache(1, total, dev) for _ in model.layers]
         self.ws = FlashWorkspace(q_chunk, 1, dev)
-        self.moe = EPPrefillMoE(moe_chunk)
+        self.moe = EPPrefillMoE(moe_chunk, mx)
         self.scores = torch.empty(q_chunk, total, dtype=torch.float32, device=dev)
         self.idx_err = torch.zeros(1, dtype=torch.int32, device=dev)
 
