@@ -534,11 +534,15 @@ void mla_flash(const Tensor &q, const Tensor &idx, const Tensor &codes, const Te
     const auto *qp = static_cast<const __nv_bfloat16 *>(q.data_ptr());
     const void *qr = q_rope ? q_rope->data_ptr() : static_cast<const void *>(qp + 512);
     const int64_t qr_ts = q_rope ? q_rope->stride(0) : q.stride(0), qr_hs = q_rope ? q_rope->stride(1) : q.stride(1);
+    static const bool bounds = [] {   // XTIER_DEBUG_BOUNDS: selected slots checked against the cache size
+        const char *v = getenv("XTIER_DEBUG_BOUNDS");
+        return v && *v && *v != '0';
+    }();
     c10::cuda::CUDAGuard g(q.device());
     check_rc(xt_mla_flash(qp, q.stride(0), q.stride(1), qr, qr_ts, qr_hs, ptr<const int32_t>(idx), int(Q), int(nsel),
                           codes.data_ptr(), scales.data_ptr(), rope.data_ptr(), optr<float>(part_o),
                           optr<float>(part_ml), out.data_ptr(), out.stride(0), out.stride(1), float(scale),
-                          int(splits), ptr<int>(err), stream()),
+                          int(splits), bounds ? int(codes.size(0)) : 0, ptr<int>(err), stream()),
              "mla_flash");
 }
 

@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
                      const int32_t *__restrict__ idx, int nsel, int bps, int nblk, const uint8_t *__restrict__ codes,
                      const uint8_t *__restrict__ scales, const __nv_bfloat16 *__restrict__ rope, float scale_log2,
                      __nv_bfloat16 *__restrict__ out, int64_t out_ts, int64_t out_hs, float *__restrict__ part_o,
-                     float *__restrict__ part_ml, int *error) {
+                     float *__restrict__ part_ml, int nslots, int *error) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *qs = smem;                                   // [9][128 x 64]
@@ -591,7 +591,11 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
         int pslot = nb > 0 ? qidx[size_t(b0) * MF_NB + kk] : -1;
         auto load_block = [&](int b) {   // this key's codes and scales of its half of every latent k-block (other
                                          // value half first), and its half of the rotary part
-            const int slot = pslot;
+            int slot = pslot;
+            if (nslots && slot >= nslots) {   // bounds-checked mode: skip the key, error word 2
+                atomicCAS(error, 0, 2);
+                slot = -1;
+            }
             if (b + 1 < nb) pslot = qidx[size_t(b0 + b + 1) * MF_NB + kk];
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
@@ -712,8 +716,9 @@ __global__ void __launch_bounds__(MF_THREADS, 1)
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&sfree[b & 1]);
-            const unsigned vlo = __ballot_sync(0xffffffffu, ilo >= 0);
-            const unsigned vhi = __ballot_sync(0xffffffffu, ihi >= 0);
+            // keys with a slot, and in bounds-checked mode only slots inside the cache (the producers skip the rest)
+            const unsigned vlo = __ballot_sync(0xffffffffu, ilo >= 0 && (!nslots || ilo < nslots));
+            const unsigned vhi = __ballot_sync(0xffffffffu, ihi >= 0 && (!nslots || ihi < nslots));
             if (b + 1 < nb) {   // the next block's slots, in flight while this block is processed
                 ilo = qidx[size_t(b0 + b + 1) * MF_NB + lane];
                 ihi = qidx[size_t(b0 + b + 1) * MF_NB + 32 + lane];
@@ -940,12 +945,13 @@ int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void
 // unit stride along d and element strides (token, head): the latent part q_lat (d = 512) and the rotary part q_rope
 // (d = 64); out [Q, 128, 512] BF16 likewise (token and head strides out_ts, out_hs). part_o [Q, splits, 128, 512] f32
 // and part_ml [Q, splits, 128, 2] are used only when splits > 1 (the splits' partials, merged by mla_merge, which
-// writes a contiguous out). nsel % 64 == 0.
+// writes a contiguous out). nsel % 64 == 0. nslots > 0 checks every selected slot against the cache size (a slot at or
+// past it is skipped and sets the error word to 2); 0 skips the check.
 int xt_mla_flash(const void *q_lat, int64_t ql_ts, int64_t ql_hs, const void *q_rope, int64_t qr_ts, int64_t qr_hs,
                  const int32_t *idx, int Q, int nsel, const void *codes, const void *scales, const void *rope,
                  float *part_o, float *part_ml, void *out, int64_t out_ts, int64_t out_hs, float scale, int splits,
-                 int *error, cudaStream_t stream) {
-    if (Q <= 0 || Q > 65535 || nsel <= 0 || nsel % MF_NB || splits < 1) return -2;
+                 int nslots, int *error, cudaStream_t stream) {
+    if (Q <= 0 || Q > 65535 || nsel <= 0 || nsel % MF_NB || splits < 1 || nslots < 0) return -2;
     const int nblk = nsel / MF_NB;
     const int bps = (nblk + splits - 1) / splits;
     splits = (nblk + bps - 1) / bps;
@@ -958,7 +964,7 @@ int xt_mla_flash(const void *q_lat, int64_t ql_ts, int64_t ql_hs, const void *q_
     mla_flash_kernel<<<dim3(2, splits, Q), MF_THREADS, MfSmem::BYTES, stream>>>(
         ml, mr, idx, nsel, bps, nblk, static_cast<const uint8_t *>(codes), static_cast<const uint8_t *>(scales),
         static_cast<const __nv_bfloat16 *>(rope), scale * 1.4426950408889634f, static_cast<__nv_bfloat16 *>(out),
-        out_ts, out_hs, part_o, part_ml, error);
+        out_ts, out_hs, part_o, part_ml, nslots, error);
     if (cudaGetLastError() != cudaSuccess) return -1;
     if (splits > 1) {
         mla_merge_kernel<<<dim3(MLA_H, Q), 128, 0, stream>>>(part_o, part_ml, splits,

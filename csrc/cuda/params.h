@@ -224,7 +224,7 @@ int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream);
 int xt_mla_flash(const void *q_lat, int64_t ql_ts, int64_t ql_hs, const void *q_rope, int64_t qr_ts, int64_t qr_hs,
                  const int32_t *idx, int Q, int nsel, const void *codes, const void *scales, const void *rope,
                  float *part_o, float *part_ml, void *out, int64_t out_ts, int64_t out_hs, float scale, int splits,
-                 int *error, cudaStream_t stream);
+                 int nslots, int *error, cudaStream_t stream);
 int xt_mla_decode(const void *q, const int32_t *idx, int Q, int nsel, const void *codes, const void *scales,
                   const void *rope, void *Kg, void *Vt, float *part_o, float *part_ml, void *out, float scale,
                   int *error, cudaStream_t stream);

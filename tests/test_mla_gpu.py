@@ -143,3 +143,40 @@ def test_rope_heads_and_fp8_query_quantization(cuda_ops):
     a = q8.view(torch.float8_e4m3fn).float()
     b = q8_ref.view(torch.float8_e4m3fn).float()
     assert bool(((a - b).abs() <= b.abs() * 0.125 + 2 ** -9).all())
+
+
+def test_mla_flash_bounds_check_flags_bad_slot():
+    """XTIER_DEBUG_BOUNDS: a selected slot past the cache is skipped and reported (error word 2), the rest of the
+    query's keys still count. Runs in a child process: the switch is read once per process."""
+    import os
+    import subprocess
+    import sys
+    code = r"""
+import copy
+import torch
+from xtier_b200 import ops
+from xtier_b200.attention.mla import FlashWorkspace, LatentCache, default_scale, mla_flash
+ops.load()
+g = torch.Generator(device='cuda').manual_seed(3)
+n = 300
+big = LatentCache(1, 2 * n)   # the slot "past the cache" below stays inside this allocation
+big.write(torch.randn(2 * n, 576, device='cuda', generator=g).bfloat16(), torch.arange(2 * n, device='cuda'))
+lc = copy.copy(big)
+lc.codes, lc.scales, lc.rope = big.codes[:n], big.scales[:n], big.rope[:n]
+q = (torch.randn(2, 128, 576, device='cuda', generator=g) * 0.5).bfloat16()
+idx = torch.stack([torch.randperm(n, device='cuda', generator=g)[:128] for _ in range(2)]).int()
+good = idx.clone()
+idx[1, 5] = n + 7                                    # past the n-slot cache, inside the allocation
+good[1, 5] = -1
+ws = FlashWorkspace(2, 1, 'cuda')
+out = mla_flash(q, idx, lc, default_scale(), 1, ws)
+ref = mla_flash(q, good, lc, default_scale(), 1, FlashWorkspace(2, 1, 'cuda'))
+torch.cuda.synchronize()
+assert int(ws.err) == 2, int(ws.err)
+assert torch.equal(out, ref)
+print('ok')
+"""
+    env = dict(os.environ, XTIER_DEBUG_BOUNDS='1')
+    r = subprocess.run([sys.executable, '-c', code], env=env, capture_output=True, text=True, timeout=300,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0 and 'ok' in r.stdout, r.stdout + r.stderr

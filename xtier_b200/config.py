@@ -91,7 +91,8 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_TIMING', 'flag', False, 'log synchronized MoE time per forward'),
     _S('XTIER_PREFILL_PROFILE', 'flag', False, 'CUDA events per prefill phase'),
     _S('XTIER_PREFILL_MX', 'flag', False, 'grouped prefill of MXFP4 experts with MXFP8 activations (kind::mxf8f6f4)'),
-    _S('XTIER_DEBUG_BOUNDS', 'flag', False, 'bounds-checked kernels: a bad index sets the device error word'),
+    _S('XTIER_DEBUG_BOUNDS', 'flag', False, 'flash MLA checks every selected cache slot: an out-of-range one is skipped '
+       'and sets the error word to 2'),
     _S('XTIER_DEBUG_STALL_US', 'int', 0, 'test only: the mailbox dispatcher stalls this long per request'),
     _S('XTIER_DEBUG_SEQ_START', 'int', 0, 'test only: first sequence number of the swap ring (wrap tests)'),
     _S('XTIER_ROWS_MODE', 'str', 'direct', 'row tables: direct (O_DIRECT reads) or ram (mapped and locked)'),

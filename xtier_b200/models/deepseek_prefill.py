@@ -235,5 +235,8 @@ class SparsePrefill:
 
     def check(self):
         for name, e in (('indexer', self.idx_err), ('MLA', self.ws.err), ('expert GEMM', self.moe.err)):
-            if e is not None and int(e.item()):
+            code = 0 if e is None else int(e.item())
+            if code == 2:
+                raise RuntimeError(f'sparse prefill: the {name} kernel met a cache slot out of range')
+            if code:
                 raise RuntimeError(f'sparse prefill: a bounded wait of the {name} kernel ran out')

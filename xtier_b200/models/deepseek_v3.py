@@ -555,7 +555,10 @@ class DeepSeekV3Model:
 
     def check(self, st: dict | None = None):
         """Raises when a bounded wait of the last steps ran out (EP exchange, mailbox, MLA of state `st`)."""
-        if st is not None and 'mla_ws' in st and int(st['mla_ws'].err.item()):
+        code = int(st['mla_ws'].err.item()) if st is not None and 'mla_ws' in st else 0
+        if code == 2:
+            raise RuntimeError('MLA attention: a cache slot out of range (XTIER_DEBUG_BOUNDS)')
+        if code:
             raise RuntimeError('MLA attention: a bounded wait ran out')
         if self.ep is not None:
             self.ep.check()
