@@ -195,6 +195,55 @@ def test_moe_decode_with_cpu_tier_and_graph(cuda_ops):
         mb.close()
 
 
+def test_moe_layer_without_gpu_slots(cuda_ops):
+    """A layer with no hot and no shared expert: every route goes to the CPU engine through the mailbox, decode
+    (eager and graph-replayed) and a prefill-sized call both match the fp32 reference."""
+    from xtier_b200.cache.pool import TieredMoE
+    from xtier_b200.engine import CpuEngine
+    from xtier_b200.engine.mailbox import Mailbox
+    E, H, I, k, m = 16, 512, 256, 4, 2
+    ex, _, router, x = _moe_case(E, H, I, k, m, formats.NVFP4, seed=9)
+    mb = Mailbox(H, timeout_s=10.0)
+    eng = CpuEngine(ex, threads=2)
+    layer = TieredMoE(5, router, ex, k, hot=[], mailbox=mb, engine=eng, device='cuda')
+    assert layer.slotless and layer.gpu_bytes() == 0
+    mb.start()
+    try:
+        xc = x.cuda()
+        out = layer.forward(xc)
+        torch.cuda.synchronize()
+        mb.check()
+        ids, w = layer.ids[:m].cpu(), layer.w[:m].cpu()
+        assert bool((layer.slots[:m].cpu() < 0).all())
+        assert _rel(out.cpu(), formats.reference_moe(x, ids, w, ex)) < 1e-2
+        out_g = torch.empty_like(out)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            layer.forward(xc, out=out_g)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            layer.forward(xc, out=out_g)
+        out_g.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out_g, out)
+        del g
+        xp = torch.randn(40, H, generator=torch.Generator().manual_seed(10)).bfloat16()
+        outp = layer.forward(xp.cuda())        # prefill-sized: the CPU engine computes every route
+        torch.cuda.synchronize()
+        from xtier_b200.cache.pool import _PREFILL_BUFS   # the prefill call's own route buffers
+        pf = _PREFILL_BUFS[(layer.kk, E, I, H, layer.device)]
+        idp, wp = pf['ids'][:40, :k].cpu(), pf['w'][:40, :k].cpu()
+        refp = formats.reference_moe(xp, idp, wp, ex)
+        assert _rel(outp.cpu(), refp) < 1e-2
+        mb.check()
+    finally:
+        mb.stop()
+        mb.close()
+
+
 def test_mailbox_wait_times_out_without_hanging(cuda_ops):
     """Nothing answers the mailbox (no dispatcher): the GPU wait gives up after its deadline and reports it."""
     import time

@@ -198,7 +198,7 @@ def install(model, extra: int | None = None) -> list[ElasticSlots]:
     out = []
     for L in model.layers:
         moe = L['moe']
-        if moe.all_hot or moe.pool is None or not moe.can_refill:
+        if moe.all_hot or moe.pool is None or getattr(moe, 'slotless', False) or not moe.can_refill:
             continue
         n = extra if extra is not None else int(round((config.get('XTIER_CACHE_ELASTIC_MAX') - 1.0) * len(moe.hot)))
         n = max(0, min(n, moe.E - len(moe.hot)))

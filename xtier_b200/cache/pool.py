@@ -27,6 +27,7 @@ MAX_DECODE_TOKENS = 16
 _STAGING: dict = {}   # (cold experts, H, I, fmt, device) -> staging ExpertWeights shared by the layers
 _PREFILL_BUFS: dict = {}   # (kk, E, I, H, device) -> prefill route buffers shared by the layers
 _BUF_NAMES = ('ids', 'w', 'slots', 'mid', 'ws_logits', 'ws_count', 'gpu_part')
+_EMPTY_POOLS: dict = {}   # (H, I, fmt, device) -> one all-zero slot: the launch operand of layers without GPU slots
 
 
 class TieredMoE:
@@ -74,7 +75,18 @@ class TieredMoE:
                 self.pool.g13 = self.pool.g13.float().contiguous()
                 self.pool.g2 = self.pool.g2.float().contiguous()
         else:
-            self.pool = None
+            # no GPU slot at all: every route goes to the CPU tier. The decode kernels still run (every route skips
+            # the pool) so that the down kernel collects the CPU part through the mailbox and adds it; they need a
+            # pool operand, one zero slot that is never read, shared by every such layer of this shape
+            key = (self.H, self.I, self.fmt, self.device)
+            if key not in _EMPTY_POOLS:
+                one = experts.select(torch.tensor([0], device=experts.w13.device))
+                _EMPTY_POOLS[key] = ExpertWeights(self.fmt, *[torch.zeros_like(getattr(one, f), device=self.device)
+                                                              for f in ('w13', 'w2', 's13', 's2')],
+                                                  torch.zeros(1, 2, dtype=torch.float32, device=self.device),
+                                                  torch.zeros(1, dtype=torch.float32, device=self.device))
+            self.pool = _EMPTY_POOLS[key]
+        self.slotless = S == 0 and self.n_shared == 0
         table = torch.full((self.E,), -1, dtype=torch.int32)
         for s, e in enumerate(self.hot):
             table[e] = s
@@ -176,8 +188,8 @@ class TieredMoE:
                          add, out, out_f32, self.fmt_code,
                          self.mailbox.handle if (use_mailbox and self.mailbox is not None) else 0,
                          gpu_part=self.gpu_part[:m], peer=self.peer, spr=self.spr, host=self.host_table, host_base=hb)
-        else:   # no GPU slots at all: every route on the CPU
-            raise NotImplementedError('a layer without GPU slots needs at least the shared/hot pool')
+        else:
+            raise RuntimeError('TieredMoE: no pool operand')
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None,
                 active: torch.Tensor | None = None):
@@ -453,7 +465,7 @@ class TieredMoE:
         return list(self.hot) + (self.elastic.occupants() if self.elastic is not None else [])
 
     def gpu_bytes(self) -> int:
-        if self.pool is None:
+        if self.pool is None or self.slotless:
             return 0
         n = sum(getattr(self.pool, f).numel() * getattr(self.pool, f).element_size() for f in ('g13', 'g2'))
         if self.elastic is not None:     # reserved address space is not memory: count what is mapped
