@@ -107,3 +107,19 @@ def test_model_takes_per_layer_slots_and_the_route_profile(tmp_path, monkeypatch
     assert len(model.engines) == 1
     for e in model.engines:
         e.close()
+
+
+def test_cost_curve_peer_term():
+    """Experts another GPU holds cost p1 on the GPU side instead of the CPU round trip: with a cheap NVLink term the
+    curve drops where those experts would otherwise be cold, and is unchanged when every expert is hot here."""
+    import numpy as np
+    from xtier_b200.planner.cost import Coeffs, layer_time_curve
+    p = np.linspace(0.3, 0.01, 16)
+    c = Coeffs(g0=8.0, g1=0.5, c0=12.0, c1=25.0, p1=1.5)
+    base = layer_time_curve(p, c, m=4)
+    held = np.zeros(16, dtype=bool)
+    held[8:] = True                                    # the 8 least routed experts live in a peer's pool
+    peer = layer_time_curve(p, c, m=4, peer_held=held)
+    assert peer[16] == base[16]
+    assert np.all(peer[:8] < base[:8])
+    assert abs(peer[8] - (c.g0 + c.g1 * (1 - (1 - p[:8]) ** 4).sum() + c.p1 * (1 - (1 - p[8:]) ** 4).sum())) < 1e-6

@@ -87,17 +87,21 @@ def guard(curves, plan, budget_slots: int, min_gain: float = 0.01):
     return (plan, t_plan, t_uni) if t_plan <= (1 - min_gain) * t_uni else (uni, t_uni, t_uni)
 
 
-def curves_from_profile(profile: dict, coeffs: Coeffs, m: int = 1) -> list[np.ndarray]:
-    """profile: {"layers": {layer: [per-token route probability of each expert]}} (plan_trace output)."""
+def curves_from_profile(profile: dict, coeffs: Coeffs, m: int = 1,
+                        peer_held: dict | None = None) -> list[np.ndarray]:
+    """profile: {"layers": {layer: [per-token route probability of each expert]}} (plan_trace output). peer_held:
+    {layer: bool [E]} experts other GPUs' pools hold (peer mode), costed at the probe's NVLink term."""
     layers = sorted(int(k) for k in profile['layers'])
     return [layer_time_curve(np.asarray(profile['layers'][str(l)] if str(l) in profile['layers']
-                                        else profile['layers'][l]), coeffs, m) for l in layers]
+                                        else profile['layers'][l]), coeffs, m,
+                             None if peer_held is None else peer_held.get(l)) for l in layers]
 
 
-def make_plan(profile: dict, probe: dict | None, budget_slots: int, granularity: int = 1) -> dict:
+def make_plan(profile: dict, probe: dict | None, budget_slots: int, granularity: int = 1,
+              peer_held: dict | None = None) -> dict:
     coeffs = Coeffs(**(probe or {}).get('coeffs', {}))
     layers = sorted(int(k) for k in profile['layers'])
-    curves = curves_from_profile(profile, coeffs)
+    curves = curves_from_profile(profile, coeffs, peer_held=peer_held)
     plan, lam = best(curves, budget_slots, granularity)
     plan, t_plan, t_uni = guard(curves, plan, budget_slots)
     return {'slots': {str(l): int(n) for l, n in zip(layers, plan)}, 'predicted_us': t_plan, 'uniform_us': t_uni,

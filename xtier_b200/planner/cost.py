@@ -8,6 +8,9 @@ experts on the GPU gives, per decode call of m tokens:
                                                                                   engine time per cold expert)
   layer     t(n)     = max(t_gpu(n), t_cpu(n)) + a                            (both halves run at the same time)
 
+With a node-wide slot pool (peer mode), a cold expert that another GPU's pool holds is read over NVLink by the GPU
+kernels instead of going to the CPU: it adds p1 per expert touched to the GPU part and leaves the CPU part.
+
 The expected distinct-expert counts treat the m * k routes of a call as independent draws (an expert is touched with
 probability 1 - (1 - p_e)^m, p_e the per-token probability of being among the token's k routes). The max of two
 random times is approximated by the max of their means plus a spread term (Clark's formula for the expected maximum
@@ -31,6 +34,7 @@ class Coeffs:
     g1: float = 0.45      # us per hot expert touched (weight streaming)
     c0: float = 12.0      # us: mailbox round trip when the CPU has work
     c1: float = 25.0      # us per cold expert touched (CPU engine)
+    p1: float = 0.0       # us per expert touched that another GPU's pool holds (NVLink read)
     a: float = 0.0        # us: per-layer work outside the MoE (attention), added to every option
     sd_frac: float = 0.15  # relative spread of both halves (for the expected max)
 
@@ -55,20 +59,25 @@ def touch_probabilities(p: np.ndarray, m: int) -> np.ndarray:
     return 1.0 - np.power(1.0 - p, m)
 
 
-def layer_time_curve(p: np.ndarray, c: Coeffs, m: int = 1) -> np.ndarray:
-    """t(n) for n = 0..E hot slots (the n most routed experts on the GPU), microseconds per call."""
+def layer_time_curve(p: np.ndarray, c: Coeffs, m: int = 1, peer_held: np.ndarray | None = None) -> np.ndarray:
+    """t(n) for n = 0..E hot slots (the n most routed experts on the GPU), microseconds per call. peer_held: bool [E]
+    (expert order of p), experts another GPU's pool holds: when not hot here they cost p1 on the GPU side."""
     order = np.argsort(-np.asarray(p))
     q = touch_probabilities(np.asarray(p)[order], m)
     E = len(q)
+    peer = (np.zeros(E, dtype=bool) if peer_held is None else np.asarray(peer_held, dtype=bool)[order])
     out = np.empty(E + 1)
     cum_hot = np.concatenate([[0.0], np.cumsum(q)])
-    total = cum_hot[-1]
-    log_none = np.concatenate([[0.0], np.cumsum(np.log1p(-np.minimum(q, 1 - 1e-12))[::-1])])[::-1]
+    # touched experts past the n hottest: the peer-held ones (NVLink) and the rest (CPU)
+    cum_peer_tail = np.concatenate([np.cumsum((q * peer)[::-1])[::-1], [0.0]])
+    cum_cpu_tail = np.concatenate([np.cumsum((q * ~peer)[::-1])[::-1], [0.0]])
+    log_none = np.concatenate([np.cumsum(np.log1p(-np.minimum(q * ~peer, 1 - 1e-12))[::-1])[::-1], [0.0]])
     for n in range(E + 1):
         hot = cum_hot[n]
-        cold = total - hot
-        p_any_cold = 1.0 - math.exp(log_none[n]) if n < E else 0.0
-        tg = c.g0 + c.g1 * hot
+        on_peer = cum_peer_tail[n]
+        cold = cum_cpu_tail[n]
+        p_any_cold = 1.0 - math.exp(log_none[n])
+        tg = c.g0 + c.g1 * hot + c.p1 * on_peer
         tc = p_any_cold * c.c0 + c.c1 * cold
         out[n] = expected_max(tg, c.sd_frac * tg, tc, c.sd_frac * tc) + c.a
     return out

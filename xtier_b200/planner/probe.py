@@ -1,8 +1,12 @@
 """Planner probes: measure the cost-model coefficients on this machine.
 
-GPU side: CUDA-event timings of the decode MoE kernels of a synthetic layer for growing numbers of hot routes
-(-> g0, g1). CPU side: the engine's decode call for growing numbers of cold experts (-> c1), plus the mailbox round
-trip of a call whose work is one tiny expert (-> c0). Results are written as {"coeffs": {...}, "samples": {...}}.
+GPU side: the decode MoE call of a synthetic layer (route, gate/up, down) for growing numbers of hot routes, timed as
+CUDA-graph replays (no launch cost) -> g0, g1. CPU side: the engine's decode call for growing numbers of cold
+experts -> c1. Mailbox: the round trip of a captured decode call of a layer without GPU slots whose single route goes
+to a tiny expert on the CPU engine, minus that expert's engine time -> c0 (GPU publish, dispatcher wake-up, engine
+hand-off and the GPU's poll, both PCIe directions). NVLink: with a second GPU, the time to read one expert's weights
+from the peer's memory (device-to-device copy over the NVLink path, events on the reader) -> p1, the cost of a route
+to an expert another GPU's slot pool holds. Results are written as {"coeffs": {...}, "samples": {...}}.
 
 Reference parity: xtier/planner/probe.py:102-227 (graph timings of real mailbox/pool decode calls).
 """
@@ -38,6 +42,30 @@ def probe_cpu(H: int, I: int, fmt: str = formats.NVFP4, threads: int | None = No
     return samples
 
 
+def _graph_time_us(fn, reps: int) -> float:
+    """Device time of one fn() call: `reps` calls captured in a CUDA graph, replayed after warm-up."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) / reps * 1e3
+
+
 def probe_gpu(H: int, I: int, fmt: str = formats.NVFP4, reps: int = 50) -> list:
     from ..cache.pool import TieredMoE
     E = 64
@@ -47,29 +75,85 @@ def probe_gpu(H: int, I: int, fmt: str = formats.NVFP4, reps: int = 50) -> list:
     for k in (1, 2, 4, 8):
         layer = TieredMoE(0, torch.randn(E, H) * 0.02, ew, k, device='cuda')
         out = torch.empty_like(x)
-        for _ in range(5):
-            layer.forward(x, out=out)
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(reps):
-            layer.forward(x, out=out)
-        e.record()
-        torch.cuda.synchronize()
-        samples.append((k, s.elapsed_time(e) / reps * 1e3))
+        samples.append((k, _graph_time_us(lambda: layer.forward(x, out=out), reps)))
     return samples
+
+
+def probe_mailbox(H: int, fmt: str = formats.NVFP4, threads: int | None = None, reps: int = 30) -> dict:
+    """Captured decode call of a layer without GPU slots (one route per call, a tiny expert of 128 intermediate
+    units on the CPU engine) and that expert's engine time alone: their difference is the mailbox round trip."""
+    from ..cache.pool import TieredMoE
+    from ..engine import CpuEngine
+    from ..engine.mailbox import Mailbox
+    E, I = 4, 128
+    ew = formats.synthetic_experts(E, H, I, fmt, 'cpu', seed=9)
+    eng = CpuEngine(ew, threads=threads)
+    mb = Mailbox(H, timeout_s=10.0)
+    layer = TieredMoE(0, torch.randn(E, H) * 0.02, ew, 1, hot=[], mailbox=mb, engine=eng, device='cuda')
+    mb.start()
+    try:
+        x = torch.randn(1, H, device='cuda').bfloat16()
+        out = torch.empty_like(x)
+        call = _graph_time_us(lambda: layer.forward(x, out=out), reps)
+        mb.check()
+        xc, ids, w = x.cpu(), torch.zeros(1, 1, dtype=torch.int32), torch.ones(1, 1)
+        for _ in range(5):
+            eng.forward(xc, ids, w, decode=True)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            eng.forward(xc, ids, w, decode=True)
+        engine = (time.perf_counter() - t0) / reps * 1e6
+    finally:
+        mb.stop()
+        mb.close()
+        eng.close()
+    return {'call_us': call, 'engine_us': engine}
+
+
+def probe_peer(H: int, I: int, fmt: str = formats.NVFP4, reps: int = 20) -> dict | None:
+    """Time for GPU 0 to read one expert's weights from GPU 1's memory (device-to-device copy, events on GPU 0):
+    the NVLink term of a route to an expert another GPU's pool holds. None with fewer than two GPUs. The decode
+    kernels read peer slots with 16-byte loads, so this DMA rate is the upper bound they approach."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        return None
+    one = formats.synthetic_experts(1, H, I, fmt, 'cpu', seed=10)
+    nbytes = one.nbytes_per_expert()
+    src = torch.empty(nbytes, dtype=torch.uint8, device='cuda:1')
+    dst = torch.empty(nbytes, dtype=torch.uint8, device='cuda:0')
+    with torch.cuda.device(0):
+        for _ in range(3):
+            dst.copy_(src)
+        torch.cuda.synchronize(0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            dst.copy_(src)
+        b.record()
+        torch.cuda.synchronize(0)
+        us = a.elapsed_time(b) / reps * 1e3
+    return {'bytes': nbytes, 'us': us, 'gbs': nbytes / us / 1e3, 'peer_access': torch.cuda.can_device_access_peer(0, 1)}
 
 
 def measure(H: int, I: int, fmt: str = formats.NVFP4, threads: int | None = None, gpu: bool = True) -> dict:
     cpu = probe_cpu(H, I, fmt, threads)
     c0, c1 = fit(cpu)
     out = {'samples': {'cpu': cpu}}
-    co = Coeffs(c0=max(c0, 1.0) + 8.0, c1=max(c1, 0.1))   # + the PCIe handshake both ways
+    co = Coeffs(c1=max(c1, 0.1))
     if gpu and torch.cuda.is_available():
         g = probe_gpu(H, I, fmt)
         g0, g1 = fit(g)
         co.g0, co.g1 = max(g0, 0.5), max(g1, 0.01)
         out['samples']['gpu'] = g
+        mbx = probe_mailbox(H, fmt, threads)
+        co.c0 = max(mbx['call_us'] - mbx['engine_us'], 1.0)
+        out['samples']['mailbox'] = mbx
+        peer = probe_peer(H, I, fmt)
+        if peer is not None:
+            co.p1 = peer['us']
+            out['samples']['peer'] = peer
+    else:   # no GPU to measure the round trip on: the engine's fixed cost plus a nominal 8 us for PCIe both ways
+        co.c0 = max(c0, 1.0) + 8.0
+        out['c0_measured'] = False
     out['coeffs'] = co.to_dict()
     out['shape'] = {'hidden': H, 'inter': I, 'fmt': fmt}
     return out
