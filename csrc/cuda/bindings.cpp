@@ -749,6 +749,34 @@ void moe_grouped_mx(const Tensor &x8, const Tensor &sfx, const Tensor &codes, co
              "moe_grouped_mx");
 }
 
+int64_t pool_ring_create(int64_t capacity) {
+    void *h = xt_pool_ring_create(int(capacity));
+    check(h != nullptr, "pool_ring_create: mapped host or device allocation failed");
+    return reinterpret_cast<int64_t>(h);
+}
+
+void pool_ring_destroy(int64_t h) { xt_pool_ring_destroy(reinterpret_cast<void *>(h)); }
+
+int64_t pool_ring_post(int64_t h, int64_t seq, int64_t layer, int64_t expert, int64_t slot) {
+    return xt_pool_ring_post(reinterpret_cast<void *>(h), seq, int(layer), int(expert), int(slot));
+}
+
+int64_t pool_ring_applied(int64_t h) { return xt_pool_ring_applied(reinterpret_cast<void *>(h)); }
+
+void pool_ring_commit(int64_t h, const Tensor &tables, const Tensor &err) {
+    cuda_contig(tables, "tables");
+    check(tables.scalar_type() == at::kLong, "pool_ring_commit: tables int64 [layers] (device pointers)");
+    c10::cuda::CUDAGuard g(tables.device());
+    check_rc(xt_pool_ring_commit(reinterpret_cast<void *>(h), reinterpret_cast<int32_t *const *>(tables.data_ptr()),
+                                 int(tables.numel()), ptr<int>(err), stream()),
+             "pool_ring_commit");
+}
+
+void pool_ring_landed(int64_t h, int64_t seq, const Tensor &like) {
+    c10::cuda::CUDAGuard g(like.device());
+    check_rc(xt_pool_ring_landed(reinterpret_cast<void *>(h), seq, stream()), "pool_ring_landed");
+}
+
 void skinny_gemm(const Tensor &x, const Tensor &w, const std::optional<Tensor> &add, const Tensor &y,
                  const std::optional<Tensor> &part, int64_t splits, const Tensor &err) {
     cuda_contig(x, "x");
@@ -817,6 +845,12 @@ TORCH_LIBRARY(xtier, m) {
     m.def("skinny_gemm(Tensor x, Tensor w, Tensor? add, Tensor(a!) y, Tensor(b!)? part, int splits, Tensor(c!) err) "
           "-> ()");
     m.def("mx_quant_rows(Tensor x, Tensor? src, Tensor(a!) x8, Tensor(b!) sfx) -> ()");
+    m.def("pool_ring_create(int capacity) -> int", &pool_ring_create);
+    m.def("pool_ring_destroy(int h) -> ()", &pool_ring_destroy);
+    m.def("pool_ring_post(int h, int seq, int layer, int expert, int slot) -> int", &pool_ring_post);
+    m.def("pool_ring_applied(int h) -> int", &pool_ring_applied);
+    m.def("pool_ring_commit(int h, Tensor tables, Tensor(a!) err) -> ()");
+    m.def("pool_ring_landed(int h, int seq, Tensor like) -> ()");
     m.def("moe_grouped_mx(Tensor x8, Tensor sfx, Tensor codes, Tensor scales, Tensor gscale, Tensor tiles, "
           "bool gate_up, int I, Tensor? route_w, Tensor(a!) out, Tensor(b!) err, Tensor? dst_rows=None) -> ()");
     m.def("dsa_quant_q(Tensor q, Tensor w, float w_scale, Tensor(a!) q8, Tensor(b!) w8) -> ()");
@@ -878,6 +912,8 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("head_gemm", &head_gemm);
     m.impl("rope_heads", &rope_heads);
     m.impl("skinny_gemm", &skinny_gemm);
+    m.impl("pool_ring_commit", &pool_ring_commit);
+    m.impl("pool_ring_landed", &pool_ring_landed);
     m.impl("mx_quant_rows", &mx_quant_rows);
     m.impl("moe_grouped_mx", &moe_grouped_mx);
     m.impl("dsa_quant_q", &dsa_quant_q);

@@ -113,6 +113,12 @@ int xt_moe_grouped_mx(const void *x8, const void *sfx, int R, const void *codes,
                       const int32_t *tiles, int T, int gate_up, int K, int N_rows, int I, const float *gscale,
                       const float *route_w, const int32_t *dst_row, void *mid, float *y, int out_cols, int *error,
                       cudaStream_t stream);
+void *xt_pool_ring_create(int capacity);
+void xt_pool_ring_destroy(void *h);
+int xt_pool_ring_post(void *h, int64_t seq, int layer, int expert, int slot);
+int64_t xt_pool_ring_applied(void *h);
+int xt_pool_ring_commit(void *h, int32_t *const *tables, int n_tables, int *error, cudaStream_t stream);
+int xt_pool_ring_landed(void *h, int64_t seq, cudaStream_t stream);
 int xt_skinny_splits(int N, int K, int sms);
 int xt_skinny_gemm(const void *x, const void *W, const void *add, void *y, float *part, int M, int N, int K,
                    int splits, int *error, cudaStream_t stream);

@@ -175,6 +175,8 @@ class ElasticSlots:
         if n >= self.mapped:
             return
         moe = self.moe
+        if moe.ring is not None:   # no MAP into a released slot may still be pending
+            moe.ring.sync()
         for j in range(n, self.mapped):
             e = self.occupant[j]
             if e >= 0:

@@ -30,6 +30,14 @@ _BUF_NAMES = ('ids', 'w', 'slots', 'mid', 'ws_logits', 'ws_count', 'gpu_part')
 _EMPTY_POOLS: dict = {}   # (H, I, fmt, device) -> one all-zero slot: the launch operand of layers without GPU slots
 
 
+def _pinned(ew: ExpertWeights) -> ExpertWeights:
+    """Page-locked copy of a small host ExpertWeights (the source of a copy that must not block the host)."""
+    if not torch.cuda.is_available() or ew.w13.is_cuda:
+        return ew
+    return ExpertWeights(ew.fmt, *[getattr(ew, f).contiguous().pin_memory()
+                                   for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2')])
+
+
 class TieredMoE:
     def __init__(self, layer: int, router_w: torch.Tensor, experts: ExpertWeights, top_k: int,
                  hot: list[int] | None = None, shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1,
@@ -109,6 +117,8 @@ class TieredMoE:
         # cold-backed CPU tier (cache/cold.py ColdPrefill): the prefill staging is gathered from the engine's RAM
         # slots and the drive store instead of a host copy of the layer
         self.cold_prefill = None
+        # swap ring (cache/ring.py SwapRing): when set, swaps and fills copy on its stream and the GPU applies them
+        self.ring = None
         self._alloc(max_tokens)
 
     def _make_bufs(self, m: int) -> dict:
@@ -206,6 +216,8 @@ class TieredMoE:
 
     # ------------------------------------------------------------------ prefill (hybrid: GPU hot || CPU rest)
     def prefill(self, x: torch.Tensor, out: torch.Tensor, add: torch.Tensor | None = None, chunk: int = 1024):
+        if self.ring is not None:   # the device tables catch up with the host residency the staging follows
+            self.ring.sync()
         grouped = (x.shape[0] >= config.get('XTIER_GPU_PREFILL_MIN') and self.pool is not None
                    and (self.all_hot or self.host is not None or getattr(self, '_host_cold', None) is not None
                         or self.cold_prefill is not None))
@@ -421,12 +433,15 @@ class TieredMoE:
         if slot < 0 or int(self.table_host[incoming]) >= 0:
             raise ValueError(f'swap {incoming} <- {victim}: bad residency')
         src = self._expert_host(incoming)
-        self.table[victim] = -1
         self.table_host[victim] = -1
-        for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
-            getattr(self.pool, f)[slot].copy_(getattr(src, f)[0], non_blocking=True)
-        self.table[incoming] = slot
         self.table_host[incoming] = slot
+        if self.ring is not None:   # unmapped now, copied on the ring's stream, mapped once the copy has landed
+            self.ring.place(self, incoming, slot, _pinned(src), victim=victim)
+        else:
+            self.table[victim] = -1
+            for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+                getattr(self.pool, f)[slot].copy_(getattr(src, f)[0], non_blocking=True)
+            self.table[incoming] = slot
         if slot >= len(self.hot):   # an elastic slot: both experts keep their prefill staging index
             self.elastic.occupant[slot - self.elastic.first] = incoming
             return
@@ -455,9 +470,12 @@ class TieredMoE:
         if slot is None or int(self.table_host[incoming]) >= 0:
             raise ValueError(f'fill {incoming}: no free elastic slot or already resident')
         src = self._expert_host(incoming)
-        for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
-            getattr(self.pool, f)[slot].copy_(getattr(src, f)[0], non_blocking=True)
-        self.table[incoming] = slot
+        if self.ring is not None:
+            self.ring.place(self, incoming, slot, _pinned(src))
+        else:
+            for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+                getattr(self.pool, f)[slot].copy_(getattr(src, f)[0], non_blocking=True)
+            self.table[incoming] = slot
         self.table_host[incoming] = slot
         self.elastic.occupant[slot - self.elastic.first] = incoming
 

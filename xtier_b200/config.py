@@ -53,6 +53,7 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_CACHE_LOG', 'int', 0, 'log the cache statistics every N policy rounds (0: off)'),
     _S('XTIER_DECODE_MISS_GPU', 'float', 0.0, 'share of a token\'s CPU-tier routes the GPU computes from pinned host '
        'memory over PCIe (one per token at most; 0: off)'),
+    _S('XTIER_CACHE_RING', 'flag', True, 'hot-slot swaps copy on a side stream and the decode step maps them'),
     _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in VMM-backed memory that prefills take back'),
     _S('XTIER_CACHE_ELASTIC_MAX', 'float', 2.0, 'address space per layer, as a multiple of its base hot slots'),
     _S('XTIER_CACHE_ELASTIC_RESERVE_GIB', 'float', 2.0, 'free device memory never given to extra slots'),

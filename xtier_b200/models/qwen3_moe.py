@@ -249,6 +249,15 @@ class Qwen3MoeModel:
             if config.get('XTIER_CACHE_ELASTIC'):
                 from ..cache.elastic import Governor, install
                 self.governor = Governor(install(self))
+        # swap ring: swaps copy on a side stream; the decode step's first kernel maps the ones that have landed.
+        # Layers whose decode kernels read the pinned host pool (XTIER_DECODE_MISS_GPU) keep stream-ordered swaps
+        self.ring = None
+        if self.policy is not None and dev.type == 'cuda' and config.get('XTIER_CACHE_RING'):
+            ring_layers = [L['moe'] for L in self.layers
+                           if L['moe'].can_refill and not L['moe'].all_hot and L['moe'].host_table is None]
+            if ring_layers:
+                from ..cache.ring import SwapRing
+                self.ring = SwapRing(ring_layers, dev)
 
     @classmethod
     def from_pretrained(cls, path, device='cuda', hot_fraction: float = 1.0, fmt: str | None = None, **kw):
@@ -329,6 +338,8 @@ class Qwen3MoeModel:
         B = buf['tokens'].shape[0]
         side = st.get('side') if B <= 16 else None
         main = torch.cuda.current_stream(self.device) if side is not None else None
+        if getattr(self, 'ring', None) is not None:   # hot-slot swaps whose copies have landed take effect
+            self.ring.commit()
         torch.add(buf['pos'], 1, out=buf['seqlens'])
         torch.index_select(self.embed, 0, buf['tokens'], out=buf['residual'])
         if self.bigram is not None:   # NVMe hashed-bigram rows, looked up inside the graph
