@@ -546,6 +546,32 @@ void mla_flash(const Tensor &q, const Tensor &idx, const Tensor &codes, const Te
              "mla_flash");
 }
 
+// Causal GQA prefill attention of q [T, Hq, 128] (a view with unit stride along the last dim) at positions
+// start .. start + T - 1 over row `row` of the caches k, v [B, Hkv, max_len, 128] (contiguous BF16); out [T, Hq, 128]
+// likewise a view.
+void attn_prefill(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor &out, int64_t row, int64_t start,
+                  double scale, const Tensor &err) {
+    auto view_ok = [](const Tensor &t) {
+        return t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 3 && t.size(2) == 128 && t.stride(2) == 1;
+    };
+    check(view_ok(q) && view_ok(out) && out.size(0) == q.size(0) && out.size(1) == q.size(1),
+          "attn_prefill: q and out [T, Hq, 128] bf16 (unit stride along the last dim)");
+    cuda_contig(k, "k");
+    cuda_contig(v, "v");
+    check(k.dim() == 4 && k.size(3) == 128 && k.sizes() == v.sizes() && k.scalar_type() == at::kBFloat16 &&
+              v.scalar_type() == at::kBFloat16,
+          "attn_prefill: k, v [B, Hkv, max_len, 128] bf16");
+    const int64_t T = q.size(0), Hq = q.size(1), Hkv = k.size(1), L = k.size(2);
+    check(row >= 0 && row < k.size(0) && start >= 0 && start + T <= L && Hq % Hkv == 0,
+          "attn_prefill: row / start out of range, or Hq not a multiple of Hkv");
+    check(err.is_cuda() && err.scalar_type() == at::kInt, "attn_prefill err int32");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_attn_prefill(q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), k.size(0) * Hkv * L,
+                             row * Hkv * L, L, int(T), int(start), int(Hq), int(Hkv), out.data_ptr(), out.stride(0),
+                             out.stride(1), float(scale), ptr<int>(err), stream()),
+             "attn_prefill");
+}
+
 void dsa_key_write(const Tensor &k, const Tensor &slot, const Tensor &codes, const Tensor &kscale) {
     cuda_contig(k, "k");
     check(k.size(-1) == 128 && slot.scalar_type() == at::kLong && slot.numel() == k.size(0) &&
@@ -890,6 +916,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("dsa_index_tc(Tensor q8, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, Tensor(a!) scores, "
           "int nq, Tensor(b!) err) -> ()");
     m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");
+    m.def("attn_prefill(Tensor q, Tensor k, Tensor v, Tensor(a!) out, int row, int start, float scale, "
+          "Tensor(b!) err) -> ()");
     m.def("mla_flash(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!)? part_o, "
           "Tensor(b!)? part_ml, Tensor(c!) out, float scale, int splits, Tensor(d!) err, Tensor? q_rope=None) -> ()");
     m.def("mla_decode(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!) kg, Tensor(b!) vt, "
@@ -938,6 +966,7 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("l2_prefetch", &l2_prefetch);
     m.impl("mla_kv_write", &mla_kv_write);
     m.impl("mla_decode", &mla_decode);
+    m.impl("attn_prefill", &attn_prefill);
     m.impl("mla_flash", &mla_flash);
     m.impl("dsa_key_write", &dsa_key_write);
     m.impl("dsa_index_decode", &dsa_index_decode);

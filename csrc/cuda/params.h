@@ -227,6 +227,9 @@ int xt_mla_prep(const void *in, int ld, int q_lora, const void *q_norm, const vo
                 void *lat_out, int T, cudaStream_t stream);
 int xt_head_gemm(const xt::HeadGemmParams *p, int heads, cudaStream_t stream);
 int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream);
+int xt_attn_prefill(const void *q, int64_t q_ts, int64_t q_hs, const void *k, const void *v, int64_t kv_rows,
+                    int64_t kv_row0, int64_t kv_hs, int T, int start, int Hq, int Hkv, void *out, int64_t out_ts,
+                    int64_t out_hs, float scale, int *error, cudaStream_t stream);
 int xt_mla_flash(const void *q_lat, int64_t ql_ts, int64_t ql_hs, const void *q_rope, int64_t qr_ts, int64_t qr_hs,
                  const int32_t *idx, int Q, int nsel, const void *codes, const void *scales, const void *rope,
                  float *part_o, float *part_ml, void *out, int64_t out_ts, int64_t out_hs, float scale, int splits,

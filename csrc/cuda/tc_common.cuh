@@ -43,6 +43,17 @@ XT_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = 1u << 24)
     return false;
 }
 
+// Non-blocking test of phase `parity`: true when it has completed.
+XT_DEV bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // 2-D TMA tile load into shared memory, completing on `bar` (x = innermost coordinate, in elements).
 XT_DEV void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
     asm volatile(

@@ -63,8 +63,6 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_CACHE_ELASTIC_CHECK', 'int', 16, 'decode steps between critical-memory checks'),
     _S('XTIER_CACHE_ELASTIC_COOLDOWN_S', 'float', 600.0, 'no growth for this long after a critical release'),
     _S('XTIER_CACHE_ELASTIC_EXTRAPOLATE', 'float', 2.0, 'how far a learnt need is scaled up to bound a larger one'),
-    _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in memory only a prefill needs (VMM granules)'),
-    _S('XTIER_CACHE_ELASTIC_RESERVE_GIB', 'float', 2.0, 'memory the elastic slots always leave free'),
     _S('XTIER_GPU2_SLOTS', 'str', '', 'auto / on: the hot slots of all GPUs of the process group form one pool, '
        'read over NVLink'),
     _S('XTIER_EP', 'int', 0, 'expert-parallel ranks of the hot-slot pool (0: the world size)'),
@@ -92,6 +90,7 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_TIMING', 'flag', False, 'log synchronized MoE time per forward'),
     _S('XTIER_PREFILL_PROFILE', 'flag', False, 'CUDA events per prefill phase'),
     _S('XTIER_PREFILL_MX', 'flag', False, 'grouped prefill of MXFP4 experts with MXFP8 activations (kind::mxf8f6f4)'),
+    _S('XTIER_ATTN_PREFILL_EMU', 'int', 3, 'prefill attention: exponential pairs of every 8 computed on the FMA pipe'),
     _S('XTIER_DEBUG_BOUNDS', 'flag', False, 'flash MLA checks every selected cache slot: an out-of-range one is skipped '
        'and sets the error word to 2'),
     _S('XTIER_DEBUG_STALL_US', 'int', 0, 'test only: the mailbox dispatcher stalls this long per request'),

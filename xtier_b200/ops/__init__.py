@@ -64,6 +64,17 @@ def attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits
     _ops().attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits, scale)
 
 
+def attn_prefill(q, k_cache, v_cache, row: int, start: int, scale: float, out=None):
+    """Causal GQA attention of q [T, Hq, 128] (a view with unit stride along the last dim) at positions
+    start .. start + T - 1 over row `row` of the caches [B, Hkv, max_len, 128] (tcgen05 flash kernel): query t sees keys
+    0 .. start + t. Returns out [T, Hq, 128] (or writes the given view). A wait that runs out sets the shared error
+    word (gemm_error_word); the caller's check() raises."""
+    if out is None:
+        out = torch.empty(q.shape[0], q.shape[1], 128, dtype=torch.bfloat16, device=q.device)
+    _ops().attn_prefill(q, k_cache, v_cache, out, row, start, scale, gemm_error_word(q.device))
+    return out
+
+
 def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k: int, mode: int = 0,
               n_group: int = 1, topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0,
               mailbox: int = 0, active=None, logits_in=None, cold_index=None, share_min: int = 0,
