@@ -125,7 +125,7 @@ XT_DEV float ap_max3(float a, float b, float c) {
 // [-1/2, 1/2] by a degree-3 polynomial (coefficients fitted here by reweighted least squares for relative error;
 // max 1.1e-4, below BF16's 2^-9), and 2^j added to the exponent field. x is clamped at -125 (2^-125 for a masked key
 // is 0 for every later use: the BF16 P times V and the row sum).
-constexpr int AP_EMU = 3;   // default: pairs of every 8 whose exponentials take the polynomial
+constexpr int AP_EMU = 0;   // default: pairs of every 8 whose exponentials take the polynomial (measured best: none)
 XT_DEV void ap_exp2_poly(float x0, float x1, float &p0, float &p1) {
     const uint64_t magic = ap_pack(12582912.f, 12582912.f), nmagic = ap_pack(-12582912.f, -12582912.f);
     const uint64_t neg1 = ap_pack(-1.f, -1.f);

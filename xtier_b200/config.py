@@ -90,7 +90,8 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_TIMING', 'flag', False, 'log synchronized MoE time per forward'),
     _S('XTIER_PREFILL_PROFILE', 'flag', False, 'CUDA events per prefill phase'),
     _S('XTIER_PREFILL_MX', 'flag', False, 'grouped prefill of MXFP4 experts with MXFP8 activations (kind::mxf8f6f4)'),
-    _S('XTIER_ATTN_PREFILL_EMU', 'int', 3, 'prefill attention: exponential pairs of every 8 computed on the FMA pipe'),
+    _S('XTIER_PREFILL_ATTN', 'str', 'tc', 'prefill attention: tc (this framework\'s tcgen05 kernel) or sdpa (PyTorch)'),
+    _S('XTIER_ATTN_PREFILL_EMU', 'int', 0, 'prefill attention: exponential pairs of every 8 computed on the FMA pipe'),
     _S('XTIER_DEBUG_BOUNDS', 'flag', False, 'flash MLA checks every selected cache slot: an out-of-range one is skipped '
        'and sets the error word to 2'),
     _S('XTIER_DEBUG_STALL_US', 'int', 0, 'test only: the mailbox dispatcher stalls this long per request'),

@@ -418,6 +418,10 @@ class Qwen3MoeModel:
         h = torch.empty_like(residual)
         moe_out = torch.empty_like(residual)
         q = torch.empty(T, cfg.heads, D, dtype=torch.bfloat16, device=dev)
+        # prefill attention: the tcgen05 kernel on a GPU (head dim 128); PyTorch's attention on the CPU and with
+        # XTIER_PREFILL_ATTN=sdpa
+        attn_flat = (torch.empty(T, cfg.heads * D, dtype=torch.bfloat16, device=dev)
+                     if dev.type == 'cuda' and D == 128 and config.get('XTIER_PREFILL_ATTN') != 'sdpa' else None)
         copy_stream = None
         if T >= config.get('XTIER_GPU_PREFILL_MIN') and dev.type == 'cuda':
             copy_stream = getattr(self, '_copy_stream', None) or torch.cuda.Stream(device=dev)
@@ -430,16 +434,21 @@ class Qwen3MoeModel:
             qkv = ops.linear(h, L['qkv'])
             ops.qk_norm_rope_kv(qkv, L['q_norm'], L['k_norm'], pos, rows, q, st['k'][li], st['v'][li], cfg.heads,
                                 cfg.kv_heads, cfg.rope_theta, cfg.eps)
-            kk = st['k'][li][row:row + 1, :, :start + T]
-            vv = st['v'][li][row:row + 1, :, :start + T]
-            qq = q.transpose(0, 1).unsqueeze(0)
-            if start == 0 or T == 1:
-                attn = _sdpa(qq, kk, vv, None, start == 0)
-            else:   # a continuation chunk: query i sees keys up to position start + i
-                mask = (torch.arange(start + T, device=dev)[None, :] <=
-                        (start + torch.arange(T, device=dev))[:, None])
-                attn = _sdpa(qq, kk, vv, mask, False)
-            o = ops.linear(attn[0].transpose(0, 1).reshape(T, -1).contiguous(), L['o'])
+            if attn_flat is not None:   # tcgen05 causal GQA kernel, written straight into the o-projection input
+                ops.attn_prefill(q, st['k'][li], st['v'][li], row, start, 1.0 / math.sqrt(D),
+                                 out=attn_flat.view(T, cfg.heads, D))
+                o = ops.linear(attn_flat, L['o'])
+            else:
+                kk = st['k'][li][row:row + 1, :, :start + T]
+                vv = st['v'][li][row:row + 1, :, :start + T]
+                qq = q.transpose(0, 1).unsqueeze(0)
+                if start == 0 or T == 1:
+                    attn = _sdpa(qq, kk, vv, None, start == 0)
+                else:   # a continuation chunk: query i sees keys up to position start + i
+                    mask = (torch.arange(start + T, device=dev)[None, :] <=
+                            (start + torch.arange(T, device=dev))[:, None])
+                    attn = _sdpa(qq, kk, vv, mask, False)
+                o = ops.linear(attn[0].transpose(0, 1).reshape(T, -1).contiguous(), L['o'])
             ops.add_rmsnorm(o, residual, L['post_norm'], h, cfg.eps)
             if copy_stream is not None and li + 1 < len(self.layers):
                 # the next layer's cold experts cross PCIe while this layer computes; its staging buffer (layer

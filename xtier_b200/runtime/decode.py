@@ -68,6 +68,11 @@ class Generator:
             self._step_body()
 
     def check(self):
+        dev = getattr(self.model, 'device', None)
+        if dev is not None and torch.device(dev).type == 'cuda':
+            from .. import ops
+            if int(ops.gemm_error_word(dev).item()):
+                raise RuntimeError('a tensor-core kernel (GEMM or prefill attention) had a bounded wait run out')
         mb = getattr(self.model, 'mailbox', None)
         if mb is not None:
             mb.check()
