@@ -40,11 +40,11 @@ constexpr int AP_D = 128;             // head dim
 constexpr int AP_KS = 2;              // K ring stages
 constexpr int AP_VS = 2;              // V ring stages
 constexpr int AP_THREADS = 384;
-constexpr float AP_TAU = 8.f;
+constexpr float AP_TAU = 8.f;         // log2 of the running-max growth tolerated before O is rescaled
 constexpr int AP_REG_LAUNCH = 168;    // registers per thread at launch (65536 / 384, rounded to the allocation unit)
 constexpr int AP_REG_LOW = 72;        // first warpgroup after the split
-constexpr int AP_REG_HIGH = 216;     // softmax warpgroups after the split
-static_assert(128 * AP_REG_LOW + 256 * AP_REG_HIGH <= AP_THREADS * AP_REG_LAUNCH, "register split over budget");         // log2 of the running-max growth tolerated before O is rescaled
+constexpr int AP_REG_HIGH = 216;      // softmax warpgroups after the split
+static_assert(128 * AP_REG_LOW + 256 * AP_REG_HIGH <= AP_THREADS * AP_REG_LAUNCH, "register split over budget");
 
 struct ApSmem {
     static constexpr int PANEL = 128 * 128;          // 16 KB: 128 rows x 64 BF16 (one 128-byte swizzled panel)

@@ -31,6 +31,7 @@ from __future__ import annotations
 import dataclasses
 import math
 
+import numpy as np
 import torch
 
 from .. import formats, ops
@@ -173,17 +174,59 @@ def ep_layout(E: int, world: int, gpu_per_rank: int, seed: int, stride: int | No
     return table, pools, sorted(cpu)
 
 
+def ep_layout_ranked(E: int, world: int, n_gpu: int, popularity, stride: int, width: int | None = None):
+    """Expert placement of one MoE layer when a plan gives its node-wide GPU expert count: the `n_gpu` most routed
+    experts (by `popularity`, any per-expert score) sit in their owners' pools (owner r holds experts
+    [r * El, (r + 1) * El)), the rest in the CPU tier, most routed first. Returns (table, pools, cpu) as ep_layout;
+    a pool over `width` slots (default stride) raises."""
+    width = stride if width is None else width
+    El = E // world
+    pop = np.asarray(popularity, dtype=np.float64)
+    order = sorted(range(E), key=lambda e: (-pop[e], e))
+    gpu = set(order[:max(0, min(E, n_gpu))])
+    table = torch.full((E,), -1, dtype=torch.int32)
+    pools = []
+    for r in range(world):
+        pool = [e for e in range(r * El, (r + 1) * El) if e in gpu]
+        if len(pool) > width:
+            raise ValueError(f'ep_layout_ranked: rank {r} gets {len(pool)} experts, its pool has {width} slots')
+        for s, e in enumerate(pool):
+            table[e] = r * stride + s
+        pools.append(pool)
+    return table, pools, [e for e in order if e not in gpu]
+
+
+def ranked_pool_width(E: int, world: int, plan: dict, popularity: dict) -> int:
+    """The largest per-rank pool `ep_layout_ranked` makes over the layers of `plan` ({layer: node-wide GPU experts})."""
+    El = E // world
+    width = 1
+    for li, n in plan.items():
+        pop = np.asarray(popularity[li], dtype=np.float64)
+        top = sorted(range(E), key=lambda e: (-pop[e], e))[:n]
+        counts = np.bincount(np.asarray(top, dtype=np.int64) // El, minlength=world) if top else [0]
+        width = max(width, int(max(counts)))
+    return width
+
+
 class DeepSeekV3Model:
     def __init__(self, cfg: DeepSeekV3Config, device='cuda', seed: int = 0, moe_factory=None, max_tokens: int = 64,
                  ep: bool = False, gpu_experts: int | None = None, mailbox=None, engine_threads: int | None = None,
-                 decode_tokens: int = 16, ep_timeout_s: float = 30.0, indexer: bool = False):
+                 decode_tokens: int = 16, ep_timeout_s: float = 30.0, indexer: bool = False,
+                 gpu_plan: dict | None = None, popularity: dict | None = None, cold=None,
+                 ram_experts: int | None = None, plan_fn=None):
         """moe_factory(layer, router_w, corr_bias, experts_fn, shared_experts) -> an MoE layer with .forward(x, out);
         experts_fn(ids) generates the quantized experts (synthetic MXFP4 bytes) of the given expert ids.
         Default: every expert on this GPU (TieredMoE, all hot).
         ep: expert parallelism over the process group (world 1 allowed); `gpu_experts` pool slots per rank and MoE
         layer (default: every owned expert), the rest in the CPU tier through `mailbox` (required then) with
         `engine_threads` workers; `decode_tokens` tokens per rank and step. indexer: build the DSA indexer's
-        projections whatever the decode attention (the sparse prefill needs them)."""
+        projections whatever the decode attention (the sparse prefill needs them).
+        Three tiers (ep only): `gpu_plan` {MoE layer: node-wide GPU experts} (a planner output) places each layer's
+        most routed experts by `popularity` {layer: per-expert score} in their owners' pools; with `cold` (a
+        cache.cold.ColdPool) the CPU engine of a layer keeps `ram_experts` of the rest in RAM and reads the others
+        from the cold store on demand (rank 0 writes the layer's records, the other ranks fill their RAM slots from
+        them). `plan_fn({layer: (router_w, corr_bias)}) -> (gpu_plan, popularity)` computes both once every
+        layer's router exists."""
         self.cfg = cfg
         dev = self.device = torch.device(device)
         g = torch.Generator(device='cpu').manual_seed(seed)
@@ -192,6 +235,10 @@ class DeepSeekV3Model:
         self.engines = []
         self.ep = None
         self.decode_tokens = decode_tokens
+        self.gpu_plan, self.popularity, self.cold, self.ram_experts = gpu_plan, popularity, cold, ram_experts
+        self.bigram = None   # tables.engram.BigramTable (attach_bigram)
+        if gpu_plan is not None and (not ep or popularity is None):
+            raise ValueError('gpu_plan places experts by popularity under expert parallelism')
 
         def randn(*shape):
             t = torch.empty(*shape, dtype=torch.bfloat16, device=dev)
@@ -204,18 +251,8 @@ class DeepSeekV3Model:
         self.final_norm = ones(H)
         qk = cfg.qk_nope + cfg.qk_rope
         stage = None
-        if ep:
-            from ..parallel import dist as xdist
-            from ..parallel.ep import EPComm
-            env = xdist.init()
-            El = cfg.experts // env.world
-            self.gpu_per_rank = El if gpu_experts is None else max(1, min(El, int(gpu_experts)))
-            if self.gpu_per_rank < El and mailbox is None:
-                raise ValueError('a CPU tier (gpu_experts < experts per rank) needs a mailbox')
-            self.ep = EPComm(H, cfg.inter, cfg.experts, cfg.top_k, decode_tokens, dev, timeout_s=ep_timeout_s,
-                             slots_per_rank=self.gpu_per_rank + cfg.shared, n_shared=cfg.shared)
-            self.ep_rank, self.ep_world = env.rank, env.world
         self.layers = []
+        pending = []   # MoE layers: built once every layer's router exists (a plan may depend on all of them)
         for li in range(cfg.layers):
             L = dict(in_norm=ones(H), post_norm=ones(H),
                      qkv_a=randn(cfg.q_lora + cfg.kv_lora + cfg.qk_rope, H), q_a_norm=ones(cfg.q_lora),
@@ -236,23 +273,47 @@ class DeepSeekV3Model:
                 router = randn(cfg.experts, H)
                 corr = torch.randn(cfg.experts, generator=g) * 0.01
                 seed_l = seed * 1000 + li
-
-                def experts_fn(ids, seed_l=seed_l):
-                    return formats.synthetic_experts(len(ids), H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
-
                 shared = formats.synthetic_experts(cfg.shared, H, cfg.inter, cfg.fmt, dev, seed=seed_l + 500,
                                                    std=cfg.std) if cfg.shared else None
-                if ep:
-                    L['moe'], stage = self._ep_layer(li, router, corr, shared, seed_l, engine_threads, stage)
-                elif moe_factory is None:
-                    from ..cache.pool import TieredMoE
-                    L['moe'] = TieredMoE(li, router, experts_fn(list(range(cfg.experts))), cfg.top_k, shared=shared,
-                                         mode=1, n_group=cfg.n_group, topk_group=cfg.topk_group, renorm=True,
-                                         scale=cfg.routed_scale, corr_bias=corr, device=dev, max_tokens=16)
-                else:
-                    L['moe'] = moe_factory(li, router, corr, experts_fn, shared)
+                pending.append((li, router, corr, shared, seed_l))
             self.layers.append(L)
-        del stage
+        if plan_fn is not None:   # e.g. the planner's auto-layout over route probabilities of these routers
+            self.gpu_plan, self.popularity = plan_fn({li: (r, c) for li, r, c, _, _ in pending})
+            gpu_plan, popularity = self.gpu_plan, self.popularity
+            if gpu_plan is not None and (not ep or popularity is None):
+                raise ValueError('gpu_plan places experts by popularity under expert parallelism')
+        if ep:
+            from ..parallel import dist as xdist
+            from ..parallel.ep import EPComm
+            env = xdist.init()
+            El = cfg.experts // env.world
+            if gpu_plan is not None:
+                self.gpu_per_rank = ranked_pool_width(cfg.experts, env.world, gpu_plan, popularity)
+                if min(gpu_plan.values()) < cfg.experts and mailbox is None:
+                    raise ValueError('a CPU tier (a plan with fewer GPU experts than experts) needs a mailbox')
+            else:
+                self.gpu_per_rank = El if gpu_experts is None else max(1, min(El, int(gpu_experts)))
+                if self.gpu_per_rank < El and mailbox is None:
+                    raise ValueError('a CPU tier (gpu_experts < experts per rank) needs a mailbox')
+            self.ep = EPComm(H, cfg.inter, cfg.experts, cfg.top_k, decode_tokens, dev, timeout_s=ep_timeout_s,
+                             slots_per_rank=self.gpu_per_rank + cfg.shared, n_shared=cfg.shared)
+            self.ep_rank, self.ep_world = env.rank, env.world
+        for li, router, corr, shared, seed_l in pending:
+            L = self.layers[li]
+
+            def experts_fn(ids, seed_l=seed_l):
+                return formats.synthetic_experts(len(ids), H, cfg.inter, cfg.fmt, dev, seed=seed_l, std=cfg.std)
+
+            if ep:
+                L['moe'], stage = self._ep_layer(li, router, corr, shared, seed_l, engine_threads, stage)
+            elif moe_factory is None:
+                from ..cache.pool import TieredMoE
+                L['moe'] = TieredMoE(li, router, experts_fn(list(range(cfg.experts))), cfg.top_k, shared=shared,
+                                     mode=1, n_group=cfg.n_group, topk_group=cfg.topk_group, renorm=True,
+                                     scale=cfg.routed_scale, corr_bias=corr, device=dev, max_tokens=16)
+            else:
+                L['moe'] = moe_factory(li, router, corr, experts_fn, shared)
+        del stage, pending
         if ep:
             from ..parallel import dist as xdist
             torch.cuda.synchronize()
@@ -264,11 +325,24 @@ class DeepSeekV3Model:
         from ..parallel.ep import EPMoE
         cfg = self.cfg
         H, I, E = cfg.hidden, cfg.inter, cfg.experts
-        table, pools, cpu_ids = ep_layout(E, self.ep_world, self.gpu_per_rank, seed_l, stride=self.ep.spr)
-        local = empty_experts(len(pools[self.ep_rank]), H, I, cfg.fmt, self.device)
-        synthetic_experts_by_id(local, pools[self.ep_rank], seed_l, cfg.std)
+        if self.gpu_plan is not None:
+            table, pools, cpu_ids = ep_layout_ranked(E, self.ep_world, int(self.gpu_plan[li]), self.popularity[li],
+                                                     self.ep.spr, self.gpu_per_rank)
+        else:
+            table, pools, cpu_ids = ep_layout(E, self.ep_world, self.gpu_per_rank, seed_l, stride=self.ep.spr)
+        mine = pools[self.ep_rank]
+        local = empty_experts(self.gpu_per_rank, H, I, cfg.fmt, self.device)
+        if mine:
+            synthetic_experts_by_id(formats.ExpertWeights(cfg.fmt, *[getattr(local, f)[:len(mine)] for f in
+                                                                     ('w13', 'w2', 's13', 's2', 'g13', 'g2')]),
+                                    mine, seed_l, cfg.std)
+        for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):   # slots a ranked plan leaves empty on this rank
+            getattr(local, f)[len(mine):].zero_()
         engine = None
-        if cpu_ids:
+        if cpu_ids and self.cold is not None:
+            engine = self._cold_engine(li, cpu_ids, seed_l, threads)
+            self.engines.append(engine)
+        elif cpu_ids:
             from ..engine import CpuEngine
             n = len(cpu_ids)
             chunk = 16
@@ -291,6 +365,49 @@ class DeepSeekV3Model:
                     topk_group=cfg.topk_group, renorm=True, scale=cfg.routed_scale, corr_bias=corr,
                     table=table, mailbox=self.mailbox, engine=engine)
         return moe, stage
+
+    def attach_bigram(self, table):
+        """Adds a hashed-bigram NVMe embedding table (tables/engram.py; rows projected to the hidden size) to the
+        token embeddings inside the decode graph. Attach before capturing the decode step."""
+        self.bigram = table
+
+    def _cold_engine(self, li: int, cpu_ids: list, seed_l: int, threads):
+        """The CPU tier of one layer over RAM and the cold store: the first `ram_experts` of `cpu_ids` (most routed
+        first) in the engine's RAM slots, the rest read from the store on demand. Rank 0 writes the layer's records
+        (every expert, generated on the GPU in chunks); the other ranks wait for it and fill their RAM slots from the
+        records."""
+        from ..engine import CpuEngine
+        from ..parallel import dist as xdist
+        cfg = self.cfg
+        H, I, E = cfg.hidden, cfg.inter, cfg.experts
+        n_ram = len(cpu_ids) if self.ram_experts is None else max(1, min(len(cpu_ids), int(self.ram_experts)))
+        ram_ids = list(cpu_ids[:n_ram])
+        engine = CpuEngine(empty_experts(1, H, I, cfg.fmt, 'cpu'), threads=threads, slots=n_ram, resident=ram_ids,
+                           total_experts=E, fill=False)
+        nodes = engine.nodes()
+        if self.ep_rank == 0:
+            host = empty_experts(E, H, I, cfg.fmt, 'cpu')
+            chunk = 16
+            for s0 in range(0, E, chunk):
+                ids = list(range(s0, min(E, s0 + chunk)))
+                tmp = empty_experts(len(ids), H, I, cfg.fmt, self.device)
+                synthetic_experts_by_id(tmp, ids, seed_l, cfg.std)
+                for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
+                    getattr(host, f)[s0:s0 + len(ids)].copy_(getattr(tmp, f))
+                del tmp
+            self.cold.ensure_layer(li, host, nodes)
+            for s, e in enumerate(ram_ids):
+                engine.write_slot(s, host, e)
+            del host
+        xdist.barrier()
+        if self.ep_rank != 0:
+            self.cold.manifest = self.cold._load_manifest()
+            self.cold.fill_engine(engine, li, ram_ids)
+        scores = np.zeros(E, np.float32)
+        scores[ram_ids] = np.linspace(1.0, 0.5, len(ram_ids), dtype=np.float32)   # initial use counts by rank
+        from .. import config
+        self.cold.attach(engine, li, scores, config.get('XTIER_COLD_HALF_LIFE'))
+        return engine
 
     # ------------------------------------------------------------------ state
     def kernel_attention(self) -> bool:
@@ -491,6 +608,7 @@ class DeepSeekV3Model:
         e = lambda *s: torch.empty(*s, dtype=torch.bfloat16, device=dev)
         return dict(
             tokens=torch.zeros(B, dtype=torch.int64, device=dev),
+            prev=torch.zeros(B, dtype=torch.int64, device=dev),   # the previous input (hashed bigram rows)
             pos=torch.zeros(B, dtype=torch.int32, device=dev),
             rows=torch.arange(B, dtype=torch.int32, device=dev),
             slot=torch.zeros(B, dtype=torch.int64, device=dev),
@@ -525,6 +643,8 @@ class DeepSeekV3Model:
         torch.add(buf['pos'], 1, out=buf['lens'])
         torch.where(buf['ar'] < buf['lens'][:, None], buf['ar'] + buf['rowbase'], buf['minus1'], out=buf['idx'])
         torch.index_select(self.embed, 0, buf['tokens'], out=buf['residual'])
+        if self.bigram is not None:   # NVMe hashed-bigram rows, looked up inside the graph
+            self.bigram.add_decode(buf['residual'], buf['prev'], buf['tokens'])
         for li, L in enumerate(self.layers):
             if li == 0:
                 ops.add_rmsnorm(buf['residual'], None, L['in_norm'], buf['h'], cfg.eps)
@@ -551,6 +671,8 @@ class DeepSeekV3Model:
         ops.add_rmsnorm(buf['blk'], buf['residual'], self.final_norm, buf['h'], cfg.eps)
         ops.linear(buf['h'], self.lm_head, out=buf['logits'])
         torch.argmax(buf['logits'], dim=-1, out=buf['next'])
+        if self.bigram is not None:
+            buf['prev'].copy_(buf['tokens'])
         return buf['next']
 
     def check(self, st: dict | None = None):
@@ -564,6 +686,8 @@ class DeepSeekV3Model:
             self.ep.check()
         if self.mailbox is not None:
             self.mailbox.check()
+        if self.bigram is not None:
+            self.bigram.check()
 
     def close(self):
         for e in self.engines:

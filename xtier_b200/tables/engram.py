@@ -107,3 +107,40 @@ class BigramTable:
 
     def check(self):
         self.lookup.check()
+
+
+def synthetic_table(path, rows: int, dim: int, std: float = 0.02, seed: int = 0, segments: int = 1,
+                    chunk_rows: int = 65536, device=None) -> list:
+    """Writes a [rows, dim] BF16 table of N(0, std) values into `segments` files path.N, chunk by chunk (a 32 GiB
+    table never sits in memory), in the layout of `tables.write_table` (a 512-byte header gap, then the rows), and
+    returns its Segment list. The chunk starting at row r is drawn from a generator seeded by (seed, r) (on
+    `device`, default the GPU when there is one), so the table's bytes depend on its shape and seed only. A table
+    written before with the same shape, std and seed (a sidecar path.json) is reused."""
+    import json
+    import os
+    from . import Segment
+    if device is None:
+        device = 'cuda' if torch.cuda.is_available() else 'cpu'
+    meta = dict(rows=rows, dim=dim, std=std, seed=seed, segments=segments, chunk_rows=chunk_rows)
+    per = (rows + segments - 1) // segments
+    bounds = [(s * per, min(rows, (s + 1) * per)) for s in range(segments) if s * per < rows]
+    segs = [Segment(f'{path}.{s}', lo, hi - lo, 512) for s, (lo, hi) in enumerate(bounds)]
+    side = f'{path}.json'
+    try:
+        with open(side) as f:
+            same = json.load(f) == meta
+    except (OSError, ValueError):
+        same = False
+    if same and all(os.path.exists(g.path) and os.path.getsize(g.path) == 512 + g.count * dim * 2 for g in segs):
+        return segs
+    for g in segs:
+        with open(g.path, 'wb') as f:
+            f.write(b'\0' * 512)
+            for lo in range(g.first, g.first + g.count, chunk_rows):
+                hi = min(g.first + g.count, lo + chunk_rows)
+                gen = torch.Generator(device=device).manual_seed(seed * 1000003 + lo)
+                x = (torch.randn(hi - lo, dim, generator=gen, device=device) * std).bfloat16()
+                f.write(x.view(torch.uint8).cpu().numpy().tobytes())
+    with open(side, 'w') as f:
+        json.dump(meta, f)
+    return segs
