@@ -743,6 +743,27 @@ void mx_quant_rows(const Tensor &x, const std::optional<Tensor> &src, const Tens
              "mx_quant_rows");
 }
 
+// y [M, N] BF16 (+ residual) = MXFP8 x8 [Mp, K] (rows past M dropped) . MXFP8 w8 [N, K]^T, both quantized by
+// mx_quant_rows (scale atoms sfx, sfw)
+void gemm_mx8(const Tensor &x8, const Tensor &sfx, int64_t M, const Tensor &w8, const Tensor &sfw,
+              const std::optional<Tensor> &residual, const Tensor &y, const Tensor &err) {
+    for (const Tensor *t : {&x8, &sfx, &w8, &sfw, &y}) cuda_contig(*t, "gemm_mx8 operand");
+    const int64_t K = x8.size(-1), Mp = x8.numel() / K, N = w8.numel() / K;
+    check(x8.scalar_type() == at::kByte && w8.scalar_type() == at::kByte && w8.size(-1) == K && K % 128 == 0 &&
+              N % 128 == 0 && Mp % 128 == 0 && M > 0 && M <= Mp && sfx.numel() >= Mp * K / 32 &&
+              sfw.numel() >= N * K / 32,
+          "gemm_mx8: x8 [Mp, K], w8 [N, K] u8 (multiples of 128), scale atoms of both");
+    check(y.scalar_type() == at::kBFloat16 && y.numel() == M * N, "gemm_mx8: y [M, N] bf16");
+    if (residual)
+        check(residual->is_contiguous() && residual->scalar_type() == at::kBFloat16 && residual->numel() == M * N,
+              "gemm_mx8: residual [M, N] bf16");
+    check(err.is_cuda() && err.scalar_type() == at::kInt, "gemm_mx8 err int32");
+    c10::cuda::CUDAGuard g(x8.device());
+    check_rc(xt_gemm_mx8(x8.data_ptr(), sfx.data_ptr(), int(M), w8.data_ptr(), sfw.data_ptr(), int(N), int(K),
+                         residual ? residual->data_ptr() : nullptr, y.data_ptr(), ptr<int>(err), stream()),
+             "gemm_mx8");
+}
+
 void moe_grouped_mx(const Tensor &x8, const Tensor &sfx, const Tensor &codes, const Tensor &scales,
                     const Tensor &gscale, const Tensor &tiles, bool gate_up, int64_t I,
                     const std::optional<Tensor> &route_w, const Tensor &out, const Tensor &err,
@@ -871,6 +892,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("skinny_gemm(Tensor x, Tensor w, Tensor? add, Tensor(a!) y, Tensor(b!)? part, int splits, Tensor(c!) err) "
           "-> ()");
     m.def("mx_quant_rows(Tensor x, Tensor? src, Tensor(a!) x8, Tensor(b!) sfx) -> ()");
+    m.def("gemm_mx8(Tensor x8, Tensor sfx, int M, Tensor w8, Tensor sfw, Tensor? residual, Tensor(a!) y, "
+          "Tensor(b!) err) -> ()");
     m.def("pool_ring_create(int capacity) -> int", &pool_ring_create);
     m.def("pool_ring_destroy(int h) -> ()", &pool_ring_destroy);
     m.def("pool_ring_post(int h, int seq, int layer, int expert, int slot) -> int", &pool_ring_post);
@@ -943,6 +966,7 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("pool_ring_commit", &pool_ring_commit);
     m.impl("pool_ring_landed", &pool_ring_landed);
     m.impl("mx_quant_rows", &mx_quant_rows);
+    m.impl("gemm_mx8", &gemm_mx8);
     m.impl("moe_grouped_mx", &moe_grouped_mx);
     m.impl("dsa_quant_q", &dsa_quant_q);
     m.impl("silu_mul", &silu_mul);

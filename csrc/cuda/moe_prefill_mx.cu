@@ -26,6 +26,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "mx_common.cuh"
 #include "params.h"
 #include "tc_common.cuh"
 
@@ -59,48 +60,6 @@ struct MxParams {
     int out_cols;
     int *error;
 };
-
-// Shared-memory descriptor of a scale atom as the source of tcgen05.cp 32x128b: K-major, no swizzle, 8-row core
-// matrices of 16-byte rows, 128 bytes apart
-XT_DEV uint64_t sf_atom_desc(uint32_t smem_addr) {
-    uint64_t d = 0;
-    d |= uint64_t((smem_addr >> 4) & 0x3FFF);
-    d |= uint64_t(128 >> 4) << 32;   // stride byte offset: the next 8 rows
-    d |= uint64_t(1) << 46;          // version
-    return d;                        // layout type 0: no swizzle
-}
-
-// Untiled bulk copy global -> shared, completing `bytes` on `bar` (both addresses 16-byte aligned, bytes % 16 == 0)
-XT_DEV void mx_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                     tc::smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
-                 : "memory");
-}
-
-XT_DEV void sf_copy(uint32_t taddr, uint64_t desc) {
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n" ::"r"(taddr), "l"(desc) : "memory");
-}
-
-XT_DEV void mma_mx(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa, uint32_t sfb,
-                   uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
-        : "memory");
-}
-
-// Instruction descriptor of kind::mxf8f6f4 block-scaled: E4M3 A (format 0), E2M1 B (format 5), both K-major, UE8M0
-// scales, M x N, scale bytes sf_id of A and B
-__host__ __device__ constexpr uint32_t idesc_mx(int M, int N, uint32_t sf_id) {
-    return (sf_id << 4)                 // B scale factor id
-           | (5u << 10)                 // B format E2M1
-           | (uint32_t(N >> 3) << 17)   // N / 8
-           | (1u << 23)                 // scale format E8M0
-           | (uint32_t(M >> 4) << 24)   // M / 16
-           | (sf_id << 29);             // A scale factor id
-}
 
 template <bool GATE_UP>
 __global__ void __launch_bounds__(MX_THREADS, 1)
@@ -259,7 +218,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
                     const uint64_t ad = tc::sw128_kmajor_desc(sa), bd = tc::sw128_kmajor_desc(sa + MxSmem::A);
 #pragma unroll
                     for (int k = 0; k < MX_BK / 32; ++k)   // K = 32 bytes per MMA; byte k of the scale words
-                        mma_mx(d, ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc_mx(MX_BM, MX_BN, uint32_t(k)),
+                        mma_mx(d, ad + uint64_t(2 * k), bd + uint64_t(2 * k), idesc_mx(MX_BM, MX_BN, uint32_t(k), MX_FMT_E2M1),
                                sfa | (uint32_t(k) << 30), sfb | (uint32_t(k) << 30), (kb > 0 || k > 0) ? 1u : 0u);
                     tc::mma_commit(&empty[stage]);
                     if (++stage == MX_STAGES) {

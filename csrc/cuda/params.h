@@ -227,6 +227,8 @@ int xt_mla_prep(const void *in, int ld, int q_lora, const void *q_norm, const vo
                 void *lat_out, int T, cudaStream_t stream);
 int xt_head_gemm(const xt::HeadGemmParams *p, int heads, cudaStream_t stream);
 int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream);
+int xt_gemm_mx8(const void *x8, const void *sfx, int M, const void *w8, const void *sfw, int N, int K,
+                const void *residual, void *y, int *error, cudaStream_t stream);
 int xt_attn_prefill(const void *q, int64_t q_ts, int64_t q_hs, const void *k, const void *v, int64_t kv_rows,
                     int64_t kv_row0, int64_t kv_hs, int T, int start, int Hq, int Hkv, void *out, int64_t out_ts,
                     int64_t out_hs, float scale, int *error, cudaStream_t stream);

@@ -1,6 +1,6 @@
 """FP8 kernels against plain PyTorch fp32 references: Engram-style FP8 rows with E8M0 block scales (gather by id with
 a row range, and the decode of rows the graph lookup brought in), the W8A16 decode GEMV with per-row x 128-column
-scales, and the dequant + tcgen05 GEMM prefill path."""
+scales, the dequant + tcgen05 GEMM prefill path and the W8A8 (MXFP8) prefill path."""
 import numpy as np
 import pytest
 import torch
@@ -73,6 +73,23 @@ def test_linear_fp8_prefill_path(cuda_ops):
     ref = x.float() @ wf.bfloat16().float().T
     rel = float((out.cpu().float() - ref).norm() / ref.norm())
     assert rel < 1e-2, rel
+
+
+def test_linear_fp8_w8a8_prefill(cuda_ops):
+    """The W8A8 path: the FP8 weight requantized to MXFP8 once, activations quantized per call, block-scaled tcgen05
+    GEMM; within E4M3 error of the fp32 product of the BF16 activations and the FP8 weight."""
+    g = torch.Generator().manual_seed(4)
+    N, K, m = 1024, 2048, 700
+    w = _e4m3_bytes((N, K), g)
+    s = torch.rand(N, K // 128, generator=g) * 0.01 + 0.001
+    x = torch.randn(m, K, generator=g).bfloat16()
+    wf = w.view(torch.float8_e4m3fn).float() * s.repeat_interleave(128, dim=1)
+    mx8 = cuda_ops.fp8_weight_to_mx8(w.cuda(), s.cuda())
+    out = cuda_ops.linear_fp8(x.cuda(), w.cuda(), s.cuda(), mx8=mx8)
+    torch.cuda.synchronize()
+    ref = x.float() @ wf.T
+    rel = float((out.cpu().float() - ref).norm() / ref.norm())
+    assert rel < 8e-2, rel
 
 
 def test_graph_lookup_fp8_rows(cuda_ops, tmp_path):

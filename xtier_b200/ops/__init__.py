@@ -130,20 +130,71 @@ def spec_truncate(q, tokens, flags, threshold: float, topk=None):
 _FP8_SCRATCH: dict = {}
 
 
-def linear_fp8(x, w, s, out=None):
-    """x @ (w * s)^T with FP8 weights (per row x 128-column scales): the W8A16 GEMV for decode-sized inputs, else a
+def linear_fp8(x, w, s, out=None, mx8=None):
+    """x @ (w * s)^T with FP8 weights (per row x 128-column scales): the W8A16 GEMV for decode-sized inputs; larger
+    inputs through the W8A8 block-scaled GEMM when `mx8` (fp8_weight_to_mx8 of the same weight) is given (activations
+    quantized to MXFP8 per call, as the reference's W8A8 prefill quantizes them to E4M3 per 128 columns), else a
     dequant pass into a per-device scratch and the tcgen05 BF16 GEMM (prefill is compute-bound)."""
     m = x.numel() // x.shape[-1]
     K = x.shape[-1]
     if m <= 16 and K * m * 2 <= 200 * 1024:
         out = torch.empty(*x.shape[:-1], w.shape[0], dtype=torch.bfloat16, device=x.device) if out is None else out
         return gemv_fp8(x, w, s, out)
+    if mx8 is not None:
+        return linear_mx8(x, mx8, out=out)
     key = (x.device, w.numel())
     buf = _FP8_SCRATCH.get(key)
     if buf is None:
         buf = _FP8_SCRATCH[key] = torch.empty(w.numel(), dtype=torch.bfloat16, device=x.device)
     wb = fp8_dequant(w, s, buf.view(w.shape))
     return linear(x.reshape(m, K), wb, out)
+
+
+class MX8Weight:
+    """A BF16 weight [N, K] quantized once to MXFP8 for `linear_mx8`: E4M3 codes [N, K] and UE8M0 scales per 32 values
+    along K, laid out as the 512-byte scale atoms the block-scaled MMA reads (N and K multiples of 128)."""
+
+    def __init__(self, w: torch.Tensor):
+        N, K = w.shape
+        if N % 128 or K % 128:
+            raise ValueError('MX8Weight: N and K must be multiples of 128')
+        self.N, self.K = N, K
+        self.w8 = torch.empty(N, K, dtype=torch.uint8, device=w.device)
+        self.sf = torch.empty(N * K // 32, dtype=torch.uint8, device=w.device)
+        _ops().mx_quant_rows(w.to(torch.bfloat16).contiguous(), None, self.w8, self.sf)
+
+
+def fp8_weight_to_mx8(w, s) -> MX8Weight:
+    """An FP8 weight with per-row x 128-column FP32 scales as MXFP8 (dequantized to BF16, then requantized with one
+    power-of-two scale per 32 values): the operand of linear_fp8's W8A8 path."""
+    return MX8Weight(fp8_dequant(w, s, torch.empty(w.shape, dtype=torch.bfloat16, device=w.device)))
+
+
+_MX_PAD: dict = {}
+
+
+def linear_mx8(x, wq: MX8Weight, residual=None, out=None):
+    """x [..., K] BF16 . wq^T (+ residual) -> [..., N] BF16 through the block-scaled FP8 tensor cores: x quantized to
+    MXFP8 per call (E4M3, one power-of-two scale per 32 values), FP32 accumulation (csrc/cuda/gemm_mx8.cu)."""
+    K = x.shape[-1]
+    M = x.numel() // K
+    Mp = (M + 127) // 128 * 128
+    dev = x.device
+    x8 = torch.empty(Mp, K, dtype=torch.uint8, device=dev)
+    sfx = torch.empty(Mp * K // 32, dtype=torch.uint8, device=dev)
+    src = None
+    if Mp != M:   # rows past M quantize zeros
+        key = (M, Mp, dev)
+        src = _MX_PAD.get(key)
+        if src is None:
+            src = torch.cat([torch.arange(M, dtype=torch.int32), torch.full((Mp - M,), -1, dtype=torch.int32)]).to(dev)
+            if len(_MX_PAD) < 64:
+                _MX_PAD[key] = src
+    _ops().mx_quant_rows(x.reshape(M, K).contiguous(), src, x8, sfx)
+    out = torch.empty(*x.shape[:-1], wq.N, dtype=torch.bfloat16, device=dev) if out is None else out
+    _ops().gemm_mx8(x8, sfx, M, wq.w8, wq.sf, None if residual is None else residual.reshape(M, wq.N), out,
+                    gemm_error_word(dev))
+    return out
 
 
 _gemm_err: dict = {}
