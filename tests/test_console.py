@@ -70,3 +70,39 @@ def test_start_and_stop_a_server_process(tmp_path):
     assert cur['pid'] > 0 and console.status()['running']
     assert console.stop() is True
     assert not console.status()['running']
+
+
+def test_stages_and_telemetry_read_back():
+    """The server's stage, telemetry and fatal lines, as the console reads them back from the log."""
+    import io
+    from xtier_b200.console import core
+    from xtier_b200.serve import Server, Stages
+    buf = io.StringIO()
+    emit = lambda line, flush=True: buf.write(line + '\n')   # noqa: E731
+    st = Stages(emit=emit)
+    assert core.progress(buf.getvalue())['phase'] == 'boot'
+    for li in range(4):
+        st.set('weights', li, 4)
+    p = core.progress(buf.getvalue())
+    assert p['phase'] == 'weights' and p['percent'] == 8 + int(72 * 3 / 4)
+    st.set('pool')
+    st.set('graphs')
+    st.set('ready')
+    assert core.progress(buf.getvalue()) == {'phase': 'ready', 'label': 'ready', 'percent': 100}
+    assert list(st.info()['times']) == ['boot', 'weights', 'pool', 'graphs', 'ready']
+    with pytest.raises(ValueError):
+        st.set('nonsense')
+    # telemetry: rates since the last line
+    srv = Server(None)
+    srv.state.update(requests=3, tokens=250)
+    line = srv.telemetry(force=True)
+    t = core.telemetry(line)
+    assert t['requests'] == 3 and t['tokens'] == 250 and t['queue'] == 0
+    assert core.short(line).startswith('decode 3 req · 250 tok')
+    assert srv.telemetry() is None                     # rate-limited
+    # why a start died
+    st.fail('RuntimeError: no CUDA device')
+    text = buf.getvalue() + 'Traceback (most recent call last):\n  File "x"\nValueError: later noise\n'
+    assert core.why_down(text) == '[xtier_b200] FATAL: RuntimeError: no CUDA device'
+    assert core.why_down('ok\nnothing here\n') == ''
+    assert core.why_down('x\nRuntimeError: CUDA error: out of memory\n') == 'RuntimeError: CUDA error: out of memory'

@@ -5,13 +5,18 @@ A card is configs/<dir>/console.py defining MODEL = {'id', 'name', 'port', 'opti
 group (stopped with the whole group), its output goes to a log file the page tails, and readiness is polled on its
 /health endpoint. The last settings are kept in a small JSON file.
 
-Reference parity: xtier/console/core.py:372-601 (Console: start, stop, status, wait_ready).
+The page's status also carries the server's startup stage (its stage log lines), the last telemetry line (requests,
+tokens, tok/s, queue, CPU tier calls) and, once it is down, why (its FATAL line or the last error).
+
+Reference parity: xtier/console/core.py:372-601 (Console: start, stop, status, wait_ready), :294-370 (the log read back:
+loading progress, short log lines, why a server is down).
 """
 from __future__ import annotations
 
 import importlib.util
 import json
 import os
+import re
 import signal
 import subprocess
 import time
@@ -19,6 +24,69 @@ import urllib.request
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[2]
+
+# ------------------------------------------------------------------ the server log, read back
+# stage lines (serve.Stages), telemetry lines (serve.Server.telemetry), fatal lines
+_STAGE = re.compile(r'\[xtier_b200\] stage (\w+) (\d+)/(\d+)')
+_TELE = re.compile(r'\[xtier_b200\] decode (\d+) req (\d+) tok ([\d.]+) tok/s queue (\d+)(?: cpu (\d+) calls (\d+) us)?')
+_FATAL = re.compile(r'\[xtier_b200\] FATAL: [^\n]*|CUDA error[^\n]*|[A-Za-z]*Error: [^\n]*')
+_ANSI = re.compile(r'\x1b\[[0-9;]*m')
+_LABELS = {'boot': ('starting the process', 3), 'weights': ('loading weights', 8), 'pool': ('expert pools, CPU engines', 84),
+           'graphs': ('capturing the decode graph', 92), 'ready': ('ready', 100)}
+
+
+def progress(text: str) -> dict:
+    """The server's startup stage from its log: the last stage line wins; weights advance 8 -> 80 % by layer."""
+    found = _STAGE.findall(text or '')
+    if not found:
+        return {'phase': 'boot', 'label': _LABELS['boot'][0], 'percent': _LABELS['boot'][1]}
+    phase, done, total = found[-1][0], int(found[-1][1]), int(found[-1][2])
+    label, pct = _LABELS.get(phase, (phase, 0))
+    if phase == 'weights' and total:
+        pct = 8 + int(72 * done / total)
+        label = f'{label} ({done}/{total} layers)'
+    return {'phase': phase, 'label': label, 'percent': pct}
+
+
+def why_down(text: str) -> str:
+    """Why a server stopped, from its log: its own FATAL line, else the last error line (an exception's last line,
+    a CUDA error); '' when the log names none."""
+    found = _FATAL.findall(text or '')
+    if not found:
+        return ''
+    fatal = [f for f in found if f.startswith('[xtier_b200] FATAL')]
+    return (fatal[-1] if fatal else found[-1]).strip()[:300]
+
+
+def telemetry(text: str) -> dict | None:
+    """The last telemetry line of the log as numbers (requests and tokens since the line before, tok/s, queue, CPU
+    tier calls and their mean time)."""
+    found = _TELE.findall(text or '')
+    if not found:
+        return None
+    req, tok, tps, queue, calls, us = found[-1]
+    out = {'requests': int(req), 'tokens': int(tok), 'tok_s': float(tps), 'queue': int(queue)}
+    if calls:
+        out.update(cpu_calls=int(calls), cpu_us=int(us))
+    return out
+
+
+def short(line: str) -> str:
+    """A log line for the page: colour codes dropped, the server's stage and telemetry lines in short."""
+    line = _ANSI.sub('', line).rstrip()
+    m = _TELE.search(line)
+    if m:
+        req, tok, tps, queue, calls, us = m.groups()
+        out = f'decode {req} req · {tok} tok · {float(tps):.1f} tok/s'
+        if queue != '0':
+            out += f' · queue {queue}'
+        if calls:
+            out += f' · CPU tier {calls} calls, {us} us'
+        return out
+    m = _STAGE.search(line)
+    if m:
+        return f'stage {m.group(1)}' + (f' {m.group(2)}/{m.group(3)}' if m.group(3) != '0' else '')
+    return line[:240]
 
 
 def load_cards(config_dir: Path | None = None) -> dict:
@@ -119,7 +187,29 @@ class Console:
             return []
         return f.read_text(errors='replace').splitlines()[-lines:]
 
+    def _log_text(self, model: str | None = None, size: int = 262144) -> str:
+        model = model or (self.current or {}).get('model') or getattr(self, '_last_model', None)
+        if not model:
+            return ''
+        try:
+            with open(self.state_dir / f'{model}.log', 'rb') as fh:
+                fh.seek(0, os.SEEK_END)
+                fh.seek(max(0, fh.tell() - size))
+                return fh.read().decode('utf-8', 'replace')
+        except OSError:
+            return ''
+
     def status(self) -> dict:
         running = self.proc is not None and self.proc.poll() is None
-        return {'running': running, 'current': self.current, 'health': self.health() if running else None,
-                'models': {k: {kk: v for kk, v in m.items() if kk != 'build'} for k, m in self.cards.items()}}
+        if self.current:
+            self._last_model = self.current['model']
+        text = self._log_text()
+        out = {'running': running, 'current': self.current, 'health': self.health() if running else None,
+               'models': {k: {kk: v for kk, v in m.items() if kk != 'build'} for k, m in self.cards.items()}}
+        if text:
+            out['stage'] = progress(text)
+            out['telemetry'] = telemetry(text)
+            out['log'] = [short(ln) for ln in text.splitlines()[-8:] if ln.strip()]
+            if not running:
+                out['down_reason'] = why_down(text)
+        return out

@@ -32,10 +32,14 @@ async function start() {{ await post(API.start, {{model: document.getElementById
 async function stop() {{ await post(API.stop, {{}}); }}
 async function poll() {{
   const s = await (await fetch('/' + API.status)).json();
-  document.getElementById('status').textContent = s.running ?
+  let line = s.running ?
     `running ${{s.current.model}} (pid ${{s.current.pid}}) ready=${{s.health && s.health.ready}}` : 'idle';
+  if (s.running && s.stage && s.stage.phase !== 'ready') line += ` · ${{s.stage.label}} ${{s.stage.percent}} %`;
+  if (s.running && s.telemetry) line += ` · ${{s.telemetry.tok_s.toFixed(1)}} tok/s, queue ${{s.telemetry.queue}}`;
+  if (!s.running && s.down_reason) line += ` · stopped: ${{s.down_reason}}`;
+  document.getElementById('status').textContent = line;
   const j = await (await fetch('/' + API.job)).json();
-  document.getElementById('log').textContent = (j.log || []).join('\\n');
+  document.getElementById('log').textContent = (j.log || s.log || []).join('\\n');
 }}
 const sel = document.getElementById('model');
 Object.keys(MODELS).forEach(k => {{ const o = document.createElement('option'); o.value = k;

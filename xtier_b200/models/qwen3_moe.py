@@ -96,14 +96,15 @@ class Qwen3MoeModel:
     def __init__(self, cfg: Qwen3MoeConfig, device='cuda', seed: int = 0, hot_fraction: float = 1.0,
                  engine_threads: int | None = None, mailbox=None, synthetic_experts: bool = True,
                  hot_sets: list[list[int]] | None = None, peer: bool | None = None, weights=None,
-                 popularity: torch.Tensor | None = None):
+                 popularity: torch.Tensor | None = None, progress=None):
         """peer: spread the hot slots over the ranks of the process group (cache/peer.py): every rank holds the same
         model (same seed), its slot pool in symmetric memory, and reads the experts other GPUs hold over NVLink
         (None: XTIER_GPU2_SLOTS=auto / on turns it on).
         weights: a weight source (models/hf.py HFWeights: embed(), lm_head(), final_norm(), layer(li)) instead of
         random init; such a model has no router bias. popularity [layers, experts]: measured route shares (a planner
         profile) that choose the hot and RAM-resident experts when hot_sets is not given; without it the random
-        model's Zipf bias does, and a loaded model takes the lowest expert ids."""
+        model's Zipf bias does, and a loaded model takes the lowest expert ids. progress(layer, layers): called as
+        each layer starts building."""
         if peer is None:
             peer = str(config.get('XTIER_GPU2_SLOTS')).strip().lower() in ('auto', '1', 'on', 'true', 'yes')
         self.cfg = cfg
@@ -159,6 +160,8 @@ class Qwen3MoeModel:
         self.zipf_tau = (zipf_temperature(cfg.experts, cfg.top_k, cfg.zipf_s, cfg.std * H ** 0.5)
                          if weights is None else 0.0)
         for li in range(cfg.layers):
+            if progress is not None:   # e.g. the server's startup stages (layer li of cfg.layers)
+                progress(li, cfg.layers)
             n_hot = hot_counts[li]
             if weights is not None:
                 src = weights.layer(li)

@@ -51,6 +51,39 @@ class BadRequest(ValueError):
     pass
 
 
+STAGES = ('boot', 'weights', 'pool', 'graphs', 'ready')
+
+
+class Stages:
+    """Startup stages of the server with their times, printed as one log line each (the console reads the last one
+    for its progress bar) and reported by /health and /metrics: boot, weights (layer i of n), pool (expert pools,
+    CPU engines, mailbox), graphs (decode step capture), ready; `fail(reason)` records why a start died."""
+
+    def __init__(self, emit=print):
+        self.t0 = time.time()
+        self.emit = emit
+        self.phase, self.done, self.total, self.error = 'boot', 0, 0, None
+        self.times = {'boot': 0.0}
+
+    def set(self, phase: str, done: int = 0, total: int = 0):
+        if phase not in STAGES:
+            raise ValueError(f'unknown stage {phase!r}')
+        first = phase != self.phase
+        self.phase, self.done, self.total = phase, done, total
+        if first:
+            self.times[phase] = round(time.time() - self.t0, 3)
+        if first or total:
+            self.emit(f'[xtier_b200] stage {phase} {done}/{total} {time.time() - self.t0:.1f}s', flush=True)
+
+    def fail(self, reason: str):
+        self.error = str(reason)[:300]
+        self.emit(f'[xtier_b200] FATAL: {self.error}', flush=True)
+
+    def info(self) -> dict:
+        return {'phase': self.phase, 'done': self.done, 'total': self.total, 'times': dict(self.times),
+                'error': self.error}
+
+
 class GenBackend:
     """The model and its decode runner behind the server: prefill a prompt, decode one token, score a text."""
 
@@ -203,10 +236,31 @@ class Server:
         self.waiting = 0
         self.state = {'ready': backend is not None, 'requests': 0, 'tokens': 0, 'aborted': 0, 'rejected': 0,
                       'prompt_tokens': 0}
+        self.stages = Stages()
+        self._tele = (time.time(), 0, 0)   # (time, requests, tokens) of the last telemetry line
 
     def set_backend(self, backend):
         self.backend = backend
         self.state['ready'] = True
+        self.stages.set('ready')
+
+    def telemetry(self, every_s: float = 5.0, force: bool = False):
+        """One log line with the counters' rates since the last line (at most one per `every_s`)."""
+        now = time.time()
+        t, r, n = self._tele
+        if not force and now - t < every_s:
+            return None
+        dt = max(now - t, 1e-9)
+        line = (f'[xtier_b200] decode {self.state["requests"] - r} req {self.state["tokens"] - n} tok '
+                f'{(self.state["tokens"] - n) / dt:.1f} tok/s queue {self.waiting}')
+        be = self.backend
+        mb = getattr(be, 'mailbox', None)
+        if mb is not None:
+            st = mb.stats()
+            line += f' cpu {st.get("calls", 0):.0f} calls {st.get("mean_us", 0) or 0:.0f} us'
+        self._tele = (now, self.state['requests'], self.state['tokens'])
+        print(line, flush=True)
+        return line
 
     # ------------------------------------------------------------------ validation
     def _ids(self, req: dict) -> list[int]:
@@ -353,6 +407,7 @@ class Server:
             self.state['requests'] += 1
             self.state['tokens'] += len(out)
             self.state['prompt_tokens'] += len(ids)
+            self.telemetry()
             if aborted:
                 self.state['aborted'] += 1
         dec = t_last - t_first
@@ -547,6 +602,7 @@ class BatchServer(Server):
             self.state['requests'] += 1
             self.state['tokens'] += len(out)
             self.state['prompt_tokens'] += len(ids)
+            self.telemetry()
             self.state['aborted'] += int(req.aborted)
         dec = times[-1] - times[0] if len(times) > 1 else 0.0
         res = {'ids': out, 'prompt_tokens': len(ids), 'completion_tokens': len(out),
@@ -702,7 +758,7 @@ def make_handler(server: Server):
                                                                     'owned_by': 'xtier-b200'}]})
             if self.path == '/health':
                 be = server.backend
-                info = {'ready': server.state['ready']}
+                info = {'ready': server.state['ready'], 'stage': server.stages.info()}
                 if be is not None and server.state['ready']:
                     info.update(vocab=be.vocab, max_len=be.max_len, tokenizer=getattr(be, 'tokenizer', None) is not None)
                 return self._json(200, info)
@@ -712,6 +768,7 @@ def make_handler(server: Server):
                 snap = be.snapshot(server.state) if be is not None and hasattr(be, 'snapshot') else {}
                 snap.update({k: server.state[k] for k in ('requests', 'tokens', 'aborted', 'rejected',
                                                           'prompt_tokens')})
+                snap['startup_s'] = server.stages.times
                 if self.path == '/metrics':
                     return self._json(200, snap)
                 return self._send(200, prometheus_text(snap).encode(), 'text/plain; version=0.0.4')
@@ -797,16 +854,19 @@ def make_handler(server: Server):
     return Handler
 
 
-def build(args):
+def build(args, stages: Stages | None = None):
     from .engine.mailbox import Mailbox
     from .models.qwen3_moe import Qwen3MoeConfig, Qwen3MoeModel
     from .runtime.decode import Generator
+    stages = stages or Stages(emit=lambda *a, **k: None)
+    progress = lambda li, n: stages.set('weights', li, n)   # noqa: E731
     tok = None
     if args.checkpoint:
         from .models.hf import HFWeights
         cfg = HFWeights(args.checkpoint).cfg
         mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
-        model = Qwen3MoeModel.from_pretrained(args.checkpoint, device='cuda', hot_fraction=args.hot, mailbox=mailbox)
+        model = Qwen3MoeModel.from_pretrained(args.checkpoint, device='cuda', hot_fraction=args.hot, mailbox=mailbox,
+                                              progress=progress)
         try:
             from transformers import AutoTokenizer
             tok = AutoTokenizer.from_pretrained(args.tokenizer or args.checkpoint)
@@ -815,7 +875,9 @@ def build(args):
     else:
         cfg = Qwen3MoeConfig(layers=args.layers)
         mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
-        model = Qwen3MoeModel(cfg, device='cuda', seed=args.seed, hot_fraction=args.hot, mailbox=mailbox)
+        model = Qwen3MoeModel(cfg, device='cuda', seed=args.seed, hot_fraction=args.hot, mailbox=mailbox,
+                              progress=progress)
+    stages.set('pool')
     if mailbox is not None:
         mailbox.start()
     if args.recall:
@@ -826,6 +888,7 @@ def build(args):
                             budget_ids=int(args.recall_gib * (1 << 28)))
         eng = recall.RecallEngine(rec, gamma=args.recall_gamma)
         return SpecBackend(model, eng, max_len=args.max_len, tokenizer=tok, mailbox=mailbox)
+    stages.set('graphs')
     if args.batch > 1:
         be = BatchBackend(model, Generator(model, batch=args.batch, max_len=args.max_len), tok, mailbox)
         be.capture()
@@ -869,7 +932,12 @@ def main(argv=None):
     server = (BatchServer if args.batch > 1 else Server)(None, args.max_queue)
     serve(server, args.host, args.port)
     print(f'[xtier_b200] loading {args.checkpoint or args.model} ...', flush=True)
-    server.set_backend(build(args))
+    server.stages.set('boot')
+    try:
+        server.set_backend(build(args, server.stages))
+    except Exception as e:   # noqa: BLE001 -- the console shows why the start died
+        server.stages.fail(f'{type(e).__name__}: {e}')
+        raise
     print(f'[xtier_b200] ready on http://{args.host}:{args.port}', flush=True)
     try:
         threading.Event().wait()
