@@ -53,6 +53,52 @@ def test_dedup_budget_and_free_space(tmp_path):
     full.close()
 
 
+def test_heat_eviction_keeps_landed_copies():
+    """A segment whose copies the target accepted is promoted to the hot zone and outlives the FIFO eviction of its
+    chunk; with FIFO eviction alone it goes with the chunk. A full hot zone drops its coldest entry."""
+    a = _text(3000, 21)
+    results = {}
+    for mode in ('heat', 'fifo'):
+        r = recall.Record(budget_ids=2 * recall.CHUNK_IDS, evict=mode, hot_frac=0.25, promote=8)
+        r.add(a)
+        m = r.lookup(a[1000:1040])
+        assert m is not None and m[1] < recall.HOT_FLAG
+        r.credit(m[1], 12)                               # 12 copied ids landed from segment m[1] // 256
+        for s in range(4):                                # enough new text to evict a's chunk
+            r.add(_text(700_000, 30 + s))
+        assert r.evicted > 0
+        results[mode] = (r.lookup(a[1030:1070]), r)   # inside the promoted stretch [1008, 1344)
+    m, r = results['heat']
+    assert m is not None and m[1] >= recall.HOT_FLAG and m[0] == 40
+    assert r.continuation(m[1], 8).tolist() == a[1070:1078]
+    st = r.stats()
+    assert st['promoted'] == 1 and st['hot_entries'] == 1 and st['hot_ids'] <= r.hot_cap
+    assert results['fifo'][0] is None and results['fifo'][1].stats()['hot_entries'] == 0
+    # hot-zone capacity: promotions beyond it drop the coldest entries
+    small = recall.Record(budget_ids=recall.CHUNK_IDS, hot_frac=0.0004, promote=4)   # room for one entry
+    b = _text(5000, 40)
+    small.add(b)
+    for i, seg in enumerate((2, 6, 10)):
+        small.credit(seg * recall.HEAT_SEG + 30, 5 + i)   # later segments hotter
+    st = small.stats()
+    assert st['promoted'] == 3 and st['hot_dropped'] == 2 and st['hot_entries'] == 1
+    assert next(iter(small.hot.values())).seg == 10
+    small.credit(2 * recall.HEAT_SEG + 30, 1)            # colder than the entry held: not promoted again
+    assert small.stats()['promoted'] == 3
+
+
+def test_engine_feedback_credits_the_record():
+    r = recall.Record(promote=4)
+    a = _text(600, 22)
+    r.add(a)
+    eng = recall.RecallEngine(r, gamma=8, min_n=0.0)
+    eng.begin_stream(1, a[:300])
+    p = eng.propose(1)
+    assert p is not None and p.source == 'record' and p.ids == a[300:308] and p.pos >= 0
+    eng.feedback(1, 6)
+    assert r.stats()['heat_segments'] >= 1 and r.stats()['promoted'] == 1
+
+
 def test_disk_record_persistence_identity_and_lock(tmp_path):
     d = tmp_path / 'rec'
     ident = {'tokenizer': 'T', 'vocab': 5000, 'digest': 'x'}

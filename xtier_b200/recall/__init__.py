@@ -21,14 +21,15 @@ fell below the bar is only probed, rarer after every probe that misses.
 
 (Reference parity: xtier/packs/deepseek_v4/recall/core.py -- RecallRecord (ids-only chunk files, identity, lock,
 dedup of repeated runs, FIFO budget, min free space, read-only refresh) and RecallEngine (own context first, match tiers,
-cooldown after a miss, probes) and the proposal broadcast to the tensor-parallel ranks (`sync_proposal`). The index
-layout, hash and expectation rule here are this project's own. Not built:
-the heat-ordered eviction with its hot zone, the prompt-hash reply store, the GPU-resident id store and tree drafts.)
+cooldown after a miss, probes, the heat-ordered eviction with its hot zone) and the proposal broadcast to the
+tensor-parallel ranks (`sync_proposal`). The index layout, hash, expectation rule and heat bookkeeping here are this
+project's own. Not built: the prompt-hash reply store, the GPU-resident id store and tree drafts.)
 """
 from __future__ import annotations
 
 import dataclasses
 import json
+import math
 import os
 import shutil
 from pathlib import Path
@@ -42,6 +43,9 @@ DEDUP_RUN = 128
 OVERLAP = 32
 MAX_BACK = 128
 MAX_RUNS = 8            # sorted index runs per chunk before they are merged
+HEAT_SEG = 256          # heat eviction: the record's segments by global position
+HOT_PRE, HOT_POST = WINDOW, 64   # ids a promoted segment takes along before and after it
+HOT_FLAG = 1 << 62      # positions at or above it name a hot-zone entry: HOT_FLAG + (uid << 20) + offset
 _P = np.uint64(0x100000001B3)          # odd multiplier of the polynomial window hash
 _M1 = np.uint64(0xBF58476D1CE4E5B9)    # SplitMix64 finalizer constants
 _M2 = np.uint64(0x94D049BB133111EB)
@@ -120,14 +124,55 @@ class _Chunk:
         return found
 
 
+class _HotEntry:
+    """A promoted stretch of the record: its ids, their sorted window index and its heat (log domain)."""
+
+    def __init__(self, uid: int, ids: np.ndarray, heat: float, seg: int):
+        self.uid, self.ids, self.heat, self.seg = uid, ids, heat, seg
+        h, off = window_hashes(ids)
+        order = np.argsort(h, kind='stable')
+        self.h, self.off = h[order], off[order]
+
+    def find(self, h: int) -> list[int]:
+        key = np.uint64(h)
+        i = int(np.searchsorted(self.h, key))
+        out = []
+        while i < self.h.shape[0] and self.h[i] == key:
+            out.append(int(self.off[i]))
+            i += 1
+        return out
+
+
 class Record:
-    """Token ids with a 16-id window index; `path` None keeps everything in memory."""
+    """Token ids with a 16-id window index; `path` None keeps everything in memory.
+
+    Eviction (`evict`): 'fifo' drops the oldest chunk past the id budget. 'heat' (default) also keeps a decayed heat
+    per 256-id segment of the record -- the copied tokens the target accepted from it, halving every
+    `heat_halflife_ids` ids added -- and copies a segment whose heat reaches `promote` (with 16 ids before it and 64
+    after) into a hot zone of `hot_frac` of the budget, which the chunks' FIFO eviction does not touch; a full hot zone
+    drops its coldest entry first. Lookups search the chunks and the hot zone (the longer match wins, the hot one on
+    ties). The hot zone lives in memory: after a restart it fills again as copies land."""
 
     def __init__(self, path=None, identity: dict | None = None, budget_ids: int = 1 << 24, min_free_gib: float = 1.0,
-                 dedup: bool = True):
+                 dedup: bool = True, evict: str = 'heat', hot_frac: float = 0.25,
+                 heat_halflife_ids: float | None = None, promote: float = 24.0):
         self.path = Path(path) if path is not None else None
         self.identity = identity or {}
         self.budget_ids = max(CHUNK_IDS, int(budget_ids))
+        if evict not in ('heat', 'fifo'):
+            raise ValueError(f'evict must be heat or fifo, not {evict!r}')
+        self.evict_mode = evict
+        self.hot_cap = int(self.budget_ids * min(0.9, max(0.0, hot_frac))) if evict == 'heat' else 0
+        self.cold_budget = max(CHUNK_IDS, self.budget_ids - self.hot_cap)
+        self.halflife = float(heat_halflife_ids or max(1, self.cold_budget // 4))
+        self.promote_at = float(promote)
+        self.clock = 0.0           # ids added so far (the heat's time axis)
+        self.heat: dict[int, float] = {}   # segment -> log2(score) + clock / halflife
+        self.hot: dict[int, _HotEntry] = {}
+        self.hot_segs: set[int] = set()
+        self.hot_ids = 0
+        self._uid = 0
+        self.promoted = self.hot_dropped = 0
         self.min_free_gib = min_free_gib
         self.dedup = dedup
         self.chunks: list[_Chunk] = []
@@ -242,11 +287,64 @@ class Record:
             seg = seg[k:]
 
     def _evict(self):
-        while len(self.chunks) > 1 and self.size > self.budget_ids:
+        while len(self.chunks) > 1 and self.size > self.cold_budget:
             c = self.chunks.pop(0)
             self.evicted += c.n
             if self.path is not None:
                 self._chunk_file(c.seq).unlink(missing_ok=True)
+        if self.heat and self.chunks:   # the heat of segments no longer held
+            first = self.chunks[0].base // HEAT_SEG
+            for seg in [g for g in self.heat if g < first]:
+                del self.heat[seg]
+
+    # ------------------------------------------------------------------ heat
+    def _score(self, L: float) -> float:
+        """A log-domain heat as the decayed score now."""
+        return 2.0 ** (L - self.clock / self.halflife)
+
+    def _bump(self, L: float | None, x: float) -> float:
+        now = self.clock / self.halflife
+        score = (2.0 ** (L - now) if L is not None else 0.0) + x
+        return math.log2(max(score, 1e-30)) + now
+
+    def credit(self, pos: int, n: int):
+        """The target accepted `n` copied tokens read from position `pos` (a record or hot-zone position)."""
+        if self.evict_mode != 'heat' or n <= 0:
+            return
+        if pos >= HOT_FLAG:
+            e = self.hot.get((pos - HOT_FLAG) >> 20)
+            if e is not None:
+                e.heat = self._bump(e.heat, n)
+            return
+        for seg in range(pos // HEAT_SEG, (pos + n - 1) // HEAT_SEG + 1):
+            lo, hi = max(pos, seg * HEAT_SEG), min(pos + n, (seg + 1) * HEAT_SEG)
+            self.heat[seg] = self._bump(self.heat.get(seg), hi - lo)
+            if seg not in self.hot_segs and self._score(self.heat[seg]) >= self.promote_at:
+                self._promote(seg)
+
+    def _promote(self, seg: int):
+        if not self.chunks:
+            return
+        g_lo, g_hi = self.chunks[0].base, self.chunks[-1].base + self.chunks[-1].n
+        g0, g1 = max(g_lo, seg * HEAT_SEG - HOT_PRE), min(g_hi, (seg + 1) * HEAT_SEG + HOT_POST)
+        ids = self._ids(g0, g1) if g0 < g1 else None
+        if ids is None or ids.shape[0] < WINDOW or ids.shape[0] > self.hot_cap:
+            return
+        L = self.heat[seg]
+        while self.hot_ids + ids.shape[0] > self.hot_cap:   # the coldest entries make room, if colder than this one
+            cold = min(self.hot.values(), key=lambda e: e.heat)
+            if cold.heat >= L:
+                return
+            del self.hot[cold.uid]
+            self.hot_segs.discard(cold.seg)
+            self.hot_ids -= cold.ids.shape[0]
+            self.hot_dropped += 1
+        self._uid += 1
+        e = _HotEntry(self._uid, np.array(ids, np.int32), L, seg)
+        self.hot[e.uid] = e
+        self.hot_segs.add(seg)
+        self.hot_ids += e.ids.shape[0]
+        self.promoted += 1
 
     def add(self, ids) -> int:
         """Adds a text; returns the ids stored (0 when read-only, short of disk space, or all already held)."""
@@ -273,6 +371,7 @@ class Record:
                 stored += j - i
             i = j
         self.added += stored
+        self.clock += stored
         self.skipped += int(skip.sum())
         self._evict()
         return stored
@@ -317,10 +416,30 @@ class Record:
                 m = WINDOW + back
                 if best is None or m > best[0]:
                     best = (m, p + WINDOW)
+        for e in self.hot.values():   # the hot zone: the longer match wins, the hot one on ties
+            for o in e.find(int(h[0])):
+                if not np.array_equal(e.ids[o:o + WINDOW], t[-WINDOW:]):
+                    continue
+                lim = min(max_back, t.shape[0] - WINDOW, o)
+                back = 0
+                if lim > 0:
+                    eq = e.ids[o - lim:o][::-1] == t[-WINDOW - lim:-WINDOW][::-1]
+                    back = int(np.argmin(eq)) if not eq.all() else lim
+                m = WINDOW + back
+                if best is None or m >= best[0]:
+                    best = (m, HOT_FLAG + (e.uid << 20) + o + WINDOW)
         return best
 
     def continuation(self, pos: int, n: int) -> np.ndarray:
-        """Up to n ids from global position `pos`, stopping at a separator."""
+        """Up to n ids from global position `pos` (or a hot-zone position), stopping at a separator."""
+        if pos >= HOT_FLAG:
+            e = self.hot.get((pos - HOT_FLAG) >> 20)
+            if e is None:
+                return np.zeros(0, np.int32)
+            o = (pos - HOT_FLAG) & ((1 << 20) - 1)
+            ids = e.ids[o:o + n]
+            stop = np.nonzero(ids == SENTINEL)[0]
+            return ids[:stop[0]] if stop.shape[0] else ids
         ids = self._ids(pos, pos + n)
         if ids is None:
             for k in range(n - 1, 0, -1):
@@ -334,7 +453,9 @@ class Record:
 
     def stats(self) -> dict:
         return dict(ids=self.size, chunks=len(self.chunks), added=self.added, skipped=self.skipped,
-                    evicted=self.evicted, writer=self.writer)
+                    evicted=self.evicted, writer=self.writer, evict=self.evict_mode, hot_entries=len(self.hot),
+                    hot_ids=self.hot_ids, promoted=self.promoted, hot_dropped=self.hot_dropped,
+                    heat_segments=len(self.heat))
 
     def clear(self):
         if not self.writer:
@@ -343,6 +464,7 @@ class Record:
             if self.path is not None:
                 self._chunk_file(c.seq).unlink(missing_ok=True)
         self.chunks = []
+        self.heat, self.hot, self.hot_segs, self.hot_ids = {}, {}, set(), 0
 
     def close(self):
         if self._lock is not None:
@@ -361,6 +483,7 @@ class Proposal:
     match: int
     tier: int
     probe: bool = False
+    pos: int = -1        # record position of the copy (heat credit)
 
 
 class _Stream:
@@ -432,7 +555,7 @@ class RecallEngine:
         if m is None:
             return None
         cont = self.record.continuation(m[1], self.gamma)
-        return (m[0], cont) if cont.shape[0] else None
+        return (m[0], cont, m[1]) if cont.shape[0] else None
 
     def propose(self, rid) -> Proposal | None:
         st = self.streams[rid]
@@ -446,7 +569,8 @@ class RecallEngine:
         if not cands:
             return None
         cands.sort(key=lambda c: (c[0], c[1]), reverse=True)    # best expectation, own context on ties
-        e, _, src, (match, cont) = cands[0]
+        e, _, src, cand = cands[0]
+        match, cont = cand[0], cand[1]
         bar = max(self.min_n, st.own_yield)
         probe = False
         if e < bar:                    # below the bar: only a probe now and then
@@ -455,7 +579,8 @@ class RecallEngine:
                 return None
             probe = True
             self.probe_left[src] = self.probe_iv[src]
-        p = Proposal(src, [int(t) for t in cont], match, tier_of(match), probe)
+        p = Proposal(src, [int(t) for t in cont], match, tier_of(match), probe,
+                     cand[2] if src == 'record' else -1)
         st.last = p
         self.offers += 1
         self.probes += probe
@@ -474,6 +599,8 @@ class RecallEngine:
         s[0] += landed
         s[1] += 1
         self.landed += landed
+        if p.source == 'record' and p.pos >= 0 and self.record is not None:
+            self.record.credit(p.pos, landed)
         if landed == 0:
             st.cooldown = self.cooldown
         if p.probe:
