@@ -764,6 +764,64 @@ void gemm_mx8(const Tensor &x8, const Tensor &sfx, int64_t M, const Tensor &w8, 
              "gemm_mx8");
 }
 
+// DeepSeek V4 mHC post-mix: x [M, H], res [M, 4, H] BF16, post [M, 4], comb [M, 4, 4] FP32 -> out [M, 4, H] BF16
+void mhc_post(const Tensor &x, const Tensor &res, const Tensor &post, const Tensor &comb, const Tensor &out) {
+    for (const Tensor *t : {&x, &res, &post, &comb, &out}) cuda_contig(*t, "mhc_post operand");
+    const int64_t M = x.size(0), H = x.size(1);
+    check(x.dim() == 2 && x.scalar_type() == at::kBFloat16 && res.scalar_type() == at::kBFloat16 &&
+              res.numel() == M * 4 * H && out.scalar_type() == at::kBFloat16 && out.numel() == M * 4 * H &&
+              post.scalar_type() == at::kFloat && post.numel() == M * 4 && comb.scalar_type() == at::kFloat &&
+              comb.numel() == M * 16 && H % 8 == 0,
+          "mhc_post: x [M, H], res / out [M, 4, H] bf16, post [M, 4], comb [M, 4, 4] f32, H % 8 == 0");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_mhc_post(x.data_ptr(), res.data_ptr(), ptr<float>(post), ptr<float>(comb), out.data_ptr(), int(M),
+                         int(H), stream()),
+             "mhc_post");
+}
+
+// DeepSeek V4 wo_a: o [T, G, D] BF16 view (unit stride along D) x W [G, R, D] (FP8 as uint8 with scale
+// [G R / 32, D / 32] FP32, or BF16) -> out [T, G, R] BF16 view
+void wo_a(const Tensor &o, const Tensor &w, const std::optional<Tensor> &scale, const Tensor &out) {
+    check(o.is_cuda() && o.dim() == 3 && o.scalar_type() == at::kBFloat16 && o.stride(2) == 1,
+          "wo_a: o [T, G, D] bf16 (unit stride along D)");
+    cuda_contig(w, "w");
+    const int64_t T = o.size(0), G = o.size(1), D = o.size(2);
+    check(w.dim() == 3 && w.size(0) == G && w.size(2) == D, "wo_a: w [G, R, D]");
+    const int64_t R = w.size(1);
+    const bool fp8 = w.scalar_type() == at::kByte;
+    check(fp8 || w.scalar_type() == at::kBFloat16, "wo_a: w uint8 (E4M3) or bf16");
+    if (fp8) {
+        check(scale && scale->is_cuda() && scale->scalar_type() == at::kFloat && scale->dim() == 2 &&
+                  scale->size(0) == G * R / 32 && scale->size(1) == D / 32 && scale->stride(1) == 1,
+              "wo_a: FP8 w needs scale [G R / 32, D / 32] f32");
+    }
+    check(out.is_cuda() && out.dim() == 3 && out.scalar_type() == at::kBFloat16 && out.size(0) == T &&
+              out.size(1) == G && out.size(2) == R && out.stride(2) == 1,
+          "wo_a: out [T, G, R] bf16 (unit stride along R)");
+    c10::cuda::CUDAGuard g(o.device());
+    check_rc(xt_wo_a(o.data_ptr(), o.stride(0), o.stride(1), fp8 ? w.data_ptr() : nullptr, fp8 ? nullptr : w.data_ptr(),
+                     fp8 ? ptr<float>(*scale) : nullptr, fp8 ? int(scale->stride(0)) : 0, out.data_ptr(),
+                     out.stride(0), out.stride(1), int(T), int(G), int(R), int(D), stream()),
+             "wo_a");
+}
+
+// Qwen4-exp hyper-connection mix: x [rows, hc * hs], w_down [L, hc * hs], w_up [hc * hs, L] BF16 -> out [rows, hs];
+// acc: FP32 workspace >= 16 * L
+void hc_mix(const Tensor &x, const Tensor &wd, const Tensor &wu, const Tensor &acc, const Tensor &out, int64_t hc) {
+    for (const Tensor *t : {&x, &wd, &wu, &acc, &out}) cuda_contig(*t, "hc_mix operand");
+    const int64_t rows = x.size(0), K = x.size(1), L = wd.size(0);
+    check(hc > 0 && K % hc == 0, "hc_mix: x [rows, hc * hs]");
+    const int64_t hs = K / hc;
+    check(x.scalar_type() == at::kBFloat16 && wd.scalar_type() == at::kBFloat16 && wu.scalar_type() == at::kBFloat16 &&
+              wd.size(1) == K && wu.size(0) == K && wu.size(1) == L && acc.scalar_type() == at::kFloat &&
+              acc.numel() >= 16 * L && out.scalar_type() == at::kBFloat16 && out.numel() == rows * hs,
+          "hc_mix: shapes / dtypes");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_hc_mix(x.data_ptr(), wd.data_ptr(), wu.data_ptr(), ptr<float>(acc), out.data_ptr(), int(rows), int(hc),
+                       int(hs), int(L), stream()),
+             "hc_mix");
+}
+
 void moe_grouped_mx(const Tensor &x8, const Tensor &sfx, const Tensor &codes, const Tensor &scales,
                     const Tensor &gscale, const Tensor &tiles, bool gate_up, int64_t I,
                     const std::optional<Tensor> &route_w, const Tensor &out, const Tensor &err,
@@ -892,6 +950,9 @@ TORCH_LIBRARY(xtier, m) {
     m.def("skinny_gemm(Tensor x, Tensor w, Tensor? add, Tensor(a!) y, Tensor(b!)? part, int splits, Tensor(c!) err) "
           "-> ()");
     m.def("mx_quant_rows(Tensor x, Tensor? src, Tensor(a!) x8, Tensor(b!) sfx) -> ()");
+    m.def("mhc_post(Tensor x, Tensor res, Tensor post, Tensor comb, Tensor(a!) out) -> ()");
+    m.def("wo_a(Tensor o, Tensor w, Tensor? scale, Tensor(a!) out) -> ()");
+    m.def("hc_mix(Tensor x, Tensor wd, Tensor wu, Tensor(a!) acc, Tensor(b!) out, int hc) -> ()");
     m.def("gemm_mx8(Tensor x8, Tensor sfx, int M, Tensor w8, Tensor sfw, Tensor? residual, Tensor(a!) y, "
           "Tensor(b!) err) -> ()");
     m.def("pool_ring_create(int capacity) -> int", &pool_ring_create);
@@ -966,6 +1027,9 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("pool_ring_commit", &pool_ring_commit);
     m.impl("pool_ring_landed", &pool_ring_landed);
     m.impl("mx_quant_rows", &mx_quant_rows);
+    m.impl("mhc_post", &mhc_post);
+    m.impl("wo_a", &wo_a);
+    m.impl("hc_mix", &hc_mix);
     m.impl("gemm_mx8", &gemm_mx8);
     m.impl("moe_grouped_mx", &moe_grouped_mx);
     m.impl("dsa_quant_q", &dsa_quant_q);

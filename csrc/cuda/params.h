@@ -227,6 +227,12 @@ int xt_mla_prep(const void *in, int ld, int q_lora, const void *q_norm, const vo
                 void *lat_out, int T, cudaStream_t stream);
 int xt_head_gemm(const xt::HeadGemmParams *p, int heads, cudaStream_t stream);
 int xt_silu_mul(const void *in, void *out, int T, int I, cudaStream_t stream);
+int xt_mhc_post(const void *x, const void *res, const float *post, const float *comb, void *out, int M, int H,
+                cudaStream_t stream);
+int xt_wo_a(const void *o, int64_t o_st, int64_t o_sg, const void *w8, const void *wb, const float *scale,
+            int s_stride, void *out, int64_t out_st, int64_t out_sg, int T, int G, int R, int D, cudaStream_t stream);
+int xt_hc_mix(const void *x, const void *wd, const void *wu, float *acc, void *out, int rows, int hc, int hs, int L,
+              cudaStream_t stream);
 int xt_gemm_mx8(const void *x8, const void *sfx, int M, const void *w8, const void *sfw, int N, int K,
                 const void *residual, void *y, int *error, cudaStream_t stream);
 int xt_attn_prefill(const void *q, int64_t q_ts, int64_t q_hs, const void *k, const void *v, int64_t kv_rows,

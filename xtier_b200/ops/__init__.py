@@ -197,6 +197,44 @@ def linear_mx8(x, wq: MX8Weight, residual=None, out=None):
     return out
 
 
+# ------------------------------------------------------------------ model-pack ops (csrc/cuda/packs.cu)
+def mhc_post(x, res, post, comb, out=None):
+    """DeepSeek V4 manifold hyper-connection post-mix: out[m, i] = BF16(post[m, i] x[m] + sum_j comb[m, j, i] res[m, j])
+    summed in the fixed order ((j0 + j1) + j2) + j3 without fused multiply-adds (bit-identical to PyTorch's FP32
+    evaluation of that expression). x [M, H], res [M, 4, H] BF16; post [M, 4], comb [M, 4, 4] FP32."""
+    out = torch.empty_like(res) if out is None else out
+    _ops().mhc_post(x.contiguous(), res.contiguous(), post.float().contiguous(), comb.float().contiguous(), out)
+    return out
+
+
+def wo_a(o, w, scale=None, out=None):
+    """DeepSeek V4 grouped low-rank output projection at decode sizes: out[t, g, r] = sum_h o[t, g, h] w[g, r, h], with
+    w FP8 E4M3 (uint8 bytes or float8_e4m3fn) and FP32 scales per 32 x 32 block of [G R, D], or w BF16."""
+    if w.dtype == torch.float8_e4m3fn:
+        w = w.view(torch.uint8)
+    T, G = o.shape[0], o.shape[1]
+    out = torch.empty(T, G, w.shape[1], dtype=torch.bfloat16, device=o.device) if out is None else out
+    _ops().wo_a(o, w, None if scale is None else scale.float(), out)
+    return out
+
+
+_HC_ACC: dict = {}
+
+
+def hc_mix(x, w_down, w_up, hc: int, out=None):
+    """Qwen4-exp hyper-connection low-rank mix: acc = x . w_down^T, t = BF16(silu(acc / hc)), gate = sigmoid(t . w_up^T)
+    [rows, hc, hs], out[m, j] = sum_g gate[m, g, j] x[m, g hs + j] / hc. x [rows, hc hs] BF16 -> out [rows, hs]."""
+    rows, K = x.shape
+    L = w_down.shape[0]
+    key = (x.device, L)
+    acc = _HC_ACC.get(key)
+    if acc is None:
+        acc = _HC_ACC[key] = torch.empty(16 * L, dtype=torch.float32, device=x.device)
+    out = torch.empty(rows, K // hc, dtype=torch.bfloat16, device=x.device) if out is None else out
+    _ops().hc_mix(x.contiguous(), w_down.contiguous(), w_up.contiguous(), acc, out, hc)
+    return out
+
+
 _gemm_err: dict = {}
 
 
