@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
                         const __grid_constant__ CUtensorMap tma_v, int T, int start, int Hq, int group, int kv_row0,
                         int kv_hs, float scale_log2, __nv_bfloat16 *__restrict__ out, int64_t out_ts, int64_t out_hs,
-                        int *error) {
+                        const unsigned long long *__restrict__ tree, int *error) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *qs = smem;                         // [2 tiles][2 panels][128 x 64]
@@ -319,6 +319,9 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
         const int nk = t ? nk1 : nk0;
         const int qmin = start + q0 + t * AP_BM;   // position of the tile's first row
         const int qpos = qmin + row;
+        // tree drafts: row r sees the keys before `start` and the tree keys (slots start + i) whose bit i is set
+        const int trow = q0 + t * AP_BM + row;
+        const unsigned long long tmask = tree != nullptr && trow < T ? tree[trow] : 0ull;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nk && ok; ++j) {
@@ -326,7 +329,15 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
             tc::tc_fence_after();
             float sv[AP_BN];
             ap_ld128(st, sv);
-            if (AP_BN * j + AP_BN - 1 > qmin) {   // the tile crosses the diagonal: keys after the row's position
+            if (tree != nullptr) {
+                if (AP_BN * j + AP_BN - 1 >= start) {
+#pragma unroll
+                    for (int i = 0; i < AP_BN; ++i) {
+                        const int kk = AP_BN * j + i - start;
+                        if (kk >= 0 && (kk >= 64 || !((tmask >> kk) & 1ull))) sv[i] = -INFINITY;
+                    }
+                }
+            } else if (AP_BN * j + AP_BN - 1 > qmin) {   // the tile crosses the diagonal: keys after the row's position
 #pragma unroll
                 for (int i = 0; i < AP_BN; ++i)
                     if (AP_BN * j + i > qpos) sv[i] = -INFINITY;
@@ -484,11 +495,15 @@ extern "C" {
 // q: [T, Hq, 128] view (unit stride along d, element strides q_ts, q_hs; multiples of 8). k, v: the cache as
 // [kv_rows, 128] contiguous rows; key `key` of kv head g is row kv_row0 + g * kv_hs + key (a [B, Hkv, max_len, 128]
 // cache: kv_row0 = b * Hkv * max_len, kv_hs = max_len). out: [T, Hq, 128] view (strides out_ts, out_hs).
-// Query t attends to keys 0 .. start + t; start + T <= kv_hs.
+// Query t attends to keys 0 .. start + t; start + T <= kv_hs. With tree_mask ([T] 64-bit words, T <= 64: a draft tree
+// whose node i sits in cache slot start + i), query t attends to keys 0 .. start - 1 and to slot start + i where bit i
+// of tree_mask[t] is set (its ancestors and itself).
 int xt_attn_prefill(const void *q, int64_t q_ts, int64_t q_hs, const void *k, const void *v, int64_t kv_rows,
                     int64_t kv_row0, int64_t kv_hs, int T, int start, int Hq, int Hkv, void *out, int64_t out_ts,
-                    int64_t out_hs, float scale, int *error, cudaStream_t stream) {
+                    int64_t out_hs, float scale, const unsigned long long *tree_mask, int *error,
+                    cudaStream_t stream) {
     if (T <= 0 || start < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || int64_t(start) + T > kv_hs) return -2;
+    if (tree_mask && T > 64) return -2;
     if (kv_rows <= 0 || kv_rows > INT32_MAX || kv_row0 < 0 || kv_row0 + Hkv * kv_hs > kv_rows) return -2;
     if ((out_ts | out_hs) % 8 || reinterpret_cast<uintptr_t>(out) % 16) return -2;
     const int64_t nqt = (int64_t(T) + 2 * AP_BM - 1) / (2 * AP_BM);
@@ -510,7 +525,7 @@ int xt_attn_prefill(const void *q, int64_t q_ts, int64_t q_hs, const void *k, co
         if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess || fa.numRegs != AP_REG_LAUNCH) return -5;
         kernel<<<unsigned(nqt * Hq), AP_THREADS, ApSmem::BYTES, stream>>>(
             mq, mk, mv, T, start, Hq, Hq / Hkv, int(kv_row0), int(kv_hs), scale * 1.4426950408889634f,
-            static_cast<__nv_bfloat16 *>(out), out_ts, out_hs, error);
+            static_cast<__nv_bfloat16 *>(out), out_ts, out_hs, tree_mask, error);
         return 0;
     };
     int rc;

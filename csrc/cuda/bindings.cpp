@@ -59,7 +59,7 @@ void add_rmsnorm(const Tensor &x, const std::optional<Tensor> &residual, const T
 
 void qk_norm_rope_kv(const Tensor &qkv, const std::optional<Tensor> &qn, const std::optional<Tensor> &kn,
                      const Tensor &pos, const Tensor &batch, const Tensor &q, const Tensor &kc, const Tensor &vc,
-                     int64_t hq, int64_t hkv, double theta, double eps) {
+                     int64_t hq, int64_t hkv, double theta, double eps, const std::optional<Tensor> &slots) {
     cuda_contig(qkv, "qkv");
     cuda_contig(kc, "k_cache");
     cuda_contig(vc, "v_cache");
@@ -70,6 +70,11 @@ void qk_norm_rope_kv(const Tensor &qkv, const std::optional<Tensor> &qn, const s
     p.kn = optr<const __nv_bfloat16>(kn);
     p.pos = ptr<const int32_t>(pos);
     p.batch = ptr<const int32_t>(batch);
+    if (slots)
+        check(slots->is_cuda() && slots->is_contiguous() && slots->scalar_type() == at::kInt &&
+                  slots->numel() == pos.numel(),
+              "qk_norm_rope_kv slots: int32 [T]");
+    p.slot = optr<const int32_t>(slots);
     p.q = ptr<__nv_bfloat16>(q);
     p.kc = ptr<__nv_bfloat16>(kc);
     p.vc = ptr<__nv_bfloat16>(vc);
@@ -550,7 +555,7 @@ void mla_flash(const Tensor &q, const Tensor &idx, const Tensor &codes, const Te
 // start .. start + T - 1 over row `row` of the caches k, v [B, Hkv, max_len, 128] (contiguous BF16); out [T, Hq, 128]
 // likewise a view.
 void attn_prefill(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor &out, int64_t row, int64_t start,
-                  double scale, const Tensor &err) {
+                  double scale, const Tensor &err, const std::optional<Tensor> &tree_mask) {
     auto view_ok = [](const Tensor &t) {
         return t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 3 && t.size(2) == 128 && t.stride(2) == 1;
     };
@@ -565,10 +570,16 @@ void attn_prefill(const Tensor &q, const Tensor &k, const Tensor &v, const Tenso
     check(row >= 0 && row < k.size(0) && start >= 0 && start + T <= L && Hq % Hkv == 0,
           "attn_prefill: row / start out of range, or Hq not a multiple of Hkv");
     check(err.is_cuda() && err.scalar_type() == at::kInt, "attn_prefill err int32");
+    if (tree_mask)
+        check(tree_mask->is_cuda() && tree_mask->is_contiguous() && tree_mask->scalar_type() == at::kLong &&
+                  tree_mask->numel() == T && T <= 64,
+              "attn_prefill tree_mask: int64 [T], T <= 64");
     c10::cuda::CUDAGuard g(q.device());
     check_rc(xt_attn_prefill(q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), k.size(0) * Hkv * L,
                              row * Hkv * L, L, int(T), int(start), int(Hq), int(Hkv), out.data_ptr(), out.stride(0),
-                             out.stride(1), float(scale), ptr<int>(err), stream()),
+                             out.stride(1), float(scale),
+                             tree_mask ? static_cast<const unsigned long long *>(tree_mask->data_ptr()) : nullptr,
+                             ptr<int>(err), stream()),
              "attn_prefill");
 }
 
@@ -968,7 +979,7 @@ TORCH_LIBRARY(xtier, m) {
           "float theta) -> ()");
     m.def("silu_mul(Tensor inp, Tensor(a!) out) -> ()");
     m.def("qk_norm_rope_kv(Tensor qkv, Tensor? q_norm, Tensor? k_norm, Tensor pos, Tensor batch, Tensor(a!) q, "
-          "Tensor(b!) k_cache, Tensor(c!) v_cache, int hq, int hkv, float theta, float eps) -> ()");
+          "Tensor(b!) k_cache, Tensor(c!) v_cache, int hq, int hkv, float theta, float eps, Tensor? slots=None) -> ()");
     m.def("attn_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seqlens, Tensor(a!) out, Tensor(b!) ws_o, "
           "Tensor(c!) ws_ml, Tensor(d!) counters, int splits, float scale) -> ()");
     m.def("moe_route(Tensor x, Tensor wr, Tensor? bias, Tensor? corr, Tensor? table, Tensor? shared_slots, "
@@ -1001,7 +1012,7 @@ TORCH_LIBRARY(xtier, m) {
           "int nq, Tensor(b!) err) -> ()");
     m.def("mla_kv_write(Tensor lat, Tensor slot, Tensor(a!) codes, Tensor(b!) scales, Tensor(c!) rope) -> ()");
     m.def("attn_prefill(Tensor q, Tensor k, Tensor v, Tensor(a!) out, int row, int start, float scale, "
-          "Tensor(b!) err) -> ()");
+          "Tensor(b!) err, Tensor? tree_mask=None) -> ()");
     m.def("mla_flash(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!)? part_o, "
           "Tensor(b!)? part_ml, Tensor(c!) out, float scale, int splits, Tensor(d!) err, Tensor? q_rope=None) -> ()");
     m.def("mla_decode(Tensor q, Tensor idx, Tensor codes, Tensor scales, Tensor rope, Tensor(a!) kg, Tensor(b!) vt, "

@@ -115,7 +115,7 @@ __global__ void qk_norm_rope_kv_kernel(RopeParams p) {
     } else {
         const int kvh = is_k ? h - p.Hq : h - p.Hq - p.Hkv;
         __nv_bfloat16 *cache = is_k ? p.kc : p.vc;
-        dst = cache + ((size_t(p.batch[t]) * p.Hkv + kvh) * p.L + p.pos[t]) * D;
+        dst = cache + ((size_t(p.batch[t]) * p.Hkv + kvh) * p.L + (p.slot ? p.slot[t] : p.pos[t])) * D;
     }
     *reinterpret_cast<__nv_bfloat162 *>(dst + 2 * lane) = __floats2bfloat162_rn(a.x, a.y);
     *reinterpret_cast<__nv_bfloat162 *>(dst + half + 2 * lane) = __floats2bfloat162_rn(b.x, b.y);

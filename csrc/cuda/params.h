@@ -75,6 +75,8 @@ struct RopeParams {
     const __nv_bfloat16 *kn;    // [D] or null
     const int32_t *pos;         // [T]
     const int32_t *batch;       // [T] cache row of each token
+    const int32_t *slot;        // [T] cache position of each token, or null: its RoPE position (tree drafts: nodes
+                                // at the same depth share a position, each has its own slot)
     __nv_bfloat16 *q;           // [T, Hq, D]
     __nv_bfloat16 *kc, *vc;     // [B, Hkv, L, D]
     int T, Hq, Hkv, D, L;
@@ -237,7 +239,8 @@ int xt_gemm_mx8(const void *x8, const void *sfx, int M, const void *w8, const vo
                 const void *residual, void *y, int *error, cudaStream_t stream);
 int xt_attn_prefill(const void *q, int64_t q_ts, int64_t q_hs, const void *k, const void *v, int64_t kv_rows,
                     int64_t kv_row0, int64_t kv_hs, int T, int start, int Hq, int Hkv, void *out, int64_t out_ts,
-                    int64_t out_hs, float scale, int *error, cudaStream_t stream);
+                    int64_t out_hs, float scale, const unsigned long long *tree_mask, int *error,
+                    cudaStream_t stream);
 int xt_mla_flash(const void *q_lat, int64_t ql_ts, int64_t ql_hs, const void *q_rope, int64_t qr_ts, int64_t qr_hs,
                  const int32_t *idx, int Q, int nsel, const void *codes, const void *scales, const void *rope,
                  float *part_o, float *part_ml, void *out, int64_t out_ts, int64_t out_hs, float scale, int splits,

@@ -28,11 +28,12 @@ ROOT = Path(__file__).resolve().parents[2]
 # ------------------------------------------------------------------ the server log, read back
 # stage lines (serve.Stages), telemetry lines (serve.Server.telemetry), fatal lines
 _STAGE = re.compile(r'\[xtier_b200\] stage (\w+) (\d+)/(\d+)')
-_TELE = re.compile(r'\[xtier_b200\] decode (\d+) req (\d+) tok ([\d.]+) tok/s queue (\d+)(?: cpu (\d+) calls (\d+) us)?')
+_TELE = re.compile(r'\[xtier_b200\] decode (\d+) req (\d+) tok ([\d.]+) tok/s queue (\d+)'
+                   r'(?: cpu (\d+) calls (\d+) us)?')
 _FATAL = re.compile(r'\[xtier_b200\] FATAL: [^\n]*|CUDA error[^\n]*|[A-Za-z]*Error: [^\n]*')
 _ANSI = re.compile(r'\x1b\[[0-9;]*m')
-_LABELS = {'boot': ('starting the process', 3), 'weights': ('loading weights', 8), 'pool': ('expert pools, CPU engines', 84),
-           'graphs': ('capturing the decode graph', 92), 'ready': ('ready', 100)}
+_LABELS = {'boot': ('starting the process', 3), 'weights': ('loading weights', 8),
+           'pool': ('expert pools, CPU engines', 84), 'graphs': ('capturing the decode graph', 92), 'ready': ('ready', 100)}
 
 
 def progress(text: str) -> dict:

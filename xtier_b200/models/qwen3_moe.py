@@ -12,6 +12,7 @@ from __future__ import annotations
 import dataclasses
 import math
 
+import numpy as np
 import torch
 
 from .. import config, formats, ops
@@ -402,15 +403,27 @@ class Qwen3MoeModel:
         return res
 
     def prefill(self, st: dict, tokens: torch.Tensor, row: int = 0, start: int = 0, return_logits: bool = False,
-                all_logits: bool = False, active: torch.Tensor | None = None):
+                all_logits: bool = False, active: torch.Tensor | None = None, tree=None):
         """Runs `tokens` [T] of sequence `row` from position `start`; fills the KV cache; returns the next token
         (and the last position's logits with return_logits; every position's with all_logits, e.g. a speculative
-        verify). `active` (int32 [T] token flags, calls of <= 16 tokens): flag-0 tokens skip their routed experts."""
+        verify). `active` (int32 [T] token flags, calls of <= 16 tokens): flag-0 tokens skip their routed experts.
+        `tree` (runtime/tree.py Tree, T <= 64 nodes, GPU only): the tokens are a draft tree in breadth-first order;
+        node i goes to cache slot start + i at RoPE position start + depth(i) and attends to the cache before `start`
+        and to its ancestors (call with all_logits; `compact_tree` keeps the accepted path)."""
         cfg = self.cfg
         dev = self.device
         T = tokens.shape[0]
         H, D = cfg.hidden, cfg.head_dim
-        pos = torch.arange(start, start + T, dtype=torch.int32, device=dev)
+        slots = tree_mask = None
+        if tree is not None:
+            if dev.type != 'cuda' or D != 128 or T != tree.n or T > 64 or self.bigram is not None:
+                raise ValueError('tree verification needs the GPU attention kernel (head dim 128), at most 64 nodes '
+                                 'and no bigram table')
+            pos = torch.as_tensor(start + tree.depth.astype(np.int64), dtype=torch.int32).to(dev)
+            slots = torch.arange(start, start + T, dtype=torch.int32, device=dev)
+            tree_mask = torch.as_tensor(tree.ancestor_words()).to(dev)
+        else:
+            pos = torch.arange(start, start + T, dtype=torch.int32, device=dev)
         rows = torch.full((T,), row, dtype=torch.int32, device=dev)
         residual = self.embed.index_select(0, tokens.to(dev)).contiguous()
         if self.bigram is not None:
@@ -424,7 +437,8 @@ class Qwen3MoeModel:
         # prefill attention: the tcgen05 kernel on a GPU (head dim 128); PyTorch's attention on the CPU and with
         # XTIER_PREFILL_ATTN=sdpa
         attn_flat = (torch.empty(T, cfg.heads * D, dtype=torch.bfloat16, device=dev)
-                     if dev.type == 'cuda' and D == 128 and config.get('XTIER_PREFILL_ATTN') != 'sdpa' else None)
+                     if dev.type == 'cuda' and D == 128 and (config.get('XTIER_PREFILL_ATTN') != 'sdpa'
+                                                             or tree is not None) else None)
         copy_stream = None
         if T >= config.get('XTIER_GPU_PREFILL_MIN') and dev.type == 'cuda':
             copy_stream = getattr(self, '_copy_stream', None) or torch.cuda.Stream(device=dev)
@@ -436,10 +450,10 @@ class Qwen3MoeModel:
                 ops.add_rmsnorm(moe_out, residual, L['in_norm'], h, cfg.eps)
             qkv = ops.linear(h, L['qkv'])
             ops.qk_norm_rope_kv(qkv, L['q_norm'], L['k_norm'], pos, rows, q, st['k'][li], st['v'][li], cfg.heads,
-                                cfg.kv_heads, cfg.rope_theta, cfg.eps)
+                                cfg.kv_heads, cfg.rope_theta, cfg.eps, slots=slots)
             if attn_flat is not None:   # tcgen05 causal GQA kernel, written straight into the o-projection input
                 ops.attn_prefill(q, st['k'][li], st['v'][li], row, start, 1.0 / math.sqrt(D),
-                                 out=attn_flat.view(T, cfg.heads, D))
+                                 out=attn_flat.view(T, cfg.heads, D), tree_mask=tree_mask)
                 o = ops.linear(attn_flat, L['o'])
             else:
                 kk = st['k'][li][row:row + 1, :, :start + T]
@@ -469,6 +483,17 @@ class Qwen3MoeModel:
         st['lengths'][row] = start + T
         nxt = torch.argmax(logits, dim=-1)
         return (nxt, logits[0]) if return_logits else nxt
+
+    def compact_tree(self, st: dict, row: int, start: int, path: list[int]):
+        """After a tree verify: the KV of the accepted nodes `path` (tree node indices, root first) moves to slots
+        start .. start + len(path) - 1 (their RoPE positions already), and the row's length ends after them."""
+        idx = torch.tensor([start + int(p) for p in path], dtype=torch.long, device=self.device)
+        dst = torch.arange(start, start + len(path), dtype=torch.long, device=self.device)
+        if not torch.equal(idx, dst):
+            for li in range(len(self.layers)):
+                for c in (st['k'][li], st['v'][li]):
+                    c[row, :, dst] = c[row, :, idx]   # gathered before it is written
+        st['lengths'][row] = start + len(path)
 
     # ------------------------------------------------------------------ fp32 reference (tests)
     def reference_logits(self, tokens: torch.Tensor) -> torch.Tensor:

@@ -56,22 +56,25 @@ def rmsnorm(x, w, eps: float, out=None):
 
 
 def qk_norm_rope_kv(qkv, q_norm, k_norm, pos, batch, q_out, k_cache, v_cache, hq: int, hkv: int, theta: float,
-                    eps: float):
-    _ops().qk_norm_rope_kv(qkv, q_norm, k_norm, pos, batch, q_out, k_cache, v_cache, hq, hkv, theta, eps)
+                    eps: float, slots=None):
+    """slots (int32 [T], optional): the cache position each token's K / V goes to (default: its RoPE position)."""
+    _ops().qk_norm_rope_kv(qkv, q_norm, k_norm, pos, batch, q_out, k_cache, v_cache, hq, hkv, theta, eps, slots)
 
 
 def attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits: int, scale: float):
     _ops().attn_decode(q, k_cache, v_cache, seqlens, out, ws_o, ws_ml, counters, splits, scale)
 
 
-def attn_prefill(q, k_cache, v_cache, row: int, start: int, scale: float, out=None):
+def attn_prefill(q, k_cache, v_cache, row: int, start: int, scale: float, out=None, tree_mask=None):
     """Causal GQA attention of q [T, Hq, 128] (a view with unit stride along the last dim) at positions
     start .. start + T - 1 over row `row` of the caches [B, Hkv, max_len, 128] (tcgen05 flash kernel): query t sees keys
     0 .. start + t. Returns out [T, Hq, 128] (or writes the given view). A wait that runs out sets the shared error
-    word (gemm_error_word); the caller's check() raises."""
+    word (gemm_error_word); the caller's check() raises. tree_mask (int64 [T], T <= 64): a draft tree in cache slots
+    start .. start + T - 1; query t then sees the keys before `start` and the tree slots whose bit is set in
+    tree_mask[t] (its ancestors and itself) instead of the causal range."""
     if out is None:
         out = torch.empty(q.shape[0], q.shape[1], 128, dtype=torch.bfloat16, device=q.device)
-    _ops().attn_prefill(q, k_cache, v_cache, out, row, start, scale, gemm_error_word(q.device))
+    _ops().attn_prefill(q, k_cache, v_cache, out, row, start, scale, gemm_error_word(q.device), tree_mask)
     return out
 
 

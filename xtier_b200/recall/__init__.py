@@ -23,7 +23,8 @@ fell below the bar is only probed, rarer after every probe that misses.
 dedup of repeated runs, FIFO budget, min free space, read-only refresh) and RecallEngine (own context first, match tiers,
 cooldown after a miss, probes, the heat-ordered eviction with its hot zone) and the proposal broadcast to the
 tensor-parallel ranks (`sync_proposal`). The index layout, hash, expectation rule and heat bookkeeping here are this
-project's own. Not built: the prompt-hash reply store, the GPU-resident id store and tree drafts.)
+project's own; the copies also feed multi-branch draft trees (`RecallEngine.candidates`, runtime/tree.py). Not
+built: the prompt-hash reply store and the GPU-resident id store.)
 """
 from __future__ import annotations
 
@@ -586,12 +587,19 @@ class RecallEngine:
         self.probes += probe
         return p
 
-    def feedback(self, rid, landed: int):
-        """The target accepted `landed` tokens of the last proposal."""
+    def candidates(self, rid) -> list[Proposal]:
+        """Every available copy of the stream (its own context's and the record's), without the offer rule: the
+        branches of a draft tree, which the target verifies in the same forward as the other drafts."""
         st = self.streams[rid]
-        p, st.last = st.last, None
-        if p is None:
-            return
+        out = []
+        for src, cand in (('own', self._own_candidate(st)), ('record', self._record_candidate(st))):
+            if cand is not None:
+                out.append(Proposal(src, [int(t) for t in cand[1]], cand[0], tier_of(cand[0]), False,
+                                    cand[2] if src == 'record' else -1))
+        return out
+
+    def note(self, p: Proposal, landed: int):
+        """`landed` tokens of copy `p` were accepted: the expectation of its source and tier, and the record's heat."""
         for k in self.sums:
             self.sums[k][0] *= self.decay
             self.sums[k][1] *= self.decay
@@ -601,6 +609,14 @@ class RecallEngine:
         self.landed += landed
         if p.source == 'record' and p.pos >= 0 and self.record is not None:
             self.record.credit(p.pos, landed)
+
+    def feedback(self, rid, landed: int):
+        """The target accepted `landed` tokens of the last proposal."""
+        st = self.streams[rid]
+        p, st.last = st.last, None
+        if p is None:
+            return
+        self.note(p, landed)
         if landed == 0:
             st.cooldown = self.cooldown
         if p.probe:

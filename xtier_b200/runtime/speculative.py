@@ -83,12 +83,14 @@ class SpeculativeDecoder:
 
     def __init__(self, target, draft=None, steps: int = 4, threshold: float | None = None, temperature: float = 0.0,
                  max_len: int = 4096, seed: int = 0, recall=None, hot_ids: torch.Tensor | None = None,
-                 draft_temp_scale: float | None = None):
+                 draft_temp_scale: float | None = None, tree: bool = False, tree_nodes: int = 16):
         """threshold: verify truncation at draft confidence (default XTIER_SPEC_TRUNCATE_Q; 0: off). hot_ids [Vd]:
         the target ids of a draft model whose head covers only a hot vocabulary (its q is scattered into the target
         vocabulary before verification: zero where the draft can never propose, so the accept test and the residual
         stay exact). draft_temp_scale: the draft samples at temperature x this (default XTIER_SPEC_DRAFT_TEMP_SCALE);
-        lossless for any scale, since verification uses the q the draft sampled from."""
+        lossless for any scale, since verification uses the q the draft sampled from. tree (greedy decoding): every
+        round merges the draft model's chain and the Recall copies into one draft tree of at most `tree_nodes` nodes
+        verified in one target forward (runtime/tree.py)."""
         from .. import config
         if draft is None and recall is None:
             raise ValueError('speculative decoding needs a draft model or a recall engine')
@@ -101,7 +103,9 @@ class SpeculativeDecoder:
         self.st_t = target.alloc_state(1, max_len)
         self.st_d = draft.alloc_state(1, max_len) if draft is not None else None
         self.gen = torch.Generator().manual_seed(seed)
-        self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0, copies=0, copied=0, copy_landed=0, plain=0, forwards=0)
+        self.tree, self.tree_nodes = tree, tree_nodes
+        self.stats = dict(rounds=0, drafted=0, accepted=0, kept=0, copies=0, copied=0, copy_landed=0, plain=0,
+                          forwards=0, tree_rounds=0, tree_nodes=0, tree_accepted=0)
 
     def _probs(self, logits: torch.Tensor, temp: float | None = None) -> torch.Tensor:
         """Target (or draft) distribution per row: one-hot argmax at temperature 0, else softmax(logits / temp)
@@ -141,6 +145,66 @@ class SpeculativeDecoder:
         return verify_chain(self._probs(logits)[:keep + 1], q[:keep], torch.tensor(drafts[:keep]), self.gen,
                             self.temp <= 0)
 
+    def _draft_chain(self, pos: int, last: int, greedy: bool):
+        """The draft model's chain of S tokens after `last` (fed at pos ..): (tokens, per-token q rows [S, V])."""
+        dev = self.target.device
+        seq = self.seq
+        if self.dpos < pos:   # the draft catches up on accepted tokens it has not seen
+            self.draft.prefill(self.st_d, torch.tensor(seq[self.dpos:pos], device=dev), start=self.dpos)
+            self.dpos = pos
+        drafts, qs, cur = [], [], last
+        V = self.target_vocab(dev)
+        for j in range(self.S):
+            _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j, return_logits=True)
+            qj = self.draft_probs(ld, V)
+            d = int(torch.argmax(qj)) if greedy else int(torch.multinomial(qj, 1, generator=self.gen))
+            drafts.append(d)
+            qs.append(qj)
+            cur = d
+        return drafts, qs
+
+    def _tree_round(self, pos: int, last: int, limit: int | None) -> list[int] | None:
+        """One greedy round over a draft tree (the draft chain and the Recall copies); None when no branch exists."""
+        from .tree import build_tree, walk_greedy
+        chains, copies, drafts = [], [], None
+        if self.recall is not None:
+            for p in self.recall.candidates(self.rid):
+                ids = p.ids[:max(1, limit)] if limit is not None else p.ids
+                copies.append((p, ids))
+                chains.append((ids, [0.9] * len(ids)))   # a copy is a point mass; longer copies rank lower per node
+        if self.draft is not None:
+            drafts, qs = self._draft_chain(pos, last, True)
+            chains.append((drafts, [float(q.max()) for q in qs]))
+        if not chains:
+            return None
+        tree = build_tree(last, chains, self.tree_nodes)
+        if tree.n == 1:
+            return None
+        dev = self.target.device
+        _, logits = self.target.prefill(self.st_t, torch.as_tensor(tree.tokens).to(dev), start=pos, all_logits=True,
+                                        tree=tree)
+        path, bonus = walk_greedy(tree, torch.argmax(logits, -1).tolist())
+        self.target.compact_tree(self.st_t, 0, pos, path)
+        acc = [int(tree.tokens[i]) for i in path[1:]] + [int(bonus)]
+
+        def common(a, b):
+            n = 0
+            while n < min(len(a), len(b)) and a[n] == b[n]:
+                n += 1
+            return n
+
+        for p, ids in copies:
+            self.recall.note(p, common(ids, acc[:-1]))
+        if drafts is not None:   # the draft's KV is valid for the accepted prefix of its own chain
+            self.dpos = pos + 1 + common(acc, drafts[:self.S - 1])
+            if self.recall is not None:
+                self.recall.observe_own(self.rid, common(drafts, acc[:-1]))
+        self.stats['tree_rounds'] += 1
+        self.stats['tree_nodes'] += tree.n
+        self.stats['tree_accepted'] += len(acc) - 1
+        self.stats['accepted'] += len(acc) - 1
+        return acc
+
     def _sample(self, logits: torch.Tensor) -> int:
         if self.temp <= 0:
             return int(torch.argmax(logits))
@@ -171,53 +235,55 @@ class SpeculativeDecoder:
         greedy = self.temp <= 0
         pos, seq = self.pos, self.seq
         last = seq[pos]
-        prop = self.recall.propose(self.rid) if self.recall is not None else None
-        if prop is not None and prop.ids:
-            drafts = prop.ids[:max(1, limit)] if limit is not None else prop.ids
-            V = self.target_vocab(dev)
-            q = torch.zeros(len(drafts), V)
-            q[torch.arange(len(drafts)), torch.tensor(drafts)] = 1.0     # a copy is a point mass
-            acc = self._verify(pos, last, drafts, q)
-            self.recall.feedback(self.rid, len(acc) - 1)
-            self.stats['copies'] += 1
-            self.stats['copied'] += len(drafts)
-            self.stats['copy_landed'] += len(acc) - 1
-        elif self.draft is None:      # a plain target step
-            _, lg = self.target.prefill(self.st_t, torch.tensor([last], device=dev), start=pos, return_logits=True)
-            acc = [self._sample(lg)]
-            self.stats['plain'] += 1
-        else:
-            if self.dpos < pos:   # the draft catches up on accepted tokens it has not seen
-                self.draft.prefill(self.st_d, torch.tensor(seq[self.dpos:pos], device=dev), start=self.dpos)
-                self.dpos = pos
-            drafts, qs, cur = [], [], last
-            V = self.target_vocab(dev)
-            for j in range(self.S):
-                _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
-                                           return_logits=True)
-                qj = self.draft_probs(ld, V)
-                d = int(torch.argmax(qj)) if greedy else int(torch.multinomial(qj, 1, generator=self.gen))
-                drafts.append(d)
-                qs.append(qj)
-                cur = d
-            q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
-            if self.th > 0:
-                q = q.to(dev)
-                vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
-                flags = truncate(q, vt, self.th, greedy=greedy)
-                keep = int(flags[0].sum()) - 1
-                active = flags[0]
-            else:                      # no truncation: every draft is verified
-                keep, active = self.S, None
-            acc = self._verify(pos, last, drafts, q[0], active=active, keep=keep)
-            self.stats['rounds'] += 1
-            self.stats['drafted'] += self.S
-            self.stats['kept'] += keep
-            self.stats['accepted'] += len(acc) - 1
-            if self.recall is not None:
-                self.recall.observe_own(self.rid, len(acc) - 1)
-            # the draft fed last, d_1..d_{S-1} at pos..pos+S-1: valid up to the accepted ones
-            self.dpos = pos + min(len(acc), self.S)
+        acc = self._tree_round(pos, last, limit) if self.tree and greedy else None
+        if acc is None:
+            prop = self.recall.propose(self.rid) if self.recall is not None else None
+            if prop is not None and prop.ids:
+                drafts = prop.ids[:max(1, limit)] if limit is not None else prop.ids
+                V = self.target_vocab(dev)
+                q = torch.zeros(len(drafts), V)
+                q[torch.arange(len(drafts)), torch.tensor(drafts)] = 1.0     # a copy is a point mass
+                acc = self._verify(pos, last, drafts, q)
+                self.recall.feedback(self.rid, len(acc) - 1)
+                self.stats['copies'] += 1
+                self.stats['copied'] += len(drafts)
+                self.stats['copy_landed'] += len(acc) - 1
+            elif self.draft is None:      # a plain target step
+                _, lg = self.target.prefill(self.st_t, torch.tensor([last], device=dev), start=pos, return_logits=True)
+                acc = [self._sample(lg)]
+                self.stats['plain'] += 1
+            else:
+                if self.dpos < pos:   # the draft catches up on accepted tokens it has not seen
+                    self.draft.prefill(self.st_d, torch.tensor(seq[self.dpos:pos], device=dev), start=self.dpos)
+                    self.dpos = pos
+                drafts, qs, cur = [], [], last
+                V = self.target_vocab(dev)
+                for j in range(self.S):
+                    _, ld = self.draft.prefill(self.st_d, torch.tensor([cur], device=dev), start=pos + j,
+                                               return_logits=True)
+                    qj = self.draft_probs(ld, V)
+                    d = int(torch.argmax(qj)) if greedy else int(torch.multinomial(qj, 1, generator=self.gen))
+                    drafts.append(d)
+                    qs.append(qj)
+                    cur = d
+                q = torch.stack(qs)[None].contiguous().float()                  # [1, S, V]
+                if self.th > 0:
+                    q = q.to(dev)
+                    vt = torch.tensor([[last] + drafts], dtype=torch.long, device=dev)
+                    flags = truncate(q, vt, self.th, greedy=greedy)
+                    keep = int(flags[0].sum()) - 1
+                    active = flags[0]
+                else:                      # no truncation: every draft is verified
+                    keep, active = self.S, None
+                acc = self._verify(pos, last, drafts, q[0], active=active, keep=keep)
+                self.stats['rounds'] += 1
+                self.stats['drafted'] += self.S
+                self.stats['kept'] += keep
+                self.stats['accepted'] += len(acc) - 1
+                if self.recall is not None:
+                    self.recall.observe_own(self.rid, len(acc) - 1)
+                # the draft fed last, d_1..d_{S-1} at pos..pos+S-1: valid up to the accepted ones
+                self.dpos = pos + min(len(acc), self.S)
         self.stats['forwards'] += 1
         seq.extend(acc)
         if self.recall is not None:
