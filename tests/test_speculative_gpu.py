@@ -78,3 +78,36 @@ def test_speculative_greedy_equals_target_greedy(cuda_ops):
     got = sd.generate(prompt, 20)
     assert got == want, (got, want)
     assert sd.stats['rounds'] < 20                      # some drafts were accepted
+
+
+def test_fp8_draft_lm_head(cuda_ops):
+    """A draft whose LM head is FP8 (W8A16 GEMV in decode, W8A8 block-scaled GEMM in prefill): its logits stay close
+    to the BF16 head's, its decode graph runs, and speculative greedy output still equals the target's."""
+    from xtier_b200.runtime.decode import Generator
+    from xtier_b200.runtime.speculative import SpeculativeDecoder
+    target = _tiny(41)
+    draft = _tiny(41, layers=1)
+    prompt = torch.randint(0, target.cfg.vocab, (150,), generator=torch.Generator().manual_seed(7)).cuda()
+    st = draft.alloc_state(1, 256)
+    _, ref = draft.prefill(st, prompt, all_logits=True)               # every position: the prefill GEMM
+    draft.quantize_lm_head()
+    assert draft.lm_head is None and draft.lm_head_fp8 is not None
+    st = draft.alloc_state(1, 256)
+    _, got = draft.prefill(st, prompt, all_logits=True)
+    assert float((got.float() - ref.float()).norm() / ref.float().norm()) < 8e-2
+    st = draft.alloc_state(1, 256)
+    _, last = draft.prefill(st, prompt, return_logits=True)           # one position: the W8A16 GEMV
+    assert float((last.float() - ref[-1].float()).norm() / ref[-1].float().norm()) < 8e-2
+    gen = Generator(draft, batch=1, max_len=256)
+    toks = gen.generate(prompt[None].cpu(), 4)
+    assert toks.shape == (1, 4)
+    gen.graph = None
+    want = []
+    st = target.alloc_state(1, 256)
+    nxt, pos = target.prefill(st, prompt[:12]), 12
+    for _ in range(16):
+        want.append(int(nxt))
+        nxt = target.prefill(st, nxt.view(1), start=pos)
+        pos += 1
+    sd = SpeculativeDecoder(target, draft, steps=4, threshold=0.0, max_len=256, draft_fp8_head=True)
+    assert sd.generate(prompt[:12], 16) == want

@@ -142,6 +142,7 @@ class Qwen3MoeModel:
         self.cold = None
         self.peers = None
         self.bigram = None   # tables.engram.BigramTable (attach_bigram)
+        self.lm_head_fp8 = None   # (E4M3 [V, H], scales [V, H / 128], MXFP8 copy or None): quantize_lm_head
         prank, pworld = 0, 1
         if peer and partial:
             from ..parallel import dist as xdist
@@ -342,6 +343,7 @@ class Qwen3MoeModel:
         B = buf['tokens'].shape[0]
         side = st.get('side') if B <= 16 else None
         main = torch.cuda.current_stream(self.device) if side is not None else None
+        forked = False
         if getattr(self, 'ring', None) is not None:   # hot-slot swaps whose copies have landed take effect
             self.ring.commit()
         torch.add(buf['pos'], 1, out=buf['seqlens'])
@@ -362,19 +364,23 @@ class Qwen3MoeModel:
             ops.linear(buf['attn'].view(B, -1), L['o'], out=buf['o'])
             ops.add_rmsnorm(buf['o'], buf['residual'], L['post_norm'], buf['h'], cfg.eps)
             if side is not None and li + 1 < len(self.layers):   # next layer's weights into L2 meanwhile
+                forked = True
                 side.wait_stream(main)
                 with torch.cuda.stream(side):
                     ops.l2_prefetch(*st['prefetch'][li + 1])
             L['moe'].forward(buf['h'], out=buf['moe_out'])
         ops.add_rmsnorm(buf['moe_out'], buf['residual'], self.final_norm, buf['h'], cfg.eps)
-        ops.gemv(buf['h'], self.lm_head, buf['logits'])
+        if self.lm_head_fp8 is not None:   # W8A16: half the bytes of the largest read of the step
+            ops.gemv_fp8(buf['h'], self.lm_head_fp8[0], self.lm_head_fp8[1], buf['logits'])
+        else:
+            ops.gemv(buf['h'], self.lm_head, buf['logits'])
         if getattr(self, 'sampling', False):   # temperature / top-p per row, decided on the device
             from ..runtime.sampling import sample
             sample(buf['logits'], buf['temp'], buf['top_p'], out=buf['next'])
         else:
             torch.argmax(buf['logits'], dim=-1, out=buf['next'])
         buf['prev'].copy_(buf['tokens'])
-        if side is not None:
+        if side is not None and forked:   # a one-layer model never forks the prefetch branch
             main.wait_stream(side)
         return buf['next']
 
@@ -476,13 +482,30 @@ class Qwen3MoeModel:
             L['moe'].forward(h, out=moe_out, active=active)
         ops.add_rmsnorm(moe_out, residual, self.final_norm, h, cfg.eps)
         if all_logits:
-            logits = ops.linear(h, self.lm_head)
+            logits = self._lm_head(h)
             st['lengths'][row] = start + T
             return torch.argmax(logits, dim=-1), logits
-        logits = ops.linear(h[-1:].contiguous(), self.lm_head)
+        logits = self._lm_head(h[-1:].contiguous())
         st['lengths'][row] = start + T
         nxt = torch.argmax(logits, dim=-1)
         return (nxt, logits[0]) if return_logits else nxt
+
+    def quantize_lm_head(self):
+        """The LM head in FP8 E4M3 with one scale per row and 128 columns (e.g. a speculative draft's, whose step is
+        dominated by it): the decode step reads it through the W8A16 GEMV, prefill through the W8A8 block-scaled GEMM
+        (weights requantized to MXFP8 once). The BF16 copy is freed."""
+        if self.lm_head_fp8 is not None or self.device.type != 'cuda':
+            return
+        w8, s = ops.fp8_quantize(self.lm_head)
+        mx8 = ops.fp8_weight_to_mx8(w8, s) if self.lm_head.shape[0] % 128 == 0 else None
+        self.lm_head_fp8 = (w8, s, mx8)
+        self.lm_head = None
+
+    def _lm_head(self, h):
+        if self.lm_head_fp8 is None:
+            return ops.linear(h, self.lm_head)
+        w8, s, mx8 = self.lm_head_fp8
+        return ops.linear_fp8(h, w8, s, mx8=mx8)
 
     def compact_tree(self, st: dict, row: int, start: int, path: list[int]):
         """After a tree verify: the KV of the accepted nodes `path` (tree node indices, root first) moves to slots
@@ -569,4 +592,6 @@ class Qwen3MoeModel:
                     out[t] += w[t, j] * ((torch.nn.functional.silu(g) * u) @ w2.t())
             x = x + out
         x = rms(x, self.final_norm)
-        return x[-1] @ self.lm_head.to(f).t()
+        head = (self.lm_head if self.lm_head is not None
+                else ops.fp8_dequant(self.lm_head_fp8[0], self.lm_head_fp8[1]))
+        return x[-1] @ head.to(f).t()

@@ -117,6 +117,16 @@ def gemv_fp8(x, w, s, out, add=None):
     return out
 
 
+def fp8_quantize(w):
+    """BF16 w [N, K] (K % 128 == 0) -> (E4M3 bytes [N, K], FP32 scales [N, K / 128]): one scale per row and 128
+    columns, amax / 448 (the layout gemv_fp8, fp8_dequant and linear_fp8 read)."""
+    N, K = w.shape
+    g = w.float().view(N, K // 128, 128)
+    s = (g.abs().amax(-1) / 448.0).clamp_min(1e-12)
+    q = (g / s.unsqueeze(-1)).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8).view(N, K)
+    return q.contiguous(), s.contiguous()
+
+
 def fp8_dequant(w, s, out=None):
     """w[N, K] E4M3 * s[N, K/128] -> BF16 [N, K]."""
     out = torch.empty(w.shape, dtype=torch.bfloat16, device=w.device) if out is None else out

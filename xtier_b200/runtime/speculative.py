@@ -83,18 +83,22 @@ class SpeculativeDecoder:
 
     def __init__(self, target, draft=None, steps: int = 4, threshold: float | None = None, temperature: float = 0.0,
                  max_len: int = 4096, seed: int = 0, recall=None, hot_ids: torch.Tensor | None = None,
-                 draft_temp_scale: float | None = None, tree: bool = False, tree_nodes: int = 16):
+                 draft_temp_scale: float | None = None, tree: bool = False, tree_nodes: int = 16,
+                 draft_fp8_head: bool = False):
         """threshold: verify truncation at draft confidence (default XTIER_SPEC_TRUNCATE_Q; 0: off). hot_ids [Vd]:
         the target ids of a draft model whose head covers only a hot vocabulary (its q is scattered into the target
         vocabulary before verification: zero where the draft can never propose, so the accept test and the residual
         stay exact). draft_temp_scale: the draft samples at temperature x this (default XTIER_SPEC_DRAFT_TEMP_SCALE);
         lossless for any scale, since verification uses the q the draft sampled from. tree (greedy decoding): every
         round merges the draft model's chain and the Recall copies into one draft tree of at most `tree_nodes` nodes
-        verified in one target forward (runtime/tree.py)."""
+        verified in one target forward (runtime/tree.py). draft_fp8_head: the draft's LM head in FP8 (its decode
+        step's largest read; `quantize_lm_head`)."""
         from .. import config
         if draft is None and recall is None:
             raise ValueError('speculative decoding needs a draft model or a recall engine')
         self.target, self.draft, self.recall = target, draft, recall
+        if draft_fp8_head and draft is not None and hasattr(draft, 'quantize_lm_head'):
+            draft.quantize_lm_head()
         self.S, self.temp = steps, temperature
         self.th = config.get('XTIER_SPEC_TRUNCATE_Q') if threshold is None else threshold
         self.draft_scale = (config.get('XTIER_SPEC_DRAFT_TEMP_SCALE') if draft_temp_scale is None
