@@ -275,8 +275,10 @@ def run_config3(args, ctx: Ctx) -> dict:
     launches = graph_launches(gen)
     if args.profile:
         return profile_steps(gen, args, ctx)
-    # the first step's next token of every request, gathered: the same job at every N gives the same tokens (up to
-    # the CPU tier's FP32 arithmetic at 1 and 2 GPUs)
+    # the first step's next token of every request, gathered (the same requests, caches and weights at every N). The
+    # tokens agree across N only in part: the projections' split-K depends on the rows per rank and the EP combine
+    # order on the rank count, and the FP32 summation-order differences flip near-tied top-8 routes and argmaxes of a
+    # random-init model (1 vs 2 GPUs, 8 layers: 18 of 32 equal)
     gen.step()
     first_tokens = ctx.gather_tokens(gen.buf['next'])
     ms, e2e_s, clocks = ctx.timed_decode(gen, args)
