@@ -230,3 +230,94 @@ def test_proposal_broadcast_two_ranks():
     want = recall.Proposal('own', [5, 6, 7], 40, 1, False)
     assert res[0][1] == want and res[1][1] == want          # rank 1 takes rank 0's drafts
     assert res[0][2] is None and res[1][2] is None          # rank 0 had none: nobody copies
+
+
+def test_reply_store_keys_disk_memory_and_cap(tmp_path):
+    from xtier_b200.recall import replies
+    p = _text(2000, 21)
+    ks = replies.prompt_keys(p)
+    assert len(ks) == 4 and len(set(ks)) == 4
+    assert len(replies.prompt_keys(p[:100])) == 2                       # only the tails shorter than the prompt
+    other_head = _text(50, 22) + p[50:]                                 # the same prompt with another head
+    assert set(replies.prompt_keys(other_head)) & set(ks)
+    reply = _text(300, 23)
+    for path in (None, tmp_path / 'rs'):
+        st = replies.ReplyStore(path)
+        assert st.get(ks) is None
+        assert not st.put(ks, reply[:replies.MIN_REPLY - 1])           # too short
+        assert st.put(ks, reply)
+        assert st.get(ks).tolist() == reply
+        assert st.get(replies.prompt_keys(other_head)).tolist() == reply   # found through a tail key
+        assert st.count() == 4
+    # on disk: one reply file for the four keys, 0600 files, seen by another process's store, survives a restart
+    files = sorted(f.name[:2] for f in (tmp_path / 'rs').iterdir())
+    assert files.count('r-') == 1 and files.count('k-') == 4
+    assert all(stat.S_IMODE(f.stat().st_mode) == 0o600 for f in (tmp_path / 'rs').iterdir())
+    ro = replies.ReplyStore(tmp_path / 'rs', writer=False)
+    assert ro.get(ks).tolist() == reply and not ro.put(ks, reply[::-1])
+    # past the cap the oldest keys go, and their reply files with them
+    st = replies.ReplyStore(tmp_path / 'cap', cap=16)
+    for i in range(40):
+        st.put([f'key{i}'], _text(20, 100 + i))
+    st._trim()
+    assert st.count() == 16 and st.get(['key39']) is not None and st.get(['key0']) is None
+    assert sum(1 for _ in (tmp_path / 'cap').glob('r-*')) == 16
+    mem = replies.ReplyStore(None, cap=8)
+    for i in range(20):
+        mem.put([f'k{i}'], _text(20, 200 + i))
+    assert mem.count() == 8 and len(mem._replies) == 8 and mem.get(['k0']) is None
+
+
+def test_reply_realign():
+    from xtier_b200.recall import replies
+    r = np.asarray([1, 2, 3, 4, 9, 9, 1, 2, 3, 4, 7, 7, 8], np.int64)
+    assert replies.realign(r, [5, 1, 2, 3, 4], 4) == 4                 # nearest occurrence to the expected spot
+    assert replies.realign(r, [5, 1, 2, 3, 4], 11) == 10
+    assert replies.realign(r, [6, 6, 6, 6], 3) == -1
+    assert replies.realign(r, [3], 3) == -1                            # shorter than the gram
+
+
+def test_engine_drafts_a_filed_reply_and_realigns(tmp_path):
+    rec = recall.Record(tmp_path / 'rec')
+    eng = recall.RecallEngine(rec, gamma=8, min_n=1.0)
+    prompt, reply = _text(200, 31), _text(120, 32)
+    eng.begin_stream('a', prompt)
+    assert eng.propose('a') is None
+    eng.extend_stream('a', reply)
+    eng.end_stream('a')
+    assert (tmp_path / 'rec' / 'replies').is_dir()
+    eng2 = recall.RecallEngine(recall.Record(tmp_path / 'rec2'), replies=eng.replies, gamma=8, min_n=1.0)
+    eng2.begin_stream('b', prompt + reply[:1], reply_from=len(prompt))   # the first reply id already sampled
+    p = eng2.propose('b')
+    assert p.source == 'reply' and p.ids == reply[1:9] and p.tier == 2
+    eng2.extend_stream('b', reply[1:4])
+    eng2.feedback('b', 3)
+    p = eng2.propose('b')
+    assert p.source == 'reply' and p.ids == reply[4:12]
+    # a divergence, then 4 ids of the reply again: the copy lines up after them
+    eng2.extend_stream('b', [99999] + reply[60:64])
+    eng2.feedback('b', 0)
+    eng2.streams['b'].cooldown = 0
+    p = eng2.propose('b')
+    assert p.source == 'reply' and p.ids == reply[64:72] and p.tier == 0
+    assert eng2.stats()['replies']['prompt_hits'] == 1 and eng2.realigns == 1
+    off = recall.RecallEngine(recall.Record(), replies=None)
+    off.begin_stream('c', prompt)
+    assert off.stats()['replies'] is None
+
+
+def test_speculative_second_run_copies_the_reply():
+    """A sampled-free bigram target whose greedy path never cycles inside 40 tokens: the record has nothing to copy
+    on the first run, and the second run of the same prompt copies the filed reply from its first token."""
+    tgt = Bigram(V=4096, seed=5)
+    prompt = torch.tensor(_text(24, 41, 4096))
+    want = _greedy(tgt, prompt.tolist(), 40)
+    eng = recall.RecallEngine(None, gamma=16, min_n=1.0)
+    dec = SpeculativeDecoder(tgt, None, temperature=0.0, recall=eng)
+    assert dec.generate(prompt, 40) == want
+    dec.end()
+    tgt.calls = 0
+    dec2 = SpeculativeDecoder(tgt, None, temperature=0.0, recall=eng)
+    assert dec2.generate(prompt, 40) == want
+    assert eng.stats()['replies']['prompt_hits'] == 1
+    assert tgt.calls <= 5 and dec2.stats['copy_landed'] >= 35

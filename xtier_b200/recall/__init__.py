@@ -23,8 +23,9 @@ fell below the bar is only probed, rarer after every probe that misses.
 dedup of repeated runs, FIFO budget, min free space, read-only refresh) and RecallEngine (own context first, match tiers,
 cooldown after a miss, probes, the heat-ordered eviction with its hot zone) and the proposal broadcast to the
 tensor-parallel ranks (`sync_proposal`). The index layout, hash, expectation rule and heat bookkeeping here are this
-project's own; the copies also feed multi-branch draft trees (`RecallEngine.candidates`, runtime/tree.py). Not
-built: the prompt-hash reply store and the GPU-resident id store.)
+project's own; the copies also feed multi-branch draft trees (`RecallEngine.candidates`, runtime/tree.py). The
+prompt-hash reply store (a third source, asked first: the reply filed for the same prompt) is in replies.py. Not
+built: the GPU-resident id store.)
 """
 from __future__ import annotations
 
@@ -36,6 +37,8 @@ import shutil
 from pathlib import Path
 
 import numpy as np
+
+from .replies import REALIGN_GRAM, ReplyStore, prompt_keys, realign
 
 WINDOW = 16
 SENTINEL = -1
@@ -479,7 +482,7 @@ def tier_of(match: int) -> int:
 
 @dataclasses.dataclass
 class Proposal:
-    source: str          # 'own' or 'record'
+    source: str          # 'own', 'record' or 'reply'
     ids: list[int]
     match: int
     tier: int
@@ -488,23 +491,46 @@ class Proposal:
 
 
 class _Stream:
-    def __init__(self, prompt):
+    def __init__(self, prompt, reply_from: int | None = None):
         self.own = Record(None, dedup=False)
         self.ids: list[int] = list(prompt)
         self.indexed = 0
         self.cooldown = 0
         self.own_yield = 0.0     # tokens the stream's own draft model lands per round (0: none)
         self.last: Proposal | None = None
-        self.prompt_len = len(prompt)
+        self.prompt_len = len(prompt) if reply_from is None else int(reply_from)
+        self.reply_keys: list[str] = []
+        self.reply: np.ndarray | None = None   # a filed reply to the same prompt
+        self.rpos = -1           # where in `reply` the stream's next id is expected (-1: not lined up)
+        self.run = 0             # ids the stream agreed with `reply` since it lined up
+
+    def follow(self, ids):
+        """Moves the reply position along the stream's new ids; a mismatch leaves the reply (-1)."""
+        if self.reply is None:
+            return
+        for t in ids:
+            if 0 <= self.rpos < self.reply.shape[0] and int(self.reply[self.rpos]) == t:
+                self.rpos += 1
+                self.run += 1
+            else:
+                self.rpos, self.run = -1, 0
 
 
 class RecallEngine:
-    SOURCES = ('own', 'record')
+    SOURCES = ('own', 'record', 'reply')
 
     def __init__(self, record: Record | None, gamma: int = 16, min_n: float = 2.0, cooldown: int = 4,
                  prior: float = 0.5, prior_weight: float = 2.0, decay: float = 0.98, probe_start: int = 16,
-                 probe_max: int = 4096):
+                 probe_max: int = 4096, replies=True):
+        """`replies`: a `ReplyStore`, True (the default: one beside the record -- `<record>/replies` for a record on
+        disk, written only by the process that writes the record -- or in memory), or None / False (off)."""
         self.record = record
+        if replies is True:
+            on_disk = record is not None and record.path is not None
+            replies = ReplyStore(record.path / 'replies' if on_disk else None,
+                                 writer=record.writer if on_disk else True)
+        self.replies = replies or None
+        self.reply_hits = self.realigns = 0
         self.gamma = gamma
         self.min_n = min_n
         self.cooldown = cooldown
@@ -517,16 +543,30 @@ class RecallEngine:
         self.offers = self.probes = self.landed = 0
 
     # ------------------------------------------------------------------ streams
-    def begin_stream(self, rid, prompt_ids):
-        self.streams[rid] = _Stream([int(t) for t in prompt_ids])
+    def begin_stream(self, rid, prompt_ids, reply_from: int | None = None):
+        """A new stream; `reply_from` is where its reply starts in `prompt_ids` (default: after all of them -- a
+        caller that already sampled the first reply id passes the prompt's length)."""
+        st = self.streams[rid] = _Stream([int(t) for t in prompt_ids], reply_from)
+        if self.replies is not None and st.prompt_len > 0:
+            st.reply_keys = prompt_keys(st.ids[:st.prompt_len])
+            ans = self.replies.get(st.reply_keys)
+            if ans is not None:
+                st.reply, st.rpos, st.run = ans, 0, 64     # a prompt hit ranks as a long match
+                self.reply_hits += 1
+                st.follow(st.ids[st.prompt_len:])
 
     def extend_stream(self, rid, ids):
-        self.streams[rid].ids += [int(t) for t in ids]
+        st = self.streams[rid]
+        ids = [int(t) for t in ids]
+        st.ids += ids
+        st.follow(ids)
 
     def end_stream(self, rid, add: bool = True):
         st = self.streams.pop(rid)
         if add and self.record is not None:
             self.record.add(st.ids)
+        if add and self.replies is not None and st.reply_keys:
+            self.replies.put(st.reply_keys, st.ids[st.prompt_len:])
 
     def observe_own(self, rid, landed: float, alpha: float = 0.25):
         """The stream's own draft model landed `landed` tokens this round (the bar a copy must reach)."""
@@ -558,13 +598,30 @@ class RecallEngine:
         cont = self.record.continuation(m[1], self.gamma)
         return (m[0], cont, m[1]) if cont.shape[0] else None
 
+    def _reply_candidate(self, st: _Stream):
+        if st.reply is None:
+            return None
+        out = st.ids[st.prompt_len:]
+        if st.rpos < 0:
+            st.rpos = realign(st.reply, out, len(out))
+            if st.rpos < 0:
+                return None
+            st.run = REALIGN_GRAM
+            self.realigns += 1
+        cont = st.reply[st.rpos:st.rpos + self.gamma]
+        return (max(st.run, WINDOW), cont) if cont.shape[0] else None
+
+    def _sources(self, st: _Stream):
+        return (('reply', self._reply_candidate(st)), ('own', self._own_candidate(st)),
+                ('record', self._record_candidate(st)))
+
     def propose(self, rid) -> Proposal | None:
         st = self.streams[rid]
         if st.cooldown > 0:
             st.cooldown -= 1
             return None
         cands = []
-        for src, cand in (('own', self._own_candidate(st)), ('record', self._record_candidate(st))):
+        for src, cand in self._sources(st):
             if cand is not None:
                 cands.append((self.expect(src, tier_of(cand[0])), src == 'own', src, cand))
         if not cands:
@@ -588,11 +645,11 @@ class RecallEngine:
         return p
 
     def candidates(self, rid) -> list[Proposal]:
-        """Every available copy of the stream (its own context's and the record's), without the offer rule: the
-        branches of a draft tree, which the target verifies in the same forward as the other drafts."""
+        """Every available copy of the stream (a filed reply's, its own context's and the record's), without the
+        offer rule: the branches of a draft tree, which the target verifies in the same forward as the other drafts."""
         st = self.streams[rid]
         out = []
-        for src, cand in (('own', self._own_candidate(st)), ('record', self._record_candidate(st))):
+        for src, cand in self._sources(st):
             if cand is not None:
                 out.append(Proposal(src, [int(t) for t in cand[1]], cand[0], tier_of(cand[0]), False,
                                     cand[2] if src == 'record' else -1))
@@ -626,13 +683,18 @@ class RecallEngine:
     def stats(self) -> dict:
         return dict(offers=self.offers, probes=self.probes, landed=self.landed,
                     expect={f'{s}/{t}': round(self.expect(s, t), 3) for s, t in self.sums},
-                    record=self.record.stats() if self.record is not None else None)
+                    record=self.record.stats() if self.record is not None else None,
+                    replies=(dict(self.replies.stats(), prompt_hits=self.reply_hits, realigns=self.realigns)
+                             if self.replies is not None else None))
+
+
+_SOURCE_CODE = {s: i for i, s in enumerate(RecallEngine.SOURCES)}
 
 
 def sync_proposal(prop: Proposal | None, group=None, src: int = 0) -> Proposal | None:
     """Every rank of `group` takes rank `src`'s proposal (tensor-parallel ranks must verify the same drafts; only
     `src` keeps a record and an engine). One broadcast of a small int64 tensor: [count, match, tier, probe, source,
-    ids...] padded to a fixed length."""
+    ids...] padded to a fixed length; the source is its index in `RecallEngine.SOURCES`."""
     import torch
     import torch.distributed as dist
     cap = 64
@@ -640,7 +702,7 @@ def sync_proposal(prop: Proposal | None, group=None, src: int = 0) -> Proposal |
     if dist.get_rank(group) == src if group is not None else dist.get_rank() == src:
         if prop is not None and prop.ids:
             ids = prop.ids[:cap]
-            buf[:5] = torch.tensor([len(ids), prop.match, prop.tier, int(prop.probe), int(prop.source == 'own')])
+            buf[:5] = torch.tensor([len(ids), prop.match, prop.tier, int(prop.probe), _SOURCE_CODE[prop.source]])
             buf[5:5 + len(ids)] = torch.tensor(ids)
         else:
             buf[0] = 0
@@ -648,7 +710,7 @@ def sync_proposal(prop: Proposal | None, group=None, src: int = 0) -> Proposal |
     n = int(buf[0])
     if n <= 0:
         return None
-    return Proposal('own' if int(buf[4]) else 'record', buf[5:5 + n].tolist(), int(buf[1]), int(buf[2]),
+    return Proposal(RecallEngine.SOURCES[int(buf[4])], buf[5:5 + n].tolist(), int(buf[1]), int(buf[2]),
                     bool(buf[3]))
 
 

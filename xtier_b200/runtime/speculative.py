@@ -225,7 +225,7 @@ class SpeculativeDecoder:
         self.seq = prompt.tolist() + [first]
         self.rid = object()
         if self.recall is not None:
-            self.recall.begin_stream(self.rid, self.seq)
+            self.recall.begin_stream(self.rid, self.seq, reply_from=T)
         if self.draft is not None and T > 1:
             self.draft.prefill(self.st_d, prompt[:-1])
         self.pos = T            # position of the last accepted token; the target holds KV for positions < pos

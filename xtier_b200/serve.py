@@ -222,6 +222,8 @@ class SpecBackend:
             snap.update(recall_offers=st['offers'], recall_landed=st['landed'], recall_probes=st['probes'])
             if st['record'] is not None:
                 snap['recall_record_ids'] = st['record']['ids']
+            if st['replies'] is not None:
+                snap.update(recall_reply_hits=st['replies']['prompt_hits'], recall_replies=st['replies']['entries'])
         return snap
 
 
