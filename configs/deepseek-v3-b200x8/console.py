@@ -1,19 +1,28 @@
-"""Console entry: the DeepSeek-V3-shaped model (61 layers, 256 MXFP4 experts) with its experts split over 8 B200s (EP=8).
-Listed for the EP benchmark tool; the generation server for this model is not wired yet (launches the EP layer
-benchmark instead)."""
+"""Console entry: the DeepSeek-V3-shaped model (61 layers, MLA, 256 MXFP4 experts, grouped sigmoid top-8; random-init
+weights). Two launches: the generation server on one B200 (the experts that do not fit in HBM on the CPU engine
+through the mailbox), or the EP=8 layer benchmark with the experts split over the node's GPUs."""
 
 MODEL = {
-    'id': 'deepseek-v3', 'order': 20, 'name': 'DeepSeek-V3 shape, EP=8 (config 3)', 'port': 18190, 'ready_timeout': 600,
-    'hardware': '8x B200, NVSwitch',
+    'id': 'deepseek-v3', 'order': 20, 'name': 'DeepSeek-V3 shape (configs 3-5)', 'port': 18190, 'ready_timeout': 1800,
+    'hardware': '1x B200 + host CPU engine, or 8x B200 over NVSwitch',
     'options': [
-        {'key': 'gpus', 'label': 'GPUs', 'default': '8', 'choices': [['8', '8'], ['4', '4'], ['2', '2']]},
-        {'key': 'tokens', 'label': 'tokens per rank', 'default': '4',
+        {'key': 'mode', 'label': 'launch', 'default': 'serve',
+         'choices': [['serve', 'generation server, 1 GPU, tiered experts'],
+                     ['ep', 'EP layer benchmark over several GPUs']]},
+        {'key': 'hot', 'label': 'GPU expert slots (serve)', 'default': '0.56',
+         'choices': [['0.56', '56% of each layer (fits one B200)'], ['0.4', '40%'], ['0.25', '25%']]},
+        {'key': 'gpus', 'label': 'GPUs (EP)', 'default': '8', 'choices': [['8', '8'], ['4', '4'], ['2', '2']]},
+        {'key': 'tokens', 'label': 'tokens per rank (EP)', 'default': '4',
          'choices': [['4', '4 (32 requests over 8 GPUs)'], ['16', '16']]},
     ],
 }
 
 
 def build(options, port):
+    """(argv, env) of the process for the chosen options."""
+    if options.get('mode', 'serve') == 'serve':
+        return (['python', '-m', 'xtier_b200.serve', '--model', 'deepseek-v3', '--hot', options['hot'],
+                 '--port', str(port)], {})
     argv = ['python', '-m', 'torch.distributed.run', '--nnodes=1', f"--nproc-per-node={options['gpus']}",
             '--master-addr', '127.0.0.1', '--master-port', str(port), '-m', 'xtier_b200.tools.ep_bench',
             '--tokens', options['tokens']]

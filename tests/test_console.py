@@ -106,3 +106,23 @@ def test_stages_and_telemetry_read_back():
     assert core.why_down(text) == '[xtier_b200] FATAL: RuntimeError: no CUDA device'
     assert core.why_down('ok\nnothing here\n') == ''
     assert core.why_down('x\nRuntimeError: CUDA error: out of memory\n') == 'RuntimeError: CUDA error: out of memory'
+
+
+def test_oneshot_card_result(tmp_path):
+    cfg = tmp_path / 'cfg' / 'tool'
+    cfg.mkdir(parents=True)
+    (cfg / 'console.py').write_text(
+        "MODEL = {'id': 'tool', 'name': 'tool', 'port': 1, 'oneshot': True, 'options': []}\n"
+        "def build(options, port):\n"
+        "    return ['python', '-c', 'print(\"working\"); print(\\'{\"tok_s\": 22.2}\\')'], {}\n")
+    console = core.Console(tmp_path / 'state', config_dir=tmp_path / 'cfg')
+    console.start('tool', {})
+    ok, why = console.wait_ready(60)
+    assert ok and why == 'finished'
+    st = console.status()
+    assert not st['running'] and st['result'] == {'tok_s': 22.2} and 'down_reason' not in st
+    assert core.last_json('a\n{"x": 1}\nnot json {\n') == {'x': 1} and core.last_json('none') is None
+    cards = core.load_cards()
+    assert cards['deepseek-v3-three-tier']['oneshot'] and not cards['deepseek-v3'].get('oneshot')
+    argv, _ = cards['deepseek-v3']['build'](core.validate(cards['deepseek-v3'], {}), 18190)
+    assert argv[:4] == ['python', '-m', 'xtier_b200.serve', '--model'] and argv[4] == 'deepseek-v3'

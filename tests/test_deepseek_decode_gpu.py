@@ -217,3 +217,46 @@ def test_ep_shared_expert_in_pool(cuda_ops):
         assert _rel(out.cpu(), ref) < 2e-2, _rel(out.cpu(), ref)
     finally:
         comm.close()
+
+
+def test_chunked_prompt_prefill_and_served_decode(cuda_ops):
+    """A prompt longer than the EP exchange's tokens prefills in chunks (each a continuation over the BF16 latent
+    cache) and gives the logits of one pass; the server's backend (serve.GenBackend over the Generator, greedy, no
+    prefix reuse) then decodes the tokens of the eager forward."""
+    from xtier_b200 import serve
+    from xtier_b200.engine.mailbox import Mailbox
+    from xtier_b200.models.deepseek_v3 import DeepSeekV3Model
+    from xtier_b200.runtime.decode import Generator
+    cfg = _small_cfg()
+    toks = torch.randint(0, cfg.vocab, (20,), generator=torch.Generator().manual_seed(9)).cuda()
+    logits = {}
+    for chunk in (8, 32):
+        mb = Mailbox(cfg.hidden, timeout_s=10.0)
+        model = DeepSeekV3Model(cfg, device='cuda', seed=6, ep=True, gpu_experts=11, mailbox=mb, engine_threads=2,
+                                decode_tokens=chunk)
+        model.keep_bf16_cache = True
+        mb.start()
+        try:
+            st = model.alloc_state(1, 128)
+            _, logits[chunk] = model.prefill(st, toks, all_logits=True)
+            model.check()
+            if chunk == 8:
+                with pytest.raises(ValueError):
+                    model.prefill({'batch': 1}, toks)          # chunks without the BF16 latent cache
+                # eager greedy continuation from the same prompt
+                want, cur = [], int(logits[chunk][-1].argmax())
+                for i in range(4):
+                    want.append(cur)
+                    nxt = model.decode_tokens_step(st, torch.tensor([cur], device='cuda'),
+                                                   torch.zeros(1, dtype=torch.int32, device='cuda'))
+                    cur = int(nxt[0])
+                be = serve.GenBackend(model, Generator(model, batch=1, max_len=128), None, mb, prefix_cache=False)
+                got = [be.prefill(toks.tolist())] + [be.decode() for _ in range(3)]
+                be.check()
+                assert got[:2] == want[:2], (got, want)
+                be.gen.graph = None
+        finally:
+            mb.stop()
+            model.close()
+    assert logits[8].shape == logits[32].shape == (20, cfg.vocab)
+    assert _rel(logits[8], logits[32]) < 2e-2, _rel(logits[8], logits[32])

@@ -6,7 +6,9 @@ group (stopped with the whole group), its output goes to a log file the page tai
 /health endpoint. The last settings are kept in a small JSON file.
 
 The page's status also carries the server's startup stage (its stage log lines), the last telemetry line (requests,
-tokens, tok/s, queue, CPU tier calls) and, once it is down, why (its FATAL line or the last error).
+tokens, tok/s, queue, CPU tier calls) and, once it is down, why (its FATAL line or the last error). A card with
+'oneshot': True runs a measuring tool instead of a server: it is done when the process exits 0, and its result is the
+last JSON line it printed.
 
 Reference parity: xtier/console/core.py:372-601 (Console: start, stop, status, wait_ready), :294-370 (the log read back:
 loading progress, short log lines, why a server is down).
@@ -90,6 +92,18 @@ def short(line: str) -> str:
     return line[:240]
 
 
+def last_json(text: str) -> dict | None:
+    """The last line of `text` that is a JSON object (what a one-shot tool prints as its result)."""
+    for ln in reversed(text.splitlines()):
+        ln = ln.strip()
+        if ln.startswith('{') and ln.endswith('}'):
+            try:
+                return json.loads(ln)
+            except ValueError:
+                continue
+    return None
+
+
 def load_cards(config_dir: Path | None = None) -> dict:
     cards = {}
     for f in sorted((config_dir or ROOT / 'configs').glob('*/console.py')):
@@ -169,10 +183,16 @@ class Console:
         except Exception:
             return None
 
+    def oneshot(self) -> bool:
+        """The current card runs a tool that prints a result and exits (no server, no /health)."""
+        return bool(self.current and self.cards[self.current['model']].get('oneshot'))
+
     def wait_ready(self, timeout_s: float) -> tuple[bool, str]:
         t0 = time.time()
         while time.time() - t0 < timeout_s:
             if self.proc is None or self.proc.poll() is not None:
+                if self.oneshot() and self.proc is not None and self.proc.returncode == 0:
+                    return True, 'finished'
                 return False, 'the server exited'
             h = self.health()
             if h and h.get('ready'):
@@ -211,6 +231,8 @@ class Console:
             out['stage'] = progress(text)
             out['telemetry'] = telemetry(text)
             out['log'] = [short(ln) for ln in text.splitlines()[-8:] if ln.strip()]
-            if not running:
+            if not running and self.oneshot() and self.proc is not None and self.proc.returncode == 0:
+                out['result'] = last_json(text)
+            elif not running:
                 out['down_reason'] = why_down(text)
         return out

@@ -37,6 +37,7 @@ async function poll() {{
   if (s.running && s.stage && s.stage.phase !== 'ready') line += ` · ${{s.stage.label}} ${{s.stage.percent}} %`;
   if (s.running && s.telemetry) line += ` · ${{s.telemetry.tok_s.toFixed(1)}} tok/s, queue ${{s.telemetry.queue}}`;
   if (!s.running && s.down_reason) line += ` · stopped: ${{s.down_reason}}`;
+  if (!s.running && s.result) line += ` · result: ${{JSON.stringify(s.result).slice(0, 400)}}`;
   document.getElementById('status').textContent = line;
   const j = await (await fetch('/' + API.job)).json();
   document.getElementById('log').textContent = (j.log || s.log || []).join('\\n');

@@ -237,6 +237,7 @@ class DeepSeekV3Model:
         self.decode_tokens = decode_tokens
         self.gpu_plan, self.popularity, self.cold, self.ram_experts = gpu_plan, popularity, cold, ram_experts
         self.bigram = None   # tables.engram.BigramTable (attach_bigram)
+        self.keep_bf16_cache = False   # alloc_state keeps the BF16 latent cache too (continuations, chunked prompts)
         if gpu_plan is not None and (not ep or popularity is None):
             raise ValueError('gpu_plan places experts by popularity under expert parallelism')
 
@@ -423,6 +424,7 @@ class DeepSeekV3Model:
         the prefill of a continuation) is kept when the kernels do not attend or bf16_cache is set."""
         cfg = self.cfg
         kern = self.kernel_attention()
+        bf16_cache = bf16_cache or self.keep_bf16_cache
         st = dict(batch=batch, max_len=max_len,
                   lengths=torch.zeros(batch, dtype=torch.int32, device=self.device))
         if bf16_cache or not kern:
@@ -541,9 +543,10 @@ class DeepSeekV3Model:
         ops.linear(a, L['down'], out=out)
 
     # ------------------------------------------------------------------ forward
-    def forward(self, st: dict, tokens: torch.Tensor, rows: torch.Tensor, pos: torch.Tensor, decode: bool):
+    def forward(self, st: dict, tokens: torch.Tensor, rows: torch.Tensor, pos: torch.Tensor, decode: bool,
+                all_logits: bool = False):
         """tokens [T] (decode: one per row), rows [T] cache row, pos [T] position. Returns logits of the last token
-        (prefill) or of every token (decode)."""
+        (prefill) or of every token (decode, or all_logits)."""
         cfg = self.cfg
         residual = self.embed.index_select(0, tokens).contiguous()
         h = torch.empty_like(residual)
@@ -581,16 +584,34 @@ class DeepSeekV3Model:
             else:
                 self._mlp(L, h, blk)
         ops.add_rmsnorm(blk, residual, self.final_norm, h, cfg.eps)
-        x = h if decode else h[-1:]
+        x = h if decode or all_logits else h[-1:]
         return ops.linear(x.contiguous(), self.lm_head)
 
-    def prefill(self, st, tokens, row: int = 0):
+    def prefill(self, st, tokens, row: int = 0, start: int = 0, return_logits: bool = False,
+                all_logits: bool = False):
+        """Prompt `tokens` [T] of cache row `row` at positions start.. (start > 0 continues a cached prefix, which
+        needs the BF16 latent cache). Returns the greedy next token [1]; with return_logits also the last position's
+        logits [V], with all_logits every position's [T, V]."""
         T = tokens.shape[0]
-        pos = torch.arange(T, dtype=torch.int32, device=self.device)
-        rows = torch.full((T,), row, dtype=torch.int32, device=self.device)
-        logits = self.forward(st, tokens.to(self.device), rows, pos, decode=False)
-        st['lengths'][row] = T
-        return logits.argmax(-1)
+        tokens = tokens.to(self.device)
+        # expert parallelism: the exchange buffers (and the CPU tier's mailbox) hold ep.T tokens, so a longer prompt
+        # goes through in chunks, each a continuation of the cached prefix
+        step = self.ep.T if self.ep is not None else T
+        if step < T and 'cache' not in st:
+            raise ValueError(f'a prompt over {step} tokens prefills in chunks, which needs the BF16 latent cache '
+                             '(alloc_state(bf16_cache=True), or keep_bf16_cache = True before the Generator)')
+        parts = []
+        for a in range(0, T, step):
+            b = min(T, a + step)
+            pos = torch.arange(start + a, start + b, dtype=torch.int32, device=self.device)
+            rows = torch.full((b - a,), row, dtype=torch.int32, device=self.device)
+            parts.append(self.forward(st, tokens[a:b], rows, pos, decode=False, all_logits=all_logits))
+        logits = torch.cat(parts) if all_logits else parts[-1]
+        st['lengths'][row] = start + T
+        nxt = logits[-1:].argmax(-1)
+        if all_logits:
+            return nxt, logits
+        return (nxt, logits[-1]) if return_logits else nxt
 
     def decode_tokens_step(self, st, tokens, rows):
         """Eager decode of one token per row (plain forward); returns the greedy next tokens."""

@@ -3,6 +3,7 @@ measures).
 
     python -m xtier_b200.serve --model qwen3-moe [--layers 48] [--hot 0.4] [--max-len 8192] --port 18180
     python -m xtier_b200.serve --checkpoint DIR [--hot 0.4] ...       # a Hugging Face qwen3_moe checkpoint
+    python -m xtier_b200.serve --model deepseek-v3 [--layers 61] [--hot 0.56] ...   # DeepSeek-V3 shape, random init
     ... [--recall DIR|memory]        # speculative serving: Recall copy drafts verified by the target (one forward
                                      # per step, several tokens when a copy lands)
 
@@ -43,7 +44,7 @@ import threading
 import time
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 
-MODELS = ('qwen3-moe',)
+MODELS = ('qwen3-moe', 'deepseek-v3')
 MAX_BODY = 64 << 20
 
 
@@ -856,11 +857,43 @@ def make_handler(server: Server):
     return Handler
 
 
+def build_deepseek(args, stages: Stages):
+    """The DeepSeek-V3-shaped model (MLA over the NVFP4 latent cache, 256 MXFP4 experts with grouped sigmoid top-8
+    routing and a shared expert; random-init weights) on this GPU: `--hot` of each MoE layer's experts in HBM slots,
+    the rest in the CPU engine through the mailbox. One request at a time, greedy; a prompt prefills in one forward
+    and every token after it is a replay of the captured decode step."""
+    from .engine.mailbox import Mailbox
+    from .models.deepseek_v3 import DeepSeekV3Config, DeepSeekV3Model
+    from .runtime.decode import Generator
+    if args.checkpoint or args.sampling or args.batch > 1 or args.recall:
+        raise ValueError('deepseek-v3 serves random-init weights greedily, one request at a time '
+                         '(no --checkpoint, --sampling, --batch or --recall)')
+    cfg = DeepSeekV3Config(layers=args.layers or 61, attn='mla')
+    gpu = max(1, min(cfg.experts, round(args.hot * cfg.experts)))
+    mailbox = Mailbox(cfg.hidden) if gpu < cfg.experts else None
+    stages.set('weights')
+    # the exchange buffers take a prompt chunk of up to 32 tokens (the mailbox's limit); decode uses one
+    model = DeepSeekV3Model(cfg, device='cuda', seed=args.seed, ep=True, gpu_experts=gpu, mailbox=mailbox,
+                            decode_tokens=32)
+    model.keep_bf16_cache = True   # prompts prefill in chunks, each continuing the cached prefix
+    stages.set('pool')
+    if mailbox is not None:
+        mailbox.start()
+    stages.set('graphs')
+    gen = Generator(model, batch=1, max_len=args.max_len)
+    # no prefix reuse: the decode step writes only the NVFP4 latent cache, and a continuation prefill reads the BF16 one
+    be = GenBackend(model, gen, None, mailbox, prefix_cache=False)
+    be.prefill([0])        # captures the decode graph before the server says it is ready
+    return be
+
+
 def build(args, stages: Stages | None = None):
     from .engine.mailbox import Mailbox
     from .models.qwen3_moe import Qwen3MoeConfig, Qwen3MoeModel
     from .runtime.decode import Generator
     stages = stages or Stages(emit=lambda *a, **k: None)
+    if args.model == 'deepseek-v3':
+        return build_deepseek(args, stages)
     progress = lambda li, n: stages.set('weights', li, n)   # noqa: E731
     tok = None
     if args.checkpoint:
@@ -875,7 +908,7 @@ def build(args, stages: Stages | None = None):
         except Exception as e:   # noqa: BLE001 -- a checkpoint without tokenizer files serves token ids only
             print(f'[xtier_b200] no tokenizer ({type(e).__name__}); prompt_ids only', flush=True)
     else:
-        cfg = Qwen3MoeConfig(layers=args.layers)
+        cfg = Qwen3MoeConfig(layers=args.layers or 48)
         mailbox = Mailbox(cfg.hidden) if args.hot < 1.0 else None
         model = Qwen3MoeModel(cfg, device='cuda', seed=args.seed, hot_fraction=args.hot, mailbox=mailbox,
                               progress=progress)
@@ -914,8 +947,8 @@ def main(argv=None):
     ap.add_argument('--model', default='qwen3-moe', choices=MODELS)
     ap.add_argument('--checkpoint', default=None, help='a Hugging Face qwen3_moe checkpoint directory')
     ap.add_argument('--tokenizer', default=None, help='tokenizer directory (default: the checkpoint)')
-    ap.add_argument('--layers', type=int, default=48)
-    ap.add_argument('--hot', type=float, default=0.4)
+    ap.add_argument('--layers', type=int, default=None, help='decoder layers (default: 48 qwen3-moe, 61 deepseek-v3)')
+    ap.add_argument('--hot', type=float, default=0.4, help='fraction of each MoE layer\'s experts in HBM slots')
     ap.add_argument('--max-len', type=int, default=8192)
     ap.add_argument('--max-queue', type=int, default=8)
     ap.add_argument('--no-prefix-cache', action='store_true', help='prefill every prompt from its first token')
