@@ -24,8 +24,9 @@ def snapshot(model=None, mailbox=None, state: dict | None = None) -> dict:
             moe = L.get('moe') if isinstance(L, dict) else None
             if moe is None or getattr(moe, 'mailbox', None) is None:
                 continue
+            E = getattr(moe, 'E', None) or moe.comm.E     # TieredMoE, or EPMoE (experts of the exchange)
             try:
-                _, ls = mailbox.layer_stats(moe.layer, moe.E)
+                _, ls = mailbox.layer_stats(moe.layer, E)
             except KeyError:
                 continue
             routes = ls['cpu_routes'] + ls['gpu_routes']
