@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -210,13 +211,14 @@ def graph_launches(gen) -> dict:
             'own_kernels': len([k for k in counts if k.startswith('_ZN2xt')])}
 
 
-def plan_config3(cfg, world: int, B: int, max_len: int, torch, reserve_gb: float):
-    """HBM pool slots per rank and MoE layer: what fits beside the dense weights, the KV cache and the workspaces."""
+def plan_config3(cfg, world: int, B: int, max_len: int, torch, reserve_gb: float, stage_slots: int = 0):
+    """HBM pool slots per rank and MoE layer: what fits beside the dense weights, the KV cache, the workspaces and the
+    PCIe staging slots (shared by the layers)."""
     free, _ = torch.cuda.mem_get_info()
     nsel = (max_len + 127) // 128 * 128
     kv = B * max_len * 416 * cfg.layers
     ws = B * nsel * 1088 * 2 + B * (nsel // 128) * 128 * 514 * 4
-    spare = free - cfg.dense_bytes() - kv - ws - int(reserve_gb * GB)
+    spare = free - cfg.dense_bytes() - kv - ws - int(reserve_gb * GB) - stage_slots * cfg.expert_bytes()
     El = cfg.experts // world
     n = max(0, spare // (cfg.expert_bytes() * cfg.moe_layers()))
     return int(min(El, n)), free
@@ -237,6 +239,15 @@ def run_config3(args, ctx: Ctx) -> dict:
     max_len = (fill + args.warmup + 2 * args.steps + 8 + 127) // 128 * 128
     El = cfg.experts // world
     gpu_per_rank, free = plan_config3(cfg, world, B, max_len, torch, args.reserve_gb)
+    S = 0   # PCIe staging slots (with a CPU tier): explicit, or the share of the touched CPU-tier experts
+    if gpu_per_rank < El:
+        from xtier_b200 import config as xconfig
+        S = xconfig.get('XTIER_EP_PCIE_SLOTS') if args.pcie_slots == -2 else args.pcie_slots
+        if S < 0:
+            touched = (cfg.experts - world * gpu_per_rank) * (1.0 - (1.0 - cfg.top_k / cfg.experts) ** B)
+            S = math.ceil(xconfig.get('XTIER_EP_PCIE_SHARE') * touched)
+        if S:
+            gpu_per_rank, free = plan_config3(cfg, world, B, max_len, torch, args.reserve_gb, S)
     if gpu_per_rank < 1:
         raise SystemExit('bench: the dense weights and the KV cache leave no HBM for routed experts')
     cpu_per_layer = world * (El - gpu_per_rank)
@@ -256,7 +267,7 @@ def run_config3(args, ctx: Ctx) -> dict:
               f'({cpu_bytes / GB:.1f} GB per rank)', file=sys.stderr, flush=True)
     t0 = time.time()
     model = DeepSeekV3Model(cfg, device='cuda', seed=1234, ep=True, gpu_experts=gpu_per_rank, mailbox=mailbox,
-                            engine_threads=ctx.threads, decode_tokens=B, indexer=with_ttft)
+                            engine_threads=ctx.threads, decode_tokens=B, indexer=with_ttft, pcie_slots=S)
     if mailbox is not None:
         mailbox.start(cpu=ctx.place.dispatcher)
     os.sched_setaffinity(0, [ctx.place.main])   # main thread off the workers' CPUs
@@ -317,6 +328,7 @@ def run_config3(args, ctx: Ctx) -> dict:
             'cpu_tier_experts_per_layer': cpu_per_layer, 'cpu_tier_gb_per_rank': round(cpu_bytes / GB, 1),
             'hbm_expert_gb_per_rank': round(gpu_experts_bytes / GB, 1),
             'cpu_engine_threads': ctx.threads if cpu_per_layer else 0, 'cpu': cpu_model(), 'cpus': os.cpu_count(),
+            'pcie_staging_slots': model.pcie_slots,
             'kv': 'NVFP4 latent cache filled with random latent rows for the random prompts (prefill measured '
                   'separately)',
             'l2': 'inputs larger than L2: each step streams tens of GB of weights',
@@ -471,6 +483,9 @@ def main():
                     help='config 3: HBM kept free beside the dense weights, KV and workspaces')
     ap.add_argument('--hot', type=float, default=0.4, help='config 2: fraction of each layer\'s experts in HBM')
     ap.add_argument('--threads', type=int, default=0, help='CPU engine workers per rank (0: auto)')
+    ap.add_argument('--pcie-slots', type=int, default=-2,
+                    help='config 3 with a CPU tier: GPU staging slots for CPU-tier experts read over PCIe (-2: '
+                         'XTIER_EP_PCIE_SLOTS, -1: XTIER_EP_PCIE_SHARE of the touched CPU-tier experts, 0: off)')
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-peer', action='store_true', help='config 2, N > 1: no node-wide slot pool')
     ap.add_argument('--profile', type=int, default=0, help='print per-kernel device time of N graph replays and exit')

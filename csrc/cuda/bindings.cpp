@@ -122,7 +122,9 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
                const Tensor &w, const Tensor &slots, const Tensor &ws_logits, const Tensor &ws_count, int64_t k,
                int64_t mode, int64_t n_group, int64_t topk_group, bool renorm, double scale, int64_t layer,
                int64_t mailbox, const std::optional<Tensor> &active, const std::optional<Tensor> &logits_in,
-               const std::optional<Tensor> &cold_index, int64_t share_min, int64_t host_base) {
+               const std::optional<Tensor> &cold_index, int64_t share_min, int64_t host_base,
+               const std::optional<Tensor> &claim, const std::optional<Tensor> &claim_list,
+               const std::optional<Tensor> &claim_count, int64_t stage_max, int64_t stage_slot0) {
     cuda_contig(x, "x");
     cuda_contig(wr, "router weight");
     RouteParams p{};
@@ -137,8 +139,21 @@ void moe_route(const Tensor &x, const Tensor &wr, const std::optional<Tensor> &b
     p.cold_index = optr<const int32_t>(cold_index);
     p.share_min = int(share_min);
     p.host_base = int(host_base);
-    if (cold_index) check(cold_index->scalar_type() == at::kInt && cold_index->numel() >= wr.size(0) && host_base > 0,
-                          "cold_index: int32 [E] and a positive host_base");
+    if (cold_index)
+        check(cold_index->scalar_type() == at::kInt && cold_index->numel() >= wr.size(0) &&
+                  (host_base > 0 || share_min == 0),
+              "cold_index: int32 [E] and a positive host_base");
+    p.stage_max = int(stage_max);
+    if (stage_max > 0) {
+        check(cold_index && claim && claim_list && claim_count && !logits_in, "PCIe staging: cold_index and claims");
+        check(claim->scalar_type() == at::kInt && claim->numel() >= wr.size(0) && claim_list->numel() >= wr.size(0) &&
+                  claim_count->numel() >= 1,
+              "PCIe staging: claim and claim_list int32 [E], claim_count [1]");
+        p.claim = ptr<int32_t>(*claim);
+        p.claim_list = ptr<int32_t>(*claim_list);
+        p.claim_count = ptr<int32_t>(*claim_count);
+        p.stage_slot0 = int(stage_slot0);
+    }
     if (logits_in)
         check(logits_in->scalar_type() == at::kFloat && logits_in->numel() >= x.size(0) * wr.size(0) && mailbox == 0,
               "logits_in: fp32 [m, E], no mailbox");
@@ -375,7 +390,10 @@ void ep_moe(const Tensor &x, const Tensor &ids, const Tensor &w, const Tensor &p
             const Tensor &mid, const Tensor &w13, const Tensor &s13, const Tensor &g13, const Tensor &w2,
             const Tensor &s2, const Tensor &g2, const std::optional<Tensor> &add, const Tensor &out, const Tensor &err,
             int64_t W, int64_t rank, int64_t E, int64_t fmt, int64_t R, std::vector<int64_t> offsets, double timeout_s,
-            int64_t phases, const std::optional<Tensor> &slots, int64_t spr, int64_t mailbox) {
+            int64_t phases, const std::optional<Tensor> &slots, int64_t spr, int64_t mailbox,
+            const std::optional<Tensor> &st_w13, const std::optional<Tensor> &st_s13,
+            const std::optional<Tensor> &st_w2, const std::optional<Tensor> &st_s2,
+            const std::optional<Tensor> &st_g13, const std::optional<Tensor> &st_g2, int64_t stage_base) {
     cuda_contig(x, "x");
     xt::EpParams p{};
     p.W = int(W);
@@ -421,11 +439,74 @@ void ep_moe(const Tensor &x, const Tensor &ids, const Tensor &w, const Tensor &p
     p.out = ptr<__nv_bfloat16>(out);
     p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
     p.error = ptr<int>(err);
+    if (stage_base > 0) {
+        check(st_w13 && st_s13 && st_w2 && st_s2 && st_g13 && st_g2 && p.slots, "ep: staging pools");
+        check(st_g13->scalar_type() == at::kFloat && st_g2->scalar_type() == at::kFloat, "ep: staging scales fp32");
+        p.st_w13 = ptr<const uint8_t>(*st_w13);
+        p.st_s13 = ptr<const uint8_t>(*st_s13);
+        p.st_w2 = ptr<const uint8_t>(*st_w2);
+        p.st_s2 = ptr<const uint8_t>(*st_s2);
+        p.st_g13 = ptr<const float>(*st_g13);
+        p.st_g2 = ptr<const float>(*st_g2);
+        p.stage_base = int(stage_base);
+    }
     check(p.T * p.k <= p.R, "ep: more routes than a receive region holds");
     check(mid.numel() >= int64_t(W) * R * p.I, "ep mid scratch too small");
     c10::cuda::CUDAGuard g(x.device());
     for (int ph = 0; ph < 4; ++ph)
         if ((phases >> ph) & 1) check_rc(xt_ep_moe(&p, ph, stream()), "ep_moe");
+}
+
+void ep_stage(const Tensor &claim_list, const Tensor &claim, const Tensor &claim_count, const Tensor &done,
+              const Tensor &cold_index, std::vector<int64_t> bases, int64_t stride, std::vector<int64_t> piece_off,
+              std::vector<int64_t> piece_bytes, const Tensor &w13, const Tensor &s13, const Tensor &w2,
+              const Tensor &s2, const Tensor &g13, const Tensor &g2, const Tensor &src_g13, const Tensor &src_g2,
+              int64_t I, int64_t H, int64_t fmt, int64_t chunks) {
+    xt::StageParams p{};
+    check(bases.size() >= 1 && bases.size() <= 8 && piece_off.size() == 6 && piece_bytes.size() == 6,
+          "ep_stage: 1-8 node bases and 6 pieces");
+    const int E = int(claim.numel());
+    check(claim.scalar_type() == at::kInt && claim_list.numel() >= E && cold_index.numel() >= E &&
+              claim_count.numel() >= 1 && done.numel() >= 1,
+          "ep_stage: claim tensors");
+    check(src_g13.scalar_type() == at::kFloat && src_g2.scalar_type() == at::kFloat && g13.scalar_type() == at::kFloat &&
+              g2.scalar_type() == at::kFloat,
+          "ep_stage: global scales fp32");
+    p.claim_list = ptr<const int32_t>(claim_list);
+    p.claim = ptr<int32_t>(claim);
+    p.claim_count = ptr<int32_t>(claim_count);
+    p.done = ptr<uint32_t>(done);
+    p.cold_index = ptr<const int32_t>(cold_index);
+    p.nodes = int(bases.size());
+    for (size_t n = 0; n < bases.size(); ++n) p.base[n] = static_cast<unsigned long long>(bases[n]);
+    p.stride = static_cast<unsigned long long>(stride);
+    for (int q = 0; q < 6; ++q) {
+        p.piece_off[q] = static_cast<unsigned long long>(piece_off[q]);
+        p.piece_bytes[q] = static_cast<unsigned long long>(piece_bytes[q]);
+    }
+    p.w13 = ptr<uint8_t>(w13);
+    p.s13 = ptr<uint8_t>(s13);
+    p.w2 = ptr<uint8_t>(w2);
+    p.s2 = ptr<uint8_t>(s2);
+    p.g13 = ptr<float>(g13);
+    p.g2 = ptr<float>(g2);
+    p.src_g13 = ptr<const float>(src_g13);
+    p.src_g2 = ptr<const float>(src_g2);
+    p.stage_max = int(w13.size(0));
+    p.E = E;
+    p.I = int(I);
+    p.H = int(H);
+    p.bs = fmt == 0 ? 16 : 32;
+    p.chunks = int(chunks);
+    const int64_t I_ = I, H_ = H, N = p.nodes;
+    const int64_t want[6] = {I_ / N * (H_ / 2), I_ / N * (H_ / 2), I_ / N * (H_ / p.bs), I_ / N * (H_ / p.bs),
+                             H_ / N * (I_ / 2), H_ / N * (I_ / p.bs)};
+    for (int q = 0; q < 6; ++q) check(piece_bytes[q] == want[q], "ep_stage: engine piece sizes differ from the pool");
+    check(w13.numel() == int64_t(p.stage_max) * 2 * I * (H / 2) && s13.numel() == int64_t(p.stage_max) * 2 * I * (H / p.bs) &&
+              w2.numel() == int64_t(p.stage_max) * H * (I / 2) && s2.numel() == int64_t(p.stage_max) * H * (I / p.bs),
+          "ep_stage: staging pool shapes");
+    c10::cuda::CUDAGuard g(w13.device());
+    check_rc(xt_ep_stage(&p, stream()), "ep_stage");
 }
 
 xt::TpParams tp_params(const Tensor &peer, const Tensor &state, const Tensor &out, const Tensor &err, int64_t M,
@@ -985,7 +1066,8 @@ TORCH_LIBRARY(xtier, m) {
     m.def("moe_route(Tensor x, Tensor wr, Tensor? bias, Tensor? corr, Tensor? table, Tensor? shared_slots, "
           "Tensor(a!) ids, Tensor(b!) w, Tensor(c!) slots, Tensor(d!) ws_logits, Tensor(e!) ws_count, int k, int mode, "
           "int n_group, int topk_group, bool renorm, float scale, int layer, int mailbox, Tensor? active=None, "
-          "Tensor? logits_in=None, Tensor? cold_index=None, int share_min=0, int host_base=0) -> ()");
+          "Tensor? logits_in=None, Tensor? cold_index=None, int share_min=0, int host_base=0, Tensor(f!)? claim=None, "
+          "Tensor(g!)? claim_list=None, Tensor(h!)? claim_count=None, int stage_max=0, int stage_slot0=0) -> ()");
     m.def("gemv(Tensor x, Tensor w, Tensor? add, Tensor(a!) out) -> ()");
     m.def("fp8_rows(Tensor tab, Tensor scales, Tensor? ids, int lo, int hi, int blk, Tensor(a!) out) -> ()");
     m.def("gemv_fp8(Tensor x, Tensor w, Tensor s, Tensor? add, Tensor(a!) out) -> ()");
@@ -998,7 +1080,12 @@ TORCH_LIBRARY(xtier, m) {
     m.def("ep_moe(Tensor x, Tensor ids, Tensor w, Tensor peer, Tensor(a!) state, Tensor(b!) mid, Tensor w13, "
           "Tensor s13, Tensor g13, Tensor w2, Tensor s2, Tensor g2, Tensor? add, Tensor(c!) out, Tensor(d!) err, "
           "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases, Tensor? slots=None, "
-          "int spr=0, int mailbox=0) -> ()");
+          "int spr=0, int mailbox=0, Tensor? st_w13=None, Tensor? st_s13=None, Tensor? st_w2=None, "
+          "Tensor? st_s2=None, Tensor? st_g13=None, Tensor? st_g2=None, int stage_base=0) -> ()");
+    m.def("ep_stage(Tensor claim_list, Tensor(a!) claim, Tensor(b!) claim_count, Tensor(c!) done, Tensor cold_index, "
+          "int[] bases, int stride, int[] piece_off, int[] piece_bytes, Tensor(d!) w13, Tensor(e!) s13, "
+          "Tensor(f!) w2, Tensor(g!) s2, Tensor(h!) g13, Tensor(i!) g2, Tensor src_g13, Tensor src_g2, int I, int H, "
+          "int fmt, int chunks) -> ()");
     m.def("l2_prefetch(Tensor ptrs, Tensor bytes, int ctas) -> ()");
     m.def("dsa_key_write(Tensor k, Tensor slot, Tensor(a!) codes, Tensor(b!) kscale) -> ()");
     m.def("dsa_index_decode(Tensor q, Tensor w, Tensor codes, Tensor kscale, Tensor base, Tensor len, "
@@ -1048,6 +1135,7 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("qk_norm_rope_kv", &qk_norm_rope_kv);
     m.impl("attn_decode", &attn_decode);
     m.impl("moe_route", &moe_route);
+    m.impl("ep_stage", &ep_stage);
     m.impl("moe_gate_up", &moe_gate_up);
     m.impl("moe_down", &moe_down);
     m.impl("gemv", &gemv);

@@ -64,4 +64,27 @@ int xt_host_ptr_mapped(const void *ptr) {
     return (a.type == cudaMemoryTypeHost && a.devicePointer == ptr) ? 1 : 0;
 }
 
+// Page-locks host memory another allocator owns (the CPU engine's weight shards) and maps it for kernels: *dev is the
+// address kernels read it through. 0 or the CUDA error code (nothing stays registered on an error).
+int xt_host_register_mapped(void *ptr, size_t bytes, void **dev) {
+    cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return int(e);
+    }
+    e = cudaHostGetDevicePointer(dev, ptr, 0);
+    if (e != cudaSuccess) {
+        cudaHostUnregister(ptr);
+        cudaGetLastError();
+        return int(e);
+    }
+    return 0;
+}
+
+int xt_host_unregister(void *ptr) {
+    const cudaError_t e = cudaHostUnregister(ptr);
+    if (e != cudaSuccess) cudaGetLastError();
+    return int(e);
+}
+
 }  // extern "C"

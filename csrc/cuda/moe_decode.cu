@@ -166,6 +166,24 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteParam
     }
 }
 
+// PCIe staging claim of expert e by one route: the first route of the call to name e takes the next staging index (or
+// marks e "no room" past stage_max) and records e in claim order; a route that finds e being claimed waits (bounded)
+// for the index. Negative: the route stays on the CPU tier (also when the wait runs out: the CPU then computes this
+// token's route, the staged copy serves the others).
+XT_DEV int stage_claim(const RouteParams &p, int e) {
+    int v = atomicCAS(&p.claim[e], -1, -2);
+    if (v == -1) {
+        const int s = atomicAdd(p.claim_count, 1);
+        if (s < p.E) p.claim_list[s] = e;
+        const int r = s < p.stage_max ? s : -3;
+        __threadfence();
+        atomicExch(&p.claim[e], r);
+        return r;
+    }
+    for (int i = 0; v == -2 && i < (1 << 16); ++i) v = *reinterpret_cast<volatile int *>(&p.claim[e]);
+    return v;
+}
+
 // Decode router, one cluster of ROUTE_CLUSTER CTAs per token (blockIdx.y): every warp of the cluster computes whole
 // expert rows (16-byte loads, all of a row's loads in flight, FP32 sums) and stores the logit straight into the
 // leader CTA's shared memory (st.shared::cluster); one cluster barrier (release / acquire) hands them over, and the
@@ -263,6 +281,10 @@ __global__ void __cluster_dims__(ROUTE_CLUSTER, 1, 1) __launch_bounds__(ROUTE_TH
                 const int ci = p.cold_index[e];
                 if (ci >= 0) slot = p.host_base + ci;
             }
+        }
+        if (p.stage_max > 0 && lane < p.k && slot < 0 && e >= 0 && p.cold_index[e] >= 0) {
+            const int s = stage_claim(p, e);   // PCIe staging: the GPU computes it from a staged copy
+            if (s >= 0) slot = p.stage_slot0 + s;
         }
         if (lane < kk) {
             const size_t o = size_t(t) * kk + lane;
@@ -969,9 +991,11 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_gate_up_stream(EpParams p, 
                 e = reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x;
                 cur = r;
             }
-            const size_t g0 = size_t(e) * 2 * p.I + size_t(rb) * half, u0 = g0 + p.I;
-            const fs::Run runs[2] = {{p.w13 + g0 * geo.wrow, p.s13 + g0 * geo.srow, half, 0},
-                                     {p.w13 + u0 * geo.wrow, p.s13 + u0 * geo.srow, half, half}};
+            const bool st = p.stage_base > 0 && e >= p.stage_base;   // a staging slot (host copy brought over PCIe)
+            const uint8_t *w13 = st ? p.st_w13 : p.w13, *s13 = st ? p.st_s13 : p.s13;
+            const size_t g0 = size_t(st ? e - p.stage_base : e) * 2 * p.I + size_t(rb) * half, u0 = g0 + p.I;
+            const fs::Run runs[2] = {{w13 + g0 * geo.wrow, s13 + g0 * geo.srow, half, 0},
+                                     {w13 + u0 * geo.wrow, s13 + u0 * geo.srow, half, half}};
             if (!fs::produce(ring, geo, runs, 2, cur_ring, filled)) break;
         }
         fs::produce_drain(ring, geo, filled);
@@ -995,8 +1019,10 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_gate_up_stream(EpParams p, 
             ep_locate(p, off, r, s, slot);
             fs::lane_load_x(L, reinterpret_cast<const __half *>(me + p.off_rx + size_t(slot) * p.H * 2));
             const int e = reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x;
-            gg = p.g13[2 * e];
-            gu = p.g13[2 * e + 1];
+            const bool stg = p.stage_base > 0 && e >= p.stage_base;
+            const float *g13 = stg ? p.st_g13 + 2 * (e - p.stage_base) : p.g13 + 2 * e;
+            gg = g13[0];
+            gu = g13[1];
             cur = r;
         }
         float v;
@@ -1045,8 +1071,10 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_down_stream(EpParams p, fs:
                 e = reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16)->x;
                 cur = r;
             }
-            const size_t row0 = size_t(e) * p.H + size_t(hb) * geo.R;
-            const fs::Run run = {p.w2 + row0 * geo.wrow, p.s2 + row0 * geo.srow, geo.R, 0};
+            const bool st = p.stage_base > 0 && e >= p.stage_base;
+            const size_t row0 = size_t(st ? e - p.stage_base : e) * p.H + size_t(hb) * geo.R;
+            const fs::Run run = {(st ? p.st_w2 : p.w2) + row0 * geo.wrow, (st ? p.st_s2 : p.s2) + row0 * geo.srow,
+                                 geo.R, 0};
             if (!fs::produce(ring, geo, &run, 1, cur_ring, filled)) break;
         }
         fs::produce_drain(ring, geo, filled);
@@ -1067,7 +1095,8 @@ __global__ void __launch_bounds__(fs::THREADS, 1) ep_down_stream(EpParams p, fs:
                 ep_locate(p, off, r, s, slot);
                 fs::lane_load_x(L, p.mid + size_t(slot) * p.I);
                 const int4 m = *reinterpret_cast<const int4 *>(me + p.off_meta + size_t(slot) * 16);
-                wt = __int_as_float(m.w) * p.g2[m.x];
+                wt = __int_as_float(m.w) *
+                     (p.stage_base > 0 && m.x >= p.stage_base ? p.st_g2[m.x - p.stage_base] : p.g2[m.x]);
                 dst_row = reinterpret_cast<float *>(ep_buf(p, s) + p.off_ret) + (size_t(m.y) * p.k + m.z) * p.H;
                 cur = r;
             }

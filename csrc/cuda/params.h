@@ -23,6 +23,12 @@ struct RouteParams {
     // GPU instead, which reads that expert from pinned host memory (slot = host_base + cold_index[expert])
     const int32_t *cold_index;
     int share_min, host_base;
+    // PCIe staging (may be null / 0; expert parallelism): a CPU-tier route whose expert has a host copy the GPU can
+    // read (cold_index >= 0) claims one of stage_max staging slots and becomes GPU slot stage_slot0 + index. claim [E]
+    // (-1 free, -2 being claimed, -3 no room, else the staging index), claim_list [E] (the experts in claim order),
+    // claim_count [1]; the staging copy kernel reads them and resets them for the next call
+    int32_t *claim, *claim_list, *claim_count;
+    int stage_max, stage_slot0;
     int32_t *ids;             // [m, kk] original expert ids (-1 for shared)
     float *w;                 // [m, kk]
     int32_t *slots;           // [m, kk] GPU slot or -1
@@ -164,6 +170,30 @@ struct EpParams {
     XtMailbox mb;
     int use_mb;
     int by_expert;   // expert streams visit the received routes grouped by pool slot (0: arrival order)
+    // PCIe staging (may be null / 0): local slots >= stage_base name staging slot (slot - stage_base), whose weights
+    // the staging copy kernel brought from host memory earlier in the same call
+    const uint8_t *st_w13, *st_s13, *st_w2, *st_s2;
+    const float *st_g13, *st_g2;
+    int stage_base;
+};
+
+// The staging copy (csrc/cuda/ep_stage.cu): the experts the router claimed, from the CPU engine's host memory (mapped,
+// read over PCIe) into the GPU staging slots. An engine slot keeps its expert as 6 pieces per NUMA node (gate codes,
+// up codes, gate scales, up scales, down codes, down scales; node n holds rows [n*I/N, (n+1)*I/N) of gate and up and
+// [n*H/N, (n+1)*H/N) of down).
+struct StageParams {
+    const int32_t *claim_list;   // [E]
+    int32_t *claim;              // [E]
+    int32_t *claim_count;        // [1]
+    uint32_t *done;              // [1] CTAs finished (the last one resets the claims)
+    const int32_t *cold_index;   // [E] engine slot of the expert, or -1
+    unsigned long long base[8];  // device address of each node's shard
+    unsigned long long stride;   // bytes per engine slot in a shard
+    unsigned long long piece_off[6], piece_bytes[6];
+    uint8_t *w13, *s13, *w2, *s2;   // staging [stage_max, ...] in the pool layout
+    float *g13, *g2;                // [stage_max, 2], [stage_max]
+    const float *src_g13, *src_g2;  // global scales by engine slot: [slots, 2], [slots]
+    int nodes, stage_max, E, I, H, bs, chunks;
 };
 
 // Per-head small GEMM of the MLA decode step (csrc/cuda/mla_proj.cu).
@@ -181,6 +211,7 @@ struct HeadGemmParams {
 }  // namespace xt
 
 extern "C" int xt_ep_moe(const xt::EpParams *p, int phase, cudaStream_t stream);
+extern "C" int xt_ep_stage(const xt::StageParams *p, cudaStream_t stream);
 
 namespace xt {
 // Tensor-parallel GEMMs fused with their collective (csrc/cuda/gemm_tp.cu).

@@ -953,6 +953,21 @@ int xt_engine_slot_pieces(void *plan, int slot, int node, void **ptrs, size_t *b
     return 0;
 }
 
+int xt_engine_shard(void *plan, int node, void **base, size_t *bytes, size_t *stride, size_t *piece_off,
+                    size_t *piece_bytes) {
+    Plan *p = static_cast<Plan *>(plan);
+    if (!p || node < 0 || node >= p->nodes) return -1;
+    const Shard &s = p->shards[node];
+    *base = s.base;
+    *bytes = s.bytes;
+    *stride = s.stride;
+    for (int q = 0; q < 6; ++q) {
+        piece_off[q] = s.piece_off[q];
+        piece_bytes[q] = s.piece_bytes[q];
+    }
+    return 0;
+}
+
 int xt_engine_nodes(void *plan) {
     Plan *p = static_cast<Plan *>(plan);
     return p ? p->nodes : -1;

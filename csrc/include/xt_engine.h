@@ -60,6 +60,10 @@ void xt_engine_slot_unpin(void *plan, int slot);
 // Six pieces of a slot on worker node `node`: gate, up, gate scales, up scales, down, down scales. 0 or -1.
 int xt_engine_slot_pieces(void *plan, int slot, int node, void **ptrs, size_t *bytes);
 int xt_engine_nodes(void *plan);
+// The whole shard of worker node `node`: base address and bytes (every slot, routed and shared), the bytes between two
+// slots, and the six pieces' offsets inside a slot and sizes. 0 or -1.
+int xt_engine_shard(void *plan, int node, void **base, size_t *bytes, size_t *stride, size_t *piece_off,
+                    size_t *piece_bytes);
 // Cold experts: forward reads experts that are not in a RAM slot from the store before computing them.
 // files/offsets [experts * nodes]: record of expert e's node part n (file -1: never cold). scores: initial use counts.
 int xt_engine_cold_attach(void *plan, void *store, const int32_t *files, const long long *offsets, const float *scores,

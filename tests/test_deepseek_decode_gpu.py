@@ -157,7 +157,7 @@ def test_batched_decode_step_matches_forward(cuda_ops):
     cfg = _small_cfg()
     mb = Mailbox(cfg.hidden, timeout_s=10.0)
     model = DeepSeekV3Model(cfg, device='cuda', seed=2, ep=True, gpu_experts=11, mailbox=mb, engine_threads=2,
-                            decode_tokens=8)
+                            decode_tokens=8, pcie_slots=0)   # every CPU-tier route on the engine
     mb.start()
     try:
         B, L0 = 3, 40
@@ -260,3 +260,53 @@ def test_chunked_prompt_prefill_and_served_decode(cuda_ops):
             model.close()
     assert logits[8].shape == logits[32].shape == (20, cfg.vocab)
     assert _rel(logits[8], logits[32]) < 2e-2, _rel(logits[8], logits[32])
+
+
+def test_pcie_staging_matches_cpu_tier(cuda_ops):
+    """PCIe staging: the router hands up to 4 of the CPU-tier experts per call to the GPU, which copies them from the
+    engine's own (CUDA-registered) host memory and computes them; the decode step's logits match the same model with
+    every CPU-tier route on the engine, the claims are reset after every call, GPU routes grow, and the captured step
+    replays the same tokens."""
+    from xtier_b200.engine.mailbox import Mailbox
+    from xtier_b200.models.deepseek_v3 import DeepSeekV3Model
+    from xtier_b200.runtime.decode import Generator
+    cfg = _small_cfg()
+    B, L0 = 4, 40
+    toks = torch.randint(0, cfg.vocab, (B,), generator=torch.Generator().manual_seed(5)).cuda()
+    res = {}
+    for S in (0, 4):
+        mb = Mailbox(cfg.hidden, timeout_s=10.0)
+        model = DeepSeekV3Model(cfg, device='cuda', seed=8, ep=True, gpu_experts=6, mailbox=mb, engine_threads=2,
+                                decode_tokens=8, pcie_slots=S)
+        mb.start()
+        try:
+            assert model.pcie_slots == S and (S == 0 or len(model.host_maps) == len(model.engines))
+            st = model.alloc_state(B, 256)
+            model.fill_synthetic_cache(st, L0, seed=2)
+            buf = model.decode_buffers(B)
+            buf['tokens'].copy_(toks)
+            buf['pos'].fill_(L0)
+            model.decode_step(st, buf)
+            torch.cuda.synchronize()
+            model.check(st)
+            layer = next(L['moe'] for L in model.layers if 'moe' in L)
+            _, ls = mb.layer_stats(layer.layer, cfg.experts)
+            res[S] = (buf['logits'].float().clone(), buf['next'].clone(), ls['gpu_routes'], ls['cpu_routes'])
+            if S:
+                assert bool((model.ep.claim == -1).all()) and int(model.ep.claim_count) == 0
+                gen = Generator(model, batch=B, max_len=256)
+                gen.state, gen.buf = st, buf
+                buf['tokens'].copy_(toks)
+                buf['pos'].fill_(L0)
+                gen.capture()
+                for _ in range(2):
+                    gen.step()
+                torch.cuda.synchronize()
+                gen.check()
+                assert bool((model.ep.claim == -1).all()) and int(model.ep.claim_count) == 0
+                gen.graph = None
+        finally:
+            mb.stop()
+            model.close()
+    assert _rel(res[4][0], res[0][0]) < 3e-2, _rel(res[4][0], res[0][0])
+    assert res[4][2] > res[0][2] and res[4][3] < res[0][3], (res[0][2:], res[4][2:])

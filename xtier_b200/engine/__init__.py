@@ -55,6 +55,7 @@ def lib():
         L.xt_engine_slot_unpin.argtypes = [_P, _I]
         L.xt_engine_slot_pieces.argtypes = [_P, _I, _I, _P, _P]
         L.xt_engine_nodes.argtypes = [_P]
+        L.xt_engine_shard.argtypes = [_P, _I, _P, _P, _P, _P, _P]
         L.xt_engine_cold_attach.argtypes = [_P, _P, _P, _P, _P, _F]
         L.xt_engine_cold_attach_pieces.argtypes = [_P, _P, _P, _P, _P, _F]
         L.xt_engine_cold_stats.argtypes = [_P, _P]
@@ -224,6 +225,15 @@ class CpuEngine:
         if lib().xt_engine_slot_pieces(self.plan, slot, node, ptrs, sizes) != 0:
             raise IndexError(f'slot {slot} node {node}')
         return list(ptrs), list(sizes)
+
+    def shard(self, node: int) -> dict:
+        """Node `node`'s shard: base address, bytes, slot stride, the six pieces' offsets and sizes in a slot."""
+        base, nbytes, stride = C.c_void_p(), C.c_size_t(), C.c_size_t()
+        off, sizes = (C.c_size_t * 6)(), (C.c_size_t * 6)()
+        if lib().xt_engine_shard(self.plan, node, C.byref(base), C.byref(nbytes), C.byref(stride), off, sizes) != 0:
+            raise IndexError(f'node {node}')
+        return dict(base=base.value or 0, bytes=nbytes.value, stride=stride.value, piece_off=list(off),
+                    piece_bytes=list(sizes))
 
     def write_slot(self, slot: int, ew: ExpertWeights, e: int):
         """Copies expert e of `ew` into RAM slot `slot` (all nodes), e.g. after reading it from a checkpoint."""

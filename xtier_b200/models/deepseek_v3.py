@@ -213,7 +213,7 @@ class DeepSeekV3Model:
                  ep: bool = False, gpu_experts: int | None = None, mailbox=None, engine_threads: int | None = None,
                  decode_tokens: int = 16, ep_timeout_s: float = 30.0, indexer: bool = False,
                  gpu_plan: dict | None = None, popularity: dict | None = None, cold=None,
-                 ram_experts: int | None = None, plan_fn=None):
+                 ram_experts: int | None = None, plan_fn=None, pcie_slots: int | None = None):
         """moe_factory(layer, router_w, corr_bias, experts_fn, shared_experts) -> an MoE layer with .forward(x, out);
         experts_fn(ids) generates the quantized experts (synthetic MXFP4 bytes) of the given expert ids.
         Default: every expert on this GPU (TieredMoE, all hot).
@@ -226,13 +226,18 @@ class DeepSeekV3Model:
         cache.cold.ColdPool) the CPU engine of a layer keeps `ram_experts` of the rest in RAM and reads the others
         from the cold store on demand (rank 0 writes the layer's records, the other ranks fill their RAM slots from
         them). `plan_fn({layer: (router_w, corr_bias)}) -> (gpu_plan, popularity)` computes both once every
-        layer's router exists."""
+        layer's router exists.
+        pcie_slots (ep with a RAM-only CPU tier; default XTIER_EP_PCIE_SLOTS): GPU staging slots, shared by the
+        layers, for CPU-tier experts the GPU reads from the engine's own host memory over PCIe while the engine
+        computes the others (the engine's shards are registered with CUDA)."""
         self.cfg = cfg
         dev = self.device = torch.device(device)
         g = torch.Generator(device='cpu').manual_seed(seed)
         H = cfg.hidden
         self.mailbox = mailbox
         self.engines = []
+        self.host_maps = []   # engine shards registered with CUDA (unregistered before the engines go)
+        self.pcie_slots = 0
         self.ep = None
         self.decode_tokens = decode_tokens
         self.gpu_plan, self.popularity, self.cold, self.ram_experts = gpu_plan, popularity, cold, ram_experts
@@ -296,8 +301,16 @@ class DeepSeekV3Model:
                 self.gpu_per_rank = El if gpu_experts is None else max(1, min(El, int(gpu_experts)))
                 if self.gpu_per_rank < El and mailbox is None:
                     raise ValueError('a CPU tier (gpu_experts < experts per rank) needs a mailbox')
+            from .. import config
+            S = config.get('XTIER_EP_PCIE_SLOTS') if pcie_slots is None else int(pcie_slots)
+            if S < 0:   # a share of the CPU-tier experts one call's routes are expected to touch
+                n_cpu = max(0, cfg.experts - env.world * self.gpu_per_rank)
+                touched = n_cpu * (1.0 - (1.0 - cfg.top_k / cfg.experts) ** decode_tokens)
+                S = math.ceil(config.get('XTIER_EP_PCIE_SHARE') * touched)
+            self.pcie_slots = S if (mailbox is not None and cold is None) else 0
             self.ep = EPComm(H, cfg.inter, cfg.experts, cfg.top_k, decode_tokens, dev, timeout_s=ep_timeout_s,
-                             slots_per_rank=self.gpu_per_rank + cfg.shared, n_shared=cfg.shared)
+                             slots_per_rank=self.gpu_per_rank + cfg.shared + self.pcie_slots, n_shared=cfg.shared,
+                             stage_slots=self.pcie_slots, stage_fmt=cfg.fmt)
             self.ep_rank, self.ep_world = env.rank, env.world
         for li, router, corr, shared, seed_l in pending:
             L = self.layers[li]
@@ -339,7 +352,7 @@ class DeepSeekV3Model:
                                     mine, seed_l, cfg.std)
         for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):   # slots a ranked plan leaves empty on this rank
             getattr(local, f)[len(mine):].zero_()
-        engine = None
+        engine = pcie = None
         if cpu_ids and self.cold is not None:
             engine = self._cold_engine(li, cpu_ids, seed_l, threads)
             self.engines.append(engine)
@@ -352,20 +365,49 @@ class DeepSeekV3Model:
             # slots filled chunk by chunk (no host copy of a whole layer); the CPU tier's bytes are the same on every
             # rank (every rank's engine holds all of them)
             engine = CpuEngine(stage, threads=threads, slots=n, resident=cpu_ids, total_experts=E, fill=False)
+            g13 = torch.empty(n, 2, dtype=torch.float32, device=self.device)
+            g2 = torch.empty(n, dtype=torch.float32, device=self.device)
             for s in range(0, n, chunk):
                 e = min(n, s + chunk)
                 tmp = empty_experts(e - s, H, I, cfg.fmt, self.device)
                 synthetic_experts_by_id(tmp, cpu_ids[s:e], seed_l, cfg.std)
+                g13[s:e].copy_(tmp.g13.float())
+                g2[s:e].copy_(tmp.g2.float())
                 for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):
                     getattr(stage, f)[:e - s].copy_(getattr(tmp, f))
                 del tmp
                 for j in range(e - s):
                     engine.write_slot(s + j, stage, j)
             self.engines.append(engine)
+            if self.pcie_slots:
+                pcie = self._map_engine(engine, cpu_ids, g13, g2)
         moe = EPMoE(li, self.ep, router, local, cfg.top_k, shared=shared, mode=1, n_group=cfg.n_group,
                     topk_group=cfg.topk_group, renorm=True, scale=cfg.routed_scale, corr_bias=corr,
-                    table=table, mailbox=self.mailbox, engine=engine)
+                    table=table, mailbox=self.mailbox, engine=engine, stage=pcie)
         return moe, stage
+
+    def _map_engine(self, engine, cpu_ids: list, g13: torch.Tensor, g2: torch.Tensor) -> dict | None:
+        """The engine's weight shards registered with CUDA and mapped for kernels (the PCIe staging reads them in
+        place): the `stage` description of EPMoE, or None (with a warning) when the registration is refused."""
+        import ctypes as C
+        L = ops.cdll()
+        L.xt_host_register_mapped.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p]
+        bases, sh = [], None
+        for node in range(engine.nodes()):
+            sh = engine.shard(node)
+            dev = C.c_void_p()
+            rc = L.xt_host_register_mapped(C.c_void_p(sh['base']), C.c_size_t(sh['bytes']), C.byref(dev))
+            if rc != 0:
+                import logging
+                logging.getLogger('xtier_b200').warning(f'PCIe staging off for this layer: cudaHostRegister of the '
+                                                        f'engine shard refused (error {rc})')
+                return None
+            self.host_maps.append(sh['base'])
+            bases.append(dev.value)
+        idx = torch.full((self.cfg.experts,), -1, dtype=torch.int32)
+        idx[torch.as_tensor(cpu_ids, dtype=torch.long)] = torch.arange(len(cpu_ids), dtype=torch.int32)
+        return dict(cold_index=idx, bases=bases, stride=sh['stride'], piece_off=sh['piece_off'],
+                    piece_bytes=sh['piece_bytes'], src_g13=g13, src_g2=g2)
 
     def attach_bigram(self, table):
         """Adds a hashed-bigram NVMe embedding table (tables/engram.py; rows projected to the hidden size) to the
@@ -711,6 +753,14 @@ class DeepSeekV3Model:
             self.bigram.check()
 
     def close(self):
+        if self.host_maps:
+            import ctypes as C
+            torch.cuda.synchronize()
+            L = ops.cdll()
+            L.xt_host_unregister.argtypes = [C.c_void_p]
+            for base in self.host_maps:
+                L.xt_host_unregister(C.c_void_p(base))
+            self.host_maps = []
         for e in self.engines:
             e.close()
         self.engines = []

@@ -81,12 +81,16 @@ def attn_prefill(q, k_cache, v_cache, row: int, start: int, scale: float, out=No
 def moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k: int, mode: int = 0,
               n_group: int = 1, topk_group: int = 1, renorm: bool = True, scale: float = 1.0, layer: int = 0,
               mailbox: int = 0, active=None, logits_in=None, cold_index=None, share_min: int = 0,
-              host_base: int = 0):
+              host_base: int = 0, claim=None, claim_list=None, claim_count=None, stage_max: int = 0,
+              stage_slot0: int = 0):
     """`active` (int32 [m], optional): token flags; a token with flag 0 skips its routed experts (GPU and CPU),
     e.g. a verify token after a truncated draft. `logits_in` (fp32 [m, E], prefill): precomputed router logits; the
-    kernel only selects (one CTA per token)."""
+    kernel only selects (one CTA per token). `stage_max` > 0 (expert parallelism): a CPU-tier route whose expert has an
+    engine slot (`cold_index` >= 0) claims one of stage_max PCIe staging slots (`claim` / `claim_list` / `claim_count`,
+    reset by `ep_stage`) and becomes GPU slot stage_slot0 + index."""
     _ops().moe_route(x, wr, bias, corr, table, shared_slots, ids, w, slots, ws_logits, ws_count, k, mode, n_group,
-                     topk_group, renorm, scale, layer, mailbox, active, logits_in, cold_index, share_min, host_base)
+                     topk_group, renorm, scale, layer, mailbox, active, logits_in, cold_index, share_min, host_base,
+                     claim, claim_list, claim_count, stage_max, stage_slot0)
 
 
 def gemm_f32(a, b, out=None):

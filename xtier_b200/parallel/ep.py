@@ -32,10 +32,13 @@ from .symm import SymmetricBuffer
 
 class EPComm:
     def __init__(self, hidden: int, inter: int, experts: int, top_k: int, max_tokens: int, device=None,
-                 timeout_s: float = 10.0, slots_per_rank: int | None = None, n_shared: int = 0):
-        """slots_per_rank: pool slots of every rank (routed experts in HBM plus the shared experts; default every
-        owned expert plus the shared ones). n_shared: shared experts per token, computed as routes to the local pool's
-        last slots."""
+                 timeout_s: float = 10.0, slots_per_rank: int | None = None, n_shared: int = 0,
+                 stage_slots: int = 0, stage_fmt: str = NVFP4):
+        """slots_per_rank: pool slots of every rank (routed experts in HBM plus the shared experts plus the staging
+        slots; default every owned expert plus the shared ones). n_shared: shared experts per token, computed as routes
+        to the local pool's slots after the routed ones. stage_slots: PCIe staging slots (the last local slots), shared
+        by the layers: CPU-tier experts the router hands to the GPU, copied from the CPU engine's host memory each
+        call (`EPMoE(stage=...)`)."""
         env = xdist.get()
         self.W, self.rank = env.world, env.rank
         self.H, self.I, self.E, self.T = hidden, inter, experts, max_tokens
@@ -69,6 +72,19 @@ class EPComm:
         self.mid = torch.empty(W * R * inter, dtype=torch.float16, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.timeout_s = timeout_s
+        self.S = int(stage_slots)
+        if self.S:
+            bs = 16 if stage_fmt == NVFP4 else 32
+            u8 = lambda *shape: torch.zeros(*shape, dtype=torch.uint8, device=self.device)   # noqa: E731
+            self.st_w13, self.st_s13 = u8(self.S, 2 * inter, hidden // 2), u8(self.S, 2 * inter, hidden // bs)
+            self.st_w2, self.st_s2 = u8(self.S, hidden, inter // 2), u8(self.S, hidden, inter // bs)
+            self.st_g13 = torch.ones(self.S, 2, dtype=torch.float32, device=self.device)
+            self.st_g2 = torch.ones(self.S, dtype=torch.float32, device=self.device)
+            self.claim = torch.full((experts,), -1, dtype=torch.int32, device=self.device)
+            self.claim_list = torch.zeros(experts, dtype=torch.int32, device=self.device)
+            self.claim_count = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.stage_done = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.stage_chunks = max(4, 148 * 8 // self.S)
 
     def check(self):
         if int(self.err.item()):
@@ -85,12 +101,18 @@ class EPMoE:
 
     `local`: this rank's GPU pool of routed experts (all of its El experts in id order, or with `table` the pool
     slots' experts). `table` (int32 [E], optional): expert -> owner * slots_per_rank + pool slot, -1 for the CPU tier,
-    whose routes go through `mailbox` to `engine` (this rank's CPU engine of every CPU-tier expert)."""
+    whose routes go through `mailbox` to `engine` (this rank's CPU engine of every CPU-tier expert).
+
+    `stage` (optional, with the exchange's staging slots): the CPU engine's weight shards mapped for the GPU --
+    dict(cold_index = int32 [E] engine slot of each CPU-tier expert or -1, bases = device address of each node's shard,
+    stride, piece_off, piece_bytes (`CpuEngine.shard`), src_g13 [slots, 2] / src_g2 [slots] global scales by engine
+    slot). The router then hands up to `comm.S` of the CPU-tier experts its tokens chose to the GPU, which copies them
+    over PCIe into the staging slots (`ep_stage`) and computes their routes while the engine computes the others."""
 
     def __init__(self, layer: int, comm: EPComm, router_w: torch.Tensor, local: ExpertWeights, top_k: int,
                  shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1, topk_group: int = 1,
                  renorm: bool = True, scale: float = 1.0, router_bias=None, corr_bias=None, table=None,
-                 mailbox=None, engine=None):
+                 mailbox=None, engine=None, stage: dict | None = None):
         self.comm = comm
         self.layer = layer
         self.k = top_k
@@ -98,8 +120,9 @@ class EPMoE:
         if n_sh != comm.n_shared or top_k + n_sh != comm.k:
             raise ValueError('EP MoE: routes per token differ from the exchange buffers (top_k / n_shared)')
         nl = local.experts
-        if nl + n_sh != comm.spr:
-            raise ValueError(f'EP MoE: {nl} pool experts + {n_sh} shared != {comm.spr} slots per rank')
+        if nl + n_sh + comm.S != comm.spr:
+            raise ValueError(f'EP MoE: {nl} pool experts + {n_sh} shared + {comm.S} staging != {comm.spr} slots per '
+                             'rank')
         parts = [local] + ([shared] if shared is not None else [])
         fields = ('w13', 'w2', 's13', 's2', 'g13', 'g2')
         self.local = ExpertWeights(local.fmt, *[torch.cat([getattr(q, f).to(comm.device) for q in parts]).contiguous()
@@ -122,9 +145,20 @@ class EPMoE:
         if self.mailbox is not None:
             self.mailbox.register(layer, engine)
         self.engine = engine
+        self.stage_base = nl + n_sh
+        self.stage = None
+        route_stage = None
+        if stage is not None and comm.S and self.mailbox is not None:
+            self.stage = dict(stage, cold_index=torch.as_tensor(stage['cold_index'], dtype=torch.int32).to(comm.device),
+                              src_g13=stage['src_g13'].to(comm.device, torch.float32).contiguous(),
+                              src_g2=stage['src_g2'].to(comm.device, torch.float32).contiguous(),
+                              bases=[int(b) for b in stage['bases']], piece_off=[int(v) for v in stage['piece_off']],
+                              piece_bytes=[int(v) for v in stage['piece_bytes']], stride=int(stage['stride']))
+            route_stage = (self.stage['cold_index'], comm.claim, comm.claim_list, comm.claim_count, comm.S,
+                           comm.rank * comm.spr + self.stage_base)
         self.router = _Router(router_w, comm.E, top_k, mode, n_group, topk_group, renorm, scale, router_bias,
                               corr_bias, comm.device, comm.T, table=self.table, layer=layer, mailbox=self.mailbox,
-                              shared_slots=self.shared_slots)
+                              shared_slots=self.shared_slots, stage=route_stage)
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, add: torch.Tensor | None = None):
         c = self.comm
@@ -133,18 +167,26 @@ class EPMoE:
             raise ValueError(f'EP MoE: {T} tokens exceed the {c.T} per rank the exchange buffers were sized for')
         out = torch.empty_like(x) if out is None else out
         ids, w = self.router(x)
+        st = self.stage
+        if st is not None:   # the claimed CPU-tier experts over PCIe into the staging slots
+            torch.ops.xtier.ep_stage(c.claim_list, c.claim, c.claim_count, c.stage_done, st['cold_index'],
+                                     st['bases'], st['stride'], st['piece_off'], st['piece_bytes'], c.st_w13,
+                                     c.st_s13, c.st_w2, c.st_s2, c.st_g13, c.st_g2, st['src_g13'], st['src_g2'], c.I,
+                                     c.H, self.fmt_code, c.stage_chunks)
+        staged = (c.st_w13, c.st_s13, c.st_w2, c.st_s2, c.st_g13, c.st_g2, self.stage_base) if st is not None else ()
         torch.ops.xtier.ep_moe(x, ids, w, c.buf.peer_table, c.state, c.mid, self.local.w13, self.local.s13,
                                self.local.g13, self.local.w2, self.local.s2, self.local.g2, add, out, c.err, c.W,
                                c.rank, c.E, self.fmt_code, c.R, c.offsets, c.timeout_s, 0xF,
                                self.router.slots[:T], c.spr,
-                               self.mailbox.handle if self.mailbox is not None else 0)
+                               self.mailbox.handle if self.mailbox is not None else 0, *staged)
         return out
 
 
 class _Router:
     def __init__(self, router_w, E, k, mode, n_group, topk_group, renorm, scale, bias, corr, device, max_tokens,
-                 table=None, layer: int = 0, mailbox=None, shared_slots=None):
+                 table=None, layer: int = 0, mailbox=None, shared_slots=None, stage=None):
         self.table, self.layer, self.mailbox, self.shared_slots = table, layer, mailbox, shared_slots
+        self.stage = stage   # (cold_index, claim, claim_list, claim_count, stage_max, stage_slot0) or None
         kk = k + (0 if shared_slots is None else shared_slots.numel())
         self.w = router_w.to(device, torch.bfloat16).contiguous()
         self.E, self.k = E, k
@@ -161,7 +203,9 @@ class _Router:
         T = x.shape[0]
         ops.moe_route(x, self.w, self.bias, self.corr, self.table, self.shared_slots, self.ids[:T], self.wt[:T], self.slots[:T],
                       self.ws_logits, self.ws_count, self.k, self.mode, self.n_group, self.topk_group, self.renorm,
-                      self.scale, self.layer, self.mailbox.handle if self.mailbox is not None else 0)
+                      self.scale, self.layer, self.mailbox.handle if self.mailbox is not None else 0,
+                      **(dict(zip(('cold_index', 'claim', 'claim_list', 'claim_count', 'stage_max', 'stage_slot0'),
+                                  self.stage)) if self.stage is not None else {}))
         return self.ids[:T], self.wt[:T]
 
 
