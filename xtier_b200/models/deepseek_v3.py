@@ -345,13 +345,17 @@ class DeepSeekV3Model:
         else:
             table, pools, cpu_ids = ep_layout(E, self.ep_world, self.gpu_per_rank, seed_l, stride=self.ep.spr)
         mine = pools[self.ep_rank]
-        local = empty_experts(self.gpu_per_rank, H, I, cfg.fmt, self.device)
+        n_sh = shared.experts if shared is not None else 0
+        gp = self.gpu_per_rank
+        local = empty_experts(gp + n_sh, H, I, cfg.fmt, self.device)   # the routed pool, then the shared experts
         if mine:
             synthetic_experts_by_id(formats.ExpertWeights(cfg.fmt, *[getattr(local, f)[:len(mine)] for f in
                                                                      ('w13', 'w2', 's13', 's2', 'g13', 'g2')]),
                                     mine, seed_l, cfg.std)
         for f in ('w13', 'w2', 's13', 's2', 'g13', 'g2'):   # slots a ranked plan leaves empty on this rank
-            getattr(local, f)[len(mine):].zero_()
+            getattr(local, f)[len(mine):gp].zero_()
+            if n_sh:
+                getattr(local, f)[gp:].copy_(getattr(shared, f))
         engine = pcie = None
         if cpu_ids and self.cold is not None:
             engine = self._cold_engine(li, cpu_ids, seed_l, threads)
@@ -383,7 +387,7 @@ class DeepSeekV3Model:
                 pcie = self._map_engine(engine, cpu_ids, g13, g2)
         moe = EPMoE(li, self.ep, router, local, cfg.top_k, shared=shared, mode=1, n_group=cfg.n_group,
                     topk_group=cfg.topk_group, renorm=True, scale=cfg.routed_scale, corr_bias=corr,
-                    table=table, mailbox=self.mailbox, engine=engine, stage=pcie)
+                    table=table, mailbox=self.mailbox, engine=engine, stage=pcie, shared_in_pool=True)
         return moe, stage
 
     def _map_engine(self, engine, cpu_ids: list, g13: torch.Tensor, g2: torch.Tensor) -> dict | None:

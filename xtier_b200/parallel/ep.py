@@ -112,20 +112,23 @@ class EPMoE:
     def __init__(self, layer: int, comm: EPComm, router_w: torch.Tensor, local: ExpertWeights, top_k: int,
                  shared: ExpertWeights | None = None, mode: int = 0, n_group: int = 1, topk_group: int = 1,
                  renorm: bool = True, scale: float = 1.0, router_bias=None, corr_bias=None, table=None,
-                 mailbox=None, engine=None, stage: dict | None = None):
+                 mailbox=None, engine=None, stage: dict | None = None, shared_in_pool: bool = False):
+        """shared_in_pool: `local` already ends with the shared experts' slots (`shared` then only gives their
+        count): no concatenated copy of the pool, whose transient second copy can be more than the HBM left."""
         self.comm = comm
         self.layer = layer
         self.k = top_k
         n_sh = 0 if shared is None else shared.experts
         if n_sh != comm.n_shared or top_k + n_sh != comm.k:
             raise ValueError('EP MoE: routes per token differ from the exchange buffers (top_k / n_shared)')
-        nl = local.experts
+        nl = local.experts - (n_sh if shared_in_pool else 0)
         if nl + n_sh + comm.S != comm.spr:
             raise ValueError(f'EP MoE: {nl} pool experts + {n_sh} shared + {comm.S} staging != {comm.spr} slots per '
                              'rank')
-        parts = [local] + ([shared] if shared is not None else [])
+        parts = [local] + ([shared] if shared is not None and not shared_in_pool else [])
         fields = ('w13', 'w2', 's13', 's2', 'g13', 'g2')
-        self.local = ExpertWeights(local.fmt, *[torch.cat([getattr(q, f).to(comm.device) for q in parts]).contiguous()
+        self.local = ExpertWeights(local.fmt, *[(torch.cat([getattr(q, f).to(comm.device) for q in parts])
+                                                 if len(parts) > 1 else getattr(local, f).to(comm.device)).contiguous()
                                                 for f in fields])
         self.local.g13 = self.local.g13.float().contiguous()
         self.local.g2 = self.local.g2.float().contiguous()
