@@ -123,3 +123,24 @@ def test_cost_curve_peer_term():
     assert peer[16] == base[16]
     assert np.all(peer[:8] < base[:8])
     assert abs(peer[8] - (c.g0 + c.g1 * (1 - (1 - p[:8]) ** 4).sum() + c.p1 * (1 - (1 - p[8:]) ** 4).sum())) < 1e-6
+
+
+def test_cost_curve_pcie_staging_term():
+    """PCIe staging moves up to `stage` touched cold experts from the engine (c1 each) to the GPU (h1 + g1 each): the
+    curve drops while the engine is the slower half, not at all when every expert is hot, and the balancing share is
+    c1 / (c1 + h1)."""
+    import numpy as np
+    from xtier_b200.planner.cost import Coeffs, layer_time_curve, staging_share, touch_probabilities
+    p = np.full(64, 8 / 64)
+    c = Coeffs(g0=20.0, g1=5.0, c0=30.0, c1=300.0, h1=500.0, stage=0, sd_frac=0.0)
+    base = layer_time_curve(p, c, m=32)
+    c.stage = 12
+    staged = layer_time_curve(p, c, m=32)
+    assert staged[64] == base[64] and np.all(staged[:40] < base[:40])
+    q = touch_probabilities(p, 32)
+    n = 10                                             # 10 hot experts, the other 54 cold
+    cold = q[n:].sum()
+    tg = c.g0 + c.g1 * (q[:n].sum() + 12) + c.h1 * 12
+    tc = (1 - np.prod(1 - q[n:])) * c.c0 + c.c1 * (cold - 12)
+    assert abs(staged[n] - max(tg, tc)) < 1e-6
+    assert abs(staging_share(c) - 300 / 800) < 1e-12 and staging_share(Coeffs()) == 0.0

@@ -18,3 +18,6 @@ def test_probes_measure_gpu_and_mailbox(cuda_ops):
     assert co['c0'] >= 1.0 and co['g0'] > 0 and 'mailbox' in out['samples']
     if torch.cuda.device_count() >= 2:
         assert co['p1'] > 0 and out['samples']['peer']['gbs'] > 0
+    # PCIe staging: the ep_stage copy from registered engine memory (bytes checked inside the probe), 1-8 experts
+    pc = out['samples']['pcie']
+    assert [n for n, _ in pc] == [1, 2, 4, 8] and all(t > 0 for _, t in pc) and co['h1'] >= 0.1

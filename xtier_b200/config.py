@@ -57,7 +57,8 @@ SETTINGS: tuple[Setting, ...] = (
        'experts the GPU reads from the engine\'s host memory over PCIe while the engine computes the others (0: off, '
        '-1: XTIER_EP_PCIE_SHARE of the CPU-tier experts a call is expected to touch)'),
     _S('XTIER_EP_PCIE_SHARE', 'float', 0.37, 'share of the touched CPU-tier experts read over PCIe when '
-       'XTIER_EP_PCIE_SLOTS is -1 (the balance of ~0.5 ms per expert over PCIe against ~0.3 ms on 14 engine threads)'),
+       'XTIER_EP_PCIE_SLOTS is -1 (the balance of ~0.5 ms per expert over PCIe against ~0.3 ms on 14 engine threads; '
+       'planner.cost.staging_share of probed coefficients gives it for another machine)'),
     _S('XTIER_CACHE_RING', 'flag', True, 'hot-slot swaps copy on a side stream and the decode step maps them'),
     _S('XTIER_CACHE_ELASTIC', 'flag', False, 'extra hot slots in VMM-backed memory that prefills take back'),
     _S('XTIER_CACHE_ELASTIC_MAX', 'float', 2.0, 'address space per layer, as a multiple of its base hot slots'),

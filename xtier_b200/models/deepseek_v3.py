@@ -392,26 +392,11 @@ class DeepSeekV3Model:
 
     def _map_engine(self, engine, cpu_ids: list, g13: torch.Tensor, g2: torch.Tensor) -> dict | None:
         """The engine's weight shards registered with CUDA and mapped for kernels (the PCIe staging reads them in
-        place): the `stage` description of EPMoE, or None (with a warning) when the registration is refused."""
-        import ctypes as C
-        L = ops.cdll()
-        L.xt_host_register_mapped.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p]
-        bases, sh = [], None
-        for node in range(engine.nodes()):
-            sh = engine.shard(node)
-            dev = C.c_void_p()
-            rc = L.xt_host_register_mapped(C.c_void_p(sh['base']), C.c_size_t(sh['bytes']), C.byref(dev))
-            if rc != 0:
-                import logging
-                logging.getLogger('xtier_b200').warning(f'PCIe staging off for this layer: cudaHostRegister of the '
-                                                        f'engine shard refused (error {rc})')
-                return None
-            self.host_maps.append(sh['base'])
-            bases.append(dev.value)
-        idx = torch.full((self.cfg.experts,), -1, dtype=torch.int32)
-        idx[torch.as_tensor(cpu_ids, dtype=torch.long)] = torch.arange(len(cpu_ids), dtype=torch.int32)
-        return dict(cold_index=idx, bases=bases, stride=sh['stride'], piece_off=sh['piece_off'],
-                    piece_bytes=sh['piece_bytes'], src_g13=g13, src_g2=g2)
+        place): the `stage` description of EPMoE, or None when the registration is refused."""
+        from ..parallel.ep import map_engine
+        stage, bases = map_engine(engine, cpu_ids, self.cfg.experts, g13, g2)
+        self.host_maps += bases
+        return stage
 
     def attach_bigram(self, table):
         """Adds a hashed-bigram NVMe embedding table (tables/engram.py; rows projected to the hidden size) to the
@@ -758,12 +743,9 @@ class DeepSeekV3Model:
 
     def close(self):
         if self.host_maps:
-            import ctypes as C
+            from ..parallel.ep import unmap_engine
             torch.cuda.synchronize()
-            L = ops.cdll()
-            L.xt_host_unregister.argtypes = [C.c_void_p]
-            for base in self.host_maps:
-                L.xt_host_unregister(C.c_void_p(base))
+            unmap_engine(self.host_maps)
             self.host_maps = []
         for e in self.engines:
             e.close()

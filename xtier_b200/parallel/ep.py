@@ -212,6 +212,44 @@ class _Router:
         return self.ids[:T], self.wt[:T]
 
 
+def map_engine(engine, expert_ids: list, E: int, g13: torch.Tensor, g2: torch.Tensor):
+    """Registers the CPU engine's weight shards with CUDA (page-locked, mapped) so that kernels read its slots in place
+    over PCIe. Returns (the `stage` description EPMoE takes -- engine slot s holds expert_ids[s], whose global scales
+    are g13[s] / g2[s] --, the registered host addresses for `unmap_engine`), or (None, []) with a warning when CUDA
+    refuses the registration."""
+    import ctypes as C
+    import logging
+    L = ops.cdll()
+    L.xt_host_register_mapped.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p]
+    bases, regs, sh = [], [], None
+    for node in range(engine.nodes()):
+        sh = engine.shard(node)
+        dev = C.c_void_p()
+        rc = L.xt_host_register_mapped(C.c_void_p(sh['base']), C.c_size_t(sh['bytes']), C.byref(dev))
+        if rc != 0:
+            logging.getLogger('xtier_b200').warning(f'PCIe staging off: cudaHostRegister of an engine shard refused '
+                                                    f'(error {rc})')
+            unmap_engine(regs)
+            return None, []
+        regs.append(sh['base'])
+        bases.append(dev.value)
+    idx = torch.full((E,), -1, dtype=torch.int32)
+    idx[torch.as_tensor(list(expert_ids), dtype=torch.long)] = torch.arange(len(expert_ids), dtype=torch.int32)
+    return dict(cold_index=idx, bases=bases, stride=sh['stride'], piece_off=sh['piece_off'],
+                piece_bytes=sh['piece_bytes'], src_g13=g13, src_g2=g2), regs
+
+
+def unmap_engine(regs: list):
+    """Unregisters what `map_engine` registered (before the engine frees its shards)."""
+    import ctypes as C
+    if not regs:
+        return
+    L = ops.cdll()
+    L.xt_host_unregister.argtypes = [C.c_void_p]
+    for base in regs:
+        L.xt_host_unregister(C.c_void_p(base))
+
+
 def nccl_ep_moe(x, ids, w, local: ExpertWeights, E: int, group=None):
     """Baseline: NCCL all-to-all of the routed rows, local expert compute, all-to-all back, route-ordered sum.
     Returns bf16 [T, H]. Not graph-captured (data-dependent split sizes)."""

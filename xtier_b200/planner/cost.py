@@ -11,6 +11,11 @@ experts on the GPU gives, per decode call of m tokens:
 With a node-wide slot pool (peer mode), a cold expert that another GPU's pool holds is read over NVLink by the GPU
 kernels instead of going to the CPU: it adds p1 per expert touched to the GPU part and leaves the CPU part.
 
+With PCIe staging (`stage` slots), up to `stage` of the touched cold experts are copied from the engine's host memory
+by the GPU instead of computed by the engine: h1 per staged expert moves to the GPU part (the copy runs before the
+expert kernels), the CPU part keeps the rest. The staging share that balances both is c1 / (c1 + h1) of the touched
+cold experts (`staging_share`).
+
 The expected distinct-expert counts treat the m * k routes of a call as independent draws (an expert is touched with
 probability 1 - (1 - p_e)^m, p_e the per-token probability of being among the token's k routes). The max of two
 random times is approximated by the max of their means plus a spread term (Clark's formula for the expected maximum
@@ -35,6 +40,8 @@ class Coeffs:
     c0: float = 12.0      # us: mailbox round trip when the CPU has work
     c1: float = 25.0      # us per cold expert touched (CPU engine)
     p1: float = 0.0       # us per expert touched that another GPU's pool holds (NVLink read)
+    h1: float = 0.0       # us per cold expert the GPU copies from host memory (PCIe staging)
+    stage: int = 0        # PCIe staging slots per call (0: off)
     a: float = 0.0        # us: per-layer work outside the MoE (attention), added to every option
     sd_frac: float = 0.15  # relative spread of both halves (for the expected max)
 
@@ -77,10 +84,16 @@ def layer_time_curve(p: np.ndarray, c: Coeffs, m: int = 1, peer_held: np.ndarray
         on_peer = cum_peer_tail[n]
         cold = cum_cpu_tail[n]
         p_any_cold = 1.0 - math.exp(log_none[n])
-        tg = c.g0 + c.g1 * hot + c.p1 * on_peer
-        tc = p_any_cold * c.c0 + c.c1 * cold
+        staged = min(float(c.stage), cold) if c.h1 > 0 else 0.0
+        tg = c.g0 + c.g1 * (hot + staged) + c.p1 * on_peer + c.h1 * staged
+        tc = p_any_cold * c.c0 + c.c1 * (cold - staged)
         out[n] = expected_max(tg, c.sd_frac * tg, tc, c.sd_frac * tc) + c.a
     return out
+
+
+def staging_share(c: Coeffs) -> float:
+    """Share of the touched cold experts to stage over PCIe so that the engine and the copy finish together."""
+    return c.c1 / (c.c1 + c.h1) if c.h1 > 0 else 0.0
 
 
 def fit(samples: list[tuple[float, float]]) -> tuple[float, float]:

@@ -6,7 +6,9 @@ experts -> c1. Mailbox: the round trip of a captured decode call of a layer with
 to a tiny expert on the CPU engine, minus that expert's engine time -> c0 (GPU publish, dispatcher wake-up, engine
 hand-off and the GPU's poll, both PCIe directions). NVLink: with a second GPU, the time to read one expert's weights
 from the peer's memory (device-to-device copy over the NVLink path, events on the reader) -> p1, the cost of a route
-to an expert another GPU's slot pool holds. Results are written as {"coeffs": {...}, "samples": {...}}.
+to an expert another GPU's slot pool holds. PCIe: the staging copy kernel (`ep_stage`) of 1-8 experts from a CPU
+engine's registered host memory, as graph replays -> h1 per staged expert. Results are written as {"coeffs": {...},
+"samples": {...}}.
 
 Reference parity: xtier/planner/probe.py:102-227 (graph timings of real mailbox/pool decode calls).
 """
@@ -134,6 +136,49 @@ def probe_peer(H: int, I: int, fmt: str = formats.NVFP4, reps: int = 20) -> dict
     return {'bytes': nbytes, 'us': us, 'gbs': nbytes / us / 1e3, 'peer_access': torch.cuda.can_device_access_peer(0, 1)}
 
 
+def probe_pcie(H: int, I: int, fmt: str = formats.NVFP4, reps: int = 10) -> list:
+    """The PCIe staging copy (`ep_stage`) of n = 1, 2, 4, 8 experts from a CPU engine's registered host memory into
+    GPU staging slots, timed as CUDA-graph replays -> h1 (us per staged expert)."""
+    from ..engine import CpuEngine
+    from ..parallel.ep import map_engine, unmap_engine
+    E, S = 8, 8
+    ew = formats.synthetic_experts(E, H, I, fmt, 'cpu', seed=11)
+    eng = CpuEngine(ew, threads=1)
+    g13 = ew.g13.float().cuda()
+    g2 = ew.g2.float().cuda()
+    stage, regs = map_engine(eng, list(range(E)), E, g13, g2)
+    if stage is None:
+        eng.close()
+        return []
+    try:
+        bs = formats.BLOCK[fmt]
+        u8 = lambda *shape: torch.zeros(*shape, dtype=torch.uint8, device='cuda')   # noqa: E731
+        st = (u8(S, 2 * I, H // 2), u8(S, 2 * I, H // bs), u8(S, H, I // 2), u8(S, H, I // bs),
+              torch.ones(S, 2, device='cuda'), torch.ones(S, device='cuda'))
+        idx = stage['cold_index'].cuda()
+        claim_list = torch.arange(E, dtype=torch.int32, device='cuda')
+        claim = torch.full((E,), -1, dtype=torch.int32, device='cuda')
+        count = torch.zeros(1, dtype=torch.int32, device='cuda')
+        done = torch.zeros(1, dtype=torch.int32, device='cuda')
+        fmt_code = 0 if fmt == formats.NVFP4 else 1
+        samples = []
+        for n in (1, 2, 4, 8):
+            def call(n=n):
+                count.fill_(n)
+                torch.ops.xtier.ep_stage(claim_list, claim, count, done, idx, stage['bases'], stage['stride'],
+                                         stage['piece_off'], stage['piece_bytes'], *st, g13, g2, I, H, fmt_code,
+                                         max(4, 148 * 8 // S))
+            samples.append((n, _graph_time_us(call, reps)))
+        ok = all(bool(torch.equal(st[0][i].cpu(), ew.w13[i])) for i in range(S))   # the last call staged every expert
+        if not ok:
+            raise RuntimeError('PCIe staging probe: the staged expert bytes differ from the engine\'s')
+        return samples
+    finally:
+        torch.cuda.synchronize()
+        unmap_engine(regs)
+        eng.close()
+
+
 def measure(H: int, I: int, fmt: str = formats.NVFP4, threads: int | None = None, gpu: bool = True) -> dict:
     cpu = probe_cpu(H, I, fmt, threads)
     c0, c1 = fit(cpu)
@@ -151,6 +196,10 @@ def measure(H: int, I: int, fmt: str = formats.NVFP4, threads: int | None = None
         if peer is not None:
             co.p1 = peer['us']
             out['samples']['peer'] = peer
+        pcie = probe_pcie(H, I, fmt)
+        if pcie:
+            co.h1 = max(fit(pcie)[1], 0.1)
+            out['samples']['pcie'] = pcie
     else:   # no GPU to measure the round trip on: the engine's fixed cost plus a nominal 8 us for PCIe both ways
         co.c0 = max(c0, 1.0) + 8.0
         out['c0_measured'] = False
