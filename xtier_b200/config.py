@@ -53,6 +53,8 @@ SETTINGS: tuple[Setting, ...] = (
     _S('XTIER_CACHE_LOG', 'int', 0, 'log the cache statistics every N policy rounds (0: off)'),
     _S('XTIER_DECODE_MISS_GPU', 'float', 0.0, 'share of a token\'s CPU-tier routes the GPU computes from pinned host '
        'memory over PCIe (one per token at most; 0: off)'),
+    _S('XTIER_GC_FREEZE', 'flag', True, 'the server freezes the Python heap once the model is built (no GC scans of '
+       'the model\'s objects while serving)'),
     _S('XTIER_EP_PCIE_SLOTS', 'int', -1, 'expert parallelism with a RAM CPU tier: GPU staging slots for CPU-tier '
        'experts the GPU reads from the engine\'s host memory over PCIe while the engine computes the others (0: off, '
        '-1: XTIER_EP_PCIE_SHARE of the CPU-tier experts a call is expected to touch)'),

@@ -88,6 +88,8 @@ class SafeTensors:
             raise KeyError(f'checkpoint has no tensor {name!r}')
         i, h, data0 = self.entries[name]
         if self._maps[i] is None:
+            from ..utils.platform import read_ahead
+            read_ahead(self.files[i])
             self._maps[i] = np.memmap(self.files[i], dtype=np.uint8, mode='r')
         a, b = h['data_offsets']
         raw = torch.from_numpy(np.array(self._maps[i][data0 + a:data0 + b]))
@@ -96,8 +98,13 @@ class SafeTensors:
             raise TypeError(f'{name}: safetensors dtype {h["dtype"]} is not supported')
         return raw.view(dt).reshape(h['shape'])
 
-    def close(self):
+    def close(self, drop_cache: bool = True):
+        """Unmaps the files; drop_cache also evicts their pages from the page cache (the tensors were copied out)."""
+        used = [f for f, m in zip(self.files, self._maps) if m is not None]
         self._maps = [None] * len(self._maps)
+        if drop_cache and used:
+            from ..utils.platform import drop_file_cache
+            drop_file_cache(used)
 
 
 def save_safetensors(path, tensors: dict, metadata: dict | None = None):

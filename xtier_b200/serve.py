@@ -973,6 +973,10 @@ def main(argv=None):
     except Exception as e:   # noqa: BLE001 -- the console shows why the start died
         server.stages.fail(f'{type(e).__name__}: {e}')
         raise
+    from . import config
+    if config.get('XTIER_GC_FREEZE'):
+        from .utils.platform import freeze_gc
+        print(f'[xtier_b200] GC heap frozen ({freeze_gc()} objects)', flush=True)
     print(f'[xtier_b200] ready on http://{args.host}:{args.port}', flush=True)
     try:
         threading.Event().wait()
