@@ -233,6 +233,15 @@ def map_engine(engine, expert_ids: list, E: int, g13: torch.Tensor, g2: torch.Te
             return None, []
         regs.append(sh['base'])
         bases.append(dev.value)
+    # the staging copy lays node n's rows of each piece at n * piece bytes: the engine must split rows evenly
+    N, H, I = len(bases), engine.H, engine.I
+    bs = 16 if engine.fmt == NVFP4 else 32
+    want = [I // N * (H // 2)] * 2 + [I // N * (H // bs)] * 2 + [H // N * (I // 2), H // N * (I // bs)]
+    aligned = all(v % 16 == 0 for v in list(sh['piece_off']) + list(sh['piece_bytes']) + [sh['stride']] + bases)
+    if list(sh['piece_bytes']) != want or I % N or H % N or not aligned:
+        logging.getLogger('xtier_b200').warning('PCIe staging off: the engine shards do not split the rows evenly')
+        unmap_engine(regs)
+        return None, []
     idx = torch.full((E,), -1, dtype=torch.int32)
     idx[torch.as_tensor(list(expert_ids), dtype=torch.long)] = torch.arange(len(expert_ids), dtype=torch.int32)
     return dict(cold_index=idx, bases=bases, stride=sh['stride'], piece_off=sh['piece_off'],
