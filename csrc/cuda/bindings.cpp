@@ -509,6 +509,41 @@ void ep_stage(const Tensor &claim_list, const Tensor &claim, const Tensor &claim
     check_rc(xt_ep_stage(&p, stream()), "ep_stage");
 }
 
+void qsa_kv_write(const Tensor &x, const Tensor &slots, const Tensor &codes, const Tensor &scales) {
+    cuda_contig(x, "qsa kv rows");
+    check(x.dim() == 3 && x.scalar_type() == at::kBFloat16, "qsa kv rows: bf16 [T, Hkv, D]");
+    const int T = int(x.size(0)), H = int(x.size(1)), D = int(x.size(2));
+    check(slots.scalar_type() == at::kLong && slots.numel() == T && slots.is_contiguous(), "qsa slots: int64 [T]");
+    check(codes.dim() == 3 && codes.size(1) == H && codes.size(2) == D / 2 && scales.dim() == 3 &&
+              scales.size(1) == H && scales.size(2) == D / 16 && codes.size(0) == scales.size(0),
+          "qsa cache: codes [slots, Hkv, D/2], scales [slots, Hkv, D/16]");
+    c10::cuda::CUDAGuard g(x.device());
+    check_rc(xt_qsa_kv_write(x.data_ptr(), ptr<const int64_t>(slots), T, H, D, codes.data_ptr(), scales.data_ptr(),
+                             stream()),
+             "qsa_kv_write");
+}
+
+void qsa_decode(const Tensor &q, const Tensor &idx, const Tensor &kc, const Tensor &ks, const Tensor &vc,
+                const Tensor &vs, const Tensor &part_o, const Tensor &part_ml, const Tensor &out, double scale) {
+    cuda_contig(q, "qsa q");
+    check(q.dim() == 3 && q.scalar_type() == at::kBFloat16, "qsa q: bf16 [B, Hq, D]");
+    const int B = int(q.size(0)), Hq = int(q.size(1)), D = int(q.size(2)), Hkv = int(kc.size(1));
+    check(idx.scalar_type() == at::kInt && idx.dim() == 2 && idx.size(0) == B && idx.is_contiguous(),
+          "qsa idx: int32 [B, nsel]");
+    const int nsel = int(idx.size(1));
+    check(Hkv > 0 && Hq % Hkv == 0 && kc.size(2) == D / 2 && vc.sizes() == kc.sizes() && vs.sizes() == ks.sizes(),
+          "qsa cache shapes");
+    const int64_t splits = (nsel + 63) / 64;
+    check(part_o.numel() >= int64_t(B) * Hq * splits * D && part_ml.numel() >= int64_t(B) * Hq * splits * 2,
+          "qsa scratch too small");
+    check(out.numel() == q.numel() && out.scalar_type() == at::kBFloat16, "qsa out: bf16 like q");
+    c10::cuda::CUDAGuard g(q.device());
+    check_rc(xt_qsa_decode(q.data_ptr(), ptr<const int32_t>(idx), B, nsel, Hq, Hkv, D, kc.data_ptr(), ks.data_ptr(),
+                           vc.data_ptr(), vs.data_ptr(), ptr<float>(part_o), ptr<float>(part_ml), out.data_ptr(),
+                           float(scale), stream()),
+             "qsa_decode");
+}
+
 xt::TpParams tp_params(const Tensor &peer, const Tensor &state, const Tensor &out, const Tensor &err, int64_t M,
                        int64_t N, int64_t K, int64_t W, int64_t rank, const std::vector<int64_t> &offs,
                        double timeout_s) {
@@ -1082,6 +1117,9 @@ TORCH_LIBRARY(xtier, m) {
           "int W, int rank, int E, int fmt, int R, int[] offsets, float timeout_s, int phases, Tensor? slots=None, "
           "int spr=0, int mailbox=0, Tensor? st_w13=None, Tensor? st_s13=None, Tensor? st_w2=None, "
           "Tensor? st_s2=None, Tensor? st_g13=None, Tensor? st_g2=None, int stage_base=0) -> ()");
+    m.def("qsa_kv_write(Tensor x, Tensor slots, Tensor(a!) codes, Tensor(b!) scales) -> ()");
+    m.def("qsa_decode(Tensor q, Tensor idx, Tensor kc, Tensor ks, Tensor vc, Tensor vs, Tensor(a!) part_o, "
+          "Tensor(b!) part_ml, Tensor(c!) out, float scale) -> ()");
     m.def("ep_stage(Tensor claim_list, Tensor(a!) claim, Tensor(b!) claim_count, Tensor(c!) done, Tensor cold_index, "
           "int[] bases, int stride, int[] piece_off, int[] piece_bytes, Tensor(d!) w13, Tensor(e!) s13, "
           "Tensor(f!) w2, Tensor(g!) s2, Tensor(h!) g13, Tensor(i!) g2, Tensor src_g13, Tensor src_g2, int I, int H, "
@@ -1136,6 +1174,8 @@ TORCH_LIBRARY_IMPL(xtier, CUDA, m) {
     m.impl("attn_decode", &attn_decode);
     m.impl("moe_route", &moe_route);
     m.impl("ep_stage", &ep_stage);
+    m.impl("qsa_kv_write", &qsa_kv_write);
+    m.impl("qsa_decode", &qsa_decode);
     m.impl("moe_gate_up", &moe_gate_up);
     m.impl("moe_down", &moe_down);
     m.impl("gemv", &gemv);

@@ -212,6 +212,11 @@ struct HeadGemmParams {
 
 extern "C" int xt_ep_moe(const xt::EpParams *p, int phase, cudaStream_t stream);
 extern "C" int xt_ep_stage(const xt::StageParams *p, cudaStream_t stream);
+extern "C" int xt_qsa_kv_write(const void *x, const int64_t *slot, int T, int H, int D, void *codes, void *scales,
+                               cudaStream_t stream);
+extern "C" int xt_qsa_decode(const void *q, const int32_t *idx, int B, int nsel, int Hq, int Hkv, int D,
+                             const void *kc, const void *ks, const void *vc, const void *vs, float *part_o,
+                             float *part_ml, void *out, float scale, cudaStream_t stream);
 
 namespace xt {
 // Tensor-parallel GEMMs fused with their collective (csrc/cuda/gemm_tp.cu).
