@@ -533,7 +533,7 @@ void qsa_decode(const Tensor &q, const Tensor &idx, const Tensor &kc, const Tens
     const int nsel = int(idx.size(1));
     check(Hkv > 0 && Hq % Hkv == 0 && kc.size(2) == D / 2 && vc.sizes() == kc.sizes() && vs.sizes() == ks.sizes(),
           "qsa cache shapes");
-    const int64_t splits = (nsel + 63) / 64;
+    const int64_t splits = (nsel + 31) / 32;
     check(part_o.numel() >= int64_t(B) * Hq * splits * D && part_ml.numel() >= int64_t(B) * Hq * splits * 2,
           "qsa scratch too small");
     check(out.numel() == q.numel() && out.scalar_type() == at::kBFloat16, "qsa out: bf16 like q");

@@ -4,8 +4,9 @@
 //   qsa_kv_write   K or V rows [T, Hkv, D] BF16 -> NVFP4 cache rows of the given slots: codes [slots, Hkv, D/2] (E2M1,
 //                  low nibble first) and one E4M3 scale per 16 values [slots, Hkv, D/16] (scale = amax / 6, no global
 //                  scale: KV values are O(1)). One warp per (token, head), one lane per 16-value block.
-//   qsa_partial    grid (key splits of 64, Hkv, B): the G = Hq / Hkv query heads of a KV head share every key and
-//                  value the CTA dequantizes (codes and scales decoded in registers, never stored as BF16). Scores: a
+//   qsa_partial    grid (key splits of 32, Hkv, B): the G = Hq / Hkv query heads of a KV head share every key and
+//                  value the CTA dequantizes (the split's NVFP4 rows staged in shared memory in one round of 16-byte
+//                  loads, decoded in registers, never stored as BF16). Scores: a
 //                  warp per key, each lane D/32 values of the row, all G heads' dots reduced with shuffles; softmax
 //                  of the split per head (max, exponentials, sum); P.V: a thread per value dimension, G accumulators.
 //                  Writes the split's unnormalized output and (max, sum) per head.
@@ -20,7 +21,7 @@
 
 namespace xt {
 
-constexpr int QSA_KEYS = 64, QSA_THREADS = 256, QSA_MAX_G = 16, QSA_MAX_D = 256;
+constexpr int QSA_KEYS = 32, QSA_THREADS = 256, QSA_MAX_G = 16, QSA_MAX_D = 256;
 #define QSA_NEG_INF __int_as_float(0xff800000)
 
 __global__ void __launch_bounds__(256) qsa_kv_write_kernel(const __nv_bfloat16 *__restrict__ x,
@@ -62,10 +63,10 @@ __global__ void __launch_bounds__(256) qsa_kv_write_kernel(const __nv_bfloat16 *
     scales[dst * (D / 16) + lane] = sc;
 }
 
-// E2M1 code -> value (the format's eight magnitudes, sign in bit 3)
+// E2M1 code -> value (the format's eight magnitudes 0, 0.5, 1, 1.5, 2, 3, 4, 6; sign in bit 3)
 XT_DEV float e2m1_val(uint32_t c) {
-    const float m[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
-    const float a = m[c & 7];
+    const float a = (c & 4) ? ((c & 2) ? ((c & 1) ? 6.f : 4.f) : ((c & 1) ? 3.f : 2.f))
+                            : ((c & 2) ? ((c & 1) ? 1.5f : 1.f) : ((c & 1) ? 0.5f : 0.f));
     return (c & 8) ? -a : a;
 }
 
@@ -80,32 +81,56 @@ struct QsaParams {
     float scale;
 };
 
+// The split's keys and values are brought into shared memory first (every 16-byte piece of the 32 rows' codes and
+// scales requested at once: one memory round trip), then decoded from there.
 __global__ void __launch_bounds__(QSA_THREADS) qsa_partial_kernel(QsaParams p) {
+    constexpr int CB = QSA_MAX_D / 2, SB = QSA_MAX_D / 16;   // row bytes of codes / scales at the largest D
     __shared__ float qs[QSA_MAX_G * QSA_MAX_D];
     __shared__ float sc[QSA_MAX_G * QSA_KEYS];
+    __shared__ __align__(16) uint8_t kcs[QSA_KEYS * CB], vcs[QSA_KEYS * CB];
+    __shared__ __align__(16) uint8_t kss[QSA_KEYS * SB], vss[QSA_KEYS * SB];
     __shared__ int slots[QSA_KEYS];
     __shared__ float ml[QSA_MAX_G * 2];
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = p.G, D = p.D;
-    for (int i = tid; i < G * D; i += QSA_THREADS)
-        qs[i] = __bfloat162float(p.q[(size_t(b) * p.Hq + size_t(kvh) * G + i / D) * D + i % D]);
+    const int G = p.G, D = p.D, cb = D / 2, sb = D / 16;
     if (tid < QSA_KEYS) {
         const int j = split * QSA_KEYS + tid;
         slots[tid] = j < p.nsel ? p.idx[size_t(b) * p.nsel + j] : -1;
+    }
+    for (int i = tid; i < G * D; i += QSA_THREADS)
+        qs[i] = __bfloat162float(p.q[(size_t(b) * p.Hq + size_t(kvh) * G + i / D) * D + i % D]);
+    __syncthreads();
+    {   // codes: cb / 16 pieces per row; scales: one piece per row (sb <= 16) -- K and V
+        const int cp = cb / 16, n_code = QSA_KEYS * cp;
+        for (int i = tid; i < 2 * n_code + 2 * QSA_KEYS; i += QSA_THREADS) {
+            const bool val = i >= n_code + QSA_KEYS;
+            const int k = val ? i - n_code - QSA_KEYS : i;
+            const int key = k < n_code ? k / cp : k - n_code;
+            const int s = slots[key];
+            if (s < 0) continue;
+            const size_t r = size_t(s) * p.Hkv + kvh;
+            if (k < n_code) {
+                const int c = k % cp;
+                const uint4 v = *reinterpret_cast<const uint4 *>((val ? p.vc : p.kc) + r * cb + c * 16);
+                *reinterpret_cast<uint4 *>((val ? vcs : kcs) + key * CB + c * 16) = v;
+            } else {
+                const uint8_t *src = (val ? p.vs : p.ks) + r * sb;
+                uint8_t *dst = (val ? vss : kss) + key * SB;
+                for (int e = 0; e < sb; ++e) dst[e] = src[e];
+            }
+        }
     }
     __syncthreads();
     // scores: a warp per key; lane covers D/32 consecutive values (inside one 16-value scale block)
     const int epl = D / 32, d0 = lane * epl;
     for (int jj = warp; jj < QSA_KEYS; jj += QSA_THREADS / 32) {
-        const int s = slots[jj];
-        if (s < 0) {
+        if (slots[jj] < 0) {
             if (lane < G) sc[lane * QSA_KEYS + jj] = QSA_NEG_INF;
             continue;
         }
-        const size_t r = size_t(s) * p.Hkv + kvh;
-        const uint8_t *kc = p.kc + r * (D / 2);
-        const float ksf = e4m3_to_f(p.ks[r * (D / 16) + d0 / 16]);
+        const uint8_t *kc = kcs + jj * CB;
+        const float ksf = e4m3_to_f(kss[jj * SB + d0 / 16]);
         float k[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -126,18 +151,17 @@ __global__ void __launch_bounds__(QSA_THREADS) qsa_partial_kernel(QsaParams p) {
         }
     }
     __syncthreads();
-    // softmax of the split, per head: a warp per head, two keys per lane
+    // softmax of the split, per head: a warp per head, one key per lane
     for (int g = warp; g < G; g += QSA_THREADS / 32) {
-        const float s0 = sc[g * QSA_KEYS + lane], s1 = sc[g * QSA_KEYS + 32 + lane];
-        float m = fmaxf(s0, s1);
+        const float s0 = sc[g * QSA_KEYS + lane];
+        float m = s0;
 #pragma unroll
         for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float p0 = m == QSA_NEG_INF ? 0.f : __expf(s0 - m), p1 = m == QSA_NEG_INF ? 0.f : __expf(s1 - m);
-        float l = p0 + p1;
+        const float p0 = m == QSA_NEG_INF ? 0.f : __expf(s0 - m);
+        float l = p0;
 #pragma unroll
         for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         sc[g * QSA_KEYS + lane] = p0;
-        sc[g * QSA_KEYS + 32 + lane] = p1;
         if (lane == 0) {
             ml[2 * g] = m;
             ml[2 * g + 1] = l;
@@ -151,11 +175,9 @@ __global__ void __launch_bounds__(QSA_THREADS) qsa_partial_kernel(QsaParams p) {
 #pragma unroll
         for (int g = 0; g < QSA_MAX_G; ++g) acc[g] = 0.f;
         for (int jj = 0; jj < QSA_KEYS; ++jj) {
-            const int s = slots[jj];
-            if (s < 0) continue;
-            const size_t r = size_t(s) * p.Hkv + kvh;
-            const uint32_t byte = p.vc[r * (D / 2) + d / 2];
-            const float v = e2m1_val((d & 1) ? byte >> 4 : byte & 15) * e4m3_to_f(p.vs[r * (D / 16) + d / 16]);
+            if (slots[jj] < 0) continue;
+            const uint32_t byte = vcs[jj * CB + d / 2];
+            const float v = e2m1_val((d & 1) ? byte >> 4 : byte & 15) * e4m3_to_f(vss[jj * SB + d / 16]);
 #pragma unroll
             for (int g = 0; g < QSA_MAX_G; ++g)
                 if (g < G) acc[g] += sc[g * QSA_KEYS + jj] * v;
@@ -205,7 +227,7 @@ extern "C" int xt_qsa_kv_write(const void *x, const int64_t *slot, int T, int H,
 
 // Attention of B decode queries (Hq heads of dim D) over their selected cache slots: out [B, Hq, D] BF16 =
 // softmax(scale * q.k) . v, keys and values dequantized from the NVFP4 cache. Scratch: part_o [B, Hkv, splits, G, D]
-// and part_ml [B, Hkv, splits, G, 2] FP32 with splits = ceil(nsel / 64).
+// and part_ml [B, Hkv, splits, G, 2] FP32 with splits = ceil(nsel / 32).
 extern "C" int xt_qsa_decode(const void *q, const int32_t *idx, int B, int nsel, int Hq, int Hkv, int D,
                              const void *kc, const void *ks, const void *vc, const void *vs, float *part_o,
                              float *part_ml, void *out, float scale, cudaStream_t stream) {
@@ -228,7 +250,7 @@ extern "C" int xt_qsa_decode(const void *q, const int32_t *idx, int B, int nsel,
     p.Hkv = Hkv;
     p.G = G;
     p.D = D;
-    p.splits = (nsel + xt::QSA_KEYS - 1) / xt::QSA_KEYS;
+    p.splits = (nsel + xt::QSA_KEYS - 1) / xt::QSA_KEYS;   // (part_o / part_ml sized for 32-key splits)
     p.scale = scale;
     xt::qsa_partial_kernel<<<dim3(p.splits, Hkv, B), xt::QSA_THREADS, 0, stream>>>(p);
     if (cudaGetLastError() != cudaSuccess) return -1;

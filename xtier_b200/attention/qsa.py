@@ -5,9 +5,9 @@ selected (top-k), keys and values kept as NVFP4 (E2M1 codes, one E4M3 scale per 
 `KvCacheFP4(rows, max_len, kv_heads, head_dim)` holds K and V of `rows` sequences; `write(k, v, slots)` quantizes new
 rows into it (csrc/cuda/qsa.cu `qsa_kv_write`), `dequant(slots)` returns the FP32 values the kernels compute with.
 `qsa_decode(q, idx, cache, scale)` is the attention: q [B, Hq, D] BF16, idx [B, nsel] int32 cache slots (-1 = none),
--> [B, Hq, D] BF16. The G = Hq / Hkv query heads of a KV head share one CTA per 64 selected keys, which dequantizes each
-key and value once in registers for all of them; the splits meet in a log-sum-exp merge. The selection comes from an
-indexer: the DSA lightning indexer of attention/dsa.py (FP8 index keys, ReLU head-sum scores, length-aware radix
+-> [B, Hq, D] BF16. The G = Hq / Hkv query heads of a KV head share one CTA per 32 selected keys, which stages their
+NVFP4 rows in shared memory and dequantizes each key and value once in registers for all of them; the splits meet in a
+log-sum-exp merge. The selection comes from an indexer: the DSA lightning indexer of attention/dsa.py (FP8 index keys, ReLU head-sum scores, length-aware radix
 top-k) has the same form as QSA's.
 
 Reference parity: xtier/packs/qwen4_exp/qsa_fp4.py:82-147 (top-k KV rows gathered from an NVFP4 pool and dequantized
@@ -21,7 +21,7 @@ import torch
 
 from .. import formats, ops
 
-KEYS_PER_SPLIT = 64
+KEYS_PER_SPLIT = 32
 
 
 class KvCacheFP4:
