@@ -21,7 +21,7 @@
 
 namespace xt {
 
-constexpr int QSA_KEYS = 32, QSA_THREADS = 256, QSA_MAX_G = 16, QSA_MAX_D = 256;
+constexpr int QSA_KEYS = 32, QSA_THREADS = 256, QSA_MAX_G = 16, QSA_MAX_D = 256, QSA_MAX_SPLITS = 1024;
 #define QSA_NEG_INF __int_as_float(0xff800000)
 
 __global__ void __launch_bounds__(256) qsa_kv_write_kernel(const __nv_bfloat16 *__restrict__ x,
@@ -98,8 +98,13 @@ __global__ void __launch_bounds__(QSA_THREADS) qsa_partial_kernel(QsaParams p) {
         const int j = split * QSA_KEYS + tid;
         slots[tid] = j < p.nsel ? p.idx[size_t(b) * p.nsel + j] : -1;
     }
-    for (int i = tid; i < G * D; i += QSA_THREADS)
-        qs[i] = __bfloat162float(p.q[(size_t(b) * p.Hq + size_t(kvh) * G + i / D) * D + i % D]);
+    // queries in lane-major order (element d = lane * D/32 + e at g * D + e * 32 + lane): the score loop's reads
+    // are then conflict-free across the warp
+    for (int i = tid; i < G * D; i += QSA_THREADS) {
+        const int g = i / D, d = i % D, epl_ = D / 32;
+        qs[g * D + (d % epl_) * 32 + d / epl_] =
+            __bfloat162float(p.q[(size_t(b) * p.Hq + size_t(kvh) * G + g) * D + d]);
+    }
     __syncthreads();
     {   // codes: cb / 16 pieces per row; scales: one piece per row (sb <= 16) -- K and V
         const int cp = cb / 16, n_code = QSA_KEYS * cp;
@@ -114,10 +119,13 @@ __global__ void __launch_bounds__(QSA_THREADS) qsa_partial_kernel(QsaParams p) {
                 const int c = k % cp;
                 const uint4 v = *reinterpret_cast<const uint4 *>((val ? p.vc : p.kc) + r * cb + c * 16);
                 *reinterpret_cast<uint4 *>((val ? vcs : kcs) + key * CB + c * 16) = v;
-            } else {
+            } else {   // one load of the row's sb scale bytes (sb = D/16: 2, 4, 8 or 16, aligned to its size)
                 const uint8_t *src = (val ? p.vs : p.ks) + r * sb;
                 uint8_t *dst = (val ? vss : kss) + key * SB;
-                for (int e = 0; e < sb; ++e) dst[e] = src[e];
+                if (sb == 16) *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+                else if (sb == 8) *reinterpret_cast<uint2 *>(dst) = *reinterpret_cast<const uint2 *>(src);
+                else if (sb == 4) *reinterpret_cast<uint32_t *>(dst) = *reinterpret_cast<const uint32_t *>(src);
+                else *reinterpret_cast<uint16_t *>(dst) = *reinterpret_cast<const uint16_t *>(src);
             }
         }
     }
@@ -144,7 +152,7 @@ __global__ void __launch_bounds__(QSA_THREADS) qsa_partial_kernel(QsaParams p) {
             float acc = 0.f;
 #pragma unroll
             for (int e = 0; e < 8; ++e)
-                if (e < epl) acc += qs[g * D + d0 + e] * k[e];
+                if (e < epl) acc += qs[g * D + e * 32 + lane] * k[e];
 #pragma unroll
             for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (lane == 0) sc[g * QSA_KEYS + jj] = acc * p.scale;
@@ -189,27 +197,36 @@ __global__ void __launch_bounds__(QSA_THREADS) qsa_partial_kernel(QsaParams p) {
     if (tid < 2 * G) p.part_ml[base * G * 2 + tid] = ml[tid];
 }
 
+// The split weights exp(m_s - M) / L are computed once per head by warp 0 into shared memory; the value loop then
+// issues independent loads of the splits' partial outputs.
 __global__ void __launch_bounds__(QSA_THREADS) qsa_merge_kernel(QsaParams p) {
-    const int hq = blockIdx.x, b = blockIdx.y;
-    const int kvh = hq / p.G, g = hq % p.G, D = p.D;
-    const size_t base = (size_t(b) * p.Hkv + kvh) * p.splits;
-    float M = QSA_NEG_INF;
-    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[((base + s) * p.G + g) * 2]);
-    float L = 0.f;
-    if (M != QSA_NEG_INF)
-        for (int s = 0; s < p.splits; ++s) {
+    __shared__ float wsp[QSA_MAX_SPLITS];
+    const int hq = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+    const int kvh = hq / p.G, g = hq % p.G, D = p.D, S = p.splits;
+    const size_t base = (size_t(b) * p.Hkv + kvh) * S;
+    if (tid < 32) {
+        float M = QSA_NEG_INF;
+        for (int s = lane; s < S; s += 32) M = fmaxf(M, p.part_ml[((base + s) * p.G + g) * 2]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.f;
+        for (int s = lane; s < S; s += 32) {
             const float m = p.part_ml[((base + s) * p.G + g) * 2];
-            if (m != QSA_NEG_INF) L += p.part_ml[((base + s) * p.G + g) * 2 + 1] * __expf(m - M);
+            const float e = m == QSA_NEG_INF ? 0.f : __expf(m - M);
+            wsp[s] = e;
+            L += e * p.part_ml[((base + s) * p.G + g) * 2 + 1];
         }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    for (int d = threadIdx.x; d < D; d += QSA_THREADS) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        for (int s = lane; s < S; s += 32) wsp[s] *= inv;
+    }
+    __syncthreads();
+    for (int d = tid; d < D; d += QSA_THREADS) {
         float o = 0.f;
-        if (L > 0.f)
-            for (int s = 0; s < p.splits; ++s) {
-                const float m = p.part_ml[((base + s) * p.G + g) * 2];
-                if (m != QSA_NEG_INF) o += p.part_o[((base + s) * p.G + g) * D + d] * __expf(m - M);
-            }
-        p.out[(size_t(b) * p.Hq + hq) * D + d] = __float2bfloat16(o * inv);
+#pragma unroll 4
+        for (int s = 0; s < S; ++s) o += wsp[s] * p.part_o[((base + s) * p.G + g) * D + d];
+        p.out[(size_t(b) * p.Hq + hq) * D + d] = __float2bfloat16(o);
     }
 }
 
@@ -232,6 +249,7 @@ extern "C" int xt_qsa_decode(const void *q, const int32_t *idx, int B, int nsel,
                              const void *kc, const void *ks, const void *vc, const void *vs, float *part_o,
                              float *part_ml, void *out, float scale, cudaStream_t stream) {
     if (B <= 0 || nsel <= 0 || Hkv <= 0 || Hq % Hkv || D % 32 || D < 32 || D > xt::QSA_MAX_D) return -2;
+    if ((nsel + xt::QSA_KEYS - 1) / xt::QSA_KEYS > xt::QSA_MAX_SPLITS) return -2;   // nsel <= 32768
     const int G = Hq / Hkv;
     if (G > xt::QSA_MAX_G) return -2;
     xt::QsaParams p{};
