@@ -319,7 +319,7 @@ def run_config3(args, ctx: Ctx) -> dict:
         'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
         'config': {
             'model': 'DeepSeek-V3-shaped 61L H7168 MLA-128h 256 MXFP4 experts top-8 (grouped sigmoid) + 1 shared, '
-                     'I2048, 3 dense layers I18432, vocab 129280 (BASELINE config 3)',
+                     'I2048, 3 dense layers I18432, vocab 129280 (benchmark config 3)',
             'global_batch': args.requests, 'seq_len': args.prompt + args.gen, 'prompt': args.prompt,
             'decode_tokens': args.gen, 'context_at_timed_steps': fill,
             'parallelism': f'ep{world} (experts) + dp{world} (attention, {B} requests per rank)',
@@ -349,7 +349,7 @@ def run_config3(args, ctx: Ctx) -> dict:
 
 
 def time_ttft(args, ctx: Ctx, model) -> dict:
-    """time to first token of one random-id prompt of --ttft-tokens tokens with DSA sparse
+    """benchmark config 4: time to first token of one random-id prompt of --ttft-tokens tokens with DSA sparse
     attention (index top-2048) over the group (models/deepseek_prefill.py). One untimed run (allocations), then one
     timed by CUDA events between barriers, max over ranks."""
     torch = ctx.torch
@@ -445,7 +445,7 @@ def run_config2(args, ctx: Ctx) -> dict:
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms / args.steps, 4),
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': round(value / QWEN_BASELINE_TOKS, 3),
         'dtype': 'bf16', 'data': 'synthetic',
-        'config': {'model': 'qwen3-style MoE 48L H2048 GQA32/4 128E top-8 I768 NVFP4 (BASELINE config 2)',
+        'config': {'model': 'qwen3-style MoE 48L H2048 GQA32/4 128E top-8 I768 NVFP4 (benchmark config 2)',
                    'global_batch': world, 'seq_len': args.prompt + args.warmup + args.steps,
                    'prompt': args.prompt, 'parallelism': f'dp{world}', 'hot_fraction': args.hot,
                    'hot_slots': ('each GPU holds hot_fraction of the experts; the GPUs\' slots form one pool read '

@@ -1,5 +1,5 @@
 #!/usr/bin/env bash
-# DeepSeek-V3 shape (BASELINE config 3's model) served from one B200: HOT of each MoE layer's 256 experts in HBM
+# DeepSeek-V3 shape (benchmark config 3's model) served from one B200: HOT of each MoE layer's 256 experts in HBM
 # slots, the rest on the CPU engine through the mailbox; random-init weights. With EP=N, the layer benchmark over N
 # GPUs instead. Override any XTIER_* setting from the environment.
 set -euo pipefail

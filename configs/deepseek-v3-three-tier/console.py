@@ -1,4 +1,4 @@
-"""Console entry: BASELINE config 5, the three-tier DeepSeek-V3-shaped decode at 32K context (planner-sized GPU slots,
+"""Console entry: benchmark config 5, the three-tier DeepSeek-V3-shaped decode at 32K context (planner-sized GPU slots,
 CPU engine RAM, NVMe cold records, a 4M x 4096 NVMe table in the graph). A run of the measuring tool: it prints one
 JSON line with the tiers, tokens per second and the cold-store and table statistics, then exits."""
 

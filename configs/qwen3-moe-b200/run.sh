@@ -1,5 +1,5 @@
 #!/usr/bin/env bash
-# Qwen3-style MoE on one B200: 40% of each layer's experts in GPU hot slots, the rest on the CPU
+# Qwen3-style MoE (benchmark config 2) on one B200: 40% of each layer's experts in GPU hot slots, the rest on the CPU
 # engine through the mailbox. Override any XTIER_* setting from the environment.
 set -euo pipefail
 cd "$(dirname "$0")/../.."

@@ -1,5 +1,5 @@
 """Long-prompt prefill of the DeepSeek-V3-shaped model with DSA sparse attention over the ranks of a node (the 64K
-time-to-first-token of BASELINE config 4).
+time-to-first-token of benchmark config 4).
 
 Layout: the prompt's tokens are split over the W ranks in contiguous slices (sequence parallel); every rank runs the
 dense parts of every layer on its own slice. Per layer:

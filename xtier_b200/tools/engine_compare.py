@@ -1,4 +1,4 @@
-"""Same-host comparison of this framework's CPU expert engine with the reference's own C++ engine (BASELINE config
+"""Same-host comparison of this framework's CPU expert engine with the reference's own C++ engine (benchmark config
 1: hidden 2048, 64 NVFP4 experts of intermediate 768, softmax top-8 with renormalized weights, 8 threads).
 
 Both engines receive the same expert bytes (the shared checkpoint layout), the same activations and routes, and are

@@ -1,4 +1,4 @@
-"""three-tier decode of the DeepSeek-V3-shaped model at batch 1 over a 32K random-id context.
+"""benchmark config 5: three-tier decode of the DeepSeek-V3-shaped model at batch 1 over a 32K random-id context.
 
 Tiers of every MoE layer: GPU hot slots (by default 20 % of the experts node-wide, spread over the process group's
 GPUs by expert parallelism: a token's routes to another GPU's experts reach that GPU over NVLink inside the fused
@@ -20,7 +20,7 @@ rows; the prefill is not part of this measurement). Device time by CUDA events o
 Full size needs about 0.8 x 256 experts x 58 layers of cold records (~260 GB) and the CPU tier's RAM (~165 GB per
 rank); `--layers` scales the model (and every tier) down to what a machine holds.
 
-Reference parity: BASELINE config 5 (the reference's three-tier run: xtier/cache/ with remote slots, the CPU engine,
+Reference parity: benchmark config 5 (the reference's three-tier run: xtier/cache/ with remote slots, the CPU engine,
 xtier/cache/cold.py, xtier/tables/lookup.py, xtier/planner/auto.py).
 """
 from __future__ import annotations
@@ -185,7 +185,7 @@ def main(argv=None):
         mb = mailbox.stats()
         cold1 = pool.stats()
         line = {
-            'tool': 'three_tier', 'config': 'BASELINE config 5', 'n_gpus': world, 'layers': cfg.layers,
+            'tool': 'three_tier', 'config': 'benchmark config 5', 'n_gpus': world, 'layers': cfg.layers,
             'moe_layers': moe_layers, 'context': a.context, 'batch_per_rank': 1, 'steps': a.steps,
             'warmup': a.warmup, 'ms_per_token': round(ms / a.steps, 3),
             'tok_s_per_request': round(a.steps / ms * 1e3, 2),
