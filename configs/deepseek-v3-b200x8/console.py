@@ -9,8 +9,8 @@ MODEL = {
         {'key': 'mode', 'label': 'launch', 'default': 'serve',
          'choices': [['serve', 'generation server, 1 GPU, tiered experts'],
                      ['ep', 'EP layer benchmark over several GPUs']]},
-        {'key': 'hot', 'label': 'GPU expert slots (serve)', 'default': '0.56',
-         'choices': [['0.56', '56% of each layer (fits one B200)'], ['0.4', '40%'], ['0.25', '25%']]},
+        {'key': 'hot', 'label': 'GPU expert slots (serve)', 'default': '0.44',
+         'choices': [['0.44', '44% of each layer (what one B200 holds)'], ['0.4', '40%'], ['0.25', '25%']]},
         {'key': 'gpus', 'label': 'GPUs (EP)', 'default': '8', 'choices': [['8', '8'], ['4', '4'], ['2', '2']]},
         {'key': 'tokens', 'label': 'tokens per rank (EP)', 'default': '4',
          'choices': [['4', '4 (32 requests over 8 GPUs)'], ['16', '16']]},

@@ -8,4 +8,4 @@ if [[ -n "${EP:-}" ]]; then
     exec timeout -k 60 1800 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$EP" \
         --master-addr 127.0.0.1 --master-port "${MASTER_PORT:-29551}" -m xtier_b200.tools.ep_bench "$@"
 fi
-exec python -m xtier_b200.serve --model deepseek-v3 --hot "${HOT:-0.56}" --port "${PORT:-18190}" "$@"
+exec python -m xtier_b200.serve --model deepseek-v3 --hot "${HOT:-0.44}" --port "${PORT:-18190}" "$@"

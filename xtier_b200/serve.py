@@ -3,7 +3,7 @@ measures).
 
     python -m xtier_b200.serve --model qwen3-moe [--layers 48] [--hot 0.4] [--max-len 8192] --port 18180
     python -m xtier_b200.serve --checkpoint DIR [--hot 0.4] ...       # a Hugging Face qwen3_moe checkpoint
-    python -m xtier_b200.serve --model deepseek-v3 [--layers 61] [--hot 0.56] ...   # DeepSeek-V3 shape, random init
+    python -m xtier_b200.serve --model deepseek-v3 [--layers 61] [--hot 0.44] ...   # DeepSeek-V3 shape, random init
     ... [--recall DIR|memory]        # speculative serving: Recall copy drafts verified by the target (one forward
                                      # per step, several tokens when a copy lands)
 
@@ -868,8 +868,13 @@ def build_deepseek(args, stages: Stages):
     if args.checkpoint or args.sampling or args.batch > 1 or args.recall:
         raise ValueError('deepseek-v3 serves random-init weights greedily, one request at a time '
                          '(no --checkpoint, --sampling, --batch or --recall)')
+    import torch
     cfg = DeepSeekV3Config(layers=args.layers or 61, attn='mla')
-    gpu = max(1, min(cfg.experts, round(args.hot * cfg.experts)))
+    # HBM slots: the --hot share, capped by what fits beside the dense weights with 6 GB kept for the KV cache, the
+    # exchange and staging buffers and the workspaces
+    free, _ = torch.cuda.mem_get_info()
+    fit = (free - cfg.dense_bytes() - (6 << 30)) // max(1, cfg.expert_bytes() * cfg.moe_layers())
+    gpu = max(1, min(cfg.experts, round(args.hot * cfg.experts), int(fit)))
     mailbox = Mailbox(cfg.hidden) if gpu < cfg.experts else None
     stages.set('weights')
     # the exchange buffers take a prompt chunk of up to 32 tokens (the mailbox's limit); decode uses one
