@@ -1,16 +1,16 @@
 // PCIe staging of CPU-tier experts for the expert-parallel decode (sm_100a).
 //
-// With part of a layer's experts in the CPU engine's host memory, the CPU tier and the PCIe link can work on the same
-// call: the router (moe_route, PCIe staging claim) hands up to stage_max of the CPU-tier experts its tokens chose to the
-// GPU, and this kernel copies those experts from the engine's own slots -- host memory registered with CUDA and mapped
-// into the device's address space, read in place over PCIe -- into GPU staging slots in the pool layout. The EP expert
-// streams then compute their routes like any pool slot while the CPU engine computes the rest. Nothing is duplicated in
-// host memory: the engine's slots are the only host copy.
+// With part of a layer's experts in the CPU engine's host memory, the CPU tier and the PCIe link can work on the
+// same call: the router (moe_route, PCIe staging claim) hands up to stage_max of the CPU-tier experts its tokens chose
+// to the GPU, and this kernel copies those experts from the engine's own slots -- host memory registered with CUDA and
+// mapped into the device's address space, read in place over PCIe -- into GPU staging slots in the pool layout. The
+// EP expert streams then compute their routes like any pool slot while the CPU engine computes the rest. Nothing is
+// duplicated in host memory: the engine's slots are the only host copy.
 //
-// Grid (chunks, stage_max): CTA (c, s) copies part c of every piece of staged expert s (of every NUMA node's shard) with
-// 16-byte loads, four in flight per thread; the global scales come from a small device table. The last CTA to finish
-// resets the claims (every expert the call's routes claimed, staged or not) and the count for the next call. No CTA
-// waits on another: the reset uses an arrival counter.
+// Grid (chunks, stage_max): CTA (c, s) copies part c of every piece of staged expert s (of every NUMA node's shard)
+// with 16-byte loads, four in flight per thread; the global scales come from a small device table. The last CTA to
+// finish resets the claims (every expert the call's routes claimed, staged or not) and the count for the next call.
+// No CTA waits on another: the reset uses an arrival counter.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -64,7 +64,8 @@ __global__ void __launch_bounds__(STAGE_THREADS) ep_stage_kernel(StageParams p) 
                 int i = threadIdx.x;
                 for (; i + 3 * STAGE_THREADS < n16; i += 4 * STAGE_THREADS) {
                     const uint4 a0 = ld_sys_v4(src + i), a1 = ld_sys_v4(src + i + STAGE_THREADS);
-                    const uint4 a2 = ld_sys_v4(src + i + 2 * STAGE_THREADS), a3 = ld_sys_v4(src + i + 3 * STAGE_THREADS);
+                    const uint4 a2 = ld_sys_v4(src + i + 2 * STAGE_THREADS);
+                    const uint4 a3 = ld_sys_v4(src + i + 3 * STAGE_THREADS);
                     dst[i] = a0;
                     dst[i + STAGE_THREADS] = a1;
                     dst[i + 2 * STAGE_THREADS] = a2;

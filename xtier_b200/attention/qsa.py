@@ -7,8 +7,8 @@ rows into it (csrc/cuda/qsa.cu `qsa_kv_write`), `dequant(slots)` returns the FP3
 `qsa_decode(q, idx, cache, scale)` is the attention: q [B, Hq, D] BF16, idx [B, nsel] int32 cache slots (-1 = none),
 -> [B, Hq, D] BF16. The G = Hq / Hkv query heads of a KV head share one CTA per 32 selected keys, which stages their
 NVFP4 rows in shared memory and dequantizes each key and value once in registers for all of them; the splits meet in a
-log-sum-exp merge. The selection comes from an indexer: the DSA lightning indexer of attention/dsa.py (FP8 index keys, ReLU head-sum scores, length-aware radix
-top-k) has the same form as QSA's.
+log-sum-exp merge. The selection comes from an indexer: the DSA lightning indexer of attention/dsa.py (FP8 index
+keys, ReLU head-sum scores, length-aware radix top-k) has the same form as QSA's.
 
 Reference parity: xtier/packs/qwen4_exp/qsa_fp4.py:82-147 (top-k KV rows gathered from an NVFP4 pool and dequantized
 in registers), qsa_decode.py:26-64 (split-key decode with a merge, 24 query / 2 KV heads of dim 256),

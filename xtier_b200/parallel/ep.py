@@ -204,7 +204,8 @@ class _Router:
 
     def __call__(self, x):
         T = x.shape[0]
-        ops.moe_route(x, self.w, self.bias, self.corr, self.table, self.shared_slots, self.ids[:T], self.wt[:T], self.slots[:T],
+        ops.moe_route(x, self.w, self.bias, self.corr, self.table, self.shared_slots, self.ids[:T], self.wt[:T],
+                      self.slots[:T],
                       self.ws_logits, self.ws_count, self.k, self.mode, self.n_group, self.topk_group, self.renorm,
                       self.scale, self.layer, self.mailbox.handle if self.mailbox is not None else 0,
                       **(dict(zip(('cold_index', 'claim', 'claim_list', 'claim_count', 'stage_max', 'stage_slot0'),
